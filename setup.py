@@ -1,0 +1,61 @@
+"""Build of the vramancer_b200 native extensions (in-tree, sm_100a only).
+
+    python setup.py build_ext --inplace
+
+produces vramancer_b200/_C*.so (CUDA kernels) and vramancer_b200/_runtime*.so
+(host-side C++ runtime: page allocator, parity, file spill, HMAC).
+"""
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension, CppExtension
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("vramancer_b200", "csrc")
+RT = os.path.join("vramancer_b200", "runtime")
+
+# Explicit -gencode: torch's own arch list is bypassed, only sm_100a code is built.
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__",
+    "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
+]
+if os.environ.get("VRM_BOUNDS_CHECK") == "1":
+    NVCC_FLAGS.append("-DVRM_BOUNDS_CHECK=1")
+
+
+def _sources(d, exts):
+    full = os.path.join(HERE, d)
+    if not os.path.isdir(full):
+        return []
+    return sorted(os.path.join(d, f) for f in os.listdir(full) if f.endswith(exts))
+
+
+cuda_sources = _sources(CSRC, (".cu", ".cpp"))
+runtime_sources = _sources(RT, (".cpp",))
+
+ext_modules = [
+    CUDAExtension(
+        name="vramancer_b200._C",
+        sources=cuda_sources,
+        extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+    ),
+]
+if runtime_sources:
+    ext_modules.append(
+        CppExtension(
+            name="vramancer_b200._runtime",
+            sources=runtime_sources,
+            extra_compile_args={"cxx": ["-O3", "-std=c++17", "-pthread"]},
+        )
+    )
+
+setup(
+    name="vramancer_b200",
+    version="0.1.0",
+    packages=["vramancer_b200"],
+    ext_modules=ext_modules,
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

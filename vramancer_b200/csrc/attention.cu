@@ -1,0 +1,666 @@
+// Paged attention over the KV pool  cache[page, layer, {k,v}, kv_head, 16, head_dim]
+// with bf16 or fp8-e4m3 pages (per-(layer, k/v, kv_head) fp32 scales).
+//
+// decode  (one new token per sequence):
+//   grid (kv_heads, batch, splits), 4 warps.  One CTA serves the whole GQA group of a
+//   KV head, so every K/V byte is read once for all its query heads.  The group
+//   (<= 8 heads) is the MMA row block; the 16 tokens of a page are the columns.  Pages
+//   of the split are dealt round-robin to the warps; each warp double-buffers its
+//   pages with cp.async and keeps its own online-softmax state; warps merge in shared
+//   memory.  With splits > 1 each CTA writes a normalised partial and the last CTA of
+//   the (sequence, kv head) merges them (flash-decoding); that CTA resets the counter,
+//   so the kernel replays inside CUDA graphs.
+// prefill (causal, varlen, chunked-prefill aware):
+//   grid (q_tiles of 64, q_heads, batch), 4 warps x 16 query rows.  Keys come from the
+//   same paged pool (cached prefix pages included), 64 keys per stage, double-buffered.
+//
+// Decode attention is bound by HBM bandwidth (the GQA group gives at most 8 rows, far
+// below the 64/128-row tcgen05 tile), so its MMAs use the warp-level m16n8k16 path and
+// the kernel is measured by DRAM throughput.
+//
+// Reference parity: csrc/paged_attention_kernel.cu:61-438 (SIMT decode over fp32 /
+// fp16 / q4 pages, not on the reference's forward path); the reference prefill runs
+// HF SDPA (core/turbo_engine.py:72-93).
+#include <algorithm>
+
+#include "vrm_common.cuh"
+#include "vrm_host.h"
+#include "vrm_kernels.h"
+
+namespace vrm {
+
+constexpr int kPage = 16;
+
+// Byte offset of 16-byte chunk `ch` of row `r` in a swizzled tile whose rows are ROWB
+// bytes long.  XOR-ing the chunk with (r & 7) puts the eight rows of every ldmatrix
+// 8x8 read in different banks.
+template <int ROWB>
+__device__ __forceinline__ uint32_t swz(int r, int ch) {
+  return (uint32_t)(r * ROWB + ((ch ^ (r & 7)) << 4));
+}
+
+// fp8 e4m3 x2 -> bf16 x2 (exact: every e4m3 value is a bf16 value)
+__device__ __forceinline__ uint32_t fp8x2_to_bf16x2(uint16_t v) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(v, __NV_E4M3);
+  const float2 f = __half22float2(*reinterpret_cast<__half2*>(&h));
+  return pack_bf16x2(f.x, f.y);
+}
+
+// Convert rows x D fp8 bytes (row-major, contiguous) at raw into the swizzled bf16
+// tile at dst, spread over nthr threads starting at index tid.
+template <int D>
+__device__ __forceinline__ void convert_fp8_tile(const uint8_t* raw, uint8_t* dst, int rows, int tid, int nthr) {
+  constexpr int kChunks = D / 16;   // 16 fp8 per 16-byte chunk
+  for (int i = tid; i < rows * kChunks; i += nthr) {
+    const int r = i / kChunks, c = i % kChunks;
+    const uint4 v = *reinterpret_cast<const uint4*>(raw + r * D + c * 16);
+    const uint16_t* p = reinterpret_cast<const uint16_t*>(&v);
+    uint4 o0, o1;
+    uint32_t* q0 = reinterpret_cast<uint32_t*>(&o0);
+    uint32_t* q1 = reinterpret_cast<uint32_t*>(&o1);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      q0[j] = fp8x2_to_bf16x2(p[j]);
+      q1[j] = fp8x2_to_bf16x2(p[4 + j]);
+    }
+    *reinterpret_cast<uint4*>(dst + swz<D * 2>(r, 2 * c)) = o0;
+    *reinterpret_cast<uint4*>(dst + swz<D * 2>(r, 2 * c + 1)) = o1;
+  }
+}
+
+// ============================================================== decode
+template <int D, bool kFp8>
+struct DecodeSmem {
+  static constexpr int kTileB = kPage * D * 2;              // one bf16 16 x D tile
+  static constexpr int kRawB = kFp8 ? kPage * D : kTileB;   // bytes per K (or V) page chunk
+  static constexpr int kStageB = 2 * kRawB;                 // K + V
+  static constexpr int kWarpB = 2 * kStageB + (kFp8 ? 2 * kTileB : 0);
+  static constexpr int kTotal = 4 * kWarpB;
+};
+
+struct DecodeParams {
+  const __nv_bfloat16* q;
+  int64_t ld_q;
+  const uint8_t* cache;
+  int layer, num_layers, KH, G;
+  const int* block_tables;
+  int bt_stride;
+  const int* context_lens;
+  const float* kv_scale;
+  float sm_scale;
+  __nv_bfloat16* out;
+  int64_t ld_o;
+  float* ws_o;
+  float* ws_ml;
+  uint32_t* counters;
+};
+
+template <int D, bool kFp8>
+__global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
+  using S = DecodeSmem<D, kFp8>;
+  constexpr int ROWB = D * 2;
+  constexpr int kEl = kFp8 ? 1 : 2;
+  constexpr int kChunkPerRow = D * kEl / 16;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float s_m[4][8], s_l[4][8];
+  __shared__ uint32_t s_last;
+
+  const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z, nsplit = gridDim.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int G = P.G, KH = P.KH;
+
+  const int ctx = P.context_lens[b];
+  const int npages = (ctx + kPage - 1) / kPage;
+  const int pps = (npages + nsplit - 1) / nsplit;
+  const int p_begin = split * pps;
+  const int p_end = min(npages, p_begin + pps);
+
+  float k_scale = 1.f, v_scale = 1.f;
+  if (kFp8) {
+    k_scale = P.kv_scale[(P.layer * 2 + 0) * KH + kvh];
+    v_scale = P.kv_scale[(P.layer * 2 + 1) * KH + kvh];
+  }
+  const float scale_log2 = P.sm_scale * 1.4426950408889634f * k_scale;
+
+  // Q fragments: rows = heads of the group (rows >= G and rows 8..15 are zero)
+  uint32_t qa[D / 16][2];
+  {
+    const __nv_bfloat16* qrow = P.q + (size_t)b * P.ld_q + (size_t)(kvh * G + g) * D;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      if (g < G) {
+        qa[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * c);
+        qa[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * c);
+      } else {
+        qa[kk][0] = qa[kk][1] = 0u;
+      }
+    }
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+
+  uint8_t* wbase = smem + warp * S::kWarpB;
+  const int* bt = P.block_tables + (size_t)b * P.bt_stride;
+  const size_t head_stride = (size_t)kPage * D * kEl;                       // one (k|v, head) chunk
+  const size_t page_stride = (size_t)P.num_layers * 2 * KH * head_stride;   // one page, all layers
+
+  auto issue = [&](int page_local, int stage) {
+    const int page = bt[page_local];
+    const uint8_t* kp = P.cache + (size_t)page * page_stride + (((size_t)P.layer * 2 + 0) * KH + kvh) * head_stride;
+    const uint8_t* vp = kp + (size_t)KH * head_stride;
+    uint8_t* dst = wbase + stage * S::kStageB;
+    const uint32_t dk = smem_u32(dst), dv = smem_u32(dst + S::kRawB);
+    constexpr int kTotalChunks = kPage * kChunkPerRow;
+#pragma unroll
+    for (int i = lane; i < kTotalChunks; i += 32) {
+      const int r = i / kChunkPerRow, ch = i % kChunkPerRow;
+      const uint32_t off = kFp8 ? (uint32_t)(i * 16) : swz<ROWB>(r, ch);
+      cp_async16(dk + off, kp + (size_t)i * 16, true);
+      cp_async16(dv + off, vp + (size_t)i * 16, true);
+    }
+  };
+
+  const int my_first = p_begin + warp;
+  if (my_first < p_end) issue(my_first, 0);
+  cp_async_commit();
+  int it = 0;
+  for (int p = my_first; p < p_end; p += 4, ++it) {
+    const int stage = it & 1;
+    if (p + 4 < p_end) issue(p + 4, stage ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    uint8_t* kt = wbase + stage * S::kStageB;
+    uint8_t* vt = kt + S::kRawB;
+    if (kFp8) {
+      uint8_t* ck = wbase + 2 * S::kStageB;
+      uint8_t* cv = ck + S::kTileB;
+      convert_fp8_tile<D>(kt, ck, kPage, lane, 32);
+      convert_fp8_tile<D>(vt, cv, kPage, lane, 32);
+      __syncwarp();
+      kt = ck;
+      vt = cv;
+    }
+    const uint32_t kaddr = smem_u32(kt), vaddr = smem_u32(vt);
+
+    // S = Q K^T : rows = heads, cols = the page's 16 tokens (two n-tiles)
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int j = lane >> 3;
+      const int row = (lane & 7) + (j >> 1) * 8;
+      const int ch = 2 * kk + (j & 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kaddr + swz<ROWB>(row, ch), b0, b1, b2, b3);
+      mma_bf16_16816(s0, qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
+      mma_bf16_16816(s1, qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
+    }
+    const int tok0 = p * kPage;
+    float x[4] = {s0[0] * scale_log2, s0[1] * scale_log2, s1[0] * scale_log2, s1[1] * scale_log2};
+    const int tix[4] = {tok0 + 2 * c, tok0 + 2 * c + 1, tok0 + 8 + 2 * c, tok0 + 8 + 2 * c + 1};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (tix[i] >= ctx) x[i] = -INFINITY;
+    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m_run - m_new);
+    float pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pr[i] = (m_new == -INFINITY) ? 0.f : exp2f(x[i] - m_new);
+    float rs = pr[0] + pr[1] + pr[2] + pr[3];
+    rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+    rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+    l_run = l_run * alpha + rs;
+    m_run = m_new;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= alpha;
+      o[i][1] *= alpha;
+    }
+    const uint32_t pa0 = pack_bf16x2(pr[0], pr[1]);
+    const uint32_t pa2 = pack_bf16x2(pr[2], pr[3]);
+    // O += P V : rows = heads, cols = head_dim (n-tiles of 8), k = 16 tokens
+#pragma unroll
+    for (int nd = 0; nd < D / 8; nd += 2) {
+      const int j = lane >> 3;
+      const int row = (lane & 7) + (j & 1) * 8;
+      const int ch = nd + (j >> 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vaddr + swz<ROWB>(row, ch), b0, b1, b2, b3);
+      mma_bf16_16816(o[nd], pa0, 0u, pa2, 0u, b0, b1);
+      mma_bf16_16816(o[nd + 1], pa0, 0u, pa2, 0u, b2, b3);
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- merge the 4 warps
+  float* s_o = reinterpret_cast<float*>(smem);   // [4][8][D]
+  if (c == 0) {
+    s_m[warp][g] = m_run;
+    s_l[warp][g] = l_run;
+  }
+#pragma unroll
+  for (int nd = 0; nd < D / 8; ++nd) {
+    s_o[(warp * 8 + g) * D + nd * 8 + 2 * c] = o[nd][0];
+    s_o[(warp * 8 + g) * D + nd * 8 + 2 * c + 1] = o[nd][1];
+  }
+  __syncthreads();
+
+  const size_t grp = (size_t)b * KH + kvh;
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][h]);
+    float L = 0.f, acc = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float f = exp2f(s_m[w][h] - M);
+        L += s_l[w][h] * f;
+        acc += s_o[(w * 8 + h) * D + d] * f;
+      }
+    }
+    if (nsplit == 1) {
+      const float r = L > 0.f ? acc / L * v_scale : 0.f;
+      P.out[(size_t)b * P.ld_o + (size_t)(kvh * G + h) * D + d] = __float2bfloat16(r);
+    } else {
+      P.ws_o[((grp * nsplit + split) * G + h) * D + d] = L > 0.f ? acc / L : 0.f;
+      if (d == 0) {
+        P.ws_ml[((grp * nsplit + split) * G + h) * 2 + 0] = M;
+        P.ws_ml[((grp * nsplit + split) * G + h) * 2 + 1] = L;
+      }
+    }
+  }
+  if (nsplit == 1) return;
+
+  // ---- the last CTA of this (sequence, kv head) merges the splits
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(&P.counters[grp], 1u);
+    s_last = (prev == (uint32_t)(nsplit - 1)) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx % D;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(P.ws_ml + ((grp * nsplit + s) * G + h) * 2));
+    float L = 0.f, acc = 0.f;
+    if (M != -INFINITY) {
+      for (int s = 0; s < nsplit; ++s) {
+        const float ms = __ldcg(P.ws_ml + ((grp * nsplit + s) * G + h) * 2);
+        const float ls = __ldcg(P.ws_ml + ((grp * nsplit + s) * G + h) * 2 + 1);
+        const float wgt = ls * exp2f(ms - M);
+        L += wgt;
+        acc += wgt * __ldcg(P.ws_o + ((grp * nsplit + s) * G + h) * D + d);
+      }
+    }
+    const float r = L > 0.f ? acc / L * v_scale : 0.f;
+    P.out[(size_t)b * P.ld_o + (size_t)(kvh * G + h) * D + d] = __float2bfloat16(r);
+  }
+  if (threadIdx.x == 0) P.counters[grp] = 0u;
+}
+
+// ============================================================== prefill
+template <int D, bool kFp8>
+struct PrefillSmem {
+  static constexpr int kRows = 64;
+  static constexpr int kQB = kRows * D * 2;
+  static constexpr int kTileB = kRows * D * 2;
+  static constexpr int kRawB = kFp8 ? kRows * D : kTileB;
+  static constexpr int kStageB = 2 * kRawB;
+  static constexpr int kTotal = kQB + 2 * kStageB + (kFp8 ? 2 * kTileB : 0);
+};
+
+struct PrefillParams {
+  const __nv_bfloat16* q;
+  int64_t ld_q;
+  const uint8_t* cache;
+  int layer, num_layers, KH, G;
+  const int* block_tables;
+  int bt_stride;
+  const int* cu_q;
+  const int* context_lens;
+  const float* kv_scale;
+  float sm_scale;
+  __nv_bfloat16* out;
+  int64_t ld_o;
+};
+
+template <int D, bool kFp8>
+__global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
+  using S = PrefillSmem<D, kFp8>;
+  constexpr int ROWB = D * 2;
+  constexpr int kEl = kFp8 ? 1 : 2;
+  constexpr int kChunkPerRow = D * kEl / 16;
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int q_start = P.cu_q[b];
+  const int q_len = P.cu_q[b + 1] - q_start;
+  const int q0 = qt * 64;
+  if (q0 >= q_len) return;
+  const int ctx = P.context_lens[b];
+  const int prefix = ctx - q_len;   // tokens already in the cache before this chunk
+  const int KH = P.KH;
+  const int kvh = h / P.G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+
+  float k_scale = 1.f, v_scale = 1.f;
+  if (kFp8) {
+    k_scale = P.kv_scale[(P.layer * 2 + 0) * KH + kvh];
+    v_scale = P.kv_scale[(P.layer * 2 + 1) * KH + kvh];
+  }
+  const float scale_log2 = P.sm_scale * 1.4426950408889634f * k_scale;
+
+  uint8_t* sq = smem;
+  uint8_t* stages = smem + S::kQB;
+  const uint32_t sq_addr = smem_u32(sq);
+
+  // Q tile -> smem (rows past q_len zero-filled)
+  for (int i = threadIdx.x; i < 64 * (D / 8); i += 128) {
+    const int r = i / (D / 8), ch = i % (D / 8);
+    const bool valid = q0 + r < q_len;
+    const __nv_bfloat16* src = P.q + (size_t)(q_start + (valid ? q0 + r : 0)) * P.ld_q + (size_t)h * D + ch * 8;
+    cp_async16(sq_addr + swz<ROWB>(r, ch), src, valid);
+  }
+  cp_async_commit();
+
+  const int kv_end = min(ctx, prefix + q0 + 64);
+  const int nchunks = (kv_end + 63) / 64;
+  const int* bt = P.block_tables + (size_t)b * P.bt_stride;
+  const size_t head_stride = (size_t)kPage * D * kEl;
+  const size_t page_stride = (size_t)P.num_layers * 2 * KH * head_stride;
+
+  auto issue = [&](int chunk, int stage) {
+    uint8_t* dst = stages + stage * S::kStageB;
+    const uint32_t dk = smem_u32(dst), dv = smem_u32(dst + S::kRawB);
+    constexpr int kPageChunks = kPage * kChunkPerRow;
+    for (int i = threadIdx.x; i < 4 * kPageChunks; i += 128) {
+      const int pg = i / kPageChunks, w = i % kPageChunks;
+      const int page_local = chunk * 4 + pg;
+      const bool valid = page_local * kPage < ctx;
+      const int page = valid ? bt[page_local] : 0;
+      const uint8_t* kp = P.cache + (size_t)page * page_stride + (((size_t)P.layer * 2 + 0) * KH + kvh) * head_stride;
+      const uint8_t* vp = kp + (size_t)KH * head_stride;
+      const int r = pg * kPage + w / kChunkPerRow, ch = w % kChunkPerRow;
+      const uint32_t off = kFp8 ? (uint32_t)(r * D + ch * 16) : swz<ROWB>(r, ch);
+      cp_async16(dk + off, kp + (size_t)w * 16, valid);
+      cp_async16(dv + off, vp + (size_t)w * 16, valid);
+    }
+  };
+
+  issue(0, 0);
+  cp_async_commit();
+  cp_async_wait<1>();
+  __syncthreads();
+
+  // Q fragments for this warp's 16 rows
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+    const int ch = 2 * kk + (lane >> 4);
+    ldsm_x4(sq_addr + swz<ROWB>(row, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  const int qrow0 = q0 + warp * 16 + g;   // query index within the sequence's new tokens
+  const int qpos[2] = {prefix + qrow0, prefix + qrow0 + 8};
+
+  for (int ck = 0; ck < nchunks; ++ck) {
+    const int stage = ck & 1;
+    if (ck + 1 < nchunks) issue(ck + 1, stage ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    uint8_t* kt = stages + stage * S::kStageB;
+    uint8_t* vt = kt + S::kRawB;
+    if (kFp8) {
+      uint8_t* ckb = stages + 2 * S::kStageB;
+      uint8_t* cvb = ckb + S::kTileB;
+      convert_fp8_tile<D>(kt, ckb, 64, threadIdx.x, 128);
+      convert_fp8_tile<D>(vt, cvb, 64, threadIdx.x, 128);
+      __syncthreads();
+      kt = ckb;
+      vt = cvb;
+    }
+    const uint32_t kaddr = smem_u32(kt), vaddr = smem_u32(vt);
+
+    float s[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int nt = 0; nt < 8; nt += 2) {
+        const int j = lane >> 3;
+        const int row = nt * 8 + (lane & 7) + (j >> 1) * 8;
+        const int ch = 2 * kk + (j & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kaddr + swz<ROWB>(row, ch), b0, b1, b2, b3);
+        mma_bf16_16816(s[nt], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
+        mma_bf16_16816(s[nt + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
+      }
+    }
+    const int key0 = ck * 64;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = key0 + nt * 8 + 2 * c + (e & 1);
+        const int r = e >> 1;
+        float v = s[nt][e] * scale_log2;
+        if (key > qpos[r] || key >= ctx) v = -INFINITY;
+        s[nt][e] = v;
+        mx[r] = fmaxf(mx[r], v);
+      }
+    }
+    float alpha[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float mn = fmaxf(m_run[r], mx[r]);
+      alpha[r] = (mn == -INFINITY) ? 1.f : exp2f(m_run[r] - mn);
+      m_run[r] = mn;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = e >> 1;
+        const float pv = (m_run[r] == -INFINITY) ? 0.f : exp2f(s[nt][e] - m_run[r]);
+        s[nt][e] = pv;
+        rs[r] += pv;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+      l_run[r] = l_run[r] * alpha[r] + rs[r];
+    }
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= alpha[0];
+      o[i][1] *= alpha[0];
+      o[i][2] *= alpha[1];
+      o[i][3] *= alpha[1];
+    }
+#pragma unroll
+    for (int kt2 = 0; kt2 < 4; ++kt2) {
+      const uint32_t a0 = pack_bf16x2(s[2 * kt2][0], s[2 * kt2][1]);
+      const uint32_t a1 = pack_bf16x2(s[2 * kt2][2], s[2 * kt2][3]);
+      const uint32_t a2 = pack_bf16x2(s[2 * kt2 + 1][0], s[2 * kt2 + 1][1]);
+      const uint32_t a3 = pack_bf16x2(s[2 * kt2 + 1][2], s[2 * kt2 + 1][3]);
+#pragma unroll
+      for (int nd = 0; nd < D / 8; nd += 2) {
+        const int j = lane >> 3;
+        const int row = kt2 * 16 + (lane & 7) + (j & 1) * 8;
+        const int ch = nd + (j >> 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vaddr + swz<ROWB>(row, ch), b0, b1, b2, b3);
+        mma_bf16_16816(o[nd], a0, a1, a2, a3, b0, b1);
+        mma_bf16_16816(o[nd + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int qi = qrow0 + r * 8;
+    if (qi >= q_len) continue;
+    const float inv = l_run[r] > 0.f ? v_scale / l_run[r] : 0.f;
+    __nv_bfloat16* orow = P.out + (size_t)(q_start + qi) * P.ld_o + (size_t)h * D;
+#pragma unroll
+    for (int nd = 0; nd < D / 8; ++nd)
+      *reinterpret_cast<uint32_t*>(orow + nd * 8 + 2 * c) = pack_bf16x2(o[nd][2 * r] * inv, o[nd][2 * r + 1] * inv);
+  }
+}
+
+// ============================================================== host
+int decode_attention_choose_splits(int B, int KH, int max_pages) {
+  const int sms = device_sm_count();
+  const int ctas = std::max(1, B * KH);
+  int s = (2 * sms + ctas - 1) / ctas;
+  s = std::min(s, std::max(1, (max_pages + 3) / 4));
+  return std::max(1, std::min(s, 128));
+}
+
+size_t decode_attention_scratch_bytes(int B, int Hq, int D, int splits) {
+  if (splits <= 1) return 0;
+  return ((size_t)B * Hq * splits * D + (size_t)B * Hq * splits * 2) * sizeof(float);
+}
+
+template <int D, bool F8>
+static void launch_decode(dim3 grid, const DecodeParams& p, cudaStream_t st) {
+  constexpr int smem = DecodeSmem<D, F8>::kTotal;
+  auto kern = paged_decode_kernel<D, F8>;
+  static bool set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!set[dev & 63]) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set[dev & 63] = true;
+  }
+  kern<<<grid, 128, smem, st>>>(p);
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
+  VRM_REQUIRE(a.D == 64 || a.D == 128, "decode attention: head_dim must be 64 or 128");
+  VRM_REQUIRE(a.KH > 0 && a.Hq % a.KH == 0 && a.Hq / a.KH <= 8, "decode attention: GQA group must be <= 8 heads");
+  VRM_REQUIRE(!a.cache_fp8 || a.kv_scale != nullptr, "decode attention: fp8 cache needs kv_scale");
+  if (a.B <= 0) return;
+  const int G = a.Hq / a.KH;
+  int splits = a.num_splits > 0 ? a.num_splits : decode_attention_choose_splits(a.B, a.KH, a.max_pages);
+  splits = std::min(splits, 128);
+  DecodeParams p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(a.q);
+  p.ld_q = a.ld_q;
+  p.cache = reinterpret_cast<const uint8_t*>(a.cache);
+  p.layer = a.layer;
+  p.num_layers = a.num_layers;
+  p.KH = a.KH;
+  p.G = G;
+  p.block_tables = a.block_tables;
+  p.bt_stride = a.bt_stride;
+  p.context_lens = a.context_lens;
+  p.kv_scale = a.kv_scale;
+  p.sm_scale = a.sm_scale;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  p.ld_o = a.ld_o;
+  p.ws_o = p.ws_ml = nullptr;
+  p.counters = nullptr;
+  if (splits > 1) {
+    const size_t need = decode_attention_scratch_bytes(a.B, a.Hq, a.D, splits);
+    float* ws = a.ws;
+    if (ws == nullptr) {
+      ws = static_cast<float*>(workspace_get(need, st));
+    } else {
+      VRM_REQUIRE(a.ws_bytes >= need, "decode attention: caller scratch too small");
+    }
+    p.ws_o = ws;
+    p.ws_ml = ws + (size_t)a.B * a.Hq * splits * a.D;
+    VRM_REQUIRE((size_t)a.B * a.KH <= 32768, "decode attention: too many (sequence, kv head) groups");
+    // counters: the upper half of the per-device array (GEMM split-K uses the lower half)
+    p.counters = a.counters ? a.counters : tile_counters_get(st) + 32768;
+  }
+  dim3 grid(a.KH, a.B, splits);
+  if (a.D == 128) {
+    if (a.cache_fp8) launch_decode<128, true>(grid, p, st);
+    else launch_decode<128, false>(grid, p, st);
+  } else {
+    if (a.cache_fp8) launch_decode<64, true>(grid, p, st);
+    else launch_decode<64, false>(grid, p, st);
+  }
+}
+
+template <int D, bool F8>
+static void launch_prefill(dim3 grid, const PrefillParams& p, cudaStream_t st) {
+  constexpr int smem = PrefillSmem<D, F8>::kTotal;
+  auto kern = paged_prefill_kernel<D, F8>;
+  static bool set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!set[dev & 63]) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set[dev & 63] = true;
+  }
+  kern<<<grid, 128, smem, st>>>(p);
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
+  VRM_REQUIRE(a.D == 64 || a.D == 128, "prefill attention: head_dim must be 64 or 128");
+  VRM_REQUIRE(a.KH > 0 && a.Hq % a.KH == 0, "prefill attention: heads");
+  VRM_REQUIRE(!a.cache_fp8 || a.kv_scale != nullptr, "prefill attention: fp8 cache needs kv_scale");
+  VRM_REQUIRE(a.ld_q % 8 == 0, "prefill attention: q row stride must be a multiple of 8");
+  if (a.B <= 0 || a.max_q_len <= 0) return;
+  PrefillParams p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(a.q);
+  p.ld_q = a.ld_q;
+  p.cache = reinterpret_cast<const uint8_t*>(a.cache);
+  p.layer = a.layer;
+  p.num_layers = a.num_layers;
+  p.KH = a.KH;
+  p.G = a.Hq / a.KH;
+  p.block_tables = a.block_tables;
+  p.bt_stride = a.bt_stride;
+  p.cu_q = a.cu_q;
+  p.context_lens = a.context_lens;
+  p.kv_scale = a.kv_scale;
+  p.sm_scale = a.sm_scale;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  p.ld_o = a.ld_o;
+  dim3 grid((a.max_q_len + 63) / 64, a.Hq, a.B);
+  if (a.D == 128) {
+    if (a.cache_fp8) launch_prefill<128, true>(grid, p, st);
+    else launch_prefill<128, false>(grid, p, st);
+  } else {
+    if (a.cache_fp8) launch_prefill<64, true>(grid, p, st);
+    else launch_prefill<64, false>(grid, p, st);
+  }
+}
+
+}  // namespace vrm

@@ -1,0 +1,468 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+//   Y[M, N] = X[M, K] @ W[N, K]^T (+ bias[N]) (+ residual[M, N])   (nn.Linear layout)
+//
+// One CTA = 6 warps, warp-specialised:
+//   warp 0      TMA producer: streams K-major 128B-swizzled tiles of both operands
+//               into a STAGES-deep shared-memory ring (mbarrier complete_tx).
+//   warp 1      allocates the TMEM accumulator and issues tcgen05.mma (one thread),
+//               releasing each smem stage with tcgen05.commit -> empty barrier.
+//   warps 2..5  epilogue: tcgen05.ld from TMEM, bias / SiLU*up / residual, bf16 store.
+//
+// Two operand orientations share the kernel:
+//   * kSwapAB = false (prefill, M > 128): MMA-M = tokens, MMA-N = features.
+//   * kSwapAB = true  (decode, M <= 128): MMA-M = 128 weight rows, MMA-N = the few
+//     tokens padded to 16/32/64/128 (TMA zero-fills rows past M).  The 128-lane tensor
+//     core then works on the weight stream, which is what bounds decode.
+// Split-K: when there are too few output tiles to cover the SMs, K is split over
+// gridDim.y.  Each split writes an fp32 partial; the last CTA to finish a tile (tile
+// counter, reset after use) sums the partials in split order (deterministic) and runs
+// the epilogue.  Workspace and counters are persistent per-device scratch.
+//
+// Reference parity: replaces the reference's cuBLAS linear layers on its HF/accelerate
+// path (core/backends.py:1390) and its SIMT NVFP4 GEMV (csrc/fp4_gemv.cu:36-116) for
+// the bf16 case.
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "vrm_common.cuh"
+#include "vrm_host.h"
+#include "vrm_kernels.h"
+
+namespace vrm {
+
+constexpr int kBM = 128;        // MMA M (TMEM lanes)
+constexpr int kBK = 64;         // K elements per stage (128 B of bf16 = one swizzle row)
+constexpr int kUmmaK = 16;      // K per tcgen05.mma kind::f16
+constexpr int kGemmThreads = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kABytes = kBM * kBK * 2;   // 16 KB
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  // full[STAGES], empty[STAGES], tmem_full, then tmem slot + flag
+  static constexpr int kTotal = kBarOffset + (2 * STAGES + 1) * 8 + 16;
+  static constexpr int kAlloc = kTotal + 1024;   // slack for 1024-B alignment
+};
+
+struct EpiParams {
+  __nv_bfloat16* out;
+  int ldo;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual;
+  int M, N;       // logical output rows (tokens) and GEMM columns (weight rows)
+  int epilogue;
+};
+
+// Store one accumulator row segment.  `tok` / `feat0` are output coordinates of the
+// first value; in swap mode the 16 values run over tokens (fixed feature), otherwise
+// over features (fixed token).
+template <bool kSwapAB>
+__device__ __forceinline__ void epi_store(const EpiParams& p, int row_glob, int col0, const float (&v)[16]) {
+  if (p.epilogue == kEpiSiluMul) {
+    // pairs (gate, up) of adjacent weight rows -> one output column
+    if (!kSwapAB) {
+      const int m = row_glob;
+      if (m >= p.M) return;
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        const int n = col0 + j;
+        if (n + 1 < p.N) {
+          float g = v[j], u = v[j + 1];
+          if (p.bias) {
+            g += __bfloat162float(p.bias[n]);
+            u += __bfloat162float(p.bias[n + 1]);
+          }
+          const float s = g / (1.f + __expf(-g));
+          p.out[(size_t)m * p.ldo + (n >> 1)] = __float2bfloat16(s * u);
+        }
+      }
+    } else {
+      // feature pairs live in adjacent lanes: exchange with the neighbour
+      const int n = row_glob;
+      const float bn = (p.bias && n < p.N) ? __bfloat162float(p.bias[n]) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float mine = v[j] + bn;
+        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+        const int m = col0 + j;
+        if ((n & 1) == 0 && n + 1 < p.N && m < p.M) {
+          const float s = mine / (1.f + __expf(-mine));
+          p.out[(size_t)m * p.ldo + (n >> 1)] = __float2bfloat16(s * other);
+        }
+      }
+    }
+    return;
+  }
+  if (!kSwapAB) {
+    const int m = row_glob;
+    if (m >= p.M) return;
+    const int n0 = col0;
+    if (n0 + 16 <= p.N && (p.ldo & 7) == 0) {
+      float t[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) t[j] = v[j];
+      if (p.bias) {
+        const uint4 b0 = *reinterpret_cast<const uint4*>(p.bias + n0);
+        const uint4 b1 = *reinterpret_cast<const uint4*>(p.bias + n0 + 8);
+        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(&b0);
+        const uint32_t* q1 = reinterpret_cast<const uint32_t*>(&b1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          t[2 * j] += bf16_lo(q0[j]);
+          t[2 * j + 1] += bf16_hi(q0[j]);
+          t[8 + 2 * j] += bf16_lo(q1[j]);
+          t[8 + 2 * j + 1] += bf16_hi(q1[j]);
+        }
+      }
+      if (p.residual) {
+        const uint4 r0 = *reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.ldo + n0);
+        const uint4 r1 = *reinterpret_cast<const uint4*>(p.residual + (size_t)m * p.ldo + n0 + 8);
+        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(&r0);
+        const uint32_t* q1 = reinterpret_cast<const uint32_t*>(&r1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          t[2 * j] += bf16_lo(q0[j]);
+          t[2 * j + 1] += bf16_hi(q0[j]);
+          t[8 + 2 * j] += bf16_lo(q1[j]);
+          t[8 + 2 * j + 1] += bf16_hi(q1[j]);
+        }
+      }
+      uint4 w0, w1;
+      uint32_t* p0 = reinterpret_cast<uint32_t*>(&w0);
+      uint32_t* p1 = reinterpret_cast<uint32_t*>(&w1);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        p0[j] = pack_bf16x2(t[2 * j], t[2 * j + 1]);
+        p1[j] = pack_bf16x2(t[8 + 2 * j], t[8 + 2 * j + 1]);
+      }
+      *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ldo + n0) = w0;
+      *reinterpret_cast<uint4*>(p.out + (size_t)m * p.ldo + n0 + 8) = w1;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + j;
+        if (n < p.N) {
+          float t = v[j];
+          if (p.bias) t += __bfloat162float(p.bias[n]);
+          if (p.residual) t += __bfloat162float(p.residual[(size_t)m * p.ldo + n]);
+          p.out[(size_t)m * p.ldo + n] = __float2bfloat16(t);
+        }
+      }
+    }
+  } else {
+    const int n = row_glob;
+    if (n >= p.N) return;
+    const float bn = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int m = col0 + j;
+      if (m < p.M) {
+        float t = v[j] + bn;
+        if (p.residual) t += __bfloat162float(p.residual[(size_t)m * p.ldo + n]);
+        p.out[(size_t)m * p.ldo + n] = __float2bfloat16(t);
+      }
+    }
+  }
+}
+
+template <int BN, int STAGES, bool kSwapAB>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters, int K,
+                        int num_a_tiles, int k_tiles_per_split, uint32_t* __restrict__ err) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tmem_full = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  uint32_t* flag_slot = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int a_tile = blockIdx.x % num_a_tiles;
+  const int b_tile = blockIdx.x / num_a_tiles;
+  const int split = blockIdx.y;
+  const int num_splits = gridDim.y;
+  const int total_k_tiles = (K + kBK - 1) / kBK;
+  const int kt_begin = split * k_tiles_per_split;
+  const int kt_end = min(total_k_tiles, kt_begin + k_tiles_per_split);
+  const int num_k = max(0, kt_end - kt_begin);
+
+  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer
+    const uint64_t pol_a = kSwapAB ? policy_evict_first() : policy_evict_last();
+    const uint64_t pol_b = kSwapAB ? policy_evict_last() : policy_evict_first();
+    int issued = 0;
+    for (int i = 0; i < num_k; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1;
+      if (!mbar_wait(&empty_bar[s], ph ^ 1, err)) break;
+      uint8_t* sa = smem + s * L::kStageBytes;
+      uint8_t* sb = sa + L::kABytes;
+      const int kc = (kt_begin + i) * kBK;
+      mbar_arrive_expect_tx(&full_bar[s], L::kStageBytes);
+      tma_load_2d(sa, &map_a, &full_bar[s], kc, a_tile * kBM, pol_a);
+      tma_load_2d(sb, &map_b, &full_bar[s], kc, b_tile * BN, pol_b);
+      ++issued;
+    }
+    // Drain: none of our bulk copies may still be in flight when the CTA exits.
+    const int first = issued > STAGES ? issued - STAGES : 0;
+    for (int j = first; j < issued; ++j) mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1, err);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    constexpr uint32_t idesc = make_idesc_bf16(kBM, BN);
+    for (int i = 0; i < num_k; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1;
+      if (!mbar_wait(&full_bar[s], ph, err)) break;
+      tc_fence_after();
+      const uint32_t sa = smem_u32(smem + s * L::kStageBytes);
+      const uint32_t sb = sa + L::kABytes;
+      const uint64_t da = make_sw128_desc(sa);
+      const uint64_t db = make_sw128_desc(sb);
+#pragma unroll
+      for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+        // advance 32 B (16 bf16) along K inside the 128 B swizzle row
+        umma_f16(tmem_base, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(&empty_bar[s]);
+    }
+    umma_commit(tmem_full);   // always: tells the epilogue every MMA has retired
+  } else if (warp >= 2) {
+    // ---------------- epilogue (128 threads, one TMEM lane each)
+    const int lane_base = 32 * (warp & 3);
+    const int row = lane_base + lane;   // TMEM lane == MMA row
+    const bool ok = mbar_wait(tmem_full, 0, err);
+    tc_fence_after();
+
+    // !swap: row -> token, columns -> features;  swap: row -> feature, columns -> tokens
+    const int r_glob = a_tile * kBM + row;
+    const int c_base = b_tile * BN;
+    const uint32_t t_row = tmem_base + ((uint32_t)lane_base << 16);
+    const bool direct = (num_splits == 1);
+    const size_t tile_id = blockIdx.x;
+    float* ws_tile = workspace + ((size_t)split * gridDim.x + tile_id) * (size_t)(kBM * BN);
+
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t r[16];
+      tmem_ld_32x32b_x16(t_row + c0, r);
+      tmem_wait_ld();
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = (ok && num_k > 0) ? __uint_as_float(r[j]) : 0.f;
+      if (direct) {
+        epi_store<kSwapAB>(ep, r_glob, c_base + c0, v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ws_tile[(size_t)(c0 + j) * kBM + row] = v[j];   // coalesced
+      }
+    }
+
+    if (!direct) {
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        const uint32_t prev = atomicAdd(&tile_counters[tile_id], 1u);
+        *flag_slot = (prev == (uint32_t)(num_splits - 1)) ? 1u : 0u;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*flag_slot) {
+        __threadfence();
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0.f;
+          for (int s = 0; s < num_splits; ++s) {
+            const float* src = workspace + ((size_t)s * gridDim.x + tile_id) * (size_t)(kBM * BN);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (size_t)(c0 + j) * kBM + row);
+          }
+          epi_store<kSwapAB>(ep, r_glob, c_base + c0, v);
+        }
+        if (threadIdx.x == 64) tile_counters[tile_id] = 0u;   // ready for the next launch
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+namespace {
+
+struct MapKey {
+  uint64_t ptr;
+  int64_t rows, cols, ld;
+  int box_rows;
+  int dev;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows && dev == o.dev;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<uint64_t>()(k.ptr);
+    h ^= std::hash<int64_t>()(k.rows * 1315423911ll + k.cols * 2654435761ll + k.ld) + 0x9e3779b9 + (h << 6) + (h >> 2);
+    return h ^ (size_t)(k.box_rows * 31 + k.dev);
+  }
+};
+
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_map_cache;
+
+}  // namespace
+
+// K-major bf16 matrix [rows, cols] with row stride ld (elements); box = box_rows x 64.
+CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  MapKey key{reinterpret_cast<uint64_t>(ptr), rows, cols, ld, box_rows, dev};
+  {
+    std::lock_guard<std::mutex> g(g_map_mu);
+    auto it = g_map_cache.find(key);
+    if (it != g_map_cache.end()) return it->second;
+  }
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_tensor_map()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  VRM_REQUIRE(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ", rows " +
+                                     std::to_string(rows) + ", cols " + std::to_string(cols) + ")");
+  std::lock_guard<std::mutex> g(g_map_mu);
+  if (g_map_cache.size() > 16384) g_map_cache.clear();
+  g_map_cache.emplace(key, map);
+  return map;
+}
+
+template <int BN, int STAGES, bool kSwap>
+static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const EpiParams& ep, int K, int a_tiles,
+                        int b_tiles, int splits, int ktps, cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES>;
+  auto kern = gemm_bf16_tc_kernel<BN, STAGES, kSwap>;
+  static int attr_dev_mask = 0;   // per-device "attribute set" bits (devices < 32)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
+    attr_dev_mask |= 1 << (dev & 31);
+  }
+  float* ws = nullptr;
+  uint32_t* counters = nullptr;
+  if (splits > 1) {
+    const size_t need = (size_t)splits * a_tiles * b_tiles * kBM * BN * sizeof(float);
+    ws = static_cast<float*>(workspace_get(need, stream));
+    VRM_REQUIRE((size_t)a_tiles * b_tiles <= 32768, "too many split-K tiles");
+    counters = tile_counters_get(stream);
+  }
+  dim3 grid(a_tiles * b_tiles, splits);
+  kern<<<grid, kGemmThreads, L::kAlloc, stream>>>(ma, mb, ep, ws, counters, K, a_tiles, ktps, error_word());
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+// Split count such that tiles * splits covers the SMs with >= min_k K-tiles per split.
+static void choose_split(int tiles, int k_tiles, int min_k, int* splits, int* ktps) {
+  const int sms = device_sm_count();
+  int s = 1;
+  if (tiles < sms) {
+    s = (sms + tiles - 1) / tiles;
+    s = std::min(s, std::max(1, k_tiles / min_k));
+  }
+  int per = (k_tiles + s - 1) / s;
+  s = (k_tiles + per - 1) / per;
+  *splits = s;
+  *ktps = per;
+}
+
+static void force_split(int force, int k_tiles, int* splits, int* ktps) {
+  int s = std::max(1, std::min(force, k_tiles));
+  int per = (k_tiles + s - 1) / s;
+  *splits = (k_tiles + per - 1) / per;
+  *ktps = per;
+}
+
+void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
+  VRM_REQUIRE(a.K % 8 == 0 && a.ldx % 8 == 0 && a.ldw % 8 == 0, "gemm: K and row strides must be multiples of 8");
+  VRM_REQUIRE((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0,
+              "gemm: operands must be 16-byte aligned");
+  VRM_REQUIRE(a.epilogue != kEpiSiluMul || (a.N % 2 == 0 && a.residual == nullptr), "gemm: silu_mul epilogue");
+  if (a.M <= 0 || a.N <= 0) return;
+  EpiParams ep;
+  ep.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  ep.ldo = (int)a.ldo;
+  ep.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  ep.residual = reinterpret_cast<const __nv_bfloat16*>(a.residual);
+  ep.M = a.M;
+  ep.N = a.N;
+  ep.epilogue = a.epilogue;
+  const int k_tiles = (a.K + kBK - 1) / kBK;
+
+  if (a.M <= 128) {
+    // decode: swap A/B so the weight rows fill the 128 TMEM lanes
+    const int BN = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
+    const int a_tiles = (a.N + kBM - 1) / kBM;
+    int splits, ktps;
+    choose_split(a_tiles, k_tiles, 4, &splits, &ktps);
+    if (a.force_splits > 0) force_split(a.force_splits, k_tiles, &splits, &ktps);
+    const CUtensorMap ma = make_kmajor_map(a.w, a.N, a.K, a.ldw, kBM);
+    const CUtensorMap mb = make_kmajor_map(a.x, a.M, a.K, a.ldx, BN);
+    switch (BN) {
+      case 16: launch_gemm<16, 8, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
+      case 32: launch_gemm<32, 8, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
+      case 64: launch_gemm<64, 6, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
+      default: launch_gemm<128, 5, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
+    }
+  } else {
+    constexpr int BN = 128;
+    const int a_tiles = (a.M + kBM - 1) / kBM;
+    const int b_tiles = (a.N + BN - 1) / BN;
+    int splits = 1, ktps = k_tiles;
+    if (a_tiles * b_tiles * 2 <= device_sm_count()) choose_split(a_tiles * b_tiles, k_tiles, 8, &splits, &ktps);
+    if (a.force_splits > 0) force_split(a.force_splits, k_tiles, &splits, &ktps);
+    const CUtensorMap ma = make_kmajor_map(a.x, a.M, a.K, a.ldx, kBM);
+    const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, BN);
+    launch_gemm<BN, 6, false>(ma, mb, ep, a.K, a_tiles, b_tiles, splits, ktps, stream);
+  }
+}
+
+}  // namespace vrm

@@ -1,0 +1,235 @@
+// Token selection over bf16 logits [B, V], one CTA (1024 threads) per row.
+//
+//   greedy:   argmax (lowest index on ties)
+//   sampling: temperature, top-k and top-p (nucleus) with exact thresholds found by
+//             two-digit radix select over the 16-bit order keys of the bf16 logits
+//             (count histograms for top-k, probability-mass histograms for top-p),
+//             then an exact draw from the renormalised kept set with the Gumbel-max
+//             trick: argmax_i (z_i + G_i), G_i = -log(-log(U_i)), U_i from a
+//             counter-based hash of (seed, row, step, i).  No sort, no host sync,
+//             fixed launch shape: replayable inside a captured decode graph.
+//
+// Reference parity: core/triton_sampling.py:55-206 (Triton softmax + torch.topk +
+// torch.multinomial), core/turbo_engine.py:605-638 (argmax fused into the graph).
+#include "vrm_common.cuh"
+#include "vrm_host.h"
+#include "vrm_kernels.h"
+
+namespace vrm {
+
+constexpr int kSampThreads = 1024;
+
+// Monotone 16-bit key of a bf16 value: larger value -> larger key.
+__device__ __forceinline__ uint32_t bf16_key(uint16_t bits) {
+  return (bits & 0x8000u) ? (uint32_t)(~bits & 0xFFFFu) : (uint32_t)(bits | 0x8000u);
+}
+
+// splitmix64 finaliser (Steele, Lea, Flood 2014) -> uniform in (0, 1)
+__device__ __forceinline__ float hash_uniform(uint64_t seed, uint64_t row, uint64_t step, uint64_t i) {
+  uint64_t z = seed ^ (row * 0x9E3779B97F4A7C15ull) ^ (step * 0xD1B54A32D192ED03ull) ^ (i * 0xBF58476D1CE4E5B9ull);
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= (z >> 31);
+  return ((float)(z >> 40) + 0.5f) * (1.0f / 16777216.0f);
+}
+
+struct ArgBest {
+  float v;
+  int i;
+};
+__device__ __forceinline__ ArgBest better(ArgBest a, ArgBest b) {
+  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+  return a;
+}
+
+__device__ ArgBest block_argmax(ArgBest a, ArgBest* sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgBest b{__shfl_xor_sync(0xffffffffu, a.v, o), __shfl_xor_sync(0xffffffffu, a.i, o)};
+    a = better(a, b);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = a;
+  __syncthreads();
+  if (w == 0) {
+    a = (l < (int)(blockDim.x >> 5)) ? sh[l] : ArgBest{-INFINITY, 0x7fffffff};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ArgBest b{__shfl_xor_sync(0xffffffffu, a.v, o), __shfl_xor_sync(0xffffffffu, a.i, o)};
+      a = better(a, b);
+    }
+    if (l == 0) sh[0] = a;
+  }
+  __syncthreads();
+  return sh[0];
+}
+
+__device__ float block_sum(float v, float* sh) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = (l < (int)(blockDim.x >> 5)) ? sh[l] : 0.f;
+    v = warp_sum(v);
+    if (l == 0) sh[0] = v;
+  }
+  __syncthreads();
+  return sh[0];
+}
+
+__global__ void __launch_bounds__(kSampThreads)
+    argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V, int* __restrict__ out) {
+  __shared__ ArgBest sh[32];
+  const int row = blockIdx.x;
+  const __nv_bfloat16* x = logits + (size_t)row * ld;
+  ArgBest best{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgBest{__bfloat162float(x[i]), i});
+  best = block_argmax(best, sh);
+  if (threadIdx.x == 0) out[row] = best.i;
+}
+
+// Among elements with key >= floor_key whose high digit matches `pref`, finds the
+// 8-bit digit at `shift` where the weight accumulated from the top reaches `target`.
+// Weights are counts (mass = false) or exp((x - M) / T) (mass = true).
+__device__ void radix_digit(const __nv_bfloat16* __restrict__ x, int V, int shift, uint32_t pref_mask, uint32_t pref,
+                            uint32_t floor_key, bool mass, float M, float invT, float target, float* hist,
+                            uint32_t* out_digit, float* out_above) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0.f;
+  __syncthreads();
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const uint16_t bits = __bfloat16_as_ushort(x[i]);
+    const uint32_t k = bf16_key(bits);
+    if (k < floor_key || (k & pref_mask) != pref) continue;
+    const float w = mass ? __expf((__bfloat162float(x[i]) - M) * invT) : 1.f;
+    atomicAdd(&hist[(k >> shift) & 0xFF], w);
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // scan the 256 bins from the top: lane l owns bins 255-8l .. 255-8l-7
+    const int l = threadIdx.x;
+    float loc[8];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      loc[j] = hist[255 - 8 * l - j];
+      s += loc[j];
+    }
+    float incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (l >= o) incl += t;
+    }
+    float run = incl - s;   // weight strictly above this lane's bins
+    int found = -1;
+    float above = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (found < 0 && run + loc[j] >= target) {
+        found = 255 - 8 * l - j;
+        above = run;
+      }
+      run += loc[j];
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, found >= 0);
+    if (m == 0u) {
+      if (l == 0) {
+        *out_digit = 0u;   // target not reached: keep everything in this prefix
+        *out_above = 0.f;
+      }
+    } else {
+      const int first = __ffs(m) - 1;
+      const int d = __shfl_sync(0xffffffffu, found, first);
+      const float ab = __shfl_sync(0xffffffffu, above, first);
+      if (l == 0) {
+        *out_digit = (uint32_t)d;
+        *out_above = ab;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kSampThreads)
+    sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temperature,
+                  const int* __restrict__ top_k, const float* __restrict__ top_p, uint64_t seed,
+                  const int* __restrict__ steps, int* __restrict__ out) {
+  __shared__ ArgBest sh[32];
+  __shared__ float shf[32];
+  __shared__ float hist[256];
+  __shared__ uint32_t s_digit;
+  __shared__ float s_above;
+  const int row = blockIdx.x;
+  const __nv_bfloat16* x = logits + (size_t)row * ld;
+  const float T = temperature ? temperature[row] : 0.f;
+
+  ArgBest best{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgBest{__bfloat162float(x[i]), i});
+  best = block_argmax(best, sh);
+  if (!(T > 0.f)) {
+    if (threadIdx.x == 0) out[row] = best.i;
+    return;
+  }
+  const float M = best.v;
+  const float invT = 1.f / T;
+  const int k = top_k ? top_k[row] : 0;
+  const float p = top_p ? top_p[row] : 1.f;
+
+  // ---- top-k threshold: count radix select over the two bytes of the 16-bit key
+  uint32_t floor_key = 0u;
+  if (k > 0 && k < V) {
+    radix_digit(x, V, 8, 0u, 0u, 0u, false, M, invT, (float)k, hist, &s_digit, &s_above);
+    const uint32_t hi = s_digit;
+    const float need = (float)k - s_above;
+    radix_digit(x, V, 0, 0xFF00u, hi << 8, 0u, false, M, invT, need, hist, &s_digit, &s_above);
+    floor_key = (hi << 8) | s_digit;
+  }
+  // ---- top-p threshold: mass radix select inside the top-k set
+  if (p < 1.f) {
+    float z = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const uint32_t kk = bf16_key(__bfloat16_as_ushort(x[i]));
+      if (kk >= floor_key) z += __expf((__bfloat162float(x[i]) - M) * invT);
+    }
+    z = block_sum(z, shf);
+    const float target = fmaxf(p, 0.f) * z;
+    radix_digit(x, V, 8, 0u, 0u, floor_key, true, M, invT, target, hist, &s_digit, &s_above);
+    const uint32_t hi = s_digit;
+    const float need = target - s_above;
+    radix_digit(x, V, 0, 0xFF00u, hi << 8, floor_key, true, M, invT, need, hist, &s_digit, &s_above);
+    const uint32_t pk = (hi << 8) | s_digit;
+    floor_key = floor_key > pk ? floor_key : pk;
+  }
+  // ---- Gumbel-max draw over the kept set
+  const uint64_t step = steps ? (uint64_t)steps[row] : 0ull;
+  ArgBest gb{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const uint16_t bits = __bfloat16_as_ushort(x[i]);
+    if (bf16_key(bits) < floor_key) continue;
+    const float u = hash_uniform(seed, (uint64_t)row, step, (uint64_t)i);
+    const float gum = -logf(-logf(u));
+    gb = better(gb, ArgBest{(__bfloat162float(x[i]) - M) * invT + gum, i});
+  }
+  gb = block_argmax(gb, sh);
+  if (threadIdx.x == 0) out[row] = gb.i < V ? gb.i : best.i;
+}
+
+void argmax_rows(const void* logits, int64_t ld, int B, int V, int* out, cudaStream_t st) {
+  if (B <= 0) return;
+  argmax_kernel<<<B, kSampThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(logits), ld, V, out);
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+void sample_rows(const void* logits, int64_t ld, int B, int V, const float* temperature, const int* top_k,
+                 const float* top_p, uint64_t seed, const int* steps, int* out, cudaStream_t st) {
+  if (B <= 0) return;
+  sample_kernel<<<B, kSampThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(logits), ld, V, temperature, top_k,
+                                            top_p, seed, steps, out);
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace vrm

@@ -1,0 +1,343 @@
+// PyTorch bindings (module vramancer_b200._C): shape/dtype checks around the raw
+// launchers of vrm_kernels.h.  Every op runs on the current CUDA stream.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "vrm_host.h"
+#include "vrm_kernels.h"
+
+namespace {
+
+using torch::Tensor;
+using OptT = c10::optional<Tensor>;
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream(); }
+
+bool has(const OptT& t) { return t.has_value() && t->defined(); }
+
+void check_bf16_2d(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, ": must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, ": must be bf16");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, ": must be 2-D with unit inner stride");
+}
+
+bool is_fp8_cache(const Tensor& cache) {
+  return cache.scalar_type() == torch::kFloat8_e4m3fn || cache.scalar_type() == torch::kUInt8;
+}
+
+void check_cache(const Tensor& cache) {
+  TORCH_CHECK(cache.is_cuda() && cache.dim() == 6 && cache.is_contiguous(),
+              "kv cache must be a contiguous [pages, layers, 2, kv_heads, page_size, head_dim] CUDA tensor");
+  TORCH_CHECK(cache.size(2) == 2, "kv cache dim 2 must be 2 (k, v)");
+  TORCH_CHECK(is_fp8_cache(cache) || cache.scalar_type() == torch::kBFloat16, "kv cache dtype must be bf16 or fp8");
+}
+
+// ---------------------------------------------------------------- GEMM
+void gemm_out(const Tensor& x, const Tensor& w, const OptT& bias, Tensor& out, int64_t force_splits, int64_t epilogue,
+              const OptT& residual) {
+  check_bf16_2d(x, "gemm x");
+  check_bf16_2d(w, "gemm w");
+  check_bf16_2d(out, "gemm out");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K, "gemm: K mismatch (", K, " vs ", w.size(1), ")");
+  const int64_t n_out = epilogue == vrm::kEpiSiluMul ? N / 2 : N;
+  TORCH_CHECK(out.size(0) == M && out.size(1) == n_out, "gemm: out must be [", M, ", ", n_out, "]");
+  vrm::GemmArgs a;
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.w = w.data_ptr();
+  a.ldw = w.stride(0);
+  if (has(bias)) {
+    TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->is_contiguous() && bias->numel() == N,
+                "gemm: bias must be contiguous bf16 [N]");
+    a.bias = bias->data_ptr();
+  }
+  if (has(residual)) {
+    check_bf16_2d(*residual, "gemm residual");
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N && residual->stride(0) == out.stride(0),
+                "gemm: residual must match out");
+    a.residual = residual->data_ptr();
+  }
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.force_splits = (int)force_splits;
+  a.epilogue = (int)epilogue;
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::gemm_bf16(a, cur_stream());
+}
+
+Tensor gemm(const Tensor& x, const Tensor& w, const OptT& bias, int64_t force_splits, int64_t epilogue) {
+  const int64_t n_out = epilogue == vrm::kEpiSiluMul ? w.size(0) / 2 : w.size(0);
+  auto out = torch::empty({x.size(0), n_out}, x.options());
+  gemm_out(x, w, bias, out, force_splits, epilogue, c10::nullopt);
+  return out;
+}
+
+// ---------------------------------------------------------------- norms
+void rmsnorm(const Tensor& x, const OptT& residual, const Tensor& w, Tensor& out, double eps) {
+  check_bf16_2d(x, "rmsnorm x");
+  check_bf16_2d(out, "rmsnorm out");
+  TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.is_contiguous() && w.numel() == x.size(1), "rmsnorm: weight");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "rmsnorm: row strides must be multiples of 8");
+  void* rp = nullptr;
+  if (has(residual)) {
+    TORCH_CHECK(residual->is_contiguous() && residual->sizes() == x.sizes() &&
+                    residual->scalar_type() == torch::kBFloat16,
+                "rmsnorm: residual must be contiguous bf16 like x");
+    rp = residual->data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::rmsnorm(x.data_ptr(), x.stride(0), rp, w.data_ptr(), out.data_ptr(), out.stride(0), (int)x.size(0),
+               (int)x.size(1), (float)eps, cur_stream());
+}
+
+void layernorm(const Tensor& x, const OptT& residual, const Tensor& w, const Tensor& b, Tensor& out, double eps) {
+  check_bf16_2d(x, "layernorm x");
+  check_bf16_2d(out, "layernorm out");
+  TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.is_contiguous() && w.numel() == x.size(1), "layernorm: weight");
+  TORCH_CHECK(b.scalar_type() == torch::kBFloat16 && b.is_contiguous() && b.numel() == x.size(1), "layernorm: bias");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "layernorm: row strides must be multiples of 8");
+  void* rp = nullptr;
+  if (has(residual)) {
+    TORCH_CHECK(residual->is_contiguous() && residual->sizes() == x.sizes() &&
+                    residual->scalar_type() == torch::kBFloat16,
+                "layernorm: residual must be contiguous bf16 like x");
+    rp = residual->data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::layernorm(x.data_ptr(), x.stride(0), rp, w.data_ptr(), b.data_ptr(), out.data_ptr(), out.stride(0),
+                 (int)x.size(0), (int)x.size(1), (float)eps, cur_stream());
+}
+
+// ---------------------------------------------------------------- rope + kv write
+void rope_kv_write(Tensor& qkv, const OptT& positions, const OptT& cos_sin, Tensor& cache, const OptT& slot_mapping,
+                   const OptT& kv_scale, int64_t layer, int64_t Hq, int64_t KH, int64_t D) {
+  check_bf16_2d(qkv, "rope qkv");
+  TORCH_CHECK(qkv.size(1) == (Hq + 2 * KH) * D, "rope: qkv width must be (Hq + 2 KH) * D");
+  check_cache(cache);
+  TORCH_CHECK(cache.size(3) == KH && cache.size(5) == D, "rope: cache kv_heads/head_dim mismatch");
+  TORCH_CHECK(layer >= 0 && layer < cache.size(1), "rope: layer out of range");
+  vrm::RopeKvArgs a;
+  a.qkv = qkv.data_ptr();
+  a.ld_qkv = qkv.stride(0);
+  a.T = (int)qkv.size(0);
+  a.Hq = (int)Hq;
+  a.KH = (int)KH;
+  a.D = (int)D;
+  if (has(cos_sin)) {
+    TORCH_CHECK(has(positions) && positions->scalar_type() == torch::kInt32 && positions->numel() >= a.T,
+                "rope: int32 positions required");
+    TORCH_CHECK(cos_sin->scalar_type() == torch::kFloat32 && cos_sin->is_contiguous() && cos_sin->dim() == 2,
+                "rope: cos_sin must be contiguous fp32 [max_pos, rot_dim]");
+    TORCH_CHECK(cos_sin->size(1) <= D && cos_sin->size(1) % 2 == 0, "rope: rot_dim");
+    a.positions = positions->data_ptr<int>();
+    a.cos_sin = cos_sin->data_ptr<float>();
+    a.rot_dim = (int)cos_sin->size(1);
+  }
+  a.cache = cache.data_ptr();
+  a.cache_fp8 = is_fp8_cache(cache);
+  a.num_layers = (int)cache.size(1);
+  a.layer = (int)layer;
+  a.page_size = (int)cache.size(4);
+  if (has(slot_mapping)) {
+    TORCH_CHECK(slot_mapping->scalar_type() == torch::kInt32 && slot_mapping->numel() >= a.T, "rope: int32 slots");
+    a.slot_mapping = slot_mapping->data_ptr<int>();
+  }
+  if (has(kv_scale)) {
+    TORCH_CHECK(kv_scale->scalar_type() == torch::kFloat32 && kv_scale->is_contiguous() &&
+                    kv_scale->numel() == cache.size(1) * 2 * KH,
+                "rope: kv_scale must be fp32 [layers, 2, kv_heads]");
+    a.kv_scale = kv_scale->data_ptr<float>();
+  }
+  TORCH_CHECK(!a.cache_fp8 || a.kv_scale, "rope: fp8 cache needs kv_scale");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  vrm::rope_kv_write(a, cur_stream());
+}
+
+// ---------------------------------------------------------------- elementwise
+void silu_mul(const Tensor& x, Tensor& out) {
+  check_bf16_2d(x, "silu_mul x");
+  check_bf16_2d(out, "silu_mul out");
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) * 2 == x.size(1), "silu_mul: out must be [T, I] for x [T, 2I]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::silu_mul(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0), (int)x.size(0), (int)out.size(1),
+                cur_stream());
+}
+
+void gelu_tanh_(Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.is_contiguous(), "gelu: contiguous bf16");
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::gelu_tanh(x.data_ptr(), x.numel(), cur_stream());
+}
+
+void embedding(const Tensor& ids, const Tensor& table, const OptT& pos, const OptT& pos_table, Tensor& out) {
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == torch::kInt32 && ids.is_contiguous(), "embedding: int32 ids");
+  TORCH_CHECK(table.scalar_type() == torch::kBFloat16 && table.is_contiguous() && table.dim() == 2, "embedding: table");
+  TORCH_CHECK(out.is_contiguous() && out.size(0) == ids.numel() && out.size(1) == table.size(1), "embedding: out");
+  const int* pp = nullptr;
+  const void* pt = nullptr;
+  if (has(pos_table)) {
+    TORCH_CHECK(has(pos) && pos->scalar_type() == torch::kInt32 && pos->is_contiguous(), "embedding: int32 positions");
+    TORCH_CHECK(pos_table->scalar_type() == torch::kBFloat16 && pos_table->is_contiguous(), "embedding: pos table");
+    pp = pos->data_ptr<int>();
+    pt = pos_table->data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(ids.device());
+  vrm::embedding(ids.data_ptr<int>(), table.data_ptr(), pp, pt, out.data_ptr(), (int)ids.numel(), (int)table.size(1),
+                 cur_stream());
+}
+
+void add_(Tensor& a, const Tensor& b) {
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && a.numel() == b.numel() &&
+                  a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16,
+              "add_: contiguous bf16 of equal size");
+  const c10::cuda::CUDAGuard guard(a.device());
+  vrm::add_inplace(a.data_ptr(), b.data_ptr(), a.numel(), cur_stream());
+}
+
+// ---------------------------------------------------------------- attention
+void attn_decode(const Tensor& q, const Tensor& cache, int64_t layer, const Tensor& block_tables,
+                 const Tensor& context_lens, const OptT& kv_scale, double sm_scale, Tensor& out, int64_t num_splits,
+                 int64_t num_q_heads) {
+  check_cache(cache);
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 2 && q.stride(1) == 1 &&
+                  q.stride(0) % 2 == 0,
+              "decode: q must be bf16 [B, >= Hq*D] with unit inner stride");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.dim() == 2 && out.stride(1) == 1, "decode: out");
+  TORCH_CHECK(block_tables.scalar_type() == torch::kInt32 && block_tables.dim() == 2 && block_tables.stride(1) == 1,
+              "decode: block_tables must be int32 [B, max_pages]");
+  TORCH_CHECK(context_lens.scalar_type() == torch::kInt32 && context_lens.is_contiguous(), "decode: int32 context_lens");
+  const int64_t B = q.size(0);
+  TORCH_CHECK(block_tables.size(0) >= B && context_lens.numel() >= B && out.size(0) >= B, "decode: batch sizes");
+  TORCH_CHECK(layer >= 0 && layer < cache.size(1), "decode: layer out of range");
+  vrm::DecodeAttnArgs a;
+  a.q = q.data_ptr();
+  a.ld_q = q.stride(0);
+  a.cache = cache.data_ptr();
+  a.cache_fp8 = is_fp8_cache(cache);
+  a.num_layers = (int)cache.size(1);
+  a.layer = (int)layer;
+  a.KH = (int)cache.size(3);
+  a.D = (int)cache.size(5);
+  a.Hq = (int)num_q_heads;
+  TORCH_CHECK(q.size(1) >= a.Hq * a.D && out.size(1) >= a.Hq * a.D, "decode: q/out width");
+  a.block_tables = block_tables.data_ptr<int>();
+  a.bt_stride = (int)block_tables.stride(0);
+  a.context_lens = context_lens.data_ptr<int>();
+  if (has(kv_scale)) {
+    TORCH_CHECK(kv_scale->scalar_type() == torch::kFloat32 && kv_scale->is_contiguous(), "decode: fp32 kv_scale");
+    a.kv_scale = kv_scale->data_ptr<float>();
+  }
+  a.sm_scale = (float)sm_scale;
+  a.out = out.data_ptr();
+  a.ld_o = out.stride(0);
+  a.B = (int)B;
+  a.max_pages = (int)block_tables.size(1);
+  a.num_splits = (int)num_splits;
+  const c10::cuda::CUDAGuard guard(q.device());
+  vrm::paged_attention_decode(a, cur_stream());
+}
+
+void attn_prefill(const Tensor& q, const Tensor& cache, int64_t layer, const Tensor& block_tables, const Tensor& cu_q,
+                  const Tensor& context_lens, const OptT& kv_scale, double sm_scale, Tensor& out, int64_t max_q_len,
+                  int64_t num_q_heads) {
+  check_cache(cache);
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 2 && q.stride(1) == 1, "prefill: q");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.dim() == 2 && out.stride(1) == 1, "prefill: out");
+  TORCH_CHECK(cu_q.scalar_type() == torch::kInt32 && cu_q.is_contiguous() && context_lens.scalar_type() == torch::kInt32 &&
+                  block_tables.scalar_type() == torch::kInt32 && block_tables.stride(1) == 1,
+              "prefill: int32 metadata");
+  TORCH_CHECK(layer >= 0 && layer < cache.size(1), "prefill: layer out of range");
+  vrm::PrefillAttnArgs a;
+  a.q = q.data_ptr();
+  a.ld_q = q.stride(0);
+  a.cache = cache.data_ptr();
+  a.cache_fp8 = is_fp8_cache(cache);
+  a.num_layers = (int)cache.size(1);
+  a.layer = (int)layer;
+  a.KH = (int)cache.size(3);
+  a.D = (int)cache.size(5);
+  a.Hq = (int)num_q_heads;
+  a.block_tables = block_tables.data_ptr<int>();
+  a.bt_stride = (int)block_tables.stride(0);
+  a.cu_q = cu_q.data_ptr<int>();
+  a.context_lens = context_lens.data_ptr<int>();
+  if (has(kv_scale)) {
+    TORCH_CHECK(kv_scale->scalar_type() == torch::kFloat32 && kv_scale->is_contiguous(), "prefill: fp32 kv_scale");
+    a.kv_scale = kv_scale->data_ptr<float>();
+  }
+  a.sm_scale = (float)sm_scale;
+  a.out = out.data_ptr();
+  a.ld_o = out.stride(0);
+  a.B = (int)cu_q.numel() - 1;
+  a.max_q_len = (int)max_q_len;
+  const c10::cuda::CUDAGuard guard(q.device());
+  vrm::paged_attention_prefill(a, cur_stream());
+}
+
+// ---------------------------------------------------------------- sampling
+void argmax(const Tensor& logits, Tensor& out) {
+  check_bf16_2d(logits, "argmax logits");
+  TORCH_CHECK(out.scalar_type() == torch::kInt32 && out.numel() >= logits.size(0), "argmax: int32 out");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  vrm::argmax_rows(logits.data_ptr(), logits.stride(0), (int)logits.size(0), (int)logits.size(1),
+                   out.data_ptr<int>(), cur_stream());
+}
+
+void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k, const Tensor& top_p, int64_t seed,
+            const Tensor& steps, Tensor& out) {
+  check_bf16_2d(logits, "sample logits");
+  const int64_t B = logits.size(0);
+  TORCH_CHECK(temperature.scalar_type() == torch::kFloat32 && temperature.numel() >= B, "sample: fp32 temperature");
+  TORCH_CHECK(top_k.scalar_type() == torch::kInt32 && top_k.numel() >= B, "sample: int32 top_k");
+  TORCH_CHECK(top_p.scalar_type() == torch::kFloat32 && top_p.numel() >= B, "sample: fp32 top_p");
+  TORCH_CHECK(steps.scalar_type() == torch::kInt32 && steps.numel() >= B, "sample: int32 steps");
+  TORCH_CHECK(out.scalar_type() == torch::kInt32 && out.numel() >= B, "sample: int32 out");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  vrm::sample_rows(logits.data_ptr(), logits.stride(0), (int)B, (int)logits.size(1), temperature.data_ptr<float>(),
+                   top_k.data_ptr<int>(), top_p.data_ptr<float>(), (uint64_t)seed, steps.data_ptr<int>(),
+                   out.data_ptr<int>(), cur_stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "vramancer_b200 sm_100a kernels";
+  m.attr("EPI_NONE") = (int)vrm::kEpiNone;
+  m.attr("EPI_SILU_MUL") = (int)vrm::kEpiSiluMul;
+  m.def("gemm", &gemm, py::arg("x"), py::arg("w"), py::arg("bias") = py::none(), py::arg("force_splits") = 0,
+        py::arg("epilogue") = 0);
+  m.def("gemm_out", &gemm_out, py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("out"),
+        py::arg("force_splits") = 0, py::arg("epilogue") = 0, py::arg("residual") = py::none());
+  m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"));
+  m.def("layernorm", &layernorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("b"), py::arg("out"),
+        py::arg("eps"));
+  m.def("rope_kv_write", &rope_kv_write, py::arg("qkv"), py::arg("positions"), py::arg("cos_sin"), py::arg("cache"),
+        py::arg("slot_mapping"), py::arg("kv_scale"), py::arg("layer"), py::arg("num_q_heads"),
+        py::arg("num_kv_heads"), py::arg("head_dim"));
+  m.def("silu_mul", &silu_mul, py::arg("x"), py::arg("out"));
+  m.def("gelu_tanh_", &gelu_tanh_, py::arg("x"));
+  m.def("embedding", &embedding, py::arg("ids"), py::arg("table"), py::arg("pos"), py::arg("pos_table"),
+        py::arg("out"));
+  m.def("add_", &add_, py::arg("a"), py::arg("b"));
+  m.def("paged_attention_decode", &attn_decode, py::arg("q"), py::arg("cache"), py::arg("layer"),
+        py::arg("block_tables"), py::arg("context_lens"), py::arg("kv_scale"), py::arg("sm_scale"), py::arg("out"),
+        py::arg("num_splits"), py::arg("num_q_heads"));
+  m.def("paged_attention_prefill", &attn_prefill, py::arg("q"), py::arg("cache"), py::arg("layer"),
+        py::arg("block_tables"), py::arg("cu_q"), py::arg("context_lens"), py::arg("kv_scale"), py::arg("sm_scale"),
+        py::arg("out"), py::arg("max_q_len"), py::arg("num_q_heads"));
+  m.def("decode_attention_splits", [](int64_t B, int64_t KH, int64_t max_pages) {
+    return vrm::decode_attention_choose_splits((int)B, (int)KH, (int)max_pages);
+  });
+  m.def("argmax", &argmax, py::arg("logits"), py::arg("out"));
+  m.def("sample", &sample, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"),
+        py::arg("seed"), py::arg("steps"), py::arg("out"));
+  m.def("read_and_clear_errors", &vrm::read_and_clear_errors, "device error word (bounded-wait timeouts)");
+  m.def("reserve_workspace", [](int64_t bytes) { vrm::workspace_reserve((size_t)bytes, cur_stream()); },
+        "pre-allocate split-K / split-KV scratch before CUDA graph capture");
+  m.def("workspace_size", []() { return (int64_t)vrm::workspace_size(); });
+}

@@ -1,0 +1,56 @@
+// Host-side runtime services shared by every kernel launcher (plain CUDA runtime,
+// no framework dependency):
+//   * the cuTensorMapEncodeTiled entry point (fetched from the driver at run time,
+//     so the library does not link libcuda directly)
+//   * a per-device error word that bounded device-side waits report into
+//   * a per-device split-K / split-KV workspace and a zeroed tile-counter array
+// Failures throw std::runtime_error.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace vrm {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tensor_map();
+
+#define VRM_CUDA_CHECK(expr)                                                                       \
+  do {                                                                                             \
+    cudaError_t _e = (expr);                                                                       \
+    if (_e != cudaSuccess)                                                                         \
+      throw std::runtime_error(std::string("CUDA error ") + cudaGetErrorString(_e) + " at " +      \
+                               __FILE__ + ":" + std::to_string(__LINE__));                         \
+  } while (0)
+
+#define VRM_REQUIRE(cond, msg)                                                                     \
+  do {                                                                                             \
+    if (!(cond)) throw std::runtime_error(std::string("vramancer_b200: ") + (msg));                \
+  } while (0)
+
+// Device word (current device) that kernels atomically OR error codes into.
+uint32_t* error_word();
+// Reads and clears the current device's error word (synchronises the device).
+uint32_t read_and_clear_errors();
+
+// Persistent scratch of at least `bytes` on the current device.  Grows only when
+// `stream` is not capturing; old buffers are never freed while the process lives
+// (graphs captured earlier may still point at them).
+void* workspace_get(size_t bytes, cudaStream_t stream);
+void workspace_reserve(size_t bytes, cudaStream_t stream);
+size_t workspace_size();
+// Zero-initialised uint32 counters (65536 per device); every user resets the
+// ones it touched before its kernel exits.
+uint32_t* tile_counters_get(cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace vrm

@@ -1,0 +1,117 @@
+// Raw-pointer launch interface of every vramancer_b200 CUDA kernel.
+//
+// The .cu files implement these with plain CUDA (no framework headers), which keeps
+// them fast to compile and callable from any host code; torch_ops.cpp wraps them for
+// Python with shape/dtype checks.  All pointers are device pointers of the current
+// device; every launch goes to `stream`.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace vrm {
+
+// ---------------------------------------------------------------- GEMM (gemm_tc.cu)
+// Y[M, N] = X[M, K] @ W[N, K]^T (+ bias[N]) in bf16 with fp32 accumulation on tcgen05.
+enum GemmEpilogue : int {
+  kEpiNone = 0,
+  // W rows are interleaved gate/up pairs (row 2j = gate j, row 2j+1 = up j); the output
+  // has N/2 columns: Y[m, j] = silu(gate) * up.
+  kEpiSiluMul = 1,
+};
+
+struct GemmArgs {
+  const void* x = nullptr;
+  int64_t ldx = 0;
+  const void* w = nullptr;
+  int64_t ldw = 0;
+  const void* bias = nullptr;
+  void* out = nullptr;
+  int64_t ldo = 0;
+  int M = 0, N = 0, K = 0;
+  int force_splits = 0;
+  int epilogue = kEpiNone;
+  const void* residual = nullptr;   // optional: Y += residual[M, N] (same ld as out)
+};
+void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- norms / rope / elementwise (norm_rope.cu)
+// out = norm(x [+ residual]); when residual != null the sum is stored back into it.
+void rmsnorm(const void* x, int64_t ldx, void* residual, const void* w, void* out, int64_t ldo, int T, int H,
+             float eps, cudaStream_t stream);
+void layernorm(const void* x, int64_t ldx, void* residual, const void* w, const void* b, void* out, int64_t ldo,
+               int T, int H, float eps, cudaStream_t stream);
+
+struct RopeKvArgs {
+  void* qkv = nullptr;          // bf16 [T, (Hq + 2 KH) * D], rotated in place
+  int64_t ld_qkv = 0;
+  int T = 0, Hq = 0, KH = 0, D = 0;
+  const int* positions = nullptr;   // [T] (null: no rotation)
+  const float* cos_sin = nullptr;   // [max_pos, rot_dim] = [cos | sin]
+  int rot_dim = 0;
+  void* cache = nullptr;            // [pages, layers, 2, KH, page_size, D]
+  bool cache_fp8 = false;
+  int num_layers = 0, layer = 0, page_size = 16;
+  const int* slot_mapping = nullptr;   // [T] page * page_size + offset, < 0 skips
+  const float* kv_scale = nullptr;     // [layers, 2, KH] (fp8 only)
+};
+void rope_kv_write(const RopeKvArgs& a, cudaStream_t stream);
+
+void silu_mul(const void* x, int64_t ldx, void* out, int64_t ldo, int T, int I, cudaStream_t stream);
+void gelu_tanh(void* x, size_t n, cudaStream_t stream);
+void embedding(const int* ids, const void* table, const int* pos, const void* pos_table, void* out, int T, int H,
+               cudaStream_t stream);
+void add_inplace(void* a, const void* b, size_t n, cudaStream_t stream);
+
+// ---------------------------------------------------------------- attention (attention.cu)
+struct DecodeAttnArgs {
+  const void* q = nullptr;   // bf16, token b head h at q + b*ld_q + h*D
+  int64_t ld_q = 0;
+  const void* cache = nullptr;
+  bool cache_fp8 = false;
+  int num_layers = 0, layer = 0, KH = 0, D = 0, Hq = 0;
+  const int* block_tables = nullptr;   // [B, bt_stride]
+  int bt_stride = 0;
+  const int* context_lens = nullptr;   // [B]
+  const float* kv_scale = nullptr;     // [layers, 2, KH] (fp8 only)
+  float sm_scale = 1.f;
+  void* out = nullptr;                 // bf16, token b head h at out + b*ld_o + h*D
+  int64_t ld_o = 0;
+  int B = 0;
+  int max_pages = 0;                   // upper bound on pages per sequence (split choice)
+  int num_splits = 0;                  // 0: choose from B, KH and max_pages
+  // scratch for split partials; null -> the per-device workspace is used
+  float* ws = nullptr;
+  size_t ws_bytes = 0;
+  uint32_t* counters = nullptr;        // >= B*KH zeroed words; null -> per-device counters
+};
+void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t stream);
+// Scratch bytes paged_attention_decode needs for a given split count.
+size_t decode_attention_scratch_bytes(int B, int Hq, int D, int splits);
+int decode_attention_choose_splits(int B, int KH, int max_pages);
+
+struct PrefillAttnArgs {
+  const void* q = nullptr;   // bf16 [T_total, ...], token t head h at q + t*ld_q + h*D
+  int64_t ld_q = 0;
+  const void* cache = nullptr;
+  bool cache_fp8 = false;
+  int num_layers = 0, layer = 0, KH = 0, D = 0, Hq = 0;
+  const int* block_tables = nullptr;
+  int bt_stride = 0;
+  const int* cu_q = nullptr;           // [B + 1] query offsets
+  const int* context_lens = nullptr;   // [B] total keys (prefix + new)
+  const float* kv_scale = nullptr;
+  float sm_scale = 1.f;
+  void* out = nullptr;
+  int64_t ld_o = 0;
+  int B = 0, max_q_len = 0;
+};
+void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- sampling (sampling.cu)
+void argmax_rows(const void* logits, int64_t ld, int B, int V, int* out, cudaStream_t stream);
+void sample_rows(const void* logits, int64_t ld, int B, int V, const float* temperature, const int* top_k,
+                 const float* top_p, uint64_t seed, const int* steps, int* out, cudaStream_t stream);
+
+}  // namespace vrm
