@@ -1,0 +1,232 @@
+"""Numerics of every CUDA kernel against the fp32 PyTorch reference of the same op
+(the CPU path of vramancer_b200.ops)."""
+import math
+
+import pytest
+import torch
+
+from vramancer_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _close(a, b, rtol=2e-2, atol=2e-2):
+    a, b = a.float().cpu(), b.float().cpu()
+    err = (a - b).abs()
+    tol = atol + rtol * b.abs()
+    bad = (err > tol).sum().item()
+    assert bad == 0, f"{bad} / {a.numel()} out of tolerance, max err {err.max().item():.4g}"
+
+
+# ------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M", [1, 5, 16, 32, 33, 64, 100, 128, 129, 300, 512])
+@pytest.mark.parametrize("N,K", [(256, 128), (384, 512), (1000, 320), (2048, 1024)])
+def test_gemm(M, N, K, cuda_errors_clean):
+    torch.manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K) * 0.5
+    w = torch.randn(N, K) * 0.05
+    b = torch.randn(N) * 0.1
+    xg, wg, bg = x.bfloat16().to(DEV), w.bfloat16().to(DEV), b.bfloat16().to(DEV)
+    y = ops.linear(xg, wg, bg)
+    ref = ops.linear(x.bfloat16(), w.bfloat16(), b.bfloat16())
+    _close(y, ref)
+
+
+@pytest.mark.parametrize("M", [1, 32, 256])
+@pytest.mark.parametrize("splits", [1, 2, 5])
+def test_gemm_splitk_deterministic(M, splits, cuda_errors_clean):
+    torch.manual_seed(0)
+    x = (torch.randn(M, 1280) * 0.5).bfloat16()
+    w = (torch.randn(640, 1280) * 0.05).bfloat16()
+    ref = ops.linear(x, w)
+    y1 = ops.linear(x.to(DEV), w.to(DEV), force_splits=splits)
+    y2 = ops.linear(x.to(DEV), w.to(DEV), force_splits=splits)
+    _close(y1, ref)
+    assert torch.equal(y1, y2), "split-K reduction must be deterministic"
+
+
+@pytest.mark.parametrize("M", [1, 20, 200])
+def test_gemm_silu_and_residual_epilogues(M, cuda_errors_clean):
+    torch.manual_seed(1)
+    K, I = 512, 384
+    x = (torch.randn(M, K) * 0.5).bfloat16()
+    wgu = (torch.randn(2 * I, K) * 0.05).bfloat16()
+    ref = ops.linear(x, wgu, epilogue=ops.EPI_SILU_MUL)
+    y = ops.linear(x.to(DEV), wgu.to(DEV), epilogue=ops.EPI_SILU_MUL)
+    _close(y, ref)
+    y2 = ops.linear(x.to(DEV), wgu.to(DEV), epilogue=ops.EPI_SILU_MUL, force_splits=3)
+    _close(y2, ref)
+    w = (torch.randn(K, K) * 0.05).bfloat16()
+    r = (torch.randn(M, K)).bfloat16()
+    ref_r = ops.linear(x, w, residual=r)
+    rg = r.to(DEV)
+    ops.linear(x.to(DEV), w.to(DEV), residual=rg, out=rg)   # in-place residual stream update
+    _close(rg, ref_r)
+
+
+# ------------------------------------------------------------------------- norms
+@pytest.mark.parametrize("H", [128, 768, 3584, 5120])
+@pytest.mark.parametrize("with_res", [False, True])
+def test_rmsnorm_layernorm(H, with_res, cuda_errors_clean):
+    torch.manual_seed(H)
+    x = torch.randn(7, H).bfloat16()
+    r = torch.randn(7, H).bfloat16() if with_res else None
+    w = (1 + 0.1 * torch.randn(H)).bfloat16()
+    b = (0.1 * torch.randn(H)).bfloat16()
+    rc = r.clone() if r is not None else None
+    ref = ops.rmsnorm(x, w, 1e-6, residual=rc)
+    rg = r.to(DEV) if r is not None else None
+    y = ops.rmsnorm(x.to(DEV), w.to(DEV), 1e-6, residual=rg)
+    _close(y, ref)
+    if r is not None:
+        _close(rg, rc, rtol=1e-2, atol=1e-2)
+    rc2 = r.clone() if r is not None else None
+    ref2 = ops.layernorm(x, w, b, 1e-5, residual=rc2)
+    rg2 = r.to(DEV) if r is not None else None
+    y2 = ops.layernorm(x.to(DEV), w.to(DEV), b.to(DEV), 1e-5, residual=rg2)
+    _close(y2, ref2)
+
+
+# ------------------------------------------------------------------------- rope + kv write
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("D", [64, 128])
+def test_rope_kv_write(fp8, D, cuda_errors_clean):
+    torch.manual_seed(D)
+    T, Hq, KH, L, P = 9, 6, 2, 3, 8
+    qkv = torch.randn(T, (Hq + 2 * KH) * D).bfloat16()
+    pos = torch.randint(0, 500, (T,), dtype=torch.int32)
+    cs = ops.rope_cos_sin(512, D, 10000.0)
+    slots = torch.randperm(P * 16)[:T].to(torch.int32)
+    slots[3] = -1
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    scale = (torch.rand(L, 2, KH) + 0.5) / 100 if fp8 else None
+    cache_c = torch.zeros(P, L, 2, KH, 16, D, dtype=dt)
+    q_c = qkv.clone()
+    ops.rope_kv_write(q_c, pos, cs, cache_c, slots, scale, 1, Hq, KH, D)
+    cache_g = cache_c.clone().zero_().to(DEV)
+    q_g = qkv.to(DEV)
+    ops.rope_kv_write(q_g, pos.to(DEV), cs.to(DEV), cache_g, slots.to(DEV),
+                      scale.to(DEV) if scale is not None else None, 1, Hq, KH, D)
+    _close(q_g, q_c)
+    _close(cache_g.float(), cache_c.float(), rtol=7e-2, atol=2e-2)
+
+
+# ------------------------------------------------------------------------- attention
+def _make_cache(lens, L, KH, D, dt, layer, seed=0):
+    torch.manual_seed(seed)
+    ps = 16
+    pages_per = [(n + ps - 1) // ps for n in lens]
+    P = sum(pages_per) + 3
+    perm = torch.randperm(P)
+    bt = torch.zeros(len(lens), max(pages_per) + 1, dtype=torch.int32)
+    k = 0
+    for b, n in enumerate(pages_per):
+        bt[b, :n] = perm[k:k + n].to(torch.int32)
+        k += n
+    cache = (torch.randn(P, L, 2, KH, ps, D) * 1.5)
+    scale = None
+    if dt == torch.float8_e4m3fn:
+        scale = (torch.rand(L, 2, KH) + 0.5) / 50
+        cache = (cache / scale.view(1, L, 2, KH, 1, 1)).clamp(-448, 448).to(dt)
+    else:
+        cache = cache.to(dt)
+    return cache, bt, scale
+
+
+@pytest.mark.parametrize("D,Hq,KH", [(128, 40, 8), (128, 28, 4), (64, 12, 12), (128, 32, 4)])
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("splits", [0, 1, 3])
+def test_paged_decode(D, Hq, KH, fp8, splits, cuda_errors_clean):
+    lens = [1, 17, 300, 64, 1033]
+    L, layer = 2, 1
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    cache, bt, scale = _make_cache(lens, L, KH, D, dt, layer, seed=D + Hq)
+    B = len(lens)
+    q = torch.randn(B, (Hq + 2 * KH) * D).bfloat16()     # q is a strided view of qkv rows
+    cl = torch.tensor(lens, dtype=torch.int32)
+    sm = 1.0 / math.sqrt(D)
+    ref = ops.paged_attention_decode(q, cache, layer, bt, cl, scale, sm, Hq)
+    out = ops.paged_attention_decode(q.to(DEV), cache.to(DEV), layer, bt.to(DEV), cl.to(DEV),
+                                     scale.to(DEV) if scale is not None else None, sm, Hq, num_splits=splits)
+    _close(out, ref, rtol=3e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("D,Hq,KH", [(128, 40, 8), (64, 12, 12)])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_paged_prefill(D, Hq, KH, fp8, cuda_errors_clean):
+    # (new tokens, total context) per sequence: plain prefill and chunked prefill with prefix
+    specs = [(5, 5), (64, 64), (70, 200), (130, 130), (1, 40)]
+    L, layer = 2, 0
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    cache, bt, scale = _make_cache([s[1] for s in specs], L, KH, D, dt, layer, seed=D)
+    cu = [0]
+    for ql, _ in specs:
+        cu.append(cu[-1] + ql)
+    T = cu[-1]
+    q = torch.randn(T, Hq * D).bfloat16()
+    cu_q = torch.tensor(cu, dtype=torch.int32)
+    cl = torch.tensor([s[1] for s in specs], dtype=torch.int32)
+    sm = 1.0 / math.sqrt(D)
+    mq = max(s[0] for s in specs)
+    ref = ops.paged_attention_prefill(q, cache, layer, bt, cu_q, cl, scale, sm, Hq, mq)
+    out = ops.paged_attention_prefill(q.to(DEV), cache.to(DEV), layer, bt.to(DEV), cu_q.to(DEV), cl.to(DEV),
+                                      scale.to(DEV) if scale is not None else None, sm, Hq, mq)
+    _close(out, ref, rtol=3e-2, atol=3e-2)
+
+
+# ------------------------------------------------------------------------- elementwise + sampling
+def test_elementwise(cuda_errors_clean):
+    torch.manual_seed(3)
+    x = torch.randn(5, 2 * 264).bfloat16()
+    _close(ops.silu_mul(x.to(DEV)), ops.silu_mul(x))
+    g = torch.randn(1000).bfloat16()
+    _close(ops.gelu_tanh_(g.clone().to(DEV)), ops.gelu_tanh_(g.clone()))
+    table = torch.randn(100, 64).bfloat16()
+    pt = torch.randn(50, 64).bfloat16()
+    ids = torch.randint(0, 100, (9,), dtype=torch.int32)
+    pos = torch.randint(0, 50, (9,), dtype=torch.int32)
+    ref = ops.embedding(ids, table, positions=pos, pos_table=pt)
+    out = ops.embedding(ids.to(DEV), table.to(DEV), positions=pos.to(DEV), pos_table=pt.to(DEV))
+    _close(out, ref)
+
+
+@pytest.mark.parametrize("V", [500, 50257, 152064])
+def test_argmax_and_sampling(V, cuda_errors_clean):
+    torch.manual_seed(V)
+    B = 6
+    logits = (torch.randn(B, V) * 3).bfloat16()
+    ref = torch.argmax(logits.float(), -1).to(torch.int32)
+    lg = logits.to(DEV)
+    assert torch.equal(ops.argmax(lg).cpu(), ref)
+    z = torch.zeros(B, dtype=torch.float32, device=DEV)
+    k0 = torch.zeros(B, dtype=torch.int32, device=DEV)
+    p1 = torch.ones(B, dtype=torch.float32, device=DEV)
+    st = torch.arange(B, dtype=torch.int32, device=DEV)
+    assert torch.equal(ops.sample(lg, z, k0, p1, 1, st).cpu(), ref)          # T=0 -> greedy
+    t1 = torch.ones(B, device=DEV)
+    assert torch.equal(ops.sample(lg, t1, torch.ones(B, dtype=torch.int32, device=DEV), p1, 7, st).cpu(), ref)
+    # top-k = 5: every draw must be one of the 5 largest logits
+    k5 = torch.full((B,), 5, dtype=torch.int32, device=DEV)
+    top5 = torch.topk(logits.float(), 5, dim=-1).indices
+    for s in range(20):
+        ids = ops.sample(lg, t1, k5, p1, 100 + s, st).cpu()
+        for b in range(B):
+            assert int(ids[b]) in top5[b].tolist()
+    # top-p = tiny: nucleus is the argmax
+    pp = torch.full((B,), 1e-4, dtype=torch.float32, device=DEV)
+    assert torch.equal(ops.sample(lg, t1, k0, pp, 3, st).cpu(), ref)
+    # unrestricted sampling frequencies follow softmax on a small vocabulary
+    if V == 500:
+        lg1 = torch.zeros(1, 500)
+        lg1[0, :4] = torch.tensor([2.0, 1.0, 0.5, 0.0])
+        lg1[0, 4:] = -30
+        lgd = lg1.bfloat16().to(DEV)
+        counts = torch.zeros(4)
+        for s in range(2000):
+            i = int(ops.sample(lgd, t1[:1], k0[:1], p1[:1], 1000 + s, st[:1]))
+            counts[i] += 1
+        freq = counts / counts.sum()
+        pref = torch.softmax(torch.tensor([2.0, 1.0, 0.5, 0.0]), 0)
+        assert (freq - pref).abs().max() < 0.04

@@ -1,0 +1,360 @@
+"""Operator layer: sm_100a kernels for CUDA tensors, PyTorch reference math for CPU.
+
+Every op takes the same arguments on both devices.  CUDA tensors always go to the
+native extension ``vramancer_b200._C`` (built by ``python setup.py build_ext
+--inplace``); if it is missing on a machine with a GPU the op raises instead of
+silently falling back.  CPU tensors run the plain-PyTorch reference of the same math,
+which is the oracle the GPU tests compare against and the path used for CPU-only
+execution (for example the split-vs-single parity check on two CPU devices).
+
+Reference parity: these ops replace the reference's Triton kernels
+(core/triton_fused_rmsnorm.py, core/triton_fused_rope.py, core/triton_sampling.py),
+its paged attention kernel (csrc/paged_attention_kernel.cu) and the cuBLAS GEMMs of
+its HF path.
+"""
+from __future__ import annotations
+
+import importlib
+import math
+import os
+from typing import Optional
+
+import torch
+
+_native = None
+_native_err: Optional[BaseException] = None
+
+
+def native():
+    """Returns the loaded extension module, raising a clear error if it is absent."""
+    global _native, _native_err
+    if _native is not None:
+        return _native
+    try:
+        _native = importlib.import_module("vramancer_b200._C")
+    except BaseException as e:  # ImportError or a loader error
+        _native_err = e
+        raise RuntimeError(
+            "vramancer_b200 native kernels are not built (run `python setup.py build_ext --inplace`): "
+            f"{e!r}") from e
+    return _native
+
+
+def native_available() -> bool:
+    try:
+        native()
+        return True
+    except RuntimeError:
+        return False
+
+
+EPI_NONE = 0
+EPI_SILU_MUL = 1
+
+
+# --------------------------------------------------------------------------- GEMM
+def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, *,
+           out: Optional[torch.Tensor] = None, epilogue: int = EPI_NONE,
+           residual: Optional[torch.Tensor] = None, force_splits: int = 0) -> torch.Tensor:
+    """y = x @ w.T (+ bias) (+ residual); with EPI_SILU_MUL, w rows are interleaved
+    (gate_j, up_j) pairs and y[:, j] = silu(gate_j) * up_j."""
+    if x.is_cuda:
+        if out is None:
+            n = w.shape[0] // 2 if epilogue == EPI_SILU_MUL else w.shape[0]
+            out = torch.empty(x.shape[0], n, dtype=x.dtype, device=x.device)
+        native().gemm_out(x, w, bias, out, force_splits, epilogue, residual)
+        return out
+    y = x.float() @ w.float().t()
+    if bias is not None:
+        y = y + bias.float()
+    if epilogue == EPI_SILU_MUL:
+        g, u = y[:, 0::2], y[:, 1::2]
+        y = torch.nn.functional.silu(g) * u
+    if residual is not None:
+        y = y + residual.float()
+    y = y.to(x.dtype)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+# --------------------------------------------------------------------------- norms
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, *, residual: Optional[torch.Tensor] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = rmsnorm(x [+ residual]) * w; the sum is written back into residual."""
+    if out is None:
+        out = torch.empty_like(x)
+    if x.is_cuda:
+        native().rmsnorm(x, residual, w, out, eps)
+        return out
+    h = x.float()
+    if residual is not None:
+        h = (h + residual.float()).to(x.dtype)
+        residual.copy_(h)
+        h = h.float()
+    y = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+    out.copy_(y.to(out.dtype))
+    return out
+
+
+def layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, *,
+              residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(x)
+    if x.is_cuda:
+        native().layernorm(x, residual, w, b, out, eps)
+        return out
+    h = x.float()
+    if residual is not None:
+        h = (h + residual.float()).to(x.dtype)
+        residual.copy_(h)
+        h = h.float()
+    y = torch.nn.functional.layer_norm(h, (h.shape[-1],), w.float(), b.float(), eps)
+    out.copy_(y.to(out.dtype))
+    return out
+
+
+# --------------------------------------------------------------------------- RoPE
+def rope_cos_sin(max_pos: int, rot_dim: int, theta: float, device=None) -> torch.Tensor:
+    """[max_pos, rot_dim] fp32 table = [cos(p * f_i) | sin(p * f_i)], f_i = theta^(-2i/rot_dim)."""
+    inv = 1.0 / (theta ** (torch.arange(0, rot_dim, 2, dtype=torch.float64) / rot_dim))
+    p = torch.arange(max_pos, dtype=torch.float64)
+    ang = torch.outer(p, inv)
+    return torch.cat([ang.cos(), ang.sin()], dim=1).to(torch.float32).to(device)
+
+
+def _fp8_dtype():
+    return torch.float8_e4m3fn
+
+
+def rope_kv_write(qkv: torch.Tensor, positions: Optional[torch.Tensor], cos_sin: Optional[torch.Tensor],
+                  cache: torch.Tensor, slot_mapping: Optional[torch.Tensor], kv_scale: Optional[torch.Tensor],
+                  layer: int, num_q_heads: int, num_kv_heads: int, head_dim: int) -> None:
+    """Rotates q/k of qkv [T, (Hq+2KH)*D] in place and stores k/v rows into the paged cache
+    [pages, layers, 2, KH, page_size, D] at slot_mapping (bf16, or fp8 e4m3 / kv_scale)."""
+    if qkv.is_cuda:
+        native().rope_kv_write(qkv, positions, cos_sin, cache, slot_mapping, kv_scale, layer,
+                               num_q_heads, num_kv_heads, head_dim)
+        return
+    T = qkv.shape[0]
+    Hq, KH, D = num_q_heads, num_kv_heads, head_dim
+    v = qkv.view(T, Hq + 2 * KH, D)
+    if cos_sin is not None and T > 0:
+        rot = cos_sin.shape[1]
+        half = rot // 2
+        cs = cos_sin[positions.long()]
+        c, s = cs[:, None, :half], cs[:, None, half:]
+        qk = v[:, :Hq + KH, :].float()
+        x1, x2 = qk[..., :half].clone(), qk[..., half:rot].clone()
+        qk[..., :half] = x1 * c - x2 * s
+        qk[..., half:rot] = x2 * c + x1 * s
+        v[:, :Hq + KH, :] = qk.to(qkv.dtype)
+    if slot_mapping is None or T == 0:
+        return
+    ps = cache.shape[4]
+    slots = slot_mapping.long()
+    valid = slots >= 0
+    if not bool(valid.any()):
+        return
+    idx = torch.nonzero(valid).flatten()
+    page, off = slots[idx] // ps, slots[idx] % ps
+    k = v[idx, Hq:Hq + KH, :]
+    vv = v[idx, Hq + KH:, :]
+    if cache.dtype in (torch.float8_e4m3fn, torch.uint8):
+        sk = kv_scale[layer, 0].view(1, KH, 1)
+        sv = kv_scale[layer, 1].view(1, KH, 1)
+        kq = (k.float() / sk).clamp(-448, 448).to(torch.float8_e4m3fn)
+        vq = (vv.float() / sv).clamp(-448, 448).to(torch.float8_e4m3fn)
+        if cache.dtype == torch.uint8:
+            kq, vq = kq.view(torch.uint8), vq.view(torch.uint8)
+        cache[page, layer, 0, :, off, :] = kq
+        cache[page, layer, 1, :, off, :] = vq
+    else:
+        cache[page, layer, 0, :, off, :] = k.to(cache.dtype)
+        cache[page, layer, 1, :, off, :] = vv.to(cache.dtype)
+
+
+# --------------------------------------------------------------------------- attention
+def _gather_kv(cache: torch.Tensor, layer: int, pages: torch.Tensor, n: int,
+               kv_scale: Optional[torch.Tensor]):
+    """[n, KH, D] float K and V of one sequence from its page list."""
+    k = cache[pages, layer, 0]  # [P, KH, ps, D]
+    v = cache[pages, layer, 1]
+    KH, ps, D = k.shape[1], k.shape[2], k.shape[3]
+    k = k.permute(0, 2, 1, 3).reshape(-1, KH, D)[:n]
+    v = v.permute(0, 2, 1, 3).reshape(-1, KH, D)[:n]
+    if cache.dtype == torch.uint8:
+        k, v = k.view(torch.float8_e4m3fn), v.view(torch.float8_e4m3fn)
+    k, v = k.float(), v.float()
+    if kv_scale is not None and cache.dtype in (torch.float8_e4m3fn, torch.uint8):
+        k = k * kv_scale[layer, 0].view(1, KH, 1)
+        v = v * kv_scale[layer, 1].view(1, KH, 1)
+    return k, v
+
+
+def paged_attention_decode(q: torch.Tensor, cache: torch.Tensor, layer: int, block_tables: torch.Tensor,
+                           context_lens: torch.Tensor, kv_scale: Optional[torch.Tensor], sm_scale: float,
+                           num_q_heads: int, *, out: Optional[torch.Tensor] = None,
+                           num_splits: int = 0) -> torch.Tensor:
+    """One query token per sequence: q [B, >=Hq*D] -> out [B, Hq*D]."""
+    B = q.shape[0]
+    D = cache.shape[5]
+    if out is None:
+        out = torch.empty(B, num_q_heads * D, dtype=q.dtype, device=q.device)
+    if q.is_cuda:
+        native().paged_attention_decode(q, cache, layer, block_tables, context_lens, kv_scale, sm_scale, out,
+                                        num_splits, num_q_heads)
+        return out
+    KH = cache.shape[3]
+    G = num_q_heads // KH
+    ps = cache.shape[4]
+    for b in range(B):
+        n = int(context_lens[b])
+        if n == 0:
+            out[b].zero_()
+            continue
+        pages = block_tables[b, : (n + ps - 1) // ps].long()
+        k, v = _gather_kv(cache, layer, pages, n, kv_scale)
+        qb = q[b, : num_q_heads * D].float().view(KH, G, D)
+        s = torch.einsum("kgd,nkd->kgn", qb, k) * sm_scale
+        p = torch.softmax(s, dim=-1)
+        o = torch.einsum("kgn,nkd->kgd", p, v)
+        out[b] = o.reshape(-1).to(out.dtype)
+    return out
+
+
+def paged_attention_prefill(q: torch.Tensor, cache: torch.Tensor, layer: int, block_tables: torch.Tensor,
+                            cu_q: torch.Tensor, context_lens: torch.Tensor, kv_scale: Optional[torch.Tensor],
+                            sm_scale: float, num_q_heads: int, max_q_len: int, *,
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal attention of new tokens (rows of q, grouped by cu_q) over their sequence's
+    cached prefix plus themselves; keys/values are read from the paged cache."""
+    T = q.shape[0]
+    D = cache.shape[5]
+    if out is None:
+        out = torch.empty(T, num_q_heads * D, dtype=q.dtype, device=q.device)
+    if q.is_cuda:
+        native().paged_attention_prefill(q, cache, layer, block_tables, cu_q, context_lens, kv_scale, sm_scale,
+                                         out, max_q_len, num_q_heads)
+        return out
+    KH = cache.shape[3]
+    G = num_q_heads // KH
+    ps = cache.shape[4]
+    B = cu_q.numel() - 1
+    for b in range(B):
+        s0, s1 = int(cu_q[b]), int(cu_q[b + 1])
+        ql = s1 - s0
+        if ql == 0:
+            continue
+        n = int(context_lens[b])
+        pages = block_tables[b, : (n + ps - 1) // ps].long()
+        k, v = _gather_kv(cache, layer, pages, n, kv_scale)
+        qb = q[s0:s1, : num_q_heads * D].float().view(ql, KH, G, D)
+        s = torch.einsum("qkgd,nkd->kgqn", qb, k) * sm_scale
+        qpos = torch.arange(n - ql, n).view(ql, 1)
+        kpos = torch.arange(n).view(1, n)
+        s = s.masked_fill(kpos > qpos, float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        o = torch.einsum("kgqn,nkd->qkgd", p, v)
+        out[s0:s1] = o.reshape(ql, -1).to(out.dtype)
+    return out
+
+
+# --------------------------------------------------------------------------- elementwise
+def silu_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[T, 2I] (gate | up) -> silu(gate) * up."""
+    I = x.shape[1] // 2
+    if out is None:
+        out = torch.empty(x.shape[0], I, dtype=x.dtype, device=x.device)
+    if x.is_cuda:
+        native().silu_mul(x, out)
+        return out
+    out.copy_((torch.nn.functional.silu(x[:, :I].float()) * x[:, I:].float()).to(out.dtype))
+    return out
+
+
+def gelu_tanh_(x: torch.Tensor) -> torch.Tensor:
+    if x.is_cuda:
+        native().gelu_tanh_(x)
+        return x
+    x.copy_(torch.nn.functional.gelu(x.float(), approximate="tanh").to(x.dtype))
+    return x
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, *, positions: Optional[torch.Tensor] = None,
+              pos_table: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    if table.is_cuda:
+        native().embedding(ids, table, positions, pos_table, out)
+        return out
+    y = table[ids.long()]
+    if pos_table is not None:
+        y = (y.float() + pos_table[positions.long()].float()).to(table.dtype)
+    out.copy_(y)
+    return out
+
+
+def add_(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    if a.is_cuda:
+        native().add_(a, b)
+        return a
+    a.copy_((a.float() + b.float()).to(a.dtype))
+    return a
+
+
+# --------------------------------------------------------------------------- sampling
+def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    if logits.is_cuda:
+        native().argmax(logits, out)
+        return out
+    out.copy_(torch.argmax(logits.float(), dim=-1).to(torch.int32))
+    return out
+
+
+def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+           seed: int, steps: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Temperature / top-k / top-p sampling (temperature <= 0 -> greedy)."""
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    if logits.is_cuda:
+        native().sample(logits, temperature, top_k, top_p, seed, steps, out)
+        return out
+    g = torch.Generator().manual_seed(int(seed))
+    for r in range(logits.shape[0]):
+        x = logits[r].float()
+        t = float(temperature[r])
+        if t <= 0:
+            out[r] = int(torch.argmax(x))
+            continue
+        z = x / t
+        k = int(top_k[r])
+        if 0 < k < z.numel():
+            thr = torch.topk(z, k).values[-1]
+            z = z.masked_fill(z < thr, float("-inf"))
+        p = float(top_p[r])
+        if p < 1.0:
+            probs = torch.softmax(z, -1)
+            sp, si = torch.sort(probs, descending=True)
+            keep = torch.cumsum(sp, 0) - sp < p
+            mask = torch.zeros_like(probs, dtype=torch.bool)
+            mask[si[keep]] = True
+            z = z.masked_fill(~mask, float("-inf"))
+        out[r] = int(torch.multinomial(torch.softmax(z, -1), 1, generator=g))
+    return out
+
+
+def reserve_workspace(nbytes: int) -> None:
+    native().reserve_workspace(int(nbytes))
+
+
+def read_and_clear_errors() -> int:
+    """Error bits raised by bounded device-side waits since the last call (0 = none)."""
+    return int(native().read_and_clear_errors())
+
+
+def decode_attention_splits(batch: int, kv_heads: int, max_pages: int) -> int:
+    return int(native().decode_attention_splits(batch, kv_heads, max_pages))
