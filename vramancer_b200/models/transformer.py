@@ -1,0 +1,189 @@
+"""Decoder forward pass over the paged KV pool, for one pipeline stage / TP rank.
+
+The residual stream `r` is a [T, H] buffer that every layer updates in place:
+  TP = 1   the o_proj and down_proj GEMMs add their product into `r` in the GEMM
+           epilogue (no separate residual kernel), then a plain RMSNorm reads `r`;
+  TP > 1   row-parallel partial sums are all-reduced first (fused kernel or NCCL)
+           and added by the residual-fused RMSNorm / an add kernel.
+Per dense layer at TP=1: RMSNorm, QKV GEMM(+bias), RoPE+KV-page write, paged
+attention, O GEMM(+residual), RMSNorm, gate/up GEMM(+SiLU*up), down GEMM(+residual):
+eight launches, all of them sm_100a kernels of this package.
+
+Reference parity: the reference runs HF modules (core/backends.py:1629-1852 manual
+path, core/turbo_engine.py:194-254 TurboForward) and its own TP layer in
+core/tensor_parallel.py:172-445 (no KV cache there); this module owns the forward.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Callable, List, Optional
+
+import torch
+
+from .. import ops
+from ..kv.pool import KVPool
+from .config import ModelConfig
+from .weights import Weights
+
+
+@dataclass
+class ForwardBatch:
+    """Device-side metadata of one forward.
+
+    decode:  T == B tokens, one per sequence; context_lens include the new token.
+    prefill: tokens of B sequences concatenated; cu_q [B+1] delimits them;
+             context_lens = cached prefix + new tokens; logits_rows selects the rows
+             whose logits are needed (last token of each finished prompt).
+    """
+    input_ids: torch.Tensor
+    positions: torch.Tensor
+    slot_mapping: torch.Tensor
+    block_tables: torch.Tensor
+    context_lens: torch.Tensor
+    is_decode: bool
+    cu_q: Optional[torch.Tensor] = None
+    max_q_len: int = 1
+    logits_rows: Optional[torch.Tensor] = None
+    attn_splits: int = 0
+
+    @property
+    def num_tokens(self) -> int:
+        return self.input_ids.shape[0]
+
+
+class TPContext:
+    """What a tensor-parallel rank needs from the communication layer."""
+
+    def __init__(self, rank: int, size: int, all_reduce: Callable[[torch.Tensor], torch.Tensor],
+                 all_gather_last: Callable[[torch.Tensor], torch.Tensor]):
+        self.rank, self.size = rank, size
+        self.all_reduce = all_reduce
+        self.all_gather_last = all_gather_last
+
+
+class DecoderModel:
+    def __init__(self, cfg: ModelConfig, weights: Weights, *, device="cpu", dtype=torch.bfloat16,
+                 first_layer: int = 0, last_layer: Optional[int] = None, tp: Optional[TPContext] = None):
+        self.cfg = cfg
+        self.w = weights
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.first_layer = first_layer
+        self.last_layer = cfg.num_layers if last_layer is None else last_layer
+        self.has_embed = first_layer == 0
+        self.has_head = self.last_layer == cfg.num_layers
+        self.tp = tp
+        tps = tp.size if tp else 1
+        self.tp_size = tps
+        self.hq = cfg.num_heads // tps
+        self.kvh = max(1, cfg.num_kv_heads // tps)
+        self.D = cfg.head_dim
+        self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
+        self.cos_sin = (ops.rope_cos_sin(cfg.max_position, cfg.rot_dim, cfg.rope_theta, self.device)
+                        if cfg.rot_dim > 0 else None)
+
+    @property
+    def num_local_layers(self) -> int:
+        return self.last_layer - self.first_layer
+
+    def lw(self, i: int, name: str) -> Optional[torch.Tensor]:
+        return self.w.get(f"layers.{i}.{name}")
+
+    # ------------------------------------------------------------------ pieces
+    def embed(self, batch: ForwardBatch) -> torch.Tensor:
+        cfg = self.cfg
+        if cfg.is_gpt2:
+            return ops.embedding(batch.input_ids, self.w["embed"], positions=batch.positions,
+                                 pos_table=self.w["pos_embed"])
+        return ops.embedding(batch.input_ids, self.w["embed"])
+
+    def _norm(self, x, i_or_name, which: str, residual=None):
+        cfg = self.cfg
+        if isinstance(i_or_name, int):
+            w = self.lw(i_or_name, f"{which}_w")
+            b = self.lw(i_or_name, f"{which}_b")
+        else:
+            w, b = self.w["final_norm_w"], self.w.get("final_norm_b")
+        if cfg.is_gpt2:
+            return ops.layernorm(x, w, b, cfg.norm_eps, residual=residual)
+        return ops.rmsnorm(x, w, cfg.norm_eps, residual=residual)
+
+    def _attention(self, i: int, x: torch.Tensor, batch: ForwardBatch, pool: KVPool) -> torch.Tensor:
+        cfg = self.cfg
+        hq, kvh, D = self.hq, self.kvh, self.D
+        qkv = ops.linear(x, self.lw(i, "qkv_w"), self.lw(i, "qkv_b"))
+        li = i - self.first_layer
+        ops.rope_kv_write(qkv, batch.positions, self.cos_sin, pool.cache, batch.slot_mapping, pool.kv_scale,
+                          li, hq, kvh, D)
+        if batch.is_decode:
+            return ops.paged_attention_decode(qkv, pool.cache, li, batch.block_tables, batch.context_lens,
+                                              pool.kv_scale, self.sm_scale, hq, num_splits=batch.attn_splits)
+        return ops.paged_attention_prefill(qkv, pool.cache, li, batch.block_tables, batch.cu_q,
+                                           batch.context_lens, pool.kv_scale, self.sm_scale, hq,
+                                           batch.max_q_len)
+
+    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], r: torch.Tensor,
+                      i: int, next_norm: Optional[str]) -> Optional[torch.Tensor]:
+        """r += x @ w.T (+ b) across the TP group; returns norm(r) if next_norm is given."""
+        if self.tp_size == 1:
+            ops.linear(x, w, b, residual=r, out=r)
+            return self._norm(r, i, next_norm) if next_norm else None
+        y = ops.linear(x, w)
+        y = self.tp.all_reduce(y)
+        if b is not None:
+            ops.add_(y, b.expand_as(y).contiguous())
+        if next_norm:
+            return self._norm(y, i, next_norm, residual=r)
+        ops.add_(r, y)
+        return None
+
+    def _mlp(self, i: int, x: torch.Tensor, r: torch.Tensor) -> None:
+        cfg = self.cfg
+        if cfg.is_gpt2:
+            h = ops.linear(x, self.lw(i, "fc_w"), self.lw(i, "fc_b"))
+            ops.gelu_tanh_(h)
+            self._row_parallel(h, self.lw(i, "proj_w"), self.lw(i, "proj_b"), r, i, None)
+        elif cfg.is_moe:
+            y = self._moe(i, x)
+            ops.add_(r, y)
+        else:
+            a = ops.linear(x, self.lw(i, "gate_up_w"), epilogue=ops.EPI_SILU_MUL)
+            self._row_parallel(a, self.lw(i, "down_w"), None, r, i, None)
+
+    def _moe(self, i: int, x: torch.Tensor) -> torch.Tensor:
+        """Top-k softmax routing over SwiGLU experts (expert-parallel version in
+        parallel/expert_parallel.py)."""
+        from ..parallel.moe import moe_forward
+        return moe_forward(self.cfg, x, self.lw(i, "router_w"), self.lw(i, "experts_gate_up_w"),
+                           self.lw(i, "experts_down_w"), shared_gate_up=self.lw(i, "shared_gate_up_w"),
+                           shared_down=self.lw(i, "shared_down_w"), shared_gate=self.lw(i, "shared_gate_w"))
+
+    def layer(self, i: int, r: torch.Tensor, batch: ForwardBatch, pool: KVPool) -> None:
+        x = self._norm(r, i, "in_norm")
+        attn = self._attention(i, x, batch, pool)
+        x = self._row_parallel(attn, self.lw(i, "o_w"), self.lw(i, "o_b"), r, i, "post_norm")
+        self._mlp(i, x, r)
+
+    def logits(self, r: torch.Tensor, rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+        h = r if rows is None else r.index_select(0, rows)
+        x = self._norm(h.contiguous(), "final", "final")
+        lg = ops.linear(x, self.w["lm_head"])
+        if self.tp_size > 1:
+            lg = self.tp.all_gather_last(lg)[:, : self.cfg.vocab_size]
+        return lg
+
+    # ------------------------------------------------------------------ entry points
+    def forward(self, batch: ForwardBatch, pool: KVPool, hidden: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Runs this stage's layers.  The first stage embeds `batch.input_ids`; later
+        stages take `hidden` (the residual stream from the previous stage).  The last
+        stage returns logits of `batch.logits_rows` (all rows if None); other stages
+        return the residual stream."""
+        r = self.embed(batch) if self.has_embed else hidden
+        if r is None:
+            raise ValueError("non-first pipeline stage needs the hidden state")
+        for i in range(self.first_layer, self.last_layer):
+            self.layer(i, r, batch, pool)
+        if self.has_head:
+            return self.logits(r, batch.logits_rows)
+        return r

@@ -1,0 +1,69 @@
+"""Mixture-of-experts layer: top-k softmax router over SwiGLU experts.
+
+Single-rank path: tokens are grouped by expert (one sort) and each expert's rows run
+through the tcgen05 GEMM (gate/up with the fused SiLU*up epilogue, then down); the
+weighted outputs are scattered back.  The expert-parallel path (tokens dispatched to
+the rank that owns the expert and combined back) lives in expert_parallel.py.
+
+Reference parity: the reference has no MoE of its own (vLLM / llama.cpp only, plus
+the expert placement hooks of core/expert_pinning.py:115-642).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from .. import ops
+from ..models.config import ModelConfig
+
+
+def route(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Returns (weights [T, k] fp32, expert ids [T, k] int64)."""
+    logits = ops.linear(x, router_w).float()
+    probs = torch.softmax(logits, dim=-1)
+    w, ids = torch.topk(probs, cfg.experts_per_token, dim=-1)
+    if cfg.norm_topk_prob:
+        w = w / w.sum(-1, keepdim=True)
+    return w, ids
+
+
+def expert_mlp(x: torch.Tensor, gate_up: torch.Tensor, down: torch.Tensor) -> torch.Tensor:
+    h = ops.linear(x, gate_up, epilogue=ops.EPI_SILU_MUL)
+    return ops.linear(h, down)
+
+
+def moe_forward(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor, experts_gate_up: torch.Tensor,
+                experts_down: torch.Tensor, *, shared_gate_up: Optional[torch.Tensor] = None,
+                shared_down: Optional[torch.Tensor] = None,
+                shared_gate: Optional[torch.Tensor] = None,
+                expert_offset: int = 0) -> torch.Tensor:
+    """x [T, H] -> [T, H].  experts_* hold experts [expert_offset, expert_offset + E_local)."""
+    T, H = x.shape
+    w, ids = route(cfg, x, router_w)
+    out = torch.zeros(T, H, dtype=torch.float32, device=x.device)
+    flat = ids.flatten()
+    order = torch.argsort(flat, stable=True)
+    e_local = experts_gate_up.shape[0]
+    counts = torch.bincount(flat - expert_offset if expert_offset else flat,
+                            minlength=max(cfg.num_experts, e_local)).cpu().tolist()
+    tok_of = order // cfg.experts_per_token
+    wflat = w.flatten()[order]
+    start = 0
+    for e, n in enumerate(counts):
+        if n == 0:
+            continue
+        sel = slice(start, start + n)
+        start += n
+        le = e
+        if le < 0 or le >= e_local:
+            continue
+        toks = tok_of[sel]
+        y = expert_mlp(x.index_select(0, toks).contiguous(), experts_gate_up[le], experts_down[le])
+        out.index_add_(0, toks, y.float() * wflat[sel].unsqueeze(1))
+    if shared_gate_up is not None:
+        ys = expert_mlp(x, shared_gate_up, shared_down).float()
+        if shared_gate is not None:
+            ys = ys * torch.sigmoid(ops.linear(x, shared_gate).float())
+        out += ys
+    return out.to(x.dtype)
