@@ -1,0 +1,245 @@
+"""Continuous-batching LLM engine over the paged KV cache.
+
+Each `step()`:
+  1. admits waiting requests while the batch and the KV pool have room (prefix-cache
+     hits skip the cached part of the prompt),
+  2. runs one chunked-prefill forward over up to `max_prefill_tokens` prompt tokens of
+     admitted requests (a request whose prompt completes gets its first token),
+  3. runs one decode step (CUDA graph) for every request that is generating,
+  4. applies stop conditions, streams tokens to callbacks, frees finished requests.
+Requests join and leave at step granularity (iteration-level scheduling).  The KV of
+a request stays in its pages for its whole life: nothing is concatenated or padded
+per step.
+
+Reference parity: ContinuousBatcher, core/continuous_batcher.py:106-1065 (waiting
+queue, admission, chunked prefill at VRM_PREFILL_CHUNK, batched decode, per-request
+sampling, streaming callback, futures) — which re-concatenates HF caches every step
+(:828-891); here decode reads pages in place.
+"""
+from __future__ import annotations
+
+import itertools
+import threading
+import time
+from collections import deque
+from concurrent.futures import Future
+from dataclasses import dataclass, field
+from typing import Callable, Deque, Dict, List, Optional, Sequence
+
+from ..kv.paged import OutOfPages, PagedKVCacheManager
+from .runner import ModelRunner, PrefillItem
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    stop_token_ids: Sequence[int] = ()
+    ignore_eos: bool = False
+
+    @property
+    def greedy(self) -> bool:
+        return self.temperature <= 0.0
+
+
+_ids = itertools.count()
+
+
+@dataclass
+class Request:
+    prompt_ids: List[int]
+    params: SamplingParams
+    request_id: object = field(default_factory=lambda: f"req-{next(_ids)}")
+    on_token: Optional[Callable[["Request", int], None]] = None
+    output_ids: List[int] = field(default_factory=list)
+    num_computed: int = 0          # prompt tokens whose KV is written
+    cached_tokens: int = 0
+    finished: bool = False
+    finish_reason: Optional[str] = None
+    arrival: float = field(default_factory=time.perf_counter)
+    first_token_time: Optional[float] = None
+    finish_time: Optional[float] = None
+    future: Optional[Future] = None
+
+    @property
+    def prefill_done(self) -> bool:
+        return self.num_computed >= len(self.prompt_ids)
+
+    @property
+    def ttft(self) -> Optional[float]:
+        return None if self.first_token_time is None else self.first_token_time - self.arrival
+
+    @property
+    def total_len(self) -> int:
+        return len(self.prompt_ids) + len(self.output_ids)
+
+
+class LLMEngine:
+    def __init__(self, runner: ModelRunner, manager: PagedKVCacheManager, *, max_batch: Optional[int] = None,
+                 max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None):
+        self.runner = runner
+        self.kv = manager
+        self.max_batch = max_batch or runner.max_batch
+        self.max_prefill_tokens = max_prefill_tokens
+        self.max_model_len = runner.max_model_len
+        self.eos_token_id = eos_token_id
+        self.waiting: Deque[Request] = deque()
+        self.running: List[Request] = []
+        self._lock = threading.RLock()
+        self.stats = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "finished": 0, "preempted": 0}
+
+    # ------------------------------------------------------------------ API
+    def add_request(self, prompt_ids: Sequence[int], params: Optional[SamplingParams] = None, *,
+                    request_id=None, on_token=None) -> Request:
+        params = params or SamplingParams()
+        if len(prompt_ids) == 0:
+            raise ValueError("empty prompt")
+        if len(prompt_ids) + 1 > self.max_model_len:
+            raise ValueError(f"prompt of {len(prompt_ids)} tokens exceeds max_model_len {self.max_model_len}")
+        req = Request(list(int(t) for t in prompt_ids), params, on_token=on_token)
+        if request_id is not None:
+            req.request_id = request_id
+        req.future = Future()
+        with self._lock:
+            self.waiting.append(req)
+        return req
+
+    def has_unfinished(self) -> bool:
+        with self._lock:
+            return bool(self.waiting or self.running)
+
+    def abort(self, request_id) -> bool:
+        with self._lock:
+            for q in (self.waiting, self.running):
+                for r in list(q):
+                    if r.request_id == request_id:
+                        self._finish(r, "abort")
+                        return True
+        return False
+
+    def generate(self, prompts: Sequence[Sequence[int]], params: Optional[SamplingParams] = None) -> List[Request]:
+        reqs = [self.add_request(p, params) for p in prompts]
+        while any(not r.finished for r in reqs):
+            self.step()
+        return reqs
+
+    # ------------------------------------------------------------------ scheduling
+    def _admit(self) -> None:
+        while self.waiting and len(self.running) < self.max_batch:
+            req = self.waiting[0]
+            need = len(req.prompt_ids) + 1
+            if not self.kv.can_allocate(need):
+                break
+            try:
+                cached = self.kv.allocate(req.request_id, len(req.prompt_ids), req.prompt_ids)
+            except OutOfPages:
+                break
+            self.waiting.popleft()
+            req.num_computed = cached
+            req.cached_tokens = cached
+            self.running.append(req)
+
+    def _finish(self, req: Request, reason: str) -> None:
+        if req.finished:
+            return
+        req.finished = True
+        req.finish_reason = reason
+        req.finish_time = time.perf_counter()
+        if req in self.running:
+            self.running.remove(req)
+        elif req in self.waiting:
+            self.waiting.remove(req)
+        self.kv.free(req.request_id)
+        self.stats["finished"] += 1
+        if req.future is not None and not req.future.done():
+            req.future.set_result(req)
+
+    def _emit(self, req: Request, tok: int) -> None:
+        req.output_ids.append(tok)
+        if req.first_token_time is None:
+            req.first_token_time = time.perf_counter()
+        if req.on_token is not None:
+            req.on_token(req, tok)
+        p = req.params
+        stop = set(p.stop_token_ids)
+        if self.eos_token_id is not None and not p.ignore_eos:
+            stop.add(self.eos_token_id)
+        if tok in stop:
+            self._finish(req, "stop")
+        elif len(req.output_ids) >= p.max_tokens:
+            self._finish(req, "length")
+        elif req.total_len >= self.max_model_len:
+            self._finish(req, "length")
+
+    def step(self) -> List[Request]:
+        """One scheduler iteration; returns requests that finished during it."""
+        with self._lock:
+            before = self.stats["finished"]
+            done: List[Request] = []
+            self._admit()
+            self._prefill_chunk(done)
+            self._decode(done)
+            self.stats["steps"] += 1
+            return done
+
+    def _prefill_chunk(self, done: List[Request]) -> None:
+        budget = self.max_prefill_tokens
+        items, reqs = [], []
+        for req in self.running:
+            if req.prefill_done or budget <= 0:
+                continue
+            n = min(len(req.prompt_ids) - req.num_computed, budget)
+            s = req.num_computed
+            slots = self.kv.slots_for(req.request_id, s, n)
+            items.append(PrefillItem(token_ids=req.prompt_ids[s:s + n], start_pos=s, slots=slots,
+                                     block_table=self.kv.block_table(req.request_id), context_len=s + n,
+                                     want_logits=(s + n == len(req.prompt_ids))))
+            reqs.append(req)
+            budget -= n
+        if not items:
+            return
+        toks = self.runner.prefill(items, [r.params.temperature for r in reqs], [r.params.top_k for r in reqs],
+                                   [r.params.top_p for r in reqs], [0 for _ in reqs])
+        for req, it, tok in zip(reqs, items, toks):
+            req.num_computed += len(it.token_ids)
+            self.stats["prefill_tokens"] += len(it.token_ids)
+            if req.prefill_done:
+                self.kv.commit_prefix(req.request_id, req.prompt_ids)
+                self._emit(req, int(tok))
+                if req.finished:
+                    done.append(req)
+
+    def _decode(self, done: List[Request]) -> None:
+        active = [r for r in self.running if r.prefill_done and not r.finished and r.output_ids]
+        if not active:
+            return
+        ids, pos, slots, ctx, bts = [], [], [], [], []
+        temp, topk, topp, steps = [], [], [], []
+        for r in active:
+            p = r.total_len - 1                     # position of the token being fed
+            s = self.kv.append_slots(r.request_id, 1)[0]
+            ids.append(r.output_ids[-1])
+            pos.append(p)
+            slots.append(s)
+            ctx.append(p + 1)
+            bts.append(self.kv.block_table(r.request_id))
+            temp.append(r.params.temperature)
+            topk.append(r.params.top_k)
+            topp.append(r.params.top_p)
+            steps.append(len(r.output_ids))
+        self._apply_cow()
+        out = self.runner.decode_step(ids, pos, slots, ctx, bts, temp, topk, topp, steps)
+        self.stats["decode_tokens"] += len(active)
+        for r, tok in zip(active, out):
+            self._emit(r, int(tok))
+            if r.finished:
+                done.append(r)
+
+    def _apply_cow(self) -> None:
+        copies = self.kv.pop_cow_copies()
+        if copies:
+            cache = self.runner.pool.cache
+            for src, dst in copies:
+                cache[dst].copy_(cache[src])

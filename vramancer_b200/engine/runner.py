@@ -1,0 +1,269 @@
+"""Model runner: builds forward batches from host metadata and executes them, with
+decode steps replayed from CUDA graphs.
+
+Decode inputs live in one device staging buffer that is filled by a single
+host->device copy per step from pinned memory (token ids, positions, cache slots,
+context lengths, block tables, sampling parameters); the captured graph reads views
+of it and writes the sampled token ids into a device buffer that is copied back to
+pinned memory.  One graph per batch-size bucket (1, 2, 4, 8, 16, 32, ... max_batch);
+padded rows have context length 0 and slot -1, so they neither read nor write KV.
+
+Reference parity: core/cuda_graph_decode.py:59-257 (per-batch-size graph cache,
+single device, rejects dynamic caches) and core/turbo_engine.py:432-603 (graph with
+argmax inside, zero-sync greedy loop).  Here the graph covers the whole paged decode
+step including sampling, at any batch bucket.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..kv.pool import KVPool
+from ..models.transformer import DecoderModel, ForwardBatch
+
+DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64, 96, 128, 192, 256)
+
+
+@dataclass
+class PrefillItem:
+    token_ids: Sequence[int]      # new tokens of this chunk
+    start_pos: int                # absolute position of token_ids[0]
+    slots: Sequence[int]          # cache slot per new token
+    block_table: Sequence[int]
+    context_len: int              # start_pos + len(token_ids)
+    want_logits: bool
+
+
+class ModelRunner:
+    def __init__(self, model: DecoderModel, pool: KVPool, *, max_batch: int = 256, max_model_len: int = 4096,
+                 use_cuda_graph: bool = True, buckets: Sequence[int] = DEFAULT_BUCKETS, seed: int = 0):
+        self.model = model
+        self.pool = pool
+        self.device = model.device
+        self.max_batch = max_batch
+        self.max_model_len = max_model_len
+        self.page_size = pool.spec.page_size
+        self.max_pages = (max_model_len + self.page_size - 1) // self.page_size
+        self.use_graph = use_cuda_graph and self.device.type == "cuda"
+        self.buckets = sorted(b for b in buckets if b <= max_batch) or [max_batch]
+        if self.buckets[-1] < max_batch:
+            self.buckets.append(max_batch)
+        self.seed = seed
+        self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        self._graph_pool = None
+        self._alloc_decode_buffers()
+        self.launches_per_decode = None
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc_decode_buffers(self):
+        B, P = self.max_batch, self.max_pages
+        # int32 section: ids, pos, slots, ctx, topk, steps (6*B) + block tables (B*P)
+        self._n_i32 = 6 * B + B * P
+        self._n_f32 = 2 * B
+        pin = self.device.type == "cuda"
+        self.h_i32 = torch.zeros(self._n_i32, dtype=torch.int32, pin_memory=pin)
+        self.h_f32 = torch.zeros(self._n_f32, dtype=torch.float32, pin_memory=pin)
+        self.d_i32 = torch.zeros(self._n_i32, dtype=torch.int32, device=self.device)
+        self.d_f32 = torch.zeros(self._n_f32, dtype=torch.float32, device=self.device)
+        d = self.d_i32
+        self.d_ids, self.d_pos, self.d_slots = d[0:B], d[B:2 * B], d[2 * B:3 * B]
+        self.d_ctx, self.d_topk, self.d_steps = d[3 * B:4 * B], d[4 * B:5 * B], d[5 * B:6 * B]
+        self.d_bt = d[6 * B:].view(B, P)
+        self.d_temp, self.d_topp = self.d_f32[0:B], self.d_f32[B:2 * B]
+        self.d_out = torch.zeros(B, dtype=torch.int32, device=self.device)
+        self.h_out = torch.zeros(B, dtype=torch.int32, pin_memory=pin)
+        hn = self.h_i32.numpy()
+        self.hn_ids, self.hn_pos, self.hn_slots = hn[0:B], hn[B:2 * B], hn[2 * B:3 * B]
+        self.hn_ctx, self.hn_topk, self.hn_steps = hn[3 * B:4 * B], hn[4 * B:5 * B], hn[5 * B:6 * B]
+        self.hn_bt = hn[6 * B:].reshape(B, P)
+        hf = self.h_f32.numpy()
+        self.hn_temp, self.hn_topp = hf[0:B], hf[B:2 * B]
+
+    def bucket_for(self, n: int) -> int:
+        for b in self.buckets:
+            if b >= n:
+                return b
+        raise ValueError(f"batch {n} exceeds max_batch {self.max_batch}")
+
+    # ------------------------------------------------------------------ decode
+    def _decode_batch(self, B: int) -> ForwardBatch:
+        splits = ops.decode_attention_splits(B, self.model.kvh, self.max_pages) if self.device.type == "cuda" else 0
+        return ForwardBatch(input_ids=self.d_ids[:B], positions=self.d_pos[:B], slot_mapping=self.d_slots[:B],
+                            block_tables=self.d_bt[:B], context_lens=self.d_ctx[:B], is_decode=True,
+                            attn_splits=splits)
+
+    def _decode_body(self, B: int) -> None:
+        batch = self._decode_batch(B)
+        logits = self.model.forward(batch, self.pool)
+        ops.sample(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.seed, self.d_steps[:B],
+                   out=self.d_out[:B])
+
+    def stage_decode_inputs(self, ids, positions, slots, ctx, block_tables: List[Sequence[int]],
+                            temperature, top_k, top_p, steps) -> int:
+        """Fills the pinned staging buffers for n live rows; returns the bucket size."""
+        n = len(ids)
+        B = self.bucket_for(n) if self.use_graph else n
+        self.hn_ids[:B] = 0
+        self.hn_pos[:B] = 0
+        self.hn_slots[:B] = -1
+        self.hn_ctx[:B] = 0
+        self.hn_ids[:n] = ids
+        self.hn_pos[:n] = positions
+        self.hn_slots[:n] = slots
+        self.hn_ctx[:n] = ctx
+        self.hn_topk[:n] = top_k
+        self.hn_steps[:n] = steps
+        self.hn_temp[:n] = temperature
+        self.hn_topp[:n] = top_p
+        for r, bt in enumerate(block_tables):
+            self.hn_bt[r, :len(bt)] = bt
+        return B
+
+    def upload_decode_inputs(self) -> None:
+        """One H2D copy of every decode input (the whole staging area)."""
+        self.d_i32.copy_(self.h_i32, non_blocking=True)
+        self.d_f32.copy_(self.h_f32, non_blocking=True)
+
+    @property
+    def h2d_bytes_per_decode(self) -> int:
+        return self.h_i32.numel() * 4 + self.h_f32.numel() * 4
+
+    def decode(self, B: int) -> torch.Tensor:
+        """Runs one decode step for bucket B on the uploaded inputs; returns d_out[:B]."""
+        if self.use_graph:
+            g = self._graphs.get(B)
+            if g is None:
+                g = self.capture(B)
+            g.replay()
+        else:
+            self._decode_body(B)
+        return self.d_out[:B]
+
+    def decode_step(self, ids, positions, slots, ctx, block_tables, temperature, top_k, top_p, steps) -> List[int]:
+        """Host-to-host decode step: stage, upload, run, read back the sampled ids."""
+        n = len(ids)
+        B = self.stage_decode_inputs(ids, positions, slots, ctx, block_tables, temperature, top_k, top_p, steps)
+        self.upload_decode_inputs()
+        out = self.decode(B)
+        if self.device.type == "cuda":
+            self.h_out[:B].copy_(out, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return self.h_out[:n].tolist()
+        return out[:n].tolist()
+
+    def capture(self, B: int) -> torch.cuda.CUDAGraph:
+        """Warm up (allocates split workspaces) and capture the decode graph of bucket B."""
+        # warm-up on zeroed inputs: slot -1 / ctx 0 rows touch no KV
+        saved_i, saved_f = self.d_i32.clone(), self.d_f32.clone()
+        self.d_ids[:B].zero_()
+        self.d_slots[:B].fill_(-1)
+        self.d_ctx[:B].zero_()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._decode_body(B)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.d_i32.copy_(saved_i)
+        self.d_f32.copy_(saved_f)
+        g = torch.cuda.CUDAGraph()
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g, pool=self._graph_pool):
+            self._decode_body(B)
+        torch.cuda.synchronize()
+        self._graphs[B] = g
+        return g
+
+    def capture_all(self, sizes: Optional[Sequence[int]] = None) -> None:
+        if not self.use_graph:
+            return
+        for B in sorted(sizes or self.buckets, reverse=True):
+            if B not in self._graphs:
+                self.capture(B)
+
+    def release_graphs(self) -> None:
+        self._graphs.clear()
+        self._graph_pool = None
+
+    # ------------------------------------------------------------------ prefill
+    def prefill(self, items: List[PrefillItem], temperature, top_k, top_p, steps) -> List[Optional[int]]:
+        """Runs one (chunked) prefill forward over several sequences; returns the
+        sampled next token for items with want_logits (None for the others)."""
+        dev = self.device
+        ids, pos, slots, cu, ctx = [], [], [], [0], []
+        maxp = 1
+        for it in items:
+            n = len(it.token_ids)
+            ids.extend(it.token_ids)
+            pos.extend(range(it.start_pos, it.start_pos + n))
+            slots.extend(it.slots)
+            cu.append(cu[-1] + n)
+            ctx.append(it.context_len)
+            maxp = max(maxp, len(it.block_table))
+        B = len(items)
+        bt = np.zeros((B, maxp), dtype=np.int32)
+        for r, it in enumerate(items):
+            bt[r, :len(it.block_table)] = it.block_table
+        rows = [cu[r + 1] - 1 for r, it in enumerate(items) if it.want_logits]
+        meta = np.concatenate([np.asarray(ids, np.int32), np.asarray(pos, np.int32), np.asarray(slots, np.int32),
+                               np.asarray(cu, np.int32), np.asarray(ctx, np.int32), bt.reshape(-1),
+                               np.asarray(rows, np.int32)])
+        h = torch.from_numpy(meta)
+        if dev.type == "cuda":
+            h = h.pin_memory()
+        d = h.to(dev, non_blocking=True)
+        T = len(ids)
+        o = 0
+        d_ids = d[o:o + T]; o += T
+        d_pos = d[o:o + T]; o += T
+        d_slots = d[o:o + T]; o += T
+        d_cu = d[o:o + B + 1]; o += B + 1
+        d_ctx = d[o:o + B]; o += B
+        d_bt = d[o:o + B * maxp].view(B, maxp); o += B * maxp
+        d_rows = d[o:o + len(rows)].long()
+        batch = ForwardBatch(input_ids=d_ids, positions=d_pos, slot_mapping=d_slots, block_tables=d_bt,
+                             context_lens=d_ctx, is_decode=False, cu_q=d_cu,
+                             max_q_len=max(len(it.token_ids) for it in items), logits_rows=d_rows)
+        if not rows:
+            # no logits wanted: still run all layers (KV must be written)
+            batch.logits_rows = d_rows
+        logits = self.model.forward(batch, self.pool)
+        if not rows:
+            return [None] * B
+        sel = [r for r, it in enumerate(items) if it.want_logits]
+        tt = torch.tensor([temperature[r] for r in sel], dtype=torch.float32)
+        tk = torch.tensor([top_k[r] for r in sel], dtype=torch.int32)
+        tp = torch.tensor([top_p[r] for r in sel], dtype=torch.float32)
+        st = torch.tensor([steps[r] for r in sel], dtype=torch.int32)
+        nxt = ops.sample(logits, tt.to(dev), tk.to(dev), tp.to(dev), self.seed, st.to(dev)).cpu().tolist()
+        res: List[Optional[int]] = [None] * B
+        for j, r in enumerate(sel):
+            res[r] = nxt[j]
+        return res
+
+    def prefill_logits(self, items: List[PrefillItem]) -> torch.Tensor:
+        """Prefill returning the raw logits rows (for scoring / speculative verify)."""
+        dev = self.device
+        ids, pos, slots, cu, ctx = [], [], [], [0], []
+        maxp = max(len(it.block_table) for it in items)
+        for it in items:
+            n = len(it.token_ids)
+            ids.extend(it.token_ids)
+            pos.extend(range(it.start_pos, it.start_pos + n))
+            slots.extend(it.slots)
+            cu.append(cu[-1] + n)
+            ctx.append(it.context_len)
+        bt = torch.zeros(len(items), maxp, dtype=torch.int32)
+        for r, it in enumerate(items):
+            bt[r, :len(it.block_table)] = torch.tensor(it.block_table, dtype=torch.int32)
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)
+        batch = ForwardBatch(input_ids=i32(ids), positions=i32(pos), slot_mapping=i32(slots),
+                             block_tables=bt.to(dev), context_lens=i32(ctx), is_decode=False, cu_q=i32(cu),
+                             max_q_len=max(len(it.token_ids) for it in items), logits_rows=None)
+        return self.model.forward(batch, self.pool)

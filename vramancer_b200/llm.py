@@ -1,0 +1,86 @@
+"""`LLM`: one-call construction of the serving stack on one device.
+
+    llm = LLM("qwen2.5-14b")                     # preset, random-init weights
+    llm = LLM("/models/Qwen2.5-14B-Instruct")    # HF checkpoint directory
+    outs = llm.generate([[1, 2, 3]], SamplingParams(max_tokens=32))
+
+Builds the weights (HF safetensors, NVFP4 checkpoint or random N(0, 0.02)), the paged
+KV pool sized from the free memory left after the weights, the block manager, the
+model runner (CUDA-graph decode) and the continuous-batching engine.
+"""
+from __future__ import annotations
+
+import os
+from typing import List, Optional, Sequence, Union
+
+import torch
+
+from .engine.engine import LLMEngine, Request, SamplingParams
+from .engine.runner import ModelRunner
+from .kv.paged import PagedKVCacheManager
+from .kv.pool import KVPool, KVPoolSpec, kv_dtype_from_str
+from .models.config import ModelConfig, get_config
+from .models.transformer import DecoderModel
+from .models.weights import load_safetensors, random_weights
+
+
+def _is_checkpoint_dir(p: str) -> bool:
+    return os.path.isdir(p) and any(f.endswith(".safetensors") for f in os.listdir(p))
+
+
+class LLM:
+    def __init__(self, model: Union[str, ModelConfig] = "qwen2.5-14b", *, device: str = "cuda",
+                 dtype: torch.dtype = torch.bfloat16, kv_cache_dtype: str = "bf16", max_batch: int = 64,
+                 max_model_len: int = 4096, kv_pages: Optional[int] = None, gpu_memory_utilization: float = 0.9,
+                 seed: int = 0, use_cuda_graph: bool = True, enable_prefix_cache: bool = True,
+                 max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, weights=None,
+                 num_layers: Optional[int] = None):
+        if isinstance(model, ModelConfig):
+            cfg = model
+        else:
+            cfg = get_config(model)
+        if num_layers is not None:
+            cfg = cfg.with_(num_layers=num_layers)
+        self.cfg = cfg
+        self.device = torch.device(device)
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        if weights is None:
+            if isinstance(model, str) and _is_checkpoint_dir(model):
+                weights = load_safetensors(model, cfg, device=self.device, dtype=dtype)
+            else:
+                weights = random_weights(cfg, device=self.device, dtype=dtype, seed=seed)
+        self.weights = weights
+        self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype)
+        kvd = kv_dtype_from_str(kv_cache_dtype)
+        if kv_pages is None:
+            kv_pages = self._pages_from_memory(cfg, kvd, gpu_memory_utilization, max_batch, max_model_len)
+        spec = KVPoolSpec(kv_pages, cfg.num_layers, self.model.kvh, cfg.head_dim, dtype=kvd)
+        self.pool = KVPool(spec, self.device)
+        self.kv = PagedKVCacheManager(kv_pages, spec.page_size, enable_prefix_cache=enable_prefix_cache)
+        self.runner = ModelRunner(self.model, self.pool, max_batch=max_batch, max_model_len=max_model_len,
+                                  use_cuda_graph=use_cuda_graph, seed=seed)
+        self.engine = LLMEngine(self.runner, self.kv, max_prefill_tokens=max_prefill_tokens,
+                                eos_token_id=eos_token_id)
+
+    def _pages_from_memory(self, cfg, kvd, util, max_batch, max_model_len) -> int:
+        need = max_batch * ((max_model_len + 15) // 16) + 16
+        if self.device.type != "cuda":
+            return min(need, 4096)
+        free, total = torch.cuda.mem_get_info(self.device)
+        budget = int(free - (1 - util) * total) - (2 << 30)   # keep ~2 GiB for activations/graphs
+        per = KVPoolSpec(1, cfg.num_layers, self.model.kvh, cfg.head_dim, dtype=kvd).bytes_per_page
+        return max(16, min(need * 2, budget // per))
+
+    # ------------------------------------------------------------------ API
+    def generate(self, prompts: Sequence[Sequence[int]], params: Optional[SamplingParams] = None) -> List[Request]:
+        return self.engine.generate(prompts, params)
+
+    def warmup(self, batch_sizes: Optional[Sequence[int]] = None) -> None:
+        """Captures the decode graphs ahead of time."""
+        self.runner.capture_all(batch_sizes)
+
+    def stats(self):
+        d = dict(self.engine.stats)
+        d.update({f"kv_{k}": v for k, v in self.kv.stats().items()})
+        return d
