@@ -34,7 +34,7 @@ class LLM:
                  max_model_len: int = 4096, kv_pages: Optional[int] = None, gpu_memory_utilization: float = 0.9,
                  seed: int = 0, use_cuda_graph: bool = True, enable_prefix_cache: bool = True,
                  max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, weights=None,
-                 num_layers: Optional[int] = None):
+                 num_layers: Optional[int] = None, tp=None):
         if isinstance(model, ModelConfig):
             cfg = model
         else:
@@ -45,13 +45,17 @@ class LLM:
         self.device = torch.device(device)
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
+        self.tp = tp
+        tp_rank, tp_size = (tp.rank, tp.size) if tp is not None else (0, 1)
         if weights is None:
             if isinstance(model, str) and _is_checkpoint_dir(model):
-                weights = load_safetensors(model, cfg, device=self.device, dtype=dtype)
+                weights = load_safetensors(model, cfg, device=self.device, dtype=dtype, tp_rank=tp_rank,
+                                           tp_size=tp_size)
             else:
-                weights = random_weights(cfg, device=self.device, dtype=dtype, seed=seed)
+                weights = random_weights(cfg, device=self.device, dtype=dtype, seed=seed, tp_rank=tp_rank,
+                                         tp_size=tp_size)
         self.weights = weights
-        self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype)
+        self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype, tp=tp)
         kvd = kv_dtype_from_str(kv_cache_dtype)
         if kv_pages is None:
             kv_pages = self._pages_from_memory(cfg, kvd, gpu_memory_utilization, max_batch, max_model_len)

@@ -25,9 +25,13 @@ _native = None
 _native_err: Optional[BaseException] = None
 
 
+LAUNCHES = [0]   # number of native kernel launches issued through this module
+
+
 def native():
     """Returns the loaded extension module, raising a clear error if it is absent."""
     global _native, _native_err
+    LAUNCHES[0] += 1
     if _native is not None:
         return _native
     try:
@@ -42,7 +46,7 @@ def native():
 
 def native_available() -> bool:
     try:
-        native()
+        _host_call()
         return True
     except RuntimeError:
         return False
@@ -347,14 +351,20 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
     return out
 
 
+def _host_call():
+    m = native()
+    LAUNCHES[0] -= 1
+    return m
+
+
 def reserve_workspace(nbytes: int) -> None:
-    native().reserve_workspace(int(nbytes))
+    _host_call().reserve_workspace(int(nbytes))
 
 
 def read_and_clear_errors() -> int:
     """Error bits raised by bounded device-side waits since the last call (0 = none)."""
-    return int(native().read_and_clear_errors())
+    return int(_host_call().read_and_clear_errors())
 
 
 def decode_attention_splits(batch: int, kv_heads: int, max_pages: int) -> int:
-    return int(native().decode_attention_splits(batch, kv_heads, max_pages))
+    return int(_host_call().decode_attention_splits(batch, kv_heads, max_pages))
