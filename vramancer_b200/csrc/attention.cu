@@ -97,6 +97,8 @@ struct DecodeParams {
 
 template <int D, bool kFp8>
 __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
+  pdl_launch();
+  pdl_wait();
   using S = DecodeSmem<D, kFp8>;
   constexpr int ROWB = D * 2;
   constexpr int kEl = kFp8 ? 1 : 2;
@@ -340,6 +342,8 @@ struct PrefillParams {
 
 template <int D, bool kFp8>
 __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
+  pdl_launch();
+  pdl_wait();
   using S = PrefillSmem<D, kFp8>;
   constexpr int ROWB = D * 2;
   constexpr int kEl = kFp8 ? 1 : 2;
@@ -563,8 +567,7 @@ static void launch_decode(dim3 grid, const DecodeParams& p, cudaStream_t st) {
     VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     set[dev & 63] = true;
   }
-  kern<<<grid, 128, smem, st>>>(p);
-  VRM_CUDA_CHECK(cudaGetLastError());
+  launch_kernel(kern, grid, dim3(128), (size_t)smem, st, p);
 }
 
 void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
@@ -627,8 +630,7 @@ static void launch_prefill(dim3 grid, const PrefillParams& p, cudaStream_t st) {
     VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     set[dev & 63] = true;
   }
-  kern<<<grid, 128, smem, st>>>(p);
-  VRM_CUDA_CHECK(cudaGetLastError());
+  launch_kernel(kern, grid, dim3(128), (size_t)smem, st, p);
 }
 
 void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t st) {

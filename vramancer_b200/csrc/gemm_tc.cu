@@ -23,6 +23,7 @@
 // path (core/backends.py:1390) and its SIMT NVFP4 GEMV (csrc/fp4_gemv.cu:36-116) for
 // the bf16 case.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -199,6 +200,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
 
+  pdl_launch();
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
@@ -222,6 +224,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------- TMA producer
     const uint64_t pol_a = kSwapAB ? policy_evict_first() : policy_evict_last();
     const uint64_t pol_b = kSwapAB ? policy_evict_last() : policy_evict_first();
+    pdl_wait();
     int issued = 0;
     for (int i = 0; i < num_k; ++i) {
       const int s = i % STAGES;
@@ -262,6 +265,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------- epilogue (128 threads, one TMEM lane each)
     const int lane_base = 32 * (warp & 3);
     const int row = lane_base + lane;   // TMEM lane == MMA row
+    pdl_wait();
     const bool ok = mbar_wait(tmem_full, 0, err);
     tc_fence_after();
 
@@ -313,6 +317,228 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (threadIdx.x == 64) tile_counters[tile_id] = 0u;   // ready for the next launch
       }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// =====================================================================================
+// Stream-K decode GEMM (swap-AB): one persistent CTA per SM.  The iteration space
+// tiles x k_tiles (tile = 128 weight rows, k_tile = 64 K elements) is cut into equal
+// contiguous ranges, one per CTA, so every SM streams the same number of weight bytes
+// whatever the tile count.  A CTA walks its range tile by tile ("segments"); a segment
+// that covers a whole tile is stored directly, otherwise its fp32 partial goes to the
+// workspace and the last contributor of the tile (tile counter) sums the partials in
+// contributor order (deterministic) and runs the epilogue.  Two TMEM accumulators let
+// the epilogue of one segment overlap the MMAs of the next.  With programmatic
+// dependent launch the producer streams the first STAGES weight tiles before waiting
+// for the kernel that produces the activations.
+struct StreamK {
+  int64_t iters;   // tiles * k_tiles
+  int ctas;
+  __device__ __forceinline__ int64_t start(int c) const { return (int64_t)c * iters / ctas; }
+  __device__ __forceinline__ int owner(int64_t i) const {
+    int c = (int)(((i + 1) * ctas - 1) / iters);
+    if (c >= ctas) c = ctas - 1;
+    while (c > 0 && start(c) > i) --c;
+    while (c + 1 < ctas && start(c + 1) <= i) ++c;
+    return c;
+  }
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_streamk_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                             EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters,
+                             int k_tiles, int max_contrib, StreamK sk, uint32_t* __restrict__ err) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  // barriers: full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2], drain
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull = empty_bar + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint32_t* flag_slot = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x;
+  const int64_t it_begin = sk.start(c), it_end = sk.start(c + 1);
+  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+
+  pdl_launch();
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&map_w);
+    tma_prefetch_desc(&map_x);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- producer
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    const int64_t total = it_end - it_begin;
+    const int pre = (int)(total < STAGES ? total : STAGES);
+    // weights do not depend on the previous kernel: start streaming them first
+    for (int g = 0; g < pre; ++g) {
+      const int64_t it = it_begin + g;
+      const int t = (int)(it / k_tiles), k = (int)(it % k_tiles);
+      uint8_t* sa = smem + g * L::kStageBytes;
+      mbar_arrive_expect_tx(&full_bar[g], L::kStageBytes);
+      tma_load_2d(sa, &map_w, &full_bar[g], k * kBK, t * kBM, pol_w);
+    }
+    pdl_wait();
+    for (int g = 0; g < pre; ++g) {
+      const int64_t it = it_begin + g;
+      const int k = (int)(it % k_tiles);
+      uint8_t* sb = smem + g * L::kStageBytes + L::kABytes;
+      tma_load_2d(sb, &map_x, &full_bar[g], k * kBK, 0, pol_x);
+    }
+    int64_t issued = pre;
+    for (int64_t g = pre; g < total; ++g) {
+      const int s = (int)(g % STAGES);
+      const uint32_t ph = (uint32_t)((g / STAGES) & 1);
+      if (!mbar_wait(&empty_bar[s], ph ^ 1, err)) break;
+      const int64_t it = it_begin + g;
+      const int t = (int)(it / k_tiles), k = (int)(it % k_tiles);
+      uint8_t* sa = smem + s * L::kStageBytes;
+      mbar_arrive_expect_tx(&full_bar[s], L::kStageBytes);
+      tma_load_2d(sa, &map_w, &full_bar[s], k * kBK, t * kBM, pol_w);
+      tma_load_2d(sa + L::kABytes, &map_x, &full_bar[s], k * kBK, 0, pol_x);
+      issued = g + 1;
+    }
+    const int64_t first = issued > STAGES ? issued - STAGES : 0;
+    for (int64_t j = first; j < issued; ++j) mbar_wait(&full_bar[j % STAGES], (uint32_t)((j / STAGES) & 1), err);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    constexpr uint32_t idesc = make_idesc_bf16(kBM, BN);
+    int64_t g = 0;
+    int seg = 0;
+    bool failed = false;
+    for (int64_t it = it_begin; it < it_end && !failed; ++seg) {
+      const int k0 = (int)(it % k_tiles);
+      const int64_t n = min((int64_t)(k_tiles - k0), it_end - it);
+      const int acc = seg & 1;
+      if (!mbar_wait(&tempty[acc], (uint32_t)(((seg >> 1) & 1) ^ 1), err)) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+      for (int64_t j = 0; j < n; ++j, ++g) {
+        const int s = (int)(g % STAGES);
+        if (!mbar_wait(&full_bar[s], (uint32_t)((g / STAGES) & 1), err)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * L::kStageBytes);
+        const uint64_t da = make_sw128_desc(sa);
+        const uint64_t db = make_sw128_desc(sa + L::kABytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+          umma_f16(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty_bar[s]);
+      }
+      umma_commit(&tfull[acc]);
+      it += n;
+    }
+    // every MMA this thread issued must retire before TMEM is freed
+    umma_commit(drain);
+    mbar_wait(drain, 0, err);
+  } else if (warp >= 2) {
+    // ---------------- epilogue
+    const int lane_base = 32 * (warp & 3);
+    const int row = lane_base + lane;
+    const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
+    pdl_wait();
+    int seg = 0;
+    for (int64_t it = it_begin; it < it_end; ++seg) {
+      const int t = (int)(it / k_tiles);
+      const int k0 = (int)(it % k_tiles);
+      const int64_t n = min((int64_t)(k_tiles - k0), it_end - it);
+      const bool whole = (k0 == 0 && n == k_tiles);
+      const int acc = seg & 1;
+      const bool ok = mbar_wait(&tfull[acc], (uint32_t)((seg >> 1) & 1), err);
+      tc_fence_after();
+      float v[BN];
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(t_lane + (uint32_t)(acc * BN + c0), r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[c0 + j] = ok ? __uint_as_float(r[j]) : 0.f;
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      const int r_glob = t * kBM + row;   // weight row == output feature
+      if (whole) {
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float w16[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) w16[j] = v[c0 + j];
+          epi_store<true>(ep, r_glob, c0, w16);
+        }
+      } else {
+        const int first_owner = sk.owner((int64_t)t * k_tiles);
+        const int last_owner = sk.owner((int64_t)t * k_tiles + k_tiles - 1);
+        const int ci = c - first_owner;
+        float* slot = workspace + ((size_t)t * max_contrib + ci) * (size_t)(kBM * BN);
+#pragma unroll
+        for (int j = 0; j < BN; ++j) slot[(size_t)j * kBM + row] = v[j];
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          const uint32_t prev = atomicAdd(&tile_counters[t], 1u);
+          *flag_slot = (prev == (uint32_t)(last_owner - first_owner)) ? 1u : 0u;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (*flag_slot) {
+          __threadfence();
+#pragma unroll
+          for (int j = 0; j < BN; ++j) v[j] = 0.f;
+          for (int q = 0; q <= last_owner - first_owner; ++q) {
+            const float* src = workspace + ((size_t)t * max_contrib + q) * (size_t)(kBM * BN);
+#pragma unroll
+            for (int j = 0; j < BN; ++j) v[j] += __ldcg(src + (size_t)j * kBM + row);
+          }
+#pragma unroll
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float w16[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w16[j] = v[c0 + j];
+            epi_store<true>(ep, r_glob, c0, w16);
+          }
+          if (threadIdx.x == 64) tile_counters[t] = 0u;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      it += n;
     }
   }
 
@@ -396,8 +622,41 @@ static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const EpiP
     counters = tile_counters_get(stream);
   }
   dim3 grid(a_tiles * b_tiles, splits);
-  kern<<<grid, kGemmThreads, L::kAlloc, stream>>>(ma, mb, ep, ws, counters, K, a_tiles, ktps, error_word());
-  VRM_CUDA_CHECK(cudaGetLastError());
+  launch_kernel(kern, grid, dim3(kGemmThreads), (size_t)L::kAlloc, stream, ma, mb, ep, ws, counters, K, a_tiles, ktps,
+                error_word());
+}
+
+template <int BN, int STAGES>
+static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const EpiParams& ep, int N, int K,
+                           int max_ctas, cudaStream_t stream) {
+  // smem: stages + 2*STAGES+4 barriers + slots
+  constexpr int kSmem = STAGES * GemmSmem<BN, STAGES>::kStageBytes + (2 * STAGES + 5) * 8 + 16 + 1024;
+  auto kern = gemm_streamk_swap_kernel<BN, STAGES>;
+  static int attr_dev_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    attr_dev_mask |= 1 << (dev & 31);
+  }
+  const int tiles = (N + kBM - 1) / kBM;
+  const int k_tiles = (K + kBK - 1) / kBK;
+  StreamK sk;
+  sk.iters = (int64_t)tiles * k_tiles;
+  sk.ctas = (int)std::min<int64_t>(max_ctas, sk.iters);
+  const int64_t per = sk.iters / sk.ctas;   // >= 1
+  const int max_contrib = (int)std::min<int64_t>(sk.ctas, k_tiles / std::max<int64_t>(per, 1) + 2);
+  float* ws = nullptr;
+  uint32_t* counters = tile_counters_get(stream);
+  VRM_REQUIRE(tiles <= 32768, "stream-K: too many tiles");
+  if (sk.ctas > tiles) {   // some tiles are shared between CTAs
+    const size_t need = (size_t)tiles * max_contrib * kBM * BN * sizeof(float);
+    ws = static_cast<float*>(workspace_get(need, stream));
+  } else {
+    ws = static_cast<float*>(workspace_get((size_t)tiles * max_contrib * kBM * BN * sizeof(float), stream));
+  }
+  launch_kernel(kern, dim3(sk.ctas), dim3(kGemmThreads), (size_t)kSmem, stream, mw, mx, ep, ws, counters, k_tiles,
+                max_contrib, sk, error_word());
 }
 
 // Split count such that tiles * splits covers the SMs with >= min_k K-tiles per split.
@@ -412,6 +671,14 @@ static void choose_split(int tiles, int k_tiles, int min_k, int* splits, int* kt
   s = (k_tiles + per - 1) / per;
   *splits = s;
   *ktps = per;
+}
+
+static bool legacy_decode() {
+  static const bool v = [] {
+    const char* e = std::getenv("VRM_GEMM_LEGACY_DECODE");
+    return e && e[0] == '1';
+  }();
+  return v;
 }
 
 static void force_split(int force, int k_tiles, int* splits, int* ktps) {
@@ -438,14 +705,24 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   const int k_tiles = (a.K + kBK - 1) / kBK;
 
   if (a.M <= 128) {
-    // decode: swap A/B so the weight rows fill the 128 TMEM lanes
+    // decode: swap A/B so the weight rows fill the 128 TMEM lanes; stream-K schedule
     const int BN = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
+    const CUtensorMap ma = make_kmajor_map(a.w, a.N, a.K, a.ldw, kBM);
+    const CUtensorMap mb = make_kmajor_map(a.x, a.M, a.K, a.ldx, BN);
+    if (a.force_splits <= 0 && !legacy_decode()) {
+      const int ctas = device_sm_count();
+      switch (BN) {
+        case 16: launch_streamk<16, 8>(ma, mb, ep, a.N, a.K, ctas, stream); break;
+        case 32: launch_streamk<32, 8>(ma, mb, ep, a.N, a.K, ctas, stream); break;
+        case 64: launch_streamk<64, 6>(ma, mb, ep, a.N, a.K, ctas, stream); break;
+        default: launch_streamk<128, 4>(ma, mb, ep, a.N, a.K, ctas, stream); break;
+      }
+      return;
+    }
     const int a_tiles = (a.N + kBM - 1) / kBM;
     int splits, ktps;
     choose_split(a_tiles, k_tiles, 4, &splits, &ktps);
     if (a.force_splits > 0) force_split(a.force_splits, k_tiles, &splits, &ktps);
-    const CUtensorMap ma = make_kmajor_map(a.w, a.N, a.K, a.ldw, kBM);
-    const CUtensorMap mb = make_kmajor_map(a.x, a.M, a.K, a.ldx, BN);
     switch (BN) {
       case 16: launch_gemm<16, 8, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
       case 32: launch_gemm<32, 8, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;

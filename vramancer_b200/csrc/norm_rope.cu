@@ -69,6 +69,8 @@ template <int VPT>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, int64_t ldx,
                                int64_t ldo, float eps) {
+  pdl_launch();
+  pdl_wait();
   __shared__ float red[33];
   const int row = blockIdx.x;
   const int nvec = H / 8;
@@ -101,6 +103,8 @@ template <int VPT>
 __global__ void layernorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                  const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ b,
                                  __nv_bfloat16* __restrict__ out, int H, int64_t ldx, int64_t ldo, float eps) {
+  pdl_launch();
+  pdl_wait();
   __shared__ float red[33];
   const int row = blockIdx.x;
   const int nvec = H / 8;
@@ -161,10 +165,10 @@ void rmsnorm(const void* x, int64_t ldx, void* residual, const void* w, void* ou
   auto rp = reinterpret_cast<__nv_bfloat16*>(residual);
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w);
   auto op = reinterpret_cast<__nv_bfloat16*>(out);
-  if (vpt <= 1) rmsnorm_kernel<1><<<T, threads, 0, st>>>(xp, rp, wp, op, H, ldx, ldo, eps);
-  else if (vpt <= 2) rmsnorm_kernel<2><<<T, threads, 0, st>>>(xp, rp, wp, op, H, ldx, ldo, eps);
-  else if (vpt <= 4) rmsnorm_kernel<4><<<T, threads, 0, st>>>(xp, rp, wp, op, H, ldx, ldo, eps);
-  else rmsnorm_kernel<8><<<T, threads, 0, st>>>(xp, rp, wp, op, H, ldx, ldo, eps);
+  if (vpt <= 1) launch_kernel(rmsnorm_kernel<1>, dim3(T), dim3(threads), 0, st, xp, rp, wp, op, H, ldx, ldo, eps);
+  else if (vpt <= 2) launch_kernel(rmsnorm_kernel<2>, dim3(T), dim3(threads), 0, st, xp, rp, wp, op, H, ldx, ldo, eps);
+  else if (vpt <= 4) launch_kernel(rmsnorm_kernel<4>, dim3(T), dim3(threads), 0, st, xp, rp, wp, op, H, ldx, ldo, eps);
+  else launch_kernel(rmsnorm_kernel<8>, dim3(T), dim3(threads), 0, st, xp, rp, wp, op, H, ldx, ldo, eps);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -178,10 +182,10 @@ void layernorm(const void* x, int64_t ldx, void* residual, const void* w, const 
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w);
   auto bp = reinterpret_cast<const __nv_bfloat16*>(b);
   auto op = reinterpret_cast<__nv_bfloat16*>(out);
-  if (vpt <= 1) layernorm_kernel<1><<<T, threads, 0, st>>>(xp, rp, wp, bp, op, H, ldx, ldo, eps);
-  else if (vpt <= 2) layernorm_kernel<2><<<T, threads, 0, st>>>(xp, rp, wp, bp, op, H, ldx, ldo, eps);
-  else if (vpt <= 4) layernorm_kernel<4><<<T, threads, 0, st>>>(xp, rp, wp, bp, op, H, ldx, ldo, eps);
-  else layernorm_kernel<8><<<T, threads, 0, st>>>(xp, rp, wp, bp, op, H, ldx, ldo, eps);
+  if (vpt <= 1) launch_kernel(layernorm_kernel<1>, dim3(T), dim3(threads), 0, st, xp, rp, wp, bp, op, H, ldx, ldo, eps);
+  else if (vpt <= 2) launch_kernel(layernorm_kernel<2>, dim3(T), dim3(threads), 0, st, xp, rp, wp, bp, op, H, ldx, ldo, eps);
+  else if (vpt <= 4) launch_kernel(layernorm_kernel<4>, dim3(T), dim3(threads), 0, st, xp, rp, wp, bp, op, H, ldx, ldo, eps);
+  else launch_kernel(layernorm_kernel<8>, dim3(T), dim3(threads), 0, st, xp, rp, wp, bp, op, H, ldx, ldo, eps);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -194,6 +198,8 @@ void layernorm(const void* x, int64_t ldx, void* residual, const void* w, const 
 // (GPT-NeoX / Llama / Qwen2) over the first rot_dim dims.  rot_dim == 0: no rotation.
 template <bool kFp8>
 __global__ void rope_kv_write_kernel(RopeKvArgs a) {
+  pdl_launch();
+  pdl_wait();
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
@@ -241,8 +247,8 @@ void rope_kv_write(const RopeKvArgs& a, cudaStream_t st) {
   if (a.T <= 0) return;
   VRM_REQUIRE(!a.cache_fp8 || a.kv_scale != nullptr, "rope_kv_write: fp8 cache needs kv_scale");
   const int threads = 32 * std::min(16, a.Hq + 2 * a.KH);
-  if (a.cache_fp8) rope_kv_write_kernel<true><<<a.T, threads, 0, st>>>(a);
-  else rope_kv_write_kernel<false><<<a.T, threads, 0, st>>>(a);
+  if (a.cache_fp8) launch_kernel(rope_kv_write_kernel<true>, dim3(a.T), dim3(threads), 0, st, a);
+  else launch_kernel(rope_kv_write_kernel<false>, dim3(a.T), dim3(threads), 0, st, a);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -250,6 +256,8 @@ void rope_kv_write(const RopeKvArgs& a, cudaStream_t st) {
 // out[t, i] = silu(x[t, i]) * x[t, I + i]   (gate | up concatenated)
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out, int I,
                                 int64_t ldx, int64_t ldo) {
+  pdl_launch();
+  pdl_wait();
   const int t = blockIdx.y;
   const int v = blockIdx.x * blockDim.x + threadIdx.x;   // vector of 8
   if (v * 8 >= I) return;
@@ -273,13 +281,15 @@ void silu_mul(const void* x, int64_t ldx, void* out, int64_t ldo, int T, int I, 
   if (T <= 0) return;
   VRM_REQUIRE(I % 8 == 0 && ldx % 8 == 0 && ldo % 8 == 0, "silu_mul: sizes must be multiples of 8");
   dim3 grid((I / 8 + 127) / 128, T);
-  silu_mul_kernel<<<grid, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x),
-                                        reinterpret_cast<__nv_bfloat16*>(out), I, ldx, ldo);
+  launch_kernel(silu_mul_kernel, grid, dim3(128), 0, st, reinterpret_cast<const __nv_bfloat16*>(x),
+                reinterpret_cast<__nv_bfloat16*>(out), I, ldx, ldo);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
 // GELU, tanh approximation (GPT-2 "gelu_new"), in place.
 __global__ void gelu_tanh_kernel(__nv_bfloat16* __restrict__ x, size_t n) {
+  pdl_launch();
+  pdl_wait();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float v = __bfloat162float(x[i]);
@@ -289,7 +299,8 @@ __global__ void gelu_tanh_kernel(__nv_bfloat16* __restrict__ x, size_t n) {
 
 void gelu_tanh(void* x, size_t n, cudaStream_t st) {
   if (n == 0) return;
-  gelu_tanh_kernel<<<(n + 255) / 256, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(x), n);
+  launch_kernel(gelu_tanh_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st,
+                reinterpret_cast<__nv_bfloat16*>(x), n);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -297,6 +308,8 @@ void gelu_tanh(void* x, size_t n, cudaStream_t st) {
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                  const int* __restrict__ pos, const __nv_bfloat16* __restrict__ pos_table,
                                  __nv_bfloat16* __restrict__ out, int H) {
+  pdl_launch();
+  pdl_wait();
   const int t = blockIdx.x;
   const __nv_bfloat16* src = table + (size_t)ids[t] * H;
   const __nv_bfloat16* psrc = pos_table ? pos_table + (size_t)pos[t] * H : nullptr;
@@ -317,21 +330,22 @@ void embedding(const int* ids, const void* table, const int* pos, const void* po
                cudaStream_t st) {
   if (T <= 0) return;
   VRM_REQUIRE(H % 8 == 0, "embedding: hidden must be a multiple of 8");
-  embedding_kernel<<<T, 128, 0, st>>>(ids, reinterpret_cast<const __nv_bfloat16*>(table), pos,
-                                      reinterpret_cast<const __nv_bfloat16*>(pos_table),
-                                      reinterpret_cast<__nv_bfloat16*>(out), H);
+  launch_kernel(embedding_kernel, dim3(T), dim3(128), 0, st, ids, reinterpret_cast<const __nv_bfloat16*>(table), pos,
+                reinterpret_cast<const __nv_bfloat16*>(pos_table), reinterpret_cast<__nv_bfloat16*>(out), H);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
 __global__ void add_inplace_kernel(__nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b, size_t n) {
+  pdl_launch();
+  pdl_wait();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) a[i] = __float2bfloat16(__bfloat162float(a[i]) + __bfloat162float(b[i]));
 }
 
 void add_inplace(void* a, const void* b, size_t n, cudaStream_t st) {
   if (n == 0) return;
-  add_inplace_kernel<<<(n + 255) / 256, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(a),
-                                                      reinterpret_cast<const __nv_bfloat16*>(b), n);
+  launch_kernel(add_inplace_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st,
+                reinterpret_cast<__nv_bfloat16*>(a), reinterpret_cast<const __nv_bfloat16*>(b), n);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 

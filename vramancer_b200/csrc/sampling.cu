@@ -81,14 +81,47 @@ __device__ float block_sum(float v, float* sh) {
   return sh[0];
 }
 
+
+// Row argmax with 16-byte loads, four in flight per thread (the scan is latency-bound
+// when one CTA reads a whole 150k-entry row).
+__device__ __forceinline__ void upd8(ArgBest& b, uint4 v, int base) {
+  const uint32_t* p = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    b = better(b, ArgBest{bf16_lo(p[j]), base + 2 * j});
+    b = better(b, ArgBest{bf16_hi(p[j]), base + 2 * j + 1});
+  }
+}
+
+__device__ ArgBest row_argmax(const __nv_bfloat16* __restrict__ x, int V, ArgBest* sh) {
+  ArgBest best{-INFINITY, 0x7fffffff};
+  const int bd = blockDim.x;
+  if ((V & 7) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    const int nv = V >> 3;
+    int i = threadIdx.x;
+    for (; i + 3 * bd < nv; i += 4 * bd) {
+      const uint4 a0 = __ldg(xv + i), a1 = __ldg(xv + i + bd), a2 = __ldg(xv + i + 2 * bd), a3 = __ldg(xv + i + 3 * bd);
+      upd8(best, a0, i * 8);
+      upd8(best, a1, (i + bd) * 8);
+      upd8(best, a2, (i + 2 * bd) * 8);
+      upd8(best, a3, (i + 3 * bd) * 8);
+    }
+    for (; i < nv; i += bd) upd8(best, __ldg(xv + i), i * 8);
+  } else {
+    for (int i = threadIdx.x; i < V; i += bd) best = better(best, ArgBest{__bfloat162float(x[i]), i});
+  }
+  return block_argmax(best, sh);
+}
+
 __global__ void __launch_bounds__(kSampThreads)
     argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V, int* __restrict__ out) {
+  pdl_launch();
+  pdl_wait();
   __shared__ ArgBest sh[32];
   const int row = blockIdx.x;
   const __nv_bfloat16* x = logits + (size_t)row * ld;
-  ArgBest best{-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgBest{__bfloat162float(x[i]), i});
-  best = block_argmax(best, sh);
+  const ArgBest best = row_argmax(x, V, sh);
   if (threadIdx.x == 0) out[row] = best.i;
 }
 
@@ -158,6 +191,8 @@ __global__ void __launch_bounds__(kSampThreads)
     sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temperature,
                   const int* __restrict__ top_k, const float* __restrict__ top_p, uint64_t seed,
                   const int* __restrict__ steps, int* __restrict__ out) {
+  pdl_launch();
+  pdl_wait();
   __shared__ ArgBest sh[32];
   __shared__ float shf[32];
   __shared__ float hist[256];
@@ -167,9 +202,7 @@ __global__ void __launch_bounds__(kSampThreads)
   const __nv_bfloat16* x = logits + (size_t)row * ld;
   const float T = temperature ? temperature[row] : 0.f;
 
-  ArgBest best{-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgBest{__bfloat162float(x[i]), i});
-  best = block_argmax(best, sh);
+  const ArgBest best = row_argmax(x, V, sh);
   if (!(T > 0.f)) {
     if (threadIdx.x == 0) out[row] = best.i;
     return;
@@ -220,15 +253,16 @@ __global__ void __launch_bounds__(kSampThreads)
 
 void argmax_rows(const void* logits, int64_t ld, int B, int V, int* out, cudaStream_t st) {
   if (B <= 0) return;
-  argmax_kernel<<<B, kSampThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(logits), ld, V, out);
+  launch_kernel(argmax_kernel, dim3(B), dim3(kSampThreads), 0, st, reinterpret_cast<const __nv_bfloat16*>(logits), ld,
+                V, out);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
 void sample_rows(const void* logits, int64_t ld, int B, int V, const float* temperature, const int* top_k,
                  const float* top_p, uint64_t seed, const int* steps, int* out, cudaStream_t st) {
   if (B <= 0) return;
-  sample_kernel<<<B, kSampThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(logits), ld, V, temperature, top_k,
-                                            top_p, seed, steps, out);
+  launch_kernel(sample_kernel, dim3(B), dim3(kSampThreads), 0, st, reinterpret_cast<const __nv_bfloat16*>(logits), ld,
+                V, temperature, top_k, top_p, seed, steps, out);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 

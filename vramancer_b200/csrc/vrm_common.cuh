@@ -234,6 +234,15 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// pdl_wait: block until the preceding kernel in the stream has completed and its
+// writes are visible (no-op when the kernel was not launched with the programmatic
+// serialization attribute).  Every global read of a predecessor's output and every
+// global write must come after it.  pdl_launch: allow the next kernel's CTAs to be
+// scheduled now (they still pdl_wait before touching our outputs).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }

@@ -2,6 +2,7 @@
 #include "vrm_host.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 namespace vrm {
@@ -106,6 +107,14 @@ uint32_t* tile_counters_get(cudaStream_t stream) {
     VRM_CUDA_CHECK(cudaMemset(s.counters, 0, kCounterCount * sizeof(uint32_t)));
   }
   return s.counters;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VRM_PDL");
+    return !(e && (e[0] == '0' || e[0] == 'n' || e[0] == 'N'));
+  }();
+  return on;
 }
 
 int device_sm_count() {

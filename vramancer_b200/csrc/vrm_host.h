@@ -13,6 +13,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 namespace vrm {
 
@@ -52,5 +53,27 @@ size_t workspace_size();
 uint32_t* tile_counters_get(cudaStream_t stream);
 
 int device_sm_count();
+
+// Programmatic dependent launch on/off (env VRM_PDL, default on).
+bool pdl_enabled();
+
+// Launches `kern` with the programmatic-stream-serialization attribute when PDL is
+// enabled, so its CTAs may start while the previous kernel drains; every kernel
+// launched this way calls pdl_wait() before touching data the predecessor produced.
+template <typename... KArgs, typename... Args>
+void launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  VRM_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
 
 }  // namespace vrm
