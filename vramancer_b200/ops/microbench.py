@@ -1,0 +1,129 @@
+"""Kernel microbenchmarks with CUDA-event timing (also the small cases for ncu).
+
+    python -m vramancer_b200.ops.microbench gemm --m 1 --n 5120 --k 13824
+    python -m vramancer_b200.ops.microbench decode-attn --batch 32 --ctx 768
+    python -m vramancer_b200.ops.microbench all
+
+Reports achieved bandwidth / FLOP rate against MEASURED_PEAKS.json when present
+(copy bandwidth and cuBLAS bf16 throughput measured on this GPU type), otherwise
+against 6.65 TB/s and 1.59 PFLOP/s.
+
+Reference parity: core/layer_profiler.py:182-611 (GPU GFLOPS / bandwidth
+microbenchmarks) and core/benchmark.py.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from . import linear, paged_attention_decode, native
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"] / 1000.0, d["bf16_tflops"], "measured"
+    return 6.65, 1590.0, "fallback"
+
+
+def time_it(fn, iters=50, warm=5):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters * 1000.0  # us
+
+
+def bench_gemm(m, n, k, iters=50, copies=None):
+    """Rotates over enough weight copies to exceed L2 so every launch streams from HBM."""
+    hbm, tflops, src = peaks()
+    wbytes = n * k * 2
+    if copies is None:
+        copies = max(1, math.ceil(3 * 126e6 / wbytes))
+    ws = [torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.02 for _ in range(copies)]
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    state = [0]
+
+    def fn():
+        linear(x, ws[state[0] % copies], out=out)
+        state[0] += 1
+
+    us = time_it(fn, iters)
+    byts = wbytes + m * k * 2 + m * n * 2
+    flops = 2.0 * m * n * k
+    return {"kernel": "gemm", "m": m, "n": n, "k": k, "us": round(us, 2),
+            "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3),
+            "tflops": round(flops / us / 1e6, 1), "frac_tc": round(flops / us / 1e6 / tflops, 3),
+            "peaks": src}
+
+
+def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4, fp8=False, iters=50):
+    hbm, _, src = peaks()
+    ps = 16
+    pages = (ctx + ps - 1) // ps
+    P = batch * pages
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    cache = torch.randn(P, layers, 2, kv_heads, ps, head_dim, device="cuda").to(dt)
+    bt = torch.arange(P, dtype=torch.int32, device="cuda").view(batch, pages)
+    cl = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    q = torch.randn(batch, q_heads * head_dim, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    scale = torch.ones(layers, 2, kv_heads, device="cuda") if fp8 else None
+    state = [0]
+
+    def fn():
+        paged_attention_decode(q, cache, state[0] % layers, bt, cl, scale, 1 / math.sqrt(head_dim), q_heads, out=out)
+        state[0] += 1
+
+    us = time_it(fn, iters)
+    byts = batch * ctx * kv_heads * head_dim * 2 * cache.element_size()
+    return {"kernel": "decode_attn", "batch": batch, "ctx": ctx, "fp8": fp8, "us": round(us, 2),
+            "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
+
+
+QWEN14B_DECODE = [("qkv", 7168, 5120), ("o_proj", 5120, 5120), ("gate_up", 27648, 5120), ("down", 5120, 13824),
+                  ("lm_head", 152064, 5120)]
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["gemm", "decode-attn", "all"])
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--n", type=int, default=5120)
+    ap.add_argument("--k", type=int, default=13824)
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--ctx", type=int, default=768)
+    ap.add_argument("--fp8", action="store_true")
+    ap.add_argument("--iters", type=int, default=50)
+    a = ap.parse_args(argv)
+    native()
+    if a.what == "gemm":
+        print(json.dumps(bench_gemm(a.m, a.n, a.k, a.iters)))
+    elif a.what == "decode-attn":
+        print(json.dumps(bench_decode_attn(a.batch, a.ctx, fp8=a.fp8, iters=a.iters)))
+    else:
+        for m in (1, 32, 512):
+            for name, n, k in QWEN14B_DECODE:
+                r = bench_gemm(m, n, k, a.iters)
+                r["name"] = name
+                print(json.dumps(r))
+        for b in (1, 32):
+            for fp8 in (False, True):
+                print(json.dumps(bench_decode_attn(b, a.ctx, fp8=fp8, iters=a.iters)))
+
+
+if __name__ == "__main__":
+    main()
