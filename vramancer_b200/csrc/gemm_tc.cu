@@ -356,7 +356,8 @@ template <int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_streamk_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                              EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters,
-                             int k_tiles, int max_contrib, StreamK sk, uint32_t* __restrict__ err) {
+                             int k_tiles, int max_contrib, StreamK sk, uint32_t* __restrict__ err,
+                             unsigned long long* __restrict__ trace) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -374,6 +375,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int c = blockIdx.x;
   const int64_t it_begin = sk.start(c), it_end = sk.start(c + 1);
   constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  // optional timeline (ns, %globaltimer): [0] entry [1] after setup [2] after pdl_wait
+  // [3] first stage ready [4] last MMA issued [5] epilogue done
+  unsigned long long* tr = trace ? trace + (size_t)blockIdx.x * 8 : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer();
 
   pdl_launch();
   if (threadIdx.x == 0) {
@@ -398,6 +403,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (tr && threadIdx.x == 0) tr[1] = globaltimer();
 
   if (warp == 0 && lane == 0) {
     // ---------------- producer
@@ -414,6 +420,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tma_load_2d(sa, &map_w, &full_bar[g], k * kBK, t * kBM, pol_w);
     }
     pdl_wait();
+    if (tr) tr[2] = globaltimer();
     for (int g = 0; g < pre; ++g) {
       const int64_t it = it_begin + g;
       const int k = (int)(it % k_tiles);
@@ -454,6 +461,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           failed = true;
           break;
         }
+        if (tr && g == 0) tr[3] = globaltimer();
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + s * L::kStageBytes);
         const uint64_t da = make_sw128_desc(sa);
@@ -466,6 +474,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       umma_commit(&tfull[acc]);
       it += n;
     }
+    if (tr) tr[4] = globaltimer();
     // every MMA this thread issued must retire before TMEM is freed
     umma_commit(drain);
     mbar_wait(drain, 0, err);
@@ -540,6 +549,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       it += n;
     }
+    if (tr && threadIdx.x == 64) tr[5] = globaltimer();
   }
 
   tc_fence_before();
@@ -626,6 +636,10 @@ static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const EpiP
                 error_word());
 }
 
+// debug timeline buffer for the stream-K kernel (set by gemm_set_trace, null = off)
+static unsigned long long* g_gemm_trace = nullptr;
+void gemm_set_trace(void* buf) { g_gemm_trace = static_cast<unsigned long long*>(buf); }
+
 template <int BN, int STAGES>
 static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const EpiParams& ep, int N, int K,
                            int max_ctas, cudaStream_t stream) {
@@ -656,7 +670,7 @@ static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const E
     ws = static_cast<float*>(workspace_get((size_t)tiles * max_contrib * kBM * BN * sizeof(float), stream));
   }
   launch_kernel(kern, dim3(sk.ctas), dim3(kGemmThreads), (size_t)kSmem, stream, mw, mx, ep, ws, counters, k_tiles,
-                max_contrib, sk, error_word());
+                max_contrib, sk, error_word(), g_gemm_trace);
 }
 
 // Split count such that tiles * splits covers the SMs with >= min_k K-tiles per split.

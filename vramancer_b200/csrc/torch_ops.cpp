@@ -336,6 +336,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax, py::arg("logits"), py::arg("out"));
   m.def("sample", &sample, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"),
         py::arg("seed"), py::arg("steps"), py::arg("out"));
+  m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {
+    vrm::gemm_set_trace(buf.has_value() && buf->defined() ? buf->data_ptr() : nullptr);
+  });
   m.def("read_and_clear_errors", &vrm::read_and_clear_errors, "device error word (bounded-wait timeouts)");
   m.def("reserve_workspace", [](int64_t bytes) { vrm::workspace_reserve((size_t)bytes, cur_stream()); },
         "pre-allocate split-K / split-KV scratch before CUDA graph capture");

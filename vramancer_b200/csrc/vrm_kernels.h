@@ -35,6 +35,8 @@ struct GemmArgs {
   const void* residual = nullptr;   // optional: Y += residual[M, N] (same ld as out)
 };
 void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
+// Debug: per-CTA timeline of the stream-K decode GEMM into buf ([ctas][8] u64 ns), null = off.
+void gemm_set_trace(void* buf);
 
 // ---------------------------------------------------------------- norms / rope / elementwise (norm_rope.cu)
 // out = norm(x [+ residual]); when residual != null the sum is stored back into it.

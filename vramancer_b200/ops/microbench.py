@@ -94,13 +94,37 @@ def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4
             "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
 
 
+def trace_gemm(m, n, k):
+    """Per-CTA timeline (us from the earliest entry) of one stream-K decode GEMM launch."""
+    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.02
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    buf = torch.zeros(1024, 8, dtype=torch.int64, device="cuda")
+    linear(x, w)
+    torch.cuda.synchronize()
+    native().gemm_set_trace(buf)
+    linear(x, w)
+    torch.cuda.synchronize()
+    native().gemm_set_trace(None)
+    t = buf[buf[:, 0] > 0].double()
+    t0 = t[:, 0].min()
+    rel = (t[:, :6] - t0) / 1000.0
+    names = ["entry", "setup", "pdl_wait", "first_stage", "last_mma", "epi_done"]
+    med = rel.median(0).values.tolist()
+    mx = rel.max(0).values.tolist()
+    mn = rel.min(0).values.tolist()
+    return {"kernel": "gemm_trace", "m": m, "n": n, "k": k, "ctas": int(t.shape[0]),
+            "median_us": dict(zip(names, [round(v, 2) for v in med])),
+            "max_us": dict(zip(names, [round(v, 2) for v in mx])),
+            "min_us": dict(zip(names, [round(v, 2) for v in mn]))}
+
+
 QWEN14B_DECODE = [("qkv", 7168, 5120), ("o_proj", 5120, 5120), ("gate_up", 27648, 5120), ("down", 5120, 13824),
                   ("lm_head", 152064, 5120)]
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "decode-attn", "all"])
+    ap.add_argument("what", choices=["gemm", "decode-attn", "all", "trace"])
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--n", type=int, default=5120)
     ap.add_argument("--k", type=int, default=13824)
@@ -110,7 +134,12 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=50)
     a = ap.parse_args(argv)
     native()
-    if a.what == "gemm":
+    if a.what == "trace":
+        for name, n, k in QWEN14B_DECODE[:4]:
+            r = trace_gemm(a.m, n, k)
+            r["name"] = name
+            print(json.dumps(r))
+    elif a.what == "gemm":
         print(json.dumps(bench_gemm(a.m, a.n, a.k, a.iters)))
     elif a.what == "decode-attn":
         print(json.dumps(bench_decode_attn(a.batch, a.ctx, fp8=a.fp8, iters=a.iters)))
