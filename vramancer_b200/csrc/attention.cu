@@ -294,21 +294,48 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  // stage every split's (max, sum) in shared memory with parallel loads, turn them
+  // into merge weights, then each output element sums independent loads
+  float* s_w = reinterpret_cast<float*>(smem);          // [nsplit][G] maxima, then weights
+  float* s_ls = s_w + nsplit * G;                       // [nsplit][G] sums
+  float* s_L = s_ls + nsplit * G;                       // [G] totals
+  const float* ml = P.ws_ml + grp * nsplit * G * 2;
+  for (int i = threadIdx.x; i < nsplit * G; i += blockDim.x) {
+    s_w[i] = __ldcg(ml + 2 * i);
+    s_ls[i] = __ldcg(ml + 2 * i + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int h = threadIdx.x;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, s_w[sp * G + h]);
+    float L = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float w = (M == -INFINITY) ? 0.f : s_ls[sp * G + h] * exp2f(s_w[sp * G + h] - M);
+      s_w[sp * G + h] = w;
+      L += w;
+    }
+    s_L[h] = L;
+  }
+  __syncthreads();
+  const float* po = P.ws_o + grp * nsplit * G * D;
   for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
     const int h = idx / D, d = idx % D;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(P.ws_ml + ((grp * nsplit + s) * G + h) * 2));
-    float L = 0.f, acc = 0.f;
-    if (M != -INFINITY) {
-      for (int s = 0; s < nsplit; ++s) {
-        const float ms = __ldcg(P.ws_ml + ((grp * nsplit + s) * G + h) * 2);
-        const float ls = __ldcg(P.ws_ml + ((grp * nsplit + s) * G + h) * 2 + 1);
-        const float wgt = ls * exp2f(ms - M);
-        L += wgt;
-        acc += wgt * __ldcg(P.ws_o + ((grp * nsplit + s) * G + h) * D + d);
-      }
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int sp = 0;
+    for (; sp + 3 < nsplit; sp += 4) {
+      const float o0 = __ldcg(po + ((size_t)(sp + 0) * G + h) * D + d);
+      const float o1 = __ldcg(po + ((size_t)(sp + 1) * G + h) * D + d);
+      const float o2 = __ldcg(po + ((size_t)(sp + 2) * G + h) * D + d);
+      const float o3 = __ldcg(po + ((size_t)(sp + 3) * G + h) * D + d);
+      a0 += s_w[(sp + 0) * G + h] * o0;
+      a1 += s_w[(sp + 1) * G + h] * o1;
+      a2 += s_w[(sp + 2) * G + h] * o2;
+      a3 += s_w[(sp + 3) * G + h] * o3;
     }
-    const float r = L > 0.f ? acc / L * v_scale : 0.f;
+    for (; sp < nsplit; ++sp) a0 += s_w[sp * G + h] * __ldcg(po + ((size_t)sp * G + h) * D + d);
+    const float L = s_L[h];
+    const float r = L > 0.f ? (a0 + a1 + a2 + a3) / L * v_scale : 0.f;
     P.out[(size_t)b * P.ld_o + (size_t)(kvh * G + h) * D + d] = __float2bfloat16(r);
   }
   if (threadIdx.x == 0) P.counters[grp] = 0u;
@@ -544,11 +571,24 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
 
 // ============================================================== host
 int decode_attention_choose_splits(int B, int KH, int max_pages) {
-  const int sms = device_sm_count();
+  // resident CTAs per SM of the bf16 D=128 kernel (64 KB smem): 3
+  const int cap = device_sm_count() * 3;
   const int ctas = std::max(1, B * KH);
-  int s = (2 * sms + ctas - 1) / ctas;
-  s = std::min(s, std::max(1, (max_pages + 3) / 4));
-  return std::max(1, std::min(s, 128));
+  const int max_s = std::max(1, std::min(64, max_pages / 2));
+  int best = 1;
+  double best_score = -1.0;
+  for (int s = 1; s <= max_s; ++s) {
+    const long total = (long)ctas * s;
+    const long waves = (total + cap - 1) / cap;
+    const double util = (double)total / (double)(waves * cap);
+    // prefer full waves; small penalty per extra split (partials + merge traffic)
+    const double score = util - 0.004 * s - (waves > 4 ? 0.05 : 0.0);
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = s;
+    }
+  }
+  return best;
 }
 
 size_t decode_attention_scratch_bytes(int B, int Hq, int D, int splits) {

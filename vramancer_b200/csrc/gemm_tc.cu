@@ -353,7 +353,7 @@ struct StreamK {
 };
 
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, 2)
     gemm_streamk_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                              EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters,
                              int k_tiles, int max_contrib, StreamK sk, uint32_t* __restrict__ err,
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     umma_commit(drain);
     mbar_wait(drain, 0, err);
   } else if (warp >= 2) {
-    // ---------------- epilogue
+    // ---------------- epilogue (16-column chunks: no full accumulator row in registers)
     const int lane_base = 32 * (warp & 3);
     const int row = lane_base + lane;
     const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
@@ -493,55 +493,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int acc = seg & 1;
       const bool ok = mbar_wait(&tfull[acc], (uint32_t)((seg >> 1) & 1), err);
       tc_fence_after();
-      float v[BN];
-#pragma unroll
+      const int r_glob = t * kBM + row;   // weight row == output feature
+      int first_owner = 0, nc = 1;
+      float* slot = nullptr;
+      if (!whole) {
+        first_owner = sk.owner((int64_t)t * k_tiles);
+        nc = sk.owner((int64_t)t * k_tiles + k_tiles - 1) - first_owner + 1;
+        slot = workspace + ((size_t)t * max_contrib + (c - first_owner)) * (size_t)(kBM * BN);
+      }
+#pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t r[16];
         tmem_ld_32x32b_x16(t_lane + (uint32_t)(acc * BN + c0), r);
         tmem_wait_ld();
+        float v[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[c0 + j] = ok ? __uint_as_float(r[j]) : 0.f;
+        for (int j = 0; j < 16; ++j) v[j] = ok ? __uint_as_float(r[j]) : 0.f;
+        if (whole) {
+          epi_store<true>(ep, r_glob, c0, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(slot + (size_t)(c0 + j) * kBM + row, v[j]);
+        }
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
-      const int r_glob = t * kBM + row;   // weight row == output feature
-      if (whole) {
-#pragma unroll
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          float w16[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) w16[j] = v[c0 + j];
-          epi_store<true>(ep, r_glob, c0, w16);
-        }
-      } else {
-        const int first_owner = sk.owner((int64_t)t * k_tiles);
-        const int last_owner = sk.owner((int64_t)t * k_tiles + k_tiles - 1);
-        const int ci = c - first_owner;
-        float* slot = workspace + ((size_t)t * max_contrib + ci) * (size_t)(kBM * BN);
-#pragma unroll
-        for (int j = 0; j < BN; ++j) slot[(size_t)j * kBM + row] = v[j];
-        __threadfence();
+      if (!whole) {
+        // CTA barrier + one release/acquire atomic publishes the whole partial
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (threadIdx.x == 64) {
-          const uint32_t prev = atomicAdd(&tile_counters[t], 1u);
-          *flag_slot = (prev == (uint32_t)(last_owner - first_owner)) ? 1u : 0u;
+          uint32_t prev;
+          asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(tile_counters + t) : "memory");
+          *flag_slot = (prev == (uint32_t)(nc - 1)) ? 1u : 0u;
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (*flag_slot) {
-          __threadfence();
-#pragma unroll
-          for (int j = 0; j < BN; ++j) v[j] = 0.f;
-          for (int q = 0; q <= last_owner - first_owner; ++q) {
-            const float* src = workspace + ((size_t)t * max_contrib + q) * (size_t)(kBM * BN);
-#pragma unroll
-            for (int j = 0; j < BN; ++j) v[j] += __ldcg(src + (size_t)j * kBM + row);
-          }
-#pragma unroll
+          const float* base = workspace + (size_t)t * max_contrib * (size_t)(kBM * BN) + row;
+#pragma unroll 1
           for (int c0 = 0; c0 < BN; c0 += 16) {
-            float w16[16];
+            float v[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) w16[j] = v[c0 + j];
-            epi_store<true>(ep, r_glob, c0, w16);
+            for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            int q = 0;
+            for (; q + 1 < nc; q += 2) {
+              float x0[16], x1[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                x0[j] = __ldcg(base + (size_t)q * (kBM * BN) + (size_t)(c0 + j) * kBM);
+                x1[j] = __ldcg(base + (size_t)(q + 1) * (kBM * BN) + (size_t)(c0 + j) * kBM);
+              }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] += x0[j] + x1[j];
+            }
+            if (q < nc) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] += __ldcg(base + (size_t)q * (kBM * BN) + (size_t)(c0 + j) * kBM);
+            }
+            epi_store<true>(ep, r_glob, c0, v);
           }
           if (threadIdx.x == 64) tile_counters[t] = 0u;
         }
@@ -725,11 +733,13 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     const CUtensorMap mb = make_kmajor_map(a.x, a.M, a.K, a.ldx, BN);
     if (a.force_splits <= 0 && !legacy_decode()) {
       const int ctas = device_sm_count();
+      // <= 113 KB of smem per CTA: a CTA of the next GEMM fits beside it and (PDL)
+      // prefetches its weights while this one drains
       switch (BN) {
-        case 16: launch_streamk<16, 8>(ma, mb, ep, a.N, a.K, ctas, stream); break;
-        case 32: launch_streamk<32, 8>(ma, mb, ep, a.N, a.K, ctas, stream); break;
-        case 64: launch_streamk<64, 6>(ma, mb, ep, a.N, a.K, ctas, stream); break;
-        default: launch_streamk<128, 4>(ma, mb, ep, a.N, a.K, ctas, stream); break;
+        case 16: launch_streamk<16, 6>(ma, mb, ep, a.N, a.K, ctas, stream); break;
+        case 32: launch_streamk<32, 5>(ma, mb, ep, a.N, a.K, ctas, stream); break;
+        case 64: launch_streamk<64, 4>(ma, mb, ep, a.N, a.K, ctas, stream); break;
+        default: launch_streamk<128, 3>(ma, mb, ep, a.N, a.K, ctas, stream); break;
       }
       return;
     }
