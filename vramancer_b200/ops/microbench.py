@@ -33,10 +33,31 @@ def peaks():
     return 6.65, 1590.0, "fallback"
 
 
-def time_it(fn, iters=50, warm=5):
+def time_it(fn, iters=50, warm=5, graph=True):
+    """Per-call device time.  With graph=True the `iters` calls are captured in one CUDA
+    graph and replayed, so host launch overhead is excluded (as in the decode graph)."""
     for _ in range(warm):
         fn()
     torch.cuda.synchronize()
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters * 1000.0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(iters):
@@ -95,27 +116,32 @@ def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4
 
 
 def trace_gemm(m, n, k):
-    """Per-CTA timeline (us from the earliest entry) of one stream-K decode GEMM launch."""
-    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.02
+    """Per-CTA timelines of two back-to-back stream-K decode GEMM launches on cold
+    weights (us from the first launch's earliest CTA entry)."""
+    copies = max(2, math.ceil(3 * 126e6 / (n * k * 2)))
+    ws = [torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.02 for _ in range(copies)]
     x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
-    buf = torch.zeros(1024, 8, dtype=torch.int64, device="cuda")
-    linear(x, w)
+    bufs = [torch.zeros(1024, 8, dtype=torch.int64, device="cuda") for _ in range(2)]
+    for w in ws:
+        linear(x, w)
     torch.cuda.synchronize()
-    native().gemm_set_trace(buf)
-    linear(x, w)
+    native().gemm_set_trace(bufs[0])
+    linear(x, ws[0])
+    native().gemm_set_trace(bufs[1])
+    linear(x, ws[1])
     torch.cuda.synchronize()
     native().gemm_set_trace(None)
-    t = buf[buf[:, 0] > 0].double()
-    t0 = t[:, 0].min()
-    rel = (t[:, :6] - t0) / 1000.0
     names = ["entry", "setup", "pdl_wait", "first_stage", "last_mma", "epi_done"]
-    med = rel.median(0).values.tolist()
-    mx = rel.max(0).values.tolist()
-    mn = rel.min(0).values.tolist()
-    return {"kernel": "gemm_trace", "m": m, "n": n, "k": k, "ctas": int(t.shape[0]),
-            "median_us": dict(zip(names, [round(v, 2) for v in med])),
-            "max_us": dict(zip(names, [round(v, 2) for v in mx])),
-            "min_us": dict(zip(names, [round(v, 2) for v in mn]))}
+    t0 = bufs[0][bufs[0][:, 0] > 0][:, 0].double().min()
+    out = {"kernel": "gemm_trace", "m": m, "n": n, "k": k}
+    for i, b in enumerate(bufs):
+        t = b[b[:, 0] > 0].double()
+        rel = (t[:, :6] - t0) / 1000.0
+        out[f"launch{i}"] = {"ctas": int(t.shape[0]),
+                             "median": dict(zip(names, [round(v, 2) for v in rel.median(0).values.tolist()])),
+                             "min": dict(zip(names, [round(v, 2) for v in rel.min(0).values.tolist()])),
+                             "max": dict(zip(names, [round(v, 2) for v in rel.max(0).values.tolist()]))}
+    return out
 
 
 QWEN14B_DECODE = [("qkv", 7168, 5120), ("o_proj", 5120, 5120), ("gate_up", 27648, 5120), ("down", 5120, 13824),
