@@ -240,6 +240,4 @@ class LLMEngine:
     def _apply_cow(self) -> None:
         copies = self.kv.pop_cow_copies()
         if copies:
-            cache = self.runner.pool.cache
-            for src, dst in copies:
-                cache[dst].copy_(cache[src])
+            self.runner.copy_pages(copies)

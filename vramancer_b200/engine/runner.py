@@ -47,7 +47,8 @@ class ModelRunner:
         self.device = model.device
         self.max_batch = max_batch
         self.max_model_len = max_model_len
-        self.page_size = pool.spec.page_size
+        ref_pool = pool if pool is not None else model.pools[0]   # pipelines own one pool per stage
+        self.page_size = ref_pool.spec.page_size
         self.max_pages = (max_model_len + self.page_size - 1) // self.page_size
         self.use_graph = use_cuda_graph and self.device.type == "cuda"
         self.buckets = sorted(b for b in buckets if b <= max_batch) or [max_batch]
@@ -186,6 +187,14 @@ class ModelRunner:
         for B in sorted(sizes or self.buckets, reverse=True):
             if B not in self._graphs:
                 self.capture(B)
+
+    def copy_pages(self, pairs) -> None:
+        """Copy-on-write page copies (src, dst) in every KV pool this runner drives."""
+        if hasattr(self.model, "copy_pages"):
+            self.model.copy_pages(pairs)
+            return
+        for src, dst in pairs:
+            self.pool.cache[dst].copy_(self.pool.cache[src])
 
     def release_graphs(self) -> None:
         self._graphs.clear()

@@ -1,0 +1,143 @@
+"""Pipeline parallelism: contiguous layer ranges (stages) on different devices.
+
+`LocalPipeline` chains stages inside one process (several GPUs of one process, or
+several CPU "devices"): stage i runs its layers over its own KV pool and hands the
+residual stream to stage i+1 (peer copy between GPUs).  It exposes the same
+`forward(batch, pool)` / `device` / `kvh` surface as a single `DecoderModel`, so the
+model runner and the continuous-batching engine drive it unchanged.
+
+`DistPipeline` runs one stage per process group of ranks (PP x TP grid): the hidden
+state crosses stages with NCCL point-to-point send/recv between ranks holding the
+same TP index, and the last stage broadcasts its logits-derived tokens through the
+runner.  Stage boundaries come from `placement.split_model_into_blocks`.
+
+Reference parity: the reference's production PP is accelerate `device_map="auto"`
+(core/backends.py:1314-1352) with activations moved by a patched `send_to_device`
+(core/inference_pipeline.py:445-495); its manual block path is broken
+(RESULTAT_PALIER_A1.md:12-22, no cache_position).  Here every stage keeps its own
+paged KV, so a split model decodes token-for-token like the single-device one.
+"""
+from __future__ import annotations
+
+from dataclasses import fields, replace
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ..kv.pool import KVPool, KVPoolSpec
+from ..models.config import ModelConfig
+from ..models.transformer import DecoderModel, ForwardBatch, TPContext
+from ..models.weights import random_weights
+from .placement import Block
+
+
+def batch_to(batch: ForwardBatch, device: torch.device) -> ForwardBatch:
+    kw = {}
+    for f in fields(ForwardBatch):
+        v = getattr(batch, f.name)
+        kw[f.name] = v.to(device, non_blocking=True) if isinstance(v, torch.Tensor) else v
+    return ForwardBatch(**kw)
+
+
+def default_transfer(x: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """Residual stream hop between stages (GPU->GPU uses the peer copy engine path)."""
+    if x.device == device:
+        return x.clone()
+    return x.to(device, non_blocking=True)
+
+
+class LocalPipeline:
+    def __init__(self, stages: Sequence[Tuple[DecoderModel, KVPool]],
+                 transfer: Callable[[torch.Tensor, torch.device], torch.Tensor] = default_transfer):
+        assert stages, "need at least one stage"
+        self.stages = list(stages)
+        self.transfer = transfer
+        self.cfg = self.stages[0][0].cfg
+        self.device = self.stages[0][0].device
+        self.kvh = self.stages[0][0].kvh
+        self.hops = 0
+
+    @property
+    def pools(self) -> List[KVPool]:
+        return [p for _, p in self.stages]
+
+    def forward(self, batch: ForwardBatch, pool=None, hidden=None) -> torch.Tensor:
+        h = hidden
+        for i, (m, p) in enumerate(self.stages):
+            b = batch if m.device == batch.input_ids.device else batch_to(batch, m.device)
+            if i > 0:
+                h = self.transfer(h, m.device)
+                self.hops += 1
+            h = m.forward(b, p, hidden=h)
+        return h
+
+    def copy_pages(self, pairs) -> None:
+        for _, p in self.stages:
+            for src, dst in pairs:
+                p.cache[dst].copy_(p.cache[src])
+
+
+def build_local_pipeline(cfg: ModelConfig, blocks: Sequence[Block], *, num_pages: int, dtype=torch.float32,
+                         kv_dtype=None, weights=None, seed: int = 0, std: float = 0.02) -> LocalPipeline:
+    """One DecoderModel + KV pool per block; weights shared with a single-device model
+    when `weights` (a full dict) is given, else random-init with the same per-tensor
+    seeds as `random_weights(cfg, seed=seed)`."""
+    stages = []
+    kv_dtype = kv_dtype or dtype
+    for blk in blocks:
+        dev = torch.device(blk.device)
+        layers = range(blk.start, blk.end)
+        if weights is not None:
+            w = {k: v.to(dev) for k, v in weights.items()
+                 if (k.startswith("layers.") and blk.start <= int(k.split(".")[1]) < blk.end)
+                 or (not k.startswith("layers.") and ((blk.start == 0 and k in ("embed", "pos_embed"))
+                                                      or (blk.end == cfg.num_layers and k in (
+                                                          "final_norm_w", "final_norm_b", "lm_head"))))}
+        else:
+            w = random_weights(cfg, device=dev, dtype=dtype, seed=seed, std=std, layers=layers,
+                               embed=blk.start == 0, head=blk.end == cfg.num_layers)
+        m = DecoderModel(cfg, w, device=dev, dtype=dtype, first_layer=blk.start, last_layer=blk.end)
+        spec = KVPoolSpec(num_pages, blk.end - blk.start, cfg.num_kv_heads, cfg.head_dim, dtype=kv_dtype)
+        stages.append((m, KVPool(spec, dev)))
+    return LocalPipeline(stages)
+
+
+class DistPipelineStage:
+    """One pipeline stage of a multi-process PP x TP job (NCCL send/recv between stages).
+
+    Ranks are laid out stage-major: rank = stage * tp_size + tp_rank.  The stage
+    model runs on this rank's GPU; `forward` receives the residual stream from the
+    previous stage (same tp_rank), runs the local layers and sends it on.  The last
+    stage returns logits; other stages return None.
+    """
+
+    def __init__(self, model: DecoderModel, pool: KVPool, stage: int, num_stages: int, tp_size: int,
+                 group=None):
+        self.model, self.pool = model, pool
+        self.stage, self.num_stages, self.tp_size = stage, num_stages, tp_size
+        self.device = model.device
+        self.kvh = model.kvh
+        self.cfg = model.cfg
+        self.rank = dist.get_rank()
+        self.group = group
+
+    @property
+    def is_first(self):
+        return self.stage == 0
+
+    @property
+    def is_last(self):
+        return self.stage == self.num_stages - 1
+
+    def forward(self, batch: ForwardBatch, pool=None, hidden=None):
+        T = batch.num_tokens
+        h = None
+        if not self.is_first:
+            h = torch.empty(T, self.cfg.hidden_size, dtype=self.model.dtype, device=self.device)
+            dist.recv(h, src=self.rank - self.tp_size, group=self.group)
+        out = self.model.forward(batch, self.pool, hidden=h)
+        if not self.is_last:
+            dist.send(out.contiguous(), dst=self.rank + self.tp_size, group=self.group)
+            return None
+        return out
