@@ -78,7 +78,8 @@ class Request:
 
 class LLMEngine:
     def __init__(self, runner: ModelRunner, manager: PagedKVCacheManager, *, max_batch: Optional[int] = None,
-                 max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None):
+                 max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, spec_num_draft: int = 0,
+                 spec_ngram: int = 3):
         self.runner = runner
         self.kv = manager
         self.max_batch = max_batch or runner.max_batch
@@ -89,6 +90,11 @@ class LLMEngine:
         self.running: List[Request] = []
         self._lock = threading.RLock()
         self.stats = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "finished": 0, "preempted": 0}
+        # prompt-lookup speculative decoding inside continuous batching (0 = off)
+        self.spec_num_draft = spec_num_draft
+        self.spec_ngram = spec_ngram
+        from .speculative import SpecStats
+        self.spec_stats = SpecStats()
 
     # ------------------------------------------------------------------ API
     def add_request(self, prompt_ids: Sequence[int], params: Optional[SamplingParams] = None, *,
@@ -214,6 +220,17 @@ class LLMEngine:
     def _decode(self, done: List[Request]) -> None:
         active = [r for r in self.running if r.prefill_done and not r.finished and r.output_ids]
         if not active:
+            return
+        if self.spec_num_draft > 0:
+            from .speculative import speculative_decode_step
+            outs = speculative_decode_step(self, active, self.spec_ngram, self.spec_num_draft, self.spec_stats)
+            for r, toks in zip(active, outs):
+                for t in toks:
+                    self.stats["decode_tokens"] += 1
+                    self._emit(r, int(t))
+                    if r.finished:
+                        done.append(r)
+                        break
             return
         ids, pos, slots, ctx, bts = [], [], [], [], []
         temp, topk, topp, steps = [], [], [], []

@@ -1,0 +1,199 @@
+"""Speculative decoding: prompt lookup (n-gram drafts) and draft-model proposals,
+verified by one forward of the target over all proposals.
+
+Verification is a chunked-prefill forward over the paged cache: every sequence
+feeds [last token, d_1 .. d_k] at its next positions, the kernels attend over the
+cached prefix plus the new rows, and greedy predictions p_0..p_k come back for all
+rows at once (batched across sequences).  Drafts are accepted while d_i == p_{i-1};
+the first mismatch contributes p_j as a bonus token; KV of rejected positions is
+truncated from the block table (their slots are simply rewritten later).  Greedy
+output is identical to plain decoding.
+
+Reference parity: prompt lookup = HF `prompt_lookup_num_tokens`
+(core/backends.py:1920-1925, vramancer/dropin.py wrap-generate); draft model =
+core/speculative_decoding.py:95-329 (gamma-adaptive, window 10), whose stochastic
+acceptance (`q > 0.5`, :268-281) is not rejection sampling and is not reproduced:
+sampled requests are not speculated here.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from .. import ops
+from .runner import PrefillItem
+
+
+def find_draft(seq: Sequence[int], max_ngram: int = 3, num_draft: int = 8, min_ngram: int = 1) -> List[int]:
+    """Continuation of the most recent earlier occurrence of the sequence's last n-gram
+    (n from max_ngram down to min_ngram)."""
+    L = len(seq)
+    for n in range(min(max_ngram, L - 1), min_ngram - 1, -1):
+        tail = list(seq[L - n:])
+        # scan backwards for the latest match that has a continuation
+        for s in range(L - n - 1, -1, -1):
+            if list(seq[s:s + n]) == tail:
+                cont = list(seq[s + n:s + n + num_draft])
+                if cont:
+                    return cont
+    return []
+
+
+def accept_greedy(draft: Sequence[int], preds: Sequence[int]) -> Tuple[List[int], int]:
+    """(accepted drafts + bonus token, number of accepted drafts)."""
+    acc = []
+    for i, d in enumerate(draft):
+        if int(preds[i]) == int(d):
+            acc.append(int(d))
+        else:
+            break
+    return acc + [int(preds[len(acc)])], len(acc)
+
+
+class SpecStats:
+    def __init__(self):
+        self.proposed = 0
+        self.accepted = 0
+        self.steps = 0
+
+    @property
+    def acceptance(self) -> float:
+        return self.accepted / self.proposed if self.proposed else 0.0
+
+    def to_dict(self):
+        return {"proposed": self.proposed, "accepted": self.accepted, "steps": self.steps,
+                "acceptance": round(self.acceptance, 4)}
+
+
+def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: SpecStats,
+                            drafts: Optional[List[List[int]]] = None):
+    """One verify step for `active` requests of an LLMEngine (greedy ones get drafts)."""
+    kv, runner = engine.kv, engine.runner
+    items, feeds, starts, ds = [], [], [], []
+    for i, r in enumerate(active):
+        seq = r.prompt_ids + r.output_ids
+        room = min(r.params.max_tokens - len(r.output_ids) - 1, engine.max_model_len - len(seq) - 1)
+        if drafts is not None:
+            d = list(drafts[i])
+        elif r.params.greedy and num_draft > 0:
+            d = find_draft(seq, ngram, num_draft)
+        else:
+            d = []
+        d = d[:max(0, room)]
+        feed = [seq[-1]] + d
+        start = len(seq) - 1
+        slots = kv.append_slots(r.request_id, len(feed))
+        items.append(PrefillItem(feed, start, slots, kv.block_table(r.request_id), start + len(feed), True))
+        feeds.append(feed)
+        starts.append(start)
+        ds.append(d)
+    engine._apply_cow()
+    logits = runner.prefill_logits(items)
+    if logits.is_cuda:
+        preds = ops.argmax(logits).cpu().tolist()
+    else:
+        preds = torch.argmax(logits.float(), -1).tolist()
+    out = []
+    off = 0
+    stats.steps += 1
+    for r, feed, start, d in zip(active, feeds, starts, ds):
+        p = preds[off:off + len(feed)]
+        off += len(feed)
+        if r.params.greedy:
+            toks, na = accept_greedy(d, p)
+        else:
+            # non-greedy: take the sampled token for the first position only
+            toks, na = [int(p[0])], 0
+        stats.proposed += len(d)
+        stats.accepted += na
+        kv.truncate(r.request_id, start + 1 + na)
+        out.append(toks)
+    return out
+
+
+class PromptLookupDecoder:
+    """Single-sequence greedy generation with prompt-lookup drafts through an LLM."""
+
+    def __init__(self, llm, num_draft: int = 8, ngram: int = 3):
+        self.llm = llm
+        self.num_draft = num_draft
+        self.ngram = ngram
+        self.stats = SpecStats()
+
+    def generate(self, prompt_ids: Sequence[int], max_new_tokens: int) -> List[int]:
+        eng = self.llm.engine
+        from .engine import SamplingParams
+        with eng._lock:
+            req = eng.add_request(prompt_ids, SamplingParams(max_tokens=max_new_tokens))
+            eng.waiting.remove(req)
+            eng.kv.allocate(req.request_id, len(req.prompt_ids))
+            eng.running.append(req)
+            try:
+                # prefill (+ first token)
+                toks = eng.runner.prefill([PrefillItem(req.prompt_ids, 0, eng.kv.slots_for(req.request_id, 0,
+                                                                                          len(req.prompt_ids)),
+                                                       eng.kv.block_table(req.request_id), len(req.prompt_ids),
+                                                       True)], [0.0], [0], [1.0], [0])
+                req.num_computed = len(req.prompt_ids)
+                eng._emit(req, int(toks[0]))
+                while not req.finished:
+                    new = speculative_decode_step(eng, [req], self.ngram, self.num_draft, self.stats)[0]
+                    for t in new:
+                        eng._emit(req, t)
+                        if req.finished:
+                            break
+            finally:
+                if not req.finished:
+                    eng._finish(req, "abort")
+        return list(req.output_ids)
+
+
+class DraftModelDecoder:
+    """Draft-model speculation: a small model proposes gamma tokens greedily, the
+    target verifies them in one forward; gamma adapts to the running acceptance
+    (window of recent rounds) between gamma_min and gamma_max."""
+
+    def __init__(self, target, draft, gamma: int = 5, adaptive: bool = True, gamma_min: int = 2, gamma_max: int = 12,
+                 window: int = 10):
+        self.target, self.draft = target, draft
+        self.gamma = gamma
+        self.adaptive = adaptive
+        self.gmin, self.gmax, self.window = gamma_min, gamma_max, window
+        self.recent: List[float] = []
+        self.stats = SpecStats()
+
+    def _propose(self, seq: List[int], k: int) -> List[int]:
+        from .engine import SamplingParams
+        r = self.draft.engine.generate([seq], SamplingParams(max_tokens=k))[0]
+        return r.output_ids
+
+    def generate(self, prompt_ids: Sequence[int], max_new_tokens: int) -> List[int]:
+        eng = self.target.engine
+        from .engine import SamplingParams
+        with eng._lock:
+            req = eng.add_request(prompt_ids, SamplingParams(max_tokens=max_new_tokens))
+            eng.waiting.remove(req)
+            eng.kv.allocate(req.request_id, len(req.prompt_ids))
+            eng.running.append(req)
+            toks = eng.runner.prefill([PrefillItem(req.prompt_ids, 0, eng.kv.slots_for(req.request_id, 0,
+                                                                                      len(req.prompt_ids)),
+                                                   eng.kv.block_table(req.request_id), len(req.prompt_ids), True)],
+                                      [0.0], [0], [1.0], [0])
+            req.num_computed = len(req.prompt_ids)
+            eng._emit(req, int(toks[0]))
+            while not req.finished:
+                seq = req.prompt_ids + req.output_ids
+                d = self._propose(seq, self.gamma)
+                new = speculative_decode_step(eng, [req], 0, 0, self.stats, drafts=[d])[0]
+                if d:
+                    self.recent = (self.recent + [(len(new) - 1) / len(d)])[-self.window:]
+                if self.adaptive and len(self.recent) >= 3:
+                    rate = sum(self.recent) / len(self.recent)
+                    self.gamma = min(self.gmax, self.gamma + 1) if rate > 0.8 else (
+                        max(self.gmin, self.gamma - 1) if rate < 0.4 else self.gamma)
+                for t in new:
+                    eng._emit(req, t)
+                    if req.finished:
+                        break
+        return list(req.output_ids)

@@ -34,7 +34,8 @@ class LLM:
                  max_model_len: int = 4096, kv_pages: Optional[int] = None, gpu_memory_utilization: float = 0.9,
                  seed: int = 0, use_cuda_graph: bool = True, enable_prefix_cache: bool = True,
                  max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, weights=None,
-                 num_layers: Optional[int] = None, tp=None):
+                 num_layers: Optional[int] = None, tp=None, quantization: Optional[str] = None,
+                 spec_num_draft: int = 0, spec_ngram: int = 3):
         if isinstance(model, ModelConfig):
             cfg = model
         else:
@@ -54,6 +55,12 @@ class LLM:
             else:
                 weights = random_weights(cfg, device=self.device, dtype=dtype, seed=seed, tp_rank=tp_rank,
                                          tp_size=tp_size)
+        self.quantization = (quantization or "").lower() or None
+        if self.quantization == "nvfp4":
+            from .quant.nvfp4 import quantize_model_weights
+            weights = quantize_model_weights(weights, cfg)
+        elif self.quantization not in (None, "none", "bf16"):
+            raise ValueError(f"unsupported quantization {quantization!r} (nvfp4 or none)")
         self.weights = weights
         self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype, tp=tp)
         kvd = kv_dtype_from_str(kv_cache_dtype)
@@ -65,7 +72,7 @@ class LLM:
         self.runner = ModelRunner(self.model, self.pool, max_batch=max_batch, max_model_len=max_model_len,
                                   use_cuda_graph=use_cuda_graph, seed=seed)
         self.engine = LLMEngine(self.runner, self.kv, max_prefill_tokens=max_prefill_tokens,
-                                eos_token_id=eos_token_id)
+                                eos_token_id=eos_token_id, spec_num_draft=spec_num_draft, spec_ngram=spec_ngram)
 
     def _pages_from_memory(self, cfg, kvd, util, max_batch, max_model_len) -> int:
         need = max_batch * ((max_model_len + 15) // 16) + 16
