@@ -62,6 +62,8 @@ class InferencePipeline:
         self.loaded_at: Optional[float] = None
         self.lora = None
         self.spec = None
+        self._bcast = None            # TP serving: rank 0 broadcasts request events
+        self._events: List = []
 
     # ------------------------------------------------------------------ load
     def load(self, model_name: str, num_gpus: Optional[int] = None, *, max_batch: int = 64,
@@ -90,6 +92,8 @@ class InferencePipeline:
                                max_model_len=max_model_len, kv_pages=kv_pages, tp=tp, use_cuda_graph=graph,
                                quantization=quantization, **kw)
                 self.mode = f"tp{world}"
+                from .parallel.follower import StepBroadcaster
+                self._bcast = StepBroadcaster()
             elif has_cuda and num_gpus > 1:
                 self.llm = self._build_pp(cfg, num_gpus, max_batch, max_model_len, kv_pages, kvd, dtype, **kw)
                 self.mode = f"pp{num_gpus}"
@@ -147,6 +151,16 @@ class InferencePipeline:
     def _loop(self) -> None:
         while not self._stop.is_set():
             eng = self.engine
+            if self._bcast is not None:
+                # keep follower ranks in lockstep: same events, then the same step
+                with self._wake:
+                    ev, self._events = self._events, []
+                if ev or (eng is not None and eng.has_unfinished()):
+                    self._bcast.exchange(ev)
+                else:
+                    with self._wake:
+                        self._wake.wait(0.02)
+                    continue
             if eng is None or not eng.has_unfinished():
                 with self._wake:
                     self._wake.wait(0.02)
@@ -185,6 +199,11 @@ class InferencePipeline:
         params = SamplingParams(max_tokens=self.autoheal.scaled(max_new_tokens), temperature=temperature,
                                 top_k=top_k, top_p=top_p, stop_token_ids=tuple(stop_token_ids))
         req = self.engine.add_request(ids, params, request_id=request_id, on_token=on_token)
+        if self._bcast is not None:
+            with self._wake:
+                self._events.append(("add", (ids, {"max_tokens": params.max_tokens, "temperature": temperature,
+                                                   "top_k": top_k, "top_p": top_p,
+                                                   "stop_token_ids": tuple(stop_token_ids)}, req.request_id)))
         if self.enable_metrics:
             METRICS.infer_requests.labels("submit").inc()
             METRICS.prompt_tokens.inc(len(ids))
@@ -283,6 +302,11 @@ class InferencePipeline:
         return {"tokens": toks, "seconds": dt, "tok_s": toks / dt, "ttft_p50_ms": 1000 * ttfts[len(ttfts) // 2]}
 
     def shutdown(self) -> None:
+        if self._bcast is not None:
+            try:
+                self._bcast.exchange("stop")
+            except Exception:
+                pass
         self._stop.set()
         self._kick()
         if self._thread is not None:
