@@ -303,6 +303,26 @@ void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k
                    out.data_ptr<int>(), cur_stream());
 }
 
+// ---------------------------------------------------------------- page migration
+void page_copy(const Tensor& src_pool, Tensor& dst_pool, const Tensor& src_idx, const Tensor& dst_idx) {
+  TORCH_CHECK(src_pool.is_cuda() && dst_pool.is_cuda() && src_pool.is_contiguous() && dst_pool.is_contiguous(),
+              "page_copy: contiguous CUDA pools");
+  TORCH_CHECK(src_pool.dim() >= 1 && dst_pool.dim() >= 1 && src_pool.nbytes() / src_pool.size(0) ==
+                  dst_pool.nbytes() / dst_pool.size(0), "page_copy: pools must have the same page size");
+  TORCH_CHECK(src_idx.scalar_type() == torch::kInt32 && dst_idx.scalar_type() == torch::kInt32 &&
+                  src_idx.numel() == dst_idx.numel() && src_idx.device() == src_pool.device() &&
+                  dst_idx.device() == src_pool.device(),
+              "page_copy: int32 index tensors on the source device");
+  const size_t page_bytes = src_pool.nbytes() / src_pool.size(0);
+  const c10::cuda::CUDAGuard guard(src_pool.device());
+  if (src_pool.device() != dst_pool.device()) {
+    TORCH_CHECK(vrm::enable_peer_access(src_pool.device().index(), dst_pool.device().index()),
+                "page_copy: no peer access between the two GPUs");
+  }
+  vrm::page_copy(src_pool.data_ptr(), dst_pool.data_ptr(), src_idx.data_ptr<int>(), dst_idx.data_ptr<int>(),
+                 (int)src_idx.numel(), page_bytes, cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -339,6 +359,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {
     vrm::gemm_set_trace(buf.has_value() && buf->defined() ? buf->data_ptr() : nullptr);
   });
+  m.def("page_copy", &page_copy, py::arg("src_pool"), py::arg("dst_pool"), py::arg("src_idx"), py::arg("dst_idx"),
+        "copy whole KV pages between pools (peer GPU allowed), runs on the source device");
+  m.def("enable_peer_access", &vrm::enable_peer_access, py::arg("device"), py::arg("peer"));
   m.def("read_and_clear_errors", &vrm::read_and_clear_errors, "device error word (bounded-wait timeouts)");
   m.def("reserve_workspace", [](int64_t bytes) { vrm::workspace_reserve((size_t)bytes, cur_stream()); },
         "pre-allocate split-K / split-KV scratch before CUDA graph capture");

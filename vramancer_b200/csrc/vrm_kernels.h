@@ -116,4 +116,12 @@ void argmax_rows(const void* logits, int64_t ld, int B, int V, int* out, cudaStr
 void sample_rows(const void* logits, int64_t ld, int B, int V, const float* temperature, const int* top_k,
                  const float* top_p, uint64_t seed, const int* steps, int* out, cudaStream_t stream);
 
+// ---------------------------------------------------------------- KV page migration (migrate.cu)
+// dst_pool[dst_idx[i]] <- src_pool[src_idx[i]] for whole pages of page_bytes; runs on the
+// current (source) device; dst_pool may be a peer GPU's memory (peer access enabled).
+void page_copy(const void* src_pool, void* dst_pool, const int* src_idx, const int* dst_idx, int n_pages,
+               size_t page_bytes, cudaStream_t stream);
+// Enables device -> peer access for this process (no-op if already enabled); false if unsupported.
+bool enable_peer_access(int device, int peer);
+
 }  // namespace vrm
