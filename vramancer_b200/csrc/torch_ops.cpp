@@ -16,6 +16,21 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream(); }
 
 bool has(const OptT& t) { return t.has_value() && t->defined(); }
 
+// Every tensor argument of one launch must live on the same device as `ref`: a kernel
+// given another GPU's pointer would fault instead of failing here.
+void same_device(const Tensor& ref, std::initializer_list<const Tensor*> ts, const char* op) {
+  for (const Tensor* t : ts)
+    if (t && t->defined())
+      TORCH_CHECK(t->device() == ref.device(), op, ": all tensors must be on ", ref.device(), ", got one on ",
+                  t->device());
+}
+void same_device_opt(const Tensor& ref, std::initializer_list<const OptT*> ts, const char* op) {
+  for (const OptT* t : ts)
+    if (t && has(*t))
+      TORCH_CHECK((*t)->device() == ref.device(), op, ": all tensors must be on ", ref.device(), ", got one on ",
+                  (*t)->device());
+}
+
 void check_bf16_2d(const Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, ": must be a CUDA tensor");
   TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, ": must be bf16");
@@ -41,6 +56,8 @@ void gemm_out(const Tensor& x, const Tensor& w, const OptT& bias, Tensor& out, i
   check_bf16_2d(out, "gemm out");
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K, "gemm: K mismatch (", K, " vs ", w.size(1), ")");
+  same_device(x, {&w, &out}, "gemm");
+  same_device_opt(x, {&bias, &residual}, "gemm");
   const int64_t n_out = epilogue == vrm::kEpiSiluMul ? N / 2 : N;
   TORCH_CHECK(out.size(0) == M && out.size(1) == n_out, "gemm: out must be [", M, ", ", n_out, "]");
   vrm::GemmArgs a;
@@ -83,6 +100,8 @@ void rmsnorm(const Tensor& x, const OptT& residual, const Tensor& w, Tensor& out
   check_bf16_2d(out, "rmsnorm out");
   TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.is_contiguous() && w.numel() == x.size(1), "rmsnorm: weight");
   TORCH_CHECK(x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "rmsnorm: row strides must be multiples of 8");
+  same_device(x, {&w, &out}, "rmsnorm");
+  same_device_opt(x, {&residual}, "rmsnorm");
   void* rp = nullptr;
   if (has(residual)) {
     TORCH_CHECK(residual->is_contiguous() && residual->sizes() == x.sizes() &&
@@ -101,6 +120,8 @@ void layernorm(const Tensor& x, const OptT& residual, const Tensor& w, const Ten
   TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.is_contiguous() && w.numel() == x.size(1), "layernorm: weight");
   TORCH_CHECK(b.scalar_type() == torch::kBFloat16 && b.is_contiguous() && b.numel() == x.size(1), "layernorm: bias");
   TORCH_CHECK(x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "layernorm: row strides must be multiples of 8");
+  same_device(x, {&w, &b, &out}, "layernorm");
+  same_device_opt(x, {&residual}, "layernorm");
   void* rp = nullptr;
   if (has(residual)) {
     TORCH_CHECK(residual->is_contiguous() && residual->sizes() == x.sizes() &&
@@ -121,6 +142,8 @@ void rope_kv_write(Tensor& qkv, const OptT& positions, const OptT& cos_sin, Tens
   check_cache(cache);
   TORCH_CHECK(cache.size(3) == KH && cache.size(5) == D, "rope: cache kv_heads/head_dim mismatch");
   TORCH_CHECK(layer >= 0 && layer < cache.size(1), "rope: layer out of range");
+  same_device(qkv, {&cache}, "rope_kv_write");
+  same_device_opt(qkv, {&positions, &cos_sin, &slot_mapping, &kv_scale}, "rope_kv_write");
   vrm::RopeKvArgs a;
   a.qkv = qkv.data_ptr();
   a.ld_qkv = qkv.stride(0);
@@ -163,6 +186,7 @@ void silu_mul(const Tensor& x, Tensor& out) {
   check_bf16_2d(x, "silu_mul x");
   check_bf16_2d(out, "silu_mul out");
   TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) * 2 == x.size(1), "silu_mul: out must be [T, I] for x [T, 2I]");
+  same_device(x, {&out}, "silu_mul");
   const c10::cuda::CUDAGuard guard(x.device());
   vrm::silu_mul(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0), (int)x.size(0), (int)out.size(1),
                 cur_stream());
@@ -178,6 +202,8 @@ void embedding(const Tensor& ids, const Tensor& table, const OptT& pos, const Op
   TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == torch::kInt32 && ids.is_contiguous(), "embedding: int32 ids");
   TORCH_CHECK(table.scalar_type() == torch::kBFloat16 && table.is_contiguous() && table.dim() == 2, "embedding: table");
   TORCH_CHECK(out.is_contiguous() && out.size(0) == ids.numel() && out.size(1) == table.size(1), "embedding: out");
+  same_device(ids, {&table, &out}, "embedding");
+  same_device_opt(ids, {&pos, &pos_table}, "embedding");
   const int* pp = nullptr;
   const void* pt = nullptr;
   if (has(pos_table)) {
@@ -195,6 +221,7 @@ void add_(Tensor& a, const Tensor& b) {
   TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && a.numel() == b.numel() &&
                   a.scalar_type() == torch::kBFloat16 && b.scalar_type() == torch::kBFloat16,
               "add_: contiguous bf16 of equal size");
+  same_device(a, {&b}, "add_");
   const c10::cuda::CUDAGuard guard(a.device());
   vrm::add_inplace(a.data_ptr(), b.data_ptr(), a.numel(), cur_stream());
 }
@@ -214,6 +241,8 @@ void attn_decode(const Tensor& q, const Tensor& cache, int64_t layer, const Tens
   const int64_t B = q.size(0);
   TORCH_CHECK(block_tables.size(0) >= B && context_lens.numel() >= B && out.size(0) >= B, "decode: batch sizes");
   TORCH_CHECK(layer >= 0 && layer < cache.size(1), "decode: layer out of range");
+  same_device(q, {&cache, &block_tables, &context_lens, &out}, "paged_attention_decode");
+  same_device_opt(q, {&kv_scale}, "paged_attention_decode");
   vrm::DecodeAttnArgs a;
   a.q = q.data_ptr();
   a.ld_q = q.stride(0);
@@ -252,6 +281,8 @@ void attn_prefill(const Tensor& q, const Tensor& cache, int64_t layer, const Ten
                   block_tables.scalar_type() == torch::kInt32 && block_tables.stride(1) == 1,
               "prefill: int32 metadata");
   TORCH_CHECK(layer >= 0 && layer < cache.size(1), "prefill: layer out of range");
+  same_device(q, {&cache, &block_tables, &cu_q, &context_lens, &out}, "paged_attention_prefill");
+  same_device_opt(q, {&kv_scale}, "paged_attention_prefill");
   vrm::PrefillAttnArgs a;
   a.q = q.data_ptr();
   a.ld_q = q.stride(0);
@@ -283,6 +314,7 @@ void attn_prefill(const Tensor& q, const Tensor& cache, int64_t layer, const Ten
 void argmax(const Tensor& logits, Tensor& out) {
   check_bf16_2d(logits, "argmax logits");
   TORCH_CHECK(out.scalar_type() == torch::kInt32 && out.numel() >= logits.size(0), "argmax: int32 out");
+  same_device(logits, {&out}, "argmax");
   const c10::cuda::CUDAGuard guard(logits.device());
   vrm::argmax_rows(logits.data_ptr(), logits.stride(0), (int)logits.size(0), (int)logits.size(1),
                    out.data_ptr<int>(), cur_stream());
@@ -297,6 +329,7 @@ void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k
   TORCH_CHECK(top_p.scalar_type() == torch::kFloat32 && top_p.numel() >= B, "sample: fp32 top_p");
   TORCH_CHECK(steps.scalar_type() == torch::kInt32 && steps.numel() >= B, "sample: int32 steps");
   TORCH_CHECK(out.scalar_type() == torch::kInt32 && out.numel() >= B, "sample: int32 out");
+  same_device(logits, {&temperature, &top_k, &top_p, &steps, &out}, "sample");
   const c10::cuda::CUDAGuard guard(logits.device());
   vrm::sample_rows(logits.data_ptr(), logits.stride(0), (int)B, (int)logits.size(1), temperature.data_ptr<float>(),
                    top_k.data_ptr<int>(), top_p.data_ptr<float>(), (uint64_t)seed, steps.data_ptr<int>(),

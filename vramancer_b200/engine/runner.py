@@ -101,6 +101,8 @@ class ModelRunner:
     def _decode_body(self, B: int) -> None:
         batch = self._decode_batch(B)
         logits = self.model.forward(batch, self.pool)
+        if logits.device != self.device:          # pipeline: last stage on another GPU
+            logits = logits.to(self.device)
         ops.sample(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.seed, self.d_steps[:B],
                    out=self.d_out[:B])
 
@@ -245,6 +247,8 @@ class ModelRunner:
         logits = self.model.forward(batch, self.pool)
         if not rows:
             return [None] * B
+        if logits.device != dev:
+            logits = logits.to(dev)
         sel = [r for r, it in enumerate(items) if it.want_logits]
         tt = torch.tensor([temperature[r] for r in sel], dtype=torch.float32)
         tk = torch.tensor([top_k[r] for r in sel], dtype=torch.int32)
