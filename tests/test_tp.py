@@ -46,3 +46,5 @@ def test_tp2_matches_tp1_gpu_nccl():
     assert res["world"] == 2
     # bf16 kernels: different reduction order across ranks -> small differences
     assert res["max_logit_diff"] < 0.05 * max(1.0, res["scale"]), res
+    # fused GEMM + all-reduce matches GEMM followed by the NCCL all-reduce
+    assert res["fused_ar_rel_diff"] is not None and res["fused_ar_rel_diff"] < 2e-2, res

@@ -352,12 +352,33 @@ struct StreamK {
   }
 };
 
-template <int BN, int STAGES>
+// Fused all-reduce over the tensor-parallel group (row-parallel GEMMs): symmetric
+// fp32 tile buffers (two halves, alternating per call) and per-(source rank, tile)
+// epoch flags on every rank; peers' pointers come from CUDA IPC.
+struct ARParams {
+  float* const* xbuf;         // [world] base of each rank's tile buffer
+  uint32_t* const* flags;     // [world] each rank's flags [world][max_tiles]
+  uint32_t* epoch;            // this rank's call counter
+  uint32_t* done;             // this rank's CTA completion counter
+  int rank, world, max_tiles;
+  long long half_floats;      // floats per half of xbuf
+};
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int BN, int STAGES, bool kAR>
 __global__ void __launch_bounds__(kGemmThreads, 2)
     gemm_streamk_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                              EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters,
                              int k_tiles, int max_contrib, StreamK sk, uint32_t* __restrict__ err,
-                             unsigned long long* __restrict__ trace) {
+                             unsigned long long* __restrict__ trace, ARParams ar) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -369,7 +390,6 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  uint32_t* flag_slot = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
@@ -480,10 +500,16 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     mbar_wait(drain, 0, err);
   } else if (warp >= 2) {
     // ---------------- epilogue (16-column chunks: no full accumulator row in registers)
+    // Split tiles use a fixed owner: the CTA holding the tile's first k-iteration (the
+    // tile is its last segment).  Other contributors (for whom the tile is the first
+    // segment) publish fp32 partials; the owner waits for them, so every CTA's waits
+    // follow its own segment order, identically on every tensor-parallel rank.
     const int lane_base = 32 * (warp & 3);
     const int row = lane_base + lane;
     const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
     pdl_wait();
+    uint32_t epoch = 0;
+    if (kAR) epoch = *reinterpret_cast<volatile uint32_t*>(ar.epoch) + 1u;
     int seg = 0;
     for (int64_t it = it_begin; it < it_end; ++seg) {
       const int t = (int)(it / k_tiles);
@@ -494,12 +520,28 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       const bool ok = mbar_wait(&tfull[acc], (uint32_t)((seg >> 1) & 1), err);
       tc_fence_after();
       const int r_glob = t * kBM + row;   // weight row == output feature
-      int first_owner = 0, nc = 1;
-      float* slot = nullptr;
+      int first_owner = c, nc = 1;
       if (!whole) {
         first_owner = sk.owner((int64_t)t * k_tiles);
         nc = sk.owner((int64_t)t * k_tiles + k_tiles - 1) - first_owner + 1;
-        slot = workspace + ((size_t)t * max_contrib + (c - first_owner)) * (size_t)(kBM * BN);
+      }
+      const bool is_owner = whole || (c == first_owner);
+      const float* base = workspace + (size_t)t * max_contrib * (size_t)(kBM * BN) + row;
+      float* xmine = nullptr;
+      if (kAR && is_owner)
+        xmine = ar.xbuf[ar.rank] + (epoch & 1u) * ar.half_floats + (size_t)t * (kBM * BN);
+      if (is_owner && !whole) {
+        // wait for the other contributors' partials (published in their first segment)
+        if (threadIdx.x == 64) {
+          const unsigned long long t0 = clock64();
+          while (ld_acquire_gpu(tile_counters + t) < (uint32_t)(nc - 1)) {
+            if ((unsigned long long)(clock64() - t0) > VRM_SPIN_LIMIT_CYCLES) {
+              report_error(err, kErrFlagTimeout);
+              break;
+            }
+          }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
       }
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -509,53 +551,90 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         float v[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = ok ? __uint_as_float(r[j]) : 0.f;
-        if (whole) {
-          epi_store<true>(ep, r_glob, c0, v);
-        } else {
+        if (!is_owner) {
+          float* slot = workspace + ((size_t)t * max_contrib + (c - first_owner)) * (size_t)(kBM * BN);
 #pragma unroll
           for (int j = 0; j < 16; ++j) __stcg(slot + (size_t)(c0 + j) * kBM + row, v[j]);
+          continue;
+        }
+        if (!whole) {
+          // owner's own contribution is index 0; add the others in contributor order
+          for (int q = 1; q < nc; ++q) {
+            float x[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) x[j] = __ldcg(base + (size_t)q * (kBM * BN) + (size_t)(c0 + j) * kBM);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += x[j];
+          }
+        }
+        if (kAR) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(xmine + (size_t)(c0 + j) * kBM + row, v[j]);
+        } else {
+          epi_store<true>(ep, r_glob, c0, v);
         }
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
-      if (!whole) {
-        // CTA barrier + one release/acquire atomic publishes the whole partial
+      if (!is_owner) {
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (threadIdx.x == 64) {
           uint32_t prev;
-          asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(tile_counters + t) : "memory");
-          *flag_slot = (prev == (uint32_t)(nc - 1)) ? 1u : 0u;
+          asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(tile_counters + t) : "memory");
         }
+      } else if (!whole && threadIdx.x == 64) {
+        tile_counters[t] = 0u;   // all contributors counted: reset for the next launch
+      }
+      if (kAR && is_owner) {
+        // publish this rank's tile to every peer, wait for theirs, reduce in rank order
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (*flag_slot) {
-          const float* base = workspace + (size_t)t * max_contrib * (size_t)(kBM * BN) + row;
-#pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 16) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0.f;
-            int q = 0;
-            for (; q + 1 < nc; q += 2) {
-              float x0[16], x1[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                x0[j] = __ldcg(base + (size_t)q * (kBM * BN) + (size_t)(c0 + j) * kBM);
-                x1[j] = __ldcg(base + (size_t)(q + 1) * (kBM * BN) + (size_t)(c0 + j) * kBM);
+        if (threadIdx.x == 64) {
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          for (int p = 0; p < ar.world; ++p)
+            if (p != ar.rank) st_release_sys_u32(ar.flags[p] + (size_t)ar.rank * ar.max_tiles + t, epoch);
+          const unsigned long long t0 = clock64();
+          for (int p = 0; p < ar.world; ++p) {
+            if (p == ar.rank) continue;
+            const uint32_t* f = ar.flags[ar.rank] + (size_t)p * ar.max_tiles + t;
+            while ((int)(ld_acquire_sys_u32(f) - epoch) < 0) {
+              if ((unsigned long long)(clock64() - t0) > VRM_SPIN_LIMIT_CYCLES) {
+                report_error(err, kErrFlagTimeout);
+                break;
               }
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] += x0[j] + x1[j];
             }
-            if (q < nc) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] += __ldcg(base + (size_t)q * (kBM * BN) + (size_t)(c0 + j) * kBM);
-            }
-            epi_store<true>(ep, r_glob, c0, v);
           }
-          if (threadIdx.x == 64) tile_counters[t] = 0u;
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
+        const size_t off = (epoch & 1u) * ar.half_floats + (size_t)t * (kBM * BN) + row;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0.f;
+          for (int p = 0; p < ar.world; ++p) {
+            const float* src = ar.xbuf[p] + off;
+            float x[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) x[j] = __ldcv(src + (size_t)(c0 + j) * kBM);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += x[j];
+          }
+          epi_store<true>(ep, r_glob, c0, v);
+        }
       }
       it += n;
+    }
+    if (kAR) {
+      // last CTA of this launch advances the epoch for the next call
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        const uint32_t prev = atomicAdd(ar.done, 1u);
+        if (prev == gridDim.x - 1) {
+          *ar.done = 0u;
+          __threadfence();
+          *reinterpret_cast<volatile uint32_t*>(ar.epoch) = epoch;
+        }
+      }
     }
     if (tr && threadIdx.x == 64) tr[5] = globaltimer();
   }
@@ -648,12 +727,12 @@ static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const EpiP
 static unsigned long long* g_gemm_trace = nullptr;
 void gemm_set_trace(void* buf) { g_gemm_trace = static_cast<unsigned long long*>(buf); }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool kAR>
 static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const EpiParams& ep, int N, int K,
-                           int max_ctas, cudaStream_t stream) {
+                           int max_ctas, cudaStream_t stream, const ARParams& ar) {
   // smem: stages + 2*STAGES+4 barriers + slots
   constexpr int kSmem = STAGES * GemmSmem<BN, STAGES>::kStageBytes + (2 * STAGES + 5) * 8 + 16 + 1024;
-  auto kern = gemm_streamk_swap_kernel<BN, STAGES>;
+  auto kern = gemm_streamk_swap_kernel<BN, STAGES, kAR>;
   static int attr_dev_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -677,8 +756,10 @@ static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const E
   } else {
     ws = static_cast<float*>(workspace_get((size_t)tiles * max_contrib * kBM * BN * sizeof(float), stream));
   }
+  if (kAR) VRM_REQUIRE(tiles <= ar.max_tiles && (long long)tiles * kBM * BN <= ar.half_floats,
+                       "fused all-reduce: output larger than the symmetric buffer");
   launch_kernel(kern, dim3(sk.ctas), dim3(kGemmThreads), (size_t)kSmem, stream, mw, mx, ep, ws, counters, k_tiles,
-                max_contrib, sk, error_word(), g_gemm_trace);
+                max_contrib, sk, error_word(), g_gemm_trace, ar);
 }
 
 // Split count such that tiles * splits covers the SMs with >= min_k K-tiles per split.
@@ -731,15 +812,27 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     const int BN = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
     const CUtensorMap ma = make_kmajor_map(a.w, a.N, a.K, a.ldw, kBM);
     const CUtensorMap mb = make_kmajor_map(a.x, a.M, a.K, a.ldx, BN);
+    VRM_REQUIRE(!a.allreduce || (a.force_splits <= 0 && !legacy_decode()),
+                "fused all-reduce runs on the stream-K decode path only");
     if (a.force_splits <= 0 && !legacy_decode()) {
       const int ctas = device_sm_count();
       // <= 113 KB of smem per CTA: a CTA of the next GEMM fits beside it and (PDL)
       // prefetches its weights while this one drains
-      switch (BN) {
-        case 16: launch_streamk<16, 6>(ma, mb, ep, a.N, a.K, ctas, stream); break;
-        case 32: launch_streamk<32, 5>(ma, mb, ep, a.N, a.K, ctas, stream); break;
-        case 64: launch_streamk<64, 4>(ma, mb, ep, a.N, a.K, ctas, stream); break;
-        default: launch_streamk<128, 3>(ma, mb, ep, a.N, a.K, ctas, stream); break;
+      const ARParams ar = a.allreduce ? *reinterpret_cast<const ARParams*>(a.allreduce) : ARParams{};
+      if (a.allreduce) {
+        switch (BN) {
+          case 16: launch_streamk<16, 6, true>(ma, mb, ep, a.N, a.K, ctas, stream, ar); break;
+          case 32: launch_streamk<32, 5, true>(ma, mb, ep, a.N, a.K, ctas, stream, ar); break;
+          case 64: launch_streamk<64, 4, true>(ma, mb, ep, a.N, a.K, ctas, stream, ar); break;
+          default: launch_streamk<128, 3, true>(ma, mb, ep, a.N, a.K, ctas, stream, ar); break;
+        }
+      } else {
+        switch (BN) {
+          case 16: launch_streamk<16, 6, false>(ma, mb, ep, a.N, a.K, ctas, stream, ar); break;
+          case 32: launch_streamk<32, 5, false>(ma, mb, ep, a.N, a.K, ctas, stream, ar); break;
+          case 64: launch_streamk<64, 4, false>(ma, mb, ep, a.N, a.K, ctas, stream, ar); break;
+          default: launch_streamk<128, 3, false>(ma, mb, ep, a.N, a.K, ctas, stream, ar); break;
+        }
       }
       return;
     }
@@ -754,6 +847,7 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
       default: launch_gemm<128, 5, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
     }
   } else {
+    VRM_REQUIRE(!a.allreduce, "fused all-reduce needs M <= 128 (decode); use the collective for prefill");
     constexpr int BN = 128;
     const int a_tiles = (a.M + kBM - 1) / kBM;
     const int b_tiles = (a.N + BN - 1) / BN;

@@ -336,6 +336,52 @@ void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k
                    out.data_ptr<int>(), cur_stream());
 }
 
+// ---------------------------------------------------------------- fused GEMM + all-reduce
+// Mirrors the device-side ARParams of gemm_tc.cu (same field order and types).
+struct ARParamsHost {
+  float* const* xbuf;
+  uint32_t* const* flags;
+  uint32_t* epoch;
+  uint32_t* done;
+  int rank, world, max_tiles;
+  long long half_floats;
+};
+
+void gemm_ar_out(const Tensor& x, const Tensor& w, const OptT& bias, Tensor& out, const OptT& residual,
+                 const Tensor& xbuf_ptrs, const Tensor& flag_ptrs, Tensor& epoch, Tensor& done, int64_t rank,
+                 int64_t world, int64_t max_tiles, int64_t half_floats) {
+  check_bf16_2d(x, "gemm_ar x");
+  check_bf16_2d(w, "gemm_ar w");
+  check_bf16_2d(out, "gemm_ar out");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N, "gemm_ar: shapes");
+  TORCH_CHECK(M <= 128, "gemm_ar: fused all-reduce is for decode shapes (M <= 128)");
+  same_device(x, {&w, &out, &xbuf_ptrs, &flag_ptrs, &epoch, &done}, "gemm_ar");
+  same_device_opt(x, {&bias, &residual}, "gemm_ar");
+  TORCH_CHECK(xbuf_ptrs.scalar_type() == torch::kInt64 && flag_ptrs.scalar_type() == torch::kInt64 &&
+                  xbuf_ptrs.numel() == world && flag_ptrs.numel() == world,
+              "gemm_ar: pointer arrays must be int64 [world]");
+  ARParamsHost ar{reinterpret_cast<float* const*>(xbuf_ptrs.data_ptr()),
+                  reinterpret_cast<uint32_t* const*>(flag_ptrs.data_ptr()),
+                  reinterpret_cast<uint32_t*>(epoch.data_ptr()), reinterpret_cast<uint32_t*>(done.data_ptr()),
+                  (int)rank, (int)world, (int)max_tiles, (long long)half_floats};
+  vrm::GemmArgs a;
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.w = w.data_ptr();
+  a.ldw = w.stride(0);
+  a.bias = has(bias) ? bias->data_ptr() : nullptr;
+  a.residual = has(residual) ? residual->data_ptr() : nullptr;
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.allreduce = &ar;
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::gemm_bf16(a, cur_stream());
+}
+
 // ---------------------------------------------------------------- page migration
 void page_copy(const Tensor& src_pool, Tensor& dst_pool, const Tensor& src_idx, const Tensor& dst_idx) {
   TORCH_CHECK(src_pool.is_cuda() && dst_pool.is_cuda() && src_pool.is_contiguous() && dst_pool.is_contiguous(),
@@ -392,6 +438,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {
     vrm::gemm_set_trace(buf.has_value() && buf->defined() ? buf->data_ptr() : nullptr);
   });
+  m.def("gemm_ar_out", &gemm_ar_out, py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("out"),
+        py::arg("residual"), py::arg("xbuf_ptrs"), py::arg("flag_ptrs"), py::arg("epoch"), py::arg("done"),
+        py::arg("rank"), py::arg("world"), py::arg("max_tiles"), py::arg("half_floats"),
+        "row-parallel GEMM with the TP all-reduce fused into its epilogue (peer loads/stores)");
+  m.def("symm_malloc", [](int64_t bytes) { return (int64_t)reinterpret_cast<uintptr_t>(vrm::symm_malloc(bytes)); });
+  m.def("symm_free", [](int64_t p) { vrm::symm_free(reinterpret_cast<void*>(p)); });
+  m.def("ipc_handle", [](int64_t p) {
+    auto v = vrm::ipc_handle(reinterpret_cast<void*>(p));
+    return py::bytes(reinterpret_cast<const char*>(v.data()), v.size());
+  });
+  m.def("ipc_open", [](py::bytes b) {
+    std::string s = b;
+    std::vector<uint8_t> v(s.begin(), s.end());
+    return (int64_t)reinterpret_cast<uintptr_t>(vrm::ipc_open(v));
+  });
+  m.def("ipc_close", [](int64_t p) { vrm::ipc_close(reinterpret_cast<void*>(p)); });
   m.def("page_copy", &page_copy, py::arg("src_pool"), py::arg("dst_pool"), py::arg("src_idx"), py::arg("dst_idx"),
         "copy whole KV pages between pools (peer GPU allowed), runs on the source device");
   m.def("enable_peer_access", &vrm::enable_peer_access, py::arg("device"), py::arg("peer"));

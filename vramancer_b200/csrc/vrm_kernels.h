@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
+#include <vector>
 
 namespace vrm {
 
@@ -33,6 +34,9 @@ struct GemmArgs {
   int force_splits = 0;
   int epilogue = kEpiNone;
   const void* residual = nullptr;   // optional: Y += residual[M, N] (same ld as out)
+  // optional fused all-reduce over the TP group (decode shapes): pointer to an ARParams
+  // (gemm_tc.cu) holding device arrays of the ranks' symmetric buffers and flags
+  const void* allreduce = nullptr;
 };
 void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
 // Debug: per-CTA timeline of the stream-K decode GEMM into buf ([ctas][8] u64 ns), null = off.
@@ -115,6 +119,13 @@ void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t stream);
 void argmax_rows(const void* logits, int64_t ld, int B, int V, int* out, cudaStream_t stream);
 void sample_rows(const void* logits, int64_t ld, int B, int V, const float* temperature, const int* top_k,
                  const float* top_p, uint64_t seed, const int* steps, int* out, cudaStream_t stream);
+
+// ---------------------------------------------------------------- symmetric buffers (symm.cu)
+void* symm_malloc(size_t bytes);
+void symm_free(void* p);
+std::vector<uint8_t> ipc_handle(void* p);
+void* ipc_open(const std::vector<uint8_t>& bytes);
+void ipc_close(void* p);
 
 // ---------------------------------------------------------------- KV page migration (migrate.cu)
 // dst_pool[dst_idx[i]] <- src_pool[src_idx[i]] for whole pages of page_bytes; runs on the

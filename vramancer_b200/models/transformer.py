@@ -56,10 +56,12 @@ class TPContext:
     """What a tensor-parallel rank needs from the communication layer."""
 
     def __init__(self, rank: int, size: int, all_reduce: Callable[[torch.Tensor], torch.Tensor],
-                 all_gather_last: Callable[[torch.Tensor], torch.Tensor]):
+                 all_gather_last: Callable[[torch.Tensor], torch.Tensor], fused_ar=None):
         self.rank, self.size = rank, size
         self.all_reduce = all_reduce
         self.all_gather_last = all_gather_last
+        # optional FusedAllReduce: row-parallel GEMM with the all-reduce in its epilogue
+        self.fused_ar = fused_ar
 
 
 class DecoderModel:
@@ -128,6 +130,10 @@ class DecoderModel:
         """r += x @ w.T (+ b) across the TP group; returns norm(r) if next_norm is given."""
         if self.tp_size == 1:
             ops.linear(x, w, b, residual=r, out=r)
+            return self._norm(r, i, next_norm) if next_norm else None
+        far = self.tp.fused_ar
+        if far is not None and x.is_cuda and far.supports(x.shape[0], w.shape[0]):
+            far.linear(x, w, b, residual=r, out=r)      # one kernel: GEMM + all-reduce + bias + residual
             return self._norm(r, i, next_norm) if next_norm else None
         y = ops.linear(x, w)
         y = self.tp.all_reduce(y)

@@ -74,7 +74,12 @@ def tp_context(group=None) -> Optional[TPContext]:
         dist.all_gather(parts, x.contiguous(), group=group)
         return torch.cat(parts, dim=-1)
 
-    return TPContext(rank, size, all_reduce, all_gather_last)
+    fused = None
+    if torch.cuda.is_available() and dist.get_backend(group) == "nccl" and \
+            os.environ.get("VRM_FUSED_AR", "1") not in ("0", "false"):
+        from .symm import FusedAllReduce
+        fused = FusedAllReduce(group, max_tokens=int(os.environ.get("VRM_FUSED_AR_MAX_TOKENS", "128")))
+    return TPContext(rank, size, all_reduce, all_gather_last, fused_ar=fused)
 
 
 def barrier() -> None:

@@ -53,9 +53,26 @@ def run(model: str, n_new: int = 8, device: str = "auto", std: float = 0.05) -> 
         items.append(llm.runner.prefill_logits([it])[-1].float().cpu())
         llm.kv.free(rid)
     diff = float((items[0] - items[1]).abs().max())
+    fused_diff = None
+    if tp is not None and tp.fused_ar is not None:
+        # fused GEMM + all-reduce vs GEMM then NCCL all-reduce, several shapes
+        from .. import ops
+        gg = torch.Generator(device=dev).manual_seed(3 + tp.rank)
+        fused_diff = 0.0
+        for m, n, k in ((1, 512, 256), (7, 1024, 512), (32, 640, 1280), (100, 256, 384)):
+            x = torch.randn(m, k, device=dev, generator=gg).to(dtype)
+            w = (torch.randn(n, k, device=dev, generator=gg) * 0.05).to(dtype)
+            r = torch.randn(m, n, device=dev, generator=gg).to(dtype)
+            ref_y = ops.linear(x, w).float()
+            torch.distributed.all_reduce(ref_y)
+            ref_y = ref_y + r.float()
+            for _ in range(3):     # repeated calls exercise the alternating buffers / epochs
+                y = tp.fused_ar.linear(x, w, residual=r)
+            fused_diff = max(fused_diff, float((y.float() - ref_y).abs().max() / (ref_y.abs().max() + 1e-6)))
+        torch.cuda.synchronize()
     same = [a.output_ids == b.output_ids for a, b in zip(r_ref, r_tp)]
     res = {"world": info.world_size, "max_logit_diff": diff, "scale": float(items[0].abs().max()),
-           "tokens_equal": same, "device": dev}
+           "tokens_equal": same, "device": dev, "fused_ar_rel_diff": fused_diff}
     comm.barrier()
     ref.runner.release_graphs()
     sharded.runner.release_graphs()
