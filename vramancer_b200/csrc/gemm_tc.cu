@@ -352,16 +352,20 @@ struct StreamK {
   }
 };
 
-// Fused all-reduce over the tensor-parallel group (row-parallel GEMMs): symmetric
-// fp32 tile buffers (two halves, alternating per call) and per-(source rank, tile)
-// epoch flags on every rank; peers' pointers come from CUDA IPC.
+// Fused all-reduce over the tensor-parallel group (row-parallel GEMMs).  Every rank
+// owns a receive buffer [2 halves][world source ranks][half_floats] (fp32 tiles) and
+// flags [world source ranks][max_tiles]; peers' pointers come from CUDA IPC.  A tile
+// owner pushes its fp32 tile into every rank's slot for it (posted NVLink stores),
+// release-stores the call's epoch into every peer's flag, waits for all peers' flags
+// for that tile, and reduces the slots from local memory in rank order, so every rank
+// gets bitwise the same sum.  Halves alternate per call (the epoch's parity).
 struct ARParams {
-  float* const* xbuf;         // [world] base of each rank's tile buffer
+  float* const* xbuf;         // [world] base of each rank's receive buffer
   uint32_t* const* flags;     // [world] each rank's flags [world][max_tiles]
   uint32_t* epoch;            // this rank's call counter
   uint32_t* done;             // this rank's CTA completion counter
   int rank, world, max_tiles;
-  long long half_floats;      // floats per half of xbuf
+  long long half_floats;      // floats per (half, source rank) slot
 };
 
 __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
@@ -527,9 +531,10 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       }
       const bool is_owner = whole || (c == first_owner);
       const float* base = workspace + (size_t)t * max_contrib * (size_t)(kBM * BN) + row;
-      float* xmine = nullptr;
-      if (kAR && is_owner)
-        xmine = ar.xbuf[ar.rank] + (epoch & 1u) * ar.half_floats + (size_t)t * (kBM * BN);
+      // offset of this rank's slot for tile t in the current half
+      const size_t xoff = kAR ? (((size_t)(epoch & 1u) * ar.world + ar.rank) * ar.half_floats +
+                                 (size_t)t * (kBM * BN) + row)
+                              : 0;
       if (is_owner && !whole) {
         // wait for the other contributors' partials (published in their first segment)
         if (threadIdx.x == 64) {
@@ -568,8 +573,12 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           }
         }
         if (kAR) {
+          // push the tile into every rank's slot for this source rank (own slot is local)
+          for (int p = 0; p < ar.world; ++p) {
+            float* dst = ar.xbuf[p] + xoff;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) __stcg(xmine + (size_t)(c0 + j) * kBM + row, v[j]);
+            for (int j = 0; j < 16; ++j) __stcg(dst + (size_t)(c0 + j) * kBM + row, v[j]);
+          }
         } else {
           epi_store<true>(ep, r_glob, c0, v);
         }
@@ -586,7 +595,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         tile_counters[t] = 0u;   // all contributors counted: reset for the next launch
       }
       if (kAR && is_owner) {
-        // publish this rank's tile to every peer, wait for theirs, reduce in rank order
+        // flag the tile to every peer, wait for theirs, reduce the slots in rank order
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (threadIdx.x == 64) {
           asm volatile("fence.acq_rel.sys;" ::: "memory");
@@ -605,17 +614,18 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           }
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        const size_t off = (epoch & 1u) * ar.half_floats + (size_t)t * (kBM * BN) + row;
+        const float* mine = ar.xbuf[ar.rank] + (size_t)(epoch & 1u) * ar.world * ar.half_floats +
+                            (size_t)t * (kBM * BN) + row;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
           float v[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
           for (int p = 0; p < ar.world; ++p) {
-            const float* src = ar.xbuf[p] + off;
+            const float* src = mine + (size_t)p * ar.half_floats;
             float x[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) x[j] = __ldcv(src + (size_t)(c0 + j) * kBM);
+            for (int j = 0; j < 16; ++j) x[j] = __ldcg(src + (size_t)(c0 + j) * kBM);
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] += x[j];
           }

@@ -1,6 +1,7 @@
 """Symmetric buffers for the fused GEMM + all-reduce of tensor-parallel decode.
 
-Every rank allocates (cudaMalloc) a tile buffer of two halves and a flag array,
+Every rank allocates (cudaMalloc) a receive buffer (two halves x one slot per source
+rank) and a flag array,
 exports CUDA IPC handles, gathers its peers' handles over the process group and opens
 them; the device then holds [world]-long arrays of the ranks' buffer and flag
 pointers, which the row-parallel GEMM epilogue uses to publish its tiles, wait for
@@ -28,7 +29,8 @@ class FusedAllReduce:
         self.half_floats = self.max_tiles * 128 * max_tokens
         nat = ops.native()
         with torch.cuda.device(self.device):
-            self.xbuf = nat.symm_malloc(2 * self.half_floats * 4)
+            # receive buffer: [2 halves][world source ranks][half_floats] fp32
+            self.xbuf = nat.symm_malloc(2 * self.world * self.half_floats * 4)
             self.flags = nat.symm_malloc(self.world * self.max_tiles * 4)
             handles = [nat.ipc_handle(self.xbuf), nat.ipc_handle(self.flags)]
             allh = [None] * self.world
