@@ -352,30 +352,11 @@ struct StreamK {
   }
 };
 
-// Fused all-reduce over the tensor-parallel group (row-parallel GEMMs).  Every rank
-// owns a receive buffer [2 halves][world source ranks][half_floats] (fp32 tiles) and
-// flags [world source ranks][max_tiles]; peers' pointers come from CUDA IPC.  A tile
-// owner pushes its fp32 tile into every rank's slot for it (posted NVLink stores),
-// release-stores the call's epoch into every peer's flag, waits for all peers' flags
-// for that tile, and reduces the slots from local memory in rank order, so every rank
-// gets bitwise the same sum.  Halves alternate per call (the epoch's parity).
-struct ARParams {
-  float* const* xbuf;         // [world] base of each rank's receive buffer
-  uint32_t* const* flags;     // [world] each rank's flags [world][max_tiles]
-  uint32_t* epoch;            // this rank's call counter
-  uint32_t* done;             // this rank's CTA completion counter
-  int rank, world, max_tiles;
-  long long half_floats;      // floats per (half, source rank) slot
-};
-
-__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+// Fused all-reduce, push half (ARPush in vrm_kernels.h): the owner of each finished
+// output tile stores the fp32 partial (pre-bias) into this rank's slot on every rank
+// (posted NVLink stores; its own slot is local) and never waits; the last CTA of the
+// launch advances the epoch and flags every peer.  ar_norm.cu reduces.
+using ARParams = ARPush;
 
 template <int BN, int STAGES, bool kAR>
 __global__ void __launch_bounds__(kGemmThreads, 2)
@@ -531,10 +512,8 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       }
       const bool is_owner = whole || (c == first_owner);
       const float* base = workspace + (size_t)t * max_contrib * (size_t)(kBM * BN) + row;
-      // offset of this rank's slot for tile t in the current half
-      const size_t xoff = kAR ? (((size_t)(epoch & 1u) * ar.world + ar.rank) * ar.half_floats +
-                                 (size_t)t * (kBM * BN) + row)
-                              : 0;
+      // this rank's slot in the current half; element (token m, feature n) at m * N + n
+      const size_t xoff = kAR ? (((size_t)(epoch & 1u) * ar.world + ar.rank) * ar.half_floats + (size_t)r_glob) : 0;
       if (is_owner && !whole) {
         // wait for the other contributors' partials (published in their first segment)
         if (threadIdx.x == 64) {
@@ -573,11 +552,14 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           }
         }
         if (kAR) {
-          // push the tile into every rank's slot for this source rank (own slot is local)
-          for (int p = 0; p < ar.world; ++p) {
-            float* dst = ar.xbuf[p] + xoff;
+          // push the partial into this rank's slot on every rank (own slot is local)
+          if (r_glob < ep.N) {
+            for (int p = 0; p < ar.world; ++p) {
+              float* dst = ar.xbuf[p] + xoff;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) __stcg(dst + (size_t)(c0 + j) * kBM + row, v[j]);
+              for (int j = 0; j < 16; ++j)
+                if (c0 + j < ep.M) __stcg(dst + (size_t)(c0 + j) * ep.N, v[j]);
+            }
           }
         } else {
           epi_store<true>(ep, r_glob, c0, v);
@@ -594,55 +576,22 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       } else if (!whole && threadIdx.x == 64) {
         tile_counters[t] = 0u;   // all contributors counted: reset for the next launch
       }
-      if (kAR && is_owner) {
-        // flag the tile to every peer, wait for theirs, reduce the slots in rank order
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (threadIdx.x == 64) {
-          asm volatile("fence.acq_rel.sys;" ::: "memory");
-          for (int p = 0; p < ar.world; ++p)
-            if (p != ar.rank) st_release_sys_u32(ar.flags[p] + (size_t)ar.rank * ar.max_tiles + t, epoch);
-          const unsigned long long t0 = clock64();
-          for (int p = 0; p < ar.world; ++p) {
-            if (p == ar.rank) continue;
-            const uint32_t* f = ar.flags[ar.rank] + (size_t)p * ar.max_tiles + t;
-            while ((int)(ld_acquire_sys_u32(f) - epoch) < 0) {
-              if ((unsigned long long)(clock64() - t0) > VRM_SPIN_LIMIT_CYCLES) {
-                report_error(err, kErrFlagTimeout);
-                break;
-              }
-            }
-          }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        const float* mine = ar.xbuf[ar.rank] + (size_t)(epoch & 1u) * ar.world * ar.half_floats +
-                            (size_t)t * (kBM * BN) + row;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          float v[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0.f;
-          for (int p = 0; p < ar.world; ++p) {
-            const float* src = mine + (size_t)p * ar.half_floats;
-            float x[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) x[j] = __ldcg(src + (size_t)(c0 + j) * kBM);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] += x[j];
-          }
-          epi_store<true>(ep, r_glob, c0, v);
-        }
-      }
       it += n;
     }
     if (kAR) {
-      // last CTA of this launch advances the epoch for the next call
+      // every thread's remote pushes are visible system-wide before the CTA counts as
+      // done; the last CTA then advances the epoch and flags every peer
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (threadIdx.x == 64) {
-        const uint32_t prev = atomicAdd(ar.done, 1u);
+        uint32_t prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ar.done) : "memory");
         if (prev == gridDim.x - 1) {
           *ar.done = 0u;
-          __threadfence();
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
           *reinterpret_cast<volatile uint32_t*>(ar.epoch) = epoch;
+          for (int p = 0; p < ar.world; ++p)
+            if (p != ar.rank) st_release_sys(ar.flags[p] + ar.rank, epoch);
         }
       }
     }
@@ -766,8 +715,7 @@ static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const E
   } else {
     ws = static_cast<float*>(workspace_get((size_t)tiles * max_contrib * kBM * BN * sizeof(float), stream));
   }
-  if (kAR) VRM_REQUIRE(tiles <= ar.max_tiles && (long long)tiles * kBM * BN <= ar.half_floats,
-                       "fused all-reduce: output larger than the symmetric buffer");
+  if (kAR) VRM_REQUIRE((long long)ep.M * N <= ar.half_floats, "fused all-reduce: output larger than the symmetric buffer");
   launch_kernel(kern, dim3(sk.ctas), dim3(kGemmThreads), (size_t)kSmem, stream, mw, mx, ep, ws, counters, k_tiles,
                 max_contrib, sk, error_word(), g_gemm_trace, ar);
 }
@@ -806,6 +754,8 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   VRM_REQUIRE((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0,
               "gemm: operands must be 16-byte aligned");
   VRM_REQUIRE(a.epilogue != kEpiSiluMul || (a.N % 2 == 0 && a.residual == nullptr), "gemm: silu_mul epilogue");
+  VRM_REQUIRE(!a.allreduce || (a.epilogue == kEpiNone && !a.bias && !a.residual),
+              "gemm: the all-reduce push stores the raw partial (bias / residual go to ar_norm)");
   if (a.M <= 0 || a.N <= 0) return;
   EpiParams ep;
   ep.out = reinterpret_cast<__nv_bfloat16*>(a.out);
@@ -828,7 +778,7 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
       const int ctas = device_sm_count();
       // <= 113 KB of smem per CTA: a CTA of the next GEMM fits beside it and (PDL)
       // prefetches its weights while this one drains
-      const ARParams ar = a.allreduce ? *reinterpret_cast<const ARParams*>(a.allreduce) : ARParams{};
+      const ARParams ar = a.allreduce ? *a.allreduce : ARParams{};
       if (a.allreduce) {
         switch (BN) {
           case 16: launch_streamk<16, 6, true>(ma, mb, ep, a.N, a.K, ctas, stream, ar); break;

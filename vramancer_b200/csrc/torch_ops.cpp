@@ -337,49 +337,75 @@ void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k
 }
 
 // ---------------------------------------------------------------- fused GEMM + all-reduce
-// Mirrors the device-side ARParams of gemm_tc.cu (same field order and types).
-struct ARParamsHost {
-  float* const* xbuf;
-  uint32_t* const* flags;
-  uint32_t* epoch;
-  uint32_t* done;
-  int rank, world, max_tiles;
-  long long half_floats;
-};
-
-void gemm_ar_out(const Tensor& x, const Tensor& w, const OptT& bias, Tensor& out, const OptT& residual,
-                 const Tensor& xbuf_ptrs, const Tensor& flag_ptrs, Tensor& epoch, Tensor& done, int64_t rank,
-                 int64_t world, int64_t max_tiles, int64_t half_floats) {
+// Push half: row-parallel GEMM whose epilogue stores the fp32 partial into every rank's
+// receive buffer and flags the peers (ARPush).  Nothing is written to a tensor here.
+void gemm_ar_push(const Tensor& x, const Tensor& w, const Tensor& xbuf_ptrs, const Tensor& flag_ptrs, Tensor& epoch,
+                  Tensor& done, int64_t rank, int64_t world, int64_t half_floats) {
   check_bf16_2d(x, "gemm_ar x");
   check_bf16_2d(w, "gemm_ar w");
-  check_bf16_2d(out, "gemm_ar out");
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
-  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N, "gemm_ar: shapes");
+  TORCH_CHECK(w.size(1) == K, "gemm_ar: shapes");
   TORCH_CHECK(M <= 128, "gemm_ar: fused all-reduce is for decode shapes (M <= 128)");
-  same_device(x, {&w, &out, &xbuf_ptrs, &flag_ptrs, &epoch, &done}, "gemm_ar");
-  same_device_opt(x, {&bias, &residual}, "gemm_ar");
+  TORCH_CHECK(M * N <= half_floats, "gemm_ar: output larger than the receive buffer");
+  same_device(x, {&w, &xbuf_ptrs, &flag_ptrs, &epoch, &done}, "gemm_ar");
   TORCH_CHECK(xbuf_ptrs.scalar_type() == torch::kInt64 && flag_ptrs.scalar_type() == torch::kInt64 &&
                   xbuf_ptrs.numel() == world && flag_ptrs.numel() == world,
               "gemm_ar: pointer arrays must be int64 [world]");
-  ARParamsHost ar{reinterpret_cast<float* const*>(xbuf_ptrs.data_ptr()),
-                  reinterpret_cast<uint32_t* const*>(flag_ptrs.data_ptr()),
-                  reinterpret_cast<uint32_t*>(epoch.data_ptr()), reinterpret_cast<uint32_t*>(done.data_ptr()),
-                  (int)rank, (int)world, (int)max_tiles, (long long)half_floats};
+  vrm::ARPush ar;
+  ar.xbuf = reinterpret_cast<float* const*>(xbuf_ptrs.data_ptr());
+  ar.flags = reinterpret_cast<uint32_t* const*>(flag_ptrs.data_ptr());
+  ar.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
+  ar.done = reinterpret_cast<uint32_t*>(done.data_ptr());
+  ar.rank = (int)rank;
+  ar.world = (int)world;
+  ar.half_floats = half_floats;
   vrm::GemmArgs a;
   a.x = x.data_ptr();
   a.ldx = x.stride(0);
   a.w = w.data_ptr();
   a.ldw = w.stride(0);
-  a.bias = has(bias) ? bias->data_ptr() : nullptr;
-  a.residual = has(residual) ? residual->data_ptr() : nullptr;
-  a.out = out.data_ptr();
-  a.ldo = out.stride(0);
   a.M = (int)M;
   a.N = (int)N;
   a.K = (int)K;
   a.allreduce = &ar;
   const c10::cuda::CUDAGuard guard(x.device());
   vrm::gemm_bf16(a, cur_stream());
+}
+
+// Reduce half fused with bias + residual + norm (ARNormArgs).  xbuf / flags / epoch
+// are this rank's own device buffers.
+void ar_norm(int64_t xbuf, int64_t flags, const Tensor& epoch, int64_t rank, int64_t world, int64_t half_floats,
+             int64_t T, int64_t H, const OptT& bias, const OptT& residual, const OptT& w, const OptT& b,
+             const OptT& out, int64_t mode, double eps) {
+  TORCH_CHECK(epoch.is_cuda(), "ar_norm: epoch must be a CUDA tensor");
+  same_device_opt(epoch, {&bias, &residual, &w, &b, &out}, "ar_norm");
+  for (const OptT* t : {&bias, &residual, &w, &b, &out})
+    if (has(*t)) TORCH_CHECK((*t)->scalar_type() == torch::kBFloat16, "ar_norm: bf16 tensors");
+  if (has(residual)) TORCH_CHECK(residual->is_contiguous() && residual->numel() == T * H, "ar_norm: residual [T, H]");
+  if (has(out)) TORCH_CHECK(out->dim() == 2 && out->size(0) == T && out->size(1) == H && out->stride(1) == 1,
+                            "ar_norm: out [T, H]");
+  if (has(bias)) TORCH_CHECK(bias->numel() == H && bias->is_contiguous(), "ar_norm: bias [H]");
+  if (has(w)) TORCH_CHECK(w->numel() == H && w->is_contiguous(), "ar_norm: weight [H]");
+  if (has(b)) TORCH_CHECK(b->numel() == H && b->is_contiguous(), "ar_norm: norm bias [H]");
+  vrm::ARNormArgs a;
+  a.xbuf = reinterpret_cast<const float*>(xbuf);
+  a.flags = reinterpret_cast<const uint32_t*>(flags);
+  a.epoch = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.half_floats = half_floats;
+  a.T = (int)T;
+  a.H = (int)H;
+  a.bias = has(bias) ? bias->data_ptr() : nullptr;
+  a.residual = has(residual) ? residual->data_ptr() : nullptr;
+  a.w = has(w) ? w->data_ptr() : nullptr;
+  a.b = has(b) ? b->data_ptr() : nullptr;
+  a.out = has(out) ? out->data_ptr() : nullptr;
+  a.ldo = has(out) ? out->stride(0) : H;
+  a.mode = (int)mode;
+  a.eps = (float)eps;
+  const c10::cuda::CUDAGuard guard(epoch.device());
+  vrm::ar_norm(a, cur_stream());
 }
 
 // ---------------------------------------------------------------- page migration
@@ -438,10 +464,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {
     vrm::gemm_set_trace(buf.has_value() && buf->defined() ? buf->data_ptr() : nullptr);
   });
-  m.def("gemm_ar_out", &gemm_ar_out, py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("out"),
-        py::arg("residual"), py::arg("xbuf_ptrs"), py::arg("flag_ptrs"), py::arg("epoch"), py::arg("done"),
-        py::arg("rank"), py::arg("world"), py::arg("max_tiles"), py::arg("half_floats"),
-        "row-parallel GEMM with the TP all-reduce fused into its epilogue (peer loads/stores)");
+  m.def("gemm_ar_push", &gemm_ar_push, py::arg("x"), py::arg("w"), py::arg("xbuf_ptrs"), py::arg("flag_ptrs"),
+        py::arg("epoch"), py::arg("done"), py::arg("rank"), py::arg("world"), py::arg("half_floats"),
+        "row-parallel GEMM pushing its fp32 partial into every rank's receive buffer (fused all-reduce, push)");
+  m.def("ar_norm", &ar_norm, py::arg("xbuf"), py::arg("flags"), py::arg("epoch"), py::arg("rank"), py::arg("world"),
+        py::arg("half_floats"), py::arg("T"), py::arg("H"), py::arg("bias"), py::arg("residual"), py::arg("w"),
+        py::arg("b"), py::arg("out"), py::arg("mode"), py::arg("eps"),
+        "fused all-reduce, reduce half: wait for peers, sum slots, + bias + residual, optional norm");
   m.def("symm_malloc", [](int64_t bytes) { return (int64_t)reinterpret_cast<uintptr_t>(vrm::symm_malloc(bytes)); });
   m.def("symm_free", [](int64_t p) { vrm::symm_free(reinterpret_cast<void*>(p)); });
   m.def("ipc_handle", [](int64_t p) {

@@ -34,9 +34,24 @@ struct GemmArgs {
   int force_splits = 0;
   int epilogue = kEpiNone;
   const void* residual = nullptr;   // optional: Y += residual[M, N] (same ld as out)
-  // optional fused all-reduce over the TP group (decode shapes): pointer to an ARParams
-  // (gemm_tc.cu) holding device arrays of the ranks' symmetric buffers and flags
-  const void* allreduce = nullptr;
+  // optional fused all-reduce over the TP group (decode shapes): instead of storing Y,
+  // push the fp32 partial into every rank's receive buffer (see ARPush)
+  const struct ARPush* allreduce = nullptr;
+};
+
+// Push half of the fused tensor-parallel all-reduce.  Every rank owns a receive
+// buffer [2 halves][world source ranks][half_floats] fp32 and flags [world source
+// ranks] (cudaMalloc + CUDA IPC, symm.cu).  The row-parallel GEMM stores its fp32
+// partial Y[m, n] at m * N + n of its own slot on every rank, then its last CTA
+// advances *epoch and release-stores it into each peer's flag for this rank.  Halves
+// alternate with the epoch's parity.  ar_norm (ar_norm.cu) is the reduce half.
+struct ARPush {
+  float* const* xbuf = nullptr;      // device array [world] of the ranks' receive buffers
+  uint32_t* const* flags = nullptr;  // device array [world] of the ranks' flag arrays
+  uint32_t* epoch = nullptr;         // this rank's call counter (device)
+  uint32_t* done = nullptr;          // this rank's CTA completion counter (device, zero)
+  int rank = 0, world = 1;
+  long long half_floats = 0;         // floats per (half, source rank) slot
 };
 void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
 // Debug: per-CTA timeline of the stream-K decode GEMM into buf ([ctas][8] u64 ns), null = off.
@@ -48,6 +63,33 @@ void rmsnorm(const void* x, int64_t ldx, void* residual, const void* w, void* ou
              float eps, cudaStream_t stream);
 void layernorm(const void* x, int64_t ldx, void* residual, const void* w, const void* b, void* out, int64_t ldo,
                int T, int H, float eps, cudaStream_t stream);
+
+// Reduce half of the fused all-reduce, fused with the residual update and the next
+// norm.  Waits (bounded) until every peer's flag for this rank reaches *epoch, then per
+// row: s = sum over source ranks in rank order of the slots (+ bias) (+ residual),
+// rounded to bf16 and stored back into residual; then
+//   mode kArAdd:       out = s (if out != residual)
+//   mode kArRmsNorm:   out = rmsnorm(s) * w
+//   mode kArLayerNorm: out = layernorm(s) * w + b
+// Every rank sums the same values in the same order: identical results on all ranks.
+enum ArNormMode { kArAdd = 0, kArRmsNorm = 1, kArLayerNorm = 2 };
+struct ARNormArgs {
+  const float* xbuf = nullptr;       // this rank's receive buffer
+  const uint32_t* flags = nullptr;   // this rank's flags [world]
+  const uint32_t* epoch = nullptr;   // this rank's call counter (advanced by the GEMM)
+  int rank = 0, world = 1;
+  long long half_floats = 0;
+  int T = 0, H = 0;
+  const void* bias = nullptr;        // bf16 [H] or null
+  void* residual = nullptr;          // bf16 [T, H] in/out or null
+  const void* w = nullptr;           // norm weight [H]
+  const void* b = nullptr;           // layernorm bias [H]
+  void* out = nullptr;               // bf16 [T, ldo]
+  int64_t ldo = 0;
+  int mode = kArAdd;
+  float eps = 1e-6f;
+};
+void ar_norm(const ARNormArgs& a, cudaStream_t stream);
 
 struct RopeKvArgs {
   void* qkv = nullptr;          // bf16 [T, (Hq + 2 KH) * D], rotated in place

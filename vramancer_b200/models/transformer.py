@@ -126,36 +126,53 @@ class DecoderModel:
                                            batch.max_q_len)
 
     def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], r: torch.Tensor,
-                      i: int, next_norm: Optional[str]) -> Optional[torch.Tensor]:
-        """r += x @ w.T (+ b) across the TP group; returns norm(r) if next_norm is given."""
+                      nxt: Optional[tuple]) -> Optional[torch.Tensor]:
+        """r += x @ w.T (+ b) across the TP group; returns norm(r) when `nxt` names the
+        norm that follows ((layer, "post_norm" | "in_norm") or (None, "final"))."""
         if self.tp_size == 1:
             ops.linear(x, w, b, residual=r, out=r)
-            return self._norm(r, i, next_norm) if next_norm else None
+            return self._norm(r, nxt[0] if nxt[0] is not None else "final", nxt[1]) if nxt else None
         far = self.tp.fused_ar
         if far is not None and x.is_cuda and far.supports(x.shape[0], w.shape[0]):
-            far.linear(x, w, b, residual=r, out=r)      # one kernel: GEMM + all-reduce + bias + residual
-            return self._norm(r, i, next_norm) if next_norm else None
+            # push the partial to every rank, then one kernel: reduce + bias + residual + norm
+            T, H = x.shape[0], w.shape[0]
+            far.push(x, w)
+            if not nxt:
+                far.reduce(T, H, bias=b, residual=r)
+                return None
+            nw, nb = self._norm_params(*nxt)
+            out = torch.empty_like(r)
+            far.reduce(T, H, bias=b, residual=r, out=out, norm_w=nw, norm_b=nb, eps=self.cfg.norm_eps,
+                       layernorm=self.cfg.is_gpt2)
+            return out
         y = ops.linear(x, w)
         y = self.tp.all_reduce(y)
         if b is not None:
             ops.add_(y, b.expand_as(y).contiguous())
-        if next_norm:
-            return self._norm(y, i, next_norm, residual=r)
+        if nxt:
+            return self._norm(y, nxt[0] if nxt[0] is not None else "final", nxt[1], residual=r)
         ops.add_(r, y)
         return None
 
-    def _mlp(self, i: int, x: torch.Tensor, r: torch.Tensor) -> None:
+    def _norm_params(self, i: Optional[int], which: str):
+        if i is None:
+            return self.w["final_norm_w"], self.w.get("final_norm_b")
+        return self.lw(i, f"{which}_w"), self.lw(i, f"{which}_b")
+
+    def _mlp(self, i: int, x: torch.Tensor, r: torch.Tensor, nxt: Optional[tuple]) -> Optional[torch.Tensor]:
+        """MLP of layer i into r; returns the next norm's output when `nxt` is given and
+        it could be fused into the MLP's output projection."""
         cfg = self.cfg
         if cfg.is_gpt2:
             h = ops.linear(x, self.lw(i, "fc_w"), self.lw(i, "fc_b"))
             ops.gelu_tanh_(h)
-            self._row_parallel(h, self.lw(i, "proj_w"), self.lw(i, "proj_b"), r, i, None)
-        elif cfg.is_moe:
+            return self._row_parallel(h, self.lw(i, "proj_w"), self.lw(i, "proj_b"), r, nxt)
+        if cfg.is_moe:
             y = self._moe(i, x)
             ops.add_(r, y)
-        else:
-            a = ops.linear(x, self.lw(i, "gate_up_w"), epilogue=ops.EPI_SILU_MUL)
-            self._row_parallel(a, self.lw(i, "down_w"), None, r, i, None)
+            return None
+        a = ops.linear(x, self.lw(i, "gate_up_w"), epilogue=ops.EPI_SILU_MUL)
+        return self._row_parallel(a, self.lw(i, "down_w"), None, r, nxt)
 
     def _moe(self, i: int, x: torch.Tensor) -> torch.Tensor:
         """Top-k softmax routing over SwiGLU experts (expert-parallel version in
@@ -165,11 +182,17 @@ class DecoderModel:
                            self.lw(i, "experts_down_w"), shared_gate_up=self.lw(i, "shared_gate_up_w"),
                            shared_down=self.lw(i, "shared_down_w"), shared_gate=self.lw(i, "shared_gate_w"))
 
-    def layer(self, i: int, r: torch.Tensor, batch: ForwardBatch, pool: KVPool) -> None:
-        x = self._norm(r, i, "in_norm")
+    def layer(self, i: int, r: torch.Tensor, batch: ForwardBatch, pool: KVPool,
+              x: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+        """Runs layer i on the residual stream r.  `x` is in_norm(r) when the previous
+        layer already produced it; returns the next layer's in_norm(r) when it could be
+        fused into this layer's last projection, else None."""
+        if x is None:
+            x = self._norm(r, i, "in_norm")
         attn = self._attention(i, x, batch, pool)
-        x = self._row_parallel(attn, self.lw(i, "o_w"), self.lw(i, "o_b"), r, i, "post_norm")
-        self._mlp(i, x, r)
+        x = self._row_parallel(attn, self.lw(i, "o_w"), self.lw(i, "o_b"), r, (i, "post_norm"))
+        nxt = (i + 1, "in_norm") if i + 1 < self.last_layer else None
+        return self._mlp(i, x, r, nxt)
 
     def logits(self, r: torch.Tensor, rows: Optional[torch.Tensor] = None) -> torch.Tensor:
         h = r if rows is None else r.index_select(0, rows)
@@ -188,8 +211,9 @@ class DecoderModel:
         r = self.embed(batch) if self.has_embed else hidden
         if r is None:
             raise ValueError("non-first pipeline stage needs the hidden state")
+        x = None
         for i in range(self.first_layer, self.last_layer):
-            self.layer(i, r, batch, pool)
+            x = self.layer(i, r, batch, pool, x)
         if self.has_head:
             return self.logits(r, batch.logits_rows)
         return r
