@@ -83,11 +83,9 @@ class FusedAllReduce:
         """out = allreduce_over_ranks(x @ w.T) (+ bias) (+ residual): push + reduce."""
         T, H = x.shape[0], w.shape[0]
         if out is None:
-            out = residual if residual is not None else torch.empty(T, H, dtype=x.dtype, device=x.device)
-        self.push(x, w)
+            out = torch.empty(T, H, dtype=x.dtype, device=x.device)
         if residual is not None and out is not residual:
-            res = residual.clone()
-            self.reduce(T, H, bias, res, out)
-        else:
-            self.reduce(T, H, bias, residual, out)
+            out.copy_(residual)          # the reduce kernel updates its residual in place
+        self.push(x, w)
+        self.reduce(T, H, bias, out if residual is not None else None, out)
         return out

@@ -63,12 +63,22 @@ def run(model: str, n_new: int = 8, device: str = "auto", std: float = 0.05) -> 
             x = torch.randn(m, k, device=dev, generator=gg).to(dtype)
             w = (torch.randn(n, k, device=dev, generator=gg) * 0.05).to(dtype)
             r = torch.randn(m, n, device=dev, generator=gg).to(dtype)
+            bias = torch.randn(n, device=dev, generator=gg).to(dtype)
+            nw = (1 + 0.1 * torch.randn(n, device=dev, generator=gg)).to(dtype)
             ref_y = ops.linear(x, w).float()
             torch.distributed.all_reduce(ref_y)
-            ref_y = ref_y + r.float()
+            ref_s = ref_y + bias.float() + r.float()
+            ref_n = ref_s * torch.rsqrt(ref_s.pow(2).mean(-1, keepdim=True) + 1e-6) * nw.float()
             for _ in range(3):     # repeated calls exercise the alternating buffers / epochs
-                y = tp.fused_ar.linear(x, w, residual=r)
-            fused_diff = max(fused_diff, float((y.float() - ref_y).abs().max() / (ref_y.abs().max() + 1e-6)))
+                y = tp.fused_ar.linear(x, w, bias, residual=r)
+            fused_diff = max(fused_diff, float((y.float() - ref_s).abs().max() / (ref_s.abs().max() + 1e-6)))
+            # push + reduce fused with the residual update and RMSNorm
+            res = r.clone()
+            out = torch.empty_like(r)
+            tp.fused_ar.push(x, w)
+            tp.fused_ar.reduce(m, n, bias=bias, residual=res, out=out, norm_w=nw, eps=1e-6)
+            fused_diff = max(fused_diff, float((res.float() - ref_s).abs().max() / (ref_s.abs().max() + 1e-6)),
+                             float((out.float() - ref_n).abs().max() / (ref_n.abs().max() + 1e-6)))
         torch.cuda.synchronize()
     same = [a.output_ids == b.output_ids for a, b in zip(r_ref, r_tp)]
     res = {"world": info.world_size, "max_logit_diff": diff, "scale": float(items[0].abs().max()),
