@@ -579,12 +579,14 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       it += n;
     }
     if (kAR) {
-      // every thread's remote pushes are visible system-wide before the CTA counts as
-      // done; the last CTA then advances the epoch and flags every peer
-      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      // the CTA's remote pushes are ordered before its completion count (barrier, then a
+      // system-scope fence by the counting thread: release is cumulative); the last CTA
+      // advances the epoch and flags every peer
+      if (ar.per_thread_fence) asm volatile("fence.acq_rel.sys;" ::: "memory");
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (threadIdx.x == 64) {
         uint32_t prev;
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ar.done) : "memory");
         if (prev == gridDim.x - 1) {
           *ar.done = 0u;

@@ -340,7 +340,7 @@ void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k
 // Push half: row-parallel GEMM whose epilogue stores the fp32 partial into every rank's
 // receive buffer and flags the peers (ARPush).  Nothing is written to a tensor here.
 void gemm_ar_push(const Tensor& x, const Tensor& w, const Tensor& xbuf_ptrs, const Tensor& flag_ptrs, Tensor& epoch,
-                  Tensor& done, int64_t rank, int64_t world, int64_t half_floats) {
+                  Tensor& done, int64_t rank, int64_t world, int64_t half_floats, bool per_thread_fence) {
   check_bf16_2d(x, "gemm_ar x");
   check_bf16_2d(w, "gemm_ar w");
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
@@ -359,6 +359,7 @@ void gemm_ar_push(const Tensor& x, const Tensor& w, const Tensor& xbuf_ptrs, con
   ar.rank = (int)rank;
   ar.world = (int)world;
   ar.half_floats = half_floats;
+  ar.per_thread_fence = per_thread_fence ? 1 : 0;
   vrm::GemmArgs a;
   a.x = x.data_ptr();
   a.ldx = x.stride(0);
@@ -466,6 +467,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("gemm_ar_push", &gemm_ar_push, py::arg("x"), py::arg("w"), py::arg("xbuf_ptrs"), py::arg("flag_ptrs"),
         py::arg("epoch"), py::arg("done"), py::arg("rank"), py::arg("world"), py::arg("half_floats"),
+        py::arg("per_thread_fence") = false,
         "row-parallel GEMM pushing its fp32 partial into every rank's receive buffer (fused all-reduce, push)");
   m.def("ar_norm", &ar_norm, py::arg("xbuf"), py::arg("flags"), py::arg("epoch"), py::arg("rank"), py::arg("world"),
         py::arg("half_floats"), py::arg("T"), py::arg("H"), py::arg("bias"), py::arg("residual"), py::arg("w"),

@@ -52,6 +52,10 @@ struct ARPush {
   uint32_t* done = nullptr;          // this rank's CTA completion counter (device, zero)
   int rank = 0, world = 1;
   long long half_floats = 0;         // floats per (half, source rank) slot
+  // 1: every epilogue thread fences its own remote stores at system scope before the
+  // CTA barrier; 0: one system-scope fence by the flagging thread after the barrier
+  // (release cumulativity over the barrier)
+  int per_thread_fence = 0;
 };
 void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
 // Debug: per-CTA timeline of the stream-K decode GEMM into buf ([ctas][8] u64 ns), null = off.

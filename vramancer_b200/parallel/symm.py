@@ -17,6 +17,7 @@ torch.cuda.nccl.all_reduce; there is no fused path.
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -35,6 +36,7 @@ class FusedAllReduce:
         self.rank = dist.get_rank(group)
         self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
         self.max_tokens = max_tokens
+        self.per_thread_fence = os.environ.get("VRM_AR_THREAD_FENCE", "0") == "1"
         self.half_floats = max_features * max_tokens
         nat = ops.native()
         with torch.cuda.device(self.device):
@@ -67,7 +69,7 @@ class FusedAllReduce:
     def push(self, x: torch.Tensor, w: torch.Tensor) -> None:
         """Row-parallel GEMM x @ w.T whose partial goes to every rank's receive buffer."""
         ops.native().gemm_ar_push(x, w, self.xbuf_ptrs, self.flag_ptrs, self.epoch, self.done, self.rank,
-                                  self.world, self.half_floats)
+                                  self.world, self.half_floats, self.per_thread_fence)
 
     def reduce(self, T: int, H: int, bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
                out: Optional[torch.Tensor] = None, norm_w: Optional[torch.Tensor] = None,
