@@ -1,7 +1,208 @@
-"""Reference arm of bench.py: runs the unmodified reference (installed into
-baseline/_ref) through its own public API on the same metric and config."""
+"""Reference arm of bench.py: the unmodified reference (installed into baseline/_ref)
+measured through its own public API on the same metric and config.
+
+What runs, all of it reference code on its stock path:
+  bs1 + TTFT  core.turbo_engine.create_turbo_engine(model, tokenizer) (torch.compile on,
+              as core/inference_pipeline.py:927 creates it) -> warmup() -> generate_ids()
+  bs32        core.continuous_batcher.ContinuousBatcher(model, tokenizer, 32).submit()
+              x 32 -> start() -> futures
+The model is transformers' Qwen2ForCausalLM built from the Qwen2.5-14B configuration with
+random N(0, 0.02) bf16 weights directly on the GPU: there are no checkpoints offline, and
+the reference's own loader (core/backends.py:1185-1390) passes a device_map to
+from_pretrained, which needs `accelerate` (not installed).  A 14B bf16 model fits one
+B200, so the reference's single-GPU bypass (core/backends.py _try_single_gpu_placement)
+places it on one GPU whatever the GPU count: under torchrun rank 0 measures, the other
+ranks only wait.
+
+Decode rates exclude prefill: each is the difference between two runs of different
+lengths (1 + W + K and 1 + W new tokens), timed with CUDA events around the public call
+(its decode loop synchronises with the host every token).
+"""
+from __future__ import annotations
+
 import json
+import os
+import statistics
+import sys
+import time
+import zlib
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.path.join(HERE, "_ref")
+
+QWEN25_14B = dict(hidden_size=5120, intermediate_size=13824, num_hidden_layers=48, num_attention_heads=40,
+                  num_key_value_heads=8, vocab_size=152064, max_position_embeddings=32768, rope_theta=1e6,
+                  rms_norm_eps=1e-6, tie_word_embeddings=False, initializer_range=0.02)
+
+
+class IdTokenizer:
+    """Tokenizer stand-in (no tokenizer files offline): a prompt is space-separated
+    token ids; other words hash to an id.  No EOS, so every request runs to its
+    max_new_tokens, as the benchmark requires."""
+    eos_token_id = None
+    pad_token_id = 0
+    pad_token = "0"
+
+    def __init__(self, vocab: int):
+        self.vocab = vocab
+
+    def _ids(self, s):
+        return [int(t) % self.vocab if t.isdigit() else zlib.crc32(t.encode()) % self.vocab for t in s.split()] or [0]
+
+    def __call__(self, text, return_tensors="pt", padding=False, **kw):
+        import torch
+        texts = [text] if isinstance(text, str) else list(text)
+        ids = [self._ids(s) for s in texts]
+        n = max(len(x) for x in ids)
+        inp = torch.zeros(len(ids), n, dtype=torch.long)
+        mask = torch.zeros_like(inp)
+        for i, x in enumerate(ids):
+            inp[i, :len(x)] = torch.tensor(x)
+            mask[i, :len(x)] = 1
+        return {"input_ids": inp, "attention_mask": mask}
+
+    def encode(self, text, **kw):
+        return self._ids(text)
+
+    def decode(self, ids, skip_special_tokens=True, **kw):
+        return " ".join(str(int(t)) for t in ids)
+
+
+def _build_model(dev):
+    import torch
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    cfg = Qwen2Config(**QWEN25_14B)
+    torch.manual_seed(1234)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = Qwen2ForCausalLM(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    return model.eval()
+
+
+def _timed(fn):
+    import torch
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    out = fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b), out
+
+
+def _bs1(model, tok, prompt_ids, steps, warm, ttft_runs, notes):
+    import torch
+    from core.turbo_engine import create_turbo_engine
+    try:
+        eng = create_turbo_engine(model, tok, max_seq_len=2048)
+        eng.warmup()
+    except Exception as e:  # the reference falls back the same way (core/inference_pipeline.py:939)
+        notes.append(f"TurboEngine compile failed ({type(e).__name__}: {str(e)[:160]}); compile=False")
+        eng = create_turbo_engine(model, tok, max_seq_len=2048, compile=False)
+        eng.warmup()
+    ids = torch.tensor([prompt_ids], dtype=torch.long)
+    eng.generate_ids(ids, max_new_tokens=1 + warm)            # warm-up at this length
+    t_short, _ = _timed(lambda: eng.generate_ids(ids, max_new_tokens=1 + warm))
+    t_long, out = _timed(lambda: eng.generate_ids(ids, max_new_tokens=1 + warm + steps))
+    produced = out.shape[1] - ids.shape[1] - (1 + warm)
+    ms_step = (t_long - t_short) / max(1, produced)
+    ttfts = [_timed(lambda: eng.generate_ids(ids, max_new_tokens=1))[0] for _ in range(ttft_runs)]
+    return {"tok_s": round(1000.0 / ms_step, 2), "ms_per_step": round(ms_step, 3), "steps": produced,
+            "compiled": bool(getattr(eng, "_compiled", False))}, statistics.median(ttfts)
+
+
+def _bs32(model, tok, prompts, steps, warm, dev):
+    from core.continuous_batcher import ContinuousBatcher
+
+    def run(n_new):
+        b = ContinuousBatcher(model, tok, max_batch_size=len(prompts), device=dev, verbose=False)
+        futs = [b.submit(p, max_new_tokens=n_new, temperature=1.0, top_k=1) for p in prompts]
+
+        def go():
+            b.start()
+            return [f.result(timeout=3600) for f in futs]
+        try:
+            return _timed(go)
+        finally:
+            b.stop()
+
+    run(2)                                                    # warm-up
+    t_short, _ = run(1 + warm)
+    t_long, outs = run(1 + warm + steps)
+    ms_step = (t_long - t_short) / steps
+    return {"tok_s": round(len(prompts) * 1000.0 / ms_step, 2), "ms_per_step": round(ms_step, 3)}
 
 
 def run(args, metric):
-    print(json.dumps({"impl": "reference", "unavailable": "reference arm not wired yet"}), flush=True)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if not os.path.isdir(os.path.join(REF, "core")):
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not installed"}), flush=True)
+        return
+    if rank != 0:
+        return                       # single-GPU placement: only rank 0's GPU is used
+    import torch
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "reference", "unavailable": "no CUDA device"}), flush=True)
+        return
+    sys.path.insert(0, REF)
+    os.environ.setdefault("VRM_LOG_LEVEL", "WARNING")
+    dev = f"cuda:{int(os.environ.get('LOCAL_RANK', '0'))}"
+    torch.cuda.set_device(dev)
+    import random
+    rng = random.Random(42)
+    P, B = args.prompt_len, args.batch
+    steps, warm = args.steps, max(3, args.warmup)
+    vocab = QWEN25_14B["vocab_size"]
+    tok = IdTokenizer(vocab)
+    notes = []
+    t0 = time.time()
+    model = _build_model(dev)
+    prompt_ids = [rng.randrange(vocab) for _ in range(P)]
+    from bench import ClockSampler
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    bs1, ttft = _bs1(model, tok, prompt_ids, steps, warm, args.ttft_runs, notes)
+    try:
+        prompts = [" ".join(str(rng.randrange(vocab)) for _ in range(P)) for _ in range(B)]
+        bs32 = _bs32(model, tok, prompts, steps, warm, dev)
+        value = bs32["tok_s"]
+    except Exception as e:
+        bs32, value = None, None
+        notes.append(f"ContinuousBatcher failed: {type(e).__name__}: {str(e)[:200]}")
+    clk = clocks.stop()
+    res = {
+        "metric": metric,
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warm,
+        "ms_per_step": bs32["ms_per_step"] if bs32 else None,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: uniform random token ids, random-init N(0,0.02) bf16 weights (HF from_config)",
+        "config": {"model": "Qwen2.5-14B architecture", "global_batch": B, "seq_len": P,
+                   "parallelism": "single GPU (reference single-GPU bypass)",
+                   "l2": "inputs larger than L2 (all weights streamed each step)"},
+        "bs1": bs1,
+        "ttft_p50_ms": round(ttft, 3),
+        "ttft_prompt_tokens": P,
+        "e2e": {"value": value, "unit": "tok/s", "api": "ContinuousBatcher.submit / TurboEngine.generate_ids"},
+        "clocks": clk,
+        "setup_s": round(time.time() - t0, 1),
+        "notes": notes,
+        "impl": "reference",
+    }
+    if value is None:
+        res["value_unavailable"] = ("bs32: the reference's ContinuousBatcher fails on this image's transformers "
+                                    "(DynamicCache has no key_cache, core/continuous_batcher.py:878); "
+                                    "bs1 and TTFT are measured")
+    print(json.dumps(res), flush=True)
