@@ -124,7 +124,7 @@ def _bs32(model, tok, prompts, steps, warm, dev):
 
         def go():
             b.start()
-            return [f.result(timeout=3600) for f in futs]
+            return [f.result(timeout=900) for f in futs]
         try:
             return _timed(go)
         finally:
