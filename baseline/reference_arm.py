@@ -94,16 +94,25 @@ def _timed(fn):
     return a.elapsed_time(b), out
 
 
-def _bs1(model, tok, prompt_ids, steps, warm, ttft_runs, notes):
+def _bs1(model_fn, tok, prompt_ids, steps, warm, ttft_runs, notes):
     import torch
     from core.turbo_engine import create_turbo_engine
+    # warmup() with the benchmark prompt: the stock default prompt "Hello" is a 1-token
+    # prefill, which the only SDPA backend the reference leaves enabled for GQA models
+    # (cuDNN, core/turbo_engine.py:72-93) rejects on this stack ("Invalid backend")
+    text = " ".join(str(t) for t in prompt_ids)
+    model = model_fn()
     try:
         eng = create_turbo_engine(model, tok, max_seq_len=2048)
-        eng.warmup()
+        eng.warmup(prompt=text, n_tokens=4, rounds=2)
     except Exception as e:  # the reference falls back the same way (core/inference_pipeline.py:939)
-        notes.append(f"TurboEngine compile failed ({type(e).__name__}: {str(e)[:160]}); compile=False")
+        notes.append(f"TurboEngine with torch.compile failed ({type(e).__name__}: {str(e)[:160]}); "
+                     "rebuilt with compile=False")
+        del model
+        torch.cuda.empty_cache()
+        model = model_fn()      # compile=True patched the model's forward in place
         eng = create_turbo_engine(model, tok, max_seq_len=2048, compile=False)
-        eng.warmup()
+        eng.warmup(prompt=text, n_tokens=4, rounds=2)
     ids = torch.tensor([prompt_ids], dtype=torch.long)
     eng.generate_ids(ids, max_new_tokens=1 + warm)            # warm-up at this length
     t_short, _ = _timed(lambda: eng.generate_ids(ids, max_new_tokens=1 + warm))
@@ -112,7 +121,7 @@ def _bs1(model, tok, prompt_ids, steps, warm, ttft_runs, notes):
     ms_step = (t_long - t_short) / max(1, produced)
     ttfts = [_timed(lambda: eng.generate_ids(ids, max_new_tokens=1))[0] for _ in range(ttft_runs)]
     return {"tok_s": round(1000.0 / ms_step, 2), "ms_per_step": round(ms_step, 3), "steps": produced,
-            "compiled": bool(getattr(eng, "_compiled", False))}, statistics.median(ttfts)
+            "compiled": bool(getattr(eng, "_compiled", False))}, statistics.median(ttfts), model
 
 
 def _bs32(model, tok, prompts, steps, warm, dev):
@@ -162,12 +171,11 @@ def run(args, metric):
     tok = IdTokenizer(vocab)
     notes = []
     t0 = time.time()
-    model = _build_model(dev)
     prompt_ids = [rng.randrange(vocab) for _ in range(P)]
     from bench import ClockSampler
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
-    bs1, ttft = _bs1(model, tok, prompt_ids, steps, warm, args.ttft_runs, notes)
+    bs1, ttft, model = _bs1(lambda: _build_model(dev), tok, prompt_ids, steps, warm, args.ttft_runs, notes)
     try:
         prompts = [" ".join(str(rng.randrange(vocab)) for _ in range(P)) for _ in range(B)]
         bs32 = _bs32(model, tok, prompts, steps, warm, dev)
