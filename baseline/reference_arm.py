@@ -80,7 +80,8 @@ def _build_model(dev):
             model = Qwen2ForCausalLM(cfg)
     finally:
         torch.set_default_dtype(prev)
-    return model.eval()
+    # some parameters (lm_head) can still be created on the host: move everything
+    return model.to(device=dev, dtype=torch.bfloat16).eval()
 
 
 def _timed(fn):
