@@ -1,9 +1,15 @@
 """Reference arm of bench.py: the unmodified reference (installed into baseline/_ref)
 measured through its own public API on the same metric and config.
 
-What runs, all of it reference code on its stock path:
-  bs1 + TTFT  core.turbo_engine.create_turbo_engine(model, tokenizer) (torch.compile on,
-              as core/inference_pipeline.py:927 creates it) -> warmup() -> generate_ids()
+What runs, all of it reference code:
+  bs1 + TTFT  core.turbo_engine.create_turbo_engine(model, tokenizer) -> warmup() ->
+              generate_ids(), the engine core/inference_pipeline.py:927 creates.  On a
+              compute-capability >= 10 GPU without torchao that engine cannot run: it
+              moves lm_head to the host to quantise it to FP4 (core/turbo_engine.py:
+              314-328), the quantiser needs torchao, and the caught ImportError leaves
+              lm_head on the host.  The arm then measures the reference's path with
+              VRM_DISABLE_TURBO: core.backends.HuggingFaceBackend.generate (HF generate
+              with KV cache, core/backends.py:1868-1934), and says so in "notes".
   bs32        core.continuous_batcher.ContinuousBatcher(model, tokenizer, 32).submit()
               x 32 -> start() -> futures
 The model is transformers' Qwen2ForCausalLM built from the Qwen2.5-14B configuration with
@@ -59,7 +65,8 @@ class IdTokenizer:
         for i, x in enumerate(ids):
             inp[i, :len(x)] = torch.tensor(x)
             mask[i, :len(x)] = 1
-        return {"input_ids": inp, "attention_mask": mask}
+        from transformers import BatchEncoding
+        return BatchEncoding({"input_ids": inp, "attention_mask": mask})
 
     def encode(self, text, **kw):
         return self._ids(text)
@@ -95,34 +102,63 @@ def _timed(fn):
     return a.elapsed_time(b), out
 
 
-def _bs1(model_fn, tok, prompt_ids, steps, warm, ttft_runs, notes):
+def _turbo_usable(dev) -> str:
+    """'' when the reference TurboEngine can run here, else why not."""
+    import importlib.util
     import torch
+    if torch.cuda.get_device_capability(dev)[0] >= 10 and importlib.util.find_spec("torchao") is None:
+        return ("TurboEngine unusable: on cc>=10 it moves lm_head to the host for FP4 quantisation, which needs "
+                "torchao (not installed); the caught ImportError leaves lm_head on the host "
+                "(core/turbo_engine.py:314-328)")
+    return ""
+
+
+def _bs1_turbo(model, tok, text, ids, steps, warm, ttft_runs):
     from core.turbo_engine import create_turbo_engine
-    # warmup() with the benchmark prompt: the stock default prompt "Hello" is a 1-token
-    # prefill, which the only SDPA backend the reference leaves enabled for GQA models
-    # (cuDNN, core/turbo_engine.py:72-93) rejects on this stack ("Invalid backend")
-    text = " ".join(str(t) for t in prompt_ids)
-    model = model_fn()
-    try:
-        eng = create_turbo_engine(model, tok, max_seq_len=2048)
-        eng.warmup(prompt=text, n_tokens=4, rounds=2)
-    except Exception as e:  # the reference falls back the same way (core/inference_pipeline.py:939)
-        notes.append(f"TurboEngine with torch.compile failed ({type(e).__name__}: {str(e)[:160]}); "
-                     "rebuilt with compile=False")
-        del model
-        torch.cuda.empty_cache()
-        model = model_fn()      # compile=True patched the model's forward in place
-        eng = create_turbo_engine(model, tok, max_seq_len=2048, compile=False)
-        eng.warmup(prompt=text, n_tokens=4, rounds=2)
-    ids = torch.tensor([prompt_ids], dtype=torch.long)
-    eng.generate_ids(ids, max_new_tokens=1 + warm)            # warm-up at this length
+    eng = create_turbo_engine(model, tok, max_seq_len=2048)
+    # warmup() with the benchmark prompt: the stock default "Hello" is a 1-token prefill,
+    # which cuDNN SDPA (the only backend the engine leaves enabled for GQA models,
+    # core/turbo_engine.py:72-93) rejects on this stack ("Invalid backend")
+    eng.warmup(prompt=text, n_tokens=4, rounds=2)
+    eng.generate_ids(ids, max_new_tokens=1 + warm)
     t_short, _ = _timed(lambda: eng.generate_ids(ids, max_new_tokens=1 + warm))
     t_long, out = _timed(lambda: eng.generate_ids(ids, max_new_tokens=1 + warm + steps))
     produced = out.shape[1] - ids.shape[1] - (1 + warm)
-    ms_step = (t_long - t_short) / max(1, produced)
     ttfts = [_timed(lambda: eng.generate_ids(ids, max_new_tokens=1))[0] for _ in range(ttft_runs)]
-    return {"tok_s": round(1000.0 / ms_step, 2), "ms_per_step": round(ms_step, 3), "steps": produced,
-            "compiled": bool(getattr(eng, "_compiled", False))}, statistics.median(ttfts), model
+    return (t_long - t_short) / max(1, produced), ttfts, "TurboEngine.generate_ids"
+
+
+def _bs1_backend(model, tok, text, steps, warm, ttft_runs):
+    from core.backends import HuggingFaceBackend
+    be = HuggingFaceBackend("qwen2.5-14b-random-init")
+    be.model, be.tokenizer = model, tok
+
+    def gen(n):
+        return be.generate(text, max_new_tokens=n, min_new_tokens=n, do_sample=False)
+    gen(1 + warm)
+    t_short, _ = _timed(lambda: gen(1 + warm))
+    t_long, _ = _timed(lambda: gen(1 + warm + steps))
+    ttfts = [_timed(lambda: gen(1))[0] for _ in range(ttft_runs)]
+    return (t_long - t_short) / steps, ttfts, "HuggingFaceBackend.generate (VRM_DISABLE_TURBO path)"
+
+
+def _bs1(model, tok, prompt_ids, steps, warm, ttft_runs, notes, dev):
+    import torch
+    text = " ".join(str(t) for t in prompt_ids)
+    why = _turbo_usable(dev)
+    if not why:
+        try:
+            ids = torch.tensor([prompt_ids], dtype=torch.long)
+            ms, ttfts, api = _bs1_turbo(model, tok, text, ids, steps, warm, ttft_runs)
+            return {"tok_s": round(1000.0 / ms, 2), "ms_per_step": round(ms, 3), "api": api}, \
+                statistics.median(ttfts)
+        except Exception as e:   # the pipeline falls back the same way (core/inference_pipeline.py:939)
+            why = f"TurboEngine failed: {type(e).__name__}: {str(e)[:160]}"
+            model.to(dev)
+    notes.append(why)
+    os.environ["VRM_DISABLE_TURBO"] = "1"
+    ms, ttfts, api = _bs1_backend(model, tok, text, steps, warm, ttft_runs)
+    return {"tok_s": round(1000.0 / ms, 2), "ms_per_step": round(ms, 3), "api": api}, statistics.median(ttfts)
 
 
 def _bs32(model, tok, prompts, steps, warm, dev):
@@ -172,11 +208,12 @@ def run(args, metric):
     tok = IdTokenizer(vocab)
     notes = []
     t0 = time.time()
+    model = _build_model(dev)
     prompt_ids = [rng.randrange(vocab) for _ in range(P)]
     from bench import ClockSampler
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
-    bs1, ttft, model = _bs1(lambda: _build_model(dev), tok, prompt_ids, steps, warm, args.ttft_runs, notes)
+    bs1, ttft = _bs1(model, tok, prompt_ids, steps, warm, args.ttft_runs, notes, dev)
     try:
         prompts = [" ".join(str(rng.randrange(vocab)) for _ in range(P)) for _ in range(B)]
         bs32 = _bs32(model, tok, prompts, steps, warm, dev)
@@ -204,7 +241,7 @@ def run(args, metric):
         "bs1": bs1,
         "ttft_p50_ms": round(ttft, 3),
         "ttft_prompt_tokens": P,
-        "e2e": {"value": value, "unit": "tok/s", "api": "ContinuousBatcher.submit / TurboEngine.generate_ids"},
+        "e2e": {"value": value, "unit": "tok/s", "api": "ContinuousBatcher.submit"},
         "clocks": clk,
         "setup_s": round(time.time() - t0, 1),
         "notes": notes,
