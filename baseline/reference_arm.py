@@ -248,7 +248,6 @@ def run(args, metric):
         "impl": "reference",
     }
     if value is None:
-        res["value_unavailable"] = ("bs32: the reference's ContinuousBatcher fails on this image's transformers "
-                                    "(DynamicCache has no key_cache, core/continuous_batcher.py:878); "
-                                    "bs1 and TTFT are measured")
+        res["value_unavailable"] = "bs32: " + (notes[-1] if notes else "ContinuousBatcher failed") + \
+            "; bs1 and TTFT are measured"
     print(json.dumps(res), flush=True)

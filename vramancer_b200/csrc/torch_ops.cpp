@@ -409,6 +409,76 @@ void ar_norm(int64_t xbuf, int64_t flags, const Tensor& epoch, int64_t rank, int
   vrm::ar_norm(a, cur_stream());
 }
 
+// ---------------------------------------------------------------- NVFP4 weights
+void check_nvfp4(const Tensor& q, const Tensor& sc, const Tensor& gs, int64_t N, int64_t K, const char* op) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kUInt8 && q.is_contiguous() && q.numel() == N * K / 2, op,
+              ": q must be contiguous uint8 [N * K / 2]");
+  TORCH_CHECK(sc.scalar_type() == torch::kUInt8 && sc.is_contiguous() && sc.numel() == N * K / 16, op,
+              ": s must be contiguous uint8 [N * K / 16]");
+  TORCH_CHECK(gs.scalar_type() == torch::kFloat32 && gs.numel() == 1, op, ": gs must be one fp32 value");
+  TORCH_CHECK(N % 16 == 0 && K % 64 == 0, op, ": N must be a multiple of 16 and K of 64");
+  same_device(q, {&sc, &gs}, op);
+}
+
+std::vector<Tensor> nvfp4_quantize(const Tensor& w, const Tensor& gs) {
+  check_bf16_2d(w, "nvfp4_quantize w");
+  const int64_t N = w.size(0), K = w.size(1);
+  auto q = torch::empty({N * K / 2}, w.options().dtype(torch::kUInt8));
+  auto sc = torch::empty({N * K / 16}, w.options().dtype(torch::kUInt8));
+  check_nvfp4(q, sc, gs, N, K, "nvfp4_quantize");
+  same_device(w, {&gs}, "nvfp4_quantize");
+  const c10::cuda::CUDAGuard guard(w.device());
+  vrm::nvfp4_quantize(w.data_ptr(), w.stride(0), (int)N, (int)K, gs.data_ptr<float>(), q.data_ptr<uint8_t>(),
+                      sc.data_ptr<uint8_t>(), cur_stream());
+  return {q, sc};
+}
+
+Tensor nvfp4_dequantize(const Tensor& q, const Tensor& sc, const Tensor& gs, int64_t N, int64_t K) {
+  check_nvfp4(q, sc, gs, N, K, "nvfp4_dequantize");
+  auto out = torch::empty({N, K}, q.options().dtype(torch::kBFloat16));
+  const c10::cuda::CUDAGuard guard(q.device());
+  vrm::nvfp4_dequantize(q.data_ptr<uint8_t>(), sc.data_ptr<uint8_t>(), gs.data_ptr<float>(), (int)N, (int)K,
+                        out.data_ptr(), cur_stream());
+  return out;
+}
+
+void nvfp4_gemm_out(const Tensor& x, const Tensor& q, const Tensor& sc, const Tensor& gs, int64_t N,
+                    const OptT& bias, Tensor& out, int64_t epilogue, const OptT& residual) {
+  check_bf16_2d(x, "nvfp4_gemm x");
+  check_bf16_2d(out, "nvfp4_gemm out");
+  const int64_t M = x.size(0), K = x.size(1);
+  check_nvfp4(q, sc, gs, N, K, "nvfp4_gemm");
+  same_device(x, {&q, &out}, "nvfp4_gemm");
+  same_device_opt(x, {&bias, &residual}, "nvfp4_gemm");
+  const int64_t n_out = epilogue == vrm::kEpiSiluMul ? N / 2 : N;
+  TORCH_CHECK(out.size(0) == M && out.size(1) == n_out, "nvfp4_gemm: out must be [", M, ", ", n_out, "]");
+  vrm::Nvfp4GemmArgs a;
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.q = q.data_ptr<uint8_t>();
+  a.s = sc.data_ptr<uint8_t>();
+  a.gs = gs.data_ptr<float>();
+  if (has(bias)) {
+    TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->is_contiguous() && bias->numel() == N,
+                "nvfp4_gemm: bias must be contiguous bf16 [N]");
+    a.bias = bias->data_ptr();
+  }
+  if (has(residual)) {
+    check_bf16_2d(*residual, "nvfp4_gemm residual");
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N && residual->stride(0) == out.stride(0),
+                "nvfp4_gemm: residual must match out");
+    a.residual = residual->data_ptr();
+  }
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.epilogue = (int)epilogue;
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::nvfp4_gemm(a, cur_stream());
+}
+
 // ---------------------------------------------------------------- page migration
 void page_copy(const Tensor& src_pool, Tensor& dst_pool, const Tensor& src_idx, const Tensor& dst_idx) {
   TORCH_CHECK(src_pool.is_cuda() && dst_pool.is_cuda() && src_pool.is_contiguous() && dst_pool.is_contiguous(),
@@ -465,6 +535,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {
     vrm::gemm_set_trace(buf.has_value() && buf->defined() ? buf->data_ptr() : nullptr);
   });
+  m.def("nvfp4_quantize", &nvfp4_quantize, py::arg("w"), py::arg("gs"),
+        "bf16 [N, K] -> (q, s) NVFP4 bytes in fragment order, per-tensor scale gs on the device");
+  m.def("nvfp4_dequantize", &nvfp4_dequantize, py::arg("q"), py::arg("s"), py::arg("gs"), py::arg("N"), py::arg("K"));
+  m.def("nvfp4_gemm_out", &nvfp4_gemm_out, py::arg("x"), py::arg("q"), py::arg("s"), py::arg("gs"), py::arg("N"),
+        py::arg("bias"), py::arg("out"), py::arg("epilogue"), py::arg("residual"),
+        "W4A16 decode GEMM (M <= 32) over NVFP4 weights");
+  m.def("nvfp4_gemm_max_m", &vrm::nvfp4_gemm_max_m);
   m.def("gemm_ar_push", &gemm_ar_push, py::arg("x"), py::arg("w"), py::arg("xbuf_ptrs"), py::arg("flag_ptrs"),
         py::arg("epoch"), py::arg("done"), py::arg("rank"), py::arg("world"), py::arg("half_floats"),
         py::arg("per_thread_fence") = false,

@@ -95,6 +95,32 @@ struct ARNormArgs {
 };
 void ar_norm(const ARNormArgs& a, cudaStream_t stream);
 
+// ---------------------------------------------------------------- NVFP4 weights (nvfp4.cu)
+// Quantises W bf16 [N, K] (N % 16 == 0, K % 64 == 0) with the per-tensor scale *gs
+// (= amax / (6 * 448), on the device) into q [N * K / 2] and s [N * K / 16] bytes in
+// fragment order; dequantises back to bf16 [N, K] row-major.
+void nvfp4_quantize(const void* w, int64_t ldw, int N, int K, const float* gs, uint8_t* q, uint8_t* s,
+                    cudaStream_t stream);
+void nvfp4_dequantize(const uint8_t* q, const uint8_t* s, const float* gs, int N, int K, void* out,
+                      cudaStream_t stream);
+// W4A16 GEMM for decode (M <= nvfp4_gemm_max_m()): out[M, N] = x @ W'^T (+ bias)
+// (+ residual), or the SiLU(gate) * up epilogue over interleaved rows (out [M, N/2]).
+struct Nvfp4GemmArgs {
+  const void* x = nullptr;      // bf16 [M, K]
+  int64_t ldx = 0;
+  const uint8_t* q = nullptr;
+  const uint8_t* s = nullptr;
+  const float* gs = nullptr;
+  const void* bias = nullptr;
+  const void* residual = nullptr;   // bf16 [M, N], leading dimension ldo
+  void* out = nullptr;
+  int64_t ldo = 0;
+  int M = 0, N = 0, K = 0;
+  int epilogue = kEpiNone;
+};
+void nvfp4_gemm(const Nvfp4GemmArgs& a, cudaStream_t stream);
+int nvfp4_gemm_max_m();
+
 struct RopeKvArgs {
   void* qkv = nullptr;          // bf16 [T, (Hq + 2 KH) * D], rotated in place
   int64_t ld_qkv = 0;

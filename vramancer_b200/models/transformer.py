@@ -133,7 +133,7 @@ class DecoderModel:
             ops.linear(x, w, b, residual=r, out=r)
             return self._norm(r, nxt[0] if nxt[0] is not None else "final", nxt[1]) if nxt else None
         far = self.tp.fused_ar
-        if far is not None and x.is_cuda and far.supports(x.shape[0], w.shape[0]):
+        if far is not None and x.is_cuda and getattr(w, "_vrm_quant", None) is None and far.supports(x.shape[0], w.shape[0]):
             # push the partial to every rank, then one kernel: reduce + bias + residual + norm
             T, H = x.shape[0], w.shape[0]
             far.push(x, w)

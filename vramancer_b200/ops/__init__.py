@@ -61,7 +61,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
            out: Optional[torch.Tensor] = None, epilogue: int = EPI_NONE,
            residual: Optional[torch.Tensor] = None, force_splits: int = 0) -> torch.Tensor:
     """y = x @ w.T (+ bias) (+ residual); with EPI_SILU_MUL, w rows are interleaved
-    (gate_j, up_j) pairs and y[:, j] = silu(gate_j) * up_j."""
+    (gate_j, up_j) pairs and y[:, j] = silu(gate_j) * up_j.  `w` may be a quantised
+    weight (quant.nvfp4.NVFP4Weight), which brings its own GEMM."""
+    if getattr(w, "_vrm_quant", None) is not None:
+        return w.linear(x, bias, out=out, epilogue=epilogue, residual=residual)
     if x.is_cuda:
         if out is None:
             n = w.shape[0] // 2 if epilogue == EPI_SILU_MUL else w.shape[0]

@@ -91,6 +91,31 @@ def bench_gemm(m, n, k, iters=50, copies=None):
             "peaks": src}
 
 
+def bench_nvfp4(m, n, k, iters=50, copies=None):
+    """W4A16 NVFP4 GEMM; bytes = packed weights + block scales + activations + output."""
+    from ..quant.nvfp4 import quantize
+    hbm, tflops, src = peaks()
+    wbytes = n * k // 2 + n * k // 16
+    if copies is None:
+        copies = max(1, math.ceil(3 * 126e6 / wbytes))
+    base = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.02
+    ws = [quantize(base * (1 + 0.01 * i)) for i in range(copies)]
+    del base
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    state = [0]
+
+    def fn():
+        linear(x, ws[state[0] % copies], out=out)
+        state[0] += 1
+
+    us = time_it(fn, iters)
+    byts = wbytes + m * k * 2 + m * n * 2
+    return {"kernel": "nvfp4_gemm", "m": m, "n": n, "k": k, "us": round(us, 2),
+            "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3),
+            "bf16_equiv_tb_s": round(n * k * 2 / us / 1e6, 3), "peaks": src}
+
+
 def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4, fp8=False, iters=50):
     hbm, _, src = peaks()
     ps = 16
@@ -150,7 +175,7 @@ QWEN14B_DECODE = [("qkv", 7168, 5120), ("o_proj", 5120, 5120), ("gate_up", 27648
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "decode-attn", "all", "trace"])
+    ap.add_argument("what", choices=["gemm", "nvfp4", "decode-attn", "all", "trace"])
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--n", type=int, default=5120)
     ap.add_argument("--k", type=int, default=13824)
@@ -167,6 +192,11 @@ def main(argv=None):
             print(json.dumps(r))
     elif a.what == "gemm":
         print(json.dumps(bench_gemm(a.m, a.n, a.k, a.iters)))
+    elif a.what == "nvfp4":
+        shapes = [(a.n, a.k)] if a.n != 5120 or a.k != 13824 else [(n, k) for _, n, k in QWEN14B_DECODE[:4]]
+        for m in ((a.m,) if a.m != 1 else (1, 8, 32)):
+            for n, k in shapes:
+                print(json.dumps(bench_nvfp4(m, n, k, a.iters)))
     elif a.what == "decode-attn":
         print(json.dumps(bench_decode_attn(a.batch, a.ctx, fp8=a.fp8, iters=a.iters)))
     else:
