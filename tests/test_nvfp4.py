@@ -73,8 +73,9 @@ def test_quantize_model_weights_skips_non_projections():
 def test_quantize_kernel_matches_oracle(N, K):
     g = torch.Generator().manual_seed(K)
     w = (torch.randn(N, K, generator=g) * torch.rand(N, 1, generator=g) * 2).to(torch.bfloat16)
-    ref = nvfp4.quantize_ref(w)
     got = nvfp4.quantize(w.cuda())
+    assert torch.equal(got.gs.cpu(), nvfp4.global_scale(w))
+    ref = nvfp4.quantize_ref(w, got.gs)
     assert torch.equal(got.s.cpu(), ref.s)
     # bytes may differ only in the sign of zero codes: compare values
     assert torch.equal(nvfp4.dequantize_ref(got), nvfp4.dequantize_ref(ref))

@@ -435,8 +435,10 @@ void nvfp4_gemm(const Nvfp4GemmArgs& a, cudaStream_t st) {
   const int NT = (a.M + 7) / 8;
   const int rbs = (a.N + kNvRows - 1) / kNvRows;
   const int ktiles = a.K / 64;
-  // ~2 CTAs per SM, and the staged X slice within the shared-memory cap
-  int splits = std::max(1, std::min(ktiles, (2 * device_sm_count() + rbs - 1) / rbs));
+  // fill the 2 CTAs per SM of one wave without spilling into a second one, and keep the
+  // staged X slice within the shared-memory cap
+  const int slots = 2 * device_sm_count();
+  int splits = std::max(1, std::min(ktiles, slots / rbs));
   auto smem_for = [&](int sp) {
     const int kc = ((ktiles + sp - 1) / sp) * 64;
     return std::max((size_t)NT * 8 * (kc + 8) * 2, (size_t)NT * 8 * kNvRows * 4);

@@ -117,7 +117,9 @@ def e2m1_values(codes: torch.Tensor) -> torch.Tensor:
 
 def global_scale(w: torch.Tensor) -> torch.Tensor:
     amax = w.abs().amax().float().reshape(1)
-    gs = amax / (FP4_MAX * E4M3_MAX)
+    # tensor / tensor: a true division on every device (CUDA divides by a Python
+    # scalar through its reciprocal, which can differ in the last bit)
+    gs = amax / torch.full_like(amax, FP4_MAX * E4M3_MAX)
     return torch.where(gs > 0, gs, torch.ones_like(gs))
 
 
@@ -129,13 +131,13 @@ def block_scales_ref(w: torch.Tensor, gs: torch.Tensor) -> torch.Tensor:
     return s.to(torch.float8_e4m3fn).view(torch.uint8)
 
 
-def quantize_ref(w: torch.Tensor) -> NVFP4Weight:
+def quantize_ref(w: torch.Tensor, gs: Optional[torch.Tensor] = None) -> NVFP4Weight:
     """Host restatement of the quantisation kernels (the test oracle)."""
     w = w.detach().cpu()
     N, K = w.shape
     if N % 16 or K % 64:
         raise ValueError(f"nvfp4: N must be a multiple of 16 and K of 64, got {N}x{K}")
-    gs = global_scale(w)
+    gs = global_scale(w) if gs is None else gs.detach().cpu().float().reshape(1)
     s8 = block_scales_ref(w, gs)
     sf = s8.view(torch.float8_e4m3fn).float()
     denom = (sf * gs).repeat_interleave(16, dim=1)
