@@ -158,14 +158,16 @@ __device__ __forceinline__ void epi_store(const EpiParams& p, int row_glob, int 
     const int n = row_glob;
     if (n >= p.N) return;
     const float bn = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
+    // out may alias residual (in-place update): read every residual value before the
+    // first store, so the 16 loads are in flight together instead of one per store
+    float rv[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      rv[j] = (p.residual && col0 + j < p.M) ? __bfloat162float(p.residual[(size_t)(col0 + j) * p.ldo + n]) : 0.f;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int m = col0 + j;
-      if (m < p.M) {
-        float t = v[j] + bn;
-        if (p.residual) t += __bfloat162float(p.residual[(size_t)m * p.ldo + n]);
-        p.out[(size_t)m * p.ldo + n] = __float2bfloat16(t);
-      }
+      if (m < p.M) p.out[(size_t)m * p.ldo + n] = __float2bfloat16(v[j] + bn + rv[j]);
     }
   }
 }
@@ -542,13 +544,19 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           continue;
         }
         if (!whole) {
-          // owner's own contribution is index 0; add the others in contributor order
-          for (int q = 1; q < nc; ++q) {
-            float x[16];
+          // owner's own contribution is index 0; add the others in contributor order,
+          // loading up to four contributors' partials at once
+          for (int q0 = 1; q0 < nc; q0 += 4) {
+            float x[4][16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) x[j] = __ldcg(base + (size_t)q * (kBM * BN) + (size_t)(c0 + j) * kBM);
+            for (int u = 0; u < 4; ++u)
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] += x[j];
+              for (int j = 0; j < 16; ++j)
+                x[u][j] = q0 + u < nc ? __ldcg(base + (size_t)(q0 + u) * (kBM * BN) + (size_t)(c0 + j) * kBM) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] += x[u][j];
           }
         }
         if (kAR) {

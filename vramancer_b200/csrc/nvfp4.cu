@@ -32,6 +32,7 @@ namespace {
 
 constexpr int kNvThreads = 256;   // 8 warps, one 16-row strip each: 128 rows per CTA
 constexpr int kNvRows = 128;
+constexpr int kSld = 132;          // fp32 accumulator tile row stride (conflict-free stores)
 
 __device__ __forceinline__ uint16_t f32x2_to_e4m3x2(float hi, float lo) {
   uint16_t r;
@@ -272,18 +273,29 @@ __global__ void __launch_bounds__(kNvThreads, 2)
   __half* xsm = reinterpret_cast<__half*>(smem);
   const auto* x = reinterpret_cast<const __nv_bfloat16*>(a.x);
   const int vpr = kc / 8;
-  for (int idx = threadIdx.x; idx < MT * vpr; idx += kNvThreads) {
-    const int m = idx / vpr, v = idx % vpr;
-    const int k = kbeg + v * 8;
-    uint4 o = make_uint4(0u, 0u, 0u, 0u);
-    if (m < a.M && k < kend) {
-      const uint4 b = *reinterpret_cast<const uint4*>(x + (size_t)m * a.ldx + k);
-      o.x = f32x2_to_f16x2_sat(bf16_lo(b.x), bf16_hi(b.x));
-      o.y = f32x2_to_f16x2_sat(bf16_lo(b.y), bf16_hi(b.y));
-      o.z = f32x2_to_f16x2_sat(bf16_lo(b.z), bf16_hi(b.z));
-      o.w = f32x2_to_f16x2_sat(bf16_lo(b.w), bf16_hi(b.w));
+  // eight independent 16-byte loads in flight per thread, then convert and store
+  constexpr int kB = 8;
+  for (int base = threadIdx.x; base < MT * vpr; base += kNvThreads * kB) {
+    uint4 raw[kB];
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int idx = base + b * kNvThreads;
+      const int m = idx / vpr, k = kbeg + (idx % vpr) * 8;
+      raw[b] = make_uint4(0u, 0u, 0u, 0u);
+      if (idx < MT * vpr && m < a.M && k < kend) raw[b] = *reinterpret_cast<const uint4*>(x + (size_t)m * a.ldx + k);
     }
-    *reinterpret_cast<uint4*>(xsm + (size_t)m * xs + v * 8) = o;
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int idx = base + b * kNvThreads;
+      if (idx >= MT * vpr) break;
+      const int m = idx / vpr, v = idx % vpr;
+      uint4 o;
+      o.x = f32x2_to_f16x2_sat(bf16_lo(raw[b].x), bf16_hi(raw[b].x));
+      o.y = f32x2_to_f16x2_sat(bf16_lo(raw[b].y), bf16_hi(raw[b].y));
+      o.z = f32x2_to_f16x2_sat(bf16_lo(raw[b].z), bf16_hi(raw[b].z));
+      o.w = f32x2_to_f16x2_sat(bf16_lo(raw[b].w), bf16_hi(raw[b].w));
+      *reinterpret_cast<uint4*>(xsm + (size_t)m * xs + v * 8) = o;
+    }
   }
   __syncthreads();
 
@@ -336,10 +348,10 @@ __global__ void __launch_bounds__(kNvThreads, 2)
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int m = nt * 8 + tig * 2;
-      S[m * kNvRows + r] = acc[nt][0];
-      S[(m + 1) * kNvRows + r] = acc[nt][1];
-      S[m * kNvRows + r + 8] = acc[nt][2];
-      S[(m + 1) * kNvRows + r + 8] = acc[nt][3];
+      S[m * kSld + r] = acc[nt][0];
+      S[(m + 1) * kSld + r] = acc[nt][1];
+      S[m * kSld + r + 8] = acc[nt][2];
+      S[(m + 1) * kSld + r + 8] = acc[nt][3];
     }
   }
   __syncthreads();
@@ -350,7 +362,7 @@ __global__ void __launch_bounds__(kNvThreads, 2)
     float* part = ws + (size_t)sp * M * N;
     for (int idx = threadIdx.x; idx < M * kNvRows; idx += kNvThreads) {
       const int m = idx / kNvRows, r = idx % kNvRows;
-      if (n0 + r < N) __stcg(part + (size_t)m * N + n0 + r, S[m * kNvRows + r]);
+      if (n0 + r < N) __stcg(part + (size_t)m * N + n0 + r, S[m * kSld + r]);
     }
     __threadfence();
     __syncthreads();
@@ -361,9 +373,24 @@ __global__ void __launch_bounds__(kNvThreads, 2)
     for (int idx = threadIdx.x; idx < M * kNvRows; idx += kNvThreads) {
       const int m = idx / kNvRows, r = idx % kNvRows;
       if (n0 + r >= N) continue;
+      // the partials' loads are independent: issue them together, add in split order
+      const float* src = ws + (size_t)m * N + n0 + r;
+      const size_t stride = (size_t)M * N;
       float v = 0.f;
-      for (int p = 0; p < splits; ++p) v += __ldcg(ws + ((size_t)p * M + m) * N + n0 + r);
-      S[m * kNvRows + r] = v;
+      int p = 0;
+      for (; p + 8 <= splits; p += 8) {
+        float t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) t[u] = __ldcg(src + (size_t)(p + u) * stride);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v += t[u];
+      }
+      float t[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) t[u] = p + u < splits ? __ldcg(src + (size_t)(p + u) * stride) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v += t[u];
+      S[m * kSld + r] = v;
     }
     if (threadIdx.x == 0) counters[rb] = 0u;
     __syncthreads();
@@ -378,7 +405,7 @@ __global__ void __launch_bounds__(kNvThreads, 2)
       const int m = idx / (kNvRows / 2), j = idx % (kNvRows / 2);
       const int n = n0 + 2 * j;
       if (n >= N) continue;
-      float gt = S[m * kNvRows + 2 * j] * gs, up = S[m * kNvRows + 2 * j + 1] * gs;
+      float gt = S[m * kSld + 2 * j] * gs, up = S[m * kSld + 2 * j + 1] * gs;
       if (bias) {
         gt += __bfloat162float(bias[n]);
         up += __bfloat162float(bias[n + 1]);
@@ -390,7 +417,7 @@ __global__ void __launch_bounds__(kNvThreads, 2)
       const int m = idx / kNvRows, r = idx % kNvRows;
       const int n = n0 + r;
       if (n >= N) continue;
-      float y = S[m * kNvRows + r] * gs;
+      float y = S[m * kSld + r] * gs;
       if (bias) y += __bfloat162float(bias[n]);
       if (res) y += __bfloat162float(res[(size_t)m * a.ldo + n]);
       out[(size_t)m * a.ldo + n] = __float2bfloat16(y);
@@ -441,7 +468,7 @@ void nvfp4_gemm(const Nvfp4GemmArgs& a, cudaStream_t st) {
   int splits = std::max(1, std::min(ktiles, slots / rbs));
   auto smem_for = [&](int sp) {
     const int kc = ((ktiles + sp - 1) / sp) * 64;
-    return std::max((size_t)NT * 8 * (kc + 8) * 2, (size_t)NT * 8 * kNvRows * 4);
+    return std::max((size_t)NT * 8 * (kc + 8) * 2, (size_t)NT * 8 * kSld * 4);
   };
   while (smem_for(splits) > (size_t)kNvSmemCap && splits < ktiles) ++splits;
   const int tps = (ktiles + splits - 1) / splits;

@@ -67,7 +67,7 @@ def time_it(fn, iters=50, warm=5, graph=True):
     return e0.elapsed_time(e1) / iters * 1000.0  # us
 
 
-def bench_gemm(m, n, k, iters=50, copies=None):
+def bench_gemm(m, n, k, iters=50, copies=None, residual=False):
     """Rotates over enough weight copies to exceed L2 so every launch streams from HBM."""
     hbm, tflops, src = peaks()
     wbytes = n * k * 2
@@ -79,13 +79,14 @@ def bench_gemm(m, n, k, iters=50, copies=None):
     state = [0]
 
     def fn():
-        linear(x, ws[state[0] % copies], out=out)
+        # residual=True: the in-place residual update of the decode step (out += x W^T)
+        linear(x, ws[state[0] % copies], out=out, residual=out if residual else None)
         state[0] += 1
 
     us = time_it(fn, iters)
-    byts = wbytes + m * k * 2 + m * n * 2
+    byts = wbytes + m * k * 2 + m * n * 2 * (2 if residual else 1)
     flops = 2.0 * m * n * k
-    return {"kernel": "gemm", "m": m, "n": n, "k": k, "us": round(us, 2),
+    return {"kernel": "gemm", "m": m, "n": n, "k": k, "residual": residual, "us": round(us, 2),
             "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3),
             "tflops": round(flops / us / 1e6, 1), "frac_tc": round(flops / us / 1e6 / tflops, 3),
             "peaks": src}
@@ -183,6 +184,7 @@ def main(argv=None):
     ap.add_argument("--ctx", type=int, default=768)
     ap.add_argument("--fp8", action="store_true")
     ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--residual", action="store_true")
     a = ap.parse_args(argv)
     native()
     if a.what == "trace":
@@ -191,7 +193,7 @@ def main(argv=None):
             r["name"] = name
             print(json.dumps(r))
     elif a.what == "gemm":
-        print(json.dumps(bench_gemm(a.m, a.n, a.k, a.iters)))
+        print(json.dumps(bench_gemm(a.m, a.n, a.k, a.iters, residual=a.residual)))
     elif a.what == "nvfp4":
         shapes = [(a.n, a.k)] if a.n != 5120 or a.k != 13824 else [(n, k) for _, n, k in QWEN14B_DECODE[:4]]
         for m in ((a.m,) if a.m != 1 else (1, 8, 32)):
@@ -205,6 +207,10 @@ def main(argv=None):
                 r = bench_gemm(m, n, k, a.iters)
                 r["name"] = name
                 print(json.dumps(r))
+                if name in ("o_proj", "down"):     # the decode step adds the residual in place
+                    r = bench_gemm(m, n, k, a.iters, residual=True)
+                    r["name"] = name + "+residual"
+                    print(json.dumps(r))
         for b in (1, 32):
             for fp8 in (False, True):
                 print(json.dumps(bench_decode_attn(b, a.ctx, fp8=fp8, iters=a.iters)))
