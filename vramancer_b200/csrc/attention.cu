@@ -98,7 +98,6 @@ struct DecodeParams {
 template <int D, bool kFp8>
 __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   pdl_launch();
-  pdl_wait();
   using S = DecodeSmem<D, kFp8>;
   constexpr int ROWB = D * 2;
   constexpr int kEl = kFp8 ? 1 : 2;
@@ -125,26 +124,6 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   }
   const float scale_log2 = P.sm_scale * 1.4426950408889634f * k_scale;
 
-  // Q fragments: rows = heads of the group (rows >= G and rows 8..15 are zero)
-  uint32_t qa[D / 16][2];
-  {
-    const __nv_bfloat16* qrow = P.q + (size_t)b * P.ld_q + (size_t)(kvh * G + g) * D;
-#pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      if (g < G) {
-        qa[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * c);
-        qa[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * c);
-      } else {
-        qa[kk][0] = qa[kk][1] = 0u;
-      }
-    }
-  }
-
-  float o[D / 8][4];
-#pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
-
   uint8_t* wbase = smem + warp * S::kWarpB;
   const int* bt = P.block_tables + (size_t)b * P.bt_stride;
   const size_t head_stride = (size_t)kPage * D * kEl;                       // one (k|v, head) chunk
@@ -166,9 +145,40 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
     }
   };
 
+  // Block tables and context lengths come from the step's input copy, which completes
+  // before the first kernel of the launch chain starts; KV pages before the one holding
+  // this step's token were written by earlier steps.  So the warp's first page is
+  // requested before waiting for the previous kernel (RoPE + KV write), unless it is
+  // the page that kernel is writing.
   const int my_first = p_begin + warp;
-  if (my_first < p_end) issue(my_first, 0);
+  const int live_page = (ctx - 1) / kPage;
+  const bool early = my_first < p_end && my_first < live_page;
+  if (early) issue(my_first, 0);
   cp_async_commit();
+  pdl_wait();
+  if (!early && my_first < p_end) issue(my_first, 0);
+  cp_async_commit();
+
+  // Q fragments: rows = heads of the group (rows >= G and rows 8..15 are zero)
+  uint32_t qa[D / 16][2];
+  {
+    const __nv_bfloat16* qrow = P.q + (size_t)b * P.ld_q + (size_t)(kvh * G + g) * D;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      if (g < G) {
+        qa[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * c);
+        qa[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * c);
+      } else {
+        qa[kk][0] = qa[kk][1] = 0u;
+      }
+    }
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;
+
   int it = 0;
   for (int p = my_first; p < p_end; p += 4, ++it) {
     const int stage = it & 1;

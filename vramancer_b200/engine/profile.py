@@ -6,7 +6,12 @@ Builds the model with random weights, prefills `batch` prompts, then runs `steps
 eager decode steps (no CUDA graph, so every kernel is a separate launch) inside the
 NVTX range "vrm_decode"; capture them with
     ncu --nvtx --nvtx-include "vrm_decode/" --metrics gpu__time_duration.sum ...
-With --events it instead prints a per-op CUDA-event breakdown of one step.
+With --ablate it prints, per op type, how much of the graph-replayed decode step that
+op costs on the critical path: the step is re-captured with the op replaced by a no-op
+(its output buffer still allocated) and the CUDA-event step times are compared.  Unlike
+a serialised ncu launch list this includes the overlap that programmatic dependent
+launch gives between neighbouring kernels.  Ablated steps compute garbage; only their
+timing is used.
 """
 from __future__ import annotations
 
@@ -14,6 +19,57 @@ import argparse
 import json
 
 import torch
+
+
+def _step_ms(runner, B: int, reps: int = 20) -> float:
+    g = runner.capture(B)
+    g.replay()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        best = min(best, a.elapsed_time(b) / reps)
+    runner._graphs.pop(B, None)
+    del g
+    return best
+
+
+def ablate(llm, B: int) -> dict:
+    """Step time with each op type removed (see module docstring)."""
+    from .. import ops
+    runner = llm.runner
+    base = _step_ms(runner, B)
+
+    def attn_stub(qkv, cache, layer, block_tables, context_lens, kv_scale, sm_scale, num_q_heads, **kw):
+        D = llm.cfg.head_dim
+        return torch.empty(qkv.shape[0], num_q_heads * D, dtype=qkv.dtype, device=qkv.device)
+
+    def norm_stub(x, w, *args, residual=None, out=None, **kw):
+        return x if out is None else out
+
+    stubs = {
+        "attention": {"paged_attention_decode": attn_stub},
+        "rope_kv_write": {"rope_kv_write": lambda *a, **k: None},
+        "norms": {"rmsnorm": norm_stub, "layernorm": norm_stub},
+        "sampler": {"sample": lambda logits, *a, out=None, **k: out},
+    }
+    res = {"batch": B, "step_ms": round(base, 4)}
+    for name, patch in stubs.items():
+        saved = {k: getattr(ops, k) for k in patch}
+        try:
+            for k, fn in patch.items():
+                setattr(ops, k, fn)
+            t = _step_ms(runner, B)
+        finally:
+            for k, fn in saved.items():
+                setattr(ops, k, fn)
+        res[name + "_ms"] = round(base - t, 4)
+    return res
 
 
 def main(argv=None):
@@ -25,7 +81,10 @@ def main(argv=None):
     ap.add_argument("--num-layers", type=int, default=None)
     ap.add_argument("--kv-dtype", default="bf16")
     ap.add_argument("--graph", action="store_true", help="replay the captured graph instead of eager steps")
+    ap.add_argument("--ablate", action="store_true", help="critical-path cost of each op type (graph replay)")
     args = ap.parse_args(argv)
+    if args.ablate:
+        args.graph = True
 
     from ..engine.engine import SamplingParams
     from ..llm import LLM
@@ -41,6 +100,9 @@ def main(argv=None):
         llm.engine.step()
     llm.engine.step()              # warm decode (captures the graph when --graph)
     torch.cuda.synchronize()
+    if args.ablate:
+        print(json.dumps(ablate(llm, llm.runner.bucket_for(B))))
+        return
     torch.cuda.nvtx.range_push("vrm_decode")
     for _ in range(args.steps):
         llm.engine.step()
