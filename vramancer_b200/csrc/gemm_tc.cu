@@ -23,6 +23,7 @@
 // path (core/backends.py:1390) and its SIMT NVFP4 GEMV (csrc/fp4_gemv.cu:36-116) for
 // the bf16 case.
 #include <algorithm>
+#include <cmath>
 #include <cstdlib>
 #include <mutex>
 #include <unordered_map>
@@ -176,7 +177,7 @@ template <int BN, int STAGES, bool kSwapAB>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters, int K,
-                        int num_a_tiles, int k_tiles_per_split, uint32_t* __restrict__ err) {
+                        int num_a_tiles, int full_tiles, int tail_splits, uint32_t* __restrict__ err) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -191,13 +192,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  const int a_tile = blockIdx.x % num_a_tiles;
-  const int b_tile = blockIdx.x / num_a_tiles;
-  const int split = blockIdx.y;
-  const int num_splits = gridDim.y;
+  // CTAs [0, full_tiles) compute whole tiles; every later tile is cut into tail_splits
+  // K ranges (one CTA each) whose fp32 partials the tile's last CTA sums.  Whole-tile
+  // rounds fill the SMs, the split tail fills the last partial round.
+  int tile, split, num_splits;
+  if ((int)blockIdx.x < full_tiles) {
+    tile = blockIdx.x;
+    split = 0;
+    num_splits = 1;
+  } else {
+    const int j = blockIdx.x - full_tiles;
+    tile = full_tiles + j / tail_splits;
+    split = j % tail_splits;
+    num_splits = tail_splits;
+  }
+  const int a_tile = tile % num_a_tiles;
+  const int b_tile = tile / num_a_tiles;
   const int total_k_tiles = (K + kBK - 1) / kBK;
-  const int kt_begin = split * k_tiles_per_split;
-  const int kt_end = min(total_k_tiles, kt_begin + k_tiles_per_split);
+  const int k_per_split = (total_k_tiles + num_splits - 1) / num_splits;
+  const int kt_begin = split * k_per_split;
+  const int kt_end = min(total_k_tiles, kt_begin + k_per_split);
   const int num_k = max(0, kt_end - kt_begin);
 
   constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
@@ -276,8 +290,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int c_base = b_tile * BN;
     const uint32_t t_row = tmem_base + ((uint32_t)lane_base << 16);
     const bool direct = (num_splits == 1);
-    const size_t tile_id = blockIdx.x;
-    float* ws_tile = workspace + ((size_t)split * gridDim.x + tile_id) * (size_t)(kBM * BN);
+    // partial slots of split tiles: [tile - full_tiles][split][row][BN] fp32, each thread's
+    // row contiguous, so the reducing CTA reads 16-byte vectors
+    const size_t tail_tile = (size_t)(tile - full_tiles);
+    auto slot = [&](int sp) {
+      return workspace + ((tail_tile * num_splits + sp) * kBM + row) * (size_t)BN;
+    };
 
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -290,8 +308,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (direct) {
         epi_store<kSwapAB>(ep, r_glob, c_base + c0, v);
       } else {
+        float4* dst = reinterpret_cast<float4*>(slot(split) + c0);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) ws_tile[(size_t)(c0 + j) * kBM + row] = v[j];   // coalesced
+        for (int q = 0; q < 4; ++q) __stcg(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
       }
     }
 
@@ -299,7 +318,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __threadfence();
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (threadIdx.x == 64) {
-        const uint32_t prev = atomicAdd(&tile_counters[tile_id], 1u);
+        const uint32_t prev = atomicAdd(&tile_counters[tile], 1u);
         *flag_slot = (prev == (uint32_t)(num_splits - 1)) ? 1u : 0u;
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -310,14 +329,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float v[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
-          for (int s = 0; s < num_splits; ++s) {
-            const float* src = workspace + ((size_t)s * gridDim.x + tile_id) * (size_t)(kBM * BN);
+          // four splits' 64-byte row segments in flight at once, summed in split order
+          for (int s0 = 0; s0 < num_splits; s0 += 4) {
+            float4 x[4][4];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (size_t)(c0 + j) * kBM + row);
+            for (int u = 0; u < 4; ++u) {
+              const float4* src = reinterpret_cast<const float4*>(slot(s0 + u) + c0);
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                x[u][q] = s0 + u < num_splits ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                v[4 * q] += x[u][q].x;
+                v[4 * q + 1] += x[u][q].y;
+                v[4 * q + 2] += x[u][q].z;
+                v[4 * q + 3] += x[u][q].w;
+              }
           }
           epi_store<kSwapAB>(ep, r_glob, c_base + c0, v);
         }
-        if (threadIdx.x == 64) tile_counters[tile_id] = 0u;   // ready for the next launch
+        if (threadIdx.x == 64) tile_counters[tile] = 0u;   // ready for the next launch
       }
     }
   }
@@ -344,6 +378,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 struct StreamK {
   int64_t iters;   // tiles * k_tiles
   int ctas;
+  int tiles_x;     // token blocks of BN tokens; tile t = (weight block t / tiles_x, token block t % tiles_x)
   __device__ __forceinline__ int64_t start(int c) const { return (int64_t)c * iters / ctas; }
   __device__ __forceinline__ int owner(int64_t i) const {
     int c = (int)(((i + 1) * ctas - 1) / iters);
@@ -364,7 +399,7 @@ template <int BN, int STAGES, bool kAR>
 __global__ void __launch_bounds__(kGemmThreads, 2)
     gemm_streamk_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                              EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters,
-                             int k_tiles, int max_contrib, StreamK sk, uint32_t* __restrict__ err,
+                             int k_tiles, StreamK sk, uint32_t* __restrict__ err,
                              unsigned long long* __restrict__ trace, ARParams ar) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -414,45 +449,67 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 
   if (warp == 0 && lane == 0) {
     // ---------------- producer
-    const uint64_t pol_w = policy_evict_first();
+    // decode reads every weight tile once (evict first); with several token blocks the
+    // next blocks re-read it from L2 (evict normal)
+    const uint64_t pol_w = sk.tiles_x > 1 ? policy_evict_normal() : policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
-    const int64_t total = it_end - it_begin;
-    const int pre = (int)(total < STAGES ? total : STAGES);
+    const int total = (int)(it_end - it_begin);
+    const int pre = total < STAGES ? total : STAGES;
+    // (k, weight block, token block) of the next load, advanced without divisions: the
+    // producer is one thread whose per-iteration latency is on the critical path
+    const int t0 = (int)(it_begin / k_tiles), k0 = (int)(it_begin - (int64_t)t0 * k_tiles);
+    const int tw0 = t0 / sk.tiles_x, tb0 = t0 - tw0 * sk.tiles_x;
+    int k = k0, tw = tw0, tb = tb0;
+    auto advance = [&](int& kk, int& w, int& b) {
+      if (++kk == k_tiles) {
+        kk = 0;
+        if (++b == sk.tiles_x) {
+          b = 0;
+          ++w;
+        }
+      }
+    };
     // weights do not depend on the previous kernel: start streaming them first
     for (int g = 0; g < pre; ++g) {
-      const int64_t it = it_begin + g;
-      const int t = (int)(it / k_tiles), k = (int)(it % k_tiles);
       uint8_t* sa = smem + g * L::kStageBytes;
       mbar_arrive_expect_tx(&full_bar[g], L::kStageBytes);
-      tma_load_2d(sa, &map_w, &full_bar[g], k * kBK, t * kBM, pol_w);
+      tma_load_2d(sa, &map_w, &full_bar[g], k * kBK, tw * kBM, pol_w);
+      advance(k, tw, tb);
     }
     pdl_wait();
     if (tr) tr[2] = globaltimer();
-    for (int g = 0; g < pre; ++g) {
-      const int64_t it = it_begin + g;
-      const int k = (int)(it % k_tiles);
-      uint8_t* sb = smem + g * L::kStageBytes + L::kABytes;
-      tma_load_2d(sb, &map_x, &full_bar[g], k * kBK, 0, pol_x);
+    {
+      int kx = k0, wx = tw0, bx = tb0;
+      for (int g = 0; g < pre; ++g) {
+        uint8_t* sb = smem + g * L::kStageBytes + L::kABytes;
+        tma_load_2d(sb, &map_x, &full_bar[g], kx * kBK, bx * BN, pol_x);
+        advance(kx, wx, bx);
+      }
     }
-    int64_t issued = pre;
-    for (int64_t g = pre; g < total; ++g) {
-      const int s = (int)(g % STAGES);
-      const uint32_t ph = (uint32_t)((g / STAGES) & 1);
+    int issued = pre;
+    int s = pre % STAGES;
+    uint32_t ph = pre == STAGES ? 1u : 0u;   // phase of stage s's next use
+    for (int g = pre; g < total; ++g) {
       if (!mbar_wait(&empty_bar[s], ph ^ 1, err)) break;
-      const int64_t it = it_begin + g;
-      const int t = (int)(it / k_tiles), k = (int)(it % k_tiles);
       uint8_t* sa = smem + s * L::kStageBytes;
       mbar_arrive_expect_tx(&full_bar[s], L::kStageBytes);
-      tma_load_2d(sa, &map_w, &full_bar[s], k * kBK, t * kBM, pol_w);
-      tma_load_2d(sa + L::kABytes, &map_x, &full_bar[s], k * kBK, 0, pol_x);
+      tma_load_2d(sa, &map_w, &full_bar[s], k * kBK, tw * kBM, pol_w);
+      tma_load_2d(sa + L::kABytes, &map_x, &full_bar[s], k * kBK, tb * BN, pol_x);
+      advance(k, tw, tb);
       issued = g + 1;
+      if (++s == STAGES) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
-    const int64_t first = issued > STAGES ? issued - STAGES : 0;
-    for (int64_t j = first; j < issued; ++j) mbar_wait(&full_bar[j % STAGES], (uint32_t)((j / STAGES) & 1), err);
+    const int first = issued > STAGES ? issued - STAGES : 0;
+    for (int j = first; j < issued; ++j) mbar_wait(&full_bar[j % STAGES], (uint32_t)((j / STAGES) & 1), err);
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
     constexpr uint32_t idesc = make_idesc_bf16(kBM, BN);
     int64_t g = 0;
+    int ms = 0;              // stage of the next full barrier, and its phase
+    uint32_t mphase = 0u;
     int seg = 0;
     bool failed = false;
     for (int64_t it = it_begin; it < it_end && !failed; ++seg) {
@@ -463,8 +520,13 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       tc_fence_after();
       const uint32_t d = tmem_base + (uint32_t)(acc * BN);
       for (int64_t j = 0; j < n; ++j, ++g) {
-        const int s = (int)(g % STAGES);
-        if (!mbar_wait(&full_bar[s], (uint32_t)((g / STAGES) & 1), err)) {
+        const int s = ms;
+        const uint32_t mph = mphase;
+        if (++ms == STAGES) {
+          ms = 0;
+          mphase ^= 1u;
+        }
+        if (!mbar_wait(&full_bar[s], mph, err)) {
           failed = true;
           break;
         }
@@ -506,14 +568,17 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       const int acc = seg & 1;
       const bool ok = mbar_wait(&tfull[acc], (uint32_t)((seg >> 1) & 1), err);
       tc_fence_after();
-      const int r_glob = t * kBM + row;   // weight row == output feature
+      const int tw = t / sk.tiles_x, tb = t - tw * sk.tiles_x;
+      const int r_glob = tw * kBM + row;   // weight row == output feature
+      const int tok0 = tb * BN;            // first token of the tile
       int first_owner = c, nc = 1;
       if (!whole) {
         first_owner = sk.owner((int64_t)t * k_tiles);
         nc = sk.owner((int64_t)t * k_tiles + k_tiles - 1) - first_owner + 1;
       }
       const bool is_owner = whole || (c == first_owner);
-      const float* base = workspace + (size_t)t * max_contrib * (size_t)(kBM * BN) + row;
+      // one partial slot per CTA: only a CTA's first segment can be a non-owner partial
+      const float* base = workspace + (size_t)first_owner * (size_t)(kBM * BN) + row;
       // this rank's slot in the current half; element (token m, feature n) at m * N + n
       const size_t xoff = kAR ? (((size_t)(epoch & 1u) * ar.world + ar.rank) * ar.half_floats + (size_t)r_glob) : 0;
       if (is_owner && !whole) {
@@ -538,7 +603,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = ok ? __uint_as_float(r[j]) : 0.f;
         if (!is_owner) {
-          float* slot = workspace + ((size_t)t * max_contrib + (c - first_owner)) * (size_t)(kBM * BN);
+          float* slot = workspace + (size_t)c * (size_t)(kBM * BN);
 #pragma unroll
           for (int j = 0; j < 16; ++j) __stcg(slot + (size_t)(c0 + j) * kBM + row, v[j]);
           continue;
@@ -566,11 +631,11 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
               float* dst = ar.xbuf[p] + xoff;
 #pragma unroll
               for (int j = 0; j < 16; ++j)
-                if (c0 + j < ep.M) __stcg(dst + (size_t)(c0 + j) * ep.N, v[j]);
+                if (tok0 + c0 + j < ep.M) __stcg(dst + (size_t)(tok0 + c0 + j) * ep.N, v[j]);
             }
           }
         } else {
-          epi_store<true>(ep, r_glob, c0, v);
+          epi_store<true>(ep, r_glob, tok0 + c0, v);
         }
       }
       tc_fence_before();
@@ -669,7 +734,7 @@ CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t cols, int64_t
 
 template <int BN, int STAGES, bool kSwap>
 static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const EpiParams& ep, int K, int a_tiles,
-                        int b_tiles, int splits, int ktps, cudaStream_t stream) {
+                        int b_tiles, int full_tiles, int tail_splits, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
   auto kern = gemm_bf16_tc_kernel<BN, STAGES, kSwap>;
   static int attr_dev_mask = 0;   // per-device "attribute set" bits (devices < 32)
@@ -679,17 +744,44 @@ static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const EpiP
     VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
     attr_dev_mask |= 1 << (dev & 31);
   }
+  const int tiles = a_tiles * b_tiles;
+  if (tail_splits <= 1) full_tiles = tiles;
   float* ws = nullptr;
   uint32_t* counters = nullptr;
-  if (splits > 1) {
-    const size_t need = (size_t)splits * a_tiles * b_tiles * kBM * BN * sizeof(float);
+  if (full_tiles < tiles) {
+    const size_t need = (size_t)(tiles - full_tiles) * tail_splits * kBM * BN * sizeof(float);
     ws = static_cast<float*>(workspace_get(need, stream));
-    VRM_REQUIRE((size_t)a_tiles * b_tiles <= 32768, "too many split-K tiles");
+    VRM_REQUIRE((size_t)tiles <= 32768, "too many split-K tiles");
     counters = tile_counters_get(stream);
   }
-  dim3 grid(a_tiles * b_tiles, splits);
-  launch_kernel(kern, grid, dim3(kGemmThreads), (size_t)L::kAlloc, stream, ma, mb, ep, ws, counters, K, a_tiles, ktps,
-                error_word());
+  dim3 grid(full_tiles + (tiles - full_tiles) * std::max(1, tail_splits));
+  launch_kernel(kern, grid, dim3(kGemmThreads), (size_t)L::kAlloc, stream, ma, mb, ep, ws, counters, K, a_tiles,
+                full_tiles, tail_splits, error_word());
+}
+
+// Whole tiles for the complete rounds over the SMs, the remaining tiles split K-wise so
+// the last round is filled: minimises rounds + (split cost) over the split count.
+static void choose_tail_split(int tiles, int k_tiles, int min_k, int* full_tiles, int* tail_splits) {
+  const int sms = device_sm_count();
+  *full_tiles = tiles;
+  *tail_splits = 1;
+  const int rounds = tiles / sms, rem = tiles % sms;
+  if (rem == 0) return;
+  // cost in tile units.  A split tail tile also pays for writing and reducing its
+  // partials; measured on B200 at about 12.8 / k_tiles tile per split (0.16 at K = 5120,
+  // 0.06 at K = 13824), so only long-K tiles gain from splitting.
+  double best = rounds + 1.0;
+  const int full = rounds * sms;
+  const double per_split = 12.8 / k_tiles;
+  for (int sp = 2; sp <= 16 && k_tiles / sp >= min_k; ++sp) {
+    const int pieces = rem * sp;
+    const double cost = rounds + std::ceil((double)pieces / sms) / sp + per_split * sp;
+    if (cost < best - 1e-9) {
+      best = cost;
+      *full_tiles = full;
+      *tail_splits = sp;
+    }
+  }
 }
 
 // debug timeline buffer for the stream-K kernel (set by gemm_set_trace, null = off)
@@ -698,7 +790,7 @@ void gemm_set_trace(void* buf) { g_gemm_trace = static_cast<unsigned long long*>
 
 template <int BN, int STAGES, bool kAR>
 static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const EpiParams& ep, int N, int K,
-                           int max_ctas, cudaStream_t stream, const ARParams& ar) {
+                           int max_ctas, cudaStream_t stream, const ARParams& ar, int tiles_x = 1) {
   // smem: stages + 2*STAGES+4 barriers + slots
   constexpr int kSmem = STAGES * GemmSmem<BN, STAGES>::kStageBytes + (2 * STAGES + 5) * 8 + 16 + 1024;
   auto kern = gemm_streamk_swap_kernel<BN, STAGES, kAR>;
@@ -709,25 +801,18 @@ static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const E
     VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     attr_dev_mask |= 1 << (dev & 31);
   }
-  const int tiles = (N + kBM - 1) / kBM;
+  const int tiles = ((N + kBM - 1) / kBM) * tiles_x;
   const int k_tiles = (K + kBK - 1) / kBK;
   StreamK sk;
+  sk.tiles_x = tiles_x;
   sk.iters = (int64_t)tiles * k_tiles;
   sk.ctas = (int)std::min<int64_t>(max_ctas, sk.iters);
-  const int64_t per = sk.iters / sk.ctas;   // >= 1
-  const int max_contrib = (int)std::min<int64_t>(sk.ctas, k_tiles / std::max<int64_t>(per, 1) + 2);
-  float* ws = nullptr;
   uint32_t* counters = tile_counters_get(stream);
   VRM_REQUIRE(tiles <= 32768, "stream-K: too many tiles");
-  if (sk.ctas > tiles) {   // some tiles are shared between CTAs
-    const size_t need = (size_t)tiles * max_contrib * kBM * BN * sizeof(float);
-    ws = static_cast<float*>(workspace_get(need, stream));
-  } else {
-    ws = static_cast<float*>(workspace_get((size_t)tiles * max_contrib * kBM * BN * sizeof(float), stream));
-  }
+  float* ws = static_cast<float*>(workspace_get((size_t)sk.ctas * kBM * BN * sizeof(float), stream));
   if (kAR) VRM_REQUIRE((long long)ep.M * N <= ar.half_floats, "fused all-reduce: output larger than the symmetric buffer");
   launch_kernel(kern, dim3(sk.ctas), dim3(kGemmThreads), (size_t)kSmem, stream, mw, mx, ep, ws, counters, k_tiles,
-                max_contrib, sk, error_word(), g_gemm_trace, ar);
+                sk, error_word(), g_gemm_trace, ar);
 }
 
 // Split count such that tiles * splits covers the SMs with >= min_k K-tiles per split.
@@ -742,6 +827,17 @@ static void choose_split(int tiles, int k_tiles, int min_k, int* splits, int* kt
   s = (k_tiles + per - 1) / per;
   *splits = s;
   *ktps = per;
+}
+
+// VRM_GEMM_PREFILL=streamk runs M > 128 on the stream-K swap kernel (default: the tiled
+// kernel, whose concurrent CTAs share each weight tile in L2; stream-K walks a weight
+// tile's token blocks one after another and re-reads it from HBM once it is evicted)
+static bool prefill_streamk() {
+  static const bool v = [] {
+    const char* e = std::getenv("VRM_GEMM_PREFILL");
+    return e && std::string(e) == "streamk";
+  }();
+  return v;
 }
 
 static bool legacy_decode() {
@@ -810,23 +906,40 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     int splits, ktps;
     choose_split(a_tiles, k_tiles, 4, &splits, &ktps);
     if (a.force_splits > 0) force_split(a.force_splits, k_tiles, &splits, &ktps);
-    switch (BN) {
-      case 16: launch_gemm<16, 8, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
-      case 32: launch_gemm<32, 8, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
-      case 64: launch_gemm<64, 6, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
-      default: launch_gemm<128, 5, true>(ma, mb, ep, a.K, a_tiles, 1, splits, ktps, stream); break;
+    switch (BN) {   // every tile split `splits` ways (full_tiles = 0)
+      case 16: launch_gemm<16, 8, true>(ma, mb, ep, a.K, a_tiles, 1, 0, splits, stream); break;
+      case 32: launch_gemm<32, 8, true>(ma, mb, ep, a.K, a_tiles, 1, 0, splits, stream); break;
+      case 64: launch_gemm<64, 6, true>(ma, mb, ep, a.K, a_tiles, 1, 0, splits, stream); break;
+      default: launch_gemm<128, 5, true>(ma, mb, ep, a.K, a_tiles, 1, 0, splits, stream); break;
     }
+  } else if (prefill_streamk() && a.M <= 4096 && a.force_splits <= 0) {
+    // prefill: the same swap-AB stream-K kernel over ceil(M / 128) token blocks per
+    // weight block (every SM gets the same number of k-iterations: no partial last
+    // wave), six stages of 32 KB, one CTA per SM
+    VRM_REQUIRE(!a.allreduce, "fused all-reduce needs M <= 128 (decode); use the collective for prefill");
+    const CUtensorMap ma = make_kmajor_map(a.w, a.N, a.K, a.ldw, kBM);
+    const CUtensorMap mb = make_kmajor_map(a.x, a.M, a.K, a.ldx, 128);
+    launch_streamk<128, 6, false>(ma, mb, ep, a.N, a.K, device_sm_count(), stream, ARParams{}, (a.M + 127) / 128);
   } else {
     VRM_REQUIRE(!a.allreduce, "fused all-reduce needs M <= 128 (decode); use the collective for prefill");
     constexpr int BN = 128;
     const int a_tiles = (a.M + kBM - 1) / kBM;
     const int b_tiles = (a.N + BN - 1) / BN;
-    int splits = 1, ktps = k_tiles;
-    if (a_tiles * b_tiles * 2 <= device_sm_count()) choose_split(a_tiles * b_tiles, k_tiles, 8, &splits, &ktps);
-    if (a.force_splits > 0) force_split(a.force_splits, k_tiles, &splits, &ktps);
+    int full = a_tiles * b_tiles, tail_splits = 1;
+    if (a.force_splits > 0) {
+      int ktps;
+      force_split(a.force_splits, k_tiles, &tail_splits, &ktps);
+      full = 0;
+    } else if (a_tiles * b_tiles * 2 <= device_sm_count()) {
+      int ktps;
+      choose_split(a_tiles * b_tiles, k_tiles, 8, &tail_splits, &ktps);
+      full = 0;
+    } else {
+      choose_tail_split(a_tiles * b_tiles, k_tiles, 8, &full, &tail_splits);
+    }
     const CUtensorMap ma = make_kmajor_map(a.x, a.M, a.K, a.ldx, kBM);
     const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, BN);
-    launch_gemm<BN, 6, false>(ma, mb, ep, a.K, a_tiles, b_tiles, splits, ktps, stream);
+    launch_gemm<BN, 6, false>(ma, mb, ep, a.K, a_tiles, b_tiles, full, tail_splits, stream);
   }
 }
 
