@@ -7,8 +7,8 @@ produces vramancer_b200/_C*.so (CUDA kernels) and vramancer_b200/_runtime*.so
 """
 import os
 
-from setuptools import setup
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension, CppExtension
+from setuptools import Extension, setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("vramancer_b200", "csrc")
@@ -44,11 +44,16 @@ ext_modules = [
     ),
 ]
 if runtime_sources:
+    # host runtime: plain C++17 + pybind11, no torch or CUDA headers (compiles in seconds)
+    import pybind11
     ext_modules.append(
-        CppExtension(
+        Extension(
             name="vramancer_b200._runtime",
             sources=runtime_sources,
-            extra_compile_args={"cxx": ["-O3", "-std=c++17", "-pthread"]},
+            include_dirs=[pybind11.get_include(), RT],
+            language="c++",
+            extra_compile_args=["-O3", "-std=c++17", "-pthread", "-fvisibility=hidden"],
+            extra_link_args=["-pthread"],
         )
     )
 
