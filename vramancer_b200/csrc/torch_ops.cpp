@@ -479,6 +479,36 @@ void nvfp4_gemm_out(const Tensor& x, const Tensor& q, const Tensor& sc, const Te
   vrm::nvfp4_gemm(a, cur_stream());
 }
 
+// ---------------------------------------------------------------- TurboQuant KV records
+Tensor tq_compress(const Tensor& x, const Tensor& signs, const Tensor& jl) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && x.size(-1) == 128, "tq_compress: contiguous CUDA [..., 128]");
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 || x.scalar_type() == torch::kFloat32, "tq_compress: bf16 or fp32");
+  TORCH_CHECK(signs.scalar_type() == torch::kFloat32 && signs.numel() == 128 && signs.is_contiguous(), "tq_compress: signs");
+  TORCH_CHECK(jl.scalar_type() == torch::kFloat32 && jl.numel() == 64 * 128 && jl.is_contiguous(), "tq_compress: jl [64, 128]");
+  same_device(x, {&signs, &jl}, "tq_compress");
+  auto sizes = x.sizes().vec();
+  sizes.back() = 64;
+  auto out = torch::empty(sizes, x.options().dtype(torch::kUInt8));
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::tq_compress(x.data_ptr(), x.scalar_type() == torch::kBFloat16, x.numel() / 128, signs.data_ptr<float>(),
+                   jl.data_ptr<float>(), out.data_ptr<uint8_t>(), cur_stream());
+  return out;
+}
+
+Tensor tq_decompress(const Tensor& rec, const Tensor& signs) {
+  TORCH_CHECK(rec.is_cuda() && rec.is_contiguous() && rec.scalar_type() == torch::kUInt8 && rec.size(-1) == 64,
+              "tq_decompress: contiguous CUDA uint8 [..., 64]");
+  TORCH_CHECK(signs.scalar_type() == torch::kFloat32 && signs.numel() == 128, "tq_decompress: signs");
+  same_device(rec, {&signs}, "tq_decompress");
+  auto sizes = rec.sizes().vec();
+  sizes.back() = 128;
+  auto out = torch::empty(sizes, rec.options().dtype(torch::kBFloat16));
+  const c10::cuda::CUDAGuard guard(rec.device());
+  vrm::tq_decompress(rec.data_ptr<uint8_t>(), rec.numel() / 64, signs.data_ptr<float>(), out.data_ptr(),
+                     cur_stream());
+  return out;
+}
+
 // ---------------------------------------------------------------- page migration
 void page_copy(const Tensor& src_pool, Tensor& dst_pool, const Tensor& src_idx, const Tensor& dst_idx) {
   TORCH_CHECK(src_pool.is_cuda() && dst_pool.is_cuda() && src_pool.is_contiguous() && dst_pool.is_contiguous(),
@@ -542,6 +572,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bias"), py::arg("out"), py::arg("epilogue"), py::arg("residual"),
         "W4A16 decode GEMM (M <= 32) over NVFP4 weights");
   m.def("nvfp4_gemm_max_m", &vrm::nvfp4_gemm_max_m);
+  m.def("tq_compress", &tq_compress, py::arg("x"), py::arg("signs"), py::arg("jl"),
+        "TurboQuant: [..., 128] -> 64-byte records (Hadamard + PolarQuant + QJL)");
+  m.def("tq_decompress", &tq_decompress, py::arg("rec"), py::arg("signs"),
+        "TurboQuant: 64-byte records -> bf16 [..., 128]");
   m.def("gemm_ar_push", &gemm_ar_push, py::arg("x"), py::arg("w"), py::arg("xbuf_ptrs"), py::arg("flag_ptrs"),
         py::arg("epoch"), py::arg("done"), py::arg("rank"), py::arg("world"), py::arg("half_floats"),
         py::arg("per_thread_fence") = false,

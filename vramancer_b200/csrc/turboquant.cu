@@ -1,0 +1,249 @@
+// TurboQuant KV records (64 bytes per 128-dim vector): randomized Hadamard rotation,
+// PolarQuant angles (3 bits), 1-bit QJL sketch of the residual.  Record layout and
+// math: vramancer_b200/kv/turboquant.py (the torch oracle of these kernels).
+//
+// One warp per vector; lane l holds elements 4l..4l+3.  The Walsh-Hadamard butterflies
+// run in registers for h = 1, 2 and across lanes with shfl_xor for h = 4..64, in the
+// oracle's stage order (identical fp32 results).  The polar tree pairs elements in
+// registers for levels 0-1 and lanes for levels 2-6; the 64 JL projections of the
+// residual are two per lane over the CTA's shared copy of P, and their signs come out
+// of two ballots already bit-packed.
+//
+// Reference parity: csrc/turboquant_kernel.cu:36-405 (Hadamard + polar encode/decode +
+// QJL in fused compress / decompress kernels).
+#include <cuda_fp16.h>
+
+#include "vrm_common.cuh"
+#include "vrm_host.h"
+#include "vrm_kernels.h"
+
+namespace vrm {
+namespace {
+
+constexpr int kTqD = 128, kTqM = 64, kTqBits = 3, kTqRec = 64;
+constexpr int kTqWarps = 8;
+constexpr float kPi = 3.14159265358979323846f;
+
+// angle-slot base of each polar level (64 + 32 + ... + 1 = 127 slots)
+__device__ __forceinline__ int level_base(int k) { return kTqD - (kTqD >> k); }
+
+__device__ __forceinline__ void fwht4(float (&v)[4], int lane) {
+  // h = 1, 2 inside the lane
+  float a = v[0], b = v[1], c = v[2], d = v[3];
+  v[0] = a + b; v[1] = a - b; v[2] = c + d; v[3] = c - d;
+  a = v[0]; b = v[1]; c = v[2]; d = v[3];
+  v[0] = a + c; v[1] = b + d; v[2] = a - c; v[3] = b - d;
+  // h = 4 .. 64: partner lane differs in bit (h / 4)
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const bool upper = lane & m;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float p = __shfl_xor_sync(0xffffffffu, v[j], m);
+      v[j] = upper ? p - v[j] : v[j] + p;
+    }
+  }
+  // divide (not multiply by the reciprocal): bit-identical to the oracle's x / sqrt(128)
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = v[j] / 11.313708498984761f;
+}
+
+__device__ __forceinline__ int quant_angle(float ang, int level) {
+  const float lo = level == 0 ? -kPi : 0.f;
+  const float span = level == 0 ? 2.f * kPi : 0.5f * kPi;
+  const float q = floorf((ang - lo) / span * (float)(1 << kTqBits));
+  return (int)fminf(fmaxf(q, 0.f), (float)((1 << kTqBits) - 1));
+}
+
+__device__ __forceinline__ float angle_centre(int q, int level) {
+  const float lo = level == 0 ? -kPi : 0.f;
+  const float span = level == 0 ? 2.f * kPi : 0.5f * kPi;
+  return lo + ((float)q + 0.5f) * span / (float)(1 << kTqBits);
+}
+
+// polar decode of the rotated vector from angle slots (shared) and the radius
+__device__ __forceinline__ void polar_decode(const uint8_t* idx, float radius, int lane, float (&v)[4]) {
+  float R = radius;
+  // levels 6 .. 2: lanes paired across bit (k - 2)
+#pragma unroll
+  for (int k = 6; k >= 2; --k) {
+    const int span = 1 << (k - 1);                 // lanes under one angle
+    const float th = angle_centre(idx[level_base(k) + lane / span], k);
+    R = (lane & (1 << (k - 2))) ? R * sinf(th) : R * cosf(th);
+  }
+  const float t1 = angle_centre(idx[level_base(1) + lane], 1);
+  const float r0 = R * cosf(t1), r1 = R * sinf(t1);
+  const float a0 = angle_centre(idx[2 * lane], 0), a1 = angle_centre(idx[2 * lane + 1], 0);
+  v[0] = r0 * cosf(a0);
+  v[1] = r0 * sinf(a0);
+  v[2] = r1 * cosf(a1);
+  v[3] = r1 * sinf(a1);
+}
+
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, float (&v)[4]);
+template <>
+__device__ __forceinline__ void load4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y);
+}
+template <>
+__device__ __forceinline__ void load4<float>(const float* p, float (&v)[4]) {
+  const float4 u = *reinterpret_cast<const float4*>(p);
+  v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTqWarps * 32) tq_compress_kernel(const T* __restrict__ x, int64_t n,
+                                                                    const float* __restrict__ signs,
+                                                                    const float* __restrict__ jl,
+                                                                    uint8_t* __restrict__ out) {
+  __shared__ float s_jl[kTqM][kTqD];
+  __shared__ float s_sign[kTqD];
+  __shared__ float s_r[kTqWarps][kTqD];
+  __shared__ uint8_t s_idx[kTqWarps][kTqD];
+  __shared__ __align__(16) uint8_t s_rec[kTqWarps][kTqRec];
+  pdl_launch();
+  for (int i = threadIdx.x; i < kTqM * kTqD; i += blockDim.x) s_jl[i / kTqD][i % kTqD] = jl[i];
+  for (int i = threadIdx.x; i < kTqD; i += blockDim.x) s_sign[i] = signs[i];
+  pdl_wait();
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* idx = s_idx[warp];
+  uint8_t* rec = s_rec[warp];
+  for (int64_t vec = (int64_t)blockIdx.x * kTqWarps + warp; vec < n; vec += (int64_t)gridDim.x * kTqWarps) {
+    float v[4];
+    load4<T>(x + vec * kTqD + 4 * lane, v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] *= s_sign[4 * lane + j];
+    fwht4(v, lane);
+    // ---- polar encode
+    const float ra = sqrtf(v[0] * v[0] + v[1] * v[1]), rb = sqrtf(v[2] * v[2] + v[3] * v[3]);
+    idx[2 * lane] = (uint8_t)quant_angle(atan2f(v[1], v[0]), 0);
+    idx[2 * lane + 1] = (uint8_t)quant_angle(atan2f(v[3], v[2]), 0);
+    idx[level_base(1) + lane] = (uint8_t)quant_angle(atan2f(rb, ra), 1);
+    float R = sqrtf(ra * ra + rb * rb);
+#pragma unroll
+    for (int k = 2; k <= 6; ++k) {
+      const int m = 1 << (k - 2);
+      const float p = __shfl_xor_sync(0xffffffffu, R, m);
+      const bool lower = !(lane & m);
+      const float a = lower ? R : p, b = lower ? p : R;
+      if ((lane & ((m << 1) - 1)) == 0) idx[level_base(k) + lane / (m << 1)] = (uint8_t)quant_angle(atan2f(b, a), k);
+      R = sqrtf(a * a + b * b);
+    }
+    if (lane == 0) idx[kTqD - 1] = 0;
+    const __half r16 = __float2half_rn(R);
+    __syncwarp();
+    // ---- residual against the decoded vector (fp16 radius, as stored)
+    float d[4];
+    polar_decode(idx, __half2float(r16), lane, d);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float r = v[j] - d[j];
+      s_r[warp][4 * lane + j] = r;
+      ss += r * r;
+    }
+    const float nrm = sqrtf(warp_sum(ss));
+    __syncwarp();
+    // ---- QJL: projections lane and lane + 32, signs by ballot
+    float p0 = 0.f, p1 = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < kTqD; ++i) {
+      const float r = s_r[warp][i];
+      p0 += s_jl[lane][i] * r;
+      p1 += s_jl[lane + 32][i] * r;
+    }
+    const uint32_t b0 = __ballot_sync(0xffffffffu, p0 > 0.f), b1 = __ballot_sync(0xffffffffu, p1 > 0.f);
+    // ---- record: angles (3 bytes per 8 slots), radius, signs, residual norm
+    if (lane < 16) {
+      uint32_t bits = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bits |= (uint32_t)idx[8 * lane + j] << (3 * j);
+      rec[3 * lane] = (uint8_t)bits;
+      rec[3 * lane + 1] = (uint8_t)(bits >> 8);
+      rec[3 * lane + 2] = (uint8_t)(bits >> 16);
+    } else if (lane == 16) {
+      const unsigned short rb16 = __half_as_ushort(r16);
+      const unsigned short nb16 = __half_as_ushort(__float2half_rn(nrm));
+      rec[48] = (uint8_t)rb16;
+      rec[49] = (uint8_t)(rb16 >> 8);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        rec[50 + j] = (uint8_t)(b0 >> (8 * j));
+        rec[54 + j] = (uint8_t)(b1 >> (8 * j));
+      }
+      rec[58] = (uint8_t)nb16;
+      rec[59] = (uint8_t)(nb16 >> 8);
+      rec[60] = rec[61] = rec[62] = rec[63] = 0;
+    }
+    __syncwarp();
+    if (lane < 16)
+      reinterpret_cast<uint32_t*>(out + vec * kTqRec)[lane] = reinterpret_cast<const uint32_t*>(rec)[lane];
+    __syncwarp();
+  }
+}
+
+__global__ void __launch_bounds__(kTqWarps * 32) tq_decompress_kernel(const uint8_t* __restrict__ rec_in, int64_t n,
+                                                                      const float* __restrict__ signs,
+                                                                      __nv_bfloat16* __restrict__ out) {
+  __shared__ __align__(16) uint8_t s_rec[kTqWarps][kTqRec];
+  __shared__ uint8_t s_idx[kTqWarps][kTqD];
+  pdl_launch();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* rec = s_rec[warp];
+  uint8_t* idx = s_idx[warp];
+  float sg[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) sg[j] = signs[4 * lane + j];
+  for (int64_t vec = (int64_t)blockIdx.x * kTqWarps + warp; vec < n; vec += (int64_t)gridDim.x * kTqWarps) {
+    if (lane < 16)
+      reinterpret_cast<uint32_t*>(rec)[lane] = reinterpret_cast<const uint32_t*>(rec_in + vec * kTqRec)[lane];
+    __syncwarp();
+    if (lane < 16) {
+      const uint32_t bits = rec[3 * lane] | (uint32_t)rec[3 * lane + 1] << 8 | (uint32_t)rec[3 * lane + 2] << 16;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) idx[8 * lane + j] = (uint8_t)((bits >> (3 * j)) & 7u);
+    }
+    const float radius = __half2float(__ushort_as_half((unsigned short)(rec[48] | (rec[49] << 8))));
+    __syncwarp();
+    float v[4];
+    polar_decode(idx, radius, lane, v);
+    fwht4(v, lane);
+    uint2 o;
+    o.x = pack_bf16x2(v[0] * sg[0], v[1] * sg[1]);
+    o.y = pack_bf16x2(v[2] * sg[2], v[3] * sg[3]);
+    *reinterpret_cast<uint2*>(out + vec * kTqD + 4 * lane) = o;
+    __syncwarp();
+  }
+}
+
+int tq_grid(int64_t n) {
+  const int64_t need = (n + kTqWarps - 1) / kTqWarps;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(need, 4ll * device_sm_count()));
+}
+
+}  // namespace
+
+void tq_compress(const void* x, bool x_bf16, int64_t n, const float* signs, const float* jl, uint8_t* out,
+                 cudaStream_t st) {
+  if (n <= 0) return;
+  if (x_bf16)
+    launch_kernel(tq_compress_kernel<__nv_bfloat16>, dim3(tq_grid(n)), dim3(kTqWarps * 32), 0, st,
+                  reinterpret_cast<const __nv_bfloat16*>(x), n, signs, jl, out);
+  else
+    launch_kernel(tq_compress_kernel<float>, dim3(tq_grid(n)), dim3(kTqWarps * 32), 0, st,
+                  reinterpret_cast<const float*>(x), n, signs, jl, out);
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+void tq_decompress(const uint8_t* rec, int64_t n, const float* signs, void* out, cudaStream_t st) {
+  if (n <= 0) return;
+  launch_kernel(tq_decompress_kernel, dim3(tq_grid(n)), dim3(kTqWarps * 32), 0, st, rec, n, signs,
+                reinterpret_cast<__nv_bfloat16*>(out));
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace vrm

@@ -121,6 +121,13 @@ struct Nvfp4GemmArgs {
 void nvfp4_gemm(const Nvfp4GemmArgs& a, cudaStream_t stream);
 int nvfp4_gemm_max_m();
 
+// ---------------------------------------------------------------- TurboQuant records (turboquant.cu)
+// n vectors of 128 dims (bf16 or fp32) -> n 64-byte records, and back to bf16.
+// signs: fp32 [128] rotation signs; jl: fp32 [64, 128] JL matrix.
+void tq_compress(const void* x, bool x_bf16, int64_t n, const float* signs, const float* jl, uint8_t* out,
+                 cudaStream_t stream);
+void tq_decompress(const uint8_t* rec, int64_t n, const float* signs, void* out, cudaStream_t stream);
+
 struct RopeKvArgs {
   void* qkv = nullptr;          // bf16 [T, (Hq + 2 KH) * D], rotated in place
   int64_t ld_qkv = 0;
