@@ -42,7 +42,7 @@ def test_nvlink_count_with_fake_nvml():
 @pytest.mark.gpu
 def test_staged_copy_on_one_gpu():
     tm = TransferManager(staging_chunk_mb=1)
-    x = torch.randn(3 << 20 // 4 + 123, device="cuda:0")       # several chunks + a tail
+    x = torch.randn((3 << 20) // 4 + 123, device="cuda:0")     # several 1 MiB chunks + a tail
     out = torch.empty_like(x)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
