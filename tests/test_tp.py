@@ -48,3 +48,22 @@ def test_tp2_matches_tp1_gpu_nccl():
     assert res["max_logit_diff"] < 0.05 * max(1.0, res["scale"]), res
     # fused GEMM + all-reduce matches GEMM followed by the NCCL all-reduce
     assert res["fused_ar_rel_diff"] is not None and res["fused_ar_rel_diff"] < 2e-2, res
+
+
+def test_apply_tensor_parallel_single_process_api_cpu():
+    """apply_tensor_parallel spawns its own ranks (gloo on CPU) and matches TP=1."""
+    from vramancer_b200.engine.engine import SamplingParams
+    from vramancer_b200.llm import LLM
+    from vramancer_b200.parallel.tensor_parallel import apply_tensor_parallel
+    kw = dict(max_batch=4, max_model_len=128, kv_pages=64)
+    prompts = [[1, 2, 3, 4, 5], list(range(10, 40))]
+    ref = LLM("tiny-qwen2", device="cpu", dtype=torch.float32, kv_cache_dtype="fp32", use_cuda_graph=False, **kw)
+    want = [o.output_ids for o in ref.generate(prompts, SamplingParams(max_tokens=6))]
+    tp = apply_tensor_parallel("tiny-qwen2", num_gpus=2, device="cpu", timeout_s=300, **kw)
+    try:
+        got = tp.generate(prompts, max_tokens=6)
+        assert got == want
+        full = tp.generate_greedy(torch.tensor([prompts[0]]), max_new_tokens=3)
+        assert full.shape == (1, 8) and full[0, :5].tolist() == prompts[0]
+    finally:
+        tp.shutdown()
