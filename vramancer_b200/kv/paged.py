@@ -49,7 +49,7 @@ def _chain_hash(prev: bytes, tokens: Sequence[int]) -> bytes:
 class PagedKVCacheManager:
     def __init__(self, num_pages: int, page_size: int = PAGE_SIZE, enable_prefix_cache: bool = True,
                  overflow: Optional[Callable[[int], Optional[int]]] = None,
-                 release_borrowed: Optional[Callable[[int], None]] = None):
+                 release_borrowed: Optional[Callable[[int], None]] = None, offload=None):
         self.num_pages = num_pages
         self.page_size = page_size
         self.enable_prefix_cache = enable_prefix_cache
@@ -61,6 +61,7 @@ class PagedKVCacheManager:
         self._lru: "OrderedDict[int, None]" = OrderedDict()  # cached pages with ref 0
         self._overflow = overflow
         self._release_borrowed = release_borrowed
+        self.offload = offload                              # host tier of the prefix cache (kv/offload.py)
         self._borrowed: Dict[int, int] = {}                 # page id (>= num_pages) -> ref
         self._lock = threading.RLock()
         self._cow: List[Tuple[int, int]] = []
@@ -87,6 +88,8 @@ class PagedKVCacheManager:
             key = self._page_key.pop(p, None)
             if key is not None and self._prefix.get(key[0]) == p:
                 del self._prefix[key[0]]
+                if self.offload is not None:
+                    self.offload.on_evict(p, key[0], key[1])
             self.stats_counters["evictions"] += 1
         else:
             p = self._overflow(1) if self._overflow is not None else None
@@ -140,6 +143,21 @@ class PagedKVCacheManager:
                     toks = tuple(int(t) for t in token_ids[i * self.page_size:(i + 1) * self.page_size])
                     h = _chain_hash(prev, toks)
                     p = self._prefix.get(h)
+                    if p is None and self.offload is not None and self.offload.has(h, toks):
+                        # host tier hit: bring the page back (stream-ordered copy)
+                        try:
+                            p = self._take_page()
+                        except OutOfPages:
+                            break
+                        self.offload.restore(h, p)
+                        self._prefix[h] = p
+                        self._page_key[p] = (h, toks)
+                        self.stats_counters["offload_hits"] = self.stats_counters.get("offload_hits", 0) + 1
+                        st.pages.append(p)
+                        st.hashes.append(h)
+                        prev = h
+                        cached += self.page_size
+                        continue
                     if p is None or self._page_key.get(p, (None, None))[1] != toks:
                         break
                     self._incref(p)

@@ -35,7 +35,7 @@ class LLM:
                  seed: int = 0, use_cuda_graph: bool = True, enable_prefix_cache: bool = True,
                  max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, weights=None,
                  num_layers: Optional[int] = None, tp=None, quantization: Optional[str] = None,
-                 spec_num_draft: int = 0, spec_ngram: int = 3):
+                 spec_num_draft: int = 0, spec_ngram: int = 3, kv_offload_pages: int = 0, hierarchy=None):
         if isinstance(model, ModelConfig):
             cfg = model
         else:
@@ -68,7 +68,13 @@ class LLM:
             kv_pages = self._pages_from_memory(cfg, kvd, gpu_memory_utilization, max_batch, max_model_len)
         spec = KVPoolSpec(kv_pages, cfg.num_layers, self.model.kvh, cfg.head_dim, dtype=kvd)
         self.pool = KVPool(spec, self.device)
-        self.kv = PagedKVCacheManager(kv_pages, spec.page_size, enable_prefix_cache=enable_prefix_cache)
+        self.offload = None
+        if kv_offload_pages > 0 and enable_prefix_cache:
+            # evicted prefix pages go to pinned host memory (and on to NVMe through `hierarchy`)
+            from .kv.offload import KVOffloader
+            self.offload = KVOffloader([self.pool.cache], kv_offload_pages, hierarchy=hierarchy)
+        self.kv = PagedKVCacheManager(kv_pages, spec.page_size, enable_prefix_cache=enable_prefix_cache,
+                                      offload=self.offload)
         self.runner = ModelRunner(self.model, self.pool, max_batch=max_batch, max_model_len=max_model_len,
                                   use_cuda_graph=use_cuda_graph, seed=seed)
         self.engine = LLMEngine(self.runner, self.kv, max_prefill_tokens=max_prefill_tokens,
