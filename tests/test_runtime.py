@@ -114,3 +114,19 @@ def test_basic_tokenize_is_deterministic():
     out = rt.basic_tokenize(["hello, world", "hello"], 1000)
     assert len(out[0]) == 3 and out[0][0] == out[1][0]
     assert all(0 <= t < 1000 for t in out[0])
+
+
+def test_tcp_frames_keep_every_dtype_aligned():
+    lis = rt.listen("127.0.0.1", 0)
+    box = {}
+    th = threading.Thread(target=_serve_once, args=(lis, b"", box))
+    th.start()
+    conn = rt.connect("127.0.0.1", lis.port)
+    x = {"a": torch.arange(3, dtype=torch.int32), "b": torch.arange(5, dtype=torch.int64),
+         "c": torch.ones(3, dtype=torch.uint8), "d": torch.randn(2, 3, dtype=torch.float64)}
+    rt.send_tensors(conn, x)
+    th.join(10)
+    conn.close()
+    lis.close()
+    got, _ = box["got"]
+    assert all(torch.equal(got[k], v) for k, v in x.items())

@@ -60,7 +60,7 @@ class LocalPipeline:
 
     @property
     def pools(self) -> List[KVPool]:
-        return [p for _, p in self.stages]
+        return [p for _, p in self.stages if p is not None]     # remote stages keep their own
 
     def forward(self, batch: ForwardBatch, pool=None, hidden=None) -> torch.Tensor:
         h = hidden
@@ -73,7 +73,10 @@ class LocalPipeline:
         return h
 
     def copy_pages(self, pairs) -> None:
-        for _, p in self.stages:
+        for m, p in self.stages:
+            if p is None:                    # remote stage (cluster/stage_server.py)
+                m.copy_pages(pairs)
+                continue
             for src, dst in pairs:
                 p.cache[dst].copy_(p.cache[src])
 

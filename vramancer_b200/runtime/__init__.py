@@ -148,10 +148,11 @@ def send_tensors(conn, tensors: Dict[str, torch.Tensor], meta: Optional[dict] = 
     for name, t in tensors.items():
         h = _host_view(t.detach())
         n = h.numel() * h.element_size()
+        off = (off + 15) & ~15          # every tensor 16-byte aligned: views of any dtype on receipt
         entries.append({"name": name, "dtype": str(h.dtype), "shape": list(h.shape), "offset": off, "nbytes": n})
         hosts.append(h)
         off += n
-    payload = torch.empty(off, dtype=torch.uint8, pin_memory=torch.cuda.is_available())
+    payload = torch.zeros(off, dtype=torch.uint8, pin_memory=torch.cuda.is_available())
     for h, e in zip(hosts, entries):
         if e["nbytes"]:
             payload[e["offset"]:e["offset"] + e["nbytes"]].copy_(h.reshape(-1).view(torch.uint8))
