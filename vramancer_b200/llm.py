@@ -35,7 +35,8 @@ class LLM:
                  seed: int = 0, use_cuda_graph: bool = True, enable_prefix_cache: bool = True,
                  max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, weights=None,
                  num_layers: Optional[int] = None, tp=None, quantization: Optional[str] = None,
-                 spec_num_draft: int = 0, spec_ngram: int = 3, kv_offload_pages: int = 0, hierarchy=None):
+                 spec_num_draft: int = 0, spec_ngram: int = 3, kv_offload_pages: int = 0, hierarchy=None,
+                 stream_layers: int = 0):
         if isinstance(model, ModelConfig):
             cfg = model
         else:
@@ -53,7 +54,9 @@ class LLM:
                 weights = load_safetensors(model, cfg, device=self.device, dtype=dtype, tp_rank=tp_rank,
                                            tp_size=tp_size)
             else:
-                weights = random_weights(cfg, device=self.device, dtype=dtype, seed=seed, tp_rank=tp_rank,
+                # streamed layers live in host memory: build them there
+                wdev = torch.device("cpu") if stream_layers > 0 else self.device
+                weights = random_weights(cfg, device=wdev, dtype=dtype, seed=seed, tp_rank=tp_rank,
                                          tp_size=tp_size)
         self.quantization = (quantization or "").lower() or None
         if self.quantization == "nvfp4":
@@ -62,7 +65,14 @@ class LLM:
         elif self.quantization not in (None, "none", "bf16"):
             raise ValueError(f"unsupported quantization {quantization!r} (nvfp4 or none)")
         self.weights = weights
-        self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype, tp=tp)
+        if stream_layers > 0:
+            # layer weights stay in pinned host memory, `stream_layers` layers resident
+            from .engine.streaming import StreamedDecoderModel
+            self.model = StreamedDecoderModel(cfg, weights, budget_layers=stream_layers, device=self.device,
+                                              dtype=dtype, tp=tp)
+            use_cuda_graph = False
+        else:
+            self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype, tp=tp)
         kvd = kv_dtype_from_str(kv_cache_dtype)
         if kv_pages is None:
             kv_pages = self._pages_from_memory(cfg, kvd, gpu_memory_utilization, max_batch, max_model_len)
