@@ -39,6 +39,11 @@ __device__ __forceinline__ uint32_t swz(int r, int ch) {
   return (uint32_t)(r * ROWB + ((ch ^ (r & 7)) << 4));
 }
 
+// Transpose of an 8x8 b16 matrix held in mma fragment layout (one register per lane).
+__device__ __forceinline__ void movmatrix_trans(uint32_t in, uint32_t& out) {
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(out) : "r"(in));
+}
+
 // fp8 e4m3 x2 -> bf16 x2 (exact: every e4m3 value is a bf16 value)
 __device__ __forceinline__ uint32_t fp8x2_to_bf16x2(uint16_t v) {
   __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(v, __NV_E4M3);
@@ -159,25 +164,30 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   if (!early && my_first < p_end) issue(my_first, 0);
   cp_async_commit();
 
-  // Q fragments: rows = heads of the group (rows >= G and rows 8..15 are zero)
-  uint32_t qa[D / 16][2];
+  // Q as the MMA B operand (k = head dims, n = the group's heads; heads >= G are zero).
+  // Scores are computed transposed, S^T = K Q^T: the 16 tokens of a page fill the MMA
+  // rows and the (<= 8) heads the columns, so no MMA row is wasted on absent heads.
+  uint32_t qb[D / 16][2];
   {
     const __nv_bfloat16* qrow = P.q + (size_t)b * P.ld_q + (size_t)(kvh * G + g) * D;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       if (g < G) {
-        qa[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * c);
-        qa[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * c);
+        qb[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * c);
+        qb[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * c);
       } else {
-        qa[kk][0] = qa[kk][1] = 0u;
+        qb[kk][0] = qb[kk][1] = 0u;
       }
     }
   }
 
-  float o[D / 8][4];
+  // O^T accumulators: tile mt covers dims [16 mt, 16 mt + 16); this thread holds
+  // (dim 16 mt + g, heads 2c, 2c+1) in [0], [1] and (dim 16 mt + g + 8, same heads) in [2], [3]
+  float o[D / 16][4];
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
+  for (int i = 0; i < D / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  // online-softmax state of heads 2c and 2c+1 (identical in the 8 lanes sharing c)
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
 
   int it = 0;
   for (int p = my_first; p < p_end; p += 4, ++it) {
@@ -199,70 +209,87 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
     }
     const uint32_t kaddr = smem_u32(kt), vaddr = smem_u32(vt);
 
-    // S = Q K^T : rows = heads, cols = the page's 16 tokens (two n-tiles)
-    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+    // S^T = K Q^T: A = the page's K rows (tokens) x 16 dims, four 8x8 matrices
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
-      const int j = lane >> 3;
-      const int row = (lane & 7) + (j >> 1) * 8;
-      const int ch = 2 * kk + (j & 1);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(kaddr + swz<ROWB>(row, ch), b0, b1, b2, b3);
-      mma_bf16_16816(s0, qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
-      mma_bf16_16816(s1, qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
+      const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int ch = 2 * kk + (lane >> 4);
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(kaddr + swz<ROWB>(row, ch), a0, a1, a2, a3);
+      mma_bf16_16816(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
     }
+    // sc[0] = (token g, head 2c), [1] = (g, 2c+1), [2] = (g+8, 2c), [3] = (g+8, 2c+1)
     const int tok0 = p * kPage;
-    float x[4] = {s0[0] * scale_log2, s0[1] * scale_log2, s1[0] * scale_log2, s1[1] * scale_log2};
-    const int tix[4] = {tok0 + 2 * c, tok0 + 2 * c + 1, tok0 + 8 + 2 * c, tok0 + 8 + 2 * c + 1};
+    float x[4] = {sc[0] * scale_log2, sc[1] * scale_log2, sc[2] * scale_log2, sc[3] * scale_log2};
+    if (tok0 + g >= ctx) x[0] = x[1] = -INFINITY;
+    if (tok0 + g + 8 >= ctx) x[2] = x[3] = -INFINITY;
+    float mx[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (tix[i] >= ctx) x[i] = -INFINITY;
-    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float m_new = fmaxf(m_run, mx);
-    const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m_run - m_new);
+    for (int j = 0; j < 2; ++j) {
+      mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 4));
+      mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 8));
+      mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 16));
+    }
+    float alpha[2], m_new[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      m_new[j] = fmaxf(m_run[j], mx[j]);
+      alpha[j] = (m_new[j] == -INFINITY) ? 1.f : exp2f(m_run[j] - m_new[j]);
+    }
     float pr[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) pr[i] = (m_new == -INFINITY) ? 0.f : exp2f(x[i] - m_new);
-    float rs = pr[0] + pr[1] + pr[2] + pr[3];
-    rs += __shfl_xor_sync(0xffffffffu, rs, 1);
-    rs += __shfl_xor_sync(0xffffffffu, rs, 2);
-    l_run = l_run * alpha + rs;
-    m_run = m_new;
+    for (int i = 0; i < 4; ++i) pr[i] = (m_new[i & 1] == -INFINITY) ? 0.f : exp2f(x[i] - m_new[i & 1]);
+    float rs[2] = {pr[0] + pr[2], pr[1] + pr[3]};
 #pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-      o[i][0] *= alpha;
-      o[i][1] *= alpha;
+    for (int j = 0; j < 2; ++j) {
+      rs[j] += __shfl_xor_sync(0xffffffffu, rs[j], 4);
+      rs[j] += __shfl_xor_sync(0xffffffffu, rs[j], 8);
+      rs[j] += __shfl_xor_sync(0xffffffffu, rs[j], 16);
+      l_run[j] = l_run[j] * alpha[j] + rs[j];
+      m_run[j] = m_new[j];
     }
-    const uint32_t pa0 = pack_bf16x2(pr[0], pr[1]);
-    const uint32_t pa2 = pack_bf16x2(pr[2], pr[3]);
-    // O += P V : rows = heads, cols = head_dim (n-tiles of 8), k = 16 tokens
 #pragma unroll
-    for (int nd = 0; nd < D / 8; nd += 2) {
-      const int j = lane >> 3;
-      const int row = (lane & 7) + (j & 1) * 8;
-      const int ch = nd + (j >> 1);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4_t(vaddr + swz<ROWB>(row, ch), b0, b1, b2, b3);
-      mma_bf16_16816(o[nd], pa0, 0u, pa2, 0u, b0, b1);
-      mma_bf16_16816(o[nd + 1], pa0, 0u, pa2, 0u, b2, b3);
+    for (int mt = 0; mt < D / 16; ++mt) {
+      o[mt][0] *= alpha[0];
+      o[mt][1] *= alpha[1];
+      o[mt][2] *= alpha[0];
+      o[mt][3] *= alpha[1];
+    }
+    // P^T as the B operand (k = tokens, n = heads): transpose the two 8x8 bf16 blocks
+    uint32_t pb0, pb1;
+    movmatrix_trans(pack_bf16x2(pr[0], pr[1]), pb0);
+    movmatrix_trans(pack_bf16x2(pr[2], pr[3]), pb1);
+    // O^T += V^T P^T: A = V^T (dims x tokens) from the V tile with transposing loads
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      const int row = (lane & 7) + (lane >> 4) * 8;
+      const int ch = 2 * mt + ((lane >> 3) & 1);
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4_t(vaddr + swz<ROWB>(row, ch), a0, a1, a2, a3);
+      mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
     }
     __syncwarp();
   }
   cp_async_wait<0>();
   __syncthreads();
 
-  // ---- merge the 4 warps
-  float* s_o = reinterpret_cast<float*>(smem);   // [4][8][D]
-  if (c == 0) {
-    s_m[warp][g] = m_run;
-    s_l[warp][g] = l_run;
+  // ---- merge the 4 warps (row stride D + 4: the transposed stores hit distinct banks)
+  constexpr int kOS = D + 4;
+  float* s_o = reinterpret_cast<float*>(smem);   // [4][8][D + 4]
+  if (g == 0) {
+    s_m[warp][2 * c] = m_run[0];
+    s_m[warp][2 * c + 1] = m_run[1];
+    s_l[warp][2 * c] = l_run[0];
+    s_l[warp][2 * c + 1] = l_run[1];
   }
 #pragma unroll
-  for (int nd = 0; nd < D / 8; ++nd) {
-    s_o[(warp * 8 + g) * D + nd * 8 + 2 * c] = o[nd][0];
-    s_o[(warp * 8 + g) * D + nd * 8 + 2 * c + 1] = o[nd][1];
+  for (int mt = 0; mt < D / 16; ++mt) {
+    float* r0 = s_o + (warp * 8 + 2 * c) * kOS + mt * 16 + g;
+    r0[0] = o[mt][0];
+    r0[kOS] = o[mt][1];
+    r0[8] = o[mt][2];
+    r0[kOS + 8] = o[mt][3];
   }
   __syncthreads();
 
@@ -278,7 +305,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
       for (int w = 0; w < 4; ++w) {
         const float f = exp2f(s_m[w][h] - M);
         L += s_l[w][h] * f;
-        acc += s_o[(w * 8 + h) * D + d] * f;
+        acc += s_o[(w * 8 + h) * kOS + d] * f;
       }
     }
     if (nsplit == 1) {
