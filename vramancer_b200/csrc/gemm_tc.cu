@@ -840,6 +840,39 @@ static bool prefill_streamk() {
   return v;
 }
 
+// Persistent CTAs of the stream-K decode GEMM.  Latency model fitted on B200 (µs): a
+// CTA streams its share of the weights at ~80 GB/s; tiles shared by nc CTAs add ~1 µs
+// plus ~0.6 µs per batch of four partials per 16-column chunk for the owner's fixup.
+// Short-K GEMMs (the tensor-parallel shards) then run fastest on one CTA per tile, long
+// ones on every SM.  VRM_GEMM_CTAS overrides (tuning).
+static int streamk_ctas(int tiles, int k_tiles, int BN, double weight_bytes) {
+  static const int env = [] {
+    const char* e = std::getenv("VRM_GEMM_CTAS");
+    return e ? std::atoi(e) : 0;
+  }();
+  const int sms = device_sm_count();
+  if (env > 0) return std::min(env, sms);
+  auto cost = [&](int ctas) {
+    const int64_t iters = (int64_t)tiles * k_tiles;
+    ctas = (int)std::min<int64_t>(ctas, iters);
+    const double per_cta = weight_bytes / ctas;
+    const int nc = (ctas + tiles - 1) / tiles;
+    double t = per_cta / 80e3;
+    if (ctas > tiles || nc > 1) t += 1.0 + 0.6 * ((nc - 1 + 3) / 4) * (BN / 16);
+    return t;
+  };
+  int best = sms;
+  double best_t = cost(sms);
+  for (int k = 1; k <= 8 && tiles * k <= sms; ++k) {
+    const double t = cost(tiles * k);
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = tiles * k;
+    }
+  }
+  return best;
+}
+
 static bool legacy_decode() {
   static const bool v = [] {
     const char* e = std::getenv("VRM_GEMM_LEGACY_DECODE");
@@ -881,7 +914,7 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     VRM_REQUIRE(!a.allreduce || (a.force_splits <= 0 && !legacy_decode()),
                 "fused all-reduce runs on the stream-K decode path only");
     if (a.force_splits <= 0 && !legacy_decode()) {
-      const int ctas = device_sm_count();
+      const int ctas = streamk_ctas((a.N + kBM - 1) / kBM, k_tiles, BN, 2.0 * a.N * a.K);
       // <= 113 KB of smem per CTA: a CTA of the next GEMM fits beside it and (PDL)
       // prefetches its weights while this one drains
       const ARParams ar = a.allreduce ? *a.allreduce : ARParams{};
