@@ -1,10 +1,10 @@
 // Reduce half of the fused tensor-parallel all-reduce, fused with the residual update
 // and the norm that follows the row-parallel projection (ARNormArgs in vrm_kernels.h).
 //
-// The row-parallel GEMM of every rank has pushed its fp32 partial into this rank's
+// The row-parallel GEMM of every rank has pushed its bf16 partial into this rank's
 // receive buffer over NVLink and flagged it (gemm_tc.cu, ARPush).  One CTA per token
 // row waits for the peers' flags (bounded spin, kErrFlagTimeout on expiry), sums the
-// world slots in rank order from local HBM, adds bias and the bf16 residual, stores the
+// world slots in rank order in fp32 from local HBM, adds bias and the bf16 residual, stores the
 // new residual and writes the normalised row for the next GEMM.  So one decode layer at
 // TP > 1 launches the same eight kernels as at TP = 1: the all-reduce costs one set of
 // posted NVLink stores in the GEMM epilogue and a flag wait here, no extra launch.
@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(256) ar_norm_kernel(ARNormArgs a, uint32_t* __
   }
   __syncthreads();
   const int H = a.H, nvec = H >> 3;
-  const float* half = a.xbuf + (size_t)(epoch & 1u) * a.world * a.half_floats + (size_t)row * H;
+  const __nv_bfloat16* half = a.xbuf + (size_t)(epoch & 1u) * a.world * a.half_floats + (size_t)row * H;
   const auto* bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   auto* res = a.residual ? reinterpret_cast<__nv_bfloat16*>(a.residual) + (size_t)row * H : nullptr;
   float vals[VPT][8];
@@ -70,10 +70,9 @@ __global__ void __launch_bounds__(256) ar_norm_kernel(ARNormArgs a, uint32_t* __
     for (int j = 0; j < 8; ++j) vals[i][j] = 0.f;
     if (v >= nvec) continue;
     for (int p = 0; p < a.world; ++p) {
-      const float4* src = reinterpret_cast<const float4*>(half + (size_t)p * a.half_floats + v * 8);
-      const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
-      vals[i][0] += x0.x; vals[i][1] += x0.y; vals[i][2] += x0.z; vals[i][3] += x0.w;
-      vals[i][4] += x1.x; vals[i][5] += x1.y; vals[i][6] += x1.z; vals[i][7] += x1.w;
+      const uint4 x = __ldcg(reinterpret_cast<const uint4*>(half + (size_t)p * a.half_floats + v * 8));
+      vals[i][0] += bf16_lo(x.x); vals[i][1] += bf16_hi(x.x); vals[i][2] += bf16_lo(x.y); vals[i][3] += bf16_hi(x.y);
+      vals[i][4] += bf16_lo(x.z); vals[i][5] += bf16_hi(x.z); vals[i][6] += bf16_lo(x.w); vals[i][7] += bf16_hi(x.w);
     }
     if (bias) {
       const uint4 bb = *reinterpret_cast<const uint4*>(bias + v * 8);

@@ -390,7 +390,8 @@ struct StreamK {
 };
 
 // Fused all-reduce, push half (ARPush in vrm_kernels.h): the owner of each finished
-// output tile stores the fp32 partial (pre-bias) into this rank's slot on every rank
+// output tile stores the partial (pre-bias, rounded to bf16 like the input of a bf16
+// NCCL all-reduce: half the NVLink bytes of fp32) into this rank's slot on every rank
 // (posted NVLink stores; its own slot is local) and never waits; the last CTA of the
 // launch advances the epoch and flags every peer.  ar_norm.cu reduces.
 using ARParams = ARPush;
@@ -628,10 +629,10 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           // push the partial into this rank's slot on every rank (own slot is local)
           if (r_glob < ep.N) {
             for (int p = 0; p < ar.world; ++p) {
-              float* dst = ar.xbuf[p] + xoff;
+              __nv_bfloat16* dst = ar.xbuf[p] + xoff;
 #pragma unroll
               for (int j = 0; j < 16; ++j)
-                if (tok0 + c0 + j < ep.M) __stcg(dst + (size_t)(tok0 + c0 + j) * ep.N, v[j]);
+                if (tok0 + c0 + j < ep.M) dst[(size_t)(tok0 + c0 + j) * ep.N] = __float2bfloat16(v[j]);
             }
           }
         } else {

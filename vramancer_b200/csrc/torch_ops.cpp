@@ -352,7 +352,7 @@ void gemm_ar_push(const Tensor& x, const Tensor& w, const Tensor& xbuf_ptrs, con
                   xbuf_ptrs.numel() == world && flag_ptrs.numel() == world,
               "gemm_ar: pointer arrays must be int64 [world]");
   vrm::ARPush ar;
-  ar.xbuf = reinterpret_cast<float* const*>(xbuf_ptrs.data_ptr());
+  ar.xbuf = reinterpret_cast<__nv_bfloat16* const*>(xbuf_ptrs.data_ptr());
   ar.flags = reinterpret_cast<uint32_t* const*>(flag_ptrs.data_ptr());
   ar.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
   ar.done = reinterpret_cast<uint32_t*>(done.data_ptr());
@@ -389,7 +389,7 @@ void ar_norm(int64_t xbuf, int64_t flags, const Tensor& epoch, int64_t rank, int
   if (has(w)) TORCH_CHECK(w->numel() == H && w->is_contiguous(), "ar_norm: weight [H]");
   if (has(b)) TORCH_CHECK(b->numel() == H && b->is_contiguous(), "ar_norm: norm bias [H]");
   vrm::ARNormArgs a;
-  a.xbuf = reinterpret_cast<const float*>(xbuf);
+  a.xbuf = reinterpret_cast<const __nv_bfloat16*>(xbuf);
   a.flags = reinterpret_cast<const uint32_t*>(flags);
   a.epoch = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
   a.rank = (int)rank;

@@ -6,6 +6,7 @@
 // device; every launch goes to `stream`.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -40,18 +41,18 @@ struct GemmArgs {
 };
 
 // Push half of the fused tensor-parallel all-reduce.  Every rank owns a receive
-// buffer [2 halves][world source ranks][half_floats] fp32 and flags [world source
+// buffer [2 halves][world source ranks][half_floats] bf16 and flags [world source
 // ranks] (cudaMalloc + CUDA IPC, symm.cu).  The row-parallel GEMM stores its fp32
 // partial Y[m, n] at m * N + n of its own slot on every rank, then its last CTA
 // advances *epoch and release-stores it into each peer's flag for this rank.  Halves
 // alternate with the epoch's parity.  ar_norm (ar_norm.cu) is the reduce half.
 struct ARPush {
-  float* const* xbuf = nullptr;      // device array [world] of the ranks' receive buffers
+  __nv_bfloat16* const* xbuf = nullptr;  // device array [world] of the ranks' receive buffers
   uint32_t* const* flags = nullptr;  // device array [world] of the ranks' flag arrays
   uint32_t* epoch = nullptr;         // this rank's call counter (device)
   uint32_t* done = nullptr;          // this rank's CTA completion counter (device, zero)
   int rank = 0, world = 1;
-  long long half_floats = 0;         // floats per (half, source rank) slot
+  long long half_floats = 0;         // elements per (half, source rank) slot
   // 1: every epilogue thread fences its own remote stores at system scope before the
   // CTA barrier; 0: one system-scope fence by the flagging thread after the barrier
   // (release cumulativity over the barrier)
@@ -78,7 +79,7 @@ void layernorm(const void* x, int64_t ldx, void* residual, const void* w, const 
 // Every rank sums the same values in the same order: identical results on all ranks.
 enum ArNormMode { kArAdd = 0, kArRmsNorm = 1, kArLayerNorm = 2 };
 struct ARNormArgs {
-  const float* xbuf = nullptr;       // this rank's receive buffer
+  const __nv_bfloat16* xbuf = nullptr;   // this rank's receive buffer
   const uint32_t* flags = nullptr;   // this rank's flags [world]
   const uint32_t* epoch = nullptr;   // this rank's call counter (advanced by the GEMM)
   int rank = 0, world = 1;

@@ -22,6 +22,8 @@ import torch
 
 
 def _step_ms(runner, B: int, reps: int = 20) -> float:
+    from ..parallel import comm
+    comm.barrier()
     g = runner.capture(B)
     g.replay()
     torch.cuda.synchronize()
@@ -36,7 +38,7 @@ def _step_ms(runner, B: int, reps: int = 20) -> float:
         best = min(best, a.elapsed_time(b) / reps)
     runner._graphs.pop(B, None)
     del g
-    return best
+    return comm.max_over_ranks(best)
 
 
 def ablate(llm, B: int) -> dict:
@@ -59,6 +61,15 @@ def ablate(llm, B: int) -> dict:
         "sampler": {"sample": lambda logits, *a, out=None, **k: out},
     }
     res = {"batch": B, "step_ms": round(base, 4)}
+    tp = getattr(llm.model, "tp", None)
+    if tp is not None:
+        # the row-parallel all-reduces (fused push/reduce or NCCL) replaced by nothing
+        saved_ar, saved_far = tp.all_reduce, tp.fused_ar
+        tp.all_reduce, tp.fused_ar = (lambda x: x), None
+        try:
+            res["allreduce_ms"] = round(base - _step_ms(runner, B), 4)
+        finally:
+            tp.all_reduce, tp.fused_ar = saved_ar, saved_far
     for name, patch in stubs.items():
         saved = {k: getattr(ops, k) for k in patch}
         try:
@@ -90,7 +101,10 @@ def main(argv=None):
     from ..llm import LLM
 
     B, P = args.batch, args.prompt_len
-    llm = LLM(args.model, device="cuda:0", max_batch=B, max_model_len=P + args.steps + 64,
+    from ..parallel import comm
+    info = comm.init_distributed()          # under torchrun: tensor parallelism over the ranks
+    tp = comm.tp_context()
+    llm = LLM(args.model, device=f"cuda:{info.local_rank}", tp=tp, max_batch=B, max_model_len=P + args.steps + 64,
               kv_pages=(B + 1) * ((P + args.steps + 80) // 16 + 1) + 16, enable_prefix_cache=False,
               use_cuda_graph=args.graph, kv_cache_dtype=args.kv_dtype, num_layers=args.num_layers)
     g = torch.Generator().manual_seed(0)
@@ -101,7 +115,12 @@ def main(argv=None):
     llm.engine.step()              # warm decode (captures the graph when --graph)
     torch.cuda.synchronize()
     if args.ablate:
-        print(json.dumps(ablate(llm, llm.runner.bucket_for(B))))
+        res = ablate(llm, llm.runner.bucket_for(B))
+        if info.rank == 0:
+            print(json.dumps(res))
+        llm.runner.release_graphs()
+        comm.barrier()
+        comm.destroy()
         return
     torch.cuda.nvtx.range_push("vrm_decode")
     for _ in range(args.steps):

@@ -1,10 +1,10 @@
 """Symmetric buffers for the fused GEMM + all-reduce of tensor-parallel decode.
 
-Every rank allocates (cudaMalloc) a receive buffer (two halves x one fp32 slot per
+Every rank allocates (cudaMalloc) a receive buffer (two halves x one bf16 slot per
 source rank) and a flag word per source rank, exports CUDA IPC handles, gathers its
 peers' handles over the process group and opens them.  A row-parallel projection is
 then two kernels of this package:
-  push    the stream-K GEMM stores its fp32 partial into its slot on every rank over
+  push    the stream-K GEMM stores its partial (bf16) into its slot on every rank over
           NVLink and flags the peers when its last CTA finishes (csrc/gemm_tc.cu);
   reduce  the next norm kernel waits for the peers' flags, sums the slots in rank
           order from local memory, adds bias + residual and normalises
@@ -43,8 +43,8 @@ class FusedAllReduce:
         self.half_floats = max_features * max_tokens
         nat = ops.native()
         with torch.cuda.device(self.device):
-            # receive buffer: [2 halves][world source ranks][half_floats] fp32; flags [world]
-            self.xbuf = nat.symm_malloc(2 * self.world * self.half_floats * 4)
+            # receive buffer: [2 halves][world source ranks][half_floats] bf16; flags [world]
+            self.xbuf = nat.symm_malloc(2 * self.world * self.half_floats * 2)
             self.flags = nat.symm_malloc(max(16, self.world * 4))
             handles = [nat.ipc_handle(self.xbuf), nat.ipc_handle(self.flags)]
             allh = [None] * self.world
