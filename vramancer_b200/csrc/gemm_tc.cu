@@ -682,6 +682,162 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
   }
 }
 
+// =====================================================================================
+// Grouped (mixture-of-experts) swap-AB GEMM over a device-built work list.  Expert
+// weights are one K-major matrix [E * N, K]; the activations of the tokens routed to
+// each expert are contiguous rows of x_perm (moe.cu builds both the permutation and the
+// list of token blocks: expert, first row, rows).  Work item i = (block i / wtiles,
+// weight tile i % wtiles) computes 128 weight rows of that expert against its block of
+// <= BN tokens over the full K; persistent CTAs take items round-robin, with double TMEM
+// accumulators so one item's epilogue overlaps the next item's MMAs.  Everything the
+// CTAs need comes from the device, so the launch has a fixed grid and no host sync.
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    moe_grouped_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                            EpiParams ep, const MoeBlock* __restrict__ blocks, const int* __restrict__ num_blocks,
+                            int n_per_expert, int k_tiles, uint32_t* __restrict__ err) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStageBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull = empty_bar + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+
+  pdl_launch();
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&map_w);
+    tma_prefetch_desc(&map_x);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();                        // the work list and x_perm come from the previous kernels
+  const int wtiles = (n_per_expert + kBM - 1) / kBM;
+  const int items = *num_blocks * wtiles;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- producer
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    int s = 0;
+    uint32_t ph = 0;
+    int64_t g = 0;
+    bool failed = false;
+    for (int i = blockIdx.x; i < items && !failed; i += gridDim.x) {
+      const MoeBlock b = blocks[i / wtiles];
+      const int wrow = b.expert * n_per_expert + (i % wtiles) * kBM;
+      for (int k = 0; k < k_tiles; ++k, ++g) {
+        if (g >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, err)) {
+          failed = true;
+          break;
+        }
+        uint8_t* sa = smem + s * L::kStageBytes;
+        mbar_arrive_expect_tx(&full_bar[s], L::kStageBytes);
+        tma_load_2d(sa, &map_w, &full_bar[s], k * kBK, wrow, pol_w);
+        tma_load_2d(sa + L::kABytes, &map_x, &full_bar[s], k * kBK, b.row0, pol_x);
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+    // the CTA may not exit while its last loads are in flight
+    const int64_t first = g > STAGES ? g - STAGES : 0;
+    for (int64_t j = first; j < g; ++j) mbar_wait(&full_bar[j % STAGES], (uint32_t)((j / STAGES) & 1), err);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    constexpr uint32_t idesc = make_idesc_bf16(kBM, BN);
+    int s = 0;
+    uint32_t ph = 0;
+    int j = 0;
+    bool failed = false;
+    for (int i = blockIdx.x; i < items && !failed; i += gridDim.x, ++j) {
+      const int acc = j & 1;
+      if (!mbar_wait(&tempty[acc], (uint32_t)(((j >> 1) & 1) ^ 1), err)) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+      for (int k = 0; k < k_tiles; ++k) {
+        if (!mbar_wait(&full_bar[s], ph, err)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * L::kStageBytes);
+        const uint64_t da = make_sw128_desc(sa);
+        const uint64_t db = make_sw128_desc(sa + L::kABytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+          umma_f16(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (k > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty_bar[s]);
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      umma_commit(&tfull[acc]);
+    }
+    umma_commit(drain);
+    mbar_wait(drain, 0, err);
+  } else if (warp >= 2) {
+    // ---------------- epilogue: rows of TMEM = weight rows (features), columns = tokens
+    const int lane_base = 32 * (warp & 3);
+    const int row = lane_base + lane;
+    const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
+    int j = 0;
+    for (int i = blockIdx.x; i < items; i += gridDim.x, ++j) {
+      const int acc = j & 1;
+      const bool ok = mbar_wait(&tfull[acc], (uint32_t)((j >> 1) & 1), err);
+      tc_fence_after();
+      const MoeBlock b = blocks[i / wtiles];
+      EpiParams e = ep;
+      e.out = ep.out + (size_t)b.row0 * ep.ldo;
+      e.M = b.nrows;
+      const int r_glob = (i % wtiles) * kBM + row;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(t_lane + (uint32_t)(acc * BN + c0), r);
+        tmem_wait_ld();
+        float v[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) v[q] = ok ? __uint_as_float(r[q]) : 0.f;
+        epi_store<true>(e, r_glob, c0, v);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 namespace {
 
@@ -975,6 +1131,54 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, BN);
     launch_gemm<BN, 6, false>(ma, mb, ep, a.K, a_tiles, b_tiles, full, tail_splits, stream);
   }
+}
+
+
+// ---------------------------------------------------------------- grouped MoE GEMM launcher
+template <int BN, int STAGES>
+static void launch_moe_grouped(const CUtensorMap& mw, const CUtensorMap& mx, const EpiParams& ep,
+                               const MoeBlock* blocks, const int* num_blocks, int n_per_expert, int K, int grid,
+                               cudaStream_t stream) {
+  constexpr int kSmem = STAGES * GemmSmem<BN, STAGES>::kStageBytes + (2 * STAGES + 5) * 8 + 16 + 1024;
+  auto kern = moe_grouped_swap_kernel<BN, STAGES>;
+  static int attr_dev_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    attr_dev_mask |= 1 << (dev & 31);
+  }
+  launch_kernel(kern, dim3(grid), dim3(kGemmThreads), (size_t)kSmem, stream, mw, mx, ep, blocks, num_blocks,
+                n_per_expert, (K + kBK - 1) / kBK, error_word());
+}
+
+void moe_grouped_gemm(const MoeGemmArgs& a, cudaStream_t stream) {
+  VRM_REQUIRE(a.K % 8 == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(a.x_perm) & 15) == 0,
+              "moe gemm: K must be a multiple of 8 and operands 16-byte aligned");
+  VRM_REQUIRE(a.BN == 16 || a.BN == 32 || a.BN == 64 || a.BN == 128, "moe gemm: BN must be 16, 32, 64 or 128");
+  VRM_REQUIRE(a.epilogue != kEpiSiluMul || a.N % 2 == 0, "moe gemm: silu_mul needs an even N");
+  if (a.max_blocks <= 0) return;
+  EpiParams ep;
+  ep.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  ep.ldo = (int)a.ldo;
+  ep.bias = nullptr;
+  ep.residual = nullptr;
+  ep.M = 0;
+  ep.N = a.N;
+  ep.epilogue = a.epilogue;
+  const CUtensorMap mw = make_kmajor_map(a.w, (int64_t)a.E * a.N, a.K, a.K, kBM);
+  const CUtensorMap mx = make_kmajor_map(a.x_perm, a.rows_cap, a.K, a.ldx, a.BN);
+  const int wtiles = (a.N + kBM - 1) / kBM;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)a.max_blocks * wtiles, device_sm_count()));
+  const auto* blocks = reinterpret_cast<const MoeBlock*>(a.blocks);
+  switch (a.BN) {
+    case 16: launch_moe_grouped<16, 8>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream); break;
+    case 32: launch_moe_grouped<32, 8>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream); break;
+    case 64: launch_moe_grouped<64, 6>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream); break;
+    default: launch_moe_grouped<128, 5>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream); break;
+  }
+  VRM_CUDA_CHECK(cudaGetLastError());
 }
 
 }  // namespace vrm

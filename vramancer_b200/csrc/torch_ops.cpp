@@ -509,6 +509,87 @@ Tensor tq_decompress(const Tensor& rec, const Tensor& signs) {
   return out;
 }
 
+// ---------------------------------------------------------------- mixture of experts
+// Routed experts of one MoE layer on the device: plan, gather, grouped gate/up GEMM with
+// the SiLU*up epilogue, grouped down GEMM, weighted combine (+ add, e.g. the shared
+// expert).  x [T, H], ids int64 [T, topk], weights fp32 [T, topk], gate_up [E, 2I, H]
+// (interleaved gate / up rows), down [E, H, I].  No host synchronisation.
+Tensor moe_experts(const Tensor& x, const Tensor& ids, const Tensor& weights, const Tensor& gate_up,
+                   const Tensor& down, int64_t BN, const OptT& add) {
+  check_bf16_2d(x, "moe x");
+  TORCH_CHECK(x.is_contiguous(), "moe: x must be contiguous");
+  TORCH_CHECK(ids.scalar_type() == torch::kInt64 && ids.dim() == 2 && ids.is_contiguous(), "moe: ids int64 [T, topk]");
+  TORCH_CHECK(weights.scalar_type() == torch::kFloat32 && weights.sizes() == ids.sizes() && weights.is_contiguous(),
+              "moe: weights fp32 [T, topk]");
+  TORCH_CHECK(gate_up.scalar_type() == torch::kBFloat16 && gate_up.dim() == 3 && gate_up.is_contiguous(),
+              "moe: gate_up bf16 [E, 2I, H]");
+  TORCH_CHECK(down.scalar_type() == torch::kBFloat16 && down.dim() == 3 && down.is_contiguous(), "moe: down bf16 [E, H, I]");
+  const int64_t T = x.size(0), H = x.size(1), topk = ids.size(1), E = gate_up.size(0), N1 = gate_up.size(1);
+  const int64_t I = N1 / 2;
+  TORCH_CHECK(ids.size(0) == T && gate_up.size(2) == H && down.size(0) == E && down.size(1) == H && down.size(2) == I,
+              "moe: shapes");
+  same_device(x, {&ids, &weights, &gate_up, &down}, "moe");
+  same_device_opt(x, {&add}, "moe");
+  if (has(add)) TORCH_CHECK(add->scalar_type() == torch::kBFloat16 && add->is_contiguous() && add->sizes() == x.sizes(),
+                            "moe: add must be bf16 [T, H]");
+  const int64_t P = T * topk;
+  const int64_t max_blocks = std::min<int64_t>(E, P) + (P + BN - 1) / BN;
+  const int64_t rows_cap = P + BN;
+  auto oi = x.options().dtype(torch::kInt32);
+  auto counts = torch::empty({E}, oi), offsets = torch::empty({E + 1}, oi);
+  auto row_of = torch::empty({P}, oi), tok = torch::empty({P}, oi);
+  auto blocks = torch::empty({max_blocks * 4}, oi), nblk = torch::empty({1}, oi);
+  auto x_perm = torch::empty({rows_cap, H}, x.options());
+  auto h_perm = torch::empty({rows_cap, I}, x.options());
+  auto y_perm = torch::empty({rows_cap, H}, x.options());
+  auto out = torch::empty({T, H}, x.options());
+  const c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = cur_stream();
+  vrm::MoePlanArgs pa;
+  pa.ids = ids.data_ptr<int64_t>();
+  pa.P = (int)P;
+  pa.topk = (int)topk;
+  pa.E = (int)E;
+  pa.BN = (int)BN;
+  pa.max_blocks = (int)max_blocks;
+  pa.counts = counts.data_ptr<int>();
+  pa.offsets = offsets.data_ptr<int>();
+  pa.row_of = row_of.data_ptr<int>();
+  pa.tok_of_row = tok.data_ptr<int>();
+  pa.blocks = reinterpret_cast<vrm::MoeBlock*>(blocks.data_ptr<int>());
+  pa.num_blocks = nblk.data_ptr<int>();
+  vrm::moe_plan(pa, st);
+  vrm::moe_gather(x.data_ptr(), H, tok.data_ptr<int>(), (int)P, (int)H, x_perm.data_ptr(), H, st);
+  vrm::MoeGemmArgs g;
+  g.w = gate_up.data_ptr();
+  g.E = (int)E;
+  g.N = (int)N1;
+  g.K = (int)H;
+  g.x_perm = x_perm.data_ptr();
+  g.ldx = H;
+  g.rows_cap = (int)rows_cap;
+  g.blocks = blocks.data_ptr<int>();
+  g.num_blocks = nblk.data_ptr<int>();
+  g.max_blocks = (int)max_blocks;
+  g.BN = (int)BN;
+  g.out = h_perm.data_ptr();
+  g.ldo = I;
+  g.epilogue = vrm::kEpiSiluMul;
+  vrm::moe_grouped_gemm(g, st);
+  g.w = down.data_ptr();
+  g.N = (int)H;
+  g.K = (int)I;
+  g.x_perm = h_perm.data_ptr();
+  g.ldx = I;
+  g.out = y_perm.data_ptr();
+  g.ldo = H;
+  g.epilogue = vrm::kEpiNone;
+  vrm::moe_grouped_gemm(g, st);
+  vrm::moe_combine(y_perm.data_ptr(), H, row_of.data_ptr<int>(), weights.data_ptr<float>(), (int)T, (int)topk,
+                   (int)H, has(add) ? add->data_ptr() : nullptr, out.data_ptr(), H, st);
+  return out;
+}
+
 // ---------------------------------------------------------------- page migration
 void page_copy(const Tensor& src_pool, Tensor& dst_pool, const Tensor& src_idx, const Tensor& dst_idx) {
   TORCH_CHECK(src_pool.is_cuda() && dst_pool.is_cuda() && src_pool.is_contiguous() && dst_pool.is_contiguous(),
@@ -576,6 +657,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "TurboQuant: [..., 128] -> 64-byte records (Hadamard + PolarQuant + QJL)");
   m.def("tq_decompress", &tq_decompress, py::arg("rec"), py::arg("signs"),
         "TurboQuant: 64-byte records -> bf16 [..., 128]");
+  m.def("moe_experts", &moe_experts, py::arg("x"), py::arg("ids"), py::arg("weights"), py::arg("gate_up"),
+        py::arg("down"), py::arg("BN"), py::arg("add"),
+        "routed experts of a MoE layer on the device (plan, gather, grouped tcgen05 GEMMs, combine)");
   m.def("gemm_ar_push", &gemm_ar_push, py::arg("x"), py::arg("w"), py::arg("xbuf_ptrs"), py::arg("flag_ptrs"),
         py::arg("epoch"), py::arg("done"), py::arg("rank"), py::arg("world"), py::arg("half_floats"),
         py::arg("per_thread_fence") = false,

@@ -62,6 +62,49 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
 // Debug: per-CTA timeline of the stream-K decode GEMM into buf ([ctas][8] u64 ns), null = off.
 void gemm_set_trace(void* buf);
 
+// ---------------------------------------------------------------- mixture of experts (moe.cu, gemm_tc.cu)
+// A block of <= BN consecutive rows of the expert-grouped activations, all routed to
+// one expert.
+struct MoeBlock {
+  int expert, row0, nrows, pad;
+};
+// Routing plan on the device: from expert ids [P = tokens * topk] builds counts,
+// offsets, the grouped row of every (token, k) pair, the token of every grouped row and
+// the list of BN-row blocks (*num_blocks of at most max_blocks).
+struct MoePlanArgs {
+  const int64_t* ids = nullptr;     // [P] expert of each (token, k), row-major [T, topk]
+  int P = 0, topk = 1, E = 0, BN = 16, max_blocks = 0;
+  int* counts = nullptr;            // [E]
+  int* offsets = nullptr;           // [E + 1]
+  int* row_of = nullptr;            // [P]
+  int* tok_of_row = nullptr;        // [P]
+  MoeBlock* blocks = nullptr;       // [max_blocks]
+  int* num_blocks = nullptr;        // [1]
+};
+void moe_plan(const MoePlanArgs& a, cudaStream_t stream);
+// x_perm[r] = x[tok_of_row[r]] for r < P (bf16 rows of K elements)
+void moe_gather(const void* x, int64_t ldx, const int* tok_of_row, int P, int K, void* x_perm, int64_t ld_perm,
+                cudaStream_t stream);
+// Grouped expert GEMM: out[row, :] = x_perm[row, :] @ W[expert(row)]^T for the rows of
+// every block (SiLU(gate) * up over interleaved rows with kEpiSiluMul).
+struct MoeGemmArgs {
+  const void* w = nullptr;          // bf16 [E, N, K] (K-major)
+  int E = 0, N = 0, K = 0;
+  const void* x_perm = nullptr;     // bf16 [rows_cap, K], leading dimension ldx
+  int64_t ldx = 0;
+  int rows_cap = 0;
+  const void* blocks = nullptr;     // MoeBlock [max_blocks]
+  const int* num_blocks = nullptr;
+  int max_blocks = 0, BN = 16;
+  void* out = nullptr;              // bf16 [rows_cap, N or N/2]
+  int64_t ldo = 0;
+  int epilogue = kEpiNone;
+};
+void moe_grouped_gemm(const MoeGemmArgs& a, cudaStream_t stream);
+// y[t, :] = sum_k w[t, k] * y_perm[row_of[t * topk + k], :] (+ add[t, :]), fp32 sum in k order
+void moe_combine(const void* y_perm, int64_t ld_perm, const int* row_of, const float* weights, int T, int topk,
+                 int H, const void* add, void* out, int64_t ldo, cudaStream_t stream);
+
 // ---------------------------------------------------------------- norms / rope / elementwise (norm_rope.cu)
 // out = norm(x [+ residual]); when residual != null the sum is stored back into it.
 void rmsnorm(const void* x, int64_t ldx, void* residual, const void* w, void* out, int64_t ldo, int T, int H,

@@ -24,6 +24,12 @@ from .models.transformer import DecoderModel
 from .models.weights import load_safetensors, random_weights
 
 
+def _moe_graph_safe() -> bool:
+    """True when MoE layers run on the device-scheduled grouped GEMM (no host sync)."""
+    from .parallel import moe
+    return getattr(moe, "DEVICE_MOE", False)
+
+
 def _is_checkpoint_dir(p: str) -> bool:
     return os.path.isdir(p) and any(f.endswith(".safetensors") for f in os.listdir(p))
 
@@ -65,6 +71,9 @@ class LLM:
         elif self.quantization not in (None, "none", "bf16"):
             raise ValueError(f"unsupported quantization {quantization!r} (nvfp4 or none)")
         self.weights = weights
+        if cfg.is_moe and not _moe_graph_safe():
+            # the host-driven expert loop reads routing counts back: no graph capture
+            use_cuda_graph = False
         if stream_layers > 0:
             # layer weights stay in pinned host memory, `stream_layers` layers resident
             from .engine.streaming import StreamedDecoderModel

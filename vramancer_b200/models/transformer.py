@@ -175,8 +175,8 @@ class DecoderModel:
         return self._row_parallel(a, self.lw(i, "down_w"), None, r, nxt)
 
     def _moe(self, i: int, x: torch.Tensor) -> torch.Tensor:
-        """Top-k softmax routing over SwiGLU experts (expert-parallel version in
-        parallel/expert_parallel.py)."""
+        """Top-k softmax routing over SwiGLU experts (device-scheduled grouped GEMM on
+        CUDA, parallel/moe.py)."""
         from ..parallel.moe import moe_forward
         return moe_forward(self.cfg, x, self.lw(i, "router_w"), self.lw(i, "experts_gate_up_w"),
                            self.lw(i, "experts_down_w"), shared_gate_up=self.lw(i, "shared_gate_up_w"),

@@ -1,9 +1,12 @@
 """Mixture-of-experts layer: top-k softmax router over SwiGLU experts.
 
-Single-rank path: tokens are grouped by expert (one sort) and each expert's rows run
-through the tcgen05 GEMM (gate/up with the fused SiLU*up epilogue, then down); the
-weighted outputs are scattered back.  The expert-parallel path (tokens dispatched to
-the rank that owns the expert and combined back) lives in expert_parallel.py.
+On CUDA the routed experts run on the device without a host round trip (capturable in
+the decode CUDA graph): router GEMM and top-k, then csrc/moe.cu plans the expert-grouped
+rows and token blocks, gathers the activations, the grouped tcgen05 GEMM
+(csrc/gemm_tc.cu, moe_grouped_swap_kernel) runs gate/up with the fused SiLU*up
+epilogue and down over every block, and the combine sums each token's top-k rows (plus
+the shared expert) in k order.  On the CPU (the oracle) tokens are grouped by expert
+with one sort and each expert runs as a dense MLP.
 
 Reference parity: the reference has no MoE of its own (vLLM / llama.cpp only, plus
 the expert placement hooks of core/expert_pinning.py:115-642).
@@ -16,6 +19,8 @@ import torch
 
 from .. import ops
 from ..models.config import ModelConfig
+
+DEVICE_MOE = True       # CUDA MoE layers need no host synchronisation (graph-capturable)
 
 
 def route(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -39,6 +44,9 @@ def moe_forward(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor, exper
                 shared_gate: Optional[torch.Tensor] = None,
                 expert_offset: int = 0) -> torch.Tensor:
     """x [T, H] -> [T, H].  experts_* hold experts [expert_offset, expert_offset + E_local)."""
+    if x.is_cuda and expert_offset == 0 and experts_gate_up.shape[0] == cfg.num_experts:
+        return _moe_device(cfg, x, router_w, experts_gate_up, experts_down, shared_gate_up, shared_down,
+                           shared_gate)
     T, H = x.shape
     w, ids = route(cfg, x, router_w)
     out = torch.zeros(T, H, dtype=torch.float32, device=x.device)
@@ -67,3 +75,27 @@ def moe_forward(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor, exper
             ys = ys * torch.sigmoid(ops.linear(x, shared_gate).float())
         out += ys
     return out.to(x.dtype)
+
+
+def moe_block_rows(tokens: int, topk: int, experts: int) -> int:
+    """Token rows per block of the grouped GEMM: the average rows per expert, rounded
+    up to an MMA width (16 / 32 / 64 / 128)."""
+    avg = -(-tokens * topk // max(1, experts))
+    for bn in (16, 32, 64):
+        if avg <= bn:
+            return bn
+    return 128
+
+
+def _moe_device(cfg: ModelConfig, x: torch.Tensor, router_w, gate_up, down, shared_gate_up, shared_down,
+                shared_gate) -> torch.Tensor:
+    w, ids = route(cfg, x, router_w)
+    add = None
+    if shared_gate_up is not None:
+        ys = expert_mlp(x, shared_gate_up, shared_down)
+        if shared_gate is not None:
+            ys = (ys.float() * torch.sigmoid(ops.linear(x, shared_gate).float())).to(x.dtype)
+        add = ys.contiguous()
+    bn = moe_block_rows(x.shape[0], cfg.experts_per_token, cfg.num_experts)
+    return ops.native().moe_experts(x.contiguous(), ids.contiguous(), w.float().contiguous(), gate_up.contiguous(),
+                                    down.contiguous(), bn, add)
