@@ -246,6 +246,42 @@ def _moe_fp32_reference(x, ids, w, gu, dn, add=None):
     return out if add is None else out + add
 
 
+@pytest.mark.parametrize("T,E,topk,BN", [(7, 128, 8, 16), (64, 16, 4, 32), (300, 8, 2, 128), (1, 4, 1, 16)])
+def test_moe_plan(T, E, topk, BN, cuda_errors_clean):
+    g = torch.Generator().manual_seed(T)
+    ids = torch.stack([torch.randperm(E, generator=g)[:topk] for _ in range(T)]).to(DEV)
+    counts, offsets, row_of, tok, blocks, nblk = ops.native().moe_plan(ids, E, BN)
+    flat = ids.flatten().cpu()
+    c_ref = torch.bincount(flat, minlength=E)
+    off_ref = torch.cat([torch.zeros(1, dtype=torch.long), c_ref.cumsum(0)])
+    assert torch.equal(counts.cpu().long(), c_ref) and torch.equal(offsets.cpu().long(), off_ref)
+    ro, tk = row_of.cpu().long(), tok.cpu().long()
+    assert sorted(ro.tolist()) == list(range(T * topk))
+    for p in range(T * topk):
+        assert off_ref[flat[p]] <= ro[p] < off_ref[flat[p] + 1] and tk[ro[p]] == p // topk
+    want = [[e, int(off_ref[e]) + r0, min(BN, int(c_ref[e]) - r0)] for e in range(E) for r0 in range(0, int(c_ref[e]), BN)]
+    assert blocks.cpu()[:int(nblk.item()), :3].tolist() == want
+
+
+@pytest.mark.parametrize("epi", [0, 1])
+def test_moe_grouped_linear(epi, cuda_errors_clean):
+    """The grouped GEMM over a plan against a per-row fp32 product with that row's expert."""
+    T, E, topk, H, N, BN = 40, 16, 4, 512, 384, 16
+    g = torch.Generator().manual_seed(3)
+    ids = torch.stack([torch.randperm(E, generator=g)[:topk] for _ in range(T)]).to(DEV)
+    _, offsets, _, _, blocks, nblk = ops.native().moe_plan(ids, E, BN)
+    P = T * topk
+    xp = (torch.randn(P + BN, H, generator=g) * 0.5).to(DEV, torch.bfloat16)
+    w = (torch.randn(E, N, H, generator=g) * 0.05).to(DEV, torch.bfloat16)
+    out = ops.native().moe_grouped_linear(xp, w, blocks, nblk, BN, epi)
+    off = offsets.cpu().tolist()
+    for e in range(E):
+        y = xp[off[e]:off[e + 1]].float() @ w[e].float().t()
+        if epi == 1:
+            y = torch.nn.functional.silu(y[:, 0::2]) * y[:, 1::2]
+        _close(out[off[e]:off[e + 1]], y, rtol=2e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("T,E,topk,H,I", [(1, 8, 2, 256, 128), (32, 64, 8, 1024, 384), (200, 16, 4, 512, 256),
                                          (7, 128, 8, 2048, 768)])
 def test_moe_device_matches_fp32(T, E, topk, H, I, cuda_errors_clean):
@@ -271,6 +307,32 @@ def test_moe_device_matches_fp32(T, E, topk, H, I, cuda_errors_clean):
     _close(got_s, ref + c(shared), rtol=3e-2, atol=3e-2)
     # repeated calls give identical bits (grouped row order may vary, the sums do not)
     assert torch.equal(moe.moe_forward(cfg, x, router, gu, dn), got)
+
+
+def test_moe_back_to_back_calls(cuda_errors_clean):
+    """Many MoE layers of changing shapes back to back, no synchronisation between them:
+    the plan is read up to four kernels after it is written by grids launched early
+    (programmatic dependent launch), which must still see the finished plan."""
+    from vramancer_b200.models.config import get_config
+    from vramancer_b200.parallel import moe
+    g = torch.Generator().manual_seed(11)
+    outs = []
+    for i, (T, E, topk, H, I) in enumerate([(7, 128, 8, 1024, 768), (7, 128, 8, 2048, 384), (33, 64, 4, 512, 256),
+                                            (1, 128, 8, 1024, 384), (96, 16, 2, 512, 128)] * 3):
+        cfg = get_config("tiny-moe").with_(hidden_size=H, num_experts=E, experts_per_token=topk,
+                                           expert_intermediate_size=I)
+        x = (torch.randn(T, H, generator=g) * 0.5).to(DEV, torch.bfloat16)
+        router = (torch.randn(E, H, generator=g) * 0.05).to(DEV, torch.bfloat16)
+        gu = (torch.randn(E, 2 * I, H, generator=g) * 0.03).to(DEV, torch.bfloat16)
+        dn = (torch.randn(E, H, I, generator=g) * 0.03).to(DEV, torch.bfloat16)
+        w, ids = moe.route(cfg, x, router)
+        outs.append((moe.moe_forward(cfg, x, router, gu, dn), x, ids, w, gu, dn))
+    torch.cuda.synchronize()
+    for got, x, ids, w, gu, dn in outs:
+        y = torch.einsum("tkoh,th->tko", gu[ids].float(), x.float())
+        h = torch.nn.functional.silu(y[..., 0::2]) * y[..., 1::2]
+        ref = (torch.einsum("tkhi,tki->tkh", dn[ids].float(), h) * w.unsqueeze(-1)).sum(1)
+        _close(got, ref, rtol=3e-2, atol=3e-2)
 
 
 def test_moe_model_decodes_under_cuda_graphs(cuda_errors_clean):

@@ -691,10 +691,15 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 // <= BN tokens over the full K; persistent CTAs take items round-robin, with double TMEM
 // accumulators so one item's epilogue overlaps the next item's MMAs.  Everything the
 // CTAs need comes from the device, so the launch has a fixed grid and no host sync.
+__device__ __forceinline__ MoeBlock load_block(const MoeBlock* blocks, int i) {
+  const int4 v = reinterpret_cast<const int4*>(blocks)[i];
+  return MoeBlock{v.x, v.y, v.z, v.w};
+}
+
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_grouped_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
-                            EpiParams ep, const MoeBlock* __restrict__ blocks, const int* __restrict__ num_blocks,
+                            EpiParams ep, const MoeBlock* blocks, const int* num_blocks,
                             int n_per_expert, int k_tiles, uint32_t* __restrict__ err) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -732,7 +737,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_wait();                        // the work list and x_perm come from the previous kernels
+  pdl_wait_for(blocks, num_blocks);  // the work list and x_perm come from earlier kernels
   const int wtiles = (n_per_expert + kBM - 1) / kBM;
   const int items = *num_blocks * wtiles;
 
@@ -745,7 +750,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int64_t g = 0;
     bool failed = false;
     for (int i = blockIdx.x; i < items && !failed; i += gridDim.x) {
-      const MoeBlock b = blocks[i / wtiles];
+      const MoeBlock b = load_block(blocks, i / wtiles);
       const int wrow = b.expert * n_per_expert + (i % wtiles) * kBM;
       for (int k = 0; k < k_tiles; ++k, ++g) {
         if (g >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1u, err)) {
@@ -809,7 +814,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int acc = j & 1;
       const bool ok = mbar_wait(&tfull[acc], (uint32_t)((j >> 1) & 1), err);
       tc_fence_after();
-      const MoeBlock b = blocks[i / wtiles];
+      const MoeBlock b = load_block(blocks, i / wtiles);
       EpiParams e = ep;
       e.out = ep.out + (size_t)b.row0 * ep.ldo;
       e.M = b.nrows;

@@ -25,7 +25,7 @@ __global__ void __launch_bounds__(kCopyThreads)
     page_copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, const int* __restrict__ src_idx,
                      const int* __restrict__ dst_idx, int n_pages, long long page_vecs) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(src, src_idx, dst_idx);
   const long long chunks_per_page = (page_vecs + kChunkVecs - 1) / kChunkVecs;
   const long long total = (long long)n_pages * chunks_per_page;
   for (long long w = blockIdx.x; w < total; w += gridDim.x) {

@@ -7,6 +7,12 @@
 // runs; every grouped row is computed independently and the combine sums each token's
 // top-k rows in k order, so the layer output does not depend on it.
 //
+// Ordering under programmatic dependent launch: the plan is consumed up to four
+// kernels later (gather, both grouped GEMMs, combine), by grids that the chain of
+// early triggers may have launched before the plan kernel finished.  That is safe as
+// long as no load of plan data is scheduled above griddepcontrol.wait, which is what
+// pdl_wait_for() guarantees for the pointers it is given.
+//
 // Reference parity: the reference has no MoE kernels (it defers MoE to vLLM /
 // llama.cpp); its expert placement hook is core/expert_pinning.py:115-642.
 #include "vrm_common.cuh"
@@ -65,7 +71,7 @@ __global__ void __launch_bounds__(kPlanThreads) moe_plan_kernel(MoePlanArgs a, u
 __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const int* __restrict__ tok,
                                   int K, __nv_bfloat16* __restrict__ xp, int64_t ldp) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(x, tok);
   const int r = blockIdx.x;
   const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok[r] * ldx);
   uint4* dst = reinterpret_cast<uint4*>(xp + (size_t)r * ldp);
@@ -78,7 +84,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ yp, int64_t
                                    const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out,
                                    int64_t ldo) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(yp, row_of, w, add);
   const int t = blockIdx.x;
   for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -128,7 +134,7 @@ void moe_gather(const void* x, int64_t ldx, const int* tok_of_row, int P, int K,
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
-void moe_combine(const void* y_perm, int64_t ld_perm, const int* row_of, const float* weights, int T, int topk,
+void moe_combine(const void* y_perm, int64_t ld_perm, const int* __restrict__ row_of, const float* weights, int T, int topk,
                  int H, const void* add, void* out, int64_t ldo, cudaStream_t st) {
   VRM_REQUIRE(H % 8 == 0 && ld_perm % 8 == 0 && ldo % 8 == 0, "moe_combine: rows must be 16-byte multiples");
   if (T <= 0) return;

@@ -70,7 +70,7 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat1
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int H, int64_t ldx,
                                int64_t ldo, float eps) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(x, w);
   __shared__ float red[33];
   const int row = blockIdx.x;
   const int nvec = H / 8;
@@ -104,7 +104,7 @@ __global__ void layernorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloa
                                  const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ b,
                                  __nv_bfloat16* __restrict__ out, int H, int64_t ldx, int64_t ldo, float eps) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(x, w, b);
   __shared__ float red[33];
   const int row = blockIdx.x;
   const int nvec = H / 8;
@@ -257,7 +257,7 @@ void rope_kv_write(const RopeKvArgs& a, cudaStream_t st) {
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out, int I,
                                 int64_t ldx, int64_t ldo) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(x);
   const int t = blockIdx.y;
   const int v = blockIdx.x * blockDim.x + threadIdx.x;   // vector of 8
   if (v * 8 >= I) return;
@@ -309,7 +309,7 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat1
                                  const int* __restrict__ pos, const __nv_bfloat16* __restrict__ pos_table,
                                  __nv_bfloat16* __restrict__ out, int H) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(ids, table, pos, pos_table);
   const int t = blockIdx.x;
   const __nv_bfloat16* src = table + (size_t)ids[t] * H;
   const __nv_bfloat16* psrc = pos_table ? pos_table + (size_t)pos[t] * H : nullptr;
@@ -337,7 +337,7 @@ void embedding(const int* ids, const void* table, const int* pos, const void* po
 
 __global__ void add_inplace_kernel(__nv_bfloat16* __restrict__ a, const __nv_bfloat16* __restrict__ b, size_t n) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(b);
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) a[i] = __float2bfloat16(__bfloat162float(a[i]) + __bfloat162float(b[i]));
 }

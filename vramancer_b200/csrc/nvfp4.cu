@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(256) nvfp4_dequant_kernel(const uint8_t* __res
                                                             __nv_bfloat16* __restrict__ out) {
   __shared__ __align__(16) __nv_bfloat16 tile_s[8][16][64 + 8];
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(q, s, gsp);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = K / 64;
   const int64_t st = (int64_t)blockIdx.x * 8 + warp;

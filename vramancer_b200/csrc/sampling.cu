@@ -117,7 +117,7 @@ __device__ ArgBest row_argmax(const __nv_bfloat16* __restrict__ x, int V, ArgBes
 __global__ void __launch_bounds__(kSampThreads)
     argmax_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V, int* __restrict__ out) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(logits);
   __shared__ ArgBest sh[32];
   const int row = blockIdx.x;
   const __nv_bfloat16* x = logits + (size_t)row * ld;
@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kSampThreads)
                   const int* __restrict__ top_k, const float* __restrict__ top_p, uint64_t seed,
                   const int* __restrict__ steps, int* __restrict__ out) {
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(logits, temperature, top_k, top_p, steps);
   __shared__ ArgBest sh[32];
   __shared__ float shf[32];
   __shared__ float hist[256];

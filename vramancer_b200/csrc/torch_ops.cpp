@@ -514,6 +514,68 @@ Tensor tq_decompress(const Tensor& rec, const Tensor& signs) {
 // the SiLU*up epilogue, grouped down GEMM, weighted combine (+ add, e.g. the shared
 // expert).  x [T, H], ids int64 [T, topk], weights fp32 [T, topk], gate_up [E, 2I, H]
 // (interleaved gate / up rows), down [E, H, I].  No host synchronisation.
+// Expert plan of a MoE layer: per-expert counts and row offsets, the grouped row of every
+// (token, k) pair, the token of every grouped row and the list of token blocks
+// (expert, first row, rows, 0) that drives the grouped GEMM.
+std::vector<Tensor> moe_plan_op(const Tensor& ids, int64_t E, int64_t BN) {
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == torch::kInt64 && ids.dim() == 2 && ids.is_contiguous(),
+              "moe: ids int64 [T, topk]");
+  const int64_t P = ids.numel();
+  const int64_t max_blocks = std::min<int64_t>(E, P) + (P + BN - 1) / BN;
+  auto oi = ids.options().dtype(torch::kInt32);
+  auto counts = torch::empty({E}, oi), offsets = torch::empty({E + 1}, oi);
+  auto row_of = torch::empty({P}, oi), tok = torch::empty({P}, oi);
+  auto blocks = torch::empty({std::max<int64_t>(1, max_blocks), 4}, oi), nblk = torch::zeros({1}, oi);
+  const c10::cuda::CUDAGuard guard(ids.device());
+  vrm::MoePlanArgs pa;
+  pa.ids = ids.data_ptr<int64_t>();
+  pa.P = (int)P;
+  pa.topk = (int)ids.size(1);
+  pa.E = (int)E;
+  pa.BN = (int)BN;
+  pa.max_blocks = (int)max_blocks;
+  pa.counts = counts.data_ptr<int>();
+  pa.offsets = offsets.data_ptr<int>();
+  pa.row_of = row_of.data_ptr<int>();
+  pa.tok_of_row = tok.data_ptr<int>();
+  pa.blocks = reinterpret_cast<vrm::MoeBlock*>(blocks.data_ptr<int>());
+  pa.num_blocks = nblk.data_ptr<int>();
+  vrm::moe_plan(pa, cur_stream());
+  return {counts, offsets, row_of, tok, blocks, nblk};
+}
+
+// Grouped expert GEMM over a plan: out[r] = x_perm[r] @ w[expert(r)].T for every row r
+// of every block (epilogue 1: SiLU(gate)*up over interleaved weight-row pairs).
+Tensor moe_grouped_linear(const Tensor& x_perm, const Tensor& w, const Tensor& blocks, const Tensor& nblk, int64_t BN,
+                          int64_t epilogue) {
+  check_bf16_2d(x_perm, "moe x_perm");
+  TORCH_CHECK(w.scalar_type() == torch::kBFloat16 && w.dim() == 3 && w.is_contiguous() && w.size(2) == x_perm.size(1),
+              "moe: w bf16 [E, N, K]");
+  TORCH_CHECK(blocks.scalar_type() == torch::kInt32 && blocks.dim() == 2 && blocks.size(1) == 4 && blocks.is_contiguous(),
+              "moe: blocks int32 [max_blocks, 4]");
+  same_device(x_perm, {&w, &blocks, &nblk}, "moe");
+  const int64_t N = epilogue == vrm::kEpiSiluMul ? w.size(1) / 2 : w.size(1);
+  auto out = torch::empty({x_perm.size(0), N}, x_perm.options());
+  const c10::cuda::CUDAGuard guard(x_perm.device());
+  vrm::MoeGemmArgs g;
+  g.w = w.data_ptr();
+  g.E = (int)w.size(0);
+  g.N = (int)w.size(1);
+  g.K = (int)w.size(2);
+  g.x_perm = x_perm.data_ptr();
+  g.ldx = x_perm.stride(0);
+  g.rows_cap = (int)x_perm.size(0);
+  g.blocks = blocks.data_ptr<int>();
+  g.num_blocks = nblk.data_ptr<int>();
+  g.max_blocks = (int)blocks.size(0);
+  g.BN = (int)BN;
+  g.out = out.data_ptr();
+  g.ldo = N;
+  g.epilogue = (int)epilogue;
+  vrm::moe_grouped_gemm(g, cur_stream());
+  return out;
+}
+
 Tensor moe_experts(const Tensor& x, const Tensor& ids, const Tensor& weights, const Tensor& gate_up,
                    const Tensor& down, int64_t BN, const OptT& add) {
   check_bf16_2d(x, "moe x");
@@ -533,59 +595,16 @@ Tensor moe_experts(const Tensor& x, const Tensor& ids, const Tensor& weights, co
   if (has(add)) TORCH_CHECK(add->scalar_type() == torch::kBFloat16 && add->is_contiguous() && add->sizes() == x.sizes(),
                             "moe: add must be bf16 [T, H]");
   const int64_t P = T * topk;
-  const int64_t max_blocks = std::min<int64_t>(E, P) + (P + BN - 1) / BN;
-  const int64_t rows_cap = P + BN;
-  auto oi = x.options().dtype(torch::kInt32);
-  auto counts = torch::empty({E}, oi), offsets = torch::empty({E + 1}, oi);
-  auto row_of = torch::empty({P}, oi), tok = torch::empty({P}, oi);
-  auto blocks = torch::empty({max_blocks * 4}, oi), nblk = torch::empty({1}, oi);
-  auto x_perm = torch::empty({rows_cap, H}, x.options());
-  auto h_perm = torch::empty({rows_cap, I}, x.options());
-  auto y_perm = torch::empty({rows_cap, H}, x.options());
-  auto out = torch::empty({T, H}, x.options());
+  auto plan = moe_plan_op(ids, E, BN);
   const c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t st = cur_stream();
-  vrm::MoePlanArgs pa;
-  pa.ids = ids.data_ptr<int64_t>();
-  pa.P = (int)P;
-  pa.topk = (int)topk;
-  pa.E = (int)E;
-  pa.BN = (int)BN;
-  pa.max_blocks = (int)max_blocks;
-  pa.counts = counts.data_ptr<int>();
-  pa.offsets = offsets.data_ptr<int>();
-  pa.row_of = row_of.data_ptr<int>();
-  pa.tok_of_row = tok.data_ptr<int>();
-  pa.blocks = reinterpret_cast<vrm::MoeBlock*>(blocks.data_ptr<int>());
-  pa.num_blocks = nblk.data_ptr<int>();
-  vrm::moe_plan(pa, st);
-  vrm::moe_gather(x.data_ptr(), H, tok.data_ptr<int>(), (int)P, (int)H, x_perm.data_ptr(), H, st);
-  vrm::MoeGemmArgs g;
-  g.w = gate_up.data_ptr();
-  g.E = (int)E;
-  g.N = (int)N1;
-  g.K = (int)H;
-  g.x_perm = x_perm.data_ptr();
-  g.ldx = H;
-  g.rows_cap = (int)rows_cap;
-  g.blocks = blocks.data_ptr<int>();
-  g.num_blocks = nblk.data_ptr<int>();
-  g.max_blocks = (int)max_blocks;
-  g.BN = (int)BN;
-  g.out = h_perm.data_ptr();
-  g.ldo = I;
-  g.epilogue = vrm::kEpiSiluMul;
-  vrm::moe_grouped_gemm(g, st);
-  g.w = down.data_ptr();
-  g.N = (int)H;
-  g.K = (int)I;
-  g.x_perm = h_perm.data_ptr();
-  g.ldx = I;
-  g.out = y_perm.data_ptr();
-  g.ldo = H;
-  g.epilogue = vrm::kEpiNone;
-  vrm::moe_grouped_gemm(g, st);
-  vrm::moe_combine(y_perm.data_ptr(), H, row_of.data_ptr<int>(), weights.data_ptr<float>(), (int)T, (int)topk,
+  // rows past the last block are read by the last block's TMA box (BN rows) and discarded
+  auto x_perm = torch::empty({P + BN, H}, x.options());
+  vrm::moe_gather(x.data_ptr(), H, plan[3].data_ptr<int>(), (int)P, (int)H, x_perm.data_ptr(), H, st);
+  auto h_perm = moe_grouped_linear(x_perm, gate_up, plan[4], plan[5], BN, vrm::kEpiSiluMul);
+  auto y_perm = moe_grouped_linear(h_perm, down, plan[4], plan[5], BN, vrm::kEpiNone);
+  auto out = torch::empty({T, H}, x.options());
+  vrm::moe_combine(y_perm.data_ptr(), H, plan[2].data_ptr<int>(), weights.data_ptr<float>(), (int)T, (int)topk,
                    (int)H, has(add) ? add->data_ptr() : nullptr, out.data_ptr(), H, st);
   return out;
 }
@@ -657,6 +676,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "TurboQuant: [..., 128] -> 64-byte records (Hadamard + PolarQuant + QJL)");
   m.def("tq_decompress", &tq_decompress, py::arg("rec"), py::arg("signs"),
         "TurboQuant: 64-byte records -> bf16 [..., 128]");
+  m.def("moe_plan", &moe_plan_op, py::arg("ids"), py::arg("E"), py::arg("BN"),
+        "MoE expert plan: counts, offsets, row_of, tok_of_row, blocks [max_blocks, 4], num_blocks");
+  m.def("moe_grouped_linear", &moe_grouped_linear, py::arg("x_perm"), py::arg("w"), py::arg("blocks"),
+        py::arg("num_blocks"), py::arg("BN"), py::arg("epilogue"), "grouped expert GEMM over a MoE plan");
   m.def("moe_experts", &moe_experts, py::arg("x"), py::arg("ids"), py::arg("weights"), py::arg("gate_up"),
         py::arg("down"), py::arg("BN"), py::arg("add"),
         "routed experts of a MoE layer on the device (plan, gather, grouped tcgen05 GEMMs, combine)");

@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kTqWarps * 32) tq_compress_kernel(const T* __r
   pdl_launch();
   for (int i = threadIdx.x; i < kTqM * kTqD; i += blockDim.x) s_jl[i / kTqD][i % kTqD] = jl[i];
   for (int i = threadIdx.x; i < kTqD; i += blockDim.x) s_sign[i] = signs[i];
-  pdl_wait();
+  pdl_wait_for(x, signs, jl);
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* idx = s_idx[warp];
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kTqWarps * 32) tq_decompress_kernel(const uint
   __shared__ __align__(16) uint8_t s_rec[kTqWarps][kTqRec];
   __shared__ uint8_t s_idx[kTqWarps][kTqD];
   pdl_launch();
-  pdl_wait();
+  pdl_wait_for(rec_in, signs);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* rec = s_rec[warp];
   uint8_t* idx = s_idx[warp];

@@ -248,6 +248,25 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// A load through a `const T* __restrict__` kernel parameter may be compiled as an
+// invariant, non-coherent load, and the compiler may then schedule it above
+// griddepcontrol.wait, i.e. before the kernel that writes the data has finished (on
+// B200 this showed up as a MoE work list read three kernels after it was written).
+// pdl_wait_for(p...) waits and then passes each pointer through an opaque asm that is
+// ordered after the wait, so every load through them is an ordinary load below it.
+// Use it for every pointer to data that an earlier kernel writes.
+template <typename P>
+__device__ __forceinline__ void opaque_after_wait(P& p) {
+  unsigned long long v = reinterpret_cast<unsigned long long>(p);
+  asm volatile("" : "+l"(v)::"memory");
+  p = reinterpret_cast<P>(v);
+}
+template <typename... P>
+__device__ __forceinline__ void pdl_wait_for(P&... p) {
+  pdl_wait();
+  (opaque_after_wait(p), ...);
+}
+
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
