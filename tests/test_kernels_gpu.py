@@ -263,6 +263,58 @@ def test_moe_plan(T, E, topk, BN, cuda_errors_clean):
     assert blocks.cpu()[:int(nblk.item()), :3].tolist() == want
 
 
+@pytest.mark.parametrize("T,E,topk", [(1, 8, 2), (128, 128, 8), (300, 64, 4), (77, 256, 8), (5, 1000, 3),
+                                      (129, 16, 1)])
+def test_moe_route_matches_torch(T, E, topk, cuda_errors_clean):
+    """Device softmax / top-k / renormalisation (fused with the plan up to 128 tokens)
+    against torch in fp32 on the same bf16 logits."""
+    g = torch.Generator().manual_seed(T * E)
+    logits = (torch.randn(T, E, generator=g) * 2).to(DEV, torch.bfloat16)
+    ids, w, counts, offsets, row_of, tok, blocks, nblk = ops.native().moe_route(logits, topk, True, 16)
+    probs = torch.softmax(logits.float(), -1)
+    rw, rids = torch.topk(probs, topk, dim=-1)
+    rw = rw / rw.sum(-1, keepdim=True)
+    same = ids == rids
+    if not bool(same.all()):
+        # only exact ties (bf16 logits) may order differently
+        pv = probs.gather(1, ids)
+        assert torch.allclose(pv, probs.gather(1, rids), rtol=0, atol=1e-7)
+    torch.testing.assert_close(w.sort(-1).values, rw.sort(-1).values, rtol=1e-5, atol=1e-6)
+    c_ref = torch.bincount(ids.flatten().cpu(), minlength=E)
+    assert torch.equal(counts.cpu().long(), c_ref)
+    ro = row_of.cpu().long()
+    assert sorted(ro.tolist()) == list(range(T * topk))
+    assert torch.equal(tok.cpu().long()[ro], torch.arange(T * topk) // topk)
+    off = torch.cat([torch.zeros(1, dtype=torch.long), c_ref.cumsum(0)])
+    want = [[e, int(off[e]) + r0, min(16, int(c_ref[e]) - r0)] for e in range(E) for r0 in range(0, int(c_ref[e]), 16)]
+    assert blocks.cpu()[:int(nblk.item()), :3].tolist() == want
+
+
+def test_moe_layer_fused_residual_norm(cuda_errors_clean):
+    """r += MoE(x) in place and the next RMSNorm, fused into the combine."""
+    from vramancer_b200.models.config import get_config
+    from vramancer_b200.parallel import moe
+    T, E, topk, H, I = 48, 32, 4, 1024, 256
+    cfg = get_config("tiny-moe").with_(hidden_size=H, num_experts=E, experts_per_token=topk,
+                                       expert_intermediate_size=I)
+    g = torch.Generator().manual_seed(5)
+    bf = lambda t: t.to(DEV, torch.bfloat16)  # noqa: E731
+    x, router = bf(torch.randn(T, H, generator=g) * 0.5), bf(torch.randn(E, H, generator=g) * 0.05)
+    gu, dn = bf(torch.randn(E, 2 * I, H, generator=g) * 0.03), bf(torch.randn(E, H, I, generator=g) * 0.03)
+    r0, nw = bf(torch.randn(T, H, generator=g)), bf(torch.rand(H, generator=g) + 0.5)
+    y = moe.moe_forward(cfg, x, router, gu, dn).float()
+    r = r0.clone()
+    xn = moe.moe_forward(cfg, x, router, gu, dn, residual=r, norm_w=nw)
+    r_ref = r0.float() + y
+    _close(r, r_ref, rtol=2e-2, atol=2e-2)
+    rr = r.float()
+    xn_ref = rr * torch.rsqrt(rr.pow(2).mean(-1, keepdim=True) + cfg.norm_eps) * nw.float()
+    _close(xn, xn_ref, rtol=2e-2, atol=2e-2)
+    r2 = r0.clone()
+    assert moe.moe_forward(cfg, x, router, gu, dn, residual=r2) is None
+    assert torch.equal(r2, r)
+
+
 @pytest.mark.parametrize("epi", [0, 1])
 def test_moe_grouped_linear(epi, cuda_errors_clean):
     """The grouped GEMM over a plan against a per-row fp32 product with that row's expert."""

@@ -517,31 +517,74 @@ Tensor tq_decompress(const Tensor& rec, const Tensor& signs) {
 // Expert plan of a MoE layer: per-expert counts and row offsets, the grouped row of every
 // (token, k) pair, the token of every grouped row and the list of token blocks
 // (expert, first row, rows, 0) that drives the grouped GEMM.
+struct MoePlanT {
+  Tensor counts, offsets, row_of, tok, blocks, nblk;
+  int64_t max_blocks;
+};
+
+MoePlanT moe_plan_alloc(const torch::TensorOptions& o, int64_t E, int64_t P, int64_t BN) {
+  MoePlanT t;
+  t.max_blocks = std::min<int64_t>(E, P) + (P + BN - 1) / BN;
+  auto oi = o.dtype(torch::kInt32);
+  t.counts = torch::empty({E}, oi);
+  t.offsets = torch::empty({E + 1}, oi);
+  t.row_of = torch::empty({std::max<int64_t>(P, 1)}, oi);
+  t.tok = torch::empty({std::max<int64_t>(P, 1)}, oi);
+  t.blocks = torch::empty({std::max<int64_t>(1, t.max_blocks), 4}, oi);
+  t.nblk = torch::zeros({1}, oi);
+  return t;
+}
+
+vrm::MoePlanArgs moe_plan_args(MoePlanT& t, int64_t P, int64_t topk, int64_t E, int64_t BN) {
+  vrm::MoePlanArgs pa;
+  pa.P = (int)P;
+  pa.topk = (int)topk;
+  pa.E = (int)E;
+  pa.BN = (int)BN;
+  pa.max_blocks = (int)t.max_blocks;
+  pa.counts = t.counts.data_ptr<int>();
+  pa.offsets = t.offsets.data_ptr<int>();
+  pa.row_of = t.row_of.data_ptr<int>();
+  pa.tok_of_row = t.tok.data_ptr<int>();
+  pa.blocks = reinterpret_cast<vrm::MoeBlock*>(t.blocks.data_ptr<int>());
+  pa.num_blocks = t.nblk.data_ptr<int>();
+  return pa;
+}
+
 std::vector<Tensor> moe_plan_op(const Tensor& ids, int64_t E, int64_t BN) {
   TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == torch::kInt64 && ids.dim() == 2 && ids.is_contiguous(),
               "moe: ids int64 [T, topk]");
   const int64_t P = ids.numel();
-  const int64_t max_blocks = std::min<int64_t>(E, P) + (P + BN - 1) / BN;
-  auto oi = ids.options().dtype(torch::kInt32);
-  auto counts = torch::empty({E}, oi), offsets = torch::empty({E + 1}, oi);
-  auto row_of = torch::empty({P}, oi), tok = torch::empty({P}, oi);
-  auto blocks = torch::empty({std::max<int64_t>(1, max_blocks), 4}, oi), nblk = torch::zeros({1}, oi);
   const c10::cuda::CUDAGuard guard(ids.device());
-  vrm::MoePlanArgs pa;
-  pa.ids = ids.data_ptr<int64_t>();
-  pa.P = (int)P;
-  pa.topk = (int)ids.size(1);
-  pa.E = (int)E;
-  pa.BN = (int)BN;
-  pa.max_blocks = (int)max_blocks;
-  pa.counts = counts.data_ptr<int>();
-  pa.offsets = offsets.data_ptr<int>();
-  pa.row_of = row_of.data_ptr<int>();
-  pa.tok_of_row = tok.data_ptr<int>();
-  pa.blocks = reinterpret_cast<vrm::MoeBlock*>(blocks.data_ptr<int>());
-  pa.num_blocks = nblk.data_ptr<int>();
+  auto t = moe_plan_alloc(ids.options(), E, P, BN);
+  auto pa = moe_plan_args(t, P, ids.size(1), E, BN);
+  pa.ids64 = ids.data_ptr<int64_t>();
   vrm::moe_plan(pa, cur_stream());
-  return {counts, offsets, row_of, tok, blocks, nblk};
+  return {t.counts, t.offsets, t.row_of, t.tok, t.blocks, t.nblk};
+}
+
+// Router on the device: softmax / top-k / renormalisation of bf16 logits [T, E] and the
+// plan.  Returns ids (int64), weights (fp32) and the plan tensors.
+std::vector<Tensor> moe_route_op(const Tensor& logits, int64_t topk, bool norm_topk, int64_t BN) {
+  check_bf16_2d(logits, "moe logits");
+  const int64_t T = logits.size(0), E = logits.size(1), P = T * topk;
+  const c10::cuda::CUDAGuard guard(logits.device());
+  auto t = moe_plan_alloc(logits.options(), E, P, BN);
+  auto ids32 = torch::empty({T, topk}, logits.options().dtype(torch::kInt32));
+  auto ids64 = torch::empty({T, topk}, logits.options().dtype(torch::kInt64));
+  auto w = torch::empty({T, topk}, logits.options().dtype(torch::kFloat32));
+  vrm::MoeRouteArgs ra;
+  ra.logits = logits.data_ptr();
+  ra.ldl = logits.stride(0);
+  ra.T = (int)T;
+  ra.norm_topk = norm_topk;
+  ra.ids32 = ids32.data_ptr<int>();
+  ra.ids64 = ids64.data_ptr<int64_t>();
+  ra.weights = w.data_ptr<float>();
+  ra.plan = moe_plan_args(t, P, topk, E, BN);
+  ra.plan.ids32 = ra.ids32;
+  vrm::moe_route(ra, cur_stream());
+  return {ids64, w, t.counts, t.offsets, t.row_of, t.tok, t.blocks, t.nblk};
 }
 
 // Grouped expert GEMM over a plan: out[r] = x_perm[r] @ w[expert(r)].T for every row r
@@ -576,37 +619,99 @@ Tensor moe_grouped_linear(const Tensor& x_perm, const Tensor& w, const Tensor& b
   return out;
 }
 
-Tensor moe_experts(const Tensor& x, const Tensor& ids, const Tensor& weights, const Tensor& gate_up,
-                   const Tensor& down, int64_t BN, const OptT& add) {
+void check_moe_weights(const Tensor& x, const Tensor& gate_up, const Tensor& down) {
   check_bf16_2d(x, "moe x");
   TORCH_CHECK(x.is_contiguous(), "moe: x must be contiguous");
-  TORCH_CHECK(ids.scalar_type() == torch::kInt64 && ids.dim() == 2 && ids.is_contiguous(), "moe: ids int64 [T, topk]");
-  TORCH_CHECK(weights.scalar_type() == torch::kFloat32 && weights.sizes() == ids.sizes() && weights.is_contiguous(),
-              "moe: weights fp32 [T, topk]");
   TORCH_CHECK(gate_up.scalar_type() == torch::kBFloat16 && gate_up.dim() == 3 && gate_up.is_contiguous(),
               "moe: gate_up bf16 [E, 2I, H]");
   TORCH_CHECK(down.scalar_type() == torch::kBFloat16 && down.dim() == 3 && down.is_contiguous(), "moe: down bf16 [E, H, I]");
-  const int64_t T = x.size(0), H = x.size(1), topk = ids.size(1), E = gate_up.size(0), N1 = gate_up.size(1);
-  const int64_t I = N1 / 2;
-  TORCH_CHECK(ids.size(0) == T && gate_up.size(2) == H && down.size(0) == E && down.size(1) == H && down.size(2) == I,
-              "moe: shapes");
-  same_device(x, {&ids, &weights, &gate_up, &down}, "moe");
-  same_device_opt(x, {&add}, "moe");
-  if (has(add)) TORCH_CHECK(add->scalar_type() == torch::kBFloat16 && add->is_contiguous() && add->sizes() == x.sizes(),
-                            "moe: add must be bf16 [T, H]");
-  const int64_t P = T * topk;
-  auto plan = moe_plan_op(ids, E, BN);
-  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t H = x.size(1), E = gate_up.size(0), I = gate_up.size(1) / 2;
+  TORCH_CHECK(gate_up.size(2) == H && down.size(0) == E && down.size(1) == H && down.size(2) == I, "moe: shapes");
+  same_device(x, {&gate_up, &down}, "moe");
+}
+
+// gather -> grouped gate/up -> grouped down -> combine over a finished plan.  Returns
+// the layer output, or (with residual) updates it in place and returns the fused
+// norm's output (undefined without norm_w).
+Tensor moe_run_experts(const Tensor& x, MoePlanT& plan, const Tensor& weights, int64_t topk, const Tensor& gate_up,
+                       const Tensor& down, int64_t BN, const OptT& add, const OptT& residual, const OptT& norm_w,
+                       double eps) {
+  const int64_t T = x.size(0), H = x.size(1), P = T * topk;
+  same_device_opt(x, {&add, &residual, &norm_w}, "moe");
+  for (const OptT* o : {&add, &residual})
+    if (has(*o)) TORCH_CHECK((*o)->scalar_type() == torch::kBFloat16 && (*o)->is_contiguous() && (*o)->sizes() == x.sizes(),
+                             "moe: add / residual must be bf16 [T, H]");
+  if (has(norm_w)) TORCH_CHECK(has(residual) && norm_w->scalar_type() == torch::kBFloat16 && norm_w->numel() == H,
+                               "moe: norm_w bf16 [H] with a residual");
   cudaStream_t st = cur_stream();
   // rows past the last block are read by the last block's TMA box (BN rows) and discarded
   auto x_perm = torch::empty({P + BN, H}, x.options());
-  vrm::moe_gather(x.data_ptr(), H, plan[3].data_ptr<int>(), (int)P, (int)H, x_perm.data_ptr(), H, st);
-  auto h_perm = moe_grouped_linear(x_perm, gate_up, plan[4], plan[5], BN, vrm::kEpiSiluMul);
-  auto y_perm = moe_grouped_linear(h_perm, down, plan[4], plan[5], BN, vrm::kEpiNone);
-  auto out = torch::empty({T, H}, x.options());
-  vrm::moe_combine(y_perm.data_ptr(), H, plan[2].data_ptr<int>(), weights.data_ptr<float>(), (int)T, (int)topk,
-                   (int)H, has(add) ? add->data_ptr() : nullptr, out.data_ptr(), H, st);
+  vrm::moe_gather(x.data_ptr(), H, plan.tok.data_ptr<int>(), (int)P, (int)H, x_perm.data_ptr(), H, st);
+  auto h_perm = moe_grouped_linear(x_perm, gate_up, plan.blocks, plan.nblk, BN, vrm::kEpiSiluMul);
+  auto y_perm = moe_grouped_linear(h_perm, down, plan.blocks, plan.nblk, BN, vrm::kEpiNone);
+  Tensor out;
+  if (!has(residual) || has(norm_w)) out = torch::empty({T, H}, x.options());
+  vrm::MoeCombineArgs c;
+  c.y_perm = y_perm.data_ptr();
+  c.ld_perm = H;
+  c.row_of = plan.row_of.data_ptr<int>();
+  c.weights = weights.data_ptr<float>();
+  c.T = (int)T;
+  c.topk = (int)topk;
+  c.H = (int)H;
+  c.add = has(add) ? add->data_ptr() : nullptr;
+  c.residual = has(residual) ? residual->data_ptr() : nullptr;
+  c.out = out.defined() ? out.data_ptr() : nullptr;
+  c.ldo = H;
+  c.norm_w = has(norm_w) ? norm_w->data_ptr() : nullptr;
+  c.eps = (float)eps;
+  vrm::moe_combine(c, st);
   return out;
+}
+
+// Routed experts with explicit routing (ids int64 [T, topk], weights fp32 [T, topk]).
+Tensor moe_experts(const Tensor& x, const Tensor& ids, const Tensor& weights, const Tensor& gate_up,
+                   const Tensor& down, int64_t BN, const OptT& add) {
+  check_moe_weights(x, gate_up, down);
+  TORCH_CHECK(ids.scalar_type() == torch::kInt64 && ids.dim() == 2 && ids.is_contiguous() && ids.size(0) == x.size(0),
+              "moe: ids int64 [T, topk]");
+  TORCH_CHECK(weights.scalar_type() == torch::kFloat32 && weights.sizes() == ids.sizes() && weights.is_contiguous(),
+              "moe: weights fp32 [T, topk]");
+  same_device(x, {&ids, &weights}, "moe");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t topk = ids.size(1), E = gate_up.size(0), P = x.size(0) * topk;
+  auto plan = moe_plan_alloc(x.options(), E, P, BN);
+  auto pa = moe_plan_args(plan, P, topk, E, BN);
+  pa.ids64 = ids.data_ptr<int64_t>();
+  vrm::moe_plan(pa, cur_stream());
+  return moe_run_experts(x, plan, weights, topk, gate_up, down, BN, add, c10::nullopt, c10::nullopt, 0.0);
+}
+
+// A whole MoE layer from the router logits (bf16 [T, E]): device routing, plan, experts,
+// combine (+ add, + residual in place, + the next RMSNorm when norm_w is given).
+Tensor moe_layer(const Tensor& x, const Tensor& logits, int64_t topk, bool norm_topk, const Tensor& gate_up,
+                 const Tensor& down, int64_t BN, const OptT& add, const OptT& residual, const OptT& norm_w,
+                 double eps) {
+  check_moe_weights(x, gate_up, down);
+  check_bf16_2d(logits, "moe logits");
+  TORCH_CHECK(logits.size(0) == x.size(0) && logits.size(1) == gate_up.size(0), "moe: logits [T, E]");
+  same_device(x, {&logits}, "moe");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t T = x.size(0), E = gate_up.size(0), P = T * topk;
+  auto plan = moe_plan_alloc(x.options(), E, P, BN);
+  auto ids32 = torch::empty({std::max<int64_t>(P, 1)}, x.options().dtype(torch::kInt32));
+  auto w = torch::empty({std::max<int64_t>(P, 1)}, x.options().dtype(torch::kFloat32));
+  vrm::MoeRouteArgs ra;
+  ra.logits = logits.data_ptr();
+  ra.ldl = logits.stride(0);
+  ra.T = (int)T;
+  ra.norm_topk = norm_topk;
+  ra.ids32 = ids32.data_ptr<int>();
+  ra.weights = w.data_ptr<float>();
+  ra.plan = moe_plan_args(plan, P, topk, E, BN);
+  ra.plan.ids32 = ra.ids32;
+  vrm::moe_route(ra, cur_stream());
+  return moe_run_experts(x, plan, w, topk, gate_up, down, BN, add, residual, norm_w, eps);
 }
 
 // ---------------------------------------------------------------- page migration
@@ -676,6 +781,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "TurboQuant: [..., 128] -> 64-byte records (Hadamard + PolarQuant + QJL)");
   m.def("tq_decompress", &tq_decompress, py::arg("rec"), py::arg("signs"),
         "TurboQuant: 64-byte records -> bf16 [..., 128]");
+  m.def("moe_route", &moe_route_op, py::arg("logits"), py::arg("topk"), py::arg("norm_topk"), py::arg("BN"),
+        "MoE router on the device: ids, weights, counts, offsets, row_of, tok_of_row, blocks, num_blocks");
+  m.def("moe_layer", &moe_layer, py::arg("x"), py::arg("logits"), py::arg("topk"), py::arg("norm_topk"),
+        py::arg("gate_up"), py::arg("down"), py::arg("BN"), py::arg("add"), py::arg("residual"), py::arg("norm_w"),
+        py::arg("eps"), "MoE layer from router logits (device routing, grouped GEMMs, fused combine)");
   m.def("moe_plan", &moe_plan_op, py::arg("ids"), py::arg("E"), py::arg("BN"),
         "MoE expert plan: counts, offsets, row_of, tok_of_row, blocks [max_blocks, 4], num_blocks");
   m.def("moe_grouped_linear", &moe_grouped_linear, py::arg("x_perm"), py::arg("w"), py::arg("blocks"),

@@ -70,9 +70,10 @@ struct MoeBlock {
 };
 // Routing plan on the device: from expert ids [P = tokens * topk] builds counts,
 // offsets, the grouped row of every (token, k) pair, the token of every grouped row and
-// the list of BN-row blocks (*num_blocks of at most max_blocks).
+// the list of BN-row blocks (*num_blocks of at most max_blocks).  E <= 2048.
 struct MoePlanArgs {
-  const int64_t* ids = nullptr;     // [P] expert of each (token, k), row-major [T, topk]
+  const int64_t* ids64 = nullptr;   // [P] expert of each (token, k), row-major [T, topk] ...
+  const int* ids32 = nullptr;       // ... or as int32 (exactly one of the two)
   int P = 0, topk = 1, E = 0, BN = 16, max_blocks = 0;
   int* counts = nullptr;            // [E]
   int* offsets = nullptr;           // [E + 1]
@@ -82,6 +83,20 @@ struct MoePlanArgs {
   int* num_blocks = nullptr;        // [1]
 };
 void moe_plan(const MoePlanArgs& a, cudaStream_t stream);
+// Router: per token softmax over E bf16 logits (fp32), top-k, optional renormalisation
+// of the k weights; then the plan of the chosen ids (plan.ids32 = ids32).  Small
+// batches do both in one kernel.
+struct MoeRouteArgs {
+  const void* logits = nullptr;     // bf16 [T, E], leading dimension ldl
+  int64_t ldl = 0;
+  int T = 0;
+  bool norm_topk = true;
+  int* ids32 = nullptr;             // [T, topk] out
+  int64_t* ids64 = nullptr;         // [T, topk] out (optional)
+  float* weights = nullptr;         // [T, topk] out
+  MoePlanArgs plan;
+};
+void moe_route(const MoeRouteArgs& a, cudaStream_t stream);
 // x_perm[r] = x[tok_of_row[r]] for r < P (bf16 rows of K elements)
 void moe_gather(const void* x, int64_t ldx, const int* tok_of_row, int P, int K, void* x_perm, int64_t ld_perm,
                 cudaStream_t stream);
@@ -101,9 +116,23 @@ struct MoeGemmArgs {
   int epilogue = kEpiNone;
 };
 void moe_grouped_gemm(const MoeGemmArgs& a, cudaStream_t stream);
-// y[t, :] = sum_k w[t, k] * y_perm[row_of[t * topk + k], :] (+ add[t, :]), fp32 sum in k order
-void moe_combine(const void* y_perm, int64_t ld_perm, const int* row_of, const float* weights, int T, int topk,
-                 int H, const void* add, void* out, int64_t ldo, cudaStream_t stream);
+// s[t, :] = sum_k w[t, k] * y_perm[row_of[t * topk + k], :] (+ add[t, :]), fp32 in k order.
+// Without residual: out = s.  With residual: residual += s (in place, bf16) and, when
+// norm_w is given, out = RMSNorm(residual) * norm_w (the next layer's input norm).
+struct MoeCombineArgs {
+  const void* y_perm = nullptr;
+  int64_t ld_perm = 0;
+  const int* row_of = nullptr;
+  const float* weights = nullptr;
+  int T = 0, topk = 1, H = 0;
+  const void* add = nullptr;        // [T, H] (optional)
+  void* residual = nullptr;         // [T, H] (optional)
+  void* out = nullptr;              // [T, H], leading dimension ldo (may be null with residual and no norm)
+  int64_t ldo = 0;
+  const void* norm_w = nullptr;     // [H] (optional, needs residual)
+  float eps = 1e-6f;
+};
+void moe_combine(const MoeCombineArgs& a, cudaStream_t stream);
 
 // ---------------------------------------------------------------- norms / rope / elementwise (norm_rope.cu)
 // out = norm(x [+ residual]); when residual != null the sum is stored back into it.

@@ -80,6 +80,40 @@ def ablate(llm, B: int) -> dict:
             for k, fn in saved.items():
                 setattr(ops, k, fn)
         res[name + "_ms"] = round(base - t, 4)
+    if llm.cfg.is_moe:
+        from ..parallel import moe
+
+        def moe_stub(cfg, x, router_w, gate_up, down, sgu, sdn, sg, residual, norm_w):
+            # the whole device MoE block (router GEMM, routing, experts, combine) replaced
+            # by the plain next-layer norm it would have fused
+            if residual is None:
+                return torch.empty_like(x)
+            return ops.rmsnorm(residual, norm_w, cfg.norm_eps) if norm_w is not None else None
+
+        def experts_stub(x, logits, *a, **k):
+            # routing GEMM kept; routing, grouped GEMMs and combine replaced
+            residual, norm_w = a[6], a[7]
+            if residual is None:
+                return torch.empty_like(x)
+            return ops.rmsnorm(residual, norm_w, 1e-6) if norm_w is not None else torch.empty(0)
+
+        saved = moe._moe_device
+        try:
+            moe._moe_device = moe_stub
+            res["moe_block_ms"] = round(base - _step_ms(runner, B), 4)
+        finally:
+            moe._moe_device = saved
+        real_native = ops.native
+
+        class _Native:
+            def __getattr__(self, k):
+                return experts_stub if k == "moe_layer" else getattr(real_native(), k)
+
+        try:
+            ops.native = lambda: _Native()
+            res["moe_route_experts_combine_ms"] = round(base - _step_ms(runner, B), 4)
+        finally:
+            ops.native = real_native
     return res
 
 

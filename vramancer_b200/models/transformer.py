@@ -168,19 +168,19 @@ class DecoderModel:
             ops.gelu_tanh_(h)
             return self._row_parallel(h, self.lw(i, "proj_w"), self.lw(i, "proj_b"), r, nxt)
         if cfg.is_moe:
-            y = self._moe(i, x)
-            ops.add_(r, y)
-            return None
+            # residual add (and the next layer's input norm) fused into the combine
+            return self._moe(i, x, r, self._norm_params(*nxt)[0] if nxt else None)
         a = ops.linear(x, self.lw(i, "gate_up_w"), epilogue=ops.EPI_SILU_MUL)
         return self._row_parallel(a, self.lw(i, "down_w"), None, r, nxt)
 
-    def _moe(self, i: int, x: torch.Tensor) -> torch.Tensor:
+    def _moe(self, i: int, x: torch.Tensor, r: torch.Tensor, norm_w: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
         """Top-k softmax routing over SwiGLU experts (device-scheduled grouped GEMM on
-        CUDA, parallel/moe.py)."""
+        CUDA, parallel/moe.py); r += MoE(x); returns RMSNorm(r) * norm_w when given."""
         from ..parallel.moe import moe_forward
         return moe_forward(self.cfg, x, self.lw(i, "router_w"), self.lw(i, "experts_gate_up_w"),
                            self.lw(i, "experts_down_w"), shared_gate_up=self.lw(i, "shared_gate_up_w"),
-                           shared_down=self.lw(i, "shared_down_w"), shared_gate=self.lw(i, "shared_gate_w"))
+                           shared_down=self.lw(i, "shared_down_w"), shared_gate=self.lw(i, "shared_gate_w"),
+                           residual=r, norm_w=norm_w)
 
     def layer(self, i: int, r: torch.Tensor, batch: ForwardBatch, pool: KVPool,
               x: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:

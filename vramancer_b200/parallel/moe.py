@@ -24,9 +24,13 @@ DEVICE_MOE = True       # CUDA MoE layers need no host synchronisation (graph-ca
 
 
 def route(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Returns (weights [T, k] fp32, expert ids [T, k] int64)."""
-    logits = ops.linear(x, router_w).float()
-    probs = torch.softmax(logits, dim=-1)
+    """Returns (weights [T, k] fp32, expert ids [T, k] int64).  On CUDA the softmax /
+    top-k / renormalisation run in the same kernel as the MoE layer's own routing."""
+    logits = ops.linear(x, router_w)
+    if x.is_cuda:
+        ids, w = ops.native().moe_route(logits, cfg.experts_per_token, bool(cfg.norm_topk_prob), 16)[:2]
+        return w, ids
+    probs = torch.softmax(logits.float(), dim=-1)
     w, ids = torch.topk(probs, cfg.experts_per_token, dim=-1)
     if cfg.norm_topk_prob:
         w = w / w.sum(-1, keepdim=True)
@@ -42,11 +46,14 @@ def moe_forward(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor, exper
                 experts_down: torch.Tensor, *, shared_gate_up: Optional[torch.Tensor] = None,
                 shared_down: Optional[torch.Tensor] = None,
                 shared_gate: Optional[torch.Tensor] = None,
-                expert_offset: int = 0) -> torch.Tensor:
-    """x [T, H] -> [T, H].  experts_* hold experts [expert_offset, expert_offset + E_local)."""
+                expert_offset: int = 0, residual: Optional[torch.Tensor] = None,
+                norm_w: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+    """x [T, H] -> [T, H].  experts_* hold experts [expert_offset, expert_offset + E_local).
+    With `residual` the output is added into it in place (bf16) and the result is
+    RMSNorm(residual) * norm_w when `norm_w` is given (the next layer's input), else None."""
     if x.is_cuda and expert_offset == 0 and experts_gate_up.shape[0] == cfg.num_experts:
         return _moe_device(cfg, x, router_w, experts_gate_up, experts_down, shared_gate_up, shared_down,
-                           shared_gate)
+                           shared_gate, residual, norm_w)
     T, H = x.shape
     w, ids = route(cfg, x, router_w)
     out = torch.zeros(T, H, dtype=torch.float32, device=x.device)
@@ -74,7 +81,10 @@ def moe_forward(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor, exper
         if shared_gate is not None:
             ys = ys * torch.sigmoid(ops.linear(x, shared_gate).float())
         out += ys
-    return out.to(x.dtype)
+    if residual is None:
+        return out.to(x.dtype)
+    residual.copy_((residual.float() + out).to(residual.dtype))
+    return ops.rmsnorm(residual, norm_w, cfg.norm_eps) if norm_w is not None else None
 
 
 def moe_block_rows(tokens: int, topk: int, experts: int) -> int:
@@ -88,14 +98,15 @@ def moe_block_rows(tokens: int, topk: int, experts: int) -> int:
 
 
 def _moe_device(cfg: ModelConfig, x: torch.Tensor, router_w, gate_up, down, shared_gate_up, shared_down,
-                shared_gate) -> torch.Tensor:
-    w, ids = route(cfg, x, router_w)
+                shared_gate, residual, norm_w) -> Optional[torch.Tensor]:
     add = None
     if shared_gate_up is not None:
         ys = expert_mlp(x, shared_gate_up, shared_down)
         if shared_gate is not None:
             ys = (ys.float() * torch.sigmoid(ops.linear(x, shared_gate).float())).to(x.dtype)
         add = ys.contiguous()
+    logits = ops.linear(x, router_w)
     bn = moe_block_rows(x.shape[0], cfg.experts_per_token, cfg.num_experts)
-    return ops.native().moe_experts(x.contiguous(), ids.contiguous(), w.float().contiguous(), gate_up.contiguous(),
-                                    down.contiguous(), bn, add)
+    out = ops.native().moe_layer(x.contiguous(), logits, cfg.experts_per_token, bool(cfg.norm_topk_prob),
+                                 gate_up.contiguous(), down.contiguous(), bn, add, residual, norm_w, cfg.norm_eps)
+    return out if (residual is None or norm_w is not None) else None
