@@ -696,11 +696,23 @@ __device__ __forceinline__ MoeBlock load_block(const MoeBlock* blocks, int i) {
   return MoeBlock{v.x, v.y, v.z, v.w};
 }
 
-template <int BN, int STAGES>
+// Expert-parallel return epilogue: row r of the grouped output belongs to pair
+// meta[r] % p_cap of rank meta[r] / p_cap and is stored straight into that rank's
+// return buffer (half = epoch parity); the last CTA flags every rank.
+struct MoeRet {
+  const int* meta = nullptr;                 // this rank's meta buffer (both halves)
+  __nv_bfloat16* const* yback = nullptr;     // [world] return buffers
+  uint32_t* const* flags = nullptr;          // [world] flag arrays ([3][world])
+  const uint32_t* epoch = nullptr;
+  uint32_t* done = nullptr;
+  int rank = 0, world = 1, p_cap = 0, H = 0;
+};
+
+template <int BN, int STAGES, bool kRet>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_grouped_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                             EpiParams ep, const MoeBlock* blocks, const int* num_blocks,
-                            int n_per_expert, int k_tiles, uint32_t* __restrict__ err) {
+                            int n_per_expert, int k_tiles, uint32_t* __restrict__ err, MoeRet ret) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -738,6 +750,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait_for(blocks, num_blocks);  // the work list and x_perm come from earlier kernels
+  const int* ret_meta = ret.meta;
+  if (kRet) opaque_after_wait(ret_meta);
   const int wtiles = (n_per_expert + kBM - 1) / kBM;
   const int items = *num_blocks * wtiles;
 
@@ -827,11 +841,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float v[16];
 #pragma unroll
         for (int q = 0; q < 16; ++q) v[q] = ok ? __uint_as_float(r[q]) : 0.f;
-        epi_store<true>(e, r_glob, c0, v);
+        if (!kRet) {
+          epi_store<true>(e, r_glob, c0, v);
+        } else if (r_glob < ep.N) {
+          // feature r_glob of up to 16 rows, each to its source rank (lanes: consecutive features)
+          const size_t half = (size_t)(*ret.epoch & 1u) * ret.p_cap;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            if (c0 + q >= b.nrows) break;
+            const int tag = ret_meta[b.row0 + c0 + q];
+            const int src = tag / ret.p_cap, p = tag - src * ret.p_cap;
+            ret.yback[src][(half + p) * ret.H + r_glob] = __float2bfloat16(v[q]);
+          }
+        }
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (!ok) break;
+    }
+    if (kRet) {
+      // every CTA counts itself done once its remote stores are ordered (barrier over
+      // the epilogue warps, then one system fence: release is cumulative); the last one
+      // flags every rank
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        uint32_t prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ret.done) : "memory");
+        if (prev == gridDim.x - 1) {
+          *ret.done = 0u;
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          const uint32_t epv = *ret.epoch;
+          for (int o = 0; o < ret.world; ++o) st_release_sys(ret.flags[o] + 2 * ret.world + ret.rank, epv);
+        }
+      }
     }
   }
 
@@ -1140,12 +1183,12 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
 
 
 // ---------------------------------------------------------------- grouped MoE GEMM launcher
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool kRet>
 static void launch_moe_grouped(const CUtensorMap& mw, const CUtensorMap& mx, const EpiParams& ep,
                                const MoeBlock* blocks, const int* num_blocks, int n_per_expert, int K, int grid,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, const MoeRet& ret) {
   constexpr int kSmem = STAGES * GemmSmem<BN, STAGES>::kStageBytes + (2 * STAGES + 5) * 8 + 16 + 1024;
-  auto kern = moe_grouped_swap_kernel<BN, STAGES>;
+  auto kern = moe_grouped_swap_kernel<BN, STAGES, kRet>;
   static int attr_dev_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1154,10 +1197,11 @@ static void launch_moe_grouped(const CUtensorMap& mw, const CUtensorMap& mx, con
     attr_dev_mask |= 1 << (dev & 31);
   }
   launch_kernel(kern, dim3(grid), dim3(kGemmThreads), (size_t)kSmem, stream, mw, mx, ep, blocks, num_blocks,
-                n_per_expert, (K + kBK - 1) / kBK, error_word());
+                n_per_expert, (K + kBK - 1) / kBK, error_word(), ret);
 }
 
-void moe_grouped_gemm(const MoeGemmArgs& a, cudaStream_t stream) {
+template <bool kRet>
+static void moe_grouped_dispatch(const MoeGemmArgs& a, cudaStream_t stream, const MoeRet& ret) {
   VRM_REQUIRE(a.K % 8 == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0 &&
                   (reinterpret_cast<uintptr_t>(a.x_perm) & 15) == 0,
               "moe gemm: K must be a multiple of 8 and operands 16-byte aligned");
@@ -1178,12 +1222,29 @@ void moe_grouped_gemm(const MoeGemmArgs& a, cudaStream_t stream) {
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)a.max_blocks * wtiles, device_sm_count()));
   const auto* blocks = reinterpret_cast<const MoeBlock*>(a.blocks);
   switch (a.BN) {
-    case 16: launch_moe_grouped<16, 8>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream); break;
-    case 32: launch_moe_grouped<32, 8>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream); break;
-    case 64: launch_moe_grouped<64, 6>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream); break;
-    default: launch_moe_grouped<128, 5>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream); break;
+    case 16: launch_moe_grouped<16, 8, kRet>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream, ret); break;
+    case 32: launch_moe_grouped<32, 8, kRet>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream, ret); break;
+    case 64: launch_moe_grouped<64, 6, kRet>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream, ret); break;
+    default: launch_moe_grouped<128, 5, kRet>(mw, mx, ep, blocks, a.num_blocks, a.N, a.K, grid, stream, ret); break;
   }
   VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+void moe_grouped_gemm(const MoeGemmArgs& a, cudaStream_t stream) { moe_grouped_dispatch<false>(a, stream, MoeRet{}); }
+
+void moe_ep_grouped_return(const MoeEpBuffers& b, const MoeGemmArgs& g, cudaStream_t stream) {
+  VRM_REQUIRE(g.epilogue == kEpiNone && g.N == b.H, "moe_ep_grouped_return: plain epilogue, N == H");
+  MoeRet ret;
+  ret.meta = b.meta_local;
+  ret.yback = b.yback;
+  ret.flags = b.flags;
+  ret.epoch = b.epoch;
+  ret.done = b.done + 1;
+  ret.rank = b.rank;
+  ret.world = b.world;
+  ret.p_cap = b.p_cap;
+  ret.H = b.H;
+  moe_grouped_dispatch<true>(g, stream, ret);
 }
 
 }  // namespace vrm

@@ -284,7 +284,7 @@ __device__ __forceinline__ void add8(float (&acc)[8], uint4 u, float s) {
 
 // one CTA per token: fp32 sum of its top-k expert rows in k order (+ add), then either
 // the plain output or residual += sum with the optional RMSNorm of the new residual
-__global__ void __launch_bounds__(kCombThreads) moe_combine_kernel(MoeCombineArgs a) {
+__global__ void __launch_bounds__(kCombThreads) moe_combine_kernel(MoeCombineArgs a, uint32_t* err) {
   pdl_launch();
   const __nv_bfloat16* yp = reinterpret_cast<const __nv_bfloat16*>(a.y_perm);
   const __nv_bfloat16* add = reinterpret_cast<const __nv_bfloat16*>(a.add);
@@ -295,6 +295,23 @@ __global__ void __launch_bounds__(kCombThreads) moe_combine_kernel(MoeCombineArg
   pdl_wait_for(yp, add, nw, res, row_of, w);
   __shared__ float red[33];
   const int t = blockIdx.x;
+  if (a.wait_flags) {
+    // expert parallelism: every owner's rows for this rank have landed in the epoch's half
+    const uint32_t ep = *reinterpret_cast<const volatile uint32_t*>(a.epoch);
+    if (threadIdx.x == 0) {
+      for (int r = 0; r < a.wait_world; ++r) {
+        const unsigned long long t0 = clock64();
+        while ((int)(ld_acquire_sys(a.wait_flags + r) - ep) < 0) {
+          if ((unsigned long long)(clock64() - t0) > VRM_SPIN_LIMIT_CYCLES) {
+            report_error(err, kErrFlagTimeout);
+            break;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    yp += (size_t)(ep & 1u) * a.half_rows * a.ld_perm;
+  }
   const int nvec = a.H / 8;
   float acc[kCombMaxV][8];
 #pragma unroll
@@ -303,11 +320,13 @@ __global__ void __launch_bounds__(kCombThreads) moe_combine_kernel(MoeCombineArg
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
   for (int k = 0; k < a.topk; ++k) {
     const float wk = w[t * a.topk + k];
-    const __nv_bfloat16* src = yp + (size_t)row_of[t * a.topk + k] * a.ld_perm;
+    const int row = row_of ? row_of[t * a.topk + k] : t * a.topk + k;
+    const uint4* src = reinterpret_cast<const uint4*>(yp + (size_t)row * a.ld_perm);
 #pragma unroll
     for (int i = 0; i < kCombMaxV; ++i) {
       const int v = threadIdx.x + i * kCombThreads;
-      if (v < nvec) add8(acc[i], *reinterpret_cast<const uint4*>(src + v * 8), wk);
+      // rows stored by peer GPUs are read from L2, past any line this SM may hold
+      if (v < nvec) add8(acc[i], a.wait_flags ? __ldcg(src + v) : src[v], wk);
     }
   }
   float ss = 0.f;
@@ -411,8 +430,20 @@ void moe_combine(const MoeCombineArgs& a, cudaStream_t st) {
   VRM_REQUIRE(a.out || (a.residual && !a.norm_w), "moe_combine: output missing");
   VRM_REQUIRE(!a.norm_w || a.residual, "moe_combine: the fused norm needs the residual");
   if (a.T <= 0) return;
-  launch_kernel(moe_combine_kernel, dim3(a.T), dim3(kCombThreads), 0, st, a);
+  launch_kernel(moe_combine_kernel, dim3(a.T), dim3(kCombThreads), 0, st, a, error_word());
   VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+void moe_ep_combine(const MoeEpBuffers& b, const MoeCombineArgs& c, cudaStream_t st) {
+  MoeCombineArgs a = c;
+  a.y_perm = b.yback_local;
+  a.ld_perm = b.H;
+  a.row_of = nullptr;
+  a.wait_flags = b.flags_local + 2 * b.world;
+  a.wait_world = b.world;
+  a.epoch = b.epoch;
+  a.half_rows = b.p_cap;
+  moe_combine(a, st);
 }
 
 }  // namespace vrm

@@ -687,6 +687,118 @@ Tensor moe_experts(const Tensor& x, const Tensor& ids, const Tensor& weights, co
   return moe_run_experts(x, plan, weights, topk, gate_up, down, BN, add, c10::nullopt, c10::nullopt, 0.0);
 }
 
+// Expert-parallel MoE layer (moe_ep.cu).  `ptrs` (CUDA int64 [5 * world]) holds the
+// ranks' cnt, xrecv, meta, yback and flag buffers; `desc` = {rank, world, E, H, p_cap,
+// r_rows, cnt_local, xrecv_local, meta_local, yback_local, flags_local}; gate_up / down
+// hold this rank's experts [E_local, ...].  Same return convention as moe_layer.
+Tensor moe_ep_layer(const Tensor& x, const Tensor& logits, int64_t topk, bool norm_topk, const Tensor& gate_up,
+                    const Tensor& down, int64_t BN, const Tensor& ptrs, std::vector<int64_t> desc, const Tensor& epoch,
+                    const Tensor& done, const OptT& add, const OptT& residual, const OptT& norm_w, double eps) {
+  TORCH_CHECK(desc.size() == 11, "moe_ep: desc has 11 entries");
+  check_moe_weights(x, gate_up, down);
+  check_bf16_2d(logits, "moe logits");
+  same_device(x, {&logits, &ptrs, &epoch, &done}, "moe_ep");
+  const int world = (int)desc[1];
+  TORCH_CHECK(ptrs.scalar_type() == torch::kInt64 && ptrs.numel() == 5 * world, "moe_ep: ptrs int64 [5 * world]");
+  TORCH_CHECK(epoch.scalar_type() == torch::kInt32 && done.scalar_type() == torch::kInt32 && done.numel() >= 2,
+              "moe_ep: epoch / done int32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::MoeEpBuffers b;
+  const int64_t* P64 = ptrs.data_ptr<int64_t>();
+  b.cnt = reinterpret_cast<int* const*>(P64);
+  b.xrecv = reinterpret_cast<__nv_bfloat16* const*>(P64 + world);
+  b.meta = reinterpret_cast<int* const*>(P64 + 2 * world);
+  b.yback = reinterpret_cast<__nv_bfloat16* const*>(P64 + 3 * world);
+  b.flags = reinterpret_cast<uint32_t* const*>(P64 + 4 * world);
+  b.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
+  b.done = reinterpret_cast<uint32_t*>(done.data_ptr<int>());
+  b.rank = (int)desc[0];
+  b.world = world;
+  b.E = (int)desc[2];
+  b.E_local = b.E / world;
+  b.H = (int)desc[3];
+  b.p_cap = (int)desc[4];
+  b.r_rows = (int)desc[5];
+  b.xrecv_local = reinterpret_cast<__nv_bfloat16*>(desc[7]);
+  b.meta_local = reinterpret_cast<int*>(desc[8]);
+  b.yback_local = reinterpret_cast<__nv_bfloat16*>(desc[9]);
+  b.flags_local = reinterpret_cast<uint32_t*>(desc[10]);
+  const int64_t T = x.size(0), H = x.size(1), E = b.E, P = T * topk;
+  TORCH_CHECK(gate_up.size(0) == b.E_local && logits.size(1) == E && H == b.H && P <= b.p_cap,
+              "moe_ep: shapes / capacity (tokens * topk <= p_cap)");
+  cudaStream_t st = cur_stream();
+  // local routing and plan over all E experts (its counts, offsets and row_of drive the dispatch)
+  auto plan = moe_plan_alloc(x.options(), E, P, 128);
+  auto ids32 = torch::empty({std::max<int64_t>(P, 1)}, x.options().dtype(torch::kInt32));
+  auto w = torch::empty({std::max<int64_t>(P, 1)}, x.options().dtype(torch::kFloat32));
+  if (T > 0) {
+    vrm::MoeRouteArgs ra;
+    ra.logits = logits.data_ptr();
+    ra.ldl = logits.stride(0);
+    ra.T = (int)T;
+    ra.norm_topk = norm_topk;
+    ra.ids32 = ids32.data_ptr<int>();
+    ra.weights = w.data_ptr<float>();
+    ra.plan = moe_plan_args(plan, P, topk, E, 128);
+    ra.plan.ids32 = ra.ids32;
+    vrm::moe_route(ra, st);
+  }
+  vrm::moe_ep_counts(b, plan.counts.data_ptr<int>(), (int)T, st);
+  vrm::moe_ep_dispatch(b, x.data_ptr(), ids32.data_ptr<int>(), plan.row_of.data_ptr<int>(),
+                       plan.offsets.data_ptr<int>(), (int)T, (int)topk, st);
+  // owner side: blocks over this rank's experts, rows of every source rank
+  const int64_t max_blocks = b.E_local + ((int64_t)world * b.p_cap + BN - 1) / BN;
+  auto blocks = torch::empty({max_blocks, 4}, x.options().dtype(torch::kInt32));
+  auto nblk = torch::zeros({1}, x.options().dtype(torch::kInt32));
+  vrm::moe_ep_owner_plan(b, (int)BN, reinterpret_cast<vrm::MoeBlock*>(blocks.data_ptr<int>()), nblk.data_ptr<int>(),
+                         (int)max_blocks, st);
+  const int64_t I = gate_up.size(1) / 2;
+  auto h = torch::empty({2 * (int64_t)b.r_rows, I}, x.options());
+  vrm::MoeGemmArgs g;
+  g.w = gate_up.data_ptr();
+  g.E = (int)b.E_local;
+  g.N = (int)gate_up.size(1);
+  g.K = (int)H;
+  g.x_perm = b.xrecv_local;
+  g.ldx = H;
+  g.rows_cap = 2 * b.r_rows;
+  g.blocks = blocks.data_ptr<int>();
+  g.num_blocks = nblk.data_ptr<int>();
+  g.max_blocks = (int)max_blocks;
+  g.BN = (int)BN;
+  g.out = h.data_ptr();
+  g.ldo = I;
+  g.epilogue = vrm::kEpiSiluMul;
+  vrm::moe_grouped_gemm(g, st);
+  g.w = down.data_ptr();
+  g.N = (int)H;
+  g.K = (int)I;
+  g.x_perm = h.data_ptr();
+  g.ldx = I;
+  g.out = nullptr;
+  g.ldo = H;
+  g.epilogue = vrm::kEpiNone;
+  vrm::moe_ep_grouped_return(b, g, st);
+  for (const OptT* o : {&add, &residual})
+    if (has(*o)) TORCH_CHECK((*o)->scalar_type() == torch::kBFloat16 && (*o)->is_contiguous() && (*o)->sizes() == x.sizes(),
+                             "moe: add / residual must be bf16 [T, H]");
+  Tensor out;
+  if (!has(residual) || has(norm_w)) out = torch::empty({T, H}, x.options());
+  vrm::MoeCombineArgs c;
+  c.weights = w.data_ptr<float>();
+  c.T = (int)T;
+  c.topk = (int)topk;
+  c.H = (int)H;
+  c.add = has(add) ? add->data_ptr() : nullptr;
+  c.residual = has(residual) ? residual->data_ptr() : nullptr;
+  c.out = out.defined() ? out.data_ptr() : nullptr;
+  c.ldo = H;
+  c.norm_w = has(norm_w) ? norm_w->data_ptr() : nullptr;
+  c.eps = (float)eps;
+  vrm::moe_ep_combine(b, c, st);
+  return out;
+}
+
 // A whole MoE layer from the router logits (bf16 [T, E]): device routing, plan, experts,
 // combine (+ add, + residual in place, + the next RMSNorm when norm_w is given).
 Tensor moe_layer(const Tensor& x, const Tensor& logits, int64_t topk, bool norm_topk, const Tensor& gate_up,
@@ -786,6 +898,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_layer", &moe_layer, py::arg("x"), py::arg("logits"), py::arg("topk"), py::arg("norm_topk"),
         py::arg("gate_up"), py::arg("down"), py::arg("BN"), py::arg("add"), py::arg("residual"), py::arg("norm_w"),
         py::arg("eps"), "MoE layer from router logits (device routing, grouped GEMMs, fused combine)");
+  m.def("moe_ep_layer", &moe_ep_layer, py::arg("x"), py::arg("logits"), py::arg("topk"), py::arg("norm_topk"),
+        py::arg("gate_up"), py::arg("down"), py::arg("BN"), py::arg("ptrs"), py::arg("desc"), py::arg("epoch"),
+        py::arg("done"), py::arg("add"), py::arg("residual"), py::arg("norm_w"), py::arg("eps"),
+        "expert-parallel MoE layer: peer-memory dispatch, grouped GEMMs with the return fused into the epilogue");
   m.def("moe_plan", &moe_plan_op, py::arg("ids"), py::arg("E"), py::arg("BN"),
         "MoE expert plan: counts, offsets, row_of, tok_of_row, blocks [max_blocks, 4], num_blocks");
   m.def("moe_grouped_linear", &moe_grouped_linear, py::arg("x_perm"), py::arg("w"), py::arg("blocks"),

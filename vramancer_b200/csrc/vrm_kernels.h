@@ -131,8 +131,59 @@ struct MoeCombineArgs {
   int64_t ldo = 0;
   const void* norm_w = nullptr;     // [H] (optional, needs residual)
   float eps = 1e-6f;
+  // expert parallelism: row_of null = rows in pair order; wait for every rank's flag
+  // in wait_flags to reach *epoch, and read the half (epoch & 1) of half_rows rows
+  const uint32_t* wait_flags = nullptr;
+  int wait_world = 0;
+  const uint32_t* epoch = nullptr;
+  long long half_rows = 0;
 };
 void moe_combine(const MoeCombineArgs& a, cudaStream_t stream);
+
+// ---------------------------------------------------------------- expert parallelism (moe_ep.cu)
+// Expert-parallel MoE over peer memory.  Rank r owns experts [r * E_local, (r + 1) *
+// E_local).  Every rank owns symmetric buffers (cudaMalloc + CUDA IPC), each in two
+// halves that alternate with the parity of the layer-call epoch:
+//   cnt    int  [2][world][E]            routed-pair counts per expert, one row per source rank
+//   xrecv  bf16 [2][r_rows][H]           rows received for this rank's experts
+//   meta   int  [2][r_rows]              source rank * p_cap + pair index of each received row
+//   yback  bf16 [2][p_cap][H]            expert outputs returned for this rank's own pairs
+//   flags  u32  [3][world]               count / dispatch / return phase, one word per peer
+// with r_rows = world * p_cap + BN_max (the last block's TMA box reads past the rows).
+struct MoeEpBuffers {
+  int* const* cnt = nullptr;                  // device arrays [world] of the ranks' base pointers
+  __nv_bfloat16* const* xrecv = nullptr;
+  int* const* meta = nullptr;
+  __nv_bfloat16* const* yback = nullptr;
+  uint32_t* const* flags = nullptr;
+  uint32_t* epoch = nullptr;                  // this rank's call counter (device)
+  uint32_t* done = nullptr;                   // this rank's completion counters [2] (device, zero)
+  int* meta_local = nullptr;                  // this rank's own meta buffer (host-visible pointer)
+  __nv_bfloat16* xrecv_local = nullptr;       // this rank's own receive buffer
+  __nv_bfloat16* yback_local = nullptr;       // this rank's own return buffer
+  uint32_t* flags_local = nullptr;            // this rank's own flag array
+  int rank = 0, world = 1, E = 0, E_local = 0, H = 0;
+  int p_cap = 0;                              // pairs per rank (max tokens * topk)
+  int r_rows = 0;                             // rows per half of xrecv / meta
+};
+// Count exchange: advances the epoch; sends this rank's per-expert counts ([E], or zeros
+// when T == 0) to every rank and flags them.
+void moe_ep_counts(const MoeEpBuffers& b, const int* counts, int T, cudaStream_t stream);
+// Dispatch: waits for every rank's counts, then stores the rows of x routed to each
+// expert into its owner's xrecv (grouped by local expert, then source rank) with their
+// meta tags, and flags the owners.  ids / row_of / offsets come from this rank's plan.
+void moe_ep_dispatch(const MoeEpBuffers& b, const void* x, const int* ids32, const int* row_of, const int* offsets,
+                     int T, int topk, cudaStream_t stream);
+// Owner plan: waits for every rank's dispatch, then builds the block list over this
+// rank's experts (row0 includes the half offset).
+void moe_ep_owner_plan(const MoeEpBuffers& b, int BN, MoeBlock* blocks, int* num_blocks, int max_blocks,
+                       cudaStream_t stream);
+// Grouped down projection whose epilogue returns each row to its source rank's yback
+// (posted NVLink stores), then flags every rank when its last CTA finishes.
+void moe_ep_grouped_return(const MoeEpBuffers& b, const MoeGemmArgs& g, cudaStream_t stream);
+// Combine on the source rank: waits for every owner's return flag, then the weighted
+// k-order sum of yback rows (+ add, residual, next RMSNorm) as moe_combine.
+void moe_ep_combine(const MoeEpBuffers& b, const MoeCombineArgs& c, cudaStream_t stream);
 
 // ---------------------------------------------------------------- norms / rope / elementwise (norm_rope.cu)
 // out = norm(x [+ residual]); when residual != null the sum is stored back into it.

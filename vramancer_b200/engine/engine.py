@@ -26,6 +26,8 @@ from concurrent.futures import Future
 from dataclasses import dataclass, field
 from typing import Callable, Deque, Dict, List, Optional, Sequence
 
+import torch
+
 from ..kv.paged import OutOfPages, PagedKVCacheManager
 from .runner import ModelRunner, PrefillItem
 
@@ -79,7 +81,10 @@ class Request:
 class LLMEngine:
     def __init__(self, runner: ModelRunner, manager: PagedKVCacheManager, *, max_batch: Optional[int] = None,
                  max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, spec_num_draft: int = 0,
-                 spec_ngram: int = 3):
+                 spec_ngram: int = 3, ep_sync: Optional["EPSync"] = None):
+        if ep_sync is not None and spec_num_draft > 0:
+            raise ValueError("speculative decoding is not supported with expert parallelism")
+        self.ep_sync = ep_sync
         self.runner = runner
         self.kv = manager
         self.max_batch = max_batch or runner.max_batch
@@ -127,6 +132,11 @@ class LLMEngine:
 
     def generate(self, prompts: Sequence[Sequence[int]], params: Optional[SamplingParams] = None) -> List[Request]:
         reqs = [self.add_request(p, params) for p in prompts]
+        if self.ep_sync is not None:
+            # every expert-parallel rank keeps stepping until all ranks are done
+            while self.ep_sync.any_rank(any(not r.finished for r in reqs)):
+                self.step()
+            return reqs
         while any(not r.finished for r in reqs):
             self.step()
         return reqs
@@ -185,8 +195,24 @@ class LLMEngine:
             before = self.stats["finished"]
             done: List[Request] = []
             self._admit()
-            self._prefill_chunk(done)
-            self._decode(done)
+            if self.ep_sync is None:
+                self._prefill_chunk(done)
+                self._decode(done)
+            else:
+                # the ranks' MoE layer calls must pair up: forward passes run on every
+                # rank when they run on any (one-token dummies where there is no work)
+                mine = any(not r.prefill_done for r in self.running)
+                if self.ep_sync.any_rank(mine):
+                    if mine:
+                        self._prefill_chunk(done)
+                    else:
+                        self.ep_sync.dummy_prefill(self.runner)
+                mine = any(r.prefill_done and not r.finished and r.output_ids for r in self.running)
+                if self.ep_sync.any_rank(mine):
+                    if mine:
+                        self._decode(done)
+                    else:
+                        self.ep_sync.dummy_decode(self.runner)
             self.stats["steps"] += 1
             return done
 
@@ -258,3 +284,38 @@ class LLMEngine:
         copies = self.kv.pop_cow_copies()
         if copies:
             self.runner.copy_pages(copies)
+
+
+class EPSync:
+    """Lockstep of expert-parallel ranks (each runs its own engine on its own
+    sequences): a host-side OR over the ranks before every forward pass, and one-token
+    dummy passes into a reserved KV page for a rank without work, so that every rank
+    makes the same sequence of MoE layer calls.
+
+    Reference parity: none (the reference has no expert parallelism)."""
+
+    DUMMY = "__ep_dummy__"
+
+    def __init__(self, manager: PagedKVCacheManager, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        manager.allocate(self.DUMMY, 1)
+        self.slot = manager.slots_for(self.DUMMY, 0, 1)[0]
+        self.block_table = manager.block_table(self.DUMMY)
+
+    def any_rank(self, flag: bool) -> bool:
+        if self.world == 1:
+            return bool(flag)
+        t = torch.tensor([1 if flag else 0], dtype=torch.int32)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX, group=self.group)
+        return bool(t.item())
+
+    def dummy_prefill(self, runner) -> None:
+        from .runner import PrefillItem
+        runner.prefill([PrefillItem(token_ids=[0], start_pos=0, slots=[self.slot], block_table=self.block_table,
+                                    context_len=1, want_logits=False)], [0.0], [0], [1.0], [0])
+
+    def dummy_decode(self, runner) -> None:
+        runner.decode_step([0], [0], [self.slot], [1], [self.block_table], [0.0], [0], [1.0], [0])

@@ -42,7 +42,7 @@ class LLM:
                  max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, weights=None,
                  num_layers: Optional[int] = None, tp=None, quantization: Optional[str] = None,
                  spec_num_draft: int = 0, spec_ngram: int = 3, kv_offload_pages: int = 0, hierarchy=None,
-                 stream_layers: int = 0):
+                 stream_layers: int = 0, ep=None):
         if isinstance(model, ModelConfig):
             cfg = model
         else:
@@ -55,15 +55,24 @@ class LLM:
             torch.cuda.set_device(self.device)
         self.tp = tp
         tp_rank, tp_size = (tp.rank, tp.size) if tp is not None else (0, 1)
+        # expert parallelism: `ep` is an ExpertParallel (or True to build one over the
+        # default process group); experts are sharded, everything else is replicated
+        if ep is True:
+            from .parallel.expert_parallel import ExpertParallel
+            ep = ExpertParallel(cfg, device=self.device)
+        if ep is not None and tp is not None and tp.size > 1:
+            raise ValueError("expert parallelism runs with data-parallel attention (tp must be 1)")
+        self.ep = ep
+        ep_rank, ep_size = (ep.rank, ep.world) if ep is not None else (0, 1)
         if weights is None:
             if isinstance(model, str) and _is_checkpoint_dir(model):
                 weights = load_safetensors(model, cfg, device=self.device, dtype=dtype, tp_rank=tp_rank,
-                                           tp_size=tp_size)
+                                           tp_size=tp_size, ep_rank=ep_rank, ep_size=ep_size)
             else:
                 # streamed layers live in host memory: build them there
                 wdev = torch.device("cpu") if stream_layers > 0 else self.device
                 weights = random_weights(cfg, device=wdev, dtype=dtype, seed=seed, tp_rank=tp_rank,
-                                         tp_size=tp_size)
+                                         tp_size=tp_size, ep_rank=ep_rank, ep_size=ep_size)
         self.quantization = (quantization or "").lower() or None
         if self.quantization == "nvfp4":
             from .quant.nvfp4 import quantize_model_weights
@@ -81,7 +90,7 @@ class LLM:
                                               dtype=dtype, tp=tp)
             use_cuda_graph = False
         else:
-            self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype, tp=tp)
+            self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype, tp=tp, ep=ep)
         kvd = kv_dtype_from_str(kv_cache_dtype)
         if kv_pages is None:
             kv_pages = self._pages_from_memory(cfg, kvd, gpu_memory_utilization, max_batch, max_model_len)
@@ -96,8 +105,23 @@ class LLM:
                                       offload=self.offload)
         self.runner = ModelRunner(self.model, self.pool, max_batch=max_batch, max_model_len=max_model_len,
                                   use_cuda_graph=use_cuda_graph, seed=seed)
+        ep_sync = None
+        if ep is not None:
+            import torch.distributed as dist
+
+            from .engine.engine import EPSync
+            grp = None
+            if dist.is_initialized() and dist.get_backend() != "gloo":
+                grp = dist.new_group(backend="gloo")      # host-side step agreement
+            ep_sync = EPSync(self.kv, group=grp)
+            max_prefill_tokens = min(max_prefill_tokens, getattr(ep, "max_tokens", max_prefill_tokens))
         self.engine = LLMEngine(self.runner, self.kv, max_prefill_tokens=max_prefill_tokens,
-                                eos_token_id=eos_token_id, spec_num_draft=spec_num_draft, spec_ngram=spec_ngram)
+                                eos_token_id=eos_token_id, spec_num_draft=spec_num_draft, spec_ngram=spec_ngram,
+                                ep_sync=ep_sync)
+        if ep is not None and self.runner.use_graph:
+            # a lazy capture runs an eager warm-up pass, which would unpair the ranks' MoE
+            # calls mid-run: every rank captures every bucket now, in the same order
+            self.runner.capture_all()
 
     def _pages_from_memory(self, cfg, kvd, util, max_batch, max_model_len) -> int:
         need = max_batch * ((max_model_len + 15) // 16) + 16

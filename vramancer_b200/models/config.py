@@ -178,6 +178,11 @@ PRESETS: Dict[str, ModelConfig] = {
     "tiny-gpt2": ModelConfig(arch="gpt2", vocab_size=500, hidden_size=128, num_layers=4, num_heads=2,
                              num_kv_heads=2, head_dim=64, intermediate_size=512, max_position=512, norm_eps=1e-5,
                              rope_theta=0.0, qkv_bias=True, tie_embeddings=True, name="tiny-gpt2"),
+    "tiny-moe-wide": ModelConfig(arch="qwen2_moe", vocab_size=512, hidden_size=1024, num_layers=2, num_heads=8,
+                                 num_kv_heads=2, head_dim=128, intermediate_size=256, max_position=2048,
+                                 norm_eps=1e-6, rope_theta=10000.0, qkv_bias=False, num_experts=16,
+                                 experts_per_token=4, expert_intermediate_size=256, norm_topk_prob=True,
+                                 name="tiny-moe-wide"),
     "tiny-moe": ModelConfig(arch="qwen2_moe", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
                             num_kv_heads=2, head_dim=64, intermediate_size=128, max_position=2048, norm_eps=1e-6,
                             rope_theta=10000.0, qkv_bias=False, num_experts=8, experts_per_token=2,

@@ -66,8 +66,10 @@ class TPContext:
 
 class DecoderModel:
     def __init__(self, cfg: ModelConfig, weights: Weights, *, device="cpu", dtype=torch.bfloat16,
-                 first_layer: int = 0, last_layer: Optional[int] = None, tp: Optional[TPContext] = None):
+                 first_layer: int = 0, last_layer: Optional[int] = None, tp: Optional[TPContext] = None,
+                 ep=None):
         self.cfg = cfg
+        self.ep = ep                  # parallel.expert_parallel.ExpertParallel (experts sharded) or None
         self.w = weights
         self.device = torch.device(device)
         self.dtype = dtype
@@ -176,7 +178,18 @@ class DecoderModel:
     def _moe(self, i: int, x: torch.Tensor, r: torch.Tensor, norm_w: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
         """Top-k softmax routing over SwiGLU experts (device-scheduled grouped GEMM on
         CUDA, parallel/moe.py); r += MoE(x); returns RMSNorm(r) * norm_w when given."""
-        from ..parallel.moe import moe_forward
+        from ..parallel.moe import expert_mlp, moe_forward
+        if self.ep is not None:
+            add = None
+            sgu = self.lw(i, "shared_gate_up_w")
+            if sgu is not None:
+                ys = expert_mlp(x, sgu, self.lw(i, "shared_down_w"))
+                sg = self.lw(i, "shared_gate_w")
+                if sg is not None:
+                    ys = (ys.float() * torch.sigmoid(ops.linear(x, sg).float())).to(x.dtype)
+                add = ys.contiguous()
+            return self.ep.forward(x, self.lw(i, "router_w"), self.lw(i, "experts_gate_up_w"),
+                                   self.lw(i, "experts_down_w"), add=add, residual=r, norm_w=norm_w)
         return moe_forward(self.cfg, x, self.lw(i, "router_w"), self.lw(i, "experts_gate_up_w"),
                            self.lw(i, "experts_down_w"), shared_gate_up=self.lw(i, "shared_gate_up_w"),
                            shared_down=self.lw(i, "shared_down_w"), shared_gate=self.lw(i, "shared_gate_w"),

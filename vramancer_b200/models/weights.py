@@ -67,14 +67,16 @@ def layer_shapes(cfg: ModelConfig, tp_rank: int = 0, tp_size: int = 1) -> Dict[s
 
 def random_weights(cfg: ModelConfig, *, device="cpu", dtype=torch.bfloat16, seed: int = 0,
                    layers: Optional[Iterable[int]] = None, embed: bool = True, head: bool = True,
-                   tp_rank: int = 0, tp_size: int = 1, std: float = 0.02) -> Weights:
+                   tp_rank: int = 0, tp_size: int = 1, std: float = 0.02, ep_rank: int = 0,
+                   ep_size: int = 1) -> Weights:
     """N(0, std) matrices, unit norm weights, zero norm biases; deterministic in `seed`.
 
     Each tensor gets its own generator seeded from (seed, name), so a layer's values do
     not depend on which other layers this process builds (pipeline stages of a split
     model hold exactly the tensors of the single-device model).  With tp_size > 1 the
     full tensor is generated and this rank's shard is kept, so TP ranks hold slices of
-    the TP=1 model.
+    the TP=1 model.  With ep_size > 1 only this expert-parallel rank's experts are kept
+    (generated in full and sliced, so EP ranks hold slices of the single-GPU model).
     """
     layers = range(cfg.num_layers) if layers is None else layers
     dev = torch.device(device)
@@ -98,6 +100,8 @@ def random_weights(cfg: ModelConfig, *, device="cpu", dtype=torch.bfloat16, seed
             t = gen(f"layers.{i}.{n}", shp, kind)
             if tp_size > 1:
                 t = shard_tensor(cfg, n, t, tp_rank, tp_size)
+            if ep_size > 1 and n.startswith("experts_"):
+                t = _ep_slice(t, ep_rank, ep_size)
             out[f"layers.{i}.{n}"] = t
     H = cfg.hidden_size
     if embed:
@@ -115,6 +119,13 @@ def random_weights(cfg: ModelConfig, *, device="cpu", dtype=torch.bfloat16, seed
         if tp_size > 1:
             out["lm_head"] = shard_tensor(cfg, "lm_head", out["lm_head"], tp_rank, tp_size)
     return out
+
+
+def _ep_slice(t: torch.Tensor, rank: int, size: int) -> torch.Tensor:
+    n = t.shape[0] // size
+    if n * size != t.shape[0]:
+        raise ValueError(f"{t.shape[0]} experts do not divide over {size} expert-parallel ranks")
+    return t[rank * n:(rank + 1) * n].clone()
 
 
 def hash_name(name: str) -> int:
@@ -235,9 +246,10 @@ def _hf_map(cfg: ModelConfig, name: str) -> Optional[Tuple[str, str]]:
 
 def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.bfloat16,
                      layers: Optional[Iterable[int]] = None, embed: bool = True, head: bool = True,
-                     tp_rank: int = 0, tp_size: int = 1) -> Weights:
+                     tp_rank: int = 0, tp_size: int = 1, ep_rank: int = 0, ep_size: int = 1) -> Weights:
     """Reads an HF checkpoint directory (*.safetensors), keeping only the tensors this
-    stage / rank needs, fusing q/k/v and gate/up into the internal layout."""
+    stage / rank needs (this expert-parallel rank's experts with ep_size > 1), fusing
+    q/k/v and gate/up into the internal layout."""
     from safetensors import safe_open
 
     want_layers = set(range(cfg.num_layers) if layers is None else layers)
@@ -275,9 +287,12 @@ def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.b
             out[iname] = interleave_gate_up(p["gate"], p["up"])
         elif base == "experts_gate_up_w":
             E = cfg.num_experts
-            out[iname] = torch.stack([interleave_gate_up(p[f"egate:{e}"], p[f"eup:{e}"]) for e in range(E)])
+            n = E // ep_size
+            own = range(ep_rank * n, (ep_rank + 1) * n)
+            out[iname] = torch.stack([interleave_gate_up(p[f"egate:{e}"], p[f"eup:{e}"]) for e in own])
         elif base == "experts_down_w":
-            out[iname] = torch.stack([p[f"edown:{e}"] for e in range(cfg.num_experts)])
+            n = cfg.num_experts // ep_size
+            out[iname] = torch.stack([p[f"edown:{e}"] for e in range(ep_rank * n, (ep_rank + 1) * n)])
     if head and "lm_head" not in out and "embed" in out:
         out["lm_head"] = out["embed"]
     if not embed:
