@@ -425,6 +425,7 @@ void moe_gather(const void* x, int64_t ldx, const int* tok_of_row, int P, int K,
 }
 
 void moe_combine(const MoeCombineArgs& a, cudaStream_t st) {
+  if (a.T <= 0) return;
   VRM_REQUIRE(a.H % 8 == 0 && a.H <= 8 * kCombThreads * kCombMaxV && a.ld_perm % 8 == 0 && a.ldo % 8 == 0,
               "moe_combine: H must be a multiple of 8 and <= 8192");
   VRM_REQUIRE(a.out || (a.residual && !a.norm_w), "moe_combine: output missing");

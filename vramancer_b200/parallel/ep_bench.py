@@ -83,14 +83,15 @@ def bench(args) -> None:
     W = info.world_size
     Bl = max(1, args.batch // W)
     ep = ExpertParallel(cfg, max_tokens=max(Bl, args.max_tokens), device=dev)
-    max_len = args.prompt_len + args.steps + args.warmup + 64
+    # requests decode while the others prefill (one chunk per lockstep step)
+    max_len = args.prompt_len + Bl + args.steps + args.warmup + 64
     llm = LLM(args.model, device=str(dev), max_batch=Bl, max_model_len=max_len,
               kv_pages=(Bl + 2) * ((max_len + 15) // 16) + 64, enable_prefix_cache=False, seed=1234, ep=ep,
               max_prefill_tokens=args.max_tokens)
     eng, runner, sync = llm.engine, llm.runner, llm.engine.ep_sync
     g = torch.Generator().manual_seed(42 + ep.rank)
     reqs = [eng.add_request(torch.randint(0, cfg.vocab_size, (args.prompt_len,), generator=g).tolist(),
-                            SamplingParams(max_tokens=args.steps + args.warmup + 8, ignore_eos=True))
+                            SamplingParams(max_tokens=max_len, ignore_eos=True))
             for _ in range(Bl)]
     while sync.any_rank(any(not r.output_ids for r in reqs)):
         eng.step()                                   # admission + prefill in lockstep
