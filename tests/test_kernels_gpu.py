@@ -153,6 +153,42 @@ def test_paged_decode(D, Hq, KH, fp8, splits, cuda_errors_clean):
     _close(out, ref, rtol=3e-2, atol=3e-2)
 
 
+@pytest.mark.parametrize("splits", [0, 2, 7])
+@pytest.mark.parametrize("tma", [False, True])
+def test_paged_decode_many_sequences(splits, tma, cuda_errors_clean):
+    """Many sequences; with the persistent TMA kernel many (sequence, head, chunk) items
+    per CTA: its page ring runs across item boundaries and chunks of one sequence land
+    on different CTAs."""
+    ops.native().set_decode_tma(tma)
+    try:
+        _many_sequences(splits)
+    finally:
+        ops.native().set_decode_tma(False)
+
+
+def _many_sequences(splits):
+    g = torch.Generator().manual_seed(splits)
+    lens = torch.randint(1, 700, (70,), generator=g).tolist()
+    D, Hq, KH, L, layer = 128, 40, 8, 2, 0
+    cache, bt, scale = _make_cache(lens, L, KH, D, torch.bfloat16, layer, seed=3)
+    B = len(lens)
+    q = torch.randn(B, (Hq + 2 * KH) * D, generator=g).bfloat16()
+    cl = torch.tensor(lens, dtype=torch.int32)
+    sm = 1.0 / math.sqrt(D)
+    ref = ops.paged_attention_decode(q, cache, layer, bt, cl, scale, sm, Hq)
+    dq, dc, dbt, dcl = q.to(DEV), cache.to(DEV), bt.to(DEV), cl.to(DEV)
+    if splits == 2:
+        # also the small-batch shapes (bs 1 and 8) through the same kernel
+        for nb in (1, 8):
+            r1 = ops.paged_attention_decode(q[:nb], cache, layer, bt[:nb], cl[:nb], scale, sm, Hq)
+            o1 = ops.paged_attention_decode(dq[:nb], dc, layer, dbt[:nb], dcl[:nb], None, sm, Hq)
+            _close(o1, r1, rtol=3e-2, atol=3e-2)
+    out = ops.paged_attention_decode(dq, dc, layer, dbt, dcl, None, sm, Hq, num_splits=splits)
+    _close(out, ref, rtol=3e-2, atol=3e-2)
+    again = ops.paged_attention_decode(dq, dc, layer, dbt, dcl, None, sm, Hq, num_splits=splits)
+    assert torch.equal(out, again)     # chunk merges are in chunk order: deterministic
+
+
 @pytest.mark.parametrize("D,Hq,KH", [(128, 40, 8), (64, 12, 12)])
 @pytest.mark.parametrize("fp8", [False, True])
 def test_paged_prefill(D, Hq, KH, fp8, cuda_errors_clean):

@@ -22,6 +22,8 @@
 // fp16 / q4 pages, not on the reference's forward path); the reference prefill runs
 // HF SDPA (core/turbo_engine.py:72-93).
 #include <algorithm>
+#include <climits>
+#include <cstdlib>
 
 #include "vrm_common.cuh"
 #include "vrm_host.h"
@@ -378,6 +380,334 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   if (threadIdx.x == 0) P.counters[grp] = 0u;
 }
 
+// ============================================================== decode, persistent + TMA (bf16 pages)
+// Work items are (page chunk, sequence, KV head), chunk-major so that every CTA's share
+// mixes sequences; CTAs walk them round-robin.  Warp 4 is the producer: one thread
+// issues the 2D tensor loads (128-byte swizzle) of each page's K and V tiles into an
+// 8-stage mbarrier ring, running ahead across item boundaries, and waits for the
+// previous kernel only before the first page that kernel writes (the live page).
+// Warps 0-3 take the item's pages round-robin with the same transposed MMA math as
+// paged_decode_kernel, merge through shared memory at the end of each item, and the
+// CTA finishing a sequence's last chunk merges the chunk partials.
+template <int D>
+struct DecodeTmaSmem {
+  static constexpr int kBoxB = kPage * 128;                // one 16 x 64 bf16 box
+  static constexpr int kTileB = kPage * D * 2;             // 16 x D tile (D / 64 boxes)
+  static constexpr int kStageB = 2 * kTileB;               // K + V
+  static constexpr int kStages = 8;
+  static constexpr int kRingB = kStages * kStageB;
+  static constexpr int kMergeB = 4 * 8 * (D + 4) * 4;
+  static constexpr int kTotal = kRingB + kMergeB + 2 * kStages * 8 + 1024;
+};
+
+// byte offset of 16-byte chunk ch of row r in a tile made of 128-byte-swizzled boxes
+__device__ __forceinline__ uint32_t swz_box(int r, int ch) {
+  return (uint32_t)((ch >> 3) * (kPage * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+}
+
+struct DecodeTmaParams {
+  const __nv_bfloat16* q;
+  int64_t ld_q;
+  int layer, num_layers, KH, G, B;
+  const int* block_tables;
+  int bt_stride;
+  const int* context_lens;
+  float sm_scale;
+  __nv_bfloat16* out;
+  int64_t ld_o;
+  float* ws_o;
+  float* ws_ml;
+  uint32_t* counters;
+  int chunk_pages, max_chunks;
+  uint32_t* err;
+};
+
+struct DecodeItem {
+  int b, kvh, c, p0, p1, nchunks;
+};
+
+__device__ __forceinline__ bool decode_item(const DecodeTmaParams& P, int w, DecodeItem& it) {
+  const int per = P.B * P.KH;
+  it.c = w / per;
+  const int rem = w - it.c * per;
+  it.b = rem / P.KH;
+  it.kvh = rem - it.b * P.KH;
+  const int ctx = P.context_lens[it.b];
+  const int npages = (ctx + kPage - 1) / kPage;
+  it.nchunks = min(P.max_chunks, (npages + P.chunk_pages - 1) / P.chunk_pages);
+  if (it.c >= it.nchunks) return false;
+  it.p0 = it.c * P.chunk_pages;
+  it.p1 = it.c == it.nchunks - 1 ? npages : it.p0 + P.chunk_pages;   // the last chunk takes the rest
+  return true;
+}
+
+template <int D>
+__global__ void __launch_bounds__(160, 1) paged_decode_tma_kernel(const __grid_constant__ CUtensorMap kvmap,
+                                                                   DecodeTmaParams P) {
+  using S = DecodeTmaSmem<D>;
+  constexpr int kChunkPerRow = D * 2 / 16;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* ring = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  float* s_o = reinterpret_cast<float*>(ring + S::kRingB);     // [4][8][D + 4]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + S::kRingB + S::kMergeB);
+  uint64_t* empty = full + S::kStages;
+  __shared__ float s_m[4][8], s_l[4][8];
+  __shared__ uint32_t s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = P.G, KH = P.KH;
+  const int total = P.B * KH * P.max_chunks;
+
+  pdl_launch();
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&kvmap);
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 4) {
+    // ---------------- producer: the warp fetches up to 32 block-table entries at once
+    // (one per lane), lane 0 issues the loads
+    const uint64_t pol = policy_evict_first();
+    bool waited = false;
+    long long g = 0;
+    for (int w = blockIdx.x; w < total; w += gridDim.x) {
+      DecodeItem it;
+      if (!decode_item(P, w, it)) continue;
+      const int* bt = P.block_tables + (size_t)it.b * P.bt_stride;
+      const int live = (P.context_lens[it.b] - 1) / kPage;
+      for (int pb = it.p0; pb < it.p1; pb += 32) {
+        const int n = min(32, it.p1 - pb);
+        const int my_page = lane < n ? bt[pb + lane] : 0;
+        for (int j = 0; j < n; ++j, ++g) {
+          const long long page = __shfl_sync(0xffffffffu, my_page, j);
+          int fail = 0;
+          if (lane == 0) {
+            const int s = (int)(g % S::kStages);
+            if (g >= S::kStages && !mbar_wait(&empty[s], (uint32_t)(((g / S::kStages) & 1) ^ 1), P.err)) {
+              fail = 1;
+            } else {
+              if (pb + j == live && !waited) {
+                pdl_wait();          // the previous kernel writes this page (this step's token)
+                waited = true;
+              }
+              const int row_k = (int)(((page * P.num_layers + P.layer) * 2 * KH + it.kvh) * kPage);
+              const int row_v = row_k + KH * kPage;
+              uint8_t* dst = ring + s * S::kStageB;
+              mbar_arrive_expect_tx(&full[s], S::kStageB);
+#pragma unroll
+              for (int q = 0; q < D / 64; ++q) {
+                tma_load_2d(dst + q * S::kBoxB, &kvmap, &full[s], q * 64, row_k, pol);
+                tma_load_2d(dst + S::kTileB + q * S::kBoxB, &kvmap, &full[s], q * 64, row_v, pol);
+              }
+            }
+          }
+          if (__shfl_sync(0xffffffffu, fail, 0)) return;
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers: warps 0-3
+  pdl_wait();
+  const int g8 = lane >> 2, c = lane & 3;
+  const float scale_log2 = P.sm_scale * 1.4426950408889634f;
+  long long g_base = 0;
+  bool ok = true;
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    DecodeItem it;
+    if (!decode_item(P, w, it)) continue;
+    const int b = it.b, kvh = it.kvh;
+    const int ctx = P.context_lens[b];
+    const int npg = it.p1 - it.p0;
+    uint32_t qb[D / 16][2];
+    {
+      const __nv_bfloat16* qrow = P.q + (size_t)b * P.ld_q + (size_t)(kvh * G + g8) * D;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        if (g8 < G) {
+          qb[kk][0] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * c);
+          qb[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * c);
+        } else {
+          qb[kk][0] = qb[kk][1] = 0u;
+        }
+      }
+    }
+    float o[D / 16][4];
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+
+    for (int j = warp; j < npg; j += 4) {
+      const long long gp = g_base + j;
+      const int s = (int)(gp % S::kStages);
+      if (ok && !mbar_wait(&full[s], (uint32_t)((gp / S::kStages) & 1), P.err)) ok = false;
+      if (ok) {
+        const uint32_t kaddr = smem_u32(ring + s * S::kStageB), vaddr = kaddr + S::kTileB;
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int ch = 2 * kk + (lane >> 4);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(kaddr + swz_box(row, ch), a0, a1, a2, a3);
+          mma_bf16_16816(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+        }
+        const int tok0 = (it.p0 + j) * kPage;
+        float x[4] = {sc[0] * scale_log2, sc[1] * scale_log2, sc[2] * scale_log2, sc[3] * scale_log2};
+        if (tok0 + g8 >= ctx) x[0] = x[1] = -INFINITY;
+        if (tok0 + g8 + 8 >= ctx) x[2] = x[3] = -INFINITY;
+        float mx[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          mx[q] = fmaxf(mx[q], __shfl_xor_sync(0xffffffffu, mx[q], 4));
+          mx[q] = fmaxf(mx[q], __shfl_xor_sync(0xffffffffu, mx[q], 8));
+          mx[q] = fmaxf(mx[q], __shfl_xor_sync(0xffffffffu, mx[q], 16));
+        }
+        float alpha[2], m_new[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          m_new[q] = fmaxf(m_run[q], mx[q]);
+          alpha[q] = (m_new[q] == -INFINITY) ? 1.f : exp2f(m_run[q] - m_new[q]);
+        }
+        float pr[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pr[i] = (m_new[i & 1] == -INFINITY) ? 0.f : exp2f(x[i] - m_new[i & 1]);
+        float rs[2] = {pr[0] + pr[2], pr[1] + pr[3]};
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          rs[q] += __shfl_xor_sync(0xffffffffu, rs[q], 4);
+          rs[q] += __shfl_xor_sync(0xffffffffu, rs[q], 8);
+          rs[q] += __shfl_xor_sync(0xffffffffu, rs[q], 16);
+          l_run[q] = l_run[q] * alpha[q] + rs[q];
+          m_run[q] = m_new[q];
+        }
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) {
+          o[mt][0] *= alpha[0];
+          o[mt][1] *= alpha[1];
+          o[mt][2] *= alpha[0];
+          o[mt][3] *= alpha[1];
+        }
+        uint32_t pb0, pb1;
+        movmatrix_trans(pack_bf16x2(pr[0], pr[1]), pb0);
+        movmatrix_trans(pack_bf16x2(pr[2], pr[3]), pb1);
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) {
+          const int row = (lane & 7) + (lane >> 4) * 8;
+          const int ch = 2 * mt + ((lane >> 3) & 1);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(vaddr + swz_box(row, ch), a0, a1, a2, a3);
+          mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);     // stage free for the producer
+    }
+    g_base += npg;
+
+    // ---- merge the 4 warps of this item
+    constexpr int kOS = D + 4;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (g8 == 0) {
+      s_m[warp][2 * c] = m_run[0];
+      s_m[warp][2 * c + 1] = m_run[1];
+      s_l[warp][2 * c] = l_run[0];
+      s_l[warp][2 * c + 1] = l_run[1];
+    }
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      float* r0 = s_o + (warp * 8 + 2 * c) * kOS + mt * 16 + g8;
+      r0[0] = o[mt][0];
+      r0[kOS] = o[mt][1];
+      r0[8] = o[mt][2];
+      r0[kOS + 8] = o[mt][3];
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const int nsplit = it.nchunks, split = it.c;
+    const size_t grp = (size_t)b * KH + kvh;
+    for (int idx = threadIdx.x; idx < G * D; idx += 128) {
+      const int h = idx / D, d = idx % D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) M = fmaxf(M, s_m[q][h]);
+      float L = 0.f, acc = 0.f;
+      if (M != -INFINITY) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float f = exp2f(s_m[q][h] - M);
+          L += s_l[q][h] * f;
+          acc += s_o[(q * 8 + h) * kOS + d] * f;
+        }
+      }
+      if (nsplit == 1) {
+        P.out[(size_t)b * P.ld_o + (size_t)(kvh * G + h) * D + d] = __float2bfloat16(L > 0.f ? acc / L : 0.f);
+      } else {
+        P.ws_o[((grp * P.max_chunks + split) * G + h) * D + d] = L > 0.f ? acc / L : 0.f;
+        if (d == 0) {
+          P.ws_ml[((grp * P.max_chunks + split) * G + h) * 2 + 0] = M;
+          P.ws_ml[((grp * P.max_chunks + split) * G + h) * 2 + 1] = L;
+        }
+      }
+    }
+    if (nsplit > 1) {
+      // the CTA finishing this sequence's last chunk merges the chunk partials
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(&P.counters[grp], 1u);
+        s_last = (prev == (uint32_t)(nsplit - 1)) ? 1u : 0u;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (s_last) {
+        __threadfence();
+        float* s_w = s_o;                          // [nsplit][G] maxima, then weights
+        float* s_ls = s_w + nsplit * G;            // [nsplit][G] sums
+        float* s_L = s_ls + nsplit * G;            // [G] totals
+        const float* ml = P.ws_ml + grp * P.max_chunks * G * 2;
+        for (int i = threadIdx.x; i < nsplit * G; i += 128) {
+          s_w[i] = __ldcg(ml + 2 * i);
+          s_ls[i] = __ldcg(ml + 2 * i + 1);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x < G) {
+          const int h = threadIdx.x;
+          float M = -INFINITY;
+          for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, s_w[sp * G + h]);
+          float L = 0.f;
+          for (int sp = 0; sp < nsplit; ++sp) {
+            const float wv = (M == -INFINITY) ? 0.f : s_ls[sp * G + h] * exp2f(s_w[sp * G + h] - M);
+            s_w[sp * G + h] = wv;
+            L += wv;
+          }
+          s_L[h] = L;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const float* po = P.ws_o + grp * P.max_chunks * G * D;
+        for (int idx = threadIdx.x; idx < G * D; idx += 128) {
+          const int h = idx / D, d = idx % D;
+          float a0 = 0.f, a1 = 0.f;
+          int sp = 0;
+          for (; sp + 1 < nsplit; sp += 2) {
+            a0 += s_w[sp * G + h] * __ldcg(po + ((size_t)sp * G + h) * D + d);
+            a1 += s_w[(sp + 1) * G + h] * __ldcg(po + ((size_t)(sp + 1) * G + h) * D + d);
+          }
+          if (sp < nsplit) a0 += s_w[sp * G + h] * __ldcg(po + ((size_t)sp * G + h) * D + d);
+          const float L = s_L[h];
+          P.out[(size_t)b * P.ld_o + (size_t)(kvh * G + h) * D + d] = __float2bfloat16(L > 0.f ? (a0 + a1) / L : 0.f);
+        }
+        if (threadIdx.x == 0) P.counters[grp] = 0u;
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");   // merge area free for the next item
+  }
+}
+
 // ============================================================== prefill
 template <int D, bool kFp8>
 struct PrefillSmem {
@@ -608,24 +938,15 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
 
 // ============================================================== host
 int decode_attention_choose_splits(int B, int KH, int max_pages) {
-  // resident CTAs per SM of the bf16 D=128 kernel (64 KB smem): 3
-  const int cap = device_sm_count() * 3;
-  const int ctas = std::max(1, B * KH);
-  const int max_s = std::max(1, std::min(64, max_pages / 2));
-  int best = 1;
-  double best_score = -1.0;
-  for (int s = 1; s <= max_s; ++s) {
-    const long total = (long)ctas * s;
-    const long waves = (total + cap - 1) / cap;
-    const double util = (double)total / (double)(waves * cap);
-    // prefer full waves; small penalty per extra split (partials + merge traffic)
-    const double score = util - 0.004 * s - (waves > 4 ? 0.05 : 0.0);
-    if (score > best_score + 1e-9) {
-      best_score = score;
-      best = s;
-    }
-  }
-  return best;
+  // Chunks per sequence for the persistent kernel (2 resident CTAs per SM): about one
+  // (sequence, head, chunk) item per resident CTA (an item's merge is serial work, so
+  // fewer, longer items win), chunks of at least 4 pages.  The
+  // per-(sequence, head, split) kernel of fp8 pages uses the same count as its splits.
+  const int slots = device_sm_count() * 2;
+  const int groups = std::max(1, B * KH);
+  int s = slots / groups;                      // about one item per resident CTA
+  s = std::min(s, std::max(1, max_pages / 4));
+  return std::max(1, std::min(s, 64));
 }
 
 size_t decode_attention_scratch_bytes(int B, int Hq, int D, int splits) {
@@ -645,6 +966,35 @@ static void launch_decode(dim3 grid, const DecodeParams& p, cudaStream_t st) {
     set[dev & 63] = true;
   }
   launch_kernel(kern, grid, dim3(128), (size_t)smem, st, p);
+}
+
+CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows);
+
+// The persistent TMA kernel is opt-in (VRM_DECODE_TMA=1 or set_decode_tma): on B200 it
+// measured 12.4 / 16.2 / 56.7 us against 8.6 / 14.6 / 48.8 us for paged_decode_kernel at
+// batch 1 / 32 / 128 (ctx 560, 40 q / 8 kv heads), which already streams 5-6 TB/s.
+static int g_decode_tma = -1;
+void set_decode_tma(bool on) { g_decode_tma = on ? 1 : 0; }
+static bool decode_tma_enabled() {
+  if (g_decode_tma < 0) {
+    const char* e = std::getenv("VRM_DECODE_TMA");
+    g_decode_tma = (e && e[0] == '1') ? 1 : 0;
+  }
+  return g_decode_tma == 1;
+}
+
+template <int D>
+static void launch_decode_tma(const CUtensorMap& map, const DecodeTmaParams& p, int grid, cudaStream_t st) {
+  constexpr int smem = DecodeTmaSmem<D>::kTotal;
+  auto kern = paged_decode_tma_kernel<D>;
+  static bool set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!set[dev & 63]) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set[dev & 63] = true;
+  }
+  launch_kernel(kern, dim3(grid), dim3(160), (size_t)smem, st, map, p);
 }
 
 void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
@@ -685,6 +1035,39 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
     VRM_REQUIRE((size_t)a.B * a.KH <= 32768, "decode attention: too many (sequence, kv head) groups");
     // counters: the upper half of the per-device array (GEMM split-K uses the lower half)
     p.counters = a.counters ? a.counters : tile_counters_get(st) + 32768;
+  }
+  // persistent TMA kernel: bf16 pages, row coordinates of the pool within int32
+  const int64_t pool_rows = a.cache_pages * a.num_layers * 2 * a.KH * kPage;
+  if (!a.cache_fp8 && a.cache_pages > 0 && pool_rows < (int64_t)INT32_MAX && decode_tma_enabled() &&
+      (reinterpret_cast<uintptr_t>(a.cache) & 15) == 0) {
+    if (splits > 1) VRM_REQUIRE(p.ws_o != nullptr && p.counters != nullptr, "decode attention: scratch");
+    DecodeTmaParams t;
+    t.q = p.q;
+    t.ld_q = p.ld_q;
+    t.layer = a.layer;
+    t.num_layers = a.num_layers;
+    t.KH = a.KH;
+    t.G = G;
+    t.B = a.B;
+    t.block_tables = a.block_tables;
+    t.bt_stride = a.bt_stride;
+    t.context_lens = a.context_lens;
+    t.sm_scale = a.sm_scale;
+    t.out = p.out;
+    t.ld_o = p.ld_o;
+    t.ws_o = p.ws_o;
+    t.ws_ml = p.ws_ml;
+    t.counters = p.counters;
+    t.max_chunks = splits;
+    t.chunk_pages = std::max(1, (std::max(1, a.max_pages) + splits - 1) / splits);
+    t.err = error_word();
+    const CUtensorMap map = make_kmajor_map(a.cache, pool_rows, a.D, a.D, kPage);
+    const int items = a.B * a.KH * splits;
+    const int grid = std::max(1, std::min(items, 2 * device_sm_count()));
+    if (a.D == 128) launch_decode_tma<128>(map, t, grid, st);
+    else launch_decode_tma<64>(map, t, grid, st);
+    VRM_CUDA_CHECK(cudaGetLastError());
+    return;
   }
   dim3 grid(a.KH, a.B, splits);
   if (a.D == 128) {

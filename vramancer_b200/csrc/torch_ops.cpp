@@ -267,6 +267,7 @@ void attn_decode(const Tensor& q, const Tensor& cache, int64_t layer, const Tens
   a.B = (int)B;
   a.max_pages = (int)block_tables.size(1);
   a.num_splits = (int)num_splits;
+  a.cache_pages = cache.size(0);
   const c10::cuda::CUDAGuard guard(q.device());
   vrm::paged_attention_decode(a, cur_stream());
 }
@@ -893,6 +894,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "TurboQuant: [..., 128] -> 64-byte records (Hadamard + PolarQuant + QJL)");
   m.def("tq_decompress", &tq_decompress, py::arg("rec"), py::arg("signs"),
         "TurboQuant: 64-byte records -> bf16 [..., 128]");
+  m.def("set_decode_tma", &vrm::set_decode_tma, py::arg("on"),
+        "use the persistent TMA decode-attention kernel for bf16 pages (default off)");
   m.def("moe_route", &moe_route_op, py::arg("logits"), py::arg("topk"), py::arg("norm_topk"), py::arg("BN"),
         "MoE router on the device: ids, weights, counts, offsets, row_of, tok_of_row, blocks, num_blocks");
   m.def("moe_layer", &moe_layer, py::arg("x"), py::arg("logits"), py::arg("topk"), py::arg("norm_topk"),

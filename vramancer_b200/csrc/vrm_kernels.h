@@ -294,8 +294,13 @@ struct DecodeAttnArgs {
   float* ws = nullptr;
   size_t ws_bytes = 0;
   uint32_t* counters = nullptr;        // >= B*KH zeroed words; null -> per-device counters
+  // pages in the pool (its first dimension): > 0 enables the persistent TMA kernel for
+  // bf16 pages (0 keeps the per-(sequence, head, split) kernel)
+  int64_t cache_pages = 0;
 };
 void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t stream);
+// Selects the persistent TMA decode kernel for bf16 pages (default off, VRM_DECODE_TMA=1).
+void set_decode_tma(bool on);
 // Scratch bytes paged_attention_decode needs for a given split count.
 size_t decode_attention_scratch_bytes(int B, int Hq, int D, int splits);
 int decode_attention_choose_splits(int B, int KH, int max_pages);
