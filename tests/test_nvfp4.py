@@ -118,3 +118,56 @@ def test_nvfp4_model_generates():
     out = llm.generate([[1, 2, 3, 4], list(range(40))], SamplingParams(max_tokens=6))
     assert all(len(o.output_ids) == 6 for o in out)
     llm.runner.release_graphs()
+
+
+# ----------------------------------------------------------------------------- block-scaled (W4A4) path
+def test_rows_ref_roundtrip_cpu():
+    from vramancer_b200.quant import nvfp4 as nv
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(130, 512, generator=g) * 3
+    q, atoms, gs = nv.quantize_rows_ref(x)
+    assert q.shape == (256, 256) and atoms.numel() == 2 * 8 * 512 and gs.shape == (256,)
+    deq = nv.dequantize_rows_ref(q, atoms, gs, 130)
+    rel = (deq - x).norm() / x.norm()
+    assert rel < 0.15                               # 4-bit values with e4m3 scales per 16
+    assert torch.equal(nv.atoms_to_sf(nv.sf_to_atoms(torch.arange(256 * 32).to(torch.uint8).view(256, 32)), 256, 512),
+                       torch.arange(256 * 32).to(torch.uint8).view(256, 32))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("valid,K,per_row", [(200, 512, True), (128, 1024, False), (1, 256, True)])
+def test_rows_quantize_matches_ref(valid, K, per_row, cuda_errors_clean):
+    from vramancer_b200 import ops
+    from vramancer_b200.quant import nvfp4 as nv
+    g = torch.Generator().manual_seed(valid + K)
+    x = (torch.randn(valid, K, generator=g) * 2).bfloat16()
+    gs = None if per_row else nv.global_scale(x.float())
+    rows = (valid + 127) // 128 * 128
+    q, atoms, gr = ops.native().nvfp4_rows_quantize(x.cuda(), rows, gs.cuda() if gs is not None else None)
+    rq, ratoms, rg = nv.quantize_rows_ref(x, rows, gs)
+    assert torch.equal(q.cpu(), rq)
+    assert torch.equal(atoms.cpu(), ratoms)
+    if per_row:
+        assert torch.equal(gr.cpu(), rg)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(128, 128, 256), (200, 384, 1024), (1, 256, 512), (300, 1280, 5120)])
+def test_blockscaled_gemm_matches_dequant(M, N, K, cuda_errors_clean):
+    """tcgen05 kind::mxf4nvf4 GEMM against fp32 math on the dequantised operands."""
+    from vramancer_b200 import ops
+    from vramancer_b200.quant import nvfp4 as nv
+    g = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g).bfloat16()
+    w = (torch.randn(N, K, generator=g) * 0.02).bfloat16()
+    gw = nv.global_scale(w.float())
+    Mp = (M + 127) // 128 * 128
+    qa, sfa, gsa = ops.native().nvfp4_rows_quantize(x.cuda(), Mp, None)
+    qb, sfb, _ = ops.native().nvfp4_rows_quantize(w.cuda(), N, gw.cuda())
+    out = ops.native().nvfp4_bs_gemm(qa, sfa, gsa, M, qb, sfb, gw.cuda())
+    torch.cuda.synchronize()
+    a = nv.dequantize_rows_ref(qa, sfa, gsa, M)
+    b = nv.dequantize_rows_ref(qb, sfb, gw, N)
+    ref = a @ b.t()
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, (err, ref.abs().max().item())

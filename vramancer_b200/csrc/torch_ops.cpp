@@ -515,6 +515,49 @@ Tensor tq_decompress(const Tensor& rec, const Tensor& signs) {
 // the SiLU*up epilogue, grouped down GEMM, weighted combine (+ add, e.g. the shared
 // expert).  x [T, H], ids int64 [T, topk], weights fp32 [T, topk], gate_up [E, 2I, H]
 // (interleaved gate / up rows), down [E, H, I].  No host synchronisation.
+// NVFP4 rows (block-scaled format of nvfp4_bs.cu): returns q [rows, K/2], the scale
+// atoms, and the per-row scales (empty when gs_tensor is given).
+std::vector<Tensor> nvfp4_rows_quantize(const Tensor& x, int64_t rows, const OptT& gs_tensor) {
+  check_bf16_2d(x, "nvfp4 rows x");
+  const int64_t valid = x.size(0), K = x.size(1);
+  TORCH_CHECK(rows >= valid && rows % 128 == 0 && K % 256 == 0, "nvfp4 rows: rows % 128, K % 256");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto o8 = x.options().dtype(torch::kUInt8);
+  auto q = torch::empty({rows, K / 2}, o8);
+  auto sf = torch::empty({rows / 128 * (K / 64) * 512}, o8);
+  Tensor gs_rows;
+  const float* gt = nullptr;
+  if (has(gs_tensor)) {
+    TORCH_CHECK(gs_tensor->scalar_type() == torch::kFloat32 && gs_tensor->numel() == 1, "nvfp4 rows: gs fp32 [1]");
+    same_device_opt(x, {&gs_tensor}, "nvfp4 rows");
+    gt = gs_tensor->data_ptr<float>();
+    gs_rows = torch::empty({0}, x.options().dtype(torch::kFloat32));
+  } else {
+    gs_rows = torch::empty({rows}, x.options().dtype(torch::kFloat32));
+  }
+  vrm::nvfp4_rows_quantize(x.data_ptr(), x.stride(0), (int)valid, (int)rows, (int)K, gt,
+                           gt ? nullptr : gs_rows.data_ptr<float>(), q.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>(),
+                           cur_stream());
+  return {q, sf, gs_rows};
+}
+
+Tensor nvfp4_bs_gemm(const Tensor& qa, const Tensor& sfa, const Tensor& gsa, int64_t M, const Tensor& qb,
+                     const Tensor& sfb, const Tensor& gsb) {
+  for (const Tensor* t : {&qa, &sfa, &qb, &sfb})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kUInt8 && t->is_contiguous(), "nvfp4 bs gemm: uint8 tensors");
+  TORCH_CHECK(gsa.scalar_type() == torch::kFloat32 && gsb.scalar_type() == torch::kFloat32 && gsb.numel() == 1,
+              "nvfp4 bs gemm: fp32 scales");
+  same_device(qa, {&sfa, &gsa, &qb, &sfb, &gsb}, "nvfp4 bs gemm");
+  const int64_t Mpad = qa.size(0), K = qa.size(1) * 2, N = qb.size(0);
+  TORCH_CHECK(qb.size(1) * 2 == K && gsa.numel() >= M && M <= Mpad, "nvfp4 bs gemm: shapes");
+  const c10::cuda::CUDAGuard guard(qa.device());
+  auto out = torch::empty({M, N}, qa.options().dtype(torch::kBFloat16));
+  vrm::nvfp4_bs_gemm(qa.data_ptr<uint8_t>(), sfa.data_ptr<uint8_t>(), gsa.data_ptr<float>(), (int)M, (int)Mpad,
+                     qb.data_ptr<uint8_t>(), sfb.data_ptr<uint8_t>(), gsb.data_ptr<float>(), (int)N, (int)K,
+                     out.data_ptr(), N, cur_stream());
+  return out;
+}
+
 // Expert plan of a MoE layer: per-expert counts and row offsets, the grouped row of every
 // (token, k) pair, the token of every grouped row and the list of token blocks
 // (expert, first row, rows, 0) that drives the grouped GEMM.
@@ -896,6 +939,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "TurboQuant: 64-byte records -> bf16 [..., 128]");
   m.def("set_decode_tma", &vrm::set_decode_tma, py::arg("on"),
         "use the persistent TMA decode-attention kernel for bf16 pages (default off)");
+  m.def("nvfp4_rows_quantize", &nvfp4_rows_quantize, py::arg("x"), py::arg("rows"), py::arg("gs_tensor"),
+        "NVFP4 rows for the block-scaled GEMM: codes, 128x4 scale atoms, per-row scales");
+  m.def("nvfp4_bs_gemm", &nvfp4_bs_gemm, py::arg("qa"), py::arg("sfa"), py::arg("gsa"), py::arg("M"), py::arg("qb"),
+        py::arg("sfb"), py::arg("gsb"), "NVFP4 x NVFP4 GEMM on tcgen05 kind::mxf4nvf4 (bf16 out)");
   m.def("moe_route", &moe_route_op, py::arg("logits"), py::arg("topk"), py::arg("norm_topk"), py::arg("BN"),
         "MoE router on the device: ids, weights, counts, offsets, row_of, tok_of_row, blocks, num_blocks");
   m.def("moe_layer", &moe_layer, py::arg("x"), py::arg("logits"), py::arg("topk"), py::arg("norm_topk"),

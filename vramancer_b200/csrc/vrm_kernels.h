@@ -140,6 +140,17 @@ struct MoeCombineArgs {
 };
 void moe_combine(const MoeCombineArgs& a, cudaStream_t stream);
 
+// ---------------------------------------------------------------- NVFP4 x NVFP4 (nvfp4_bs.cu)
+// Rows [0, valid) of x (bf16 [*, K], K % 256 == 0) to e2m1 codes q [rows, K/2] and e4m3
+// block scales in 128x4 atoms; rows [valid, rows) zero.  gs_tensor: one fp32 scale for
+// the tensor (weights); else a per-row scale amax / (6 * 448) is written to gs_rows.
+void nvfp4_rows_quantize(const void* x, int64_t ldx, int valid, int rows, int K, const float* gs_tensor,
+                         float* gs_rows, uint8_t* q, uint8_t* sf, cudaStream_t stream);
+// out[m, n] = sum_k A[m, k] B[n, k] * gsa[m] * gsb on tcgen05 kind::mxf4nvf4 (bf16 out,
+// rows m < M written); A padded to Mpad rows, N % 128 == 0, K % 256 == 0.
+void nvfp4_bs_gemm(const uint8_t* qa, const uint8_t* sfa, const float* gsa, int M, int Mpad, const uint8_t* qb,
+                   const uint8_t* sfb, const float* gsb, int N, int K, void* out, int64_t ldo, cudaStream_t stream);
+
 // ---------------------------------------------------------------- expert parallelism (moe_ep.cu)
 // Expert-parallel MoE over peer memory.  Rank r owns experts [r * E_local, (r + 1) *
 // E_local).  Every rank owns symmetric buffers (cudaMalloc + CUDA IPC), each in two

@@ -165,6 +165,56 @@ def dequantize_ref(w: NVFP4Weight) -> torch.Tensor:
     return vals * sf * w.gs.cpu().float()
 
 
+# ---------------------------------------------------------------- block-scaled rows (tcgen05 mxf4nvf4 format)
+# Row-major codes q [rows, K/2] (element 2i in the low nibble of byte i) and e4m3 block
+# scales in 512-byte atoms of 128 rows x 4 blocks: atom (row // 128, k // 64), byte
+# (row % 32) * 16 + (row // 32 % 4) * 4 + k // 16 % 4 (csrc/nvfp4_bs.cu).
+def sf_to_atoms(s8: torch.Tensor) -> torch.Tensor:
+    """uint8 [rows, K/16] row-major block scales (rows % 128 == 0) -> the atom layout."""
+    rows, nb = s8.shape
+    return s8.view(rows // 128, 4, 32, nb // 4, 4).permute(0, 3, 2, 1, 4).reshape(-1).contiguous()
+
+
+def atoms_to_sf(atoms: torch.Tensor, rows: int, K: int) -> torch.Tensor:
+    return atoms.view(rows // 128, K // 64, 32, 4, 4).permute(0, 3, 2, 1, 4).reshape(rows, K // 16)
+
+
+def quantize_rows_ref(x: torch.Tensor, rows: Optional[int] = None, gs: Optional[torch.Tensor] = None):
+    """Host restatement of nvfp4_rows_quantize: (q, scale atoms, per-row gs or empty)."""
+    x = x.detach().cpu().float()
+    valid, K = x.shape
+    rows = rows or (valid + 127) // 128 * 128
+    if gs is None:
+        amax = x.abs().amax(1)
+        gsr = torch.where(amax > 0, amax / torch.full_like(amax, FP4_MAX * E4M3_MAX), torch.ones_like(amax))
+    else:
+        gsr = gs.detach().cpu().float().reshape(1).expand(valid)
+    bam = x.view(valid, K // 16, 16).abs().amax(-1)
+    s8 = (bam / FP4_MAX / gsr[:, None]).clamp(max=E4M3_MAX).to(torch.float8_e4m3fn).view(torch.uint8)
+    denom = (s8.view(torch.float8_e4m3fn).float() * gsr[:, None]).repeat_interleave(16, dim=1)
+    v = torch.where(denom > 0, x / denom, torch.zeros_like(denom))
+    codes = e2m1_codes(v)
+    q = torch.zeros(rows, K // 2, dtype=torch.uint8)
+    q[:valid] = codes[:, 0::2] | (codes[:, 1::2] << 4)
+    sp = torch.zeros(rows, K // 16, dtype=torch.uint8)
+    sp[:valid] = s8
+    g = torch.zeros(rows) if gs is None else torch.empty(0)
+    if gs is None:
+        g[:valid] = gsr
+    return q, sf_to_atoms(sp), g
+
+
+def dequantize_rows_ref(q: torch.Tensor, atoms: torch.Tensor, gs: torch.Tensor, valid: int) -> torch.Tensor:
+    """fp32 [valid, K] from block-scaled rows (gs: per-row [rows] or per-tensor [1])."""
+    q = q.cpu()
+    rows, K = q.shape[0], q.shape[1] * 2
+    codes = torch.stack([q & 15, q >> 4], dim=-1).reshape(rows, K)
+    sf = atoms_to_sf(atoms.cpu(), rows, K).view(torch.float8_e4m3fn).float().repeat_interleave(16, dim=1)
+    g = gs.cpu().float()
+    g = g[:rows].view(rows, 1) if g.numel() > 1 else g.view(1, 1)
+    return (e2m1_values(codes) * sf * g)[:valid]
+
+
 # ---------------------------------------------------------------- public API
 def quantize(w: torch.Tensor) -> NVFP4Weight:
     """NVFP4 copy of a 2-D weight [N, K] (N % 16 == 0, K % 64 == 0), on w's device."""
