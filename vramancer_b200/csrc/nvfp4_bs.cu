@@ -194,6 +194,9 @@ struct BsParams {
   const float* gsb;      // [1]
   __nv_bfloat16* out;
   int64_t ldo;
+  const __nv_bfloat16* bias;      // [N] or null
+  const __nv_bfloat16* residual;  // [M, ldo] or null (may alias out)
+  int silu_mul;          // 1: out[m, n/2] = silu(y[m, n]) * y[m, n+1] over interleaved pairs
   int M, N, k_tiles, kb64;
   uint32_t* err;
 };
@@ -235,6 +238,8 @@ __global__ void __launch_bounds__(kBsThreads, 1) nvfp4_bs_gemm_kernel(const __gr
   const float* gsa = P.gsa;
   const float* gsb = P.gsb;
   pdl_wait_for(sfa, sfb, gsa, gsb);
+  opaque_after_wait(P.bias);
+  opaque_after_wait(P.residual);
 
   if (warp == 0 && lane == 0) {
     // ---------------- producer
@@ -293,15 +298,58 @@ __global__ void __launch_bounds__(kBsThreads, 1) nvfp4_bs_gemm_kernel(const __gr
       tmem_ld_32x32b_x16(t_lane + (uint32_t)c0, r);
       tmem_wait_ld();
       if (!ok || m >= P.M || n0 + c0 >= P.N) continue;
+      const int n = n0 + c0;
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]) * g;
+      if (P.bias) {
+        const uint4 b0 = *reinterpret_cast<const uint4*>(P.bias + n);
+        const uint4 b1 = *reinterpret_cast<const uint4*>(P.bias + n + 8);
+        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(&b0);
+        const uint32_t* q1 = reinterpret_cast<const uint32_t*>(&b1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[2 * j] += bf16_lo(q0[j]);
+          v[2 * j + 1] += bf16_hi(q0[j]);
+          v[8 + 2 * j] += bf16_lo(q1[j]);
+          v[8 + 2 * j + 1] += bf16_hi(q1[j]);
+        }
+      }
+      if (P.silu_mul) {
+        // interleaved (gate, up) pairs -> 8 outputs at column n / 2
+        uint4 o;
+        uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float g0 = v[4 * j], u0 = v[4 * j + 1], g1 = v[4 * j + 2], u1 = v[4 * j + 3];
+          po[j] = pack_bf16x2(g0 / (1.f + __expf(-g0)) * u0, g1 / (1.f + __expf(-g1)) * u1);
+        }
+        *reinterpret_cast<uint4*>(P.out + (size_t)m * P.ldo + n / 2) = o;
+        continue;
+      }
+      __nv_bfloat16* dst = P.out + (size_t)m * P.ldo + n;
+      if (P.residual) {
+        const __nv_bfloat16* rs = P.residual + (size_t)m * P.ldo + n;
+        const uint4 r0 = *reinterpret_cast<const uint4*>(rs);
+        const uint4 r1 = *reinterpret_cast<const uint4*>(rs + 8);
+        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(&r0);
+        const uint32_t* q1 = reinterpret_cast<const uint32_t*>(&r1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[2 * j] += bf16_lo(q0[j]);
+          v[2 * j + 1] += bf16_hi(q0[j]);
+          v[8 + 2 * j] += bf16_lo(q1[j]);
+          v[8 + 2 * j + 1] += bf16_hi(q1[j]);
+        }
+      }
       uint4 o0, o1;
       uint32_t* p0 = reinterpret_cast<uint32_t*>(&o0);
       uint32_t* p1 = reinterpret_cast<uint32_t*>(&o1);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        p0[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * g, __uint_as_float(r[2 * j + 1]) * g);
-        p1[j] = pack_bf16x2(__uint_as_float(r[8 + 2 * j]) * g, __uint_as_float(r[8 + 2 * j + 1]) * g);
+        p0[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+        p1[j] = pack_bf16x2(v[8 + 2 * j], v[8 + 2 * j + 1]);
       }
-      __nv_bfloat16* dst = P.out + (size_t)m * P.ldo + n0 + c0;
       *reinterpret_cast<uint4*>(dst) = o0;
       *reinterpret_cast<uint4*>(dst + 8) = o1;
     }
@@ -343,7 +391,9 @@ void nvfp4_rows_quantize(const void* x, int64_t ldx, int valid, int rows, int K,
 }
 
 void nvfp4_bs_gemm(const uint8_t* qa, const uint8_t* sfa, const float* gsa, int M, int Mpad, const uint8_t* qb,
-                   const uint8_t* sfb, const float* gsb, int N, int K, void* out, int64_t ldo, cudaStream_t st) {
+                   const uint8_t* sfb, const float* gsb, int N, int K, void* out, int64_t ldo, cudaStream_t st,
+                   const void* bias, const void* residual, int silu_mul) {
+  VRM_REQUIRE(!silu_mul || residual == nullptr, "nvfp4 block-scaled gemm: silu_mul takes no residual");
   VRM_REQUIRE(K % 256 == 0 && N % kBsBN == 0 && Mpad % kBsBM == 0 && M <= Mpad,
               "nvfp4 block-scaled gemm: K % 256, N % 128, padded M % 128");
   VRM_REQUIRE(ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0, "nvfp4 block-scaled gemm: out alignment");
@@ -357,6 +407,9 @@ void nvfp4_bs_gemm(const uint8_t* qa, const uint8_t* sfa, const float* gsa, int 
   p.gsb = gsb;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
+  p.silu_mul = silu_mul;
   p.M = M;
   p.N = N;
   p.k_tiles = K / 256;

@@ -542,7 +542,8 @@ std::vector<Tensor> nvfp4_rows_quantize(const Tensor& x, int64_t rows, const Opt
 }
 
 Tensor nvfp4_bs_gemm(const Tensor& qa, const Tensor& sfa, const Tensor& gsa, int64_t M, const Tensor& qb,
-                     const Tensor& sfb, const Tensor& gsb) {
+                     const Tensor& sfb, const Tensor& gsb, const OptT& bias, const OptT& residual, int64_t epilogue,
+                     const OptT& out_opt) {
   for (const Tensor* t : {&qa, &sfa, &qb, &sfb})
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kUInt8 && t->is_contiguous(), "nvfp4 bs gemm: uint8 tensors");
   TORCH_CHECK(gsa.scalar_type() == torch::kFloat32 && gsb.scalar_type() == torch::kFloat32 && gsb.numel() == 1,
@@ -551,10 +552,19 @@ Tensor nvfp4_bs_gemm(const Tensor& qa, const Tensor& sfa, const Tensor& gsa, int
   const int64_t Mpad = qa.size(0), K = qa.size(1) * 2, N = qb.size(0);
   TORCH_CHECK(qb.size(1) * 2 == K && gsa.numel() >= M && M <= Mpad, "nvfp4 bs gemm: shapes");
   const c10::cuda::CUDAGuard guard(qa.device());
-  auto out = torch::empty({M, N}, qa.options().dtype(torch::kBFloat16));
+  const int64_t No = epilogue == vrm::kEpiSiluMul ? N / 2 : N;
+  Tensor out = has(out_opt) ? *out_opt : torch::empty({M, No}, qa.options().dtype(torch::kBFloat16));
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.size(0) == M && out.size(1) == No,
+              "nvfp4 bs gemm: out bf16 [M, N or N/2]");
+  if (has(bias)) TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->numel() == N, "nvfp4 bs gemm: bias");
+  if (has(residual))
+    TORCH_CHECK(residual->scalar_type() == torch::kBFloat16 && residual->is_contiguous() && residual->sizes() == out.sizes(),
+                "nvfp4 bs gemm: residual [M, N]");
+  same_device_opt(qa, {&bias, &residual, &out_opt}, "nvfp4 bs gemm");
   vrm::nvfp4_bs_gemm(qa.data_ptr<uint8_t>(), sfa.data_ptr<uint8_t>(), gsa.data_ptr<float>(), (int)M, (int)Mpad,
                      qb.data_ptr<uint8_t>(), sfb.data_ptr<uint8_t>(), gsb.data_ptr<float>(), (int)N, (int)K,
-                     out.data_ptr(), N, cur_stream());
+                     out.data_ptr(), No, cur_stream(), has(bias) ? bias->data_ptr() : nullptr,
+                     has(residual) ? residual->data_ptr() : nullptr, epilogue == vrm::kEpiSiluMul ? 1 : 0);
   return out;
 }
 
@@ -942,7 +952,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_rows_quantize", &nvfp4_rows_quantize, py::arg("x"), py::arg("rows"), py::arg("gs_tensor"),
         "NVFP4 rows for the block-scaled GEMM: codes, 128x4 scale atoms, per-row scales");
   m.def("nvfp4_bs_gemm", &nvfp4_bs_gemm, py::arg("qa"), py::arg("sfa"), py::arg("gsa"), py::arg("M"), py::arg("qb"),
-        py::arg("sfb"), py::arg("gsb"), "NVFP4 x NVFP4 GEMM on tcgen05 kind::mxf4nvf4 (bf16 out)");
+        py::arg("sfb"), py::arg("gsb"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
+        py::arg("epilogue") = 0, py::arg("out") = py::none(),
+        "NVFP4 x NVFP4 GEMM on tcgen05 kind::mxf4nvf4 (bf16 out, bias / residual / silu_mul epilogue)");
   m.def("moe_route", &moe_route_op, py::arg("logits"), py::arg("topk"), py::arg("norm_topk"), py::arg("BN"),
         "MoE router on the device: ids, weights, counts, offsets, row_of, tok_of_row, blocks, num_blocks");
   m.def("moe_layer", &moe_layer, py::arg("x"), py::arg("logits"), py::arg("topk"), py::arg("norm_topk"),

@@ -148,8 +148,11 @@ void nvfp4_rows_quantize(const void* x, int64_t ldx, int valid, int rows, int K,
                          float* gs_rows, uint8_t* q, uint8_t* sf, cudaStream_t stream);
 // out[m, n] = sum_k A[m, k] B[n, k] * gsa[m] * gsb on tcgen05 kind::mxf4nvf4 (bf16 out,
 // rows m < M written); A padded to Mpad rows, N % 128 == 0, K % 256 == 0.
+// Epilogue: + bias[n], + residual[m, n] (may alias out), or SiLU(gate) * up over
+// interleaved weight-row pairs (out has N / 2 columns).
 void nvfp4_bs_gemm(const uint8_t* qa, const uint8_t* sfa, const float* gsa, int M, int Mpad, const uint8_t* qb,
-                   const uint8_t* sfb, const float* gsb, int N, int K, void* out, int64_t ldo, cudaStream_t stream);
+                   const uint8_t* sfb, const float* gsb, int N, int K, void* out, int64_t ldo, cudaStream_t stream,
+                   const void* bias = nullptr, const void* residual = nullptr, int silu_mul = 0);
 
 // ---------------------------------------------------------------- expert parallelism (moe_ep.cu)
 // Expert-parallel MoE over peer memory.  Rank r owns experts [r * E_local, (r + 1) *

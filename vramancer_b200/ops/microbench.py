@@ -141,6 +141,28 @@ def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4
             "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
 
 
+def bench_nvfp4_prefill(m, n, k, iters=20):
+    """Prefill-sized GEMM three ways: bf16 tcgen05 GEMM, NVFP4 W4A4 block-scaled tcgen05
+    GEMM (codes already quantised), and W4A4 including the activation quantisation."""
+    from ..quant import nvfp4 as nv
+    _, tflops, src = peaks()
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.02
+    qw = nv.quantize(w)
+    mp = (m + 127) // 128 * 128
+    qa, sfa, gsa = native().nvfp4_rows_quantize(x, mp, None)
+    flop = 2.0 * m * n * k
+    t_bf16 = time_it(lambda: linear(x, w), iters)
+    t_gemm = time_it(lambda: native().nvfp4_bs_gemm(qa, sfa, gsa, m, qw.q_rows, qw.s_atoms, qw.gs), iters)
+    t_full = time_it(lambda: linear(x, qw), iters)
+    r = {"kernel": "nvfp4_prefill", "m": m, "n": n, "k": k, "bf16_us": round(t_bf16, 2),
+         "bf16_tflops": round(flop / t_bf16 / 1e6, 1), "w4a4_gemm_us": round(t_gemm, 2),
+         "w4a4_gemm_tflops": round(flop / t_gemm / 1e6, 1), "w4a4_with_act_quant_us": round(t_full, 2),
+         "w4a4_with_act_quant_tflops": round(flop / t_full / 1e6, 1), "peaks": src,
+         "bf16_frac_of_measured": round(flop / t_bf16 / 1e6 / tflops, 3)}
+    return r
+
+
 def trace_gemm(m, n, k):
     """Per-CTA timelines of two back-to-back stream-K decode GEMM launches on cold
     weights (us from the first launch's earliest CTA entry)."""
@@ -176,7 +198,7 @@ QWEN14B_DECODE = [("qkv", 7168, 5120), ("o_proj", 5120, 5120), ("gate_up", 27648
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "nvfp4", "decode-attn", "all", "trace"])
+    ap.add_argument("what", choices=["gemm", "nvfp4", "nvfp4-prefill", "decode-attn", "all", "trace"])
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--n", type=int, default=5120)
     ap.add_argument("--k", type=int, default=13824)
@@ -199,6 +221,9 @@ def main(argv=None):
         for m in ((a.m,) if a.m != 1 else (1, 8, 32)):
             for n, k in shapes:
                 print(json.dumps(bench_nvfp4(m, n, k, a.iters)))
+    elif a.what == "nvfp4-prefill":
+        for n, k in ([(a.n, a.k)] if a.n != 5120 or a.k != 13824 else [(27648, 5120), (5120, 13824), (7168, 5120)]):
+            print(json.dumps(bench_nvfp4_prefill(a.m if a.m != 1 else 4096, n, k, a.iters)))
     elif a.what == "decode-attn":
         print(json.dumps(bench_decode_attn(a.batch, a.ctx, fp8=a.fp8, iters=a.iters)))
     else:

@@ -1,8 +1,9 @@
 """NVFP4 weights (e2m1 values, e4m3 scale per 16 K-elements, fp32 per-tensor scale).
 
     w = quantize(w_bf16)            # NVFP4Weight, on w's device
-    y = ops.linear(x, w, ...)       # W4A16 tensor-core GEMM for M <= 32 (decode),
-                                    # dequantise + bf16 GEMM above (prefill)
+    y = ops.linear(x, w, ...)       # W4A16 warp-MMA GEMM for M <= 32 (decode); above,
+                                    # fused activation quantisation + W4A4 block-scaled
+                                    # tcgen05 GEMM (csrc/nvfp4_bs.cu, prefill)
     weights = quantize_model_weights(weights, cfg)    # every layer projection
 
 Convention: gs = amax / (6 * 448); block scale s = e4m3_rn_sat(block_amax / 6 / gs);
@@ -16,6 +17,7 @@ reference's activation quantisation, W4A4).  Here weights are W4 and activations
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Dict, Optional
 
@@ -39,6 +41,10 @@ class NVFP4Weight:
     gs: torch.Tensor     # fp32 [1], per-tensor scale
     N: int
     K: int
+    # the same codes and scales in the block-scaled layout of csrc/nvfp4_bs.cu (row-major
+    # codes [N, K/2] + 128x4 scale atoms) for the tcgen05 W4A4 GEMM of prefill batches
+    q_rows: Optional[torch.Tensor] = None
+    s_atoms: Optional[torch.Tensor] = None
     _vrm_quant = "nvfp4"
 
     @property
@@ -58,7 +64,8 @@ class NVFP4Weight:
         return self.q.is_cuda
 
     def nbytes(self) -> int:
-        return self.q.numel() + self.s.numel() + 4
+        extra = 0 if self.q_rows is None else self.q_rows.numel() + self.s_atoms.numel()
+        return self.q.numel() + self.s.numel() + 4 + extra
 
     def dequantize(self) -> torch.Tensor:
         if self.q.is_cuda:
@@ -68,11 +75,19 @@ class NVFP4Weight:
     def linear(self, x: torch.Tensor, bias: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None,
                epilogue: int = ops.EPI_NONE, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         if x.is_cuda and x.shape[0] <= 32:
+            # decode: W4A16, bandwidth-bound (fragment-order codes, warp-level MMAs)
             if out is None:
                 n = self.N // 2 if epilogue == ops.EPI_SILU_MUL else self.N
                 out = torch.empty(x.shape[0], n, dtype=x.dtype, device=x.device)
             ops.native().nvfp4_gemm_out(x, self.q, self.s, self.gs, self.N, bias, out, epilogue, residual)
             return out
+        if x.is_cuda and self.q_rows is not None and x.dtype == torch.bfloat16:
+            # prefill: fused activation quantisation (per-token scale) + W4A4 block-scaled
+            # tcgen05 GEMM with the epilogue in the kernel
+            M = x.shape[0]
+            qa, sfa, gsa = ops.native().nvfp4_rows_quantize(x.contiguous(), (M + 127) // 128 * 128, None)
+            return ops.native().nvfp4_bs_gemm(qa, sfa, gsa, M, self.q_rows, self.s_atoms, self.gs, bias, residual,
+                                              epilogue, out)
         return ops.linear(x, self.dequantize(), bias, out=out, epilogue=epilogue, residual=residual)
 
 
@@ -225,7 +240,11 @@ def quantize(w: torch.Tensor) -> NVFP4Weight:
     w = w.to(torch.bfloat16).contiguous()
     gs = global_scale(w)
     q, s = ops.native().nvfp4_quantize(w, gs)
-    return NVFP4Weight(q, s, gs, w.shape[0], w.shape[1])
+    qr = sa = None
+    N, K = w.shape
+    if N % 128 == 0 and K % 256 == 0 and os.environ.get("VRM_NVFP4_PREFILL", "w4a4") == "w4a4":
+        qr, sa, _ = ops.native().nvfp4_rows_quantize(w, N, gs)
+    return NVFP4Weight(q, s, gs, N, K, qr, sa)
 
 
 def quantizable(w: torch.Tensor) -> bool:
