@@ -937,6 +937,18 @@ CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t cols, int64_t
   return map;
 }
 
+// Prefill tiles: 3 stages (96 KB) so two CTAs share an SM and one's epilogue overlaps
+// the other's main loop: 10-27% faster than one 6-stage CTA per SM on B200 at M = 512
+// and 4096 of the Qwen2.5-14B projections (0.63-0.75 of cuBLAS instead of 0.56-0.65).
+// VRM_GEMM_PREFILL_STAGES=6 restores the single-CTA layout.
+static int prefill_stages() {
+  static const int v = [] {
+    const char* e = std::getenv("VRM_GEMM_PREFILL_STAGES");
+    return (e && e[0] == '6') ? 6 : 3;
+  }();
+  return v;
+}
+
 template <int BN, int STAGES, bool kSwap>
 static void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const EpiParams& ep, int K, int a_tiles,
                         int b_tiles, int full_tiles, int tail_splits, cudaStream_t stream) {
@@ -1177,7 +1189,10 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     }
     const CUtensorMap ma = make_kmajor_map(a.x, a.M, a.K, a.ldx, kBM);
     const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, BN);
-    launch_gemm<BN, 6, false>(ma, mb, ep, a.K, a_tiles, b_tiles, full, tail_splits, stream);
+    if (prefill_stages() == 3)   // two CTAs per SM: one's epilogue overlaps the other's main loop
+      launch_gemm<BN, 3, false>(ma, mb, ep, a.K, a_tiles, b_tiles, full, tail_splits, stream);
+    else
+      launch_gemm<BN, 6, false>(ma, mb, ep, a.K, a_tiles, b_tiles, full, tail_splits, stream);
   }
 }
 

@@ -86,10 +86,23 @@ def bench_gemm(m, n, k, iters=50, copies=None, residual=False):
     us = time_it(fn, iters)
     byts = wbytes + m * k * 2 + m * n * 2 * (2 if residual else 1)
     flops = 2.0 * m * n * k
-    return {"kernel": "gemm", "m": m, "n": n, "k": k, "residual": residual, "us": round(us, 2),
-            "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3),
-            "tflops": round(flops / us / 1e6, 1), "frac_tc": round(flops / us / 1e6 / tflops, 3),
-            "peaks": src}
+    r = {"kernel": "gemm", "m": m, "n": n, "k": k, "residual": residual, "us": round(us, 2),
+         "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3),
+         "tflops": round(flops / us / 1e6, 1), "frac_tc": round(flops / us / 1e6 / tflops, 3),
+         "peaks": src}
+    if m >= 256 and not residual:
+        # the library GEMM on the same operands, for comparison only
+        wt = [w.t() for w in ws]
+        st2 = [0]
+
+        def lib():
+            torch.matmul(x, wt[st2[0] % copies], out=out)
+            st2[0] += 1
+
+        lus = time_it(lib, iters)
+        r["cublas_us"] = round(lus, 2)
+        r["vs_cublas"] = round(lus / us, 3)
+    return r
 
 
 def bench_nvfp4(m, n, k, iters=50, copies=None):
