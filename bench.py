@@ -5,8 +5,11 @@ CUDA-graph decode.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs under torchrun (one process per GPU, NCCL) as tensor parallelism TP=N with
-the global batch fixed at 32 (strong scaling).  Rank 0 prints one JSON line.
+N > 1 runs under torchrun (one process per GPU, NCCL).  By default the batch-32 value is
+measured on N data-parallel replicas (global batch 32 x N, weak scaling: the 14B model
+fits on one B200), and the single-stream numbers (bs1, TTFT) and a strong-scaling
+batch-32 figure ("tp") on the same N GPUs as tensor parallelism TP=N;
+--parallel tp measures everything at TP=N.  Rank 0 prints one JSON line.
 
 value   = aggregate decode tok/s at batch 32 (prompt 512), device-timed with CUDA
           events over exactly K decode steps (inputs staged on the device), max over
@@ -49,6 +52,8 @@ def parse_args(argv=None):
     p.add_argument("--kv-dtype", default="bf16")
     p.add_argument("--ttft-runs", type=int, default=5)
     p.add_argument("--num-layers", type=int, default=None, help="debug only: truncates the model (invalid run)")
+    p.add_argument("--parallel", choices=["dp", "tp"], default=None,
+                   help="N > 1: data-parallel replicas (default; bs1 / TTFT still measured at TP=N) or TP=N only")
     return p.parse_args(argv)
 
 
@@ -71,7 +76,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
@@ -126,129 +131,165 @@ def run_ours(args):
     rank, world = info.rank, info.world_size
     dev = torch.device("cuda", info.local_rank)
     torch.cuda.set_device(dev)
-    tp = comm.tp_context()
+    mode = args.parallel or ("dp" if world > 1 else "tp")
     B, P = args.batch, args.prompt_len
     steps, warm = args.steps, args.warmup
     max_len = P + warm + steps + 64
     kv_pages = (B + 2) * ((max_len + 15) // 16) * 2 + 64
-    llm = LLM(args.model, device=str(dev), kv_cache_dtype=args.kv_dtype, max_batch=B, max_model_len=max_len,
-              kv_pages=kv_pages, enable_prefix_cache=False, seed=1234, tp=tp, num_layers=args.num_layers)
-    runner, eng = llm.runner, llm.engine
-    cfg = llm.cfg
-    g = torch.Generator().manual_seed(42)
 
-    def prompts(n):
-        return [torch.randint(0, cfg.vocab_size, (P,), generator=g).tolist() for _ in range(n)]
+    def measure(tp, want_bs32=True, want_bs1=True, want_ttft=True, want_e2e=True, clocks=None):
+        """Builds the model (TP=world when tp is given, else a full replica per rank)
+        and measures the decode step on it; every rank runs the same calls."""
+        llm = LLM(args.model, device=str(dev), kv_cache_dtype=args.kv_dtype, max_batch=B, max_model_len=max_len,
+                  kv_pages=kv_pages, enable_prefix_cache=False, seed=1234, tp=tp, num_layers=args.num_layers)
+        runner, eng = llm.runner, llm.engine
+        cfg = llm.cfg
+        g = torch.Generator().manual_seed(42)
 
-    runner.capture_all([1, B])
-    comm.barrier()
+        def prompts(n):
+            return [torch.randint(0, cfg.vocab_size, (P,), generator=g).tolist() for _ in range(n)]
 
-    # ---------------------------------------------------------------- TTFT (engine API)
-    ttfts = []
-    for _ in range(args.ttft_runs + 1):
-        torch.cuda.synchronize()
-        r = eng.add_request(prompts(1)[0], SamplingParams(max_tokens=1, ignore_eos=True))
-        while not r.finished:
-            eng.step()
-        ttfts.append(r.ttft * 1000.0)
-    ttfts = ttfts[1:]   # first one includes lazy initialisation
+        runner.capture_all([1, B])
+        comm.barrier()
+        res = {"cfg": cfg}
 
-    # ---------------------------------------------------------------- device-timed decode
-    def device_decode(nb: int):
-        """K decode steps of nb sequences with inputs pre-staged on the device;
-        each step = D2D copy of its metadata + token feedback + graph replay."""
-        reqs = [eng.add_request(p, SamplingParams(max_tokens=warm + steps + 2, ignore_eos=True))
-                for p in prompts(nb)]
-        while any(not r.output_ids for r in reqs):
-            eng.step()          # admission + prefill (+ first token)
-        live = list(reqs)
-        assert all(not r.finished for r in live)
-        S = warm + steps
-        bucket = runner.bucket_for(nb)
-        rows_i, rows_f = [], []
-        for t in range(S):
-            ids, pos, slots, ctx = [], [], [], []
+        # ------------------------------------------------------------ TTFT (engine API)
+        if want_ttft:
+            ttfts = []
+            for _ in range(args.ttft_runs + 1):
+                torch.cuda.synchronize()
+                r = eng.add_request(prompts(1)[0], SamplingParams(max_tokens=1, ignore_eos=True))
+                while not r.finished:
+                    eng.step()
+                ttfts.append(r.ttft * 1000.0)
+            res["ttft_p50_ms"] = statistics.median(ttfts[1:])   # the first includes lazy initialisation
+
+        # ------------------------------------------------------------ device-timed decode
+        def device_decode(nb: int):
+            """K decode steps of nb sequences with inputs pre-staged on the device;
+            each step = D2D copy of its metadata + token feedback + graph replay."""
+            reqs = [eng.add_request(p, SamplingParams(max_tokens=warm + steps + 2, ignore_eos=True))
+                    for p in prompts(nb)]
+            while any(not r.output_ids for r in reqs):
+                eng.step()          # admission + prefill (+ first token)
+            live = list(reqs)
+            assert all(not r.finished for r in live)
+            S = warm + steps
+            bucket = runner.bucket_for(nb)
+            rows_i, rows_f = [], []
+            for t in range(S):
+                ids, pos, slots, ctx = [], [], [], []
+                for r in live:
+                    p = r.total_len - 1 + t
+                    slots.append(llm.kv.append_slots(r.request_id, 1)[0])
+                    pos.append(p)
+                    ctx.append(p + 1)
+                    ids.append(0)
+                bts = [llm.kv.block_table(r.request_id) for r in live]
+                runner.stage_decode_inputs(ids, pos, slots, ctx, bts, [0.0] * nb, [0] * nb, [1.0] * nb,
+                                           [t] * nb)
+                rows_i.append(runner.h_i32.clone())
+                rows_f.append(runner.h_f32.clone())
+            d_pre_i = torch.stack(rows_i).to(dev)
+            d_pre_f = torch.stack(rows_f).to(dev)
+            first = torch.tensor([r.output_ids[-1] for r in live] + [0] * (bucket - nb), dtype=torch.int32)
+            runner.d_out[:bucket].copy_(first.to(dev))
+            graph = runner._graphs[bucket]
+
+            def step(t):
+                runner.d_i32.copy_(d_pre_i[t], non_blocking=True)
+                runner.d_f32.copy_(d_pre_f[t], non_blocking=True)
+                runner.d_ids[:bucket].copy_(runner.d_out[:bucket], non_blocking=True)
+                graph.replay()
+
+            if clocks is not None and nb == B:
+                clocks.start()      # from the warm-up replays on: short timed regions still get samples
+            for t in range(warm):
+                step(t)
+            torch.cuda.synchronize()
+            comm.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for t in range(warm, S):
+                step(t)
+            e1.record()
+            torch.cuda.synchronize()
+            if clocks is not None and nb == B:
+                res["clocks"] = clocks.stop()
+            comm.barrier()
+            ms = e0.elapsed_time(e1)
             for r in live:
-                p = r.total_len - 1 + t
-                slots.append(llm.kv.append_slots(r.request_id, 1)[0])
-                pos.append(p)
-                ctx.append(p + 1)
-                ids.append(0)
-            bts = [llm.kv.block_table(r.request_id) for r in live]
-            runner.stage_decode_inputs(ids, pos, slots, ctx, bts, [0.0] * nb, [0] * nb, [1.0] * nb,
-                                       [t] * nb)
-            rows_i.append(runner.h_i32.clone())
-            rows_f.append(runner.h_f32.clone())
-        d_pre_i = torch.stack(rows_i).to(dev)
-        d_pre_f = torch.stack(rows_f).to(dev)
-        first = torch.tensor([r.output_ids[-1] for r in live] + [0] * (bucket - nb), dtype=torch.int32)
-        runner.d_out[:bucket].copy_(first.to(dev))
-        graph = runner._graphs[bucket]
+                eng.abort(r.request_id)
+            return comm.max_over_ranks(ms)
 
-        def step(t):
-            runner.d_i32.copy_(d_pre_i[t], non_blocking=True)
-            runner.d_f32.copy_(d_pre_f[t], non_blocking=True)
-            runner.d_ids[:bucket].copy_(runner.d_out[:bucket], non_blocking=True)
-            graph.replay()
+        # ------------------------------------------------------------ e2e decode (engine API)
+        def e2e_decode(nb: int):
+            reqs = [eng.add_request(p, SamplingParams(max_tokens=warm + steps + 2, ignore_eos=True))
+                    for p in prompts(nb)]
+            while any(not r.output_ids for r in reqs):
+                eng.step()
+            for _ in range(warm):
+                eng.step()
+            torch.cuda.synchronize()
+            comm.barrier()
+            t0 = time.perf_counter()
+            n0 = sum(len(r.output_ids) for r in reqs)
+            for _ in range(steps):
+                eng.step()
+            torch.cuda.synchronize()
+            t1 = time.perf_counter()
+            comm.barrier()
+            n1 = sum(len(r.output_ids) for r in reqs)
+            for r in reqs:
+                eng.abort(r.request_id)
+            el = comm.max_over_ranks(t1 - t0)
+            return (n1 - n0) / el, el
 
-        for t in range(warm):
-            step(t)
+        ops.LAUNCHES[0] = 0
+        if want_bs32:
+            res["ms32"] = device_decode(B)
+        if want_bs1:
+            res["ms1"] = device_decode(1)
+        if want_e2e:
+            res["e2e32"], _ = e2e_decode(B)
+        # launches per decode step: count one eager decode body of bucket B
+        n0 = ops.LAUNCHES[0]
+        runner._decode_body(runner.bucket_for(B))
         torch.cuda.synchronize()
+        res["per_step"] = ops.LAUNCHES[0] - n0
+        res["err"] = ops.read_and_clear_errors()
+        res["h2d"] = runner.h2d_bytes_per_decode
+        res["d2h"] = 4 * runner.bucket_for(B)
+        runner.release_graphs()
         comm.barrier()
+        del llm, runner, eng
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for t in range(warm, S):
-            step(t)
-        e1.record()
-        torch.cuda.synchronize()
-        comm.barrier()
-        ms = e0.elapsed_time(e1)
-        for r in live:
-            eng.abort(r.request_id)
-        return comm.max_over_ranks(ms)
+        torch.cuda.empty_cache()
+        return res
 
-    # ---------------------------------------------------------------- e2e decode (engine API)
-    def e2e_decode(nb: int):
-        reqs = [eng.add_request(p, SamplingParams(max_tokens=warm + steps + 2, ignore_eos=True))
-                for p in prompts(nb)]
-        while any(not r.output_ids for r in reqs):
-            eng.step()
-        for _ in range(warm):
-            eng.step()
-        torch.cuda.synchronize()
-        comm.barrier()
-        t0 = time.perf_counter()
-        n0 = sum(len(r.output_ids) for r in reqs)
-        for _ in range(steps):
-            eng.step()
-        torch.cuda.synchronize()
-        t1 = time.perf_counter()
-        comm.barrier()
-        n1 = sum(len(r.output_ids) for r in reqs)
-        for r in reqs:
-            eng.abort(r.request_id)
-        el = comm.max_over_ranks(t1 - t0)
-        return (n1 - n0) / el, el
-
-    clocks = ClockSampler(info.local_rank)
-    if rank == 0:
-        clocks.start()
-    ops.LAUNCHES[0] = 0
-    ms32 = device_decode(B)
-    ms1 = device_decode(1)
-    e2e32, e2e_el = e2e_decode(B)
-    clk = clocks.stop() if rank == 0 else {}
-
-    # launches per decode step: count one eager decode body of bucket B
-    n0 = ops.LAUNCHES[0]
-    runner._decode_body(runner.bucket_for(B))
-    torch.cuda.synchronize()
-    per_step = ops.LAUNCHES[0] - n0
-    err = ops.read_and_clear_errors()
-
-    tok32 = B * steps / (ms32 / 1000.0)
+    sampler = ClockSampler(info.local_rank) if rank == 0 else None
+    if world == 1 or mode == "tp":
+        tp = comm.tp_context()
+        main = measure(tp, clocks=sampler)
+        lat = main
+        tpres = None
+    else:
+        # data parallel: a full replica per GPU, global batch B per replica (weak scaling);
+        # then the same model as TP=world for the single-stream latency (bs1, TTFT)
+        main = measure(None, want_bs1=False, want_ttft=False, clocks=sampler)
+        tp = comm.tp_context()
+        lat = measure(tp, want_e2e=False)
+        tpres = lat
+    cfg = main["cfg"]
+    dp = world > 1 and mode == "dp"
+    replicas = world if dp else 1
+    ms32, ms1 = main["ms32"], lat["ms1"]
+    tok32 = replicas * B * steps / (ms32 / 1000.0)
     tok1 = steps / (ms1 / 1000.0)
+    # with data parallelism every replica decodes its own batch through its own engine:
+    # the aggregate is world x the rate over the slowest replica's time
+    e2e = world * main["e2e32"] if dp else main["e2e32"]
     res = {
         "metric": METRIC,
         "value": round(tok32, 2),
@@ -258,30 +299,34 @@ def run_ours(args):
         "warmup": warm,
         "ms_per_step": round(ms32 / steps, 4),
         "higher_is_better": True,
-        "scaling": "strong",
+        "scaling": "weak" if dp else "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: uniform random token ids, random-init N(0,0.02) bf16 weights",
         "config": {"model": "Qwen2.5-14B architecture" if args.model == "qwen2.5-14b" else args.model,
-                   "global_batch": B, "seq_len": P, "parallelism": f"tp{world}",
+                   "global_batch": B * replicas, "seq_len": P,
+                   "parallelism": f"dp{world}" if dp else f"tp{world}",
                    "kv_cache": f"paged 16-token pages, {args.kv_dtype}",
                    "decode": "CUDA graph per step", "l2": "inputs larger than L2 (all weights streamed each step)",
                    "num_layers": args.num_layers or cfg.num_layers},
         "bs1": {"tok_s": round(tok1, 2), "ms_per_step": round(ms1 / steps, 4),
-                "vs_baseline": round(tok1 / BASELINE_BS1_TOK_S, 2)},
-        "ttft_p50_ms": round(statistics.median(ttfts), 3),
+                "vs_baseline": round(tok1 / BASELINE_BS1_TOK_S, 2), "parallelism": f"tp{world}"},
+        "ttft_p50_ms": round(lat["ttft_p50_ms"], 3),
         "ttft_prompt_tokens": P,
-        "e2e": {"value": round(e2e32, 2), "unit": "tok/s", "h2d_bytes_per_step": runner.h2d_bytes_per_decode,
-                "d2h_bytes_per_step": 4 * runner.bucket_for(B), "api": "LLMEngine.step"},
-        "gpu_launches": per_step * steps,
-        "gpu_launches_per_step": per_step,
-        "device_errors": err,
-        "clocks": clk,
+        "ttft_parallelism": f"tp{world}",
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": main["h2d"],
+                "d2h_bytes_per_step": main["d2h"], "api": "LLMEngine.step"},
+        "gpu_launches": main["per_step"] * steps,
+        "gpu_launches_per_step": main["per_step"],
+        "device_errors": main["err"] | (tpres["err"] if tpres else 0),
+        "clocks": main.get("clocks", {}),
         "impl": "ours",
     }
+    if tpres is not None:
+        res["tp"] = {"parallelism": f"tp{world}", "global_batch": B, "value": round(B * steps / (tpres["ms32"] / 1000.0), 2),
+                     "ms_per_step": round(tpres["ms32"] / steps, 4), "scaling": "strong"}
     if args.num_layers:
         res["invalid"] = "truncated model (--num-layers): debugging only"
-    runner.release_graphs()
     comm.barrier()
     if rank == 0:
         print(json.dumps(res), flush=True)
