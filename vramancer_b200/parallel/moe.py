@@ -22,6 +22,15 @@ from ..models.config import ModelConfig
 
 DEVICE_MOE = True       # CUDA MoE layers need no host synchronisation (graph-capturable)
 
+_usage_hook = None      # parallel.expert_placement.ExpertUsage (or None)
+
+
+def set_usage_hook(usage) -> None:
+    """Every MoE layer call reports its routing to `usage.observe(ids)` (None: off).  On
+    CUDA the routing is then computed twice per call (once for the hook)."""
+    global _usage_hook
+    _usage_hook = usage
+
 
 def route(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """Returns (weights [T, k] fp32, expert ids [T, k] int64).  On CUDA the softmax /
@@ -51,6 +60,8 @@ def moe_forward(cfg: ModelConfig, x: torch.Tensor, router_w: torch.Tensor, exper
     """x [T, H] -> [T, H].  experts_* hold experts [expert_offset, expert_offset + E_local).
     With `residual` the output is added into it in place (bf16) and the result is
     RMSNorm(residual) * norm_w when `norm_w` is given (the next layer's input), else None."""
+    if _usage_hook is not None and x.shape[0] > 0:
+        _usage_hook.observe(route(cfg, x, router_w)[1])
     if x.is_cuda and expert_offset == 0 and experts_gate_up.shape[0] == cfg.num_experts:
         return _moe_device(cfg, x, router_w, experts_gate_up, experts_down, shared_gate_up, shared_down,
                            shared_gate, residual, norm_w)
