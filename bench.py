@@ -52,6 +52,8 @@ def parse_args(argv=None):
     p.add_argument("--kv-dtype", default="bf16")
     p.add_argument("--ttft-runs", type=int, default=5)
     p.add_argument("--num-layers", type=int, default=None, help="debug only: truncates the model (invalid run)")
+    p.add_argument("--quantization", default=None, choices=["nvfp4", "fp8"],
+                   help="weight format (the headline is bf16; these are extra measurements)")
     p.add_argument("--parallel", choices=["dp", "tp"], default=None,
                    help="N > 1: data-parallel replicas (default; bs1 / TTFT still measured at TP=N) or TP=N only")
     return p.parse_args(argv)
@@ -141,7 +143,8 @@ def run_ours(args):
         """Builds the model (TP=world when tp is given, else a full replica per rank)
         and measures the decode step on it; every rank runs the same calls."""
         llm = LLM(args.model, device=str(dev), kv_cache_dtype=args.kv_dtype, max_batch=B, max_model_len=max_len,
-                  kv_pages=kv_pages, enable_prefix_cache=False, seed=1234, tp=tp, num_layers=args.num_layers)
+                  kv_pages=kv_pages, enable_prefix_cache=False, seed=1234, tp=tp, num_layers=args.num_layers,
+                  quantization=args.quantization)
         runner, eng = llm.runner, llm.engine
         cfg = llm.cfg
         g = torch.Generator().manual_seed(42)
@@ -301,7 +304,7 @@ def run_ours(args):
         "higher_is_better": True,
         "scaling": "weak" if dp else "strong",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "bf16" if not args.quantization else f"{args.quantization} weights, bf16 activations / KV",
         "data": "synthetic: uniform random token ids, random-init N(0,0.02) bf16 weights",
         "config": {"model": "Qwen2.5-14B architecture" if args.model == "qwen2.5-14b" else args.model,
                    "global_batch": B * replicas, "seq_len": P,

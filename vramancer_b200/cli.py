@@ -19,6 +19,23 @@ from typing import List, Optional
 __version__ = "0.1.0"
 
 
+
+# `-q` accepts the reference's names too.  nf4 / int8 are served by the formats the B200
+# tensor cores run natively (4-bit NVFP4, 8-bit FP8 e4m3 W8A8); gptq / awq name
+# pre-quantised checkpoint layouts, which this loader does not read.
+QUANT_CHOICES = ["nvfp4", "fp8", "none", "nf4", "int8", "gptq", "awq"]
+_QUANT_ALIASES = {"nf4": "nvfp4", "int8": "fp8"}
+
+
+def resolve_quantization(q):
+    if q in ("gptq", "awq"):
+        raise SystemExit(f"-q {q}: pre-quantised {q.upper()} checkpoints are not read by this loader; load the "
+                         f"bf16 checkpoint with -q nvfp4 (4-bit) or -q fp8 (8-bit) instead")
+    if q in _QUANT_ALIASES:
+        print(f"-q {q}: using {_QUANT_ALIASES[q]} (the B200-native {'4' if q == 'nf4' else '8'}-bit weight format)")
+        return _QUANT_ALIASES[q]
+    return q
+
 def _print(obj) -> None:
     print(json.dumps(obj, indent=1, default=str))
 
@@ -34,7 +51,7 @@ def build_parser() -> argparse.ArgumentParser:
     r.add_argument("--temperature", type=float, default=0.7)
     r.add_argument("--backend", default="auto")
     r.add_argument("--gpus", type=int, default=None)
-    r.add_argument("--quantization", "-q", default=None, choices=["nvfp4", "fp8", "none"])
+    r.add_argument("--quantization", "-q", default=None, choices=QUANT_CHOICES)
     r.add_argument("--num-layers", type=int, default=None, help=argparse.SUPPRESS)
 
     s = sub.add_parser("serve", help="OpenAI-compatible API server")
@@ -45,7 +62,7 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks (torchrun, one process per GPU)")
     s.add_argument("--host", default="0.0.0.0")
     s.add_argument("--port", type=int, default=5030)
-    s.add_argument("--quantization", default=None, choices=["nvfp4", "fp8", "none"])
+    s.add_argument("--quantization", "-q", default=None, choices=QUANT_CHOICES)
     s.add_argument("--no-cluster", dest="cluster", action="store_false", default=True)
     s.add_argument("--profile", default=None, choices=["coding", "multi-user"])
     s.add_argument("--max-model-len", type=int, default=None)
@@ -99,7 +116,7 @@ def build_parser() -> argparse.ArgumentParser:
 
 def _cmd_run(a) -> int:
     from .pipeline import InferencePipeline
-    pipe = InferencePipeline(verbose=True).load(a.model, num_gpus=a.gpus, quantization=a.quantization,
+    pipe = InferencePipeline(verbose=True).load(a.model, num_gpus=a.gpus, quantization=resolve_quantization(a.quantization),
                                                 num_layers=a.num_layers)
     try:
         if a.prompt is not None:
@@ -143,7 +160,7 @@ def _cmd_serve(a) -> int:
         kw = {}
         if a.max_model_len:
             kw["max_model_len"] = a.max_model_len
-        pipe = InferencePipeline().load(model, num_gpus=a.gpus, quantization=a.quantization,
+        pipe = InferencePipeline().load(model, num_gpus=a.gpus, quantization=resolve_quantization(a.quantization),
                                         num_layers=a.num_layers, **kw)
     if int(os.environ.get("RANK", "0")) != 0:
         from .parallel.follower import follow

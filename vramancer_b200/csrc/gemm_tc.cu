@@ -57,13 +57,31 @@ struct EpiParams {
   const __nv_bfloat16* residual;
   int M, N;       // logical output rows (tokens) and GEMM columns (weight rows)
   int epilogue;
+  // FP8 operands: the accumulator is scaled by scale_w[weight row] * scale_x[token] first
+  const float* scale_w;
+  const float* scale_x;
 };
 
 // Store one accumulator row segment.  `tok` / `feat0` are output coordinates of the
 // first value; in swap mode the 16 values run over tokens (fixed feature), otherwise
 // over features (fixed token).
 template <bool kSwapAB>
-__device__ __forceinline__ void epi_store(const EpiParams& p, int row_glob, int col0, const float (&v)[16]) {
+__device__ __forceinline__ void epi_store(const EpiParams& p, int row_glob, int col0, const float (&v_in)[16]) {
+  float v[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = v_in[j];
+  if (p.scale_w) {
+    // FP8: per weight row x per token scales (out-of-range rows / tokens are never stored)
+    if (kSwapAB) {
+      const float sw = row_glob < p.N ? p.scale_w[row_glob] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] *= sw * (col0 + j < p.M ? p.scale_x[col0 + j] : 0.f);
+    } else {
+      const float sx = row_glob < p.M ? p.scale_x[row_glob] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] *= sx * (col0 + j < p.N ? p.scale_w[col0 + j] : 0.f);
+    }
+  }
   if (p.epilogue == kEpiSiluMul) {
     // pairs (gate, up) of adjacent weight rows -> one output column
     if (!kSwapAB) {
@@ -396,7 +414,7 @@ struct StreamK {
 // launch advances the epoch and flags every peer.  ar_norm.cu reduces.
 using ARParams = ARPush;
 
-template <int BN, int STAGES, bool kAR>
+template <int BN, int STAGES, bool kAR, bool kF8 = false>
 __global__ void __launch_bounds__(kGemmThreads, 2)
     gemm_streamk_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                              EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters,
@@ -507,7 +525,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     for (int j = first; j < issued; ++j) mbar_wait(&full_bar[j % STAGES], (uint32_t)((j / STAGES) & 1), err);
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer
-    constexpr uint32_t idesc = make_idesc_bf16(kBM, BN);
+    constexpr uint32_t idesc = kF8 ? make_idesc_e4m3(kBM, BN) : make_idesc_bf16(kBM, BN);
     int64_t g = 0;
     int ms = 0;              // stage of the next full barrier, and its phase
     uint32_t mphase = 0u;
@@ -537,8 +555,13 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         const uint64_t da = make_sw128_desc(sa);
         const uint64_t db = make_sw128_desc(sa + L::kABytes);
 #pragma unroll
-        for (int kk = 0; kk < kBK / kUmmaK; ++kk)
-          umma_f16(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+          // bf16: K 16 per MMA; e4m3: K 32 per MMA -- 32 bytes of the swizzle row either way
+          if (kF8)
+            umma_f8(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+          else
+            umma_f16(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        }
         umma_commit(&empty_bar[s]);
       }
       umma_commit(&tfull[acc]);
@@ -1005,12 +1028,13 @@ static void choose_tail_split(int tiles, int k_tiles, int min_k, int* full_tiles
 static unsigned long long* g_gemm_trace = nullptr;
 void gemm_set_trace(void* buf) { g_gemm_trace = static_cast<unsigned long long*>(buf); }
 
-template <int BN, int STAGES, bool kAR>
+template <int BN, int STAGES, bool kAR, bool kF8 = false>
 static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const EpiParams& ep, int N, int K,
                            int max_ctas, cudaStream_t stream, const ARParams& ar, int tiles_x = 1) {
-  // smem: stages + 2*STAGES+4 barriers + slots
+  // smem: stages + 2*STAGES+4 barriers + slots.  K counts bf16 elements (for e4m3
+  // operands: pairs of bytes, so that one K-tile is the same 128-byte swizzle row)
   constexpr int kSmem = STAGES * GemmSmem<BN, STAGES>::kStageBytes + (2 * STAGES + 5) * 8 + 16 + 1024;
-  auto kern = gemm_streamk_swap_kernel<BN, STAGES, kAR>;
+  auto kern = gemm_streamk_swap_kernel<BN, STAGES, kAR, kF8>;
   static int attr_dev_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1121,6 +1145,8 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   ep.M = a.M;
   ep.N = a.N;
   ep.epilogue = a.epilogue;
+  ep.scale_w = nullptr;
+  ep.scale_x = nullptr;
   const int k_tiles = (a.K + kBK - 1) / kBK;
 
   if (a.M <= 128) {
@@ -1197,6 +1223,49 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
 }
 
 
+// ---------------------------------------------------------------- FP8 (e4m3) W8A8
+// The stream-K swap kernel with kind::f8f6f4 MMAs.  The e4m3 operands are described to
+// TMA as bf16 pairs, so one K-tile is still a 128-byte swizzle row (128 elements) and
+// every address, box and descriptor step is the bf16 one; the epilogue scales by
+// scale_w[n] * scale_x[m].  Any M: token blocks of 128 beyond the first.
+void gemm_fp8(const GemmArgs& a, const float* scale_x, const float* scale_w, cudaStream_t stream) {
+  VRM_REQUIRE(a.K % 128 == 0 && a.ldx % 16 == 0 && a.ldw % 16 == 0, "gemm fp8: K % 128, row strides % 16 bytes");
+  VRM_REQUIRE((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0,
+              "gemm fp8: operands must be 16-byte aligned");
+  VRM_REQUIRE(!a.allreduce && scale_x && scale_w, "gemm fp8: scales required, no fused all-reduce");
+  VRM_REQUIRE(a.epilogue != kEpiSiluMul || (a.N % 2 == 0 && a.residual == nullptr), "gemm fp8: silu_mul epilogue");
+  if (a.M <= 0 || a.N <= 0) return;
+  EpiParams ep;
+  ep.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  ep.ldo = (int)a.ldo;
+  ep.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  ep.residual = reinterpret_cast<const __nv_bfloat16*>(a.residual);
+  ep.M = a.M;
+  ep.N = a.N;
+  ep.epilogue = a.epilogue;
+  ep.scale_w = scale_w;
+  ep.scale_x = scale_x;
+  const int64_t Kp = a.K / 2;                               // bf16-pair units
+  const int k_tiles = (int)((Kp + kBK - 1) / kBK);
+  const CUtensorMap ma = make_kmajor_map(a.w, a.N, Kp, a.ldw / 2, kBM);
+  const int n_tiles = (a.N + kBM - 1) / kBM;
+  if (a.M <= 128) {
+    const int BN = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
+    const CUtensorMap mb = make_kmajor_map(a.x, a.M, Kp, a.ldx / 2, BN);
+    const int ctas = streamk_ctas(n_tiles, k_tiles, BN, (double)a.N * a.K);
+    switch (BN) {
+      case 16: launch_streamk<16, 6, false, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ARParams{}); break;
+      case 32: launch_streamk<32, 5, false, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ARParams{}); break;
+      case 64: launch_streamk<64, 4, false, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ARParams{}); break;
+      default: launch_streamk<128, 3, false, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ARParams{}); break;
+    }
+  } else {
+    const CUtensorMap mb = make_kmajor_map(a.x, a.M, Kp, a.ldx / 2, 128);
+    launch_streamk<128, 3, false, true>(ma, mb, ep, a.N, (int)Kp, device_sm_count(), stream, ARParams{},
+                                        (a.M + 127) / 128);
+  }
+}
+
 // ---------------------------------------------------------------- grouped MoE GEMM launcher
 template <int BN, int STAGES, bool kRet>
 static void launch_moe_grouped(const CUtensorMap& mw, const CUtensorMap& mx, const EpiParams& ep,
@@ -1231,6 +1300,8 @@ static void moe_grouped_dispatch(const MoeGemmArgs& a, cudaStream_t stream, cons
   ep.M = 0;
   ep.N = a.N;
   ep.epilogue = a.epilogue;
+  ep.scale_w = nullptr;
+  ep.scale_x = nullptr;
   const CUtensorMap mw = make_kmajor_map(a.w, (int64_t)a.E * a.N, a.K, a.K, kBM);
   const CUtensorMap mx = make_kmajor_map(a.x_perm, a.rows_cap, a.K, a.ldx, a.BN);
   const int wtiles = (a.N + kBM - 1) / kBM;

@@ -515,6 +515,49 @@ Tensor tq_decompress(const Tensor& rec, const Tensor& signs) {
 // the SiLU*up epilogue, grouped down GEMM, weighted combine (+ add, e.g. the shared
 // expert).  x [T, H], ids int64 [T, topk], weights fp32 [T, topk], gate_up [E, 2I, H]
 // (interleaved gate / up rows), down [E, H, I].  No host synchronisation.
+// FP8 rows: e4m3 codes [rows, K] and per-row scales.
+std::vector<Tensor> fp8_rows_quantize(const Tensor& x) {
+  check_bf16_2d(x, "fp8 rows x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto q = torch::empty({x.size(0), x.size(1)}, x.options().dtype(torch::kUInt8));
+  auto sc = torch::empty({x.size(0)}, x.options().dtype(torch::kFloat32));
+  vrm::fp8_rows_quantize(x.data_ptr(), x.stride(0), (int)x.size(0), (int)x.size(1), q.data_ptr<uint8_t>(),
+                         sc.data_ptr<float>(), cur_stream());
+  return {q, sc};
+}
+
+// y = (x_q w_q^T) * sx[m] * sw[n] (+ bias, + residual, or silu_mul) into out.
+void gemm_fp8_out(const Tensor& xq, const Tensor& sx, const Tensor& wq, const Tensor& sw, const OptT& bias,
+                  Tensor& out, int64_t epilogue, const OptT& residual) {
+  for (const Tensor* t : {&xq, &wq})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kUInt8 && t->dim() == 2 && t->stride(1) == 1,
+                "gemm fp8: uint8 (e4m3) [rows, K] operands");
+  TORCH_CHECK(sx.scalar_type() == torch::kFloat32 && sw.scalar_type() == torch::kFloat32 &&
+                  sx.numel() >= xq.size(0) && sw.numel() >= wq.size(0),
+              "gemm fp8: fp32 scales");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.stride(1) == 1, "gemm fp8: bf16 out");
+  same_device(xq, {&sx, &wq, &sw, &out}, "gemm fp8");
+  same_device_opt(xq, {&bias, &residual}, "gemm fp8");
+  const int64_t M = xq.size(0), K = xq.size(1), N = wq.size(0);
+  TORCH_CHECK(wq.size(1) == K, "gemm fp8: K mismatch");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == (epilogue == vrm::kEpiSiluMul ? N / 2 : N), "gemm fp8: out shape");
+  const c10::cuda::CUDAGuard guard(xq.device());
+  vrm::GemmArgs a;
+  a.x = xq.data_ptr();
+  a.ldx = xq.stride(0);
+  a.w = wq.data_ptr();
+  a.ldw = wq.stride(0);
+  a.bias = has(bias) ? bias->data_ptr() : nullptr;
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.epilogue = (int)epilogue;
+  a.residual = has(residual) ? residual->data_ptr() : nullptr;
+  vrm::gemm_fp8(a, sx.data_ptr<float>(), sw.data_ptr<float>(), cur_stream());
+}
+
 // NVFP4 rows (block-scaled format of nvfp4_bs.cu): returns q [rows, K/2], the scale
 // atoms, and the per-row scales (empty when gs_tensor is given).
 std::vector<Tensor> nvfp4_rows_quantize(const Tensor& x, int64_t rows, const OptT& gs_tensor) {
@@ -949,6 +992,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "TurboQuant: 64-byte records -> bf16 [..., 128]");
   m.def("set_decode_tma", &vrm::set_decode_tma, py::arg("on"),
         "use the persistent TMA decode-attention kernel for bf16 pages (default off)");
+  m.def("fp8_rows_quantize", &fp8_rows_quantize, py::arg("x"), "e4m3 rows with per-row scales");
+  m.def("gemm_fp8_out", &gemm_fp8_out, py::arg("xq"), py::arg("sx"), py::arg("wq"), py::arg("sw"), py::arg("bias"),
+        py::arg("out"), py::arg("epilogue"), py::arg("residual"),
+        "FP8 W8A8 GEMM (stream-K tcgen05 kind::f8f6f4, per-token x per-channel scales)");
   m.def("nvfp4_rows_quantize", &nvfp4_rows_quantize, py::arg("x"), py::arg("rows"), py::arg("gs_tensor"),
         "NVFP4 rows for the block-scaled GEMM: codes, 128x4 scale atoms, per-row scales");
   m.def("nvfp4_bs_gemm", &nvfp4_bs_gemm, py::arg("qa"), py::arg("sfa"), py::arg("gsa"), py::arg("M"), py::arg("qb"),

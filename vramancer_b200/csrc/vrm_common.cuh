@@ -158,6 +158,16 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t desc_a, uint6
       : "memory");
 }
 
+__device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
@@ -204,6 +214,13 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N) {
   return (1u << 4)                       // D format f32
          | (1u << 7)                     // A format bf16
          | (1u << 10)                    // B format bf16
+         | ((uint32_t)(N >> 3) << 17)    // N / 8
+         | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+// Instruction descriptor, kind::f8f6f4 with e4m3 A/B (format 0), fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t make_idesc_e4m3(int M, int N) {
+  return (1u << 4)                       // D format f32
          | ((uint32_t)(N >> 3) << 17)    // N / 8
          | ((uint32_t)(M >> 4) << 24);   // M / 16
 }

@@ -59,6 +59,11 @@ struct ARPush {
   int per_thread_fence = 0;
 };
 void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
+// FP8 W8A8: x, w are e4m3 bytes ([M, K], [N, K], strides in bytes); y = (x w^T) *
+// scale_x[m] * scale_w[n] (+ bias / residual / silu_mul as gemm_bf16).  K % 128 == 0.
+void gemm_fp8(const GemmArgs& a, const float* scale_x, const float* scale_w, cudaStream_t stream);
+// Per-row e4m3 quantisation: scale[r] = amax(|x[r]|) / 448, q = e4m3_rn_sat(x / scale).
+void fp8_rows_quantize(const void* x, int64_t ldx, int rows, int K, uint8_t* q, float* scale, cudaStream_t stream);
 // Debug: per-CTA timeline of the stream-K decode GEMM into buf ([ctas][8] u64 ns), null = off.
 void gemm_set_trace(void* buf);
 

@@ -77,8 +77,11 @@ class LLM:
         if self.quantization == "nvfp4":
             from .quant.nvfp4 import quantize_model_weights
             weights = quantize_model_weights(weights, cfg)
+        elif self.quantization == "fp8":
+            from .quant.fp8 import quantize_model_weights as fp8_quantize
+            weights = fp8_quantize(weights, cfg)
         elif self.quantization not in (None, "none", "bf16"):
-            raise ValueError(f"unsupported quantization {quantization!r} (nvfp4 or none)")
+            raise ValueError(f"unsupported quantization {quantization!r} (nvfp4, fp8 or none)")
         self.weights = weights
         if cfg.is_moe and not _moe_graph_safe():
             # the host-driven expert loop reads routing counts back: no graph capture
