@@ -98,7 +98,9 @@ __global__ void __launch_bounds__(kTqWarps * 32) tq_compress_kernel(const T* __r
                                                                     const float* __restrict__ signs,
                                                                     const float* __restrict__ jl,
                                                                     uint8_t* __restrict__ out) {
-  __shared__ float s_jl[kTqM][kTqD];
+  // rows padded to 129 floats: lane l reads row l (and l + 32) at the same column, so
+  // an unpadded 128-float stride puts all 32 lanes in one bank (32-way conflicts)
+  __shared__ float s_jl[kTqM][kTqD + 1];
   __shared__ float s_sign[kTqD];
   __shared__ float s_r[kTqWarps][kTqD];
   __shared__ uint8_t s_idx[kTqWarps][kTqD];

@@ -20,7 +20,8 @@ import os
 
 import torch
 
-from . import linear, paged_attention_decode, native
+from . import (argmax, linear, native, paged_attention_decode, paged_attention_prefill, rmsnorm, rope_cos_sin,
+               rope_kv_write, sample)
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
@@ -176,6 +177,129 @@ def bench_nvfp4_prefill(m, n, k, iters=20):
     return r
 
 
+def bench_rmsnorm(tokens, hidden=5120, iters=50):
+    """Residual add + RMSNorm over [tokens, hidden] bf16 (the decode step's norm)."""
+    hbm, _, src = peaks()
+    n = max(2, math.ceil(3 * 126e6 / (tokens * hidden * 2 * 3)))
+    xs = [torch.randn(tokens, hidden, device="cuda", dtype=torch.bfloat16) for _ in range(n)]
+    rs = [torch.randn(tokens, hidden, device="cuda", dtype=torch.bfloat16) for _ in range(n)]
+    w = torch.randn(hidden, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(tokens, hidden, device="cuda", dtype=torch.bfloat16)
+    state = [0]
+
+    def fn():
+        i = state[0] % n
+        rmsnorm(xs[i], w, 1e-6, residual=rs[i], out=out)
+        state[0] += 1
+
+    us = time_it(fn, iters)
+    byts = tokens * hidden * 2 * 4   # read x, residual; write residual, out
+    return {"kernel": "rmsnorm_residual", "tokens": tokens, "hidden": hidden, "us": round(us, 2),
+            "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
+
+
+def bench_rope_kv(tokens, q_heads=40, kv_heads=8, head_dim=128, fp8=False, iters=50):
+    """RoPE on q/k + K/V rows written into 16-token pages (bf16, or fp8 with per-head scales)."""
+    hbm, _, src = peaks()
+    ps, layers = 16, 4
+    width = (q_heads + 2 * kv_heads) * head_dim
+    qkv = torch.randn(tokens, width, device="cuda", dtype=torch.bfloat16)
+    pages = (tokens + ps - 1) // ps + 1
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    cache = torch.zeros(pages, layers, 2, kv_heads, ps, head_dim, device="cuda", dtype=dt)
+    cs = rope_cos_sin(8192, head_dim, 1e6, device="cuda")
+    pos = torch.randint(0, 8192, (tokens,), device="cuda", dtype=torch.int32)
+    slots = torch.randperm(pages * ps, device="cuda")[:tokens].to(torch.int32)
+    scale = torch.full((layers, 2, kv_heads), 0.05, device="cuda") if fp8 else None
+    state = [0]
+
+    def fn():
+        rope_kv_write(qkv, pos, cs, cache, slots, scale, state[0] % layers, q_heads, kv_heads, head_dim)
+        state[0] += 1
+
+    us = time_it(fn, iters)
+    byts = tokens * (width * 2 + (q_heads + kv_heads) * head_dim * 2 + 2 * kv_heads * head_dim * cache.element_size())
+    return {"kernel": "rope_kv_write", "tokens": tokens, "fp8": fp8, "us": round(us, 2),
+            "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
+
+
+def bench_prefill_attn(batch, seq, q_heads=40, kv_heads=8, head_dim=128, fp8=False, iters=10):
+    """Causal paged prefill attention of `batch` sequences of `seq` new tokens (no prefix)."""
+    _, tflops, src = peaks()
+    ps, layers = 16, 1
+    pages = (seq + ps - 1) // ps
+    P = batch * pages
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    cache = torch.randn(P, layers, 2, kv_heads, ps, head_dim, device="cuda").to(dt)
+    bt = torch.arange(P, dtype=torch.int32, device="cuda").view(batch, pages)
+    cl = torch.full((batch,), seq, dtype=torch.int32, device="cuda")
+    cu = torch.arange(0, (batch + 1) * seq, seq, dtype=torch.int32, device="cuda")
+    q = torch.randn(batch * seq, q_heads * head_dim, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    scale = torch.ones(layers, 2, kv_heads, device="cuda") if fp8 else None
+
+    def fn():
+        paged_attention_prefill(q, cache, 0, bt, cu, cl, scale, 1 / math.sqrt(head_dim), q_heads, seq, out=out)
+
+    us = time_it(fn, iters)
+    flop = batch * q_heads * 4.0 * head_dim * seq * (seq + 1) / 2   # causal QK^T + PV
+    return {"kernel": "prefill_attn", "batch": batch, "seq": seq, "fp8": fp8, "us": round(us, 2),
+            "tflops": round(flop / us / 1e6, 1), "frac_of_measured_bf16": round(flop / us / 1e6 / tflops, 3),
+            "peaks": src}
+
+
+def bench_sample(batch, vocab=152064, greedy=False, iters=50):
+    """Sampler over bf16 logits [batch, vocab]: argmax, or temperature / top-k / top-p."""
+    hbm, _, src = peaks()
+    logits = torch.randn(batch, vocab, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(batch, dtype=torch.int32, device="cuda")
+    temp = torch.full((batch,), 0.8, device="cuda")
+    topk = torch.full((batch,), 50, dtype=torch.int32, device="cuda")
+    topp = torch.full((batch,), 0.9, device="cuda")
+    steps = torch.zeros(batch, dtype=torch.int32, device="cuda")
+    if greedy:
+        fn = lambda: argmax(logits, out)   # noqa: E731
+    else:
+        fn = lambda: sample(logits, temp, topk, topp, 1234, steps, out)   # noqa: E731
+    us = time_it(fn, iters)
+    byts = batch * vocab * 2
+    return {"kernel": "argmax" if greedy else "sample_topk_topp", "batch": batch, "vocab": vocab,
+            "us": round(us, 2), "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3),
+            "peaks": src}
+
+
+def bench_turboquant(vectors, head_dim=128, iters=20):
+    """TurboQuant record compress / decompress of `vectors` head_dim vectors (bf16)."""
+    from ..kv.turboquant import KVCacheCompressor
+    hbm, _, src = peaks()
+    comp = KVCacheCompressor(head_dim=head_dim).to("cuda")
+    x = torch.randn(vectors, head_dim, device="cuda", dtype=torch.bfloat16)
+    rec = comp.compress(x)
+    t_c = time_it(lambda: comp.compress(x), iters, graph=False)
+    t_d = time_it(lambda: comp.decompress(rec), iters, graph=False)
+    rb = rec.numel() * rec.element_size()
+    xb = x.numel() * 2
+    return {"kernel": "turboquant", "vectors": vectors, "record_bytes": rec.shape[-1],
+            "compress_us": round(t_c, 2), "compress_tb_s": round((xb + rb) / t_c / 1e6, 3),
+            "decompress_us": round(t_d, 2), "decompress_tb_s": round((xb + rb) / t_d / 1e6, 3),
+            "frac_hbm_decompress": round((xb + rb) / t_d / 1e6 / hbm, 3), "peaks": src}
+
+
+def bench_act_quant(tokens, hidden=5120, iters=50):
+    """Per-token activation quantisers feeding the low-precision GEMMs: fp8 e4m3 rows
+    (per-token scale) and NVFP4 rows (per-token scale, e4m3 scale per 16, e2m1 codes)."""
+    hbm, _, src = peaks()
+    x = torch.randn(tokens, hidden, device="cuda", dtype=torch.bfloat16)
+    mp = (tokens + 127) // 128 * 128
+    t8 = time_it(lambda: native().fp8_rows_quantize(x), iters)
+    t4 = time_it(lambda: native().nvfp4_rows_quantize(x, mp, None), iters)
+    b8 = tokens * hidden * 3
+    b4 = tokens * hidden * 2 + tokens * hidden // 2 + tokens * hidden // 16
+    return {"kernel": "act_quant", "tokens": tokens, "hidden": hidden,
+            "fp8_us": round(t8, 2), "fp8_frac_hbm": round(b8 / t8 / 1e6 / hbm, 3),
+            "nvfp4_us": round(t4, 2), "nvfp4_frac_hbm": round(b4 / t4 / 1e6 / hbm, 3), "peaks": src}
+
+
 def trace_gemm(m, n, k):
     """Per-CTA timelines of two back-to-back stream-K decode GEMM launches on cold
     weights (us from the first launch's earliest CTA entry)."""
@@ -211,7 +335,11 @@ QWEN14B_DECODE = [("qkv", 7168, 5120), ("o_proj", 5120, 5120), ("gate_up", 27648
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "nvfp4", "nvfp4-prefill", "decode-attn", "all", "trace"])
+    ap.add_argument("what", choices=["gemm", "nvfp4", "nvfp4-prefill", "decode-attn", "all", "trace", "rmsnorm",
+                                     "rope-kv", "prefill-attn", "sample", "turboquant", "act-quant", "others"])
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=2048)
+    ap.add_argument("--greedy", action="store_true")
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--n", type=int, default=5120)
     ap.add_argument("--k", type=int, default=13824)
@@ -239,6 +367,33 @@ def main(argv=None):
             print(json.dumps(bench_nvfp4_prefill(a.m if a.m != 1 else 4096, n, k, a.iters)))
     elif a.what == "decode-attn":
         print(json.dumps(bench_decode_attn(a.batch, a.ctx, fp8=a.fp8, iters=a.iters)))
+    elif a.what == "rmsnorm":
+        print(json.dumps(bench_rmsnorm(a.tokens or a.batch, iters=a.iters)))
+    elif a.what == "rope-kv":
+        print(json.dumps(bench_rope_kv(a.tokens or a.batch, fp8=a.fp8, iters=a.iters)))
+    elif a.what == "prefill-attn":
+        print(json.dumps(bench_prefill_attn(a.batch, a.seq, fp8=a.fp8, iters=a.iters)))
+    elif a.what == "sample":
+        print(json.dumps(bench_sample(a.batch, greedy=a.greedy, iters=a.iters)))
+    elif a.what == "turboquant":
+        print(json.dumps(bench_turboquant(a.tokens or 65536, iters=a.iters)))
+    elif a.what == "act-quant":
+        print(json.dumps(bench_act_quant(a.tokens or 4096, iters=a.iters)))
+    elif a.what == "others":
+        for t in (1, 32, 4096):
+            print(json.dumps(bench_rmsnorm(t, iters=a.iters)))
+        for t in (32, 4096):
+            for fp8 in (False, True):
+                print(json.dumps(bench_rope_kv(t, fp8=fp8, iters=a.iters)))
+        for b, s in ((1, 4096), (4, 2048)):
+            for fp8 in (False, True):
+                print(json.dumps(bench_prefill_attn(b, s, fp8=fp8, iters=10)))
+        for b in (1, 32):
+            print(json.dumps(bench_sample(b, greedy=True, iters=a.iters)))
+            print(json.dumps(bench_sample(b, iters=a.iters)))
+        print(json.dumps(bench_turboquant(65536, iters=20)))
+        for t in (32, 4096):
+            print(json.dumps(bench_act_quant(t, iters=a.iters)))
     else:
         for m in (1, 32, 512):
             for name, n, k in QWEN14B_DECODE:
