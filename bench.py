@@ -175,6 +175,7 @@ def run_ours(args):
                     for p in prompts(nb)]
             while any(not r.output_ids for r in reqs):
                 eng.step()          # admission + prefill (+ first token)
+            eng.flush()             # the engine's overlapped decode step, if one is in flight
             live = list(reqs)
             assert all(not r.finished for r in live)
             S = warm + steps

@@ -19,6 +19,7 @@ sampling, streaming callback, futures) — which re-concatenates HF caches every
 from __future__ import annotations
 
 import itertools
+import os
 import threading
 import time
 from collections import deque
@@ -81,7 +82,7 @@ class Request:
 class LLMEngine:
     def __init__(self, runner: ModelRunner, manager: PagedKVCacheManager, *, max_batch: Optional[int] = None,
                  max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, spec_num_draft: int = 0,
-                 spec_ngram: int = 3, ep_sync: Optional["EPSync"] = None):
+                 spec_ngram: int = 3, ep_sync: Optional["EPSync"] = None, lookahead: bool = True):
         if ep_sync is not None and spec_num_draft > 0:
             raise ValueError("speculative decoding is not supported with expert parallelism")
         self.ep_sync = ep_sync
@@ -100,6 +101,10 @@ class LLMEngine:
         self.spec_ngram = spec_ngram
         from .speculative import SpecStats
         self.spec_stats = SpecStats()
+        # overlapped decode: step n+1 is launched (fed from the device) before step n's
+        # tokens are read back, so host scheduling hides behind the GPU's work
+        self.lookahead = lookahead and ep_sync is None and os.environ.get("VRM_LOOKAHEAD", "1") != "0"
+        self._pending = None          # (requests, PendingDecode) of the step in flight
 
     # ------------------------------------------------------------------ API
     def add_request(self, prompt_ids: Sequence[int], params: Optional[SamplingParams] = None, *,
@@ -116,6 +121,14 @@ class LLMEngine:
         with self._lock:
             self.waiting.append(req)
         return req
+
+    def flush(self) -> List[Request]:
+        """Reads the decode step still in flight (overlapped decode), emitting its
+        tokens; returns the requests that finished."""
+        with self._lock:
+            done: List[Request] = []
+            self._drain(done)
+            return done
 
     def has_unfinished(self) -> bool:
         with self._lock:
@@ -245,25 +258,69 @@ class LLMEngine:
 
     def _decode(self, done: List[Request]) -> None:
         active = [r for r in self.running if r.prefill_done and not r.finished and r.output_ids]
+        if self.spec_num_draft > 0 and active:
+            from .speculative import find_draft, speculative_decode_step
+            drafts = [find_draft(r.prompt_ids + r.output_ids, self.spec_ngram, self.spec_num_draft)
+                      if r.params.greedy else [] for r in active]
+            if any(drafts):
+                self._drain(done)
+                active = [r for r in active if not r.finished]
+                drafts = [find_draft(r.prompt_ids + r.output_ids, self.spec_ngram, self.spec_num_draft)
+                          if r.params.greedy else [] for r in active]
+                outs = speculative_decode_step(self, active, self.spec_ngram, self.spec_num_draft, self.spec_stats,
+                                               drafts=drafts)
+                for r, toks in zip(active, outs):
+                    for t in toks:
+                        self.stats["decode_tokens"] += 1
+                        self._emit(r, int(t))
+                        if r.finished:
+                            done.append(r)
+                            break
+                return
+            # nothing to draft: an ordinary (graph-replayed) decode step
+        pend = self._pending
+        if pend is not None and active and self._can_chain(pend[0], active):
+            # launch step n+1 on the device-resident tokens of step n, then read step n
+            nxt = self._launch(active, chained=True)
+            self._pending = None
+            self._consume(pend[0], pend[1], done)
+            self._pending = (active, nxt)
+            return
+        self._drain(done)
+        active = [r for r in active if not r.finished]
         if not active:
             return
-        if self.spec_num_draft > 0:
-            from .speculative import speculative_decode_step
-            outs = speculative_decode_step(self, active, self.spec_ngram, self.spec_num_draft, self.spec_stats)
-            for r, toks in zip(active, outs):
-                for t in toks:
-                    self.stats["decode_tokens"] += 1
-                    self._emit(r, int(t))
-                    if r.finished:
-                        done.append(r)
-                        break
-            return
+        handle = self._launch(active, chained=False)
+        if self.lookahead:
+            self._pending = (active, handle)
+        else:
+            self._consume(active, handle, done)
+
+    def _can_chain(self, prev: List[Request], active: List[Request]) -> bool:
+        """Step n+1 may run before step n is read when the batch is the same requests
+        in the same rows, none of them ends by length with step n's token, and the KV
+        pool has a page for every sequence that starts one."""
+        if not self.lookahead or len(prev) != len(active) or any(a is not b for a, b in zip(prev, active)):
+            return False
+        ps = self.kv.page_size
+        new_pages = 0
+        for r in active:
+            if r.finished or len(r.output_ids) + 1 >= r.params.max_tokens or r.total_len + 1 >= self.max_model_len:
+                return False
+            if self.kv.seq_len(r.request_id) % ps == 0:
+                new_pages += 1
+        return new_pages <= self.kv.num_free_pages()
+
+    def _launch(self, active: List[Request], chained: bool):
+        """Appends one KV slot per request and launches the decode step.  Chained: the
+        token fed is the one step n sampled (still on the device), one position later."""
+        off = 1 if chained else 0
         ids, pos, slots, ctx, bts = [], [], [], [], []
         temp, topk, topp, steps = [], [], [], []
         for r in active:
-            p = r.total_len - 1                     # position of the token being fed
+            p = r.total_len - 1 + off               # position of the token being fed
             s = self.kv.append_slots(r.request_id, 1)[0]
-            ids.append(r.output_ids[-1])
+            ids.append(0 if chained else r.output_ids[-1])
             pos.append(p)
             slots.append(s)
             ctx.append(p + 1)
@@ -271,14 +328,27 @@ class LLMEngine:
             temp.append(r.params.temperature)
             topk.append(r.params.top_k)
             topp.append(r.params.top_p)
-            steps.append(len(r.output_ids))
+            steps.append(len(r.output_ids) + off)
         self._apply_cow()
-        out = self.runner.decode_step(ids, pos, slots, ctx, bts, temp, topk, topp, steps)
-        self.stats["decode_tokens"] += len(active)
-        for r, tok in zip(active, out):
+        return self.runner.launch_decode(ids, pos, slots, ctx, bts, temp, topk, topp, steps, ids_on_device=chained)
+
+    def _consume(self, reqs: List[Request], handle, done: List[Request]) -> None:
+        """Reads a launched step's tokens and emits them (requests that finished or were
+        aborted meanwhile drop theirs)."""
+        toks = self.runner.collect_decode(handle)
+        for r, tok in zip(reqs, toks):
+            if r.finished:
+                continue
+            self.stats["decode_tokens"] += 1
             self._emit(r, int(tok))
             if r.finished:
                 done.append(r)
+
+    def _drain(self, done: List[Request]) -> None:
+        """Reads the step still in flight, if any."""
+        pend, self._pending = self._pending, None
+        if pend is not None:
+            self._consume(pend[0], pend[1], done)
 
     def _apply_cow(self) -> None:
         copies = self.kv.pop_cow_copies()

@@ -39,6 +39,34 @@ class PrefillItem:
     want_logits: bool
 
 
+class _Stage:
+    """One pinned staging area (decode inputs + sampled ids) and the event recorded
+    after the last copies that read or write it."""
+
+    def __init__(self, n_i32: int, n_f32: int, B: int, pin: bool):
+        self.h_i32 = torch.zeros(n_i32, dtype=torch.int32, pin_memory=pin)
+        self.h_f32 = torch.zeros(n_f32, dtype=torch.float32, pin_memory=pin)
+        self.h_out = torch.zeros(B, dtype=torch.int32, pin_memory=pin)
+        self.event = torch.cuda.Event() if pin else None
+        self.pending = False
+
+    def record(self) -> None:
+        self.event.record()
+        self.pending = True
+
+    def wait(self) -> None:
+        if self.pending:
+            self.event.synchronize()
+            self.pending = False
+
+
+class PendingDecode:
+    """A launched decode step whose sampled ids have not been read yet."""
+
+    def __init__(self, stage: _Stage, n: int):
+        self.stage, self.n = stage, n
+
+
 class ModelRunner:
     def __init__(self, model: DecoderModel, pool: KVPool, *, max_batch: int = 256, max_model_len: int = 4096,
                  use_cuda_graph: bool = True, buckets: Sequence[int] = DEFAULT_BUCKETS, seed: int = 0):
@@ -67,8 +95,9 @@ class ModelRunner:
         self._n_i32 = 6 * B + B * P
         self._n_f32 = 2 * B
         pin = self.device.type == "cuda"
-        self.h_i32 = torch.zeros(self._n_i32, dtype=torch.int32, pin_memory=pin)
-        self.h_f32 = torch.zeros(self._n_f32, dtype=torch.float32, pin_memory=pin)
+        # two pinned staging areas: step n+1 is staged while step n's copies are in flight
+        self._stages = [_Stage(self._n_i32, self._n_f32, B, pin) for _ in range(2)]
+        self._stage_idx = 0
         self.d_i32 = torch.zeros(self._n_i32, dtype=torch.int32, device=self.device)
         self.d_f32 = torch.zeros(self._n_f32, dtype=torch.float32, device=self.device)
         d = self.d_i32
@@ -77,11 +106,17 @@ class ModelRunner:
         self.d_bt = d[6 * B:].view(B, P)
         self.d_temp, self.d_topp = self.d_f32[0:B], self.d_f32[B:2 * B]
         self.d_out = torch.zeros(B, dtype=torch.int32, device=self.device)
-        self.h_out = torch.zeros(B, dtype=torch.int32, pin_memory=pin)
+        self._use_stage(0)
+
+    def _use_stage(self, i: int) -> None:
+        """Points the staging views (h_i32, h_f32, h_out, hn_*) at staging area i."""
+        st = self._stages[i]
+        B = self.max_batch
+        self.h_i32, self.h_f32, self.h_out = st.h_i32, st.h_f32, st.h_out
         hn = self.h_i32.numpy()
         self.hn_ids, self.hn_pos, self.hn_slots = hn[0:B], hn[B:2 * B], hn[2 * B:3 * B]
         self.hn_ctx, self.hn_topk, self.hn_steps = hn[3 * B:4 * B], hn[4 * B:5 * B], hn[5 * B:6 * B]
-        self.hn_bt = hn[6 * B:].reshape(B, P)
+        self.hn_bt = hn[6 * B:].reshape(B, self.max_pages)
         hf = self.h_f32.numpy()
         self.hn_temp, self.hn_topp = hf[0:B], hf[B:2 * B]
 
@@ -147,17 +182,40 @@ class ModelRunner:
             self._decode_body(B)
         return self.d_out[:B]
 
-    def decode_step(self, ids, positions, slots, ctx, block_tables, temperature, top_k, top_p, steps) -> List[int]:
-        """Host-to-host decode step: stage, upload, run, read back the sampled ids."""
-        n = len(ids)
-        B = self.stage_decode_inputs(ids, positions, slots, ctx, block_tables, temperature, top_k, top_p, steps)
+    def launch_decode(self, ids, positions, slots, ctx, block_tables, temperature, top_k, top_p, steps, *,
+                      ids_on_device: bool = False) -> "PendingDecode":
+        """Stages, uploads and launches one decode step without waiting for it; the
+        sampled ids are copied into pinned memory behind it (collect_decode reads them).
+        With ids_on_device the token fed to row r is row r of the previous step's
+        sampled output, still on the device: the host launches step n+1 before it has
+        read step n's tokens, so its scheduling overlaps the GPU's work."""
+        n = len(positions)
+        st = self._stages[self._stage_idx]
+        st.wait()                               # this area's previous copies have run
+        self._use_stage(self._stage_idx)
+        B = self.stage_decode_inputs(ids if not ids_on_device else [0] * n, positions, slots, ctx, block_tables,
+                                     temperature, top_k, top_p, steps)
         self.upload_decode_inputs()
+        if ids_on_device:
+            self.d_ids[:n].copy_(self.d_out[:n], non_blocking=True)
         out = self.decode(B)
         if self.device.type == "cuda":
-            self.h_out[:B].copy_(out, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            return self.h_out[:n].tolist()
-        return out[:n].tolist()
+            st.h_out[:B].copy_(out, non_blocking=True)
+            st.record()
+        else:
+            st.h_out[:B].copy_(out)
+        self._stage_idx ^= 1
+        return PendingDecode(st, n)
+
+    def collect_decode(self, p: "PendingDecode") -> List[int]:
+        """Waits for a launched decode step and returns its sampled ids."""
+        p.stage.wait()
+        return p.stage.h_out[:p.n].tolist()
+
+    def decode_step(self, ids, positions, slots, ctx, block_tables, temperature, top_k, top_p, steps) -> List[int]:
+        """Host-to-host decode step: stage, upload, run, read back the sampled ids."""
+        return self.collect_decode(self.launch_decode(ids, positions, slots, ctx, block_tables, temperature,
+                                                      top_k, top_p, steps))
 
     def capture(self, B: int) -> torch.cuda.CUDAGraph:
         """Warm up (allocates split workspaces) and capture the decode graph of bucket B."""

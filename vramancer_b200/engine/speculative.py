@@ -94,6 +94,25 @@ def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: S
         preds = ops.argmax(logits).cpu().tolist()
     else:
         preds = torch.argmax(logits.float(), -1).tolist()
+    # non-greedy requests (fed one token, no draft) draw their token with their own
+    # temperature / top-k / top-p from the logits of that position
+    rows, samp = [], []
+    off = 0
+    for r, feed in zip(active, feeds):
+        if not r.params.greedy:
+            rows.append(off)
+            samp.append(r)
+        off += len(feed)
+    if samp:
+        dev = logits.device
+        sel = logits[torch.tensor(rows, device=dev)].contiguous()
+        f32 = lambda v: torch.tensor(v, dtype=torch.float32, device=dev)   # noqa: E731
+        i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)     # noqa: E731
+        drawn = ops.sample(sel, f32([r.params.temperature for r in samp]), i32([r.params.top_k for r in samp]),
+                           f32([r.params.top_p for r in samp]), runner.seed,
+                           i32([len(r.output_ids) for r in samp])).cpu().tolist()
+        for row, tok in zip(rows, drawn):
+            preds[row] = int(tok)
     out = []
     off = 0
     stats.steps += 1

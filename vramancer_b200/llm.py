@@ -52,6 +52,8 @@ class LLM:
         self.cfg = cfg
         self.device = torch.device(device)
         if self.device.type == "cuda":
+            if self.device.index is None:         # "cuda" = the current device
+                self.device = torch.device("cuda", torch.cuda.current_device())
             torch.cuda.set_device(self.device)
         self.tp = tp
         tp_rank, tp_size = (tp.rank, tp.size) if tp is not None else (0, 1)
