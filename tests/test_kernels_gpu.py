@@ -153,6 +153,41 @@ def test_paged_decode(D, Hq, KH, fp8, splits, cuda_errors_clean):
     _close(out, ref, rtol=3e-2, atol=3e-2)
 
 
+@pytest.mark.parametrize("D,Hq,KH,rope", [(128, 40, 8, True), (128, 28, 4, True), (64, 12, 12, False)])
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("splits", [0, 1, 3])
+def test_paged_decode_fused_rope_kv_write(D, Hq, KH, rope, fp8, splits, cuda_errors_clean):
+    """Decode attention that also rotates q / k and writes this step's k / v into the
+    cache gives the same bits (output and cache) as the standalone RoPE + KV write
+    kernel followed by decode attention.  Row 2 is a padded row (no context, slot -1)."""
+    lens = [1, 17, 0, 300, 64, 1033]
+    L, layer = 2, 1
+    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    cache, bt, scale = _make_cache([max(n, 1) for n in lens], L, KH, D, dt, layer, seed=D + Hq + 7)
+    B = len(lens)
+    g = torch.Generator().manual_seed(splits)
+    qkv = torch.randn(B, (Hq + 2 * KH) * D, generator=g).bfloat16()
+    cl = torch.tensor(lens, dtype=torch.int32)
+    pos = torch.tensor([max(n - 1, 0) for n in lens], dtype=torch.int32)
+    slots = torch.tensor([int(bt[b, (n - 1) // 16]) * 16 + (n - 1) % 16 if n > 0 else -1
+                          for b, n in enumerate(lens)], dtype=torch.int32)
+    cs = ops.rope_cos_sin(2048, D, 1e6, device=DEV) if rope else None
+    sm = 1.0 / math.sqrt(D)
+    d = lambda t: t.to(DEV) if t is not None else None   # noqa: E731
+    # standalone kernels
+    c1, q1 = d(cache).clone(), d(qkv).clone()
+    ops.rope_kv_write(q1, d(pos), cs, c1, d(slots), d(scale), layer, Hq, KH, D)
+    o1 = ops.paged_attention_decode(q1, c1, layer, d(bt), d(cl), d(scale), sm, Hq, num_splits=splits)
+    # fused
+    c2, q2 = d(cache).clone(), d(qkv).clone()
+    o2 = ops.paged_attention_decode(q2, c2, layer, d(bt), d(cl), d(scale), sm, Hq, num_splits=splits,
+                                    positions=d(pos), cos_sin=cs, slot_mapping=d(slots))
+    torch.cuda.synchronize()
+    assert torch.equal(c1.view(torch.uint8), c2.view(torch.uint8))
+    assert torch.equal(o1[[0, 1, 3, 4, 5]], o2[[0, 1, 3, 4, 5]])
+    assert torch.equal(q2, d(qkv))            # the fused kernel leaves the qkv rows as they were
+
+
 @pytest.mark.parametrize("splits", [0, 2, 7])
 @pytest.mark.parametrize("tma", [False, True])
 def test_paged_decode_many_sequences(splits, tma, cuda_errors_clean):

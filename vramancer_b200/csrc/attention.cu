@@ -100,7 +100,58 @@ struct DecodeParams {
   float* ws_o;
   float* ws_ml;
   uint32_t* counters;
+  // Fused RoPE + KV write (positions != null): q holds the unrotated qkv rows (k of KV
+  // head h at column (Hq + h) * D, v at (Hq + KH + h) * D); q and the new k are rotated
+  // here (rotate-half over all D dims; cos_sin null = no rotation) and the token's k / v
+  // are stored at slot_mapping[b] by the warp that reads that page.
+  const int* positions;
+  const float* cos_sin;      // [max_pos, D] = [cos | sin]
+  const int* slot_mapping;
+  uint8_t* cache_w;
+  int Hq;
 };
+
+// Stores this step's k (rotated) and v of sequence b, KV head kvh, into its cache slot,
+// with the rounding of the standalone RoPE + KV write kernel (k rounded to bf16 after
+// rotation; fp8 pages take that bf16 value / scale, saturating).
+template <int D, bool kFp8>
+__device__ __forceinline__ void decode_write_new_kv(const DecodeParams& P, int b, int kvh, int lane) {
+  const int slot = P.slot_mapping[b];
+  if (slot < 0) return;
+  constexpr int kEl = kFp8 ? 1 : 2;
+  constexpr int H2 = D / 2;
+  const int KH = P.KH;
+  const __nv_bfloat16* row = P.q + (size_t)b * P.ld_q;
+  const __nv_bfloat16* ks = row + (size_t)(P.Hq + kvh) * D;
+  const __nv_bfloat16* vs = row + (size_t)(P.Hq + KH + kvh) * D;
+  const int page = slot / kPage, off = slot % kPage;
+  const size_t head_stride = (size_t)kPage * D * kEl;
+  uint8_t* kd = P.cache_w + (size_t)page * ((size_t)P.num_layers * 2 * KH * head_stride) +
+                (((size_t)P.layer * 2 + 0) * KH + kvh) * head_stride + (size_t)off * D * kEl;
+  uint8_t* vd = kd + (size_t)KH * head_stride;
+  float kinv = 1.f, vinv = 1.f;
+  if (kFp8) {
+    kinv = 1.f / P.kv_scale[(P.layer * 2 + 0) * KH + kvh];
+    vinv = 1.f / P.kv_scale[(P.layer * 2 + 1) * KH + kvh];
+  }
+  auto put = [&](uint8_t* dst, int d, __nv_bfloat16 x, float inv) {
+    if (kFp8) dst[d] = __nv_cvt_float_to_fp8(__bfloat162float(x) * inv, __NV_SATFINITE, __NV_E4M3);
+    else reinterpret_cast<__nv_bfloat16*>(dst)[d] = x;
+  };
+  const float* cs = P.cos_sin ? P.cos_sin + (size_t)P.positions[b] * D : nullptr;
+  for (int i = lane; i < H2; i += 32) {
+    __nv_bfloat16 a = ks[i], c2 = ks[i + H2];
+    if (cs) {
+      float o1, o2;
+      rope_rotate(__bfloat162float(a), __bfloat162float(c2), cs[i], cs[H2 + i], o1, o2);
+      a = __float2bfloat16(o1);
+      c2 = __float2bfloat16(o2);
+    }
+    put(kd, i, a, kinv);
+    put(kd, i + H2, c2, kinv);
+  }
+  for (int d = lane; d < D; d += 32) put(vd, d, vs[d], vinv);
+}
 
 template <int D, bool kFp8>
 __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
@@ -163,6 +214,14 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   if (early) issue(my_first, 0);
   cp_async_commit();
   pdl_wait();
+  if (P.positions != nullptr && ctx > 0 && live_page >= p_begin && live_page < p_end &&
+      warp == ((live_page - p_begin) & 3)) {
+    // fused KV write: the warp that reads the live page stores this step's token first;
+    // the fence orders the stores before that warp's cp.async reads of the page
+    decode_write_new_kv<D, kFp8>(P, b, kvh, lane);
+    __threadfence();
+    __syncwarp();
+  }
   if (!early && my_first < p_end) issue(my_first, 0);
   cp_async_commit();
 
@@ -179,6 +238,23 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
         qb[kk][1] = *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 8 + 2 * c);
       } else {
         qb[kk][0] = qb[kk][1] = 0u;
+      }
+    }
+    if (P.positions != nullptr && P.cos_sin != nullptr && g < G) {
+      // fused RoPE on q: dims d and d + D/2 sit in chunks kk and kk + D/32 of this thread
+      const float* cs = P.cos_sin + (size_t)P.positions[b] * D;
+#pragma unroll
+      for (int kk = 0; kk < D / 32; ++kk) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int d = kk * 16 + h * 8 + 2 * c;
+          const uint32_t lo = qb[kk][h], hi = qb[kk + D / 32][h];
+          float a0, a1, b0, b1;
+          rope_rotate(bf16_lo(lo), bf16_lo(hi), cs[d], cs[D / 2 + d], a0, b0);
+          rope_rotate(bf16_hi(lo), bf16_hi(hi), cs[d + 1], cs[D / 2 + d + 1], a1, b1);
+          qb[kk][h] = pack_bf16x2(a0, a1);
+          qb[kk + D / 32][h] = pack_bf16x2(b0, b1);
+        }
       }
     }
   }
@@ -1022,6 +1098,15 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   p.ld_o = a.ld_o;
   p.ws_o = p.ws_ml = nullptr;
   p.counters = nullptr;
+  p.positions = a.positions;
+  p.cos_sin = a.cos_sin;
+  p.slot_mapping = a.slot_mapping;
+  p.cache_w = reinterpret_cast<uint8_t*>(const_cast<void*>(a.cache));
+  p.Hq = a.Hq;
+  if (a.positions != nullptr) {
+    VRM_REQUIRE(a.slot_mapping != nullptr, "decode attention: fused KV write needs slot_mapping");
+    VRM_REQUIRE(a.cos_sin == nullptr || a.rot_dim == a.D, "decode attention: fused RoPE needs rot_dim == head_dim");
+  }
   if (splits > 1) {
     const size_t need = decode_attention_scratch_bytes(a.B, a.Hq, a.D, splits);
     float* ws = a.ws;
@@ -1038,7 +1123,8 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   }
   // persistent TMA kernel: bf16 pages, row coordinates of the pool within int32
   const int64_t pool_rows = a.cache_pages * a.num_layers * 2 * a.KH * kPage;
-  if (!a.cache_fp8 && a.cache_pages > 0 && pool_rows < (int64_t)INT32_MAX && decode_tma_enabled() &&
+  if (!a.cache_fp8 && a.positions == nullptr && a.cache_pages > 0 && pool_rows < (int64_t)INT32_MAX &&
+      decode_tma_enabled() &&
       (reinterpret_cast<uintptr_t>(a.cache) & 15) == 0) {
     if (splits > 1) VRM_REQUIRE(p.ws_o != nullptr && p.counters != nullptr, "decode attention: scratch");
     DecodeTmaParams t;

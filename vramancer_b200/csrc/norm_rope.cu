@@ -215,10 +215,10 @@ __global__ void rope_kv_write_kernel(RopeKvArgs a) {
     if (!is_v && cs != nullptr && half > 0) {
       for (int i = lane; i < half; i += 32) {
         const float c = cs[i], s = cs[half + i];
-        const float x1 = __bfloat162float(hv[i]);
-        const float x2 = __bfloat162float(hv[i + half]);
-        hv[i] = __float2bfloat16(x1 * c - x2 * s);
-        hv[i + half] = __float2bfloat16(x2 * c + x1 * s);
+        float o1, o2;
+        rope_rotate(__bfloat162float(hv[i]), __bfloat162float(hv[i + half]), c, s, o1, o2);
+        hv[i] = __float2bfloat16(o1);
+        hv[i + half] = __float2bfloat16(o2);
       }
       __syncwarp();
     }

@@ -229,7 +229,7 @@ void add_(Tensor& a, const Tensor& b) {
 // ---------------------------------------------------------------- attention
 void attn_decode(const Tensor& q, const Tensor& cache, int64_t layer, const Tensor& block_tables,
                  const Tensor& context_lens, const OptT& kv_scale, double sm_scale, Tensor& out, int64_t num_splits,
-                 int64_t num_q_heads) {
+                 int64_t num_q_heads, const OptT& positions, const OptT& cos_sin, const OptT& slot_mapping) {
   check_cache(cache);
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 2 && q.stride(1) == 1 &&
                   q.stride(0) % 2 == 0,
@@ -268,6 +268,24 @@ void attn_decode(const Tensor& q, const Tensor& cache, int64_t layer, const Tens
   a.max_pages = (int)block_tables.size(1);
   a.num_splits = (int)num_splits;
   a.cache_pages = cache.size(0);
+  if (has(positions)) {
+    // fused RoPE + KV write: q is the whole qkv row
+    TORCH_CHECK(has(slot_mapping), "decode: fused KV write needs slot_mapping");
+    TORCH_CHECK(positions->scalar_type() == torch::kInt32 && positions->is_contiguous() && positions->numel() >= B,
+                "decode: int32 positions [B]");
+    TORCH_CHECK(slot_mapping->scalar_type() == torch::kInt32 && slot_mapping->is_contiguous() &&
+                    slot_mapping->numel() >= B, "decode: int32 slot_mapping [B]");
+    TORCH_CHECK(q.size(1) >= (a.Hq + 2 * a.KH) * a.D, "decode: fused KV write needs the qkv row");
+    same_device_opt(q, {&positions, &cos_sin, &slot_mapping}, "paged_attention_decode");
+    a.positions = positions->data_ptr<int>();
+    a.slot_mapping = slot_mapping->data_ptr<int>();
+    if (has(cos_sin)) {
+      TORCH_CHECK(cos_sin->scalar_type() == torch::kFloat32 && cos_sin->is_contiguous() && cos_sin->dim() == 2,
+                  "decode: fp32 cos_sin [max_pos, rot_dim]");
+      a.cos_sin = cos_sin->data_ptr<float>();
+      a.rot_dim = (int)cos_sin->size(1);
+    }
+  }
   const c10::cuda::CUDAGuard guard(q.device());
   vrm::paged_attention_decode(a, cur_stream());
 }
@@ -966,7 +984,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("add_", &add_, py::arg("a"), py::arg("b"));
   m.def("paged_attention_decode", &attn_decode, py::arg("q"), py::arg("cache"), py::arg("layer"),
         py::arg("block_tables"), py::arg("context_lens"), py::arg("kv_scale"), py::arg("sm_scale"), py::arg("out"),
-        py::arg("num_splits"), py::arg("num_q_heads"));
+        py::arg("num_splits"), py::arg("num_q_heads"), py::arg("positions") = py::none(),
+        py::arg("cos_sin") = py::none(), py::arg("slot_mapping") = py::none());
   m.def("paged_attention_prefill", &attn_prefill, py::arg("q"), py::arg("cache"), py::arg("layer"),
         py::arg("block_tables"), py::arg("cu_q"), py::arg("context_lens"), py::arg("kv_scale"), py::arg("sm_scale"),
         py::arg("out"), py::arg("max_q_len"), py::arg("num_q_heads"));

@@ -291,6 +291,14 @@ __device__ __forceinline__ unsigned long long globaltimer() {
 }
 
 // ---------------------------------------------------------------- misc
+// Rotate-half RoPE of one (x1, x2) pair: (x1 c - x2 s, x2 c + x1 s), with the products
+// and sums rounded separately (no FMA contraction), so every kernel that rotates q or k
+// (the standalone RoPE + KV write and the fused decode attention) gives the same bits.
+__device__ __forceinline__ void rope_rotate(float x1, float x2, float c, float s, float& o1, float& o2) {
+  o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+  o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+}
+
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -316,6 +316,12 @@ struct DecodeAttnArgs {
   // pages in the pool (its first dimension): > 0 enables the persistent TMA kernel for
   // bf16 pages (0 keeps the per-(sequence, head, split) kernel)
   int64_t cache_pages = 0;
+  // fused RoPE + KV write of this step's token (positions != null): q is the
+  // unrotated qkv row [Hq q | KH k | KH v heads]; the cache is written at slot_mapping
+  const int* positions = nullptr;      // [B]
+  const float* cos_sin = nullptr;      // [max_pos, rot_dim] or null (no rotation)
+  int rot_dim = 0;                     // must equal D when cos_sin is given
+  const int* slot_mapping = nullptr;   // [B], -1 = no write
 };
 void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t stream);
 // Selects the persistent TMA decode kernel for bf16 pages (default off, VRM_DECODE_TMA=1).

@@ -16,6 +16,7 @@ core/tensor_parallel.py:172-445 (no KV cache there); this module owns the forwar
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Callable, List, Optional
 
@@ -86,6 +87,10 @@ class DecoderModel:
         self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
         self.cos_sin = (ops.rope_cos_sin(cfg.max_position, cfg.rot_dim, cfg.rope_theta, self.device)
                         if cfg.rot_dim > 0 else None)
+        # decode attention does RoPE + the KV write itself when rotation covers the whole
+        # head (or there is none); VRM_FUSED_ROPE=0 keeps the separate kernel
+        self.fused_rope = (cfg.rot_dim in (0, cfg.head_dim) and cfg.head_dim in (64, 128)
+                           and os.environ.get("VRM_FUSED_ROPE", "1") != "0")
 
     @property
     def num_local_layers(self) -> int:
@@ -118,6 +123,12 @@ class DecoderModel:
         hq, kvh, D = self.hq, self.kvh, self.D
         qkv = ops.linear(x, self.lw(i, "qkv_w"), self.lw(i, "qkv_b"))
         li = i - self.first_layer
+        if batch.is_decode and self.fused_rope and qkv.is_cuda:
+            # RoPE + KV-page write inside the decode attention kernel (one launch fewer)
+            return ops.paged_attention_decode(qkv, pool.cache, li, batch.block_tables, batch.context_lens,
+                                              pool.kv_scale, self.sm_scale, hq, num_splits=batch.attn_splits,
+                                              positions=batch.positions, cos_sin=self.cos_sin,
+                                              slot_mapping=batch.slot_mapping)
         ops.rope_kv_write(qkv, batch.positions, self.cos_sin, pool.cache, batch.slot_mapping, pool.kv_scale,
                           li, hq, kvh, D)
         if batch.is_decode:
