@@ -7,7 +7,7 @@ produces vramancer_b200/_C*.so (CUDA kernels) and vramancer_b200/_runtime*.so
 """
 import os
 
-from setuptools import Extension, setup
+from setuptools import Extension, find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -60,7 +60,8 @@ if runtime_sources:
 setup(
     name="vramancer_b200",
     version="0.1.0",
-    packages=["vramancer_b200"],
+    packages=find_packages(include=["vramancer_b200", "vramancer_b200.*"]),
+    entry_points={"console_scripts": ["vramancer = vramancer_b200.cli:main"]},
     ext_modules=ext_modules,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )
