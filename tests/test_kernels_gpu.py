@@ -113,6 +113,95 @@ def test_rope_kv_write(fp8, D, cuda_errors_clean):
     _close(cache_g.float(), cache_c.float(), rtol=7e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("M", [1, 7, 32, 100])
+def test_gemm_folded_norm_producer(M, cuda_errors_clean):
+    """A residual GEMM that also stores per-(128-feature tile, token) sums of squares of
+    its bf16 output: same output bits as without, sums equal to the fp32 reference."""
+    torch.manual_seed(M)
+    K, N = 512, 640
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) * 0.05).bfloat16()
+    r = torch.randn(M, N, device=DEV).bfloat16()
+    ref = r.clone()
+    ops.linear(x, w, residual=ref, out=ref)
+    out = r.clone()
+    buf = torch.full((8, 128), -1.0, device=DEV)
+    ops.linear(x, w, residual=out, out=out, ssq_out=buf)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    want = (out.float() ** 2).view(M, 5, 128).sum(-1).t()
+    _close(buf[:5, :M], want, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("M", [1, 16, 48, 128])
+@pytest.mark.parametrize("silu", [False, True])
+def test_gemm_folded_norm_consumer(M, silu, cuda_errors_clean):
+    """GEMM on the raw residual stream scaled per token by rsqrt(mean of squares + eps)
+    from partial sums (the folded RMSNorm) against the fp32 reference."""
+    torch.manual_seed(M + 3 * silu)
+    K, N = 640, 768
+    h = (torch.randn(M, K) * 2).bfloat16()
+    w = (torch.randn(N, K) * 0.05).bfloat16()
+    b = None if silu else (torch.randn(N) * 0.1).bfloat16()
+    buf = torch.zeros(8, 128)
+    buf[:5, :M] = (h.float() ** 2).view(M, 5, 128).sum(-1).t()
+    epi = ops.EPI_SILU_MUL if silu else ops.EPI_NONE
+    ref = ops.linear(h, w, b, epilogue=epi, ssq_in=buf, ssq_parts=5, norm_eps=1e-6)
+    got = ops.linear(h.to(DEV), w.to(DEV), b.to(DEV) if b is not None else None, epilogue=epi,
+                     ssq_in=buf.to(DEV), ssq_parts=5, norm_eps=1e-6)
+    _close(got, ref)
+    # the same as RMSNorm (weight 1) followed by the plain GEMM
+    xn = ops.rmsnorm(h.to(DEV), torch.ones(K, device=DEV).bfloat16(), 1e-6)
+    _close(got, ops.linear(xn, w.to(DEV), b.to(DEV) if b is not None else None, epilogue=epi))
+
+
+def test_folded_norm_decode_logits(cuda_errors_clean):
+    """A model whose RMSNorms run inside the decode GEMMs (folded weights, norm sums
+    from the residual GEMMs) gives the logits of the same model with standalone norm
+    kernels: prefill (norms without weight + folded weights) and a decode step."""
+    from vramancer_b200.kv.pool import KVPool, KVPoolSpec
+    from vramancer_b200.models.config import PRESETS
+    from vramancer_b200.models.transformer import DecoderModel, ForwardBatch
+    from vramancer_b200.models.weights import random_weights
+    cfg = PRESETS["tiny-qwen2-d128"]
+    lens = [5, 20, 33]
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=DEV)   # noqa: E731
+
+    def run(fold):
+        w = random_weights(cfg, device=DEV, dtype=torch.bfloat16, seed=11)
+        model = DecoderModel(cfg, w, device=DEV, dtype=torch.bfloat16)
+        if fold:
+            assert model.fold_norms()
+        pool = KVPool(KVPoolSpec(16, cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, dtype=torch.bfloat16), DEV)
+        bt = [[4 * b + j for j in range(4)] for b in range(3)]
+        ids, pos, slots, cu = [], [], [], [0]
+        for b, p in enumerate(prompts):
+            ids += p
+            pos += list(range(len(p)))
+            slots += [bt[b][t // 16] * 16 + t % 16 for t in range(len(p))]
+            cu.append(cu[-1] + len(p))
+        pre = ForwardBatch(input_ids=i32(ids), positions=i32(pos), slot_mapping=i32(slots), block_tables=i32(bt),
+                           context_lens=i32(lens), is_decode=False, cu_q=i32(cu), max_q_len=max(lens),
+                           logits_rows=torch.tensor([c - 1 for c in cu[1:]], device=DEV))
+        lp = model.forward(pre, pool).float()
+        dec = ForwardBatch(input_ids=i32([7, 8, 9]), positions=i32(lens),
+                           slot_mapping=i32([bt[b][n // 16] * 16 + n % 16 for b, n in enumerate(lens)]),
+                           block_tables=i32(bt), context_lens=i32([n + 1 for n in lens]), is_decode=True,
+                           attn_splits=0)
+        ld = model.forward(dec, pool).float()
+        return lp, ld, model.folded
+
+    lp0, ld0, f0 = run(False)
+    lp1, ld1, f1 = run(True)
+    assert not f0 and f1
+    scale = ld0.abs().max().item()
+    _close(lp1, lp0, rtol=0.0, atol=0.03 * scale)
+    _close(ld1, ld0, rtol=0.0, atol=0.03 * scale)
+    assert (ld1 - ld0).abs().mean().item() < 0.005 * scale
+
+
 # ------------------------------------------------------------------------- attention
 def _make_cache(lens, L, KH, D, dt, layer, seed=0):
     torch.manual_seed(seed)

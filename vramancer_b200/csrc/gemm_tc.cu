@@ -60,13 +60,59 @@ struct EpiParams {
   // FP8 operands: the accumulator is scaled by scale_w[weight row] * scale_x[token] first
   const float* scale_w;
   const float* scale_x;
+  // RMSNorm folded into the decode GEMMs (swap-AB stream-K kernel only; GemmArgs):
+  // a producer (residual epilogue) stores per (weight tile, token) the sum over the
+  // tile's 128 features of bf16(out)^2 at ssq_out[tile * ssq_ld + token]; a consumer
+  // scales its accumulator by rstd[m] = rsqrt(sum_p ssq_in[p * ssq_ld + m] / norm_dim
+  // + eps) before bias and SiLU (its weight columns carry the norm weight).
+  float* ssq_out = nullptr;
+  const float* ssq_in = nullptr;
+  int ssq_ld = 0, ssq_parts = 0, norm_dim = 0;
+  float norm_eps = 0.f;
 };
+
+// Sum over the warp's 32 lanes of each of 16 per-lane values, reduce-scatter style
+// (16 shuffles instead of 16 x 5): every lane returns the total of value index
+// (lane >> 1) & 15.  Partners add the same two numbers, so both lanes of a pair agree.
+__device__ __forceinline__ float warp_sum16_scatter(float (&q)[16], int lane) {
+  {
+    const bool up = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float send = up ? q[i] : q[i + 8], keep = up ? q[i + 8] : q[i];
+      q[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+  }
+  {
+    const bool up = lane & 8;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = up ? q[i] : q[i + 4], keep = up ? q[i + 4] : q[i];
+      q[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+  }
+  {
+    const bool up = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = up ? q[i] : q[i + 2], keep = up ? q[i + 2] : q[i];
+      q[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+  }
+  {
+    const bool up = lane & 2;
+    const float send = up ? q[0] : q[1], keep = up ? q[1] : q[0];
+    q[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return q[0] + __shfl_xor_sync(0xffffffffu, q[0], 1);
+}
 
 // Store one accumulator row segment.  `tok` / `feat0` are output coordinates of the
 // first value; in swap mode the 16 values run over tokens (fixed feature), otherwise
 // over features (fixed token).
 template <bool kSwapAB>
-__device__ __forceinline__ void epi_store(const EpiParams& p, int row_glob, int col0, const float (&v_in)[16]) {
+__device__ __forceinline__ void epi_store(const EpiParams& p, int row_glob, int col0, const float (&v_in)[16],
+                                          float* rounded = nullptr) {
   float v[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = v_in[j];
@@ -186,7 +232,9 @@ __device__ __forceinline__ void epi_store(const EpiParams& p, int row_glob, int 
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int m = col0 + j;
-      if (m < p.M) p.out[(size_t)m * p.ldo + n] = __float2bfloat16(v[j] + bn + rv[j]);
+      const __nv_bfloat16 o = __float2bfloat16(v[j] + bn + rv[j]);
+      if (m < p.M) p.out[(size_t)m * p.ldo + n] = o;
+      if (rounded) rounded[j] = m < p.M ? __bfloat162float(o) : 0.f;   // (caller zero-fills)
     }
   }
 }
@@ -431,6 +479,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* s_ssq = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(tmem_slot) + 16);   // [2][4 warps][16]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
@@ -583,6 +632,27 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     pdl_wait();
     uint32_t epoch = 0;
     if (kAR) epoch = *reinterpret_cast<volatile uint32_t*>(ar.epoch) + 1u;
+    // folded RMSNorm (consumer): rstd of token lane + 32 i in rs[i] of every epilogue warp
+    float rs[4] = {1.f, 1.f, 1.f, 1.f};
+    if (ep.ssq_in != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int m = lane + 32 * i;
+        if (m < ep.M) {
+          // eight independent loads per round: a few L2 round trips, not one per part
+          float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          int q = 0;
+          for (; q + 8 <= ep.ssq_parts; q += 8) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) a[u] += ep.ssq_in[(size_t)(q + u) * ep.ssq_ld + m];
+          }
+          for (; q < ep.ssq_parts; ++q) a[0] += ep.ssq_in[(size_t)q * ep.ssq_ld + m];
+          const float sq = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+          rs[i] = rsqrtf(sq / (float)ep.norm_dim + ep.norm_eps);
+        }
+      }
+    }
+    int chunk_no = 0;   // parity selects the s_ssq half (one barrier per chunk)
     int seg = 0;
     for (int64_t it = it_begin; it < it_end; ++seg) {
       const int t = (int)(it / k_tiles);
@@ -659,7 +729,37 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
             }
           }
         } else {
-          epi_store<true>(ep, r_glob, tok0 + c0, v);
+          if (ep.ssq_in != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int m = tok0 + c0 + j;   // the same for every lane
+              const int i = (m >> 5) & 3;
+              const float sel = i == 0 ? rs[0] : i == 1 ? rs[1] : i == 2 ? rs[2] : rs[3];
+              v[j] *= __shfl_sync(0xffffffffu, sel, m & 31);
+            }
+          }
+          if (ep.ssq_out == nullptr) {
+            epi_store<true>(ep, r_glob, tok0 + c0, v);
+          } else {
+            // folded RMSNorm (producer): per-token sum of squares of the stored values
+            float q[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) q[j] = 0.f;
+            epi_store<true>(ep, r_glob, tok0 + c0, v, q);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) q[j] *= q[j];
+            const float part = warp_sum16_scatter(q, lane);
+            float* buf = s_ssq + (chunk_no & 1) * 64;
+            if ((lane & 1) == 0) buf[(warp & 3) * 16 + ((lane >> 1) & 15)] = part;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (threadIdx.x >= 64 && threadIdx.x < 80) {
+              const int j = threadIdx.x - 64;
+              const int m = tok0 + c0 + j;
+              const float tot = buf[j] + buf[16 + j] + buf[32 + j] + buf[48 + j];
+              if (m < ep.M) ep.ssq_out[(size_t)tw * ep.ssq_ld + m] = tot;
+            }
+            ++chunk_no;
+          }
         }
       }
       tc_fence_before();
@@ -1033,7 +1133,7 @@ static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const E
                            int max_ctas, cudaStream_t stream, const ARParams& ar, int tiles_x = 1) {
   // smem: stages + 2*STAGES+4 barriers + slots.  K counts bf16 elements (for e4m3
   // operands: pairs of bytes, so that one K-tile is the same 128-byte swizzle row)
-  constexpr int kSmem = STAGES * GemmSmem<BN, STAGES>::kStageBytes + (2 * STAGES + 5) * 8 + 16 + 1024;
+  constexpr int kSmem = STAGES * GemmSmem<BN, STAGES>::kStageBytes + (2 * STAGES + 5) * 8 + 16 + 512 + 1024;
   auto kern = gemm_streamk_swap_kernel<BN, STAGES, kAR, kF8>;
   static int attr_dev_mask = 0;
   int dev = 0;
@@ -1147,7 +1247,21 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   ep.epilogue = a.epilogue;
   ep.scale_w = nullptr;
   ep.scale_x = nullptr;
+  ep.ssq_out = a.ssq_out;
+  ep.ssq_in = a.ssq_in;
+  ep.ssq_ld = a.ssq_ld;
+  ep.ssq_parts = a.ssq_parts;
+  ep.norm_dim = a.norm_dim;
+  ep.norm_eps = a.norm_eps;
   const int k_tiles = (a.K + kBK - 1) / kBK;
+  if (a.ssq_out || a.ssq_in) {
+    VRM_REQUIRE(a.M <= 128 && a.M <= a.ssq_ld && a.force_splits <= 0 && !legacy_decode() && !a.allreduce,
+                "gemm: the folded RMSNorm runs on the stream-K decode path (M <= 128) only");
+    VRM_REQUIRE(!a.ssq_out || (a.residual != nullptr && a.epilogue == kEpiNone &&
+                               (a.N + kBM - 1) / kBM <= a.ssq_parts_cap),
+                "gemm: norm sums come from a residual epilogue, one slot per weight tile");
+    VRM_REQUIRE(!a.ssq_in || (a.ssq_parts > 0 && a.norm_dim > 0), "gemm: folded norm needs its sums");
+  }
 
   if (a.M <= 128) {
     // decode: swap A/B so the weight rows fill the 128 TMEM lanes; stream-K schedule

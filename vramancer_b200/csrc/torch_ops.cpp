@@ -50,7 +50,7 @@ void check_cache(const Tensor& cache) {
 
 // ---------------------------------------------------------------- GEMM
 void gemm_out(const Tensor& x, const Tensor& w, const OptT& bias, Tensor& out, int64_t force_splits, int64_t epilogue,
-              const OptT& residual) {
+              const OptT& residual, const OptT& ssq_out, const OptT& ssq_in, int64_t ssq_parts, double norm_eps) {
   check_bf16_2d(x, "gemm x");
   check_bf16_2d(w, "gemm w");
   check_bf16_2d(out, "gemm out");
@@ -80,6 +80,26 @@ void gemm_out(const Tensor& x, const Tensor& w, const OptT& bias, Tensor& out, i
   a.ldo = out.stride(0);
   a.M = (int)M;
   a.N = (int)N;
+  for (const OptT* t : {&ssq_out, &ssq_in}) {
+    if (has(*t)) {
+      TORCH_CHECK((*t)->scalar_type() == torch::kFloat32 && (*t)->is_contiguous() && (*t)->dim() == 2,
+                  "gemm: norm sums must be contiguous fp32 [parts, tokens]");
+      same_device(x, {&**t}, "gemm");
+    }
+  }
+  if (has(ssq_out)) {
+    a.ssq_out = ssq_out->data_ptr<float>();
+    a.ssq_ld = (int)ssq_out->size(1);
+    a.ssq_parts_cap = (int)ssq_out->size(0);
+  }
+  if (has(ssq_in)) {
+    TORCH_CHECK(ssq_parts > 0 && ssq_parts <= ssq_in->size(0), "gemm: ssq_parts out of range");
+    a.ssq_in = ssq_in->data_ptr<float>();
+    a.ssq_ld = (int)ssq_in->size(1);
+    a.ssq_parts = (int)ssq_parts;
+    a.norm_dim = (int)K;
+    a.norm_eps = (float)norm_eps;
+  }
   a.K = (int)K;
   a.force_splits = (int)force_splits;
   a.epilogue = (int)epilogue;
@@ -90,7 +110,7 @@ void gemm_out(const Tensor& x, const Tensor& w, const OptT& bias, Tensor& out, i
 Tensor gemm(const Tensor& x, const Tensor& w, const OptT& bias, int64_t force_splits, int64_t epilogue) {
   const int64_t n_out = epilogue == vrm::kEpiSiluMul ? w.size(0) / 2 : w.size(0);
   auto out = torch::empty({x.size(0), n_out}, x.options());
-  gemm_out(x, w, bias, out, force_splits, epilogue, c10::nullopt);
+  gemm_out(x, w, bias, out, force_splits, epilogue, c10::nullopt, c10::nullopt, c10::nullopt, 0, 0.0);
   return out;
 }
 
@@ -970,7 +990,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, py::arg("x"), py::arg("w"), py::arg("bias") = py::none(), py::arg("force_splits") = 0,
         py::arg("epilogue") = 0);
   m.def("gemm_out", &gemm_out, py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("out"),
-        py::arg("force_splits") = 0, py::arg("epilogue") = 0, py::arg("residual") = py::none());
+        py::arg("force_splits") = 0, py::arg("epilogue") = 0, py::arg("residual") = py::none(),
+        py::arg("ssq_out") = py::none(), py::arg("ssq_in") = py::none(), py::arg("ssq_parts") = 0,
+        py::arg("norm_eps") = 0.0);
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"));
   m.def("layernorm", &layernorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("b"), py::arg("out"),
         py::arg("eps"));

@@ -38,6 +38,15 @@ struct GemmArgs {
   // optional fused all-reduce over the TP group (decode shapes): instead of storing Y,
   // push the fp32 partial into every rank's receive buffer (see ARPush)
   const struct ARPush* allreduce = nullptr;
+  // RMSNorm folded into decode GEMMs (M <= 128, stream-K path).  Producer (needs a
+  // residual epilogue): ssq_out[t * ssq_ld + m] = sum over weight tile t's 128 rows of
+  // bf16(Y[m, n])^2, for ceil(N / 128) <= ssq_parts_cap tiles.  Consumer: Y[m, :] is
+  // scaled by rsqrt(sum_{p < ssq_parts} ssq_in[p * ssq_ld + m] / norm_dim + norm_eps)
+  // before bias / SiLU (the norm weight is folded into W's columns).
+  float* ssq_out = nullptr;
+  const float* ssq_in = nullptr;
+  int ssq_ld = 0, ssq_parts = 0, ssq_parts_cap = 0, norm_dim = 0;
+  float norm_eps = 0.f;
 };
 
 // Push half of the fused tensor-parallel all-reduce.  Every rank owns a receive

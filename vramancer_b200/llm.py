@@ -42,7 +42,7 @@ class LLM:
                  max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, weights=None,
                  num_layers: Optional[int] = None, tp=None, quantization: Optional[str] = None,
                  spec_num_draft: int = 0, spec_ngram: int = 3, kv_offload_pages: int = 0, hierarchy=None,
-                 stream_layers: int = 0, ep=None):
+                 stream_layers: int = 0, ep=None, fold_norms: bool = True):
         if isinstance(model, ModelConfig):
             cfg = model
         else:
@@ -96,6 +96,10 @@ class LLM:
             use_cuda_graph = False
         else:
             self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype, tp=tp, ep=ep)
+            if (fold_norms and self.quantization is None and ep is None and (tp is None or tp.size == 1)
+                    and os.environ.get("VRM_FOLD_NORM", "1") != "0"):
+                # small decode batches run the RMSNorms inside the GEMMs (weights folded in place)
+                self.model.fold_norms()
         kvd = kv_dtype_from_str(kv_cache_dtype)
         if kv_pages is None:
             kv_pages = self._pages_from_memory(cfg, kvd, gpu_memory_utilization, max_batch, max_model_len)

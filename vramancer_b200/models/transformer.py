@@ -65,6 +65,13 @@ class TPContext:
         self.fused_ar = fused_ar
 
 
+# Returned in place of a normalised activation when the next GEMM applies the RMSNorm
+# itself (decode with folded norms): it reads the residual stream and the per-token
+# sums of squares the previous GEMM stored.
+_FOLDED = object()
+FOLD_MAX_TOKENS = int(os.environ.get("VRM_FOLD_MAX_TOKENS", "16"))
+
+
 class DecoderModel:
     def __init__(self, cfg: ModelConfig, weights: Weights, *, device="cpu", dtype=torch.bfloat16,
                  first_layer: int = 0, last_layer: Optional[int] = None, tp: Optional[TPContext] = None,
@@ -91,6 +98,14 @@ class DecoderModel:
         # head (or there is none); VRM_FUSED_ROPE=0 keeps the separate kernel
         self.fused_rope = (cfg.rot_dim in (0, cfg.head_dim) and cfg.head_dim in (64, 128)
                            and os.environ.get("VRM_FUSED_ROPE", "1") != "0")
+        # folded RMSNorm (fold_norms): weights already folded by another model over the
+        # same tensors are detected, so every model on them normalises without weight
+        self._ssq = None
+        self._ssq_parts = 0
+        self._fold_active = False
+        first_qkv = self.lw(self.first_layer, "qkv_w") if self.last_layer > self.first_layer else None
+        self.folded = getattr(first_qkv, "_vrm_norm_w", None) is not None
+        self._ones = (torch.ones(cfg.hidden_size, dtype=dtype, device=self.device) if self.folded else None)
 
     @property
     def num_local_layers(self) -> int:
@@ -107,21 +122,67 @@ class DecoderModel:
                                  pos_table=self.w["pos_embed"])
         return ops.embedding(batch.input_ids, self.w["embed"])
 
+    def fold_norms(self) -> bool:
+        """Folds each layer's input and post-attention RMSNorm weight into the columns of
+        the GEMM that consumes the normalised activation (qkv_w, gate_up_w: W' = W
+        diag(w_norm), in place, marked on the tensor), so that small decode batches run
+        the norms inside the GEMMs: the GEMM that adds into the residual stream stores
+        per-token sums of squares of its output, the next GEMM reads the residual stream
+        and scales by rsqrt(mean + eps) (two launches fewer per layer).  Prefill and
+        larger batches normalise without weight and use W'.  Dense RMSNorm models at
+        TP = 1 with resident bf16 CUDA weights; returns whether the weights are folded."""
+        cfg = self.cfg
+        if self.folded:
+            return self._alloc_fold()
+        if (self.device.type != "cuda" or self.tp_size != 1 or cfg.is_gpt2 or cfg.is_moe
+                or self.dtype != torch.bfloat16 or cfg.hidden_size > 64 * 128 or self.last_layer <= self.first_layer):
+            return False
+        pairs = []
+        for i in range(self.first_layer, self.last_layer):
+            for wk, nk in (("qkv_w", "in_norm_w"), ("gate_up_w", "post_norm_w")):
+                W, nw = self.lw(i, wk), self.lw(i, nk)
+                if (not isinstance(W, torch.Tensor) or getattr(W, "_vrm_quant", None) is not None or nw is None
+                        or W.dtype != torch.bfloat16 or W.device.type != "cuda" or W.shape[1] != nw.numel()
+                        or (self.device.index is not None and W.device.index != self.device.index)):
+                    return False
+                pairs.append((W, nw))
+        for W, nw in pairs:
+            W.mul_(nw.to(W.dtype).view(1, -1))
+            W._vrm_norm_w = nw.detach().clone()
+        self.folded = True
+        self._ones = torch.ones(cfg.hidden_size, dtype=self.dtype, device=self.device)
+        return self._alloc_fold()
+
+    def _alloc_fold(self) -> bool:
+        if self.device.type == "cuda" and self.tp_size == 1 and self._ssq is None:
+            self._ssq_parts = (self.cfg.hidden_size + 127) // 128
+            self._ssq = torch.zeros(self._ssq_parts, 128, dtype=torch.float32, device=self.device)
+        return self.folded
+
+    def _in_proj(self, x, r: torch.Tensor, w, b, epilogue: int = 0) -> torch.Tensor:
+        """The GEMM that consumes a normalised activation (or, folded, the residual stream)."""
+        if x is _FOLDED:
+            return ops.linear(r, w, b, epilogue=epilogue, ssq_in=self._ssq, ssq_parts=self._ssq_parts,
+                              norm_eps=self.cfg.norm_eps)
+        return ops.linear(x, w, b, epilogue=epilogue)
+
     def _norm(self, x, i_or_name, which: str, residual=None):
         cfg = self.cfg
         if isinstance(i_or_name, int):
             w = self.lw(i_or_name, f"{which}_w")
             b = self.lw(i_or_name, f"{which}_b")
+            if self.folded and which in ("in_norm", "post_norm"):
+                w = self._ones          # the weight lives in the next GEMM's columns
         else:
             w, b = self.w["final_norm_w"], self.w.get("final_norm_b")
         if cfg.is_gpt2:
             return ops.layernorm(x, w, b, cfg.norm_eps, residual=residual)
         return ops.rmsnorm(x, w, cfg.norm_eps, residual=residual)
 
-    def _attention(self, i: int, x: torch.Tensor, batch: ForwardBatch, pool: KVPool) -> torch.Tensor:
+    def _attention(self, i: int, x, batch: ForwardBatch, pool: KVPool, r: Optional[torch.Tensor] = None) -> torch.Tensor:
         cfg = self.cfg
         hq, kvh, D = self.hq, self.kvh, self.D
-        qkv = ops.linear(x, self.lw(i, "qkv_w"), self.lw(i, "qkv_b"))
+        qkv = self._in_proj(x, r, self.lw(i, "qkv_w"), self.lw(i, "qkv_b"))
         li = i - self.first_layer
         if batch.is_decode and self.fused_rope and qkv.is_cuda:
             # RoPE + KV-page write inside the decode attention kernel (one launch fewer)
@@ -143,6 +204,10 @@ class DecoderModel:
         """r += x @ w.T (+ b) across the TP group; returns norm(r) when `nxt` names the
         norm that follows ((layer, "post_norm" | "in_norm") or (None, "final"))."""
         if self.tp_size == 1:
+            if self._fold_active and nxt and nxt[0] is not None:
+                # the next GEMM normalises: store the per-token sums of squares instead
+                ops.linear(x, w, b, residual=r, out=r, ssq_out=self._ssq)
+                return _FOLDED
             ops.linear(x, w, b, residual=r, out=r)
             return self._norm(r, nxt[0] if nxt[0] is not None else "final", nxt[1]) if nxt else None
         far = self.tp.fused_ar
@@ -183,7 +248,7 @@ class DecoderModel:
         if cfg.is_moe:
             # residual add (and the next layer's input norm) fused into the combine
             return self._moe(i, x, r, self._norm_params(*nxt)[0] if nxt else None)
-        a = ops.linear(x, self.lw(i, "gate_up_w"), epilogue=ops.EPI_SILU_MUL)
+        a = self._in_proj(x, r, self.lw(i, "gate_up_w"), None, ops.EPI_SILU_MUL)
         return self._row_parallel(a, self.lw(i, "down_w"), None, r, nxt)
 
     def _moe(self, i: int, x: torch.Tensor, r: torch.Tensor, norm_w: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -213,7 +278,7 @@ class DecoderModel:
         fused into this layer's last projection, else None."""
         if x is None:
             x = self._norm(r, i, "in_norm")
-        attn = self._attention(i, x, batch, pool)
+        attn = self._attention(i, x, batch, pool, r)
         x = self._row_parallel(attn, self.lw(i, "o_w"), self.lw(i, "o_b"), r, (i, "post_norm"))
         nxt = (i + 1, "in_norm") if i + 1 < self.last_layer else None
         return self._mlp(i, x, r, nxt)
@@ -235,6 +300,12 @@ class DecoderModel:
         r = self.embed(batch) if self.has_embed else hidden
         if r is None:
             raise ValueError("non-first pipeline stage needs the hidden state")
+        # small decode batches run the folded norms inside the GEMMs.  Measured on B200
+        # (Qwen2.5-14B, graph-replayed step): batch 1 6.38 -> 6.26 ms, but batch 32 7.58 ->
+        # 8.36 ms (the norm-sum epilogue and the per-token rsqrt cost more than the norm
+        # launches they replace there), so batches above 16 keep the norm kernels.
+        self._fold_active = (self._ssq is not None and batch.is_decode and r.is_cuda
+                             and r.shape[0] <= FOLD_MAX_TOKENS)
         x = None
         for i in range(self.first_layer, self.last_layer):
             x = self.layer(i, r, batch, pool, x)

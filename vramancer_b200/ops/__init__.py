@@ -59,19 +59,31 @@ EPI_SILU_MUL = 1
 # --------------------------------------------------------------------------- GEMM
 def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, *,
            out: Optional[torch.Tensor] = None, epilogue: int = EPI_NONE,
-           residual: Optional[torch.Tensor] = None, force_splits: int = 0) -> torch.Tensor:
+           residual: Optional[torch.Tensor] = None, force_splits: int = 0,
+           ssq_out: Optional[torch.Tensor] = None, ssq_in: Optional[torch.Tensor] = None,
+           ssq_parts: int = 0, norm_eps: float = 0.0) -> torch.Tensor:
     """y = x @ w.T (+ bias) (+ residual); with EPI_SILU_MUL, w rows are interleaved
     (gate_j, up_j) pairs and y[:, j] = silu(gate_j) * up_j.  `w` may be a quantised
-    weight (quant.nvfp4.NVFP4Weight), which brings its own GEMM."""
+    weight (quant.nvfp4.NVFP4Weight), which brings its own GEMM.
+
+    Folded RMSNorm (decode, M <= 128): with `ssq_out` [parts, >= M] fp32 (needs
+    `residual`), ssq_out[t, m] = sum over output features 128 t .. 128 t + 127 of
+    bf16(y[m, n])^2; with `ssq_in`, x @ w.T is first scaled per row by
+    rsqrt(sum_{t < ssq_parts} ssq_in[t, m] / K + norm_eps) (w carries the norm weight)."""
     if getattr(w, "_vrm_quant", None) is not None:
+        if ssq_out is not None or ssq_in is not None:
+            raise ValueError("the folded RMSNorm needs a bf16 weight")
         return w.linear(x, bias, out=out, epilogue=epilogue, residual=residual)
     if x.is_cuda:
         if out is None:
             n = w.shape[0] // 2 if epilogue == EPI_SILU_MUL else w.shape[0]
             out = torch.empty(x.shape[0], n, dtype=x.dtype, device=x.device)
-        native().gemm_out(x, w, bias, out, force_splits, epilogue, residual)
+        native().gemm_out(x, w, bias, out, force_splits, epilogue, residual, ssq_out, ssq_in, ssq_parts, norm_eps)
         return out
     y = x.float() @ w.float().t()
+    if ssq_in is not None:
+        sq = ssq_in[:ssq_parts, : x.shape[0]].sum(0)
+        y = y * torch.rsqrt(sq / x.shape[1] + norm_eps)[:, None]
     if bias is not None:
         y = y + bias.float()
     if epilogue == EPI_SILU_MUL:
@@ -80,6 +92,11 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None
     if residual is not None:
         y = y + residual.float()
     y = y.to(x.dtype)
+    if ssq_out is not None:
+        M, N = y.shape
+        parts = (N + 127) // 128
+        yf = torch.nn.functional.pad(y.float(), (0, parts * 128 - N))
+        ssq_out[:parts, :M] = (yf * yf).view(M, parts, 128).sum(-1).t()
     if out is not None:
         out.copy_(y)
         return out

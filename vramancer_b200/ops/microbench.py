@@ -68,8 +68,10 @@ def time_it(fn, iters=50, warm=5, graph=True):
     return e0.elapsed_time(e1) / iters * 1000.0  # us
 
 
-def bench_gemm(m, n, k, iters=50, copies=None, residual=False):
-    """Rotates over enough weight copies to exceed L2 so every launch streams from HBM."""
+def bench_gemm(m, n, k, iters=50, copies=None, residual=False, fold=None):
+    """Rotates over enough weight copies to exceed L2 so every launch streams from HBM.
+    fold="producer": residual GEMM that also stores the per-token norm sums;
+    fold="consumer": GEMM scaled by the folded RMSNorm (norm sums read per call)."""
     hbm, tflops, src = peaks()
     wbytes = n * k * 2
     if copies is None:
@@ -79,15 +81,24 @@ def bench_gemm(m, n, k, iters=50, copies=None, residual=False):
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
     state = [0]
 
+    ssq = torch.ones(64, 128, device="cuda") if fold else None
+    parts = (k + 127) // 128
+    if fold == "producer":
+        residual = True
+
     def fn():
         # residual=True: the in-place residual update of the decode step (out += x W^T)
-        linear(x, ws[state[0] % copies], out=out, residual=out if residual else None)
+        if fold == "consumer":
+            linear(x, ws[state[0] % copies], out=out, ssq_in=ssq, ssq_parts=parts, norm_eps=1e-6)
+        else:
+            linear(x, ws[state[0] % copies], out=out, residual=out if residual else None,
+                   ssq_out=ssq if fold == "producer" else None)
         state[0] += 1
 
     us = time_it(fn, iters)
     byts = wbytes + m * k * 2 + m * n * 2 * (2 if residual else 1)
     flops = 2.0 * m * n * k
-    r = {"kernel": "gemm", "m": m, "n": n, "k": k, "residual": residual, "us": round(us, 2),
+    r = {"kernel": "gemm", "m": m, "n": n, "k": k, "residual": residual, "fold": fold, "us": round(us, 2),
          "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3),
          "tflops": round(flops / us / 1e6, 1), "frac_tc": round(flops / us / 1e6 / tflops, 3),
          "peaks": src}
@@ -348,6 +359,7 @@ def main(argv=None):
     ap.add_argument("--fp8", action="store_true")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--residual", action="store_true")
+    ap.add_argument("--fold", action="store_true", help="gemm: also the folded-norm producer / consumer modes")
     a = ap.parse_args(argv)
     native()
     if a.what == "trace":
@@ -355,6 +367,14 @@ def main(argv=None):
             r = trace_gemm(a.m, n, k)
             r["name"] = name
             print(json.dumps(r))
+    elif a.what == "gemm" and a.fold:
+        for m in (1, 32):
+            for name, n, k in QWEN14B_DECODE[:4]:
+                for mode in ((None, "consumer") if name in ("qkv", "gate_up") else (None, "producer")):
+                    r = bench_gemm(m, n, k, a.iters, residual=(mode is None and name in ("o_proj", "down")),
+                                   fold=mode)
+                    r["name"] = name
+                    print(json.dumps(r))
     elif a.what == "gemm":
         print(json.dumps(bench_gemm(a.m, a.n, a.k, a.iters, residual=a.residual)))
     elif a.what == "nvfp4":

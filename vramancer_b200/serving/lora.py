@@ -84,6 +84,10 @@ class LoRAManager:
                 continue
             delta = (B.float() @ A.float()) * (scale * sign)
             delta = delta.to(W.device)
+            nw = getattr(W, "_vrm_norm_w", None)
+            if nw is not None:
+                # W carries its input RMSNorm weight in its columns (folded norms)
+                delta = delta * nw.float().view(1, -1)
             if key == "qkv_w":
                 off = {"q": 0, "k": cfg.q_size, "v": cfg.q_size + cfg.kv_size}[part]
                 rows = W[off:off + delta.shape[0]]
