@@ -34,7 +34,8 @@ def _sources(d, exts):
 
 
 cuda_sources = _sources(CSRC, (".cu", ".cpp"))
-runtime_sources = _sources(RT, (".cpp",))
+# selftest.cpp is the standalone sanitizer driver (tests/test_runtime_sanitizers.py), not part of the module
+runtime_sources = [f for f in _sources(RT, (".cpp",)) if not f.endswith("selftest.cpp")]
 
 ext_modules = [
     CUDAExtension(
