@@ -41,3 +41,18 @@ def test_runtime_asan_ubsan(tmp_path):
 
 def test_runtime_tsan(tmp_path):
     _build_and_run(tmp_path, ["-fsanitize=thread"], {"TSAN_OPTIONS": "halt_on_error=1"})
+
+
+def test_kernel_bounds_check_build_compiles(tmp_path):
+    """The bounds-check variant (-DVRM_BOUNDS_CHECK=1) of the kernels that index the KV
+    pool through tables (paged attention, RoPE + KV write, page copy) still compiles
+    for sm_100a."""
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(nvcc):
+        pytest.skip("no nvcc")
+    csrc = os.path.join(os.path.dirname(RT), "csrc")
+    for f in ("norm_rope.cu", "migrate.cu", "attention.cu"):
+        r = subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O1", "-std=c++17",
+                            "--expt-relaxed-constexpr", "-DVRM_BOUNDS_CHECK=1", "-c", os.path.join(csrc, f),
+                            "-o", str(tmp_path / (f + ".o"))], capture_output=True, text=True, timeout=900)
+        assert r.returncode == 0, (f, r.stderr[-2000:])

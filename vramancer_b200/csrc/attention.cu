@@ -109,6 +109,8 @@ struct DecodeParams {
   const int* slot_mapping;
   uint8_t* cache_w;
   int Hq;
+  long long num_pages;       // pool pages (checked in bounds-check builds)
+  uint32_t* err;
 };
 
 // Stores this step's k (rotated) and v of sequence b, KV head kvh, into its cache slot,
@@ -117,7 +119,7 @@ struct DecodeParams {
 template <int D, bool kFp8>
 __device__ __forceinline__ void decode_write_new_kv(const DecodeParams& P, int b, int kvh, int lane) {
   const int slot = P.slot_mapping[b];
-  if (slot < 0) return;
+  if (slot < 0 || !in_bounds(slot / kPage, P.num_pages, P.err)) return;
   constexpr int kEl = kFp8 ? 1 : 2;
   constexpr int H2 = D / 2;
   const int KH = P.KH;
@@ -188,7 +190,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   const size_t page_stride = (size_t)P.num_layers * 2 * KH * head_stride;   // one page, all layers
 
   auto issue = [&](int page_local, int stage) {
-    const int page = bt[page_local];
+    int page = bt[page_local];
+    if (!in_bounds(page, P.num_pages, P.err)) page = 0;   // bounds-check builds: read page 0 instead
     const uint8_t* kp = P.cache + (size_t)page * page_stride + (((size_t)P.layer * 2 + 0) * KH + kvh) * head_stride;
     const uint8_t* vp = kp + (size_t)KH * head_stride;
     uint8_t* dst = wbase + stage * S::kStageB;
@@ -808,6 +811,8 @@ struct PrefillParams {
   float sm_scale;
   __nv_bfloat16* out;
   int64_t ld_o;
+  long long num_pages;       // pool pages (checked in bounds-check builds)
+  uint32_t* err;
 };
 
 template <int D, bool kFp8>
@@ -866,7 +871,8 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
       const int pg = i / kPageChunks, w = i % kPageChunks;
       const int page_local = chunk * 4 + pg;
       const bool valid = page_local * kPage < ctx;
-      const int page = valid ? bt[page_local] : 0;
+      int page = valid ? bt[page_local] : 0;
+      if (!in_bounds(page, P.num_pages, P.err)) page = 0;   // bounds-check builds
       const uint8_t* kp = P.cache + (size_t)page * page_stride + (((size_t)P.layer * 2 + 0) * KH + kvh) * head_stride;
       const uint8_t* vp = kp + (size_t)KH * head_stride;
       const int r = pg * kPage + w / kChunkPerRow, ch = w % kChunkPerRow;
@@ -1103,6 +1109,8 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   p.slot_mapping = a.slot_mapping;
   p.cache_w = reinterpret_cast<uint8_t*>(const_cast<void*>(a.cache));
   p.Hq = a.Hq;
+  p.num_pages = a.cache_pages;
+  p.err = error_word();
   if (a.positions != nullptr) {
     VRM_REQUIRE(a.slot_mapping != nullptr, "decode attention: fused KV write needs slot_mapping");
     VRM_REQUIRE(a.cos_sin == nullptr || a.rot_dim == a.D, "decode attention: fused RoPE needs rot_dim == head_dim");
@@ -1201,6 +1209,8 @@ void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
   p.sm_scale = a.sm_scale;
   p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
   p.ld_o = a.ld_o;
+  p.num_pages = a.cache_pages;
+  p.err = error_word();
   dim3 grid((a.max_q_len + 63) / 64, a.Hq, a.B);
   if (a.D == 128) {
     if (a.cache_fp8) launch_prefill<128, true>(grid, p, st);

@@ -23,7 +23,8 @@ constexpr int kChunkVecs = kCopyThreads * kVecPerThread;           // 2048 vecto
 
 __global__ void __launch_bounds__(kCopyThreads)
     page_copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, const int* __restrict__ src_idx,
-                     const int* __restrict__ dst_idx, int n_pages, long long page_vecs) {
+                     const int* __restrict__ dst_idx, int n_pages, long long page_vecs, long long src_pages,
+                     long long dst_pages, uint32_t* err) {
   pdl_launch();
   pdl_wait_for(src, src_idx, dst_idx);
   const long long chunks_per_page = (page_vecs + kChunkVecs - 1) / kChunkVecs;
@@ -31,6 +32,7 @@ __global__ void __launch_bounds__(kCopyThreads)
   for (long long w = blockIdx.x; w < total; w += gridDim.x) {
     const int p = (int)(w / chunks_per_page);
     const long long c = w - (long long)p * chunks_per_page;
+    if (!in_bounds(src_idx[p], src_pages, err) || !in_bounds(dst_idx[p], dst_pages, err)) continue;
     const uint4* s = src + (long long)src_idx[p] * page_vecs + c * kChunkVecs;
     uint4* d = dst + (long long)dst_idx[p] * page_vecs + c * kChunkVecs;
     const long long lim = min((long long)kChunkVecs, page_vecs - c * kChunkVecs);
@@ -49,7 +51,7 @@ __global__ void __launch_bounds__(kCopyThreads)
 }
 
 void page_copy(const void* src_pool, void* dst_pool, const int* src_idx, const int* dst_idx, int n_pages,
-               size_t page_bytes, cudaStream_t stream) {
+               size_t page_bytes, cudaStream_t stream, int64_t src_pages, int64_t dst_pages) {
   if (n_pages <= 0) return;
   VRM_REQUIRE(page_bytes % 16 == 0, "page_copy: page size must be a multiple of 16 bytes");
   VRM_REQUIRE((reinterpret_cast<uintptr_t>(src_pool) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst_pool) & 15) == 0,
@@ -58,7 +60,8 @@ void page_copy(const void* src_pool, void* dst_pool, const int* src_idx, const i
   const long long chunks = (long long)n_pages * ((page_vecs + kChunkVecs - 1) / kChunkVecs);
   const int grid = (int)std::min<long long>(chunks, (long long)device_sm_count() * 4);
   launch_kernel(page_copy_kernel, dim3(grid), dim3(kCopyThreads), 0, stream, reinterpret_cast<const uint4*>(src_pool),
-                reinterpret_cast<uint4*>(dst_pool), src_idx, dst_idx, n_pages, page_vecs);
+                reinterpret_cast<uint4*>(dst_pool), src_idx, dst_idx, n_pages, page_vecs, (long long)src_pages,
+                (long long)dst_pages, error_word());
 }
 
 bool enable_peer_access(int device, int peer) {

@@ -222,7 +222,7 @@ __global__ void rope_kv_write_kernel(RopeKvArgs a) {
       }
       __syncwarp();
     }
-    if (h >= a.Hq && slot >= 0) {
+    if (h >= a.Hq && slot >= 0 && in_bounds(slot / a.page_size, a.num_pages, a.err)) {
       const int kvh = is_v ? h - a.Hq - a.KH : h - a.Hq;
       const int kv = is_v ? 1 : 0;
       const int page = slot / a.page_size, off = slot % a.page_size;
@@ -243,8 +243,10 @@ __global__ void rope_kv_write_kernel(RopeKvArgs a) {
   }
 }
 
-void rope_kv_write(const RopeKvArgs& a, cudaStream_t st) {
-  if (a.T <= 0) return;
+void rope_kv_write(const RopeKvArgs& a_in, cudaStream_t st) {
+  if (a_in.T <= 0) return;
+  RopeKvArgs a = a_in;
+  a.err = error_word();
   VRM_REQUIRE(!a.cache_fp8 || a.kv_scale != nullptr, "rope_kv_write: fp8 cache needs kv_scale");
   const int threads = 32 * std::min(16, a.Hq + 2 * a.KH);
   if (a.cache_fp8) launch_kernel(rope_kv_write_kernel<true>, dim3(a.T), dim3(threads), 0, st, a);

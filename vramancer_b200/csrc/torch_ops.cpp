@@ -183,6 +183,7 @@ void rope_kv_write(Tensor& qkv, const OptT& positions, const OptT& cos_sin, Tens
   }
   a.cache = cache.data_ptr();
   a.cache_fp8 = is_fp8_cache(cache);
+  a.num_pages = cache.size(0);
   a.num_layers = (int)cache.size(1);
   a.layer = (int)layer;
   a.page_size = (int)cache.size(4);
@@ -327,6 +328,7 @@ void attn_prefill(const Tensor& q, const Tensor& cache, int64_t layer, const Ten
   a.ld_q = q.stride(0);
   a.cache = cache.data_ptr();
   a.cache_fp8 = is_fp8_cache(cache);
+  a.cache_pages = cache.size(0);
   a.num_layers = (int)cache.size(1);
   a.layer = (int)layer;
   a.KH = (int)cache.size(3);
@@ -978,7 +980,7 @@ void page_copy(const Tensor& src_pool, Tensor& dst_pool, const Tensor& src_idx, 
                 "page_copy: no peer access between the two GPUs");
   }
   vrm::page_copy(src_pool.data_ptr(), dst_pool.data_ptr(), src_idx.data_ptr<int>(), dst_idx.data_ptr<int>(),
-                 (int)src_idx.numel(), page_bytes, cur_stream());
+                 (int)src_idx.numel(), page_bytes, cur_stream(), src_pool.size(0), dst_pool.size(0));
 }
 
 }  // namespace

@@ -32,11 +32,27 @@ enum ErrCode : uint32_t {
   kErrMbarTimeout = 1,     // an mbarrier wait ran out of its budget
   kErrFlagTimeout = 2,     // a cross-CTA / cross-GPU flag wait ran out
   kErrBadShape = 4,        // launch-time shape check failed on device
+  kErrBounds = 8,          // bounds-check build: a page / slot index outside its pool
 };
 
 __device__ __forceinline__ void report_error(uint32_t* err, uint32_t code) {
   if (err) atomicOr(err, code);
 }
+
+// Bounds-check builds (VRM_BOUNDS_CHECK=1 python setup.py build_ext --inplace): page
+// and slot indices read from block tables / slot maps / page lists are checked against
+// the pool they index (n > 0); an index out of range sets kErrBounds in the error word
+// and the caller skips or redirects the access instead of touching memory outside the
+// pool.  Default builds compile the check away.
+#if defined(VRM_BOUNDS_CHECK) && VRM_BOUNDS_CHECK
+__device__ __forceinline__ bool in_bounds(long long i, long long n, uint32_t* err) {
+  if (n <= 0 || (i >= 0 && i < n)) return true;
+  report_error(err, kErrBounds);
+  return false;
+}
+#else
+__device__ __forceinline__ bool in_bounds(long long, long long, uint32_t*) { return true; }
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

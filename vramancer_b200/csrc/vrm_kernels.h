@@ -292,6 +292,8 @@ struct RopeKvArgs {
   int num_layers = 0, layer = 0, page_size = 16;
   const int* slot_mapping = nullptr;   // [T] page * page_size + offset, < 0 skips
   const float* kv_scale = nullptr;     // [layers, 2, KH] (fp8 only)
+  int64_t num_pages = 0;               // pool pages (checked in bounds-check builds)
+  uint32_t* err = nullptr;             // error word (set by rope_kv_write)
 };
 void rope_kv_write(const RopeKvArgs& a, cudaStream_t stream);
 
@@ -354,6 +356,7 @@ struct PrefillAttnArgs {
   void* out = nullptr;
   int64_t ld_o = 0;
   int B = 0, max_q_len = 0;
+  int64_t cache_pages = 0;             // pool pages (checked in bounds-check builds)
 };
 void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t stream);
 
@@ -372,8 +375,9 @@ void ipc_close(void* p);
 // ---------------------------------------------------------------- KV page migration (migrate.cu)
 // dst_pool[dst_idx[i]] <- src_pool[src_idx[i]] for whole pages of page_bytes; runs on the
 // current (source) device; dst_pool may be a peer GPU's memory (peer access enabled).
+// src_pages / dst_pages: the pools' page counts (checked in bounds-check builds; 0 = unknown)
 void page_copy(const void* src_pool, void* dst_pool, const int* src_idx, const int* dst_idx, int n_pages,
-               size_t page_bytes, cudaStream_t stream);
+               size_t page_bytes, cudaStream_t stream, int64_t src_pages = 0, int64_t dst_pages = 0);
 // Enables device -> peer access for this process (no-op if already enabled); false if unsupported.
 bool enable_peer_access(int device, int peer);
 
