@@ -62,6 +62,7 @@ setup(
     name="vramancer_b200",
     version="0.1.0",
     packages=find_packages(include=["vramancer_b200", "vramancer_b200.*"]),
+    package_data={"vramancer_b200.utils": ["monitoring/*.yml", "monitoring/*.json"]},
     entry_points={"console_scripts": ["vramancer = vramancer_b200.cli:main"]},
     ext_modules=ext_modules,
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

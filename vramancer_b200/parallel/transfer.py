@@ -146,6 +146,10 @@ class TransferManager:
         self._peer_enabled.add((src, dst))
 
     def _record(self, r: TransferResult) -> TransferResult:
+        from ..utils import observability as obs
+        m = getattr(r.method, "value", str(r.method))
+        obs.METRICS.transfer_bytes.labels(m).inc(r.bytes_transferred)
+        obs.METRICS.transfer_seconds.labels(m).observe(r.duration_s)
         with self._lock:
             self.results.append(r)
             if len(self.results) > 10000:

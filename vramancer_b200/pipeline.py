@@ -170,6 +170,10 @@ class InferencePipeline:
                 if self.enable_metrics:
                     METRICS.batch_size.set(len(eng.running))
                     METRICS.queue_depth.set(len(eng.waiting))
+                    free = eng.kv.num_free_pages()
+                    dev = str(getattr(eng.runner, "device", "cpu"))
+                    METRICS.kv_free_pages.labels(dev).set(free)
+                    METRICS.kv_used_pages.labels(dev).set(eng.kv.num_pages - free)
             except Exception as e:   # fail the running requests, keep serving
                 log.error("engine step failed: %s", e)
                 if self.fault is not None and self.fault.states:
@@ -217,16 +221,22 @@ class InferencePipeline:
         with span("pipeline.generate", model=str(self.model_name), max_new_tokens=max_new_tokens):
             if (enable_speculative or self.spec is not None) and temperature <= 0 and self.spec is not None:
                 ids = self.spec.generate(self._encode(prompt), max_new_tokens)
-                out_ids, ttft = ids, None
+                out_ids, ttft, itl = ids, None, None
             else:
                 req: Request = self.submit(prompt, max_new_tokens, temperature, top_p, top_k, **kw).result(timeout)
                 out_ids, ttft = req.output_ids, req.ttft
+                # mean inter-token latency of this request (first token to last)
+                itl = None
+                if len(out_ids) > 1 and req.first_token_time is not None and req.finish_time is not None:
+                    itl = (req.finish_time - req.first_token_time) / (len(out_ids) - 1)
         dt = time.perf_counter() - t0
         if self.enable_metrics:
             METRICS.tokens_generated.inc(len(out_ids))
             METRICS.infer_latency.observe(dt)
             if ttft is not None:
                 METRICS.ttft.observe(ttft)
+            if itl is not None:
+                METRICS.itl.observe(itl)
         self.history.record("generate", str(self.model_name), len(self._encode(prompt)), len(out_ids), dt, ttft)
         return out_ids if return_ids else self.tokenizer.decode(out_ids)
 

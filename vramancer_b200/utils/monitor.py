@@ -81,6 +81,11 @@ class GPUMonitor:
 
     def poll(self) -> List[Dict[str, float]]:
         self.latest = [self.nvml.sample(i) for i in range(self.nvml.count())]
+        from . import observability as obs
+        for d in self.latest:
+            g = str(int(d["index"]))
+            obs.METRICS.gpu_mem_used.labels(g).set(d["mem_used"])
+            obs.METRICS.gpu_mem_total.labels(g).set(d["mem_total"])
         for cb in list(self.callbacks):
             try:
                 cb(self.latest)
