@@ -107,6 +107,28 @@ __device__ __forceinline__ float warp_sum16_scatter(float (&q)[16], int lane) {
   return q[0] + __shfl_xor_sync(0xffffffffu, q[0], 1);
 }
 
+// Stream-K fixup: out[j] = sum over contributors 1 .. nc-1 (in order) of their fp32
+// partial of this thread's row, columns c0 .. c0+15 (`base` = contributor 0's slot at
+// this row; slots are kBM x BN apart, column-major with kBM rows).  Two contributors'
+// loads are in flight at once.
+template <int BN>
+__device__ __forceinline__ void sum_partials16_t(const float* base, int nc, int c0, float (&out)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) out[j] = 0.f;
+  for (int q0 = 1; q0 < nc; q0 += 2) {
+    float x[2][16];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        x[u][j] = q0 + u < nc ? __ldcg(base + (size_t)(q0 + u) * (kBM * BN) + (size_t)(c0 + j) * kBM) : 0.f;
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j] += x[u][j];
+  }
+}
+
 // Store one accumulator row segment.  `tok` / `feat0` are output coordinates of the
 // first value; in swap mode the 16 values run over tokens (fixed feature), otherwise
 // over features (fixed token).
@@ -660,8 +682,6 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       const int64_t n = min((int64_t)(k_tiles - k0), it_end - it);
       const bool whole = (k0 == 0 && n == k_tiles);
       const int acc = seg & 1;
-      const bool ok = mbar_wait(&tfull[acc], (uint32_t)((seg >> 1) & 1), err);
-      tc_fence_after();
       const int tw = t / sk.tiles_x, tb = t - tw * sk.tiles_x;
       const int r_glob = tw * kBM + row;   // weight row == output feature
       const int tok0 = tb * BN;            // first token of the tile
@@ -675,8 +695,14 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       const float* base = workspace + (size_t)first_owner * (size_t)(kBM * BN) + row;
       // this rank's slot in the current half; element (token m, feature n) at m * N + n
       const size_t xoff = kAR ? (((size_t)(epoch & 1u) * ar.world + ar.rank) * ar.half_floats + (size_t)r_glob) : 0;
+      // The owner's fixup input does not depend on its own accumulator: wait for the
+      // other contributors' partials (published in their first segment) and sum the
+      // first 16-column chunk of them while this segment's MMAs are still running, so
+      // the tail after the last MMA is the TMEM read, one add and the epilogue.
+      float others0[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) others0[j] = 0.f;
       if (is_owner && !whole) {
-        // wait for the other contributors' partials (published in their first segment)
         if (threadIdx.x == 64) {
           const unsigned long long t0 = clock64();
           while (ld_acquire_gpu(tile_counters + t) < (uint32_t)(nc - 1)) {
@@ -687,7 +713,10 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           }
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
+        sum_partials16_t<BN>(base, nc, 0, others0);
       }
+      const bool ok = mbar_wait(&tfull[acc], (uint32_t)((seg >> 1) & 1), err);
+      tc_fence_after();
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t r[16];
@@ -703,20 +732,16 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           continue;
         }
         if (!whole) {
-          // owner's own contribution is index 0; add the others in contributor order,
-          // loading up to four contributors' partials at once
-          for (int q0 = 1; q0 < nc; q0 += 4) {
-            float x[4][16];
+          // own contribution + (sum of the others in contributor order)
+          float o[16];
+          if (c0 == 0) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-              for (int j = 0; j < 16; ++j)
-                x[u][j] = q0 + u < nc ? __ldcg(base + (size_t)(q0 + u) * (kBM * BN) + (size_t)(c0 + j) * kBM) : 0.f;
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] += x[u][j];
+            for (int j = 0; j < 16; ++j) o[j] = others0[j];
+          } else {
+            sum_partials16_t<BN>(base, nc, c0, o);
           }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += o[j];
         }
         if (kAR) {
           // push the partial into this rank's slot on every rank (own slot is local)
