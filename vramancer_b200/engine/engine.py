@@ -57,8 +57,9 @@ class Request:
     request_id: object = field(default_factory=lambda: f"req-{next(_ids)}")
     on_token: Optional[Callable[["Request", int], None]] = None
     output_ids: List[int] = field(default_factory=list)
-    num_computed: int = 0          # prompt tokens whose KV is written
+    num_computed: int = 0          # tokens of prefill_ids whose KV is written
     cached_tokens: int = 0
+    resumed: bool = False          # preempted after producing tokens: re-prefill, then keep decoding
     finished: bool = False
     finish_reason: Optional[str] = None
     arrival: float = field(default_factory=time.perf_counter)
@@ -67,8 +68,16 @@ class Request:
     future: Optional[Future] = None
 
     @property
+    def prefill_ids(self) -> List[int]:
+        """Tokens whose KV a prefill writes: the prompt, or after a preemption the prompt
+        and every generated token but the last (which the next decode step feeds)."""
+        if self.resumed and self.output_ids:
+            return self.prompt_ids + self.output_ids[:-1]
+        return self.prompt_ids
+
+    @property
     def prefill_done(self) -> bool:
-        return self.num_computed >= len(self.prompt_ids)
+        return self.num_computed >= len(self.prefill_ids)
 
     @property
     def ttft(self) -> Optional[float]:
@@ -158,11 +167,16 @@ class LLMEngine:
     def _admit(self) -> None:
         while self.waiting and len(self.running) < self.max_batch:
             req = self.waiting[0]
-            need = len(req.prompt_ids) + 1
+            ids = req.prefill_ids
+            need = len(ids) + 1
+            if req.resumed:
+                # a preempted sequence comes back only with a page of headroom for every
+                # running one, or it would be preempted again at the next page boundary
+                need += self.kv.page_size * len(self.running)
             if not self.kv.can_allocate(need):
                 break
             try:
-                cached = self.kv.allocate(req.request_id, len(req.prompt_ids), req.prompt_ids)
+                cached = self.kv.allocate(req.request_id, len(ids), ids)
             except OutOfPages:
                 break
             self.waiting.popleft()
@@ -235,12 +249,13 @@ class LLMEngine:
         for req in self.running:
             if req.prefill_done or budget <= 0:
                 continue
-            n = min(len(req.prompt_ids) - req.num_computed, budget)
+            ids = req.prefill_ids
+            n = min(len(ids) - req.num_computed, budget)
             s = req.num_computed
             slots = self.kv.slots_for(req.request_id, s, n)
-            items.append(PrefillItem(token_ids=req.prompt_ids[s:s + n], start_pos=s, slots=slots,
+            items.append(PrefillItem(token_ids=ids[s:s + n], start_pos=s, slots=slots,
                                      block_table=self.kv.block_table(req.request_id), context_len=s + n,
-                                     want_logits=(s + n == len(req.prompt_ids))))
+                                     want_logits=(s + n == len(ids))))
             reqs.append(req)
             budget -= n
         if not items:
@@ -251,7 +266,11 @@ class LLMEngine:
             req.num_computed += len(it.token_ids)
             self.stats["prefill_tokens"] += len(it.token_ids)
             if req.prefill_done:
-                self.kv.commit_prefix(req.request_id, req.prompt_ids)
+                self.kv.commit_prefix(req.request_id, req.prefill_ids)
+                if req.resumed:
+                    # KV rebuilt up to the last generated token: decoding resumes from it
+                    req.resumed = False
+                    continue
                 self._emit(req, int(tok))
                 if req.finished:
                     done.append(req)
@@ -288,6 +307,7 @@ class LLMEngine:
             return
         self._drain(done)
         active = [r for r in active if not r.finished]
+        active = self._ensure_pages(active, done)
         if not active:
             return
         handle = self._launch(active, chained=False)
@@ -295,6 +315,35 @@ class LLMEngine:
             self._pending = (active, handle)
         else:
             self._consume(active, handle, done)
+
+    def _ensure_pages(self, active: List[Request], done: List[Request]) -> List[Request]:
+        """Recompute preemption: when the pool cannot give every sequence of this decode
+        step the page its next token starts, the most recently admitted sequences give
+        their pages back and wait again; on re-admission they prefill prompt + generated
+        tokens (the prefix cache keeps what it still holds) and continue where they
+        stopped.  A lone sequence that outgrows the whole pool ends with reason "length"."""
+        if getattr(self.kv, "_overflow", None) is not None:
+            return active              # the lending pool supplies overflow pages
+        ps = self.kv.page_size
+        while active:
+            need = sum(1 for r in active if self.kv.seq_len(r.request_id) % ps == 0)
+            if need <= self.kv.num_free_pages():
+                return active
+            victim = active[-1]
+            if len(active) == 1:
+                self._finish(victim, "length")
+                done.append(victim)
+                return []
+            active = active[:-1]
+            self.kv.free(victim.request_id)
+            if victim in self.running:
+                self.running.remove(victim)
+            victim.num_computed = 0
+            victim.cached_tokens = 0
+            victim.resumed = True
+            self.waiting.appendleft(victim)
+            self.stats["preempted"] += 1
+        return active
 
     def _can_chain(self, prev: List[Request], active: List[Request]) -> bool:
         """Step n+1 may run before step n is read when the batch is the same requests
