@@ -28,6 +28,7 @@ from concurrent.futures import ThreadPoolExecutor
 from concurrent.futures import TimeoutError as FutTimeout
 from typing import Any, Dict, List, Optional
 
+import torch
 from fastapi import FastAPI, Request
 from fastapi.responses import HTMLResponse, JSONResponse, PlainTextResponse, StreamingResponse
 
@@ -437,6 +438,75 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
     def nodes():
         from ..cluster.discovery import known_nodes
         return {"nodes": known_nodes()}
+
+    # ------------------------------------------------------------------ cross-node workers
+    from ..cluster import worker_api
+    node = worker_api.NodeWorker()
+    app.state.node_worker = node
+
+    def _node_key(body) -> bytes:
+        k = body.get("key") or os.environ.get("VRM_CLUSTER_KEY", "")
+        return k.encode() if isinstance(k, str) else bytes(k)
+
+    @app.get("/api/worker/model_info")
+    def worker_model_info():
+        return node.model_info()
+
+    @app.post("/api/worker/load_partial")
+    async def worker_load_partial(request: Request):
+        try:
+            body = await _json(request)
+            info = await asyncio.get_running_loop().run_in_executor(None, lambda: node.load_partial(
+                str(body["model"]), int(body.get("start_layer", 0)), int(body.get("end_layer", -1)),
+                device=str(body.get("device", "cpu")), dtype=str(body.get("dtype", "float32")),
+                seed=int(body.get("seed", 0)), tcp_port=body.get("tcp_port"),
+                tcp_host=str(body.get("tcp_host", "127.0.0.1")), key=_node_key(body),
+                num_pages=int(body.get("num_pages", 256))))
+            return info
+        except (KeyError, ValueError, ValidationError) as e:
+            return _err(400, f"load_partial: {e}")
+
+    @app.post("/api/worker/forward_layers")
+    async def worker_forward_layers(request: Request):
+        try:
+            body = await _json(request)
+            hidden = worker_api.decode_tensor(body["hidden"]) if body.get("hidden") else None
+            ids = torch.as_tensor(body["input_ids"], dtype=torch.int32) if body.get("input_ids") is not None else None
+            pos = torch.as_tensor(body["positions"], dtype=torch.int32) if body.get("positions") is not None else None
+            out = await asyncio.get_running_loop().run_in_executor(
+                None, lambda: node.forward_layers(hidden=hidden, input_ids=ids, positions=pos))
+            kind = "logits" if node.end == node.cfg.num_layers else "hidden"
+            return {"kind": kind, "layers": [node.start, node.end], "output": worker_api.encode_tensor(out)}
+        except (KeyError, ValueError, ValidationError) as e:
+            return _err(400, f"forward_layers: {e}")
+        except RuntimeError as e:
+            return _err(409, str(e))
+
+    @app.post("/api/distributed/generate")
+    async def distributed_generate(request: Request):
+        try:
+            body = await _json(request)
+            prompts = body.get("prompts") or [body["prompt_ids"]]
+            outs = await asyncio.get_running_loop().run_in_executor(None, lambda: worker_api.distributed_generate(
+                str(body["model"]), [list(map(int, p)) for p in prompts], int(body.get("max_tokens", 16)),
+                int(body["split"]), body.get("workers", []), device=str(body.get("device", "cpu")),
+                dtype=str(body.get("dtype", "float32")), seed=int(body.get("seed", 0)), key=_node_key(body),
+                num_pages=int(body.get("num_pages", 256)), temperature=float(body.get("temperature", 0.0))))
+            return {"outputs": outs, "workers": len(body.get("workers", []))}
+        except (KeyError, ValueError, ValidationError) as e:
+            return _err(400, f"distributed generate: {e}")
+        except (RuntimeError, OSError) as e:
+            return _err(502, f"distributed generate: {e}", "server_error")
+
+    @app.post("/api/swarm/awaken")
+    async def swarm_awaken(request: Request):
+        try:
+            body = await _json(request)
+            n = worker_api.wake_on_lan(body.get("macs", []), str(body.get("broadcast", "255.255.255.255")),
+                                       int(body.get("port", 9)))
+            return {"sent": n}
+        except (ValueError, OSError, ValidationError) as e:
+            return _err(400, f"awaken: {e}")
 
     @app.post("/api/benchmark")
     async def benchmark(request: Request):
