@@ -75,3 +75,48 @@ def test_wrong_drafts_are_rejected_without_changing_output():
             if req.finished:
                 break
     assert req.output_ids == ref
+
+
+def test_speculative_sampling_keeps_the_target_distribution():
+    """Deterministic-draft rejection sampling: the first emitted token is distributed
+    exactly as the target's distribution, whatever the draft."""
+    from vramancer_b200.engine.speculative import accept_sampled
+    p0 = torch.tensor([0.5, 0.3, 0.15, 0.05])
+    p1 = torch.tensor([0.1, 0.2, 0.3, 0.4])
+    probs = torch.stack([p0, p1])
+    gen = torch.Generator().manual_seed(0)
+    for d in (0, 2, 3):
+        counts = torch.zeros(4)
+        n_acc = 0
+        N = 20000
+        for _ in range(N):
+            toks, na = accept_sampled([d], probs, gen)
+            counts[toks[0]] += 1
+            n_acc += na
+        assert (counts / N - p0).abs().max() < 0.015, (d, counts / N)
+        assert abs(n_acc / N - float(p0[d])) < 0.015
+
+
+def test_filtered_probs_top_k_top_p():
+    from vramancer_b200.engine.speculative import filtered_probs
+    lg = torch.log(torch.tensor([[0.5, 0.3, 0.15, 0.05]]))
+    assert torch.allclose(filtered_probs(lg, 1.0, 0, 1.0), torch.tensor([[0.5, 0.3, 0.15, 0.05]]), atol=1e-6)
+    assert torch.allclose(filtered_probs(lg, 1.0, 2, 1.0), torch.tensor([[0.625, 0.375, 0.0, 0.0]]), atol=1e-6)
+    assert torch.allclose(filtered_probs(lg, 1.0, 0, 0.7), torch.tensor([[0.625, 0.375, 0.0, 0.0]]), atol=1e-6)
+
+
+def test_prompt_lookup_with_sampled_requests_runs_and_drafts():
+    """Sampled requests are speculated too (rejection sampling) and still finish with
+    the requested number of tokens."""
+    from vramancer_b200.engine.engine import SamplingParams
+    from vramancer_b200.llm import LLM
+    from vramancer_b200.models.config import PRESETS
+    from vramancer_b200.models.weights import random_weights
+    cfg = PRESETS["tiny-qwen2"]
+    w = random_weights(cfg, device="cpu", dtype=torch.float32, seed=2, std=0.2)
+    llm = LLM(cfg, device="cpu", dtype=torch.float32, kv_cache_dtype="fp32", weights=w, max_batch=4,
+              max_model_len=256, kv_pages=64, spec_num_draft=6, spec_ngram=2)
+    span = list(range(40, 56))
+    reqs = llm.generate([span * 4, span * 3], SamplingParams(max_tokens=24, temperature=0.7, top_k=20))
+    assert all(len(r.output_ids) == 24 for r in reqs)
+    assert llm.engine.spec_stats.proposed > 0

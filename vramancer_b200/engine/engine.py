@@ -280,12 +280,12 @@ class LLMEngine:
         if self.spec_num_draft > 0 and active:
             from .speculative import find_draft, speculative_decode_step
             drafts = [find_draft(r.prompt_ids + r.output_ids, self.spec_ngram, self.spec_num_draft)
-                      if r.params.greedy else [] for r in active]
+                      for r in active]
             if any(drafts):
                 self._drain(done)
                 active = [r for r in active if not r.finished]
                 drafts = [find_draft(r.prompt_ids + r.output_ids, self.spec_ngram, self.spec_num_draft)
-                          if r.params.greedy else [] for r in active]
+                          for r in active]
                 outs = speculative_decode_step(self, active, self.spec_ngram, self.spec_num_draft, self.spec_stats,
                                                drafts=drafts)
                 for r, toks in zip(active, outs):

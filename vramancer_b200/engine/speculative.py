@@ -12,11 +12,18 @@ output is identical to plain decoding.
 Reference parity: prompt lookup = HF `prompt_lookup_num_tokens`
 (core/backends.py:1920-1925, vramancer/dropin.py wrap-generate); draft model =
 core/speculative_decoding.py:95-329 (gamma-adaptive, window 10), whose stochastic
-acceptance (`q > 0.5`, :268-281) is not rejection sampling and is not reproduced:
-sampled requests are not speculated here.
+acceptance (`q > 0.5`, :268-281) is not rejection sampling and is not reproduced.
+Sampled requests use speculative sampling (Leviathan et al. 2023; Chen et al. 2023)
+with a deterministic draft (q = a point mass on each drafted token): draft d_i is kept
+with probability p_i(d_i), where p_i is the target's filtered distribution
+(temperature, top-k, top-p) at that position; at the first rejection the token comes
+from p_i with d_i removed and renormalised, and when every draft is kept a bonus token
+comes from p_k.  The emitted tokens are distributed exactly as plain sampling from
+the target.
 """
 from __future__ import annotations
 
+import zlib
 from typing import List, Optional, Sequence, Tuple
 
 import torch
@@ -51,6 +58,48 @@ def accept_greedy(draft: Sequence[int], preds: Sequence[int]) -> Tuple[List[int]
     return acc + [int(preds[len(acc)])], len(acc)
 
 
+def filtered_probs(logits: torch.Tensor, temperature: float, top_k: int, top_p: float) -> torch.Tensor:
+    """Sampling distribution of logits rows [n, V] under temperature / top-k / top-p
+    (top-k first, then the smallest top-p nucleus of what is left), fp32."""
+    z = logits.float() / max(float(temperature), 1e-6)
+    V = z.shape[-1]
+    if 0 < top_k < V:
+        thr = torch.topk(z, top_k, dim=-1).values[..., -1:]
+        z = z.masked_fill(z < thr, float("-inf"))
+    p = torch.softmax(z, dim=-1)
+    if top_p < 1.0:
+        sp, si = torch.sort(p, dim=-1, descending=True)
+        keep = (torch.cumsum(sp, dim=-1) - sp) < top_p
+        mask = torch.zeros_like(keep).scatter(-1, si, keep)
+        p = torch.where(mask, p, torch.zeros_like(p))
+        p = p / p.sum(-1, keepdim=True)
+    return p
+
+
+def accept_sampled(draft: Sequence[int], probs: torch.Tensor, gen: torch.Generator) -> Tuple[List[int], int]:
+    """Speculative sampling with a deterministic draft: probs [len(draft) + 1, V] are the
+    target's distributions at the draft positions and after the last draft.  Returns
+    (kept drafts + one sampled token, number of kept drafts)."""
+    probs = probs.float().cpu()
+    out: List[int] = []
+    for i, d in enumerate(draft):
+        pi = probs[i]
+        u = float(torch.rand((), generator=gen))
+        if u < float(pi[int(d)]):
+            out.append(int(d))
+            continue
+        residual = pi.clone()
+        residual[int(d)] = 0.0
+        tot = float(residual.sum())
+        if tot <= 0.0:          # p_i was a point mass on d: unreachable after a rejection
+            out.append(int(d))
+            continue
+        out.append(int(torch.multinomial(residual / tot, 1, generator=gen)))
+        return out, i
+    out.append(int(torch.multinomial(probs[len(draft)], 1, generator=gen)))
+    return out, len(draft)
+
+
 class SpecStats:
     def __init__(self):
         self.proposed = 0
@@ -76,7 +125,7 @@ def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: S
         room = min(r.params.max_tokens - len(r.output_ids) - 1, engine.max_model_len - len(seq) - 1)
         if drafts is not None:
             d = list(drafts[i])
-        elif r.params.greedy and num_draft > 0:
+        elif num_draft > 0:
             d = find_draft(seq, ngram, num_draft)
         else:
             d = []
@@ -94,12 +143,12 @@ def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: S
         preds = ops.argmax(logits).cpu().tolist()
     else:
         preds = torch.argmax(logits.float(), -1).tolist()
-    # non-greedy requests (fed one token, no draft) draw their token with their own
-    # temperature / top-k / top-p from the logits of that position
+    # non-greedy requests without a draft draw their token with their own temperature /
+    # top-k / top-p from the logits of that position (the sampling kernel)
     rows, samp = [], []
     off = 0
     for r, feed in zip(active, feeds):
-        if not r.params.greedy:
+        if not r.params.greedy and len(feed) == 1:
             rows.append(off)
             samp.append(r)
         off += len(feed)
@@ -121,9 +170,14 @@ def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: S
         off += len(feed)
         if r.params.greedy:
             toks, na = accept_greedy(d, p)
-        else:
-            # non-greedy: take the sampled token for the first position only
+        elif not d:
             toks, na = [int(p[0])], 0
+        else:
+            pr = filtered_probs(logits[off - len(feed):off], r.params.temperature, r.params.top_k, r.params.top_p)
+            # seeded from (runner seed, request, position): the same on every rank
+            gen = torch.Generator().manual_seed((runner.seed * 1000003 + zlib.crc32(str(r.request_id).encode()) * 7919
+                                                 + len(r.output_ids)) & 0x7FFFFFFFFFFFFFFF)
+            toks, na = accept_sampled(d, pr, gen)
         stats.proposed += len(d)
         stats.accepted += na
         kv.truncate(r.request_id, start + 1 + na)
