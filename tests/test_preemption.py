@@ -40,3 +40,23 @@ def test_sequence_larger_than_pool_ends_instead_of_failing():
               max_model_len=160, kv_pages=3)
     r = llm.generate([[1, 2, 3, 4, 5]], SamplingParams(max_tokens=100))[0]
     assert r.finished and r.finish_reason == "length" and 0 < len(r.output_ids) < 100
+
+
+def test_speculation_with_a_small_pool():
+    """Prompt-lookup speculation on a pool too small for every verify step: drafts are
+    skipped when their pages are missing, preemption makes room, and the greedy tokens
+    equal those of an unconstrained engine."""
+    cfg = PRESETS["tiny-qwen2"]
+    outs = []
+    for pages in (96, 9):
+        w = random_weights(cfg, device="cpu", dtype=torch.float32, seed=0)   # repetitive output: drafts hit
+        llm = LLM(cfg, device="cpu", dtype=torch.float32, kv_cache_dtype="fp32", weights=w, max_batch=4,
+                  max_model_len=200, kv_pages=pages, spec_num_draft=6, spec_ngram=2)
+        g = torch.Generator().manual_seed(5)
+        prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (30, 20, 12)]
+        reqs = llm.generate(prompts, SamplingParams(max_tokens=40))
+        outs.append([r.output_ids for r in reqs])
+        assert llm.engine.spec_stats.proposed > 0
+        if pages == 9:
+            assert llm.engine.stats["preempted"] > 0
+    assert outs[0] == outs[1]

@@ -286,6 +286,9 @@ class LLMEngine:
                 active = [r for r in active if not r.finished]
                 drafts = [find_draft(r.prompt_ids + r.output_ids, self.spec_ngram, self.spec_num_draft)
                           for r in active]
+                if not self._pages_for_verify(active, drafts):
+                    drafts = []          # not enough KV pages: plain decode (with preemption)
+            if drafts and any(drafts):
                 outs = speculative_decode_step(self, active, self.spec_ngram, self.spec_num_draft, self.spec_stats,
                                                drafts=drafts)
                 for r, toks in zip(active, outs):
@@ -297,6 +300,7 @@ class LLMEngine:
                             break
                 return
             # nothing to draft: an ordinary (graph-replayed) decode step
+            active = [r for r in active if not r.finished]
         pend = self._pending
         if pend is not None and active and self._can_chain(pend[0], active):
             # launch step n+1 on the device-resident tokens of step n, then read step n
@@ -315,6 +319,18 @@ class LLMEngine:
             self._pending = (active, handle)
         else:
             self._consume(active, handle, done)
+
+    def _pages_for_verify(self, active: List[Request], drafts) -> bool:
+        """Whether the pool has the pages a verify step (last token + drafts per
+        sequence) needs; the lending pool, when present, supplies overflow pages."""
+        if getattr(self.kv, "_overflow", None) is not None:
+            return True
+        ps = self.kv.page_size
+        need = 0
+        for r, d in zip(active, drafts):
+            n0 = self.kv.seq_len(r.request_id)
+            need += -(-(n0 + 1 + len(d)) // ps) - (-(-n0 // ps))
+        return need <= self.kv.num_free_pages()
 
     def _ensure_pages(self, active: List[Request], done: List[Request]) -> List[Request]:
         """Recompute preemption: when the pool cannot give every sequence of this decode
