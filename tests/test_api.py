@@ -89,3 +89,30 @@ def test_hmac_signing():
     ts, sig = sign_request("s3", "POST", "/v1/completions", b"{}")
     assert verify_signature("s3", "POST", "/v1/completions", b"{}", ts, sig)
     assert not verify_signature("s3", "POST", "/v1/completions", b"{1}", ts, sig)
+
+
+def test_stop_strings_and_n(client):
+    """OpenAI `stop` (text cut before the first stop string, finish_reason "stop") and
+    `n` independent choices; streaming ends before a stop string too."""
+    base = client.post("/v1/completions", json={"prompt": "hello world", "max_tokens": 12}).json()
+    full = base["choices"][0]["text"]
+    assert len(full) > 4
+    stop = full[2:4]
+    r = client.post("/v1/completions", json={"prompt": "hello world", "max_tokens": 12, "stop": [stop]}).json()
+    c = r["choices"][0]
+    assert c["finish_reason"] == "stop" and stop not in c["text"] and full.startswith(c["text"])
+    r = client.post("/v1/completions", json={"prompt": "hello world", "max_tokens": 6, "n": 3,
+                                              "temperature": 0.9}).json()
+    assert [c["index"] for c in r["choices"]] == [0, 1, 2]
+    assert 3 <= r["usage"]["completion_tokens"] <= 18
+    body = {"prompt": "hello world", "max_tokens": 12, "stream": True, "stop": stop}
+    with client.stream("POST", "/v1/completions", json=body) as s:
+        text = "".join(json.loads(line[6:])["choices"][0]["text"] for line in s.iter_lines()
+                       if line.startswith("data: {"))
+    assert stop not in text and full.startswith(text)
+    assert client.post("/v1/completions", json={"prompt": "x", "stop": ["a"] * 5}).status_code == 400
+    assert client.post("/v1/completions", json={"prompt": "x", "n": 9}).status_code == 400
+    assert client.post("/v1/completions", json={"prompt": "x", "n": 2, "stream": True}).status_code == 400
+    chat = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                     "max_tokens": 5, "n": 2}).json()
+    assert len(chat["choices"]) == 2

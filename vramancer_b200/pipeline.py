@@ -41,6 +41,16 @@ from .utils.observability import METRICS, RequestHistory, get_logger, span
 log = get_logger("vramancer.pipeline")
 
 
+def stop_index(text: str, stop: Optional[Sequence[str]]) -> int:
+    """Index of the earliest occurrence of any stop string in text, or -1."""
+    best = -1
+    for st in stop or ():
+        i = text.find(st)
+        if i >= 0 and (best < 0 or i < best):
+            best = i
+    return best
+
+
 class InferencePipeline:
     def __init__(self, backend_name: str = "auto", enable_metrics: bool = True, enable_discovery: bool = False,
                  verbose: bool = False):
@@ -241,10 +251,15 @@ class InferencePipeline:
         return out_ids if return_ids else self.tokenizer.decode(out_ids)
 
     def generate_stream(self, prompt: Union[str, Sequence[int]], max_new_tokens: int = 128, temperature: float = 0.0,
-                        top_p: float = 1.0, top_k: int = 0, **kw) -> Iterator[str]:
+                        top_p: float = 1.0, top_k: int = 0, stop: Optional[Sequence[str]] = None,
+                        **kw) -> Iterator[str]:
+        """Text deltas as tokens arrive.  With `stop` strings the stream ends before the
+        first one and the request is aborted (no further tokens are computed)."""
         q: "queue.Queue" = queue.Queue()
+        holder = {}
 
         def on_tok(req, tok):
+            holder["id"] = req.request_id
             q.put(tok)
 
         fut = self.submit(prompt, max_new_tokens, temperature, top_p, top_k, on_token=on_tok, **kw)
@@ -259,10 +274,39 @@ class InferencePipeline:
                 continue
             ids.append(tok)
             text = self.tokenizer.decode(ids)
+            cut = stop_index(text, stop) if stop else -1
+            if cut >= 0:
+                if cut > len(prev):
+                    yield text[len(prev):cut]
+                self.abort(holder.get("id"))
+                break
             if len(text) > len(prev):
                 yield text[len(prev):]
                 prev = text
         fut.result()
+
+    def abort(self, request_id) -> bool:
+        """Ends a request early (its tokens so far stay in its result)."""
+        if request_id is None or self.engine is None:
+            return False
+        if self._bcast is not None:
+            with self._wake:
+                self._events.append(("abort", request_id))
+        return self.engine.abort(request_id)
+
+    def stop_watcher(self, stop: Sequence[str]):
+        """on_token callback that aborts a request once its text contains a stop string
+        (single-process serving; under tensor parallelism the text is cut afterwards)."""
+        if not stop or self._bcast is not None:
+            return None
+        ids: List[int] = []
+
+        def on_tok(req, tok):
+            ids.append(tok)
+            tail = ids if len(ids) <= 256 else ids[-64:]
+            if stop_index(self.tokenizer.decode(tail), stop) >= 0:
+                self.engine.abort(req.request_id)
+        return on_tok
 
     def infer(self, input_ids: Union[torch.Tensor, Sequence[int]]) -> torch.Tensor:
         """Last-position logits of one sequence (no generation)."""

@@ -152,6 +152,14 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
             queue.release()
             METRICS.circuit_state.set(breaker.code())
 
+    def _finish_text(text: str, reason: Optional[str], stops) -> tuple:
+        """Text cut before the first stop string (finish_reason "stop"), else as produced."""
+        from ..pipeline import stop_index
+        cut = stop_index(text, stops)
+        if cut >= 0:
+            return text[:cut], "stop"
+        return text, ("stop" if reason in (None, "abort") else reason)
+
     def context_check(p, n_prompt: int, max_new: int):
         limit = p.engine.max_model_len
         if n_prompt + 1 > limit:
@@ -197,9 +205,13 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
             return _err(400, str(e), code="context_length_exceeded")
         rid = f"cmpl-{uuid.uuid4().hex[:24]}"
         created = int(time.time())
+        stops, n_choices = params.pop("stop"), params.pop("n")
         if body.get("stream"):
+            if n_choices > 1:
+                return _err(400, "n > 1 is not supported with stream")
+
             def gen():
-                for delta in p.generate_stream(prompt, **params):
+                for delta in p.generate_stream(prompt, stop=stops, **params):
                     yield {"id": rid, "object": "text_completion", "created": created, "model": alias(),
                            "choices": [{"index": 0, "text": delta, "finish_reason": None}]}
                 yield {"id": rid, "object": "text_completion", "created": created, "model": alias(),
@@ -208,18 +220,20 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
 
         def work(pp):
             t0 = time.perf_counter()
-            fut = pp.submit(prompt, **params)
-            req = fut.result()
-            text = pp.tokenizer.decode(req.output_ids)
+            futs = [pp.submit(prompt, on_token=pp.stop_watcher(stops), **params) for _ in range(n_choices)]
+            reqs = [f.result() for f in futs]
+            choices = []
+            for i, req in enumerate(reqs):
+                text, finish = _finish_text(pp.tokenizer.decode(req.output_ids), req.finish_reason, stops)
+                choices.append({"index": i, "text": text, "finish_reason": finish, "logprobs": None})
             dt = time.perf_counter() - t0
-            pp.history.record("completions", alias(), n_prompt, len(req.output_ids), dt, req.ttft)
+            n_out = sum(len(r.output_ids) for r in reqs)
+            pp.history.record("completions", alias(), n_prompt, n_out, dt, reqs[0].ttft)
             return {"id": rid, "object": "text_completion", "created": created, "model": alias(),
-                    "choices": [{"index": 0, "text": text, "finish_reason": req.finish_reason or "stop",
-                                 "logprobs": None}],
-                    "usage": {"prompt_tokens": n_prompt, "completion_tokens": len(req.output_ids),
-                              "total_tokens": n_prompt + len(req.output_ids)},
-                    "timing": {"total_s": dt, "ttft_s": req.ttft,
-                               "tok_s": len(req.output_ids) / dt if dt > 0 else 0.0}}
+                    "choices": choices,
+                    "usage": {"prompt_tokens": n_prompt, "completion_tokens": n_out,
+                              "total_tokens": n_prompt + n_out},
+                    "timing": {"total_s": dt, "ttft_s": reqs[0].ttft, "tok_s": n_out / dt if dt > 0 else 0.0}}
         return await asyncio.get_running_loop().run_in_executor(
             None, lambda: run_guarded(work, float(flags.VRM_REQUEST_TIMEOUT)))
 
@@ -245,11 +259,15 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
             return _err(400, str(e), code="context_length_exceeded")
         rid = f"chatcmpl-{uuid.uuid4().hex[:24]}"
         created = int(time.time())
+        stops, n_choices = params.pop("stop"), params.pop("n")
         if body.get("stream"):
+            if n_choices > 1:
+                return _err(400, "n > 1 is not supported with stream")
+
             def gen():
                 yield {"id": rid, "object": "chat.completion.chunk", "created": created, "model": alias(),
                        "choices": [{"index": 0, "delta": {"role": "assistant"}, "finish_reason": None}]}
-                for delta in p.generate_stream(prompt, **params):
+                for delta in p.generate_stream(prompt, stop=stops, **params):
                     yield {"id": rid, "object": "chat.completion.chunk", "created": created, "model": alias(),
                            "choices": [{"index": 0, "delta": {"content": delta}, "finish_reason": None}]}
                 yield {"id": rid, "object": "chat.completion.chunk", "created": created, "model": alias(),
@@ -258,17 +276,21 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
 
         def work(pp):
             t0 = time.perf_counter()
-            req = pp.submit(prompt, **params).result()
-            text = pp.tokenizer.decode(req.output_ids)
-            msg, finish = build_chat_message(text)
-            if finish != "tool_calls":
-                finish = req.finish_reason or "stop"
+            futs = [pp.submit(prompt, on_token=pp.stop_watcher(stops), **params) for _ in range(n_choices)]
+            reqs = [f.result() for f in futs]
+            choices = []
+            for i, req in enumerate(reqs):
+                text, finish = _finish_text(pp.tokenizer.decode(req.output_ids), req.finish_reason, stops)
+                msg, tool_finish = build_chat_message(text)
+                choices.append({"index": i, "message": msg,
+                                "finish_reason": "tool_calls" if tool_finish == "tool_calls" else finish})
             dt = time.perf_counter() - t0
-            pp.history.record("chat", alias(), n_prompt, len(req.output_ids), dt, req.ttft)
+            n_out = sum(len(r.output_ids) for r in reqs)
+            pp.history.record("chat", alias(), n_prompt, n_out, dt, reqs[0].ttft)
             return {"id": rid, "object": "chat.completion", "created": created, "model": alias(),
-                    "choices": [{"index": 0, "message": msg, "finish_reason": finish}],
-                    "usage": {"prompt_tokens": n_prompt, "completion_tokens": len(req.output_ids),
-                              "total_tokens": n_prompt + len(req.output_ids)}}
+                    "choices": choices,
+                    "usage": {"prompt_tokens": n_prompt, "completion_tokens": n_out,
+                              "total_tokens": n_prompt + n_out}}
         return await asyncio.get_running_loop().run_in_executor(
             None, lambda: run_guarded(work, float(flags.VRM_REQUEST_TIMEOUT)))
 
@@ -283,12 +305,17 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
         except ValidationError as e:
             return _err(400, str(e))
 
+        stops = params.pop("stop")
+        params.pop("n")
+
         def work(pp):
-            futs = [pp.submit(x, **params) for x in prompts]
+            futs = [pp.submit(x, on_token=pp.stop_watcher(stops), **params) for x in prompts]
             reqs = [f.result() for f in futs]
-            return {"object": "batch.completion", "model": alias(),
-                    "choices": [{"index": i, "text": pp.tokenizer.decode(r.output_ids),
-                                 "finish_reason": r.finish_reason} for i, r in enumerate(reqs)]}
+            choices = []
+            for i, r in enumerate(reqs):
+                text, finish = _finish_text(pp.tokenizer.decode(r.output_ids), r.finish_reason, stops)
+                choices.append({"index": i, "text": text, "finish_reason": finish})
+            return {"object": "batch.completion", "model": alias(), "choices": choices}
         return await asyncio.get_running_loop().run_in_executor(
             None, lambda: run_guarded(work, float(flags.VRM_REQUEST_TIMEOUT)))
 

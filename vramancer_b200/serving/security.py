@@ -51,6 +51,23 @@ def validate_generation_params(body: Dict[str, Any], max_tokens_cap: int = 32768
     if k < 0:
         raise ValidationError("top_k must be >= 0")
     out["top_k"] = k
+    # OpenAI "stop": up to 4 non-empty strings; "n": independent completions per prompt
+    stop = body.get("stop")
+    if stop is None:
+        stop = []
+    elif isinstance(stop, str):
+        stop = [stop]
+    if not isinstance(stop, list) or len(stop) > 4 or not all(isinstance(x, str) and x for x in stop):
+        raise ValidationError("stop must be a non-empty string or a list of at most 4")
+    out["stop"] = stop
+    n = body.get("n", 1)
+    try:
+        n = int(1 if n is None else n)
+    except (TypeError, ValueError):
+        raise ValidationError("n must be an integer")
+    if not (1 <= n <= 8):
+        raise ValidationError("n must be in [1, 8]")
+    out["n"] = n
     return out
 
 
