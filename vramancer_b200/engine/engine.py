@@ -60,6 +60,7 @@ class Request:
     num_computed: int = 0          # tokens of prefill_ids whose KV is written
     cached_tokens: int = 0
     resumed: bool = False          # preempted after producing tokens: re-prefill, then keep decoding
+    retries: int = 0               # re-runs after failed engine steps
     finished: bool = False
     finish_reason: Optional[str] = None
     arrival: float = field(default_factory=time.perf_counter)
@@ -130,6 +131,34 @@ class LLMEngine:
         with self._lock:
             self.waiting.append(req)
         return req
+
+    def recover(self, max_retries: int = 2) -> List[Request]:
+        """After a failed step: the running requests give their KV pages back and wait
+        again at the front of the queue; on re-admission they prefill their prompt and
+        the tokens they already have, then continue (request-level resume).  A request
+        that already failed `max_retries` times is returned instead (out of the running
+        set, pages freed, not yet finished: the caller reports the error and finishes it
+        with reason "error")."""
+        with self._lock:
+            self._pending = None               # the in-flight step's tokens are lost
+            failed: List[Request] = []
+            back: List[Request] = []
+            for r in list(self.running):
+                if r.finished:
+                    continue
+                self.running.remove(r)
+                self.kv.free(r.request_id)
+                r.retries += 1
+                if r.retries > max_retries:
+                    failed.append(r)
+                    continue
+                r.num_computed = 0
+                r.cached_tokens = 0
+                r.resumed = bool(r.output_ids)
+                back.append(r)
+            for r in reversed(back):
+                self.waiting.appendleft(r)
+            return failed
 
     def flush(self) -> List[Request]:
         """Reads the decode step still in flight (overlapped decode), emitting its

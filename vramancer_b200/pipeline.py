@@ -184,11 +184,17 @@ class InferencePipeline:
                     dev = str(getattr(eng.runner, "device", "cpu"))
                     METRICS.kv_free_pages.labels(dev).set(free)
                     METRICS.kv_used_pages.labels(dev).set(eng.kv.num_pages - free)
-            except Exception as e:   # fail the running requests, keep serving
+            except Exception as e:   # resume the running requests (bounded), keep serving
                 log.error("engine step failed: %s", e)
                 if self.fault is not None and self.fault.states:
                     self.fault.handle_fault(0, e)
-                for r in list(eng.running) + list(eng.waiting):
+                if self._bcast is None:
+                    # request-level resume: re-prefill from token ids, at most twice each
+                    failed = eng.recover(max_retries=2)
+                else:
+                    # tensor-parallel ranks would have to agree on the recovery: fail fast
+                    failed = [r for r in list(eng.running) + list(eng.waiting) if not r.finished]
+                for r in failed:
                     if r.future is not None and not r.future.done():
                         r.future.set_exception(e)
                     eng._finish(r, "error")
