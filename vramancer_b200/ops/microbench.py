@@ -311,6 +311,36 @@ def bench_act_quant(tokens, hidden=5120, iters=50):
             "nvfp4_us": round(t4, 2), "nvfp4_frac_hbm": round(b4 / t4 / 1e6 / hbm, 3), "peaks": src}
 
 
+def bench_fp8(m, n, k, iters=50):
+    """FP8 W8A8 GEMM (per-channel weight scales, per-token activation scales, activation
+    quantisation included) against the bf16 GEMM on the same shape; weights rotated past
+    L2."""
+    from ..quant import fp8 as f8
+    hbm, tflops, src = peaks()
+    copies = max(1, math.ceil(3 * 126e6 / (n * k)))
+    ws = [(torch.randn(n, k, device="cuda") * 0.02).bfloat16() for _ in range(copies)]
+    qs = [f8.quantize(w) for w in ws]
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    st = [0, 0]
+
+    def f():
+        linear(x, qs[st[0] % copies])
+        st[0] += 1
+
+    def b():
+        linear(x, ws[st[1] % copies])
+        st[1] += 1
+
+    t8 = time_it(f, iters)
+    t16 = time_it(b, iters)
+    flop = 2.0 * m * n * k
+    wb8, wb16 = n * k, 2 * n * k
+    return {"kernel": "fp8_w8a8_gemm", "m": m, "n": n, "k": k, "fp8_us": round(t8, 2), "bf16_us": round(t16, 2),
+            "speedup": round(t16 / t8, 3), "fp8_weight_tb_s": round(wb8 / t8 / 1e6, 3),
+            "fp8_frac_hbm": round(wb8 / t8 / 1e6 / hbm, 3), "fp8_tflops": round(flop / t8 / 1e6, 1),
+            "bf16_frac_hbm": round(wb16 / t16 / 1e6 / hbm, 3), "peaks": src}
+
+
 def trace_gemm(m, n, k):
     """Per-CTA timelines of two back-to-back stream-K decode GEMM launches on cold
     weights (us from the first launch's earliest CTA entry)."""
@@ -346,7 +376,7 @@ QWEN14B_DECODE = [("qkv", 7168, 5120), ("o_proj", 5120, 5120), ("gate_up", 27648
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "nvfp4", "nvfp4-prefill", "decode-attn", "all", "trace", "rmsnorm",
+    ap.add_argument("what", choices=["gemm", "nvfp4", "nvfp4-prefill", "fp8", "decode-attn", "all", "trace", "rmsnorm",
                                      "rope-kv", "prefill-attn", "sample", "turboquant", "act-quant", "others"])
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--seq", type=int, default=2048)
@@ -387,6 +417,12 @@ def main(argv=None):
             print(json.dumps(bench_nvfp4_prefill(a.m if a.m != 1 else 4096, n, k, a.iters)))
     elif a.what == "decode-attn":
         print(json.dumps(bench_decode_attn(a.batch, a.ctx, fp8=a.fp8, iters=a.iters)))
+    elif a.what == "fp8":
+        for m in ((a.m,) if a.m != 1 else (1, 32, 4096)):
+            for name, n, k in QWEN14B_DECODE[:4]:
+                r = bench_fp8(m, n, k, a.iters if m < 1024 else 10)
+                r["name"] = name
+                print(json.dumps(r))
     elif a.what == "rmsnorm":
         print(json.dumps(bench_rmsnorm(a.tokens or a.batch, iters=a.iters)))
     elif a.what == "rope-kv":
