@@ -32,3 +32,11 @@ def test_prefill_and_decode_drivers():
     rows = _run(["decode", "--model", "tiny-gpt2", "--batches", "1,3", "--prompt-len", "12", "--steps", "3",
                  "--warmup", "1"])
     assert [x["batch"] for x in rows] == [1, 3] and all(x["tok_s"] > 0 for x in rows)
+
+
+def test_cli_benchmark_workload(capsys):
+    from vramancer_b200 import cli
+    assert cli.main(["benchmark", "--workload", "decode", "--model", "tiny-qwen2", "--", "--batches", "2",
+                     "--prompt-len", "8", "--steps", "2", "--warmup", "1"]) == 0
+    out = capsys.readouterr().out
+    assert '"workload": "decode"' in out and '"batch": 2' in out

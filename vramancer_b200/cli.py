@@ -75,9 +75,12 @@ def build_parser() -> argparse.ArgumentParser:
     g.add_argument("--num-layers", type=int, default=None, help=argparse.SUPPRESS)
 
     sub.add_parser("status", help="GPUs, kernels and configuration")
-    b = sub.add_parser("benchmark", help="kernel microbenchmarks or a model benchmark")
+    b = sub.add_parser("benchmark", help="kernel microbenchmarks, a model benchmark or a serving workload")
     b.add_argument("--size", type=int, default=4096)
     b.add_argument("--model", default=None)
+    b.add_argument("--workload", default=None, choices=["serve", "spec", "prefill", "decode"],
+                   help="run a serving workload (vramancer_b200.workloads) on --model; extra options after --")
+    b.add_argument("rest", nargs=argparse.REMAINDER)
     d = sub.add_parser("discover", help="listen for nodes announcing themselves")
     d.add_argument("--timeout", type=float, default=5.0)
     sp = sub.add_parser("split", help="show the layer split across GPUs")
@@ -239,6 +242,11 @@ def main(argv: Optional[List[str]] = None) -> int:
         _print(st)
         return 0
     if cmd == "benchmark":
+        if a.workload:
+            from . import workloads
+            extra = [x for x in a.rest if x != "--"]
+            workloads.main([a.workload] + (["--model", a.model] if a.model else []) + extra)
+            return 0
         if a.model:
             from .pipeline import InferencePipeline
             pipe = InferencePipeline().load(a.model)
