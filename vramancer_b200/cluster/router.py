@@ -2,9 +2,10 @@
 gateway that spreads whole requests over several `vramancer serve` nodes.
 
 `ClusterRouter` spawns workers (each pins one GPU through CUDA_VISIBLE_DEVICES and
-loads its own InferencePipeline), feeds them from a shared queue (work stealing: an
-idle worker takes the next request), demultiplexes results by request id in a
-collector thread and restarts workers that die.  `Gateway` forwards to the
+loads its own InferencePipeline), sends each request to the live worker with the
+fewest outstanding requests over that worker's pipe, demultiplexes results by request
+id in a collector thread and restarts workers that die (the requests a dead worker
+held go to the others again, once by default).  `Gateway` forwards to the
 least-loaded healthy node of a node list (health loop on /health, load from
 /api/queue/status).
 
@@ -25,94 +26,192 @@ from concurrent.futures import Future
 from typing import Dict, List, Optional, Sequence
 
 
-def _worker_main(gpu: Optional[int], model: str, load_kw: Dict, inq, outq, ready) -> None:
+def _worker_main(slot: int, gpu: Optional[int], model: str, load_kw: Dict, conn) -> None:
     if gpu is not None:
         os.environ["CUDA_VISIBLE_DEVICES"] = str(gpu)
     from ..pipeline import InferencePipeline
     pipe = InferencePipeline(enable_metrics=False).load(model, **load_kw)
-    ready.put(gpu)
+    conn.send(("ready", slot))
     while True:
-        item = inq.get()
+        try:
+            item = conn.recv()
+        except (EOFError, OSError):
+            break
         if item is None:
             break
         rid, prompt, kw = item
         try:
             text = pipe.generate(prompt, **kw)
-            outq.put((rid, True, text, gpu))
+            conn.send(("done", rid, True, text))
         except Exception as e:  # noqa: BLE001
-            outq.put((rid, False, repr(e), gpu))
+            conn.send(("done", rid, False, repr(e)))
     pipe.shutdown()
 
 
 class ClusterRouter:
+    """Worker processes with one duplex pipe each.  A shared multiprocessing queue is
+    not used on purpose: a worker killed while it blocks in get() keeps the queue's
+    reader lock and every other worker stalls behind it; a pipe only affects its own
+    worker (EOF).  Requests go to the live worker with the fewest assigned requests;
+    the requests assigned to a worker that dies go to the others again (up to
+    max_retries times each, then their futures fail)."""
+
     def __init__(self, model: str, gpus: Sequence[Optional[int]], load_kw: Optional[Dict] = None,
-                 start_method: str = "spawn", monitor_interval_s: float = 2.0):
+                 start_method: str = "spawn", monitor_interval_s: float = 2.0, max_retries: int = 1):
         self.model = model
         self.gpus = list(gpus)
         self.load_kw = load_kw or {}
         self.ctx = mp.get_context(start_method)
-        self.inq = self.ctx.Queue()
-        self.outq = self.ctx.Queue()
-        self.ready = self.ctx.Queue()
         self.procs: Dict[int, mp.Process] = {}
+        self.conns: Dict[int, object] = {}
+        self.ready_slots: set = set()
         self.pending: Dict[str, Future] = {}
-        self.served: Dict[Optional[int], int] = {g: 0 for g in self.gpus}
+        self.requests: Dict[str, list] = {}     # rid -> [prompt, kw, attempts]
+        self.assigned: Dict[int, List[str]] = {i: [] for i in range(len(self.gpus))}
+        self.backlog: List[str] = []            # requests waiting for a live worker
+        self.served: Dict[int, int] = {i: 0 for i in range(len(self.gpus))}
         self.restarts = 0
+        self.resubmitted = 0
+        self.max_retries = max_retries
         self._stop = threading.Event()
-        self._lock = threading.Lock()
+        self._lock = threading.RLock()
         self.monitor_interval = monitor_interval_s
 
+    # kept for code that looks at the request a worker is on
+    @property
+    def inflight(self) -> Dict[int, str]:
+        with self._lock:
+            return {s: rids[0] for s, rids in self.assigned.items() if rids}
+
     def _spawn(self, slot: int) -> None:
-        p = self.ctx.Process(target=_worker_main, args=(self.gpus[slot], self.model, self.load_kw, self.inq,
-                                                        self.outq, self.ready), daemon=True)
+        parent, child = self.ctx.Pipe(duplex=True)
+        p = self.ctx.Process(target=_worker_main, args=(slot, self.gpus[slot], self.model, self.load_kw, child),
+                             daemon=True)
         p.start()
-        self.procs[slot] = p
+        child.close()
+        with self._lock:
+            self.procs[slot] = p
+            self.conns[slot] = parent
+            self.ready_slots.discard(slot)
 
     def start(self, wait_ready: bool = True, timeout: float = 600.0) -> "ClusterRouter":
         for i in range(len(self.gpus)):
             self._spawn(i)
-        if wait_ready:
-            for _ in self.gpus:
-                self.ready.get(timeout=timeout)
         threading.Thread(target=self._collect, name="vrm-cluster-collect", daemon=True).start()
         threading.Thread(target=self._monitor, name="vrm-cluster-monitor", daemon=True).start()
+        if wait_ready:
+            t0 = time.time()
+            while len(self.ready_slots) < len(self.gpus):
+                if time.time() - t0 > timeout:
+                    raise TimeoutError("cluster workers did not come up")
+                time.sleep(0.05)
         return self
 
+    def _dispatch(self, rid: str) -> None:
+        """Sends a request to the live, ready worker with the fewest assigned requests
+        (or parks it until one is ready).  Caller holds the lock."""
+        live = [s for s in self.ready_slots if self.procs.get(s) is not None and self.procs[s].is_alive()]
+        if not live:
+            self.backlog.append(rid)
+            return
+        slot = min(live, key=lambda s: len(self.assigned[s]))
+        prompt, kw, _ = self.requests[rid]
+        try:
+            self.conns[slot].send((rid, prompt, kw))
+            self.assigned[slot].append(rid)
+        except (OSError, EOFError, BrokenPipeError):
+            self.backlog.append(rid)             # the monitor restarts that worker
+
     def _collect(self) -> None:
+        from multiprocessing.connection import wait
         while not self._stop.is_set():
-            try:
-                rid, ok, payload, gpu = self.outq.get(timeout=0.2)
-            except queue.Empty:
-                continue
             with self._lock:
-                fut = self.pending.pop(rid, None)
-                self.served[gpu] = self.served.get(gpu, 0) + 1
-            if fut is not None:
-                fut.set_result(payload) if ok else fut.set_exception(RuntimeError(payload))
+                conns = {c: s for s, c in self.conns.items()}
+            if not conns:
+                time.sleep(0.05)
+                continue
+            for c in wait(list(conns), timeout=0.2):
+                slot = conns[c]
+                try:
+                    msg = c.recv()
+                except (EOFError, OSError):
+                    with self._lock:
+                        if self.conns.get(slot) is c:
+                            self.ready_slots.discard(slot)
+                    continue
+                if msg[0] == "ready":
+                    with self._lock:
+                        self.ready_slots.add(slot)
+                        parked, self.backlog = self.backlog, []
+                        for rid in parked:
+                            self._dispatch(rid)
+                    continue
+                _, rid, ok, payload = msg
+                with self._lock:
+                    if rid in self.assigned[slot]:
+                        self.assigned[slot].remove(rid)
+                    fut = self.pending.pop(rid, None)
+                    self.requests.pop(rid, None)
+                    self.served[slot] = self.served.get(slot, 0) + 1
+                if fut is not None:
+                    fut.set_result(payload) if ok else fut.set_exception(RuntimeError(payload))
 
     def _monitor(self) -> None:
         while not self._stop.wait(self.monitor_interval):
-            for slot, p in list(self.procs.items()):
-                if not p.is_alive():
-                    self.restarts += 1
-                    self._spawn(slot)
+            self._check_workers()
+
+    def _check_workers(self) -> None:
+        """Restarts dead workers and sends the requests they held elsewhere."""
+        for slot, p in list(self.procs.items()):
+            if p.is_alive():
+                continue
+            self.restarts += 1
+            with self._lock:
+                self.ready_slots.discard(slot)
+                held, self.assigned[slot] = self.assigned[slot], []
+                old = self.conns.pop(slot, None)
+                for rid in held:
+                    req = self.requests.get(rid)
+                    if req is None:
+                        continue
+                    req[2] += 1
+                    if req[2] > self.max_retries:
+                        self.requests.pop(rid, None)
+                        fut = self.pending.pop(rid, None)
+                        if fut is not None:
+                            fut.set_exception(RuntimeError(f"worker {slot} died while serving the request"))
+                        continue
+                    self.resubmitted += 1
+                    self._dispatch(rid)
+            if old is not None:
+                try:
+                    old.close()
+                except OSError:
+                    pass
+            self._spawn(slot)
 
     def submit(self, prompt: str, **kw) -> Future:
         rid = uuid.uuid4().hex
         fut: Future = Future()
         with self._lock:
             self.pending[rid] = fut
-        self.inq.put((rid, prompt, kw))
+            self.requests[rid] = [prompt, kw, 0]
+            self._dispatch(rid)
         return fut
 
     def stats(self) -> Dict:
         return {"workers": len(self.procs), "alive": sum(p.is_alive() for p in self.procs.values()),
-                "served": dict(self.served), "pending": len(self.pending), "restarts": self.restarts}
+                "served": dict(self.served), "pending": len(self.pending), "restarts": self.restarts,
+                "resubmitted": self.resubmitted}
 
     def stop(self) -> None:
         self._stop.set()
-        for _ in self.procs:
-            self.inq.put(None)
+        with self._lock:
+            for c in self.conns.values():
+                try:
+                    c.send(None)
+                except (OSError, EOFError, BrokenPipeError):
+                    pass
         for p in self.procs.values():
             p.join(timeout=10)
             if p.is_alive():
