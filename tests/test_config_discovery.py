@@ -1,0 +1,71 @@
+"""Configuration (defaults -> YAML -> VRM_* environment, live flag view, validation,
+reload hooks) and node discovery (UDP announcements on localhost, static VRM_NODES,
+expiry of silent nodes)."""
+import socket
+import time
+
+from vramancer_b200.cluster import discovery
+from vramancer_b200.utils import config
+
+
+def test_flags_live_view(monkeypatch):
+    monkeypatch.delenv("VRM_MAX_BATCH_SIZE", raising=False)
+    assert config.flags.VRM_MAX_BATCH_SIZE == 64
+    monkeypatch.setenv("VRM_MAX_BATCH_SIZE", "12")
+    assert config.flags.VRM_MAX_BATCH_SIZE == 12
+    monkeypatch.setenv("VRM_MAX_BATCH_SIZE", "not-a-number")
+    assert config.flags.VRM_MAX_BATCH_SIZE == 64          # bad values fall back to the default
+    monkeypatch.setenv("VRM_CUDA_GRAPH", "off")
+    assert config.flags.VRM_CUDA_GRAPH is False
+    names = {d["name"] for d in config.flags.describe()}
+    assert {"VRM_API_TOKEN", "VRM_KV_CACHE_DTYPE", "VRM_PROMPT_LOOKUP"} <= names
+
+
+def test_yaml_then_env_then_validation_and_reload(tmp_path, monkeypatch):
+    p = tmp_path / "config.yaml"
+    p.write_text("max_batch: 7\nport: 6000\nkv_cache_dtype: fp8\ncustom_key: 3\n")
+    monkeypatch.setenv("VRM_CONFIG", str(p))
+    monkeypatch.setenv("VRM_N_CTX", "2048")
+    monkeypatch.delenv("VRM_MAX_BATCH_SIZE", raising=False)
+    seen = []
+    config.on_reload(seen.append)
+    c = config.reload_config()
+    assert (c.max_batch, c.port, c.kv_cache_dtype, c.max_model_len) == (7, 6000, "fp8", 2048)
+    assert c.extra == {"custom_key": 3} and seen and seen[-1] is c
+    monkeypatch.setenv("VRM_MAX_BATCH_SIZE", "3")        # the environment wins over the file
+    assert config.reload_config().max_batch == 3
+    assert config.get_config().validate() == []
+    bad = config.Config(port=0, gpu_memory_utilization=2.0, max_batch=0, kv_cache_dtype="int4")
+    assert len(bad.validate()) == 4
+    monkeypatch.delenv("VRM_CONFIG")
+    config.reload_config()
+
+
+def _free_udp_port():
+    s = socket.socket(socket.AF_INET, socket.SOCK_DGRAM)
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def test_discovery_over_udp_and_static_nodes(monkeypatch):
+    port = _free_udp_port()
+    d = discovery.ClusterDiscovery(port=port, bind="127.0.0.1")
+    assert d.start()
+    try:
+        assert discovery.announce("10.0.0.7", 5030, {"gpus": 8}, discovery_port=port, broadcast_addr="127.0.0.1")
+        t0 = time.time()
+        while time.time() - t0 < 5:
+            urls = {n["url"]: n for n in discovery.known_nodes()}
+            if "http://10.0.0.7:5030" in urls:
+                break
+            time.sleep(0.05)
+        assert urls["http://10.0.0.7:5030"]["gpus"] == 8
+    finally:
+        d.stop()
+    monkeypatch.setenv("VRM_NODES", "http://static-a:5030, http://static-b:5030")
+    discovery.register_node("http://old:5030")
+    discovery._nodes["http://old:5030"]["last_seen"] -= 100
+    urls = {n["url"] for n in discovery.known_nodes(ttl_s=30)}
+    assert {"http://static-a:5030", "http://static-b:5030"} <= urls and "http://old:5030" not in urls
