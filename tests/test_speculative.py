@@ -120,3 +120,32 @@ def test_prompt_lookup_with_sampled_requests_runs_and_drafts():
     reqs = llm.generate([span * 4, span * 3], SamplingParams(max_tokens=24, temperature=0.7, top_k=20))
     assert all(len(r.output_ids) == 24 for r in reqs)
     assert llm.engine.spec_stats.proposed > 0
+
+
+def test_sampled_draft_rejection_sampling_keeps_the_target_distribution():
+    """Drafts drawn from q, kept with min(1, p/q), residual norm(max(0, p - q)): the
+    first emitted token follows p."""
+    from vramancer_b200.engine.speculative import accept_with_draft_probs
+    p = torch.tensor([0.5, 0.3, 0.15, 0.05])
+    q = torch.tensor([0.1, 0.2, 0.3, 0.4])
+    probs = torch.stack([p, torch.tensor([0.25] * 4)])
+    gen = torch.Generator().manual_seed(1)
+    counts = torch.zeros(4)
+    N = 20000
+    for _ in range(N):
+        d = int(torch.multinomial(q, 1, generator=gen))
+        toks, _ = accept_with_draft_probs([d], probs, q.view(1, 4), gen)
+        counts[toks[0]] += 1
+    assert (counts / N - p).abs().max() < 0.015, counts / N
+
+
+def test_draft_model_sampling_with_an_identical_draft_accepts_everything():
+    from vramancer_b200.engine.speculative import DraftModelDecoder
+    g = torch.Generator().manual_seed(9)
+    p = torch.randint(0, 512, (10,), generator=g).tolist()
+    target, _ = _llm()
+    drafter, _ = _llm()
+    dec = DraftModelDecoder(target, drafter, gamma=4, adaptive=False)
+    out = dec.generate(p, 20, params=SamplingParams(max_tokens=20, temperature=0.8, top_k=40), seed=3)
+    assert len(out) == 20
+    assert dec.stats.proposed > 0 and dec.stats.acceptance > 0.9

@@ -19,7 +19,9 @@ with probability p_i(d_i), where p_i is the target's filtered distribution
 (temperature, top-k, top-p) at that position; at the first rejection the token comes
 from p_i with d_i removed and renormalised, and when every draft is kept a bonus token
 comes from p_k.  The emitted tokens are distributed exactly as plain sampling from
-the target.
+the target.  A draft model that samples its proposals from q uses the general rule:
+keep d_i with probability min(1, p_i(d_i) / q_i(d_i)), else draw from
+norm(max(0, p_i - q_i)).
 """
 from __future__ import annotations
 
@@ -100,6 +102,29 @@ def accept_sampled(draft: Sequence[int], probs: torch.Tensor, gen: torch.Generat
     return out, len(draft)
 
 
+def accept_with_draft_probs(draft: Sequence[int], probs: torch.Tensor, qprobs: torch.Tensor,
+                            gen: torch.Generator) -> Tuple[List[int], int]:
+    """Speculative sampling with a sampled draft: d_i was drawn from q_i (qprobs row i);
+    keep it with probability min(1, p_i(d_i) / q_i(d_i)), else draw from
+    norm(max(0, p_i - q_i)) and stop; after every draft is kept, draw from p_k."""
+    probs = probs.float().cpu()
+    qprobs = qprobs.float().cpu()
+    out: List[int] = []
+    for i, d in enumerate(draft):
+        p, q = probs[i], qprobs[i]
+        d = int(d)
+        u = float(torch.rand((), generator=gen))
+        if float(q[d]) > 0.0 and u < min(1.0, float(p[d]) / float(q[d])):
+            out.append(d)
+            continue
+        residual = torch.clamp(p - q, min=0.0)
+        tot = float(residual.sum())
+        out.append(int(torch.multinomial(residual / tot if tot > 0 else p, 1, generator=gen)))
+        return out, i
+    out.append(int(torch.multinomial(probs[len(draft)], 1, generator=gen)))
+    return out, len(draft)
+
+
 class SpecStats:
     def __init__(self):
         self.proposed = 0
@@ -116,8 +141,11 @@ class SpecStats:
 
 
 def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: SpecStats,
-                            drafts: Optional[List[List[int]]] = None):
-    """One verify step for `active` requests of an LLMEngine (greedy ones get drafts)."""
+                            drafts: Optional[List[List[int]]] = None,
+                            draft_probs: Optional[List[Optional[torch.Tensor]]] = None):
+    """One verify step for `active` requests of an LLMEngine.  `draft_probs[i]`, when
+    given, holds the draft model's distributions [len(draft), V] the drafts of a sampled
+    request were drawn from (else the draft counts as deterministic)."""
     kv, runner = engine.kv, engine.runner
     items, feeds, starts, ds = [], [], [], []
     for i, r in enumerate(active):
@@ -177,7 +205,8 @@ def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: S
             # seeded from (runner seed, request, position): the same on every rank
             gen = torch.Generator().manual_seed((runner.seed * 1000003 + zlib.crc32(str(r.request_id).encode()) * 7919
                                                  + len(r.output_ids)) & 0x7FFFFFFFFFFFFFFF)
-            toks, na = accept_sampled(d, pr, gen)
+            q = draft_probs[len(out)] if draft_probs is not None else None
+            toks, na = accept_sampled(d, pr, gen) if q is None else accept_with_draft_probs(d, pr, q, gen)
         stats.proposed += len(d)
         stats.accepted += na
         kv.truncate(r.request_id, start + 1 + na)
@@ -222,6 +251,19 @@ class PromptLookupDecoder:
         return list(req.output_ids)
 
 
+def _full_logits(llm, seq: Sequence[int]) -> torch.Tensor:
+    """Last-position logits of `seq` under `llm` (a prefill into a scratch sequence)."""
+    eng = llm.engine
+    rid = f"draft-{id(seq)}-{len(seq)}"
+    with eng._lock:
+        eng.kv.allocate(rid, len(seq))
+        try:
+            it = PrefillItem(list(seq), 0, eng.kv.slots_for(rid, 0, len(seq)), eng.kv.block_table(rid), len(seq), True)
+            return llm.runner.prefill_logits([it])[-1:].float()
+        finally:
+            eng.kv.free(rid)
+
+
 class DraftModelDecoder:
     """Draft-model speculation: a small model proposes gamma tokens greedily, the
     target verifies them in one forward; gamma adapts to the running acceptance
@@ -241,24 +283,53 @@ class DraftModelDecoder:
         r = self.draft.engine.generate([seq], SamplingParams(max_tokens=k))[0]
         return r.output_ids
 
-    def generate(self, prompt_ids: Sequence[int], max_new_tokens: int) -> List[int]:
+    def _propose_sampled(self, seq: List[int], k: int, params, gen: torch.Generator):
+        """k draft tokens drawn from the draft model's filtered distributions (same
+        temperature / top-k / top-p as the request); returns (tokens, q rows [k, V])."""
+        runner = self.draft.runner
+        toks: List[int] = []
+        rows = []
+        cur = list(seq)
+        for _ in range(k):
+            if len(cur) + 1 > self.draft.engine.max_model_len:
+                break
+            logits = _full_logits(self.draft, cur)
+            q = filtered_probs(logits, params.temperature, params.top_k, params.top_p)[0]
+            t = int(torch.multinomial(q.cpu(), 1, generator=gen))
+            toks.append(t)
+            rows.append(q.cpu())
+            cur.append(t)
+        return toks, (torch.stack(rows) if rows else None)
+
+    def generate(self, prompt_ids: Sequence[int], max_new_tokens: int, params=None, seed: int = 0) -> List[int]:
+        """Greedy by default; with sampling `params` (temperature > 0) the draft samples
+        its proposals and the target accepts them by rejection sampling, so the output
+        follows the target's distribution exactly."""
         eng = self.target.engine
         from .engine import SamplingParams
+        sp = params if params is not None else SamplingParams(max_tokens=max_new_tokens)
+        sp = SamplingParams(max_tokens=max_new_tokens, temperature=sp.temperature, top_k=sp.top_k, top_p=sp.top_p,
+                            stop_token_ids=sp.stop_token_ids, ignore_eos=sp.ignore_eos)
+        gen = torch.Generator().manual_seed(seed)
         with eng._lock:
-            req = eng.add_request(prompt_ids, SamplingParams(max_tokens=max_new_tokens))
+            req = eng.add_request(prompt_ids, sp)
             eng.waiting.remove(req)
             eng.kv.allocate(req.request_id, len(req.prompt_ids))
             eng.running.append(req)
             toks = eng.runner.prefill([PrefillItem(req.prompt_ids, 0, eng.kv.slots_for(req.request_id, 0,
                                                                                       len(req.prompt_ids)),
                                                    eng.kv.block_table(req.request_id), len(req.prompt_ids), True)],
-                                      [0.0], [0], [1.0], [0])
+                                      [sp.temperature], [sp.top_k], [sp.top_p], [0])
             req.num_computed = len(req.prompt_ids)
             eng._emit(req, int(toks[0]))
             while not req.finished:
                 seq = req.prompt_ids + req.output_ids
-                d = self._propose(seq, self.gamma)
-                new = speculative_decode_step(eng, [req], 0, 0, self.stats, drafts=[d])[0]
+                if sp.greedy:
+                    d, q = self._propose(seq, self.gamma), None
+                else:
+                    d, q = self._propose_sampled(seq, self.gamma, sp, gen)
+                new = speculative_decode_step(eng, [req], 0, 0, self.stats, drafts=[d],
+                                              draft_probs=None if q is None else [q])[0]
                 if d:
                     self.recent = (self.recent + [(len(new) - 1) / len(d)])[-self.window:]
                 if self.adaptive and len(self.recent) >= 3:
