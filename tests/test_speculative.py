@@ -1,4 +1,5 @@
 """Speculative decoding must reproduce plain greedy decoding exactly (CPU reference ops)."""
+import pytest
 import torch
 
 from vramancer_b200.engine.engine import SamplingParams
@@ -149,3 +150,20 @@ def test_draft_model_sampling_with_an_identical_draft_accepts_everything():
     out = dec.generate(p, 20, params=SamplingParams(max_tokens=20, temperature=0.8, top_k=40), seed=3)
     assert len(out) == 20
     assert dec.stats.proposed > 0 and dec.stats.acceptance > 0.9
+
+
+@pytest.mark.gpu
+def test_prompt_lookup_on_gpu_greedy_and_sampled(cuda_errors_clean):
+    """Speculation through the CUDA kernels (verify = paged prefill forward): greedy and
+    sampled requests finish with their token counts and drafts get accepted on a
+    repetitive random-init model."""
+    from vramancer_b200.engine.engine import SamplingParams
+    from vramancer_b200.llm import LLM
+    llm = LLM("tiny-qwen2-d128", device="cuda:0", max_batch=4, max_model_len=256, kv_pages=64, spec_num_draft=6,
+              spec_ngram=2)
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (30, 12)]
+    reqs = llm.generate(prompts, SamplingParams(max_tokens=32))
+    reqs += llm.generate(prompts[:1], SamplingParams(max_tokens=24, temperature=0.7, top_k=20))
+    assert [len(r.output_ids) for r in reqs] == [32, 32, 24]
+    assert llm.engine.spec_stats.proposed > 0
