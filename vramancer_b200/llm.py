@@ -7,6 +7,13 @@
 Builds the weights (HF safetensors, NVFP4 checkpoint or random N(0, 0.02)), the paged
 KV pool sized from the free memory left after the weights, the block manager, the
 model runner (CUDA-graph decode) and the continuous-batching engine.
+
+With `fold_norms=True` (the default; dense RMSNorm models with bf16 weights on one
+GPU) the input and post-attention RMSNorm weights are multiplied into the columns of
+`qkv_w` / `gate_up_w` in place, so small decode batches run the norms inside the
+GEMMs.  `llm.weights` then holds the folded matrices (each marked with the norm weight
+it carries, `_vrm_norm_w`); pass `fold_norms=False` to keep checkpoint tensors as
+loaded.
 """
 from __future__ import annotations
 
