@@ -334,6 +334,10 @@ def save_safetensors(weights: Weights, cfg: ModelConfig, path: str) -> None:
                 continue
             _, i, n = k.split(".", 2)
             pre = f"model.layers.{i}."
+            nw = getattr(t, "_vrm_norm_w", None)
+            if nw is not None:
+                # folded RMSNorm weight (LLM(fold_norms=True)): write the checkpoint's matrix
+                t = (t.float() / nw.float().view(1, -1)).to(t.dtype)
             if n in ("qkv_w", "qkv_b"):
                 q, kk, v = torch.split(t, [cfg.q_size, cfg.kv_size, cfg.kv_size], 0)
                 suf = "weight" if n == "qkv_w" else "bias"
