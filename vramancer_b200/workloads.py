@@ -139,6 +139,7 @@ def run_spec(args, info, dev, tp) -> dict:
     span_len, reps = 64, 8
     out = {"workload": "spec", "model": args.model, "quantization": args.quantization or "bf16",
            "ngram": args.ngram, "num_draft": args.draft, "prompt": f"random {span_len}-token span x {reps}",
+           "temperature": args.temperature, "top_k": args.top_k,
            "output_tokens": args.output, "batch": args.batch}
     results = {}
     ref_tokens = None
@@ -151,7 +152,8 @@ def run_spec(args, info, dev, tp) -> dict:
         for _ in range(args.batch):
             span = [r2.randrange(vocab) for _ in range(span_len)]
             prompts.append(span * reps)
-        params = SamplingParams(max_tokens=args.output, ignore_eos=True)
+        params = SamplingParams(max_tokens=args.output, ignore_eos=True, temperature=args.temperature,
+                                top_k=args.top_k)
         llm.warmup()
         llm.engine.generate([prompts[0][:128]], SamplingParams(max_tokens=16, ignore_eos=True))
         st0 = (llm.engine.spec_stats.proposed, llm.engine.spec_stats.accepted)
@@ -174,8 +176,8 @@ def run_spec(args, info, dev, tp) -> dict:
         results[mode] = res
         if ref_tokens is None:
             ref_tokens = toks
-        else:
-            out["tokens_equal"] = toks == ref_tokens
+        elif args.temperature <= 0:
+            out["tokens_equal"] = toks == ref_tokens   # greedy only: sampled runs draw differently
         del llm
         torch.cuda.empty_cache() if dev.type == "cuda" else None
     out.update(results)
@@ -257,6 +259,8 @@ def parse_args(argv=None):
     ap.add_argument("--prefill-chunk", type=int, default=8192)
     ap.add_argument("--ngram", type=int, default=3)
     ap.add_argument("--draft", type=int, default=8)
+    ap.add_argument("--temperature", type=float, default=0.0, help="spec: > 0 measures speculative sampling")
+    ap.add_argument("--top-k", type=int, default=0)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--batches", default="1,8,64")
