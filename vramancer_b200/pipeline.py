@@ -306,11 +306,14 @@ class InferencePipeline:
         if not stop or self._bcast is not None:
             return None
         ids: List[int] = []
+        # a stop string of n characters spans at most n tokens: checking the text of the
+        # last n + 4 tokens at every token finds it as soon as it is complete, at a cost
+        # independent of the output length (this runs inside the engine step)
+        window = max(len(x) for x in stop) + 4
 
         def on_tok(req, tok):
             ids.append(tok)
-            tail = ids if len(ids) <= 256 else ids[-64:]
-            if stop_index(self.tokenizer.decode(tail), stop) >= 0:
+            if stop_index(self.tokenizer.decode(ids[-window:]), stop) >= 0:
                 self.engine.abort(req.request_id)
         return on_tok
 
