@@ -2,7 +2,8 @@
 //
 // Everything here is thin inline PTX around Blackwell primitives:
 //   * mbarrier (init / arrive / expect_tx / bounded try_wait)
-//   * TMA tiled loads (cp.async.bulk.tensor, never with .multicast::cluster)
+//   * TMA tiled loads (cp.async.bulk.tensor), each CTA loading its own tiles (no cluster
+//     multicast of loads anywhere in this code)
 //   * tcgen05 (TMEM alloc/dealloc, UMMA issue, commit, TMEM->register loads)
 //   * warp-level mma.sync / ldmatrix / cp.async for the small-M kernels
 // plus a device-wide error word that every bounded wait reports into.
