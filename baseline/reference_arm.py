@@ -11,7 +11,17 @@ What runs, all of it reference code:
               VRM_DISABLE_TURBO: core.backends.HuggingFaceBackend.generate (HF generate
               with KV cache, core/backends.py:1868-1934), and says so in "notes".
   bs32        core.continuous_batcher.ContinuousBatcher(model, tokenizer, 32).submit()
-              x 32 -> start() -> futures
+              x 32 -> start() -> futures, when it can run on the installed transformers:
+              its per-request cache split (_unbatch_kv_cache, core/continuous_batcher.py:
+              869-891) reads DynamicCache.key_cache, which transformers 5 removed (caches
+              keep per-layer objects in .layers), so every batched-prefill request fails
+              there.  The arm then measures the reference's batched generation call,
+              core.backends.HuggingFaceBackend.generate_batch (core/backends.py:2113-2171:
+              left-padded prompts, one HF generate with KV cache), and says so in "notes".
+The model's parameters are frozen (requires_grad False), as for any inference load: the
+batcher's worker thread runs its forwards without torch.no_grad, and with trainable
+parameters autograd keeps every activation of the batched prefill alive (about 150 GB
+for 32 x 512 tokens of the 14B model), which is what ran the GPU out of memory.
 The model is transformers' Qwen2ForCausalLM built from the Qwen2.5-14B configuration with
 random N(0, 0.02) bf16 weights directly on the GPU: there are no checkpoints offline, and
 the reference's own loader (core/backends.py:1185-1390) passes a device_map to
@@ -48,6 +58,7 @@ class IdTokenizer:
     eos_token_id = None
     pad_token_id = 0
     pad_token = "0"
+    padding_side = "right"
 
     def __init__(self, vocab: int):
         self.vocab = vocab
@@ -63,8 +74,9 @@ class IdTokenizer:
         inp = torch.zeros(len(ids), n, dtype=torch.long)
         mask = torch.zeros_like(inp)
         for i, x in enumerate(ids):
-            inp[i, :len(x)] = torch.tensor(x)
-            mask[i, :len(x)] = 1
+            sl = slice(n - len(x), n) if self.padding_side == "left" else slice(0, len(x))
+            inp[i, sl] = torch.tensor(x)
+            mask[i, sl] = 1
         from transformers import BatchEncoding
         return BatchEncoding({"input_ids": inp, "attention_mask": mask})
 
@@ -88,7 +100,9 @@ def _build_model(dev):
     finally:
         torch.set_default_dtype(prev)
     # some parameters (lm_head) can still be created on the host: move everything
-    return model.to(device=dev, dtype=torch.bfloat16).eval()
+    model = model.to(device=dev, dtype=torch.bfloat16).eval()
+    model.requires_grad_(False)
+    return model
 
 
 def _timed(fn):
@@ -161,7 +175,44 @@ def _bs1(model, tok, prompt_ids, steps, warm, ttft_runs, notes, dev):
     return {"tok_s": round(1000.0 / ms, 2), "ms_per_step": round(ms, 3), "api": api}, statistics.median(ttfts)
 
 
-def _bs32(model, tok, prompts, steps, warm, dev):
+def _batcher_usable() -> str:
+    """'' when the stock ContinuousBatcher can split a batched cache here, else why not."""
+    try:
+        from transformers import DynamicCache
+    except ImportError:
+        return ""
+    if not hasattr(DynamicCache(), "key_cache"):
+        import transformers
+        return (f"ContinuousBatcher unusable on transformers {transformers.__version__}: _unbatch_kv_cache reads "
+                "DynamicCache.key_cache (core/continuous_batcher.py:869-891), which this version no longer has, "
+                "so every batched-prefill request fails; bs32 measured with HuggingFaceBackend.generate_batch")
+    return ""
+
+
+def _bs32_generate_batch(model, tok, prompts, steps, warm, dev):
+    """bs32 through the reference's batched generation call: one left-padded HF
+    generate with KV cache over all prompts (core/backends.py:2113-2171)."""
+    from core.backends import HuggingFaceBackend
+    be = HuggingFaceBackend("qwen2.5-14b-random-init")
+    be.model, be.tokenizer = model, tok
+    be.block_devices = [int(str(dev).split(":")[-1])]
+
+    def gen(n):
+        return be.generate_batch(prompts, max_new_tokens=n, min_new_tokens=n, do_sample=False)
+    gen(2)                                                    # warm-up
+    t_short, _ = _timed(lambda: gen(1 + warm))
+    t_long, outs = _timed(lambda: gen(1 + warm + steps))
+    ms_step = (t_long - t_short) / steps
+    n_tok = sum(len(o.split()) for o in outs)
+    return {"tok_s": round(len(prompts) * 1000.0 / ms_step, 2), "ms_per_step": round(ms_step, 3),
+            "api": "HuggingFaceBackend.generate_batch", "tokens_returned": n_tok}
+
+
+def _bs32(model, tok, prompts, steps, warm, dev, notes):
+    why = _batcher_usable()
+    if why:
+        notes.append(why)
+        return _bs32_generate_batch(model, tok, prompts, steps, warm, dev)
     from core.continuous_batcher import ContinuousBatcher
 
     def run(n_new):
@@ -180,7 +231,8 @@ def _bs32(model, tok, prompts, steps, warm, dev):
     t_short, _ = run(1 + warm)
     t_long, outs = run(1 + warm + steps)
     ms_step = (t_long - t_short) / steps
-    return {"tok_s": round(len(prompts) * 1000.0 / ms_step, 2), "ms_per_step": round(ms_step, 3)}
+    return {"tok_s": round(len(prompts) * 1000.0 / ms_step, 2), "ms_per_step": round(ms_step, 3),
+            "api": "ContinuousBatcher.submit"}
 
 
 def run(args, metric):
@@ -216,7 +268,7 @@ def run(args, metric):
     bs1, ttft = _bs1(model, tok, prompt_ids, steps, warm, args.ttft_runs, notes, dev)
     try:
         prompts = [" ".join(str(rng.randrange(vocab)) for _ in range(P)) for _ in range(B)]
-        bs32 = _bs32(model, tok, prompts, steps, warm, dev)
+        bs32 = _bs32(model, tok, prompts, steps, warm, dev, notes)
         value = bs32["tok_s"]
     except Exception as e:
         bs32, value = None, None
@@ -241,7 +293,13 @@ def run(args, metric):
         "bs1": bs1,
         "ttft_p50_ms": round(ttft, 3),
         "ttft_prompt_tokens": P,
-        "e2e": {"value": value, "unit": "tok/s", "api": "ContinuousBatcher.submit"},
+        # end to end: prompts go in as host strings and results come back as host
+        # strings through the public call; per decode step the host copies in nothing
+        # new and HF generate's stopping check reads one flag per sequence back
+        "e2e": {"value": value, "unit": "tok/s", "api": bs32["api"] if bs32 else None,
+                "h2d_bytes_per_step": round(B * P * 8 / (1 + warm + steps)) if bs32 else None,
+                "d2h_bytes_per_step": B if bs32 else None,
+                "note": "prompt ids (int64) copied once per call, amortised over its decode steps"},
         "clocks": clk,
         "setup_s": round(time.time() - t0, 1),
         "notes": notes,

@@ -5,11 +5,13 @@ CUDA-graph decode.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs under torchrun (one process per GPU, NCCL).  By default the batch-32 value is
-measured on N data-parallel replicas (global batch 32 x N, weak scaling: the 14B model
-fits on one B200), and the single-stream numbers (bs1, TTFT) and a strong-scaling
-batch-32 figure ("tp") on the same N GPUs as tensor parallelism TP=N;
---parallel tp measures everything at TP=N.  Rank 0 prints one JSON line.
+N > 1 runs under torchrun (one process per GPU, NCCL) as tensor parallelism TP=N: the
+same model and the same batch of 32 on N GPUs (strong scaling), every row-parallel
+projection all-reduced inside its GEMM + norm kernels over NVLink.  The same job also
+measures N data-parallel replicas of the full model (key "dp", global batch 32 x N,
+weak scaling) and checks TP=N logits and greedy tokens against TP=1 on a small model
+(key "tp_check").  --parallel dp makes the replicas the headline.  Rank 0 prints one
+JSON line.
 
 value   = aggregate decode tok/s at batch 32 (prompt 512), device-timed with CUDA
           events over exactly K decode steps (inputs staged on the device), max over
@@ -37,7 +39,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (bs1, bs32) + p50 TTFT, Qwen2.5-14B-arch bf16 @1/2/4/8 B200"
-BASELINE_BS1_TOK_S = 5.41   # BASELINE.md row 1 (reference, Qwen2.5-14B bf16, 2 consumer GPUs)
+BASELINE_BS1_TOK_S = 5.41   # reference's published Qwen2.5-14B bf16 decode rate (2 consumer GPUs)
 
 
 def parse_args(argv=None):
@@ -54,8 +56,10 @@ def parse_args(argv=None):
     p.add_argument("--num-layers", type=int, default=None, help="debug only: truncates the model (invalid run)")
     p.add_argument("--quantization", default=None, choices=["nvfp4", "fp8"],
                    help="weight format (the headline is bf16; these are extra measurements)")
-    p.add_argument("--parallel", choices=["dp", "tp"], default=None,
-                   help="N > 1: data-parallel replicas (default; bs1 / TTFT still measured at TP=N) or TP=N only")
+    p.add_argument("--parallel", choices=["dp", "tp"], default="tp",
+                   help="N > 1: headline at TP=N (default) or on N data-parallel replicas")
+    p.add_argument("--no-extras", action="store_true",
+                   help="N > 1: skip the data-parallel figure and the TP numeric check")
     return p.parse_args(argv)
 
 
@@ -133,7 +137,7 @@ def run_ours(args):
     rank, world = info.rank, info.world_size
     dev = torch.device("cuda", info.local_rank)
     torch.cuda.set_device(dev)
-    mode = args.parallel or ("dp" if world > 1 else "tp")
+    mode = args.parallel if world > 1 else "tp"
     B, P = args.batch, args.prompt_len
     steps, warm = args.steps, args.warmup
     max_len = P + warm + steps + 64
@@ -273,18 +277,22 @@ def run_ours(args):
         return res
 
     sampler = ClockSampler(info.local_rank) if rank == 0 else None
+    tp = comm.tp_context()
+    dpres = tpres = check = None
     if world == 1 or mode == "tp":
-        tp = comm.tp_context()
         main = measure(tp, clocks=sampler)
         lat = main
-        tpres = None
+        if world > 1 and not args.no_extras:
+            # the same GPUs as data-parallel replicas (a full model per GPU, batch B each)
+            dpres = measure(None, want_bs1=False, want_ttft=False, want_e2e=False)
     else:
-        # data parallel: a full replica per GPU, global batch B per replica (weak scaling);
-        # then the same model as TP=world for the single-stream latency (bs1, TTFT)
+        # data parallel headline: a full replica per GPU, global batch B per replica (weak
+        # scaling); then the same model as TP=world for the single-stream latency (bs1, TTFT)
         main = measure(None, want_bs1=False, want_ttft=False, clocks=sampler)
-        tp = comm.tp_context()
         lat = measure(tp, want_e2e=False)
         tpres = lat
+    if world > 1 and not args.no_extras:
+        check = tp_numeric_check()
     cfg = main["cfg"]
     dp = world > 1 and mode == "dp"
     replicas = world if dp else 1
@@ -329,12 +337,30 @@ def run_ours(args):
     if tpres is not None:
         res["tp"] = {"parallelism": f"tp{world}", "global_batch": B, "value": round(B * steps / (tpres["ms32"] / 1000.0), 2),
                      "ms_per_step": round(tpres["ms32"] / steps, 4), "scaling": "strong"}
+    if dpres is not None:
+        res["dp"] = {"parallelism": f"dp{world}", "global_batch": B * world,
+                     "value": round(world * B * steps / (dpres["ms32"] / 1000.0), 2),
+                     "ms_per_step": round(dpres["ms32"] / steps, 4), "scaling": "weak"}
+        res["device_errors"] |= dpres["err"]
+    if check is not None:
+        res["tp_check"] = check
     if args.num_layers:
         res["invalid"] = "truncated model (--num-layers): debugging only"
     comm.barrier()
     if rank == 0:
         print(json.dumps(res), flush=True)
     comm.destroy()
+
+
+def tp_numeric_check() -> dict:
+    """TP=world vs TP=1 on a small Qwen2-shaped model (8 query / 8 KV heads of 128, bf16,
+    CUDA graphs, the fused all-reduce):
+    largest prefill logit difference relative to the logit scale, greedy tokens equal."""
+    from vramancer_b200.parallel import tp_check
+    r = tp_check.run("tiny-qwen2-tp8", n_new=8, device="cuda")
+    return {"model": "tiny-qwen2-tp8", "max_logit_diff": round(r["max_logit_diff"], 5),
+            "logit_scale": round(r["scale"], 4), "tokens_equal": r["tokens_equal"],
+            "fused_ar_rel_diff": r["fused_ar_rel_diff"]}
 
 
 # ----------------------------------------------------------------------------- reference arm

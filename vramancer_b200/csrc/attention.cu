@@ -1110,7 +1110,7 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   p.cache_w = reinterpret_cast<uint8_t*>(const_cast<void*>(a.cache));
   p.Hq = a.Hq;
   p.num_pages = a.cache_pages;
-  p.err = error_word();
+  p.err = a.err ? a.err : error_word();
   if (a.positions != nullptr) {
     VRM_REQUIRE(a.slot_mapping != nullptr, "decode attention: fused KV write needs slot_mapping");
     VRM_REQUIRE(a.cos_sin == nullptr || a.rot_dim == a.D, "decode attention: fused RoPE needs rot_dim == head_dim");
@@ -1154,7 +1154,7 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
     t.counters = p.counters;
     t.max_chunks = splits;
     t.chunk_pages = std::max(1, (std::max(1, a.max_pages) + splits - 1) / splits);
-    t.err = error_word();
+    t.err = p.err;
     const CUtensorMap map = make_kmajor_map(a.cache, pool_rows, a.D, a.D, kPage);
     const int items = a.B * a.KH * splits;
     const int grid = std::max(1, std::min(items, 2 * device_sm_count()));

@@ -1,7 +1,8 @@
 // Allocation-free variant of the split-KV paged decode attention launch (see
-// vrm_noalloc.h for who needs it and its limits).  The split partials and the
-// per-(sequence, kv head) merge counters live in the two file-scope device arrays
-// below instead of the per-device workspace that the regular launcher allocates.
+// vrm_noalloc.h for who needs it and its limits).  The split partials, the
+// per-(sequence, kv head) merge counters and the error word that bounded waits and
+// bounds checks report into live in the file-scope device arrays below instead of the
+// per-device workspace and error word that the regular launcher allocates lazily.
 //
 // In host code the array names are host-side stand-ins, not device addresses; the
 // device address is resolved once per device with cudaGetSymbolAddress (device
@@ -18,12 +19,14 @@ namespace {
 
 static __device__ __align__(256) float g_noalloc_scratch[VRM_NOALLOC_SCRATCH_BYTES / sizeof(float)];
 static __device__ __align__(256) uint32_t g_noalloc_counters[VRM_NOALLOC_MAX_GROUPS];
+static __device__ __align__(256) uint32_t g_noalloc_err[1];
 
 constexpr int kMaxDevices = 64;
 
 struct DeviceSlot {
   float* scratch = nullptr;
   uint32_t* counters = nullptr;
+  uint32_t* err = nullptr;
   bool ready = false;
 };
 
@@ -42,8 +45,12 @@ cudaError_t resolve(int dev, DeviceSlot* out) {
     void* c = nullptr;
     e = cudaGetSymbolAddress(&c, g_noalloc_counters);
     if (e != cudaSuccess) return e;
+    void* w = nullptr;
+    e = cudaGetSymbolAddress(&w, g_noalloc_err);
+    if (e != cudaSuccess) return e;
     s.scratch = static_cast<float*>(p);
     s.counters = static_cast<uint32_t*>(c);
+    s.err = static_cast<uint32_t*>(w);
     s.ready = true;
   }
   *out = s;
@@ -53,6 +60,17 @@ cudaError_t resolve(int dev, DeviceSlot* out) {
 int fail(const std::string& msg) {
   g_last_error = msg;
   return -1;
+}
+
+// Resolves the current device's slot; 0 or a failure code (message set).
+int current_slot(DeviceSlot* slot) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail("device index out of range");
+  e = resolve(dev, slot);
+  if (e != cudaSuccess) return fail(std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+  return 0;
 }
 
 }  // namespace
@@ -65,13 +83,9 @@ extern "C" int vrm_paged_attention_decode_noalloc(const void* q, int64_t ld_q, c
                                                   int batch, int max_pages, int num_splits, cudaStream_t stream) {
   g_last_error.clear();
   try {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return fail(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
-    if (dev < 0 || dev >= kMaxDevices) return fail("device index out of range");
     DeviceSlot slot;
-    e = resolve(dev, &slot);
-    if (e != cudaSuccess) return fail(std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    if (current_slot(&slot) != 0) return -1;
+    cudaError_t e = cudaSuccess;
     if (batch <= 0) return 0;
     if (num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 || num_q_heads / num_kv_heads > 8)
       return fail("GQA group (num_q_heads / num_kv_heads) must be a whole number <= 8");
@@ -84,7 +98,7 @@ extern "C" int vrm_paged_attention_decode_noalloc(const void* q, int64_t ld_q, c
       splits = vrm::decode_attention_choose_splits(batch, num_kv_heads, max_pages);
       while (splits > 1 && vrm::decode_attention_scratch_bytes(batch, num_q_heads, head_dim, splits) > cap) --splits;
     }
-    if (splits > 128) splits = 128;
+    if (splits > 128) return fail("num_splits must be <= 128 (got " + std::to_string(splits) + ")");
     const size_t need = vrm::decode_attention_scratch_bytes(batch, num_q_heads, head_dim, splits);
     if (need > cap)
       return fail("request needs " + std::to_string(need) + " bytes of split scratch (batch " + std::to_string(batch) +
@@ -123,6 +137,7 @@ extern "C" int vrm_paged_attention_decode_noalloc(const void* q, int64_t ld_q, c
     a.ws = slot.scratch;
     a.ws_bytes = cap;
     a.counters = slot.counters;
+    a.err = slot.err;
     vrm::paged_attention_decode(a, stream);
     return 0;
   } catch (const std::exception& ex) {
@@ -133,3 +148,26 @@ extern "C" int vrm_paged_attention_decode_noalloc(const void* q, int64_t ld_q, c
 extern "C" const char* vrm_noalloc_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" size_t vrm_noalloc_scratch_capacity(void) { return VRM_NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int vrm_noalloc_setup(void) {
+  g_last_error.clear();
+  DeviceSlot slot;
+  return current_slot(&slot);
+}
+
+extern "C" int vrm_noalloc_read_and_clear_errors(uint32_t* flags) {
+  g_last_error.clear();
+  DeviceSlot slot;
+  if (current_slot(&slot) != 0) return -1;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(std::string("cudaDeviceSynchronize: ") + cudaGetErrorString(e));
+  uint32_t v = 0;
+  e = cudaMemcpy(&v, slot.err, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(std::string("cudaMemcpy: ") + cudaGetErrorString(e));
+  e = cudaMemset(slot.err, 0, sizeof(uint32_t));
+  if (e != cudaSuccess) return fail(std::string("cudaMemset: ") + cudaGetErrorString(e));
+  if (flags) *flags = v;
+  return 0;
+}
+
+extern "C" uint64_t vrm_host_device_allocations(void) { return vrm::device_allocations(); }

@@ -479,9 +479,9 @@ struct StreamK {
 
 // Fused all-reduce, push half (ARPush in vrm_kernels.h): the owner of each finished
 // output tile stores the partial (pre-bias, rounded to bf16 like the input of a bf16
-// NCCL all-reduce: half the NVLink bytes of fp32) into this rank's slot on every rank
-// (posted NVLink stores; its own slot is local) and never waits; the last CTA of the
-// launch advances the epoch and flags every peer.  ar_norm.cu reduces.
+// NCCL all-reduce) into this rank's slot on every rank (posted NVLink stores; its own
+// slot is local) and never waits.  No fence and no flag: ar_norm.cu polls the values
+// themselves (empty pattern 0x8000), so the transfer costs one NVLink write latency.
 using ARParams = ARPush;
 
 template <int BN, int STAGES, bool kAR, bool kF8 = false>
@@ -653,7 +653,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     const uint32_t t_lane = tmem_base + ((uint32_t)lane_base << 16);
     pdl_wait();
     uint32_t epoch = 0;
-    if (kAR) epoch = *reinterpret_cast<volatile uint32_t*>(ar.epoch) + 1u;
+    if (kAR) epoch = *reinterpret_cast<const volatile uint32_t*>(ar.epoch);
     // folded RMSNorm (consumer): rstd of token lane + 32 i in rs[i] of every epilogue warp
     float rs[4] = {1.f, 1.f, 1.f, 1.f};
     if (ep.ssq_in != nullptr) {
@@ -744,13 +744,22 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           for (int j = 0; j < 16; ++j) v[j] += o[j];
         }
         if (kAR) {
-          // push the partial into this rank's slot on every rank (own slot is local)
+          // push the partial into this rank's slot on every rank (own slot is local);
+          // e4m3 operands: per weight row x per token scales first
           if (r_glob < ep.N) {
+            if (kF8) {
+              const float sw = ep.scale_w[r_glob];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] *= sw * (tok0 + c0 + j < ep.M ? ep.scale_x[tok0 + c0 + j] : 0.f);
+            }
+            uint16_t bits[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) bits[j] = bf16_bits_nonempty(v[j]);
             for (int p = 0; p < ar.world; ++p) {
               __nv_bfloat16* dst = ar.xbuf[p] + xoff;
 #pragma unroll
               for (int j = 0; j < 16; ++j)
-                if (tok0 + c0 + j < ep.M) dst[(size_t)(tok0 + c0 + j) * ep.N] = __float2bfloat16(v[j]);
+                if (tok0 + c0 + j < ep.M) st_relaxed_sys_u16(dst + (size_t)(tok0 + c0 + j) * ep.N, bits[j]);
             }
           }
         } else {
@@ -799,25 +808,6 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         tile_counters[t] = 0u;   // all contributors counted: reset for the next launch
       }
       it += n;
-    }
-    if (kAR) {
-      // the CTA's remote pushes are ordered before its completion count (barrier, then a
-      // system-scope fence by the counting thread: release is cumulative); the last CTA
-      // advances the epoch and flags every peer
-      if (ar.per_thread_fence) asm volatile("fence.acq_rel.sys;" ::: "memory");
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) {
-        uint32_t prev;
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ar.done) : "memory");
-        if (prev == gridDim.x - 1) {
-          *ar.done = 0u;
-          asm volatile("fence.acq_rel.sys;" ::: "memory");
-          *reinterpret_cast<volatile uint32_t*>(ar.epoch) = epoch;
-          for (int p = 0; p < ar.world; ++p)
-            if (p != ar.rank) st_release_sys(ar.flags[p] + ar.rank, epoch);
-        }
-      }
     }
     if (tr && threadIdx.x == 64) tr[5] = globaltimer();
   }
@@ -1371,7 +1361,9 @@ void gemm_fp8(const GemmArgs& a, const float* scale_x, const float* scale_w, cud
   VRM_REQUIRE(a.K % 128 == 0 && a.ldx % 16 == 0 && a.ldw % 16 == 0, "gemm fp8: K % 128, row strides % 16 bytes");
   VRM_REQUIRE((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0,
               "gemm fp8: operands must be 16-byte aligned");
-  VRM_REQUIRE(!a.allreduce && scale_x && scale_w, "gemm fp8: scales required, no fused all-reduce");
+  VRM_REQUIRE(scale_x && scale_w, "gemm fp8: scales required");
+  VRM_REQUIRE(!a.allreduce || (a.M <= 128 && a.epilogue == kEpiNone && !a.bias && !a.residual),
+              "gemm fp8: the all-reduce push stores the raw partial of a decode GEMM (M <= 128)");
   VRM_REQUIRE(a.epilogue != kEpiSiluMul || (a.N % 2 == 0 && a.residual == nullptr), "gemm fp8: silu_mul epilogue");
   if (a.M <= 0 || a.N <= 0) return;
   EpiParams ep;
@@ -1392,6 +1384,16 @@ void gemm_fp8(const GemmArgs& a, const float* scale_x, const float* scale_w, cud
     const int BN = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
     const CUtensorMap mb = make_kmajor_map(a.x, a.M, Kp, a.ldx / 2, BN);
     const int ctas = streamk_ctas(n_tiles, k_tiles, BN, (double)a.N * a.K);
+    if (a.allreduce) {
+      const ARParams ar = *a.allreduce;
+      switch (BN) {
+        case 16: launch_streamk<16, 6, true, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ar); break;
+        case 32: launch_streamk<32, 5, true, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ar); break;
+        case 64: launch_streamk<64, 4, true, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ar); break;
+        default: launch_streamk<128, 3, true, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ar); break;
+      }
+      return;
+    }
     switch (BN) {
       case 16: launch_streamk<16, 6, false, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ARParams{}); break;
       case 32: launch_streamk<32, 5, false, true>(ma, mb, ep, a.N, (int)Kp, ctas, stream, ARParams{}); break;

@@ -412,6 +412,17 @@ __global__ void __launch_bounds__(kNvThreads, 2)
       }
       out[(size_t)m * a.ldo + n / 2] = __float2bfloat16(gt / (1.f + __expf(-gt)) * up);
     }
+  } else if (a.push) {
+    // fused all-reduce: posted stores of the partial into this rank's slot on every rank
+    const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(a.ar.epoch);
+    const size_t slot = ((size_t)(epoch & 1u) * a.ar.world + a.ar.rank) * (size_t)a.ar.half_floats;
+    for (int idx = threadIdx.x; idx < M * kNvRows; idx += kNvThreads) {
+      const int m = idx / kNvRows, r = idx % kNvRows;
+      const int n = n0 + r;
+      if (n >= N) continue;
+      const uint16_t bits = bf16_bits_nonempty(S[m * kSld + r] * gs);
+      for (int p = 0; p < a.ar.world; ++p) st_relaxed_sys_u16(a.ar.xbuf[p] + slot + (size_t)m * N + n, bits);
+    }
   } else {
     for (int idx = threadIdx.x; idx < M * kNvRows; idx += kNvThreads) {
       const int m = idx / kNvRows, r = idx % kNvRows;
@@ -459,6 +470,9 @@ void nvfp4_gemm(const Nvfp4GemmArgs& a, cudaStream_t st) {
   VRM_REQUIRE(a.M >= 1 && a.M <= 32, "nvfp4 gemm: M must be in [1, 32] (dequantise for larger M)");
   VRM_REQUIRE(a.ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0, "nvfp4 gemm: x rows 16-byte aligned");
   VRM_REQUIRE(a.epilogue != kEpiSiluMul || a.residual == nullptr, "nvfp4 gemm: silu_mul takes no residual");
+  VRM_REQUIRE(!a.push || (a.epilogue == kEpiNone && !a.bias && !a.residual && a.ar.xbuf && a.ar.epoch &&
+                          (long long)a.M * a.N <= a.ar.half_floats),
+              "nvfp4 gemm: the all-reduce push stores the raw partial into the receive buffer");
   const int NT = (a.M + 7) / 8;
   const int rbs = (a.N + kNvRows - 1) / kNvRows;
   const int ktiles = a.K / 64;

@@ -22,6 +22,19 @@ void symm_free(void* p) {
   if (p) cudaFree(p);
 }
 
+namespace {
+__global__ void fill_u16_kernel(uint16_t* p, size_t n, uint16_t v) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
+}
+}  // namespace
+
+void symm_fill_u16(void* p, size_t count, uint16_t value) {
+  if (count == 0) return;
+  fill_u16_kernel<<<256, 256>>>(static_cast<uint16_t*>(p), count, value);
+  VRM_CUDA_CHECK(cudaGetLastError());
+  VRM_CUDA_CHECK(cudaDeviceSynchronize());
+}
+
 std::vector<uint8_t> ipc_handle(void* p) {
   cudaIpcMemHandle_t h;
   VRM_CUDA_CHECK(cudaIpcGetMemHandle(&h, p));

@@ -378,32 +378,34 @@ void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k
 }
 
 // ---------------------------------------------------------------- fused GEMM + all-reduce
-// Push half: row-parallel GEMM whose epilogue stores the fp32 partial into every rank's
-// receive buffer and flags the peers (ARPush).  Nothing is written to a tensor here.
-void gemm_ar_push(const Tensor& x, const Tensor& w, const Tensor& xbuf_ptrs, const Tensor& flag_ptrs, Tensor& epoch,
-                  Tensor& done, int64_t rank, int64_t world, int64_t half_floats, bool per_thread_fence) {
-  check_bf16_2d(x, "gemm_ar x");
-  check_bf16_2d(w, "gemm_ar w");
+// Push half: row-parallel GEMM (bf16, or e4m3 with its scales) whose epilogue stores the
+// partial into this rank's slot of every rank's receive buffer (ARPush).  Nothing is
+// written to a tensor here.
+void gemm_ar_push(const Tensor& x, const Tensor& w, const Tensor& xbuf_ptrs, const Tensor& epoch, int64_t rank,
+                  int64_t world, int64_t half_floats, const OptT& scale_x, const OptT& scale_w) {
+  const bool f8 = w.scalar_type() == torch::kFloat8_e4m3fn || w.scalar_type() == torch::kByte;
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1,
+              "gemm_ar: 2-D CUDA operands with unit inner stride");
+  TORCH_CHECK(f8 ? (x.scalar_type() == torch::kFloat8_e4m3fn || x.scalar_type() == torch::kByte)
+                 : (x.scalar_type() == torch::kBFloat16 && w.scalar_type() == torch::kBFloat16),
+              "gemm_ar: bf16 x bf16 or e4m3 x e4m3 operands");
+  TORCH_CHECK(!f8 || (has(scale_x) && has(scale_w)), "gemm_ar: e4m3 operands need scale_x and scale_w");
   const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K, "gemm_ar: shapes");
   TORCH_CHECK(M <= 128, "gemm_ar: fused all-reduce is for decode shapes (M <= 128)");
   TORCH_CHECK(M * N <= half_floats, "gemm_ar: output larger than the receive buffer");
-  same_device(x, {&w, &xbuf_ptrs, &flag_ptrs, &epoch, &done}, "gemm_ar");
-  TORCH_CHECK(xbuf_ptrs.scalar_type() == torch::kInt64 && flag_ptrs.scalar_type() == torch::kInt64 &&
-                  xbuf_ptrs.numel() == world && flag_ptrs.numel() == world,
-              "gemm_ar: pointer arrays must be int64 [world]");
+  same_device(x, {&w, &xbuf_ptrs, &epoch}, "gemm_ar");
+  TORCH_CHECK(xbuf_ptrs.scalar_type() == torch::kInt64 && xbuf_ptrs.numel() == world,
+              "gemm_ar: pointer array must be int64 [world]");
   vrm::ARPush ar;
   ar.xbuf = reinterpret_cast<__nv_bfloat16* const*>(xbuf_ptrs.data_ptr());
-  ar.flags = reinterpret_cast<uint32_t* const*>(flag_ptrs.data_ptr());
-  ar.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
-  ar.done = reinterpret_cast<uint32_t*>(done.data_ptr());
+  ar.epoch = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
   ar.rank = (int)rank;
   ar.world = (int)world;
   ar.half_floats = half_floats;
-  ar.per_thread_fence = per_thread_fence ? 1 : 0;
   vrm::GemmArgs a;
   a.x = x.data_ptr();
-  a.ldx = x.stride(0);
+  a.ldx = x.stride(0);   // elements (bf16) or bytes (e4m3)
   a.w = w.data_ptr();
   a.ldw = w.stride(0);
   a.M = (int)M;
@@ -411,16 +413,25 @@ void gemm_ar_push(const Tensor& x, const Tensor& w, const Tensor& xbuf_ptrs, con
   a.K = (int)K;
   a.allreduce = &ar;
   const c10::cuda::CUDAGuard guard(x.device());
-  vrm::gemm_bf16(a, cur_stream());
+  if (f8) {
+    same_device_opt(x, {&scale_x, &scale_w}, "gemm_ar");
+    TORCH_CHECK(scale_x->scalar_type() == torch::kFloat32 && scale_w->scalar_type() == torch::kFloat32 &&
+                    scale_x->numel() >= M && scale_w->numel() >= N,
+                "gemm_ar: fp32 scales [M] and [N]");
+    vrm::gemm_fp8(a, scale_x->data_ptr<float>(), scale_w->data_ptr<float>(), cur_stream());
+  } else {
+    vrm::gemm_bf16(a, cur_stream());
+  }
 }
 
-// Reduce half fused with bias + residual + norm (ARNormArgs).  xbuf / flags / epoch
-// are this rank's own device buffers.
-void ar_norm(int64_t xbuf, int64_t flags, const Tensor& epoch, int64_t rank, int64_t world, int64_t half_floats,
+// Reduce half fused with bias + residual + norm (ARNormArgs).  xbuf / epoch / done are
+// this rank's own device buffers.
+void ar_norm(int64_t xbuf, const Tensor& epoch, const Tensor& done, int64_t rank, int64_t world, int64_t half_floats,
              int64_t T, int64_t H, const OptT& bias, const OptT& residual, const OptT& w, const OptT& b,
-             const OptT& out, int64_t mode, double eps) {
-  TORCH_CHECK(epoch.is_cuda(), "ar_norm: epoch must be a CUDA tensor");
-  same_device_opt(epoch, {&bias, &residual, &w, &b, &out}, "ar_norm");
+             const OptT& out, int64_t mode, double eps, int64_t spin_limit, const OptT& err) {
+  TORCH_CHECK(epoch.is_cuda() && done.is_cuda(), "ar_norm: epoch and done must be CUDA tensors");
+  same_device_opt(epoch, {&bias, &residual, &w, &b, &out, &err}, "ar_norm");
+  same_device(epoch, {&done}, "ar_norm");
   for (const OptT* t : {&bias, &residual, &w, &b, &out})
     if (has(*t)) TORCH_CHECK((*t)->scalar_type() == torch::kBFloat16, "ar_norm: bf16 tensors");
   if (has(residual)) TORCH_CHECK(residual->is_contiguous() && residual->numel() == T * H, "ar_norm: residual [T, H]");
@@ -429,10 +440,11 @@ void ar_norm(int64_t xbuf, int64_t flags, const Tensor& epoch, int64_t rank, int
   if (has(bias)) TORCH_CHECK(bias->numel() == H && bias->is_contiguous(), "ar_norm: bias [H]");
   if (has(w)) TORCH_CHECK(w->numel() == H && w->is_contiguous(), "ar_norm: weight [H]");
   if (has(b)) TORCH_CHECK(b->numel() == H && b->is_contiguous(), "ar_norm: norm bias [H]");
+  if (has(err)) TORCH_CHECK(err->scalar_type() == torch::kInt32 && err->numel() >= 1, "ar_norm: err int32 [1]");
   vrm::ARNormArgs a;
-  a.xbuf = reinterpret_cast<const __nv_bfloat16*>(xbuf);
-  a.flags = reinterpret_cast<const uint32_t*>(flags);
-  a.epoch = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  a.xbuf = reinterpret_cast<__nv_bfloat16*>(xbuf);
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr());
+  a.done = reinterpret_cast<uint32_t*>(done.data_ptr());
   a.rank = (int)rank;
   a.world = (int)world;
   a.half_floats = half_floats;
@@ -446,6 +458,8 @@ void ar_norm(int64_t xbuf, int64_t flags, const Tensor& epoch, int64_t rank, int
   a.ldo = has(out) ? out->stride(0) : H;
   a.mode = (int)mode;
   a.eps = (float)eps;
+  a.spin_limit = spin_limit > 0 ? (unsigned long long)spin_limit : 0ull;
+  a.err = has(err) ? reinterpret_cast<uint32_t*>(err->data_ptr()) : nullptr;
   const c10::cuda::CUDAGuard guard(epoch.device());
   vrm::ar_norm(a, cur_stream());
 }
@@ -516,6 +530,37 @@ void nvfp4_gemm_out(const Tensor& x, const Tensor& q, const Tensor& sc, const Te
   a.N = (int)N;
   a.K = (int)K;
   a.epilogue = (int)epilogue;
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::nvfp4_gemm(a, cur_stream());
+}
+
+// Fused all-reduce push of the W4A16 decode GEMM: the partial goes to this rank's slot
+// of every rank's receive buffer (ARPush); nothing is written to a tensor here.
+void nvfp4_gemm_ar_push(const Tensor& x, const Tensor& q, const Tensor& sc, const Tensor& gs, int64_t N,
+                        const Tensor& xbuf_ptrs, const Tensor& epoch, int64_t rank, int64_t world,
+                        int64_t half_floats) {
+  check_bf16_2d(x, "nvfp4_gemm_ar x");
+  const int64_t M = x.size(0), K = x.size(1);
+  check_nvfp4(q, sc, gs, N, K, "nvfp4_gemm_ar");
+  same_device(x, {&q, &xbuf_ptrs, &epoch}, "nvfp4_gemm_ar");
+  TORCH_CHECK(xbuf_ptrs.scalar_type() == torch::kInt64 && xbuf_ptrs.numel() == world,
+              "nvfp4_gemm_ar: pointer array must be int64 [world]");
+  TORCH_CHECK(M * N <= half_floats, "nvfp4_gemm_ar: output larger than the receive buffer");
+  vrm::Nvfp4GemmArgs a;
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.q = q.data_ptr<uint8_t>();
+  a.s = sc.data_ptr<uint8_t>();
+  a.gs = gs.data_ptr<float>();
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.push = 1;
+  a.ar.xbuf = reinterpret_cast<__nv_bfloat16* const*>(xbuf_ptrs.data_ptr());
+  a.ar.epoch = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  a.ar.rank = (int)rank;
+  a.ar.world = (int)world;
+  a.ar.half_floats = half_floats;
   const c10::cuda::CUDAGuard guard(x.device());
   vrm::nvfp4_gemm(a, cur_stream());
 }
@@ -1028,6 +1073,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_gemm_out", &nvfp4_gemm_out, py::arg("x"), py::arg("q"), py::arg("s"), py::arg("gs"), py::arg("N"),
         py::arg("bias"), py::arg("out"), py::arg("epilogue"), py::arg("residual"),
         "W4A16 decode GEMM (M <= 32) over NVFP4 weights");
+  m.def("nvfp4_gemm_ar_push", &nvfp4_gemm_ar_push, py::arg("x"), py::arg("q"), py::arg("s"), py::arg("gs"),
+        py::arg("N"), py::arg("xbuf_ptrs"), py::arg("epoch"), py::arg("rank"), py::arg("world"),
+        py::arg("half_floats"), "W4A16 decode GEMM pushing its partial into every rank's receive buffer");
   m.def("nvfp4_gemm_max_m", &vrm::nvfp4_gemm_max_m);
   m.def("tq_compress", &tq_compress, py::arg("x"), py::arg("signs"), py::arg("jl"),
         "TurboQuant: [..., 128] -> 64-byte records (Hadamard + PolarQuant + QJL)");
@@ -1061,14 +1109,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_experts", &moe_experts, py::arg("x"), py::arg("ids"), py::arg("weights"), py::arg("gate_up"),
         py::arg("down"), py::arg("BN"), py::arg("add"),
         "routed experts of a MoE layer on the device (plan, gather, grouped tcgen05 GEMMs, combine)");
-  m.def("gemm_ar_push", &gemm_ar_push, py::arg("x"), py::arg("w"), py::arg("xbuf_ptrs"), py::arg("flag_ptrs"),
-        py::arg("epoch"), py::arg("done"), py::arg("rank"), py::arg("world"), py::arg("half_floats"),
-        py::arg("per_thread_fence") = false,
-        "row-parallel GEMM pushing its fp32 partial into every rank's receive buffer (fused all-reduce, push)");
-  m.def("ar_norm", &ar_norm, py::arg("xbuf"), py::arg("flags"), py::arg("epoch"), py::arg("rank"), py::arg("world"),
+  m.def("gemm_ar_push", &gemm_ar_push, py::arg("x"), py::arg("w"), py::arg("xbuf_ptrs"), py::arg("epoch"),
+        py::arg("rank"), py::arg("world"), py::arg("half_floats"), py::arg("scale_x") = py::none(),
+        py::arg("scale_w") = py::none(),
+        "row-parallel GEMM storing its partial into every rank's receive buffer (fused all-reduce, push)");
+  m.def("ar_norm", &ar_norm, py::arg("xbuf"), py::arg("epoch"), py::arg("done"), py::arg("rank"), py::arg("world"),
         py::arg("half_floats"), py::arg("T"), py::arg("H"), py::arg("bias"), py::arg("residual"), py::arg("w"),
-        py::arg("b"), py::arg("out"), py::arg("mode"), py::arg("eps"),
-        "fused all-reduce, reduce half: wait for peers, sum slots, + bias + residual, optional norm");
+        py::arg("b"), py::arg("out"), py::arg("mode"), py::arg("eps"), py::arg("spin_limit") = 0,
+        py::arg("err") = py::none(),
+        "fused all-reduce, reduce half: poll the slots, sum in rank order, + bias + residual, optional norm");
+  m.def("symm_fill_u16", [](int64_t p, int64_t count, int64_t value) {
+    vrm::symm_fill_u16(reinterpret_cast<void*>(p), (size_t)count, (uint16_t)value);
+  });
   m.def("symm_malloc", [](int64_t bytes) { return (int64_t)reinterpret_cast<uintptr_t>(vrm::symm_malloc(bytes)); });
   m.def("symm_free", [](int64_t p) { vrm::symm_free(reinterpret_cast<void*>(p)); });
   m.def("ipc_handle", [](int64_t p) {

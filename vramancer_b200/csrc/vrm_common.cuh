@@ -352,4 +352,31 @@ __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Data-polled ("empty pattern") exchange of bf16 values between GPUs: a free receive
+// slot holds 0x8000 (bf16 -0.0) in every element; a producer stores finished values
+// with -0.0 turned into +0.0 (numerically the same), so a reader knows an element has
+// arrived as soon as it differs from 0x8000, without a flag or a fence.
+constexpr uint32_t kBf16Empty = 0x8000u;
+constexpr uint32_t kBf16EmptyX2 = 0x80008000u;
+__device__ __forceinline__ uint16_t bf16_bits_nonempty(float v) {
+  const uint16_t b = __bfloat16_as_ushort(__float2bfloat16(v));
+  return b == (uint16_t)kBf16Empty ? (uint16_t)0 : b;
+}
+__device__ __forceinline__ void st_relaxed_sys_u16(void* p, uint16_t v) {
+  asm volatile("st.relaxed.sys.global.b16 [%0], %1;" ::"l"(p), "h"(v) : "memory");
+}
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+// true when any of the 8 bf16 lanes of x still holds the empty pattern
+__device__ __forceinline__ bool bf16x8_has_empty(uint4 x) {
+  auto e = [](uint32_t w) { return (w & 0xffffu) == kBf16Empty || (w >> 16) == kBf16Empty; };
+  return e(x.x) || e(x.y) || e(x.z) || e(x.w);
+}
+
 }  // namespace vrm

@@ -2,6 +2,7 @@
 #include "vrm_host.h"
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 
@@ -21,6 +22,13 @@ struct DeviceScratch {
 
 std::mutex g_mu;
 DeviceScratch g_dev[kMaxDevices];
+std::atomic<uint64_t> g_allocs{0};
+
+// every device allocation of the host services goes through here (counted)
+cudaError_t counted_malloc(void** p, size_t bytes) {
+  g_allocs.fetch_add(1, std::memory_order_relaxed);
+  return cudaMalloc(p, bytes);
+}
 
 int current_device() {
   int d = 0;
@@ -53,7 +61,7 @@ uint32_t* error_word() {
   const int d = current_device();
   std::lock_guard<std::mutex> g(g_mu);
   if (!g_dev[d].err) {
-    VRM_CUDA_CHECK(cudaMalloc(&g_dev[d].err, sizeof(uint32_t)));
+    VRM_CUDA_CHECK(counted_malloc(reinterpret_cast<void**>(&g_dev[d].err), sizeof(uint32_t)));
     VRM_CUDA_CHECK(cudaMemset(g_dev[d].err, 0, sizeof(uint32_t)));
   }
   return g_dev[d].err;
@@ -77,7 +85,7 @@ void* workspace_get(size_t bytes, cudaStream_t stream) {
                 "workspace too small during CUDA graph capture; reserve_workspace() before capture");
     size_t sz = std::max(bytes, (size_t)32 << 20);
     void* p = nullptr;
-    VRM_CUDA_CHECK(cudaMalloc(&p, sz));
+    VRM_CUDA_CHECK(counted_malloc(&p, sz));
     // the old buffer is intentionally kept: captured graphs may still use it
     s.ws = p;
     s.ws_bytes = sz;
@@ -103,7 +111,7 @@ uint32_t* tile_counters_get(cudaStream_t stream) {
   DeviceScratch& s = g_dev[d];
   if (!s.counters) {
     VRM_REQUIRE(!capturing(stream), "tile counters must be created before CUDA graph capture");
-    VRM_CUDA_CHECK(cudaMalloc(&s.counters, kCounterCount * sizeof(uint32_t)));
+    VRM_CUDA_CHECK(counted_malloc(reinterpret_cast<void**>(&s.counters), kCounterCount * sizeof(uint32_t)));
     VRM_CUDA_CHECK(cudaMemset(s.counters, 0, kCounterCount * sizeof(uint32_t)));
   }
   return s.counters;
@@ -123,5 +131,7 @@ int device_sm_count() {
   if (g_dev[d].sms == 0) VRM_CUDA_CHECK(cudaDeviceGetAttribute(&g_dev[d].sms, cudaDevAttrMultiProcessorCount, d));
   return g_dev[d].sms;
 }
+
+uint64_t device_allocations() { return g_allocs.load(std::memory_order_relaxed); }
 
 }  // namespace vrm

@@ -54,6 +54,10 @@ uint32_t* tile_counters_get(cudaStream_t stream);
 
 int device_sm_count();
 
+// Number of device allocations (cudaMalloc) this library's host services have made in
+// this process, all devices together.
+uint64_t device_allocations();
+
 // Programmatic dependent launch on/off (env VRM_PDL, default on).
 bool pdl_enabled();
 

@@ -49,23 +49,18 @@ struct GemmArgs {
   float norm_eps = 0.f;
 };
 
-// Push half of the fused tensor-parallel all-reduce.  Every rank owns a receive
-// buffer [2 halves][world source ranks][half_floats] bf16 and flags [world source
-// ranks] (cudaMalloc + CUDA IPC, symm.cu).  The row-parallel GEMM stores its fp32
-// partial Y[m, n] at m * N + n of its own slot on every rank, then its last CTA
-// advances *epoch and release-stores it into each peer's flag for this rank.  Halves
-// alternate with the epoch's parity.  ar_norm (ar_norm.cu) is the reduce half.
+// Push half of the fused tensor-parallel all-reduce (one shot, data-polled).  Every
+// rank owns a receive buffer [2 halves][world source ranks][half_floats] bf16
+// (cudaMalloc + CUDA IPC, symm.cu) whose free slots hold the "empty" pattern 0x8000
+// (bf16 -0.0).  The row-parallel GEMM stores its partial Y[m, n] (rounded to bf16, a
+// -0.0 stored as +0.0) at m * N + n of its own slot in half (*epoch & 1) on every rank:
+// plain posted stores, no fence and no flag.  ar_norm (ar_norm.cu) polls the values
+// themselves until none is empty, then empties the slots again and advances *epoch.
 struct ARPush {
   __nv_bfloat16* const* xbuf = nullptr;  // device array [world] of the ranks' receive buffers
-  uint32_t* const* flags = nullptr;  // device array [world] of the ranks' flag arrays
-  uint32_t* epoch = nullptr;         // this rank's call counter (device)
-  uint32_t* done = nullptr;          // this rank's CTA completion counter (device, zero)
+  const uint32_t* epoch = nullptr;       // this rank's call counter (device, advanced by ar_norm)
   int rank = 0, world = 1;
-  long long half_floats = 0;         // elements per (half, source rank) slot
-  // 1: every epilogue thread fences its own remote stores at system scope before the
-  // CTA barrier; 0: one system-scope fence by the flagging thread after the barrier
-  // (release cumulativity over the barrier)
-  int per_thread_fence = 0;
+  long long half_floats = 0;             // elements per (half, source rank) slot
 };
 void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
 // FP8 W8A8: x, w are e4m3 bytes ([M, K], [N, K], strides in bytes); y = (x w^T) *
@@ -230,9 +225,9 @@ void layernorm(const void* x, int64_t ldx, void* residual, const void* w, const 
 // Every rank sums the same values in the same order: identical results on all ranks.
 enum ArNormMode { kArAdd = 0, kArRmsNorm = 1, kArLayerNorm = 2 };
 struct ARNormArgs {
-  const __nv_bfloat16* xbuf = nullptr;   // this rank's receive buffer
-  const uint32_t* flags = nullptr;   // this rank's flags [world]
-  const uint32_t* epoch = nullptr;   // this rank's call counter (advanced by the GEMM)
+  __nv_bfloat16* xbuf = nullptr;     // this rank's receive buffer (emptied after reading)
+  uint32_t* epoch = nullptr;         // this rank's call counter (advanced here)
+  uint32_t* done = nullptr;          // zeroed CTA completion counter (device)
   int rank = 0, world = 1;
   long long half_floats = 0;
   int T = 0, H = 0;
@@ -244,6 +239,10 @@ struct ARNormArgs {
   int64_t ldo = 0;
   int mode = kArAdd;
   float eps = 1e-6f;
+  // clock cycles one CTA polls for missing values before it reports kErrFlagTimeout
+  // (missing values count as 0); 0 = the library default (about one second)
+  unsigned long long spin_limit = 0;
+  uint32_t* err = nullptr;           // null = the per-device error word
 };
 void ar_norm(const ARNormArgs& a, cudaStream_t stream);
 
@@ -269,6 +268,10 @@ struct Nvfp4GemmArgs {
   int64_t ldo = 0;
   int M = 0, N = 0, K = 0;
   int epilogue = kEpiNone;
+  // fused all-reduce push (push != 0): the partial (times the per-tensor scale, no bias
+  // or residual) goes to this rank's slot of every rank's receive buffer instead of out
+  int push = 0;
+  ARPush ar;
 };
 void nvfp4_gemm(const Nvfp4GemmArgs& a, cudaStream_t stream);
 int nvfp4_gemm_max_m();
@@ -333,6 +336,9 @@ struct DecodeAttnArgs {
   const float* cos_sin = nullptr;      // [max_pos, rot_dim] or null (no rotation)
   int rot_dim = 0;                     // must equal D when cos_sin is given
   const int* slot_mapping = nullptr;   // [B], -1 = no write
+  // device word that bounds / timeout errors are OR-ed into; null -> the per-device
+  // error word (error_word())
+  uint32_t* err = nullptr;
 };
 void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t stream);
 // Selects the persistent TMA decode kernel for bf16 pages (default off, VRM_DECODE_TMA=1).
@@ -368,6 +374,8 @@ void sample_rows(const void* logits, int64_t ld, int B, int V, const float* temp
 // ---------------------------------------------------------------- symmetric buffers (symm.cu)
 void* symm_malloc(size_t bytes);
 void symm_free(void* p);
+// Fills count 16-bit words at p (current device) with value and waits for it.
+void symm_fill_u16(void* p, size_t count, uint16_t value);
 std::vector<uint8_t> ipc_handle(void* p);
 void* ipc_open(const std::vector<uint8_t>& bytes);
 void ipc_close(void* p);

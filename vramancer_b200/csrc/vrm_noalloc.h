@@ -15,9 +15,13 @@
  *   - a request whose split partials need more scratch than that is rejected with a
  *     non-zero return code and a message from vrm_noalloc_last_error(); with
  *     num_splits <= 0 the split count is chosen automatically and lowered until it
- *     fits (one split needs no scratch at all);
- *   - the first call on a device resolves the scratch address on that device (with
- *     it current); make that first call before any stream capture;
+ *     fits (one split needs no scratch at all); an explicit num_splits above 128 is
+ *     rejected the same way;
+ *   - the first call on a device (vrm_noalloc_setup(), or else the first decode
+ *     call) resolves the scratch address on that device (with it current); make that
+ *     first call before any stream capture;
+ *   - errors that the kernel's bounded waits and bounds checks detect go to a static
+ *     error word of this entry point, read with vrm_noalloc_read_and_clear_errors();
  *   - all calls share the one scratch array and it keeps the last call's contents:
  *     calls that overlap on the GPU (different streams, or threads without ordering)
  *     race with each other and must be serialised by the caller;
@@ -48,6 +52,19 @@ int vrm_paged_attention_decode_noalloc(const void* q, int64_t ld_q, const void* 
                                        const int* context_lens, const float* kv_scale, float sm_scale,
                                        void* out, int64_t ld_out, int batch, int max_pages, int num_splits,
                                        cudaStream_t stream);
+
+/* Resolves the scratch of the current device ahead of the first decode call (for
+ * example before a stream capture).  Returns 0 on success. */
+int vrm_noalloc_setup(void);
+
+/* Synchronises the current device, stores the error bits the allocation-free calls
+ * reported since the last read into *flags (0 = none) and clears them.  Returns 0
+ * on success. */
+int vrm_noalloc_read_and_clear_errors(uint32_t* flags);
+
+/* Device allocations the library's host services have made so far in this process
+ * (a check for callers and tests that the calls above add none). */
+uint64_t vrm_host_device_allocations(void);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* vrm_noalloc_last_error(void);

@@ -5,7 +5,7 @@
 Builds the model with random weights, prefills `batch` prompts, then runs `steps`
 eager decode steps (no CUDA graph, so every kernel is a separate launch) inside the
 NVTX range "vrm_decode"; capture them with
-    ncu --nvtx --nvtx-include "vrm_decode/" --metrics gpu__time_duration.sum ...
+    ncu --clock-control none --nvtx --nvtx-include "vrm_decode/" --metrics gpu__time_duration.sum ...
 With --ablate it prints, per op type, how much of the graph-replayed decode step that
 op costs on the critical path: the step is re-captured with the op replaced by a no-op
 (its output buffer still allocated) and the CUDA-event step times are compared.  Unlike

@@ -175,6 +175,10 @@ PRESETS: Dict[str, ModelConfig] = {
     "tiny-qwen2-d128": ModelConfig(arch="qwen2", vocab_size=1024, hidden_size=512, num_layers=2, num_heads=8,
                                    num_kv_heads=2, head_dim=128, intermediate_size=1024, max_position=4096,
                                    norm_eps=1e-6, rope_theta=1_000_000.0, qkv_bias=True, name="tiny-qwen2-d128"),
+    # every head count, the FFN and the vocabulary divide over 8 tensor-parallel ranks
+    "tiny-qwen2-tp8": ModelConfig(arch="qwen2", vocab_size=4096, hidden_size=1024, num_layers=2, num_heads=8,
+                                  num_kv_heads=8, head_dim=128, intermediate_size=2048, max_position=4096,
+                                  norm_eps=1e-6, rope_theta=1_000_000.0, qkv_bias=True, name="tiny-qwen2-tp8"),
     "tiny-gpt2": ModelConfig(arch="gpt2", vocab_size=500, hidden_size=128, num_layers=4, num_heads=2,
                              num_kv_heads=2, head_dim=64, intermediate_size=512, max_position=512, norm_eps=1e-5,
                              rope_theta=0.0, qkv_bias=True, tie_embeddings=True, name="tiny-gpt2"),

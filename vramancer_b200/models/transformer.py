@@ -211,10 +211,11 @@ class DecoderModel:
             ops.linear(x, w, b, residual=r, out=r)
             return self._norm(r, nxt[0] if nxt[0] is not None else "final", nxt[1]) if nxt else None
         far = self.tp.fused_ar
-        if far is not None and x.is_cuda and getattr(w, "_vrm_quant", None) is None and far.supports(x.shape[0], w.shape[0]):
-            # push the partial to every rank, then one kernel: reduce + bias + residual + norm
+        if far is not None and x.is_cuda and far.supports_weight(x.shape[0], w):
+            # push the partial to every rank (bf16, fp8 or NVFP4 weights), then one
+            # kernel: reduce + bias + residual + norm
             T, H = x.shape[0], w.shape[0]
-            far.push(x, w)
+            far.push_weight(x, w)
             if not nxt:
                 far.reduce(T, H, bias=b, residual=r)
                 return None
