@@ -58,6 +58,8 @@ def parse_args(argv=None):
                    help="weight format (the headline is bf16; these are extra measurements)")
     p.add_argument("--parallel", choices=["dp", "tp"], default="tp",
                    help="N > 1: headline at TP=N (default) or on N data-parallel replicas")
+    p.add_argument("--shard-of", type=int, default=0,
+                   help="debug only: one GPU runs rank 0's shard of a TP=N model without its peers (invalid run)")
     p.add_argument("--no-extras", action="store_true",
                    help="N > 1: skip the data-parallel figure and the TP numeric check")
     return p.parse_args(argv)
@@ -278,6 +280,9 @@ def run_ours(args):
 
     sampler = ClockSampler(info.local_rank) if rank == 0 else None
     tp = comm.tp_context()
+    if args.shard_of > 1 and world == 1:
+        from vramancer_b200.parallel.tp_emulate import shard_context
+        tp = shard_context(args.shard_of, str(dev))
     dpres = tpres = check = None
     if world == 1 or mode == "tp":
         main = measure(tp, clocks=sampler)
@@ -346,6 +351,8 @@ def run_ours(args):
         res["tp_check"] = check
     if args.num_layers:
         res["invalid"] = "truncated model (--num-layers): debugging only"
+    if args.shard_of > 1 and world == 1:
+        res["invalid"] = f"rank 0's shard of TP={args.shard_of} without its peers (--shard-of): debugging only"
     comm.barrier()
     if rank == 0:
         print(json.dumps(res), flush=True)

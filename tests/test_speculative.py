@@ -152,6 +152,38 @@ def test_draft_model_sampling_with_an_identical_draft_accepts_everything():
     assert dec.stats.proposed > 0 and dec.stats.acceptance > 0.9
 
 
+def test_draft_with_a_different_vocabulary_size():
+    """A draft whose vocabulary is padded larger (or smaller) than the target's: greedy
+    drafts stop at ids the target lacks, sampled drafts only propose the target's ids,
+    and the output still follows the target (greedy: exactly)."""
+    from vramancer_b200.engine.speculative import DraftModelDecoder
+    g = torch.Generator().manual_seed(11)
+    p = torch.randint(0, 500, (10,), generator=g).tolist()
+    plain, cfg = _llm()
+    ref = plain.generate([p], SamplingParams(max_tokens=16))[0].output_ids
+    for dv in (cfg.vocab_size + 64, cfg.vocab_size - 12):
+        dcfg = cfg.with_(vocab_size=dv)
+        dw = random_weights(dcfg, device="cpu", dtype=torch.float32, seed=5, std=0.2)
+        drafter = LLM(dcfg, device="cpu", dtype=torch.float32, kv_cache_dtype="fp32", weights=dw, max_batch=4,
+                      max_model_len=512, kv_pages=128)
+        target, _ = _llm()
+        dec = DraftModelDecoder(target, drafter, gamma=4, adaptive=False)
+        assert dec.generate(p, 16) == ref
+        out = dec.generate(p, 12, params=SamplingParams(max_tokens=12, temperature=0.9, top_k=50), seed=2)
+        assert len(out) == 12 and all(0 <= t < cfg.vocab_size for t in out)
+
+
+def test_draft_probs_wider_than_target_are_aligned():
+    from vramancer_b200.engine.speculative import accept_with_draft_probs
+    p = torch.tensor([[0.5, 0.3, 0.2], [0.2, 0.3, 0.5]])
+    q = torch.tensor([[0.4, 0.3, 0.2, 0.1]])          # one padded id the target lacks
+    gen = torch.Generator().manual_seed(0)
+    toks, kept = accept_with_draft_probs([1], p, q, gen)
+    assert all(t < 3 for t in toks)
+    toks, kept = accept_with_draft_probs([3], p, q, gen)
+    assert kept == 0 and toks[0] < 3
+
+
 @pytest.mark.gpu
 def test_prompt_lookup_on_gpu_greedy_and_sampled(cuda_errors_clean):
     """Speculation through the CUDA kernels (verify = paged prefill forward): greedy and

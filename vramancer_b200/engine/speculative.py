@@ -109,8 +109,19 @@ def accept_with_draft_probs(draft: Sequence[int], probs: torch.Tensor, qprobs: t
     norm(max(0, p_i - q_i)) and stop; after every draft is kept, draw from p_k."""
     probs = probs.float().cpu()
     qprobs = qprobs.float().cpu()
+    V = probs.shape[-1]
+    if qprobs.shape[-1] != V:
+        # draft and target vocabularies differ in padding: the draft's mass on ids the
+        # target does not have is dropped (such ids are never proposed) and q renormalised
+        q2 = torch.zeros(qprobs.shape[0], V)
+        n = min(V, qprobs.shape[-1])
+        q2[:, :n] = qprobs[:, :n]
+        qprobs = q2 / q2.sum(-1, keepdim=True).clamp_min(1e-30)
     out: List[int] = []
     for i, d in enumerate(draft):
+        if int(d) >= V:
+            out.append(int(torch.multinomial(probs[i], 1, generator=gen)))
+            return out, i
         p, q = probs[i], qprobs[i]
         d = int(d)
         u = float(torch.rand((), generator=gen))
@@ -278,22 +289,39 @@ class DraftModelDecoder:
         self.recent: List[float] = []
         self.stats = SpecStats()
 
+    @property
+    def target_vocab(self) -> int:
+        return self.target.cfg.vocab_size
+
     def _propose(self, seq: List[int], k: int) -> List[int]:
         from .engine import SamplingParams
         r = self.draft.engine.generate([seq], SamplingParams(max_tokens=k))[0]
-        return r.output_ids
+        out = []
+        for t in r.output_ids:      # an id the target's vocabulary lacks ends the draft
+            if t >= self.target_vocab:
+                break
+            out.append(t)
+        return out
 
     def _propose_sampled(self, seq: List[int], k: int, params, gen: torch.Generator):
         """k draft tokens drawn from the draft model's filtered distributions (same
-        temperature / top-k / top-p as the request); returns (tokens, q rows [k, V])."""
-        runner = self.draft.runner
+        temperature / top-k / top-p as the request), over the target's vocabulary (draft
+        logits of ids the target lacks are masked, missing ids get none); returns
+        (tokens, q rows [k, V_target])."""
         toks: List[int] = []
         rows = []
         cur = list(seq)
+        V = self.target_vocab
         for _ in range(k):
             if len(cur) + 1 > self.draft.engine.max_model_len:
                 break
             logits = _full_logits(self.draft, cur)
+            if logits.shape[-1] > V:
+                logits = logits[..., :V]
+            elif logits.shape[-1] < V:
+                pad = torch.full((*logits.shape[:-1], V - logits.shape[-1]), float("-inf"), dtype=logits.dtype,
+                                 device=logits.device)
+                logits = torch.cat([logits, pad], dim=-1)
             q = filtered_probs(logits, params.temperature, params.top_k, params.top_p)[0]
             t = int(torch.multinomial(q.cpu(), 1, generator=gen))
             toks.append(t)

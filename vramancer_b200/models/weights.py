@@ -337,7 +337,13 @@ def save_safetensors(weights: Weights, cfg: ModelConfig, path: str) -> None:
             nw = getattr(t, "_vrm_norm_w", None)
             if nw is not None:
                 # folded RMSNorm weight (LLM(fold_norms=True)): write the checkpoint's matrix
-                t = (t.float() / nw.float().view(1, -1)).to(t.dtype)
+                # back.  The bf16 multiply-then-divide is not bit-exact (a last-bit
+                # difference per element is possible); a column whose norm weight is 0 was
+                # zeroed by the fold and is written as 0, which gives the same model
+                # output since that column is multiplied by the 0 norm weight anyway.
+                d = nw.float().view(1, -1)
+                tf = t.float()
+                t = torch.where(d == 0, torch.zeros_like(tf), tf / torch.where(d == 0, torch.ones_like(d), d)).to(t.dtype)
             if n in ("qkv_w", "qkv_b"):
                 q, kk, v = torch.split(t, [cfg.q_size, cfg.kv_size, cfg.kv_size], 0)
                 suf = "weight" if n == "qkv_w" else "bias"

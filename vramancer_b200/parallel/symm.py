@@ -35,10 +35,14 @@ EMPTY_BF16 = 0x8000
 
 
 class FusedAllReduce:
-    def __init__(self, group=None, max_tokens: int = 128, max_features: int = 16384, device=None):
+    def __init__(self, group=None, max_tokens: int = 128, max_features: int = 16384, device=None,
+                 local: bool = False):
+        """`local=True` builds a one-rank instance without a process group: the kernels
+        run exactly as on a tensor-parallel rank, with only this GPU's slot (used to
+        time a TP shard's compute on one GPU)."""
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.world = 1 if local else dist.get_world_size(group)
+        self.rank = 0 if local else dist.get_rank(group)
         if self.world not in (1, 2, 4, 8):
             raise ValueError("fused all-reduce: world size must be 1, 2, 4 or 8")
         self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
@@ -51,9 +55,11 @@ class FusedAllReduce:
             n = 2 * self.world * self.half_floats
             self.xbuf = nat.symm_malloc(n * 2)
             nat.symm_fill_u16(self.xbuf, n, EMPTY_BF16)
-            handles = [nat.ipc_handle(self.xbuf)]
-            allh = [None] * self.world
-            dist.all_gather_object(allh, handles, group=group)
+            handles = [nat.ipc_handle(self.xbuf)] if not local else [None]
+            allh = [handles]
+            if not local:
+                allh = [None] * self.world
+                dist.all_gather_object(allh, handles, group=group)
             xs = []
             self._opened = []
             for r, (hx,) in enumerate(allh):
@@ -66,7 +72,8 @@ class FusedAllReduce:
             self.xbuf_ptrs = torch.tensor(xs, dtype=torch.int64, device=self.device)
             self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
             self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
-        dist.barrier(group=group)
+        if not local:
+            dist.barrier(group=group)
 
     def supports(self, m: int, n: int) -> bool:
         return self.min_tokens <= m <= self.max_tokens and n % 8 == 0 and n * m <= self.half_floats \

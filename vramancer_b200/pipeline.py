@@ -306,10 +306,13 @@ class InferencePipeline:
         if not stop or self._bcast is not None:
             return None
         ids: List[int] = []
-        # a stop string of n characters spans at most n tokens: checking the text of the
-        # last n + 4 tokens at every token finds it as soon as it is complete, at a cost
-        # independent of the output length (this runs inside the engine step)
-        window = max(len(x) for x in stop) + 4
+        # a stop string of n UTF-8 bytes spans at most n tokens that each decode to at
+        # least one byte; byte-level BPE can also emit tokens that decode to nothing on
+        # their own (a partial multi-byte character), so allow up to 4 tokens per byte.
+        # Checking the text of that many last tokens at every token finds the stop
+        # string as soon as it is complete, at a cost independent of the output length
+        # (this runs inside the engine step)
+        window = 4 * max(len(x.encode("utf-8")) for x in stop) + 4
 
         def on_tok(req, tok):
             ids.append(tok)

@@ -7,10 +7,14 @@ Routes
   operations  GET /health /ready /live /metrics /api/status /api/gpu /api/gpu/info
               /api/system /api/pipeline/status /api/queue/status /api/batcher/stats
               /api/history /api/nodes; POST /api/benchmark; GET /chat, /dashboard
-Protection: bearer token (VRM_API_TOKEN), optional HMAC signatures
-(VRM_HMAC_SECRET), per-IP rate limit, body cap, read-only mode, audit log; 400 on
-validation / context overflow, 401 auth, 413 body, 429 queue or rate, 503 circuit
-open or no model, 504 timeout.
+  accounts    POST /api/auth/login, /api/auth/refresh, /api/auth/change-password;
+              GET /api/auth/me; GET / POST /api/auth/users (admin)
+Protection: JWT access tokens with roles user < ops < admin (serving/auth.py) or the
+static bearer token (VRM_API_TOKEN, admin), per-route minimum roles, CORS origin
+policy (VRM_CORS_ORIGINS), optional HMAC signatures (VRM_HMAC_SECRET), per-IP rate
+limit, body cap, read-only mode, audit log; 400 on validation / context overflow,
+401 auth, 403 role or origin, 413 body, 429 queue or rate, 503 circuit open or no
+model, 504 timeout.
 
 Reference parity: core/production_api.py:156-1556 (Flask app, routes, SSE, queue
 counter, circuit breaker, timeouts), core/api/routes_ops.py:23-375,
@@ -20,6 +24,7 @@ surface is served with FastAPI/uvicorn.
 from __future__ import annotations
 
 import asyncio
+import hmac
 import json
 import os
 import time
@@ -30,11 +35,12 @@ from typing import Any, Dict, List, Optional
 
 import torch
 from fastapi import FastAPI, Request
-from fastapi.responses import HTMLResponse, JSONResponse, PlainTextResponse, StreamingResponse
+from fastapi.responses import HTMLResponse, JSONResponse, PlainTextResponse, Response, StreamingResponse
 
 from ..utils.config import flags
 from ..utils.monitor import GPUMonitor, health_report, system_info
 from ..utils.observability import METRICS, get_logger
+from .auth import Auth, AuthError, CorsPolicy, required_role, role_allows
 from .security import (AuditLog, CircuitBreaker, QueueCounter, RateLimiter, ValidationError, startup_checks,
                        validate_generation_params, verify_signature)
 from .tool_calls import build_chat_message, build_chat_prompt
@@ -42,6 +48,7 @@ from .tool_calls import build_chat_message, build_chat_prompt
 log = get_logger("vramancer.api")
 
 PUBLIC = {"/health", "/ready", "/live", "/metrics", "/", "/chat", "/dashboard"}
+AUTH_OPEN = {"/api/auth/login", "/api/auth/refresh"}     # credentials travel in the body
 
 
 def _err(status: int, message: str, etype: str = "invalid_request_error", code: Optional[str] = None):
@@ -79,6 +86,11 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
     limiter = RateLimiter(int(flags.VRM_RATE_LIMIT_RPM))
     queue = QueueCounter(int(flags.VRM_MAX_QUEUE))
     audit = AuditLog()
+    auth = Auth()
+    cors = CorsPolicy()
+    if os.environ.get("VRM_DEFAULT_ADMIN_PASS"):
+        auth.ensure_default_admin(production=bool(flags.VRM_PRODUCTION))
+    app.state.auth, app.state.cors = auth, cors
     executor = ThreadPoolExecutor(max_workers=max(1, int(flags.VRM_MAX_CONCURRENT)) * 8,
                                   thread_name_prefix="vrm-api")
     monitor = GPUMonitor()
@@ -91,21 +103,48 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
         return model_alias or flags.VRM_MODEL_ALIAS or (p.model_name if p else "none")
 
     # ------------------------------------------------------------------ middleware
+    def resolve_role(request: Request) -> Optional[str]:
+        """Role of the caller: JWT access token -> its role; the static API token ->
+        admin; nothing configured (development) -> admin; else None (401)."""
+        token = os.environ.get("VRM_API_TOKEN", "")
+        authz = request.headers.get("authorization", "")
+        cred = authz[7:] if authz.startswith("Bearer ") else request.headers.get("x-api-key", "")
+        if cred:
+            claims = auth.access_claims(cred)
+            if claims is not None:
+                request.state.user = claims["sub"]
+                return claims.get("role", "user")
+            if token and hmac.compare_digest(cred, token):
+                request.state.user = "api-token"
+                return "admin"
+        if not token and not auth.configured:
+            request.state.user = "anonymous"
+            return "admin"
+        return None
+
     @app.middleware("http")
     async def protect(request: Request, call_next):
         path = request.url.path
         client = request.client.host if request.client else "?"
+        origin = request.headers.get("origin")
+        if not cors.allowed(origin):
+            audit.log(client, request.method, path, 403, f"forbidden origin {origin}")
+            return _err(403, "forbidden origin", "permission_error")
+        if request.method == "OPTIONS" and origin:
+            return Response(status_code=204, headers=cors.headers(origin))
         cl = request.headers.get("content-length")
         if cl and int(cl) > int(flags.VRM_MAX_BODY_BYTES):
             return _err(413, "request body too large")
-        if path not in PUBLIC:
-            token = os.environ.get("VRM_API_TOKEN", "")
-            if token:
-                auth = request.headers.get("authorization", "")
-                key = request.headers.get("x-api-key", "")
-                if auth != f"Bearer {token}" and key != token:
-                    audit.log(client, request.method, path, 401)
-                    return _err(401, "invalid or missing API token", "authentication_error")
+        if path not in PUBLIC and path not in AUTH_OPEN:
+            role = resolve_role(request)
+            if role is None:
+                audit.log(client, request.method, path, 401)
+                return _err(401, "invalid or missing API token", "authentication_error")
+            request.state.role = role
+            need = required_role(request.method, path)
+            if need and not role_allows(role, need):
+                audit.log(client, request.method, path, 403, f"role {role} < {need}")
+                return _err(403, f"role '{need}' required", "permission_error")
             secret = os.environ.get("VRM_HMAC_SECRET", "")
             if secret and request.method == "POST":
                 body = await request.body()
@@ -120,7 +159,54 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
         resp = await call_next(request)
         if path not in PUBLIC:
             audit.log(client, request.method, path, resp.status_code)
+        for k, v in cors.headers(origin).items():
+            resp.headers[k] = v
         return resp
+
+    # ------------------------------------------------------------------ accounts
+    @app.post("/api/auth/login")
+    async def auth_login(request: Request):
+        body = await request.json()
+        try:
+            return auth.login(str(body.get("username", "")), str(body.get("password", "")))
+        except AuthError as e:
+            return _err(401, str(e), "authentication_error")
+
+    @app.post("/api/auth/refresh")
+    async def auth_refresh(request: Request):
+        body = await request.json()
+        try:
+            return auth.refresh(str(body.get("refresh", "")))
+        except (AuthError, ValueError) as e:
+            return _err(401, str(e), "authentication_error")
+
+    @app.get("/api/auth/me")
+    async def auth_me(request: Request):
+        return {"user": getattr(request.state, "user", None), "role": getattr(request.state, "role", None)}
+
+    @app.post("/api/auth/change-password")
+    async def auth_change_password(request: Request):
+        body = await request.json()
+        user = str(body.get("username") or getattr(request.state, "user", ""))
+        if user != getattr(request.state, "user", None) and request.state.role != "admin":
+            return _err(403, "only an admin changes another user's password", "permission_error")
+        if not auth.change_password(user, str(body.get("old_password", "")), str(body.get("new_password", ""))):
+            return _err(401, "invalid credentials", "authentication_error")
+        return {"ok": True}
+
+    @app.get("/api/auth/users")
+    async def auth_list_users():
+        return {"users": [{"username": u.username, "role": u.role} for u in auth.users.values()]}
+
+    @app.post("/api/auth/users")
+    async def auth_create_user(request: Request):
+        body = await request.json()
+        try:
+            u = auth.create_user(str(body.get("username", "")), str(body.get("password", "")),
+                                 str(body.get("role", "user")))
+        except AuthError as e:
+            return _err(400, str(e))
+        return {"username": u.username, "role": u.role}
 
     # ------------------------------------------------------------------ helpers
     def run_guarded(fn, timeout: float):
