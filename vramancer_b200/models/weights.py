@@ -244,24 +244,72 @@ def _hf_map(cfg: ModelConfig, name: str) -> Optional[Tuple[str, str]]:
     return None
 
 
+# quantised-tensor suffixes of one HF linear module: the reference's DirectFP4Linear
+# buffers and ModelOpt-style NVFP4 tensors (quant/nvfp4_io.py)
+_NVFP4_SUFFIX = {"w_qdata": "codes", "w_scale": "atoms", "w_per_tensor_scale": "gs", "w_scale_row": "scale_row",
+                 "weight_scale": "scale_rm", "weight_scale_2": "gs", "input_scale": None}
+
+
+def _tp_slice(cfg: ModelConfig, iname: str, role: str, shape, rank: int, size: int):
+    """(rows, cols) slices of an HF tensor that this tensor-parallel rank keeps, or None
+    (read whole).  Fused q/k/v and gate/up are sliced per part, so assembling the
+    parts gives shard_tensor's result of the fused tensor."""
+    if size == 1 or cfg.is_gpt2:
+        return None
+    base = iname.split(".")[-1]
+    D = cfg.head_dim
+    if base in ("qkv_w", "qkv_b"):
+        if role == "q":
+            hq = cfg.num_heads // size
+            return slice(rank * hq * D, (rank + 1) * hq * D), None
+        if cfg.num_kv_heads >= size:
+            kvh = cfg.num_kv_heads // size
+            return slice(rank * kvh * D, (rank + 1) * kvh * D), None
+        grp = (rank * cfg.num_kv_heads) // size
+        return slice(grp * D, (grp + 1) * D), None
+    if base in ("gate_up_w", "shared_gate_up_w") and role in ("gate", "up"):
+        n = shape[0] // size
+        return slice(rank * n, (rank + 1) * n), None
+    if base in ("o_w", "down_w", "shared_down_w") and len(shape) == 2:
+        n = shape[1] // size
+        return None, slice(rank * n, (rank + 1) * n)
+    if base == "lm_head":
+        n = (shape[0] + size - 1) // size
+        return slice(rank * n, min(shape[0], (rank + 1) * n)), None
+    return None
+
+
 def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.bfloat16,
                      layers: Optional[Iterable[int]] = None, embed: bool = True, head: bool = True,
                      tp_rank: int = 0, tp_size: int = 1, ep_rank: int = 0, ep_size: int = 1) -> Weights:
     """Reads an HF checkpoint directory (*.safetensors), keeping only the tensors this
-    stage / rank needs (this expert-parallel rank's experts with ep_size > 1), fusing
-    q/k/v and gate/up into the internal layout."""
+    stage / rank needs, fusing q/k/v and gate/up into the internal layout.
+
+    Tensor-parallel ranks read only their slices (safetensors get_slice), and
+    expert-parallel ranks only their experts, so no rank reads the whole checkpoint.
+    Projections stored NVFP4-quantised (the reference's DirectFP4Linear buffers
+    w_qdata / w_scale / w_per_tensor_scale, or ModelOpt weight / weight_scale /
+    weight_scale_2) load as NVFP4Weight without re-quantisation."""
     from safetensors import safe_open
 
     want_layers = set(range(cfg.num_layers) if layers is None else layers)
     files = sorted(f for f in os.listdir(path) if f.endswith(".safetensors"))
     if not files:
         raise FileNotFoundError(f"no .safetensors files in {path}")
+    n_exp = cfg.num_experts // ep_size if cfg.is_moe else 0
+    own_experts = set(range(ep_rank * n_exp, (ep_rank + 1) * n_exp))
     parts: Dict[str, Dict[str, torch.Tensor]] = {}
+    nv_parts: Dict[str, Dict[str, Dict[str, torch.Tensor]]] = {}
     out: Weights = {}
+    sharded = set()
     for fn in files:
         with safe_open(os.path.join(path, fn), framework="pt", device="cpu") as f:
             for name in f.keys():
-                m = _hf_map(cfg, name)
+                mod, _, leaf = name.rpartition(".")
+                nv_part = _NVFP4_SUFFIX.get(leaf, "") if leaf in _NVFP4_SUFFIX else ""
+                if nv_part is None:
+                    continue                     # activation scale: not used
+                m = _hf_map(cfg, mod + ".weight" if nv_part else name)
                 if m is None:
                     continue
                 iname, role = m
@@ -272,7 +320,22 @@ def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.b
                     continue
                 elif iname in ("final_norm_w", "final_norm_b", "lm_head") and not head:
                     continue
-                t = f.get_tensor(name)
+                if ":" in role and int(role.split(":")[1]) not in own_experts:
+                    continue                     # another expert-parallel rank's expert
+                sl = f.get_slice(name)
+                if not nv_part and sl.get_dtype() in ("U8", "I8") and leaf == "weight":
+                    nv_part = "codes_mo"         # ModelOpt packed e2m1 codes
+                if nv_part:
+                    nv_parts.setdefault(iname, {}).setdefault(role, {})[nv_part] = f.get_tensor(name)
+                    continue
+                cut = _tp_slice(cfg, iname, role, sl.get_shape(), tp_rank, tp_size)
+                if cut is None:
+                    t = f.get_tensor(name)
+                else:
+                    rows, cols = cut
+                    t = sl[rows] if cols is None else sl[:, cols]
+                    t = t.contiguous()
+                    sharded.add(iname)
                 if role == "conv1d":
                     t = t.t().contiguous()
                 if role == "copy":
@@ -286,13 +349,9 @@ def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.b
         elif base in ("gate_up_w", "shared_gate_up_w"):
             out[iname] = interleave_gate_up(p["gate"], p["up"])
         elif base == "experts_gate_up_w":
-            E = cfg.num_experts
-            n = E // ep_size
-            own = range(ep_rank * n, (ep_rank + 1) * n)
-            out[iname] = torch.stack([interleave_gate_up(p[f"egate:{e}"], p[f"eup:{e}"]) for e in own])
+            out[iname] = torch.stack([interleave_gate_up(p[f"egate:{e}"], p[f"eup:{e}"]) for e in sorted(own_experts)])
         elif base == "experts_down_w":
-            n = cfg.num_experts // ep_size
-            out[iname] = torch.stack([p[f"edown:{e}"] for e in range(ep_rank * n, (ep_rank + 1) * n)])
+            out[iname] = torch.stack([p[f"edown:{e}"] for e in sorted(own_experts)])
     if head and "lm_head" not in out and "embed" in out:
         out["lm_head"] = out["embed"]
     if not embed:
@@ -300,11 +359,23 @@ def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.b
         out.pop("pos_embed", None)
     res: Weights = {}
     for k, t in out.items():
-        if tp_size > 1:
+        if k == "lm_head" and k in sharded:
+            n = (cfg.vocab_size + tp_size - 1) // tp_size
+            if t.shape[0] < n:       # the last rank's slice is padded to the others' size
+                t = torch.cat([t, torch.zeros(n - t.shape[0], t.shape[1], dtype=t.dtype)], 0)
+        elif tp_size > 1 and k not in sharded:
             t = shard_tensor(cfg, k, t, tp_rank, tp_size)
         res[k] = t.to(device=device, dtype=dtype).contiguous()
     if "lm_head" in out and "embed" in out and out["lm_head"] is out["embed"] and tp_size == 1:
         res["lm_head"] = res["embed"]
+    if nv_parts:
+        from ..quant import nvfp4_io
+        for iname, per_role in nv_parts.items():
+            base = iname.split(".")[-1]
+            mods = {role: nvfp4_io.assemble(pp, f"{iname}:{role}") for role, pp in per_role.items()}
+            w = nvfp4_io.fuse_module_weights(base, mods)
+            w = nvfp4_io.shard_nvfp4(cfg, iname, w, tp_rank, tp_size)
+            res[iname] = nvfp4_io.from_rows(*nvfp4_io.rows_order(w), w.gs, device=device)
     return res
 
 
