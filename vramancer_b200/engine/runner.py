@@ -136,10 +136,14 @@ class ModelRunner:
     def _decode_body(self, B: int) -> None:
         batch = self._decode_batch(B)
         logits = self.model.forward(batch, self.pool)
-        if logits.device != self.device:          # pipeline: last stage on another GPU
-            logits = logits.to(self.device)
-        ops.sample(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.seed, self.d_steps[:B],
-                   out=self.d_out[:B])
+        if logits is not None:                    # None: a pipeline stage before the last
+            if logits.device != self.device:      # in-process pipeline: last stage on another GPU
+                logits = logits.to(self.device)
+            ops.sample(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.seed, self.d_steps[:B],
+                       out=self.d_out[:B])
+        share = getattr(self.model, "share_sampled", None)
+        if share is not None:                     # multi-process pipeline: every rank gets the ids
+            share(self.d_out[:B])
 
     def stage_decode_inputs(self, ids, positions, slots, ctx, block_tables: List[Sequence[int]],
                             temperature, top_k, top_p, steps) -> int:
@@ -305,14 +309,21 @@ class ModelRunner:
         logits = self.model.forward(batch, self.pool)
         if not rows:
             return [None] * B
-        if logits.device != dev:
-            logits = logits.to(dev)
         sel = [r for r, it in enumerate(items) if it.want_logits]
-        tt = torch.tensor([temperature[r] for r in sel], dtype=torch.float32)
-        tk = torch.tensor([top_k[r] for r in sel], dtype=torch.int32)
-        tp = torch.tensor([top_p[r] for r in sel], dtype=torch.float32)
-        st = torch.tensor([steps[r] for r in sel], dtype=torch.int32)
-        nxt = ops.sample(logits, tt.to(dev), tk.to(dev), tp.to(dev), self.seed, st.to(dev)).cpu().tolist()
+        if logits is not None:
+            if logits.device != dev:
+                logits = logits.to(dev)
+            tt = torch.tensor([temperature[r] for r in sel], dtype=torch.float32)
+            tk = torch.tensor([top_k[r] for r in sel], dtype=torch.int32)
+            tp = torch.tensor([top_p[r] for r in sel], dtype=torch.float32)
+            st = torch.tensor([steps[r] for r in sel], dtype=torch.int32)
+            nxt_t = ops.sample(logits, tt.to(dev), tk.to(dev), tp.to(dev), self.seed, st.to(dev))
+        else:                                     # a pipeline stage before the last
+            nxt_t = torch.zeros(len(sel), dtype=torch.int32, device=dev)
+        share = getattr(self.model, "share_sampled", None)
+        if share is not None:
+            share(nxt_t)
+        nxt = nxt_t.cpu().tolist()
         res: List[Optional[int]] = [None] * B
         for j, r in enumerate(sel):
             res[r] = nxt[j]

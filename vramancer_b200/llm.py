@@ -49,7 +49,8 @@ class LLM:
                  max_prefill_tokens: int = 8192, eos_token_id: Optional[int] = None, weights=None,
                  num_layers: Optional[int] = None, tp=None, quantization: Optional[str] = None,
                  spec_num_draft: int = 0, spec_ngram: int = 3, kv_offload_pages: int = 0, hierarchy=None,
-                 stream_layers: int = 0, ep=None, fold_norms: bool = True):
+                 stream_layers: int = 0, ep=None, fold_norms: bool = True, pp_grid=None,
+                 prefill_microbatches: int = 0, decode_microbatches: int = 1):
         if isinstance(model, ModelConfig):
             cfg = model
         else:
@@ -73,15 +74,21 @@ class LLM:
             raise ValueError("expert parallelism runs with data-parallel attention (tp must be 1)")
         self.ep = ep
         ep_rank, ep_size = (ep.rank, ep.world) if ep is not None else (0, 1)
+        # pipeline x tensor parallelism (parallel/pp.py): this rank's stage only
+        self.pp_grid = pp_grid
+        part = {}
+        if pp_grid is not None:
+            first, last = pp_grid.layers(cfg.num_layers)
+            part = dict(layers=range(first, last), embed=pp_grid.is_first, head=pp_grid.is_last)
         if weights is None:
             if isinstance(model, str) and _is_checkpoint_dir(model):
                 weights = load_safetensors(model, cfg, device=self.device, dtype=dtype, tp_rank=tp_rank,
-                                           tp_size=tp_size, ep_rank=ep_rank, ep_size=ep_size)
+                                           tp_size=tp_size, ep_rank=ep_rank, ep_size=ep_size, **part)
             else:
                 # streamed layers live in host memory: build them there
                 wdev = torch.device("cpu") if stream_layers > 0 else self.device
                 weights = random_weights(cfg, device=wdev, dtype=dtype, seed=seed, tp_rank=tp_rank,
-                                         tp_size=tp_size, ep_rank=ep_rank, ep_size=ep_size)
+                                         tp_size=tp_size, ep_rank=ep_rank, ep_size=ep_size, **part)
         self.quantization = (quantization or "").lower() or None
         if self.quantization == "nvfp4":
             from .quant.nvfp4 import quantize_model_weights
@@ -101,6 +108,11 @@ class LLM:
             self.model = StreamedDecoderModel(cfg, weights, budget_layers=stream_layers, device=self.device,
                                               dtype=dtype, tp=tp)
             use_cuda_graph = False
+        elif pp_grid is not None:
+            from .parallel.pp import PPStageModel
+            self.model = PPStageModel(cfg, weights, pp_grid, device=self.device, dtype=dtype, tp=tp,
+                                      prefill_microbatches=prefill_microbatches,
+                                      decode_microbatches=decode_microbatches)
         else:
             self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype, tp=tp, ep=ep)
             if (fold_norms and self.quantization is None and ep is None and (tp is None or tp.size == 1)
@@ -110,7 +122,7 @@ class LLM:
         kvd = kv_dtype_from_str(kv_cache_dtype)
         if kv_pages is None:
             kv_pages = self._pages_from_memory(cfg, kvd, gpu_memory_utilization, max_batch, max_model_len)
-        spec = KVPoolSpec(kv_pages, cfg.num_layers, self.model.kvh, cfg.head_dim, dtype=kvd)
+        spec = KVPoolSpec(kv_pages, self._kv_layers(), self.model.kvh, cfg.head_dim, dtype=kvd)
         self.pool = KVPool(spec, self.device)
         self.offload = None
         if kv_offload_pages > 0 and enable_prefix_cache:
@@ -139,13 +151,17 @@ class LLM:
             # calls mid-run: every rank captures every bucket now, in the same order
             self.runner.capture_all()
 
+    def _kv_layers(self) -> int:
+        """Layers whose KV this rank holds (a pipeline stage holds its own layers')."""
+        return self.model.num_local_layers if self.pp_grid is not None else self.cfg.num_layers
+
     def _pages_from_memory(self, cfg, kvd, util, max_batch, max_model_len) -> int:
         need = max_batch * ((max_model_len + 15) // 16) + 16
         if self.device.type != "cuda":
             return min(need, 4096)
         free, total = torch.cuda.mem_get_info(self.device)
         budget = int(free - (1 - util) * total) - (2 << 30)   # keep ~2 GiB for activations/graphs
-        per = KVPoolSpec(1, cfg.num_layers, self.model.kvh, cfg.head_dim, dtype=kvd).bytes_per_page
+        per = KVPoolSpec(1, self._kv_layers(), self.model.kvh, cfg.head_dim, dtype=kvd).bytes_per_page
         return max(16, min(need * 2, budget // per))
 
     # ------------------------------------------------------------------ API

@@ -6,10 +6,9 @@ residual stream to stage i+1 (peer copy between GPUs).  It exposes the same
 `forward(batch, pool)` / `device` / `kvh` surface as a single `DecoderModel`, so the
 model runner and the continuous-batching engine drive it unchanged.
 
-`DistPipeline` runs one stage per process group of ranks (PP x TP grid): the hidden
-state crosses stages with NCCL point-to-point send/recv between ranks holding the
-same TP index, and the last stage broadcasts its logits-derived tokens through the
-runner.  Stage boundaries come from `placement.split_model_into_blocks`.
+Pipeline stages in separate processes (a PP x TP grid of ranks, NCCL p2p between
+stages) are parallel/pp.py.  Stage boundaries come from
+`placement.split_model_into_blocks`.
 
 Reference parity: the reference's production PP is accelerate `device_map="auto"`
 (core/backends.py:1314-1352) with activations moved by a patched `send_to_device`
@@ -23,7 +22,6 @@ from dataclasses import fields, replace
 from typing import Callable, List, Optional, Sequence, Tuple
 
 import torch
-import torch.distributed as dist
 
 from ..kv.pool import KVPool, KVPoolSpec
 from ..models.config import ModelConfig
@@ -104,43 +102,3 @@ def build_local_pipeline(cfg: ModelConfig, blocks: Sequence[Block], *, num_pages
         spec = KVPoolSpec(num_pages, blk.end - blk.start, cfg.num_kv_heads, cfg.head_dim, dtype=kv_dtype)
         stages.append((m, KVPool(spec, dev)))
     return LocalPipeline(stages)
-
-
-class DistPipelineStage:
-    """One pipeline stage of a multi-process PP x TP job (NCCL send/recv between stages).
-
-    Ranks are laid out stage-major: rank = stage * tp_size + tp_rank.  The stage
-    model runs on this rank's GPU; `forward` receives the residual stream from the
-    previous stage (same tp_rank), runs the local layers and sends it on.  The last
-    stage returns logits; other stages return None.
-    """
-
-    def __init__(self, model: DecoderModel, pool: KVPool, stage: int, num_stages: int, tp_size: int,
-                 group=None):
-        self.model, self.pool = model, pool
-        self.stage, self.num_stages, self.tp_size = stage, num_stages, tp_size
-        self.device = model.device
-        self.kvh = model.kvh
-        self.cfg = model.cfg
-        self.rank = dist.get_rank()
-        self.group = group
-
-    @property
-    def is_first(self):
-        return self.stage == 0
-
-    @property
-    def is_last(self):
-        return self.stage == self.num_stages - 1
-
-    def forward(self, batch: ForwardBatch, pool=None, hidden=None):
-        T = batch.num_tokens
-        h = None
-        if not self.is_first:
-            h = torch.empty(T, self.cfg.hidden_size, dtype=self.model.dtype, device=self.device)
-            dist.recv(h, src=self.rank - self.tp_size, group=self.group)
-        out = self.model.forward(batch, self.pool, hidden=h)
-        if not self.is_last:
-            dist.send(out.contiguous(), dst=self.rank + self.tp_size, group=self.group)
-            return None
-        return out

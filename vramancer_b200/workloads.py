@@ -39,16 +39,35 @@ from typing import List, Optional
 import torch
 
 
-def _init():
+_PP_GRID = None
+
+
+def _init(args=None):
+    """Process group, device and the tensor-parallel context.  With --pp P under torchrun
+    the ranks form a P x (world / P) pipeline x tensor-parallel grid (parallel/pp.py)."""
+    global _PP_GRID
     from .parallel import comm
     info = comm.init_distributed()
     dev = torch.device("cuda", info.local_rank) if torch.cuda.is_available() else torch.device("cpu")
     if dev.type == "cuda":
         torch.cuda.set_device(dev)
     tp = None
-    if info.world_size > 1:
+    pp = getattr(args, "pp", 1) if args is not None else 1
+    if info.world_size > 1 and pp > 1:
+        from .models.config import get_config
+        from .parallel.pp import PPGrid
+        cfg = get_config(args.model)
+        _PP_GRID = PPGrid(pp, info.world_size // pp, num_layers=args.num_layers or cfg.num_layers)
+        tp = comm.tp_context(_PP_GRID.tp_group) if _PP_GRID.tp > 1 else None
+    elif info.world_size > 1:
         tp = comm.tp_context()
     return info, dev, tp
+
+
+def _layout(info) -> dict:
+    if _PP_GRID is not None:
+        return {"pp": _PP_GRID.pp, "tp": _PP_GRID.tp, "parallelism": f"pp{_PP_GRID.pp}xtp{_PP_GRID.tp}"}
+    return {"pp": 1, "tp": info.world_size, "parallelism": f"tp{info.world_size}"}
 
 
 def _sync(dev):
@@ -79,6 +98,8 @@ class _Timer:
 
 def _build(args, dev, tp, *, max_batch: int, max_len: int, kv_pages: Optional[int] = None, **kw):
     from .llm import LLM
+    if _PP_GRID is not None:
+        kw.setdefault("pp_grid", _PP_GRID)
     return LLM(args.model, device=str(dev), kv_cache_dtype=args.kv_dtype, max_batch=max_batch,
                max_model_len=max_len, kv_pages=kv_pages, quantization=args.quantization, tp=tp,
                num_layers=args.num_layers, **kw)
@@ -118,6 +139,8 @@ def run_serve(args, info, dev, tp) -> dict:
         batch_hist.append(nrun)
     _sync(dev)
     wall = time.perf_counter() - t0
+    from .parallel import comm
+    wall = comm.max_over_ranks(wall)            # the slowest rank's time
     out_tok = sum(len(r.output_ids) for r in reqs)
     ttft = [r.ttft * 1e3 for r in reqs if r.ttft is not None]
     decode_steps = eng.stats["steps"] - s0["steps"]
@@ -128,8 +151,8 @@ def run_serve(args, info, dev, tp) -> dict:
             "total_tok_s": round((out_tok + sum(lens)) / wall, 1),
             "ttft_p50_ms": round(_pct(ttft, 0.5), 1), "ttft_p99_ms": round(_pct(ttft, 0.99), 1),
             "engine_steps": decode_steps, "mean_running": round(statistics.mean(batch_hist), 1) if batch_hist else 0,
-            "preempted": eng.stats["preempted"] - s0["preempted"], "tp": info.world_size,
-            "timing": "wall clock between device synchronisations (engine API end to end)",
+            "preempted": eng.stats["preempted"] - s0["preempted"], **_layout(info),
+            "timing": "wall clock between device synchronisations (engine API end to end), max over ranks",
             "data": "synthetic ids, random-init N(0,0.02) weights"}
 
 
@@ -208,7 +231,7 @@ def run_prefill(args, info, dev, tp) -> dict:
     med = statistics.median(times)
     return {"workload": "prefill", "model": args.model, "quantization": args.quantization or "bf16",
             "batch": B, "seq": S, "ms": round(med * 1e3, 2), "prompt_tok_s": round(B * S / med, 1),
-            "iters": args.iters, "tp": info.world_size,
+            "iters": args.iters, **_layout(info),
             "timing": "CUDA events around one engine step that prefills every prompt (first token sampled)",
             "data": "synthetic ids, random-init N(0,0.02) weights"}
 
@@ -238,7 +261,7 @@ def run_decode(args, info, dev, tp) -> List[dict]:
             llm.engine.step()
         outs.append({"workload": "decode", "model": args.model, "quantization": args.quantization or "bf16",
                      "kv_dtype": args.kv_dtype, "batch": B, "prompt_len": P, "ms_per_step": round(ms, 4),
-                     "tok_s": round(B / ms * 1e3, 1), "tp": info.world_size,
+                     "tok_s": round(B / ms * 1e3, 1), **_layout(info),
                      "graph": bool(getattr(runner, "use_graph", False)),
                      "timing": "CUDA events over engine steps (host scheduling and the per-step H2D/D2H included)"})
     return outs
@@ -268,12 +291,13 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--pp", type=int, default=1, help="torchrun: pipeline stages (ranks = pp x tp)")
     return ap.parse_args(argv)
 
 
 def main(argv=None) -> None:
     args = parse_args(argv)
-    info, dev, tp = _init()
+    info, dev, tp = _init(args)
     fn = {"serve": run_serve, "spec": run_spec, "prefill": run_prefill, "decode": run_decode}[args.what]
     res = fn(args, info, dev, tp)
     if info.rank == 0:
