@@ -127,6 +127,8 @@ def main(argv=None):
     ap.add_argument("--kv-dtype", default="bf16")
     ap.add_argument("--graph", action="store_true", help="replay the captured graph instead of eager steps")
     ap.add_argument("--ablate", action="store_true", help="critical-path cost of each op type (graph replay)")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="one GPU runs rank 0's shard of a TP=N model without its peers (parallel/tp_emulate.py)")
     args = ap.parse_args(argv)
     if args.ablate:
         args.graph = True
@@ -138,6 +140,9 @@ def main(argv=None):
     from ..parallel import comm
     info = comm.init_distributed()          # under torchrun: tensor parallelism over the ranks
     tp = comm.tp_context()
+    if args.shard_of > 1 and info.world_size == 1:
+        from ..parallel.tp_emulate import shard_context
+        tp = shard_context(args.shard_of, f"cuda:{info.local_rank}")
     llm = LLM(args.model, device=f"cuda:{info.local_rank}", tp=tp, max_batch=B, max_model_len=P + args.steps + 64,
               kv_pages=(B + 1) * ((P + args.steps + 80) // 16 + 1) + 16, enable_prefix_cache=False,
               use_cuda_graph=args.graph, kv_cache_dtype=args.kv_dtype, num_layers=args.num_layers)

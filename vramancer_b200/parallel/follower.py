@@ -6,18 +6,43 @@ ranks then call `engine.step()` with identical state, so their collectives line 
 """
 from __future__ import annotations
 
+import pickle
+
+import torch
 import torch.distributed as dist
 
 
 class StepBroadcaster:
+    """Per-step control message from rank 0.  The common case (no new request, no
+    abort) costs one 8-byte broadcast on the gloo group; events are pickled and sent as
+    a byte tensor only in steps that have some."""
+
+    STOP = -1
+
     def __init__(self):
         self.group = dist.new_group(backend="gloo") if dist.is_initialized() else None
 
     def exchange(self, msgs):
-        box = [msgs]
-        if self.group is not None:
-            dist.broadcast_object_list(box, src=0, group=self.group)
-        return box[0]
+        if self.group is None:
+            return msgs
+        n = torch.zeros(1, dtype=torch.int64)
+        payload = None
+        if dist.get_rank() == 0:
+            if msgs == "stop":
+                n[0] = self.STOP
+            elif msgs:
+                payload = torch.frombuffer(bytearray(pickle.dumps(msgs)), dtype=torch.uint8)
+                n[0] = payload.numel()
+        dist.broadcast(n, src=0, group=self.group)
+        size = int(n[0])
+        if size == self.STOP:
+            return "stop"
+        if size == 0:
+            return None
+        if payload is None:
+            payload = torch.empty(size, dtype=torch.uint8)
+        dist.broadcast(payload, src=0, group=self.group)
+        return pickle.loads(payload.numpy().tobytes())
 
 
 def follow(pipe) -> int:
