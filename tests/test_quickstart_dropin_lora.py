@@ -74,3 +74,34 @@ def test_lora_merge_switch_disable():
     assert llm.generate(prompt, SamplingParams(max_tokens=6))[0].output_ids == base_out
     lora.delete_adapter("a")
     assert lora.list_adapters() == {"adapters": ["b"], "active": None}
+
+
+def test_quickstart_launches_run_and_serve():
+    from types import SimpleNamespace
+    gpus = [SimpleNamespace(free_gb=178.0, capability=(10, 0))]
+    calls = []
+
+    def launcher(kind, ns):
+        calls.append((kind, ns))
+        return 0
+    rec = quickstart.run_quickstart("chat", gpus=gpus, launcher=launcher)
+    assert calls == [] and rec["command"].startswith("vramancer run ")
+    rec = quickstart.run_quickstart("chat", run=True, prompt="hello", gpus=gpus, launcher=launcher)
+    kind, ns = calls[-1]
+    assert kind == "run" and rec["launched"] == "run" and ns.model == rec["model"] and ns.prompt == "hello"
+    assert (ns.quantization or "bf16") == rec["quantization"]
+    rec = quickstart.run_quickstart("code-assistant", serve=True, port=6001, gpus=gpus, launcher=launcher)
+    kind, ns = calls[-1]
+    assert kind == "serve" and ns.port == 6001 and rec["command"].startswith("vramancer serve ")
+
+
+def test_quickstart_run_goes_through_the_run_command(monkeypatch):
+    """Without a launcher the recommendation runs through cli._cmd_run (as `vramancer run`)."""
+    from types import SimpleNamespace
+
+    from vramancer_b200 import cli
+    seen = {}
+    monkeypatch.setattr(cli, "_cmd_run", lambda a: seen.setdefault("run", a.model) and 0)
+    gpus = [SimpleNamespace(free_gb=30.0, capability=(10, 0))]
+    rec = quickstart.run_quickstart("chat", run=True, gpus=gpus)
+    assert seen["run"] == rec["model"] and rec["exit_code"] == 0

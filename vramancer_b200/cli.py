@@ -94,8 +94,10 @@ def build_parser() -> argparse.ArgumentParser:
     db.add_argument("--cli", action="store_true")
     q = sub.add_parser("quickstart", help="recommend the largest model that fits")
     q.add_argument("use_case", nargs="?", default="chat", choices=["code-assistant", "chat", "summarize"])
-    q.add_argument("--run", action="store_true")
-    q.add_argument("--serve", action="store_true")
+    q.add_argument("--run", action="store_true", help="launch the recommended model (interactive, or --prompt)")
+    q.add_argument("--serve", action="store_true", help="serve the recommended model (OpenAI API)")
+    q.add_argument("--prompt", "-p", default=None)
+    q.add_argument("--port", type=int, default=5030)
     h = sub.add_parser("hub", help="inspect a model directory / name")
     h.add_argument("model")
     sub.add_parser("health", help="node health report")
@@ -281,9 +283,9 @@ def main(argv: Optional[List[str]] = None) -> int:
         return 0
     if cmd == "quickstart":
         from .quickstart import run_quickstart
-        rec = run_quickstart(a.use_case)
+        rec = run_quickstart(a.use_case, run=a.run, serve=a.serve, prompt=a.prompt, port=a.port)
         _print(rec or {"error": "no catalog model fits the detected GPUs"})
-        return 0
+        return int(rec.get("exit_code", 0)) if rec else 2
     if cmd == "hub":
         return _cmd_hub(a)
     if cmd == "health":
