@@ -69,3 +69,41 @@ def test_discovery_over_udp_and_static_nodes(monkeypatch):
     discovery._nodes["http://old:5030"]["last_seen"] -= 100
     urls = {n["url"] for n in discovery.known_nodes(ttl_s=30)}
     assert {"http://static-a:5030", "http://static-b:5030"} <= urls and "http://old:5030" not in urls
+
+
+def test_mdns_wire_format_roundtrip():
+    from vramancer_b200.cluster import mdns
+    r = mdns.MDNSResponder("node7", "10.0.0.7", 5030, {"model": "qwen2.5-14b", "gpus": 8})
+    msg = mdns.parse_message(r.records())
+    assert msg["response"]
+    types = {rt: val for _, rt, _, _, val in msg["records"]}
+    assert types[mdns.T_PTR] == "node7._vramancer._tcp.local."
+    assert types[mdns.T_SRV][2] == 5030 and types[mdns.T_A] == "10.0.0.7"
+    assert types[mdns.T_TXT]["model"] == "qwen2.5-14b" and types[mdns.T_TXT]["url"] == "http://10.0.0.7:5030"
+    q = mdns.parse_message(mdns.build_query())
+    assert q["questions"][0][:2] == (mdns.SERVICE_TYPE, mdns.T_PTR) and not q["response"]
+
+
+def test_mdns_browse_finds_a_responder_on_loopback():
+    from vramancer_b200.cluster import mdns
+    port = _free_udp_port()
+    r = mdns.MDNSResponder("b200-a", "10.1.2.3", 5031, {"gpus": 8}, group="127.0.0.1", mdns_port=port,
+                           bind="127.0.0.1")
+    assert r.start()
+    try:
+        found = mdns.browse(timeout=1.0, group="127.0.0.1", mdns_port=port)
+        assert [f["url"] for f in found] == ["http://10.1.2.3:5031"]
+        assert found[0]["gpus"] == "8" and found[0]["discovery"] == "mdns"
+        assert any(n["url"] == "http://10.1.2.3:5031" for n in discovery.known_nodes())
+        assert r.answered >= 1
+    finally:
+        r.stop()
+
+
+def _free_udp_port():
+    import socket
+    s = socket.socket(socket.AF_INET, socket.SOCK_DGRAM)
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p

@@ -10,6 +10,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import socket
 import secrets
 import subprocess
 import sys
@@ -172,7 +173,10 @@ def _cmd_serve(a) -> int:
         return follow(pipe)
     if a.cluster:
         from .cluster.discovery import announce
+        from .cluster.mdns import MDNSResponder
         announce(a.host, a.port, {"model": model})
+        ip = a.host if a.host not in ("0.0.0.0", "") else socket.gethostbyname(socket.gethostname())
+        MDNSResponder(f"vrm-{socket.gethostname()}-{a.port}", ip, a.port, {"model": model or ""}).start()
     run_server(a.host, a.port, pipeline=pipe)
     return 0
 
@@ -260,9 +264,11 @@ def main(argv: Optional[List[str]] = None) -> int:
         return 0
     if cmd == "discover":
         from .cluster.discovery import ClusterDiscovery, known_nodes
+        from .cluster.mdns import browse
         d = ClusterDiscovery()
         d.start()
-        time.sleep(a.timeout)
+        browse(timeout=min(2.0, a.timeout))      # mDNS / DNS-SD answers go into the same table
+        time.sleep(max(0.0, a.timeout - 2.0))
         d.stop()
         _print(known_nodes())
         return 0

@@ -3,8 +3,8 @@
 Each `vramancer serve` node can `announce()` itself (JSON datagram with host, port,
 model, GPU count) on the discovery port; `ClusterDiscovery` listens, keeps a table of
 nodes with last-seen times and drops nodes whose heartbeat is older than `ttl_s`.
-VRM_NODES (comma-separated URLs) adds static nodes.  (mDNS/zeroconf is not available
-offline; UDP broadcast covers the LAN case.)
+VRM_NODES (comma-separated URLs) adds static nodes, and cluster/mdns.py finds nodes
+by mDNS / DNS-SD (service "_vramancer._tcp.local.") into the same table.
 
 Reference parity: experimental/cluster_discovery.py:225-1016 (mDNS + UDP broadcast +
 static list, heartbeat), core/cluster_gateway.py discovery hook.
