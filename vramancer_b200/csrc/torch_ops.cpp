@@ -1118,6 +1118,33 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b"), py::arg("out"), py::arg("mode"), py::arg("eps"), py::arg("spin_limit") = 0,
         py::arg("err") = py::none(),
         "fused all-reduce, reduce half: poll the slots, sum in rank order, + bias + residual, optional norm");
+  m.def("vmm_granularity", [](int64_t device) { return (int64_t)vrm::vmm_granularity((int)device); });
+  m.def("vmm_reserve", [](int64_t bytes, int64_t align) { return (int64_t)vrm::vmm_reserve(bytes, align); });
+  m.def("vmm_map", [](int64_t base, int64_t offset, int64_t bytes, int64_t location, std::vector<int64_t> access,
+                      bool shareable) {
+    std::vector<int> acc(access.begin(), access.end());
+    vrm::vmm_map((uint64_t)base, offset, bytes, (int)location, acc, shareable);
+  });
+  m.def("vmm_export_fd", [](int64_t base, int64_t offset) { return vrm::vmm_export_fd((uint64_t)base, offset); });
+  m.def("vmm_map_fd", [](int64_t base, int64_t offset, int64_t bytes, int64_t fd, std::vector<int64_t> access) {
+    std::vector<int> acc(access.begin(), access.end());
+    vrm::vmm_map_fd((uint64_t)base, offset, bytes, (int)fd, acc);
+  });
+  m.def("vmm_unmap", [](int64_t base, int64_t offset) { vrm::vmm_unmap((uint64_t)base, offset); });
+  m.def("vmm_free", [](int64_t base) { vrm::vmm_free((uint64_t)base); });
+  m.def("tensor_from_ptr", [](int64_t ptr, std::vector<int64_t> shape, std::string dtype, int64_t device) {
+    // a tensor view of device memory this library manages (no ownership: the caller
+    // keeps the region alive for the tensor's lifetime)
+    at::ScalarType st;
+    if (dtype == "bfloat16") st = torch::kBFloat16;
+    else if (dtype == "float8_e4m3fn") st = torch::kFloat8_e4m3fn;
+    else if (dtype == "float32") st = torch::kFloat32;
+    else if (dtype == "uint8") st = torch::kByte;
+    else if (dtype == "float16") st = torch::kHalf;
+    else TORCH_CHECK(false, "tensor_from_ptr: unsupported dtype ", dtype);
+    auto opts = torch::TensorOptions().dtype(st).device(torch::kCUDA, (int)device);
+    return torch::from_blob(reinterpret_cast<void*>(ptr), shape, opts);
+  });
   m.def("symm_fill_u16", [](int64_t p, int64_t count, int64_t value) {
     vrm::symm_fill_u16(reinterpret_cast<void*>(p), (size_t)count, (uint16_t)value);
   });

@@ -376,6 +376,18 @@ void* symm_malloc(size_t bytes);
 void symm_free(void* p);
 // Fills count 16-bit words at p (current device) with value and waits for it.
 void symm_fill_u16(void* p, size_t count, uint16_t value);
+
+// ---------------------------------------------------------------- virtual memory regions (vmm.cpp)
+// One reserved virtual range whose chunks are backed by physical memory on chosen
+// devices and readable / writable from the listed devices.
+size_t vmm_granularity(int device);
+uint64_t vmm_reserve(size_t bytes, size_t alignment);
+void vmm_map(uint64_t base, size_t offset, size_t bytes, int location_device, const std::vector<int>& access,
+             bool shareable);
+int vmm_export_fd(uint64_t base, size_t offset);
+void vmm_map_fd(uint64_t base, size_t offset, size_t bytes, int fd, const std::vector<int>& access);
+void vmm_unmap(uint64_t base, size_t offset);
+void vmm_free(uint64_t base);
 std::vector<uint8_t> ipc_handle(void* p);
 void* ipc_open(const std::vector<uint8_t>& bytes);
 void ipc_close(void* p);

@@ -250,6 +250,12 @@ class LLMEngine:
         with self._lock:
             before = self.stats["finished"]
             done: List[Request] = []
+            pool = getattr(self.runner, "pool", None)
+            if getattr(pool, "reclaim_requested", False):
+                # a lender wants its memory back: borrowed KV pages move home between
+                # steps, after the step in flight has been read
+                self._drain(done)
+                pool.reclaim(self.kv)
             self._admit()
             if self.ep_sync is None:
                 self._prefill_chunk(done)

@@ -61,6 +61,7 @@ class PagedKVCacheManager:
         self._lru: "OrderedDict[int, None]" = OrderedDict()  # cached pages with ref 0
         self._overflow = overflow
         self._release_borrowed = release_borrowed
+        self._overflow_capacity: Optional[Callable[[], int]] = None   # pages the overflow can still give
         self.offload = offload                              # host tier of the prefix cache (kv/offload.py)
         self._borrowed: Dict[int, int] = {}                 # page id (>= num_pages) -> ref
         self._lock = threading.RLock()
@@ -77,7 +78,33 @@ class PagedKVCacheManager:
         return (num_tokens + self.page_size - 1) // self.page_size
 
     def can_allocate(self, num_tokens: int) -> bool:
-        return self.pages_needed(num_tokens) <= self.num_free_pages()
+        extra = self._overflow_capacity() if self._overflow_capacity is not None else 0
+        return self.pages_needed(num_tokens) <= self.num_free_pages() + extra
+
+    def relocate_borrowed(self, copy_page: Callable[[int, int], None]) -> int:
+        """Moves borrowed pages that are in use into free local pages: copy_page(src, dst)
+        copies the data, every sequence's page list is rewritten and the borrowed page is
+        released.  Stops when no local page is free; returns the pages moved."""
+        moved = 0
+        with self._lock:
+            for p in sorted(self._borrowed):
+                if not self._free:
+                    break
+                q = self._free.popleft()
+                copy_page(p, q)
+                refs = self._borrowed[p]
+                self._ref[q] = refs
+                for st in self._seqs.values():
+                    st.pages = [q if x == p else x for x in st.pages]
+                key = self._page_key.pop(p, None)
+                if key is not None:
+                    self._page_key[q] = key
+                    if self._prefix.get(key[0]) == p:
+                        self._prefix[key[0]] = q
+                self._borrowed[p] = 1
+                self._decref(p)                 # releases the borrowed page
+                moved += 1
+        return moved
 
     # ------------------------------------------------------------------ page alloc
     def _take_page(self) -> int:

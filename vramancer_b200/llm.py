@@ -8,6 +8,11 @@ Builds the weights (HF safetensors, NVFP4 checkpoint or random N(0, 0.02)), the 
 KV pool sized from the free memory left after the weights, the block manager, the
 model runner (CUDA-graph decode) and the continuous-batching engine.
 
+With `kv_lender=d` (or a `lending_pool`), KV pages beyond the local pool are borrowed
+from GPU d's memory (kv/overflow.py) and read in place by the attention kernels, so a
+sequence may grow past the local pool; the memory returns to the lender when its pages
+are freed or reclaimed.
+
 With `fold_norms=True` (the default; dense RMSNorm models with bf16 weights on one
 GPU) the input and post-attention RMSNorm weights are multiplied into the columns of
 `qkv_w` / `gate_up_w` in place, so small decode batches run the norms inside the
@@ -50,7 +55,8 @@ class LLM:
                  num_layers: Optional[int] = None, tp=None, quantization: Optional[str] = None,
                  spec_num_draft: int = 0, spec_ngram: int = 3, kv_offload_pages: int = 0, hierarchy=None,
                  stream_layers: int = 0, ep=None, fold_norms: bool = True, pp_grid=None,
-                 prefill_microbatches: int = 0, decode_microbatches: int = 1):
+                 prefill_microbatches: int = 0, decode_microbatches: int = 1, kv_lender: Optional[int] = None,
+                 kv_borrow_pages: int = 0, lending_pool=None):
         if isinstance(model, ModelConfig):
             cfg = model
         else:
@@ -123,7 +129,14 @@ class LLM:
         if kv_pages is None:
             kv_pages = self._pages_from_memory(cfg, kvd, gpu_memory_utilization, max_batch, max_model_len)
         spec = KVPoolSpec(kv_pages, self._kv_layers(), self.model.kvh, cfg.head_dim, dtype=kvd)
-        self.pool = KVPool(spec, self.device)
+        if kv_lender is not None or lending_pool is not None:
+            # VRAM lending: pages beyond the local pool are borrowed from another GPU's
+            # memory and read in place by the kernels (kv/overflow.py)
+            from .kv.overflow import ExtensiblePagePool
+            self.pool = ExtensiblePagePool(spec, self.device, kv_lender, kv_borrow_pages or kv_pages,
+                                           lending_pool=lending_pool)
+        else:
+            self.pool = KVPool(spec, self.device)
         self.offload = None
         if kv_offload_pages > 0 and enable_prefix_cache:
             # evicted prefix pages go to pinned host memory (and on to NVMe through `hierarchy`)
@@ -131,6 +144,8 @@ class LLM:
             self.offload = KVOffloader([self.pool.cache], kv_offload_pages, hierarchy=hierarchy)
         self.kv = PagedKVCacheManager(kv_pages, spec.page_size, enable_prefix_cache=enable_prefix_cache,
                                       offload=self.offload)
+        if hasattr(self.pool, "attach"):
+            self.pool.attach(self.kv)
         self.runner = ModelRunner(self.model, self.pool, max_batch=max_batch, max_model_len=max_model_len,
                                   use_cuda_graph=use_cuda_graph, seed=seed)
         ep_sync = None

@@ -142,7 +142,10 @@ def bench_nvfp4(m, n, k, iters=50, copies=None):
             "bf16_equiv_tb_s": round(n * k * 2 / us / 1e6, 3), "peaks": src}
 
 
-def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4, fp8=False, iters=50):
+def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4, fp8=False, iters=50,
+                      splits=0, fused=False):
+    """splits > 0 forces the split count; fused runs the model's path (RoPE on q and the
+    step's K/V written into its page inside the kernel)."""
     hbm, _, src = peaks()
     ps = 16
     pages = (ctx + ps - 1) // ps
@@ -151,18 +154,26 @@ def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4
     cache = torch.randn(P, layers, 2, kv_heads, ps, head_dim, device="cuda").to(dt)
     bt = torch.arange(P, dtype=torch.int32, device="cuda").view(batch, pages)
     cl = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
-    q = torch.randn(batch, q_heads * head_dim, device="cuda", dtype=torch.bfloat16)
-    out = torch.empty_like(q)
+    q = torch.randn(batch, (q_heads + (2 * kv_heads if fused else 0)) * head_dim, device="cuda",
+                    dtype=torch.bfloat16)
+    out = torch.empty(batch, q_heads * head_dim, device="cuda", dtype=torch.bfloat16)
     scale = torch.ones(layers, 2, kv_heads, device="cuda") if fp8 else None
     state = [0]
+    kw = {}
+    if fused:
+        pos = torch.full((batch,), ctx - 1, dtype=torch.int32, device="cuda")
+        slots = bt[:, (ctx - 1) // ps] * ps + (ctx - 1) % ps
+        kw = dict(positions=pos, cos_sin=rope_cos_sin(ctx + 16, head_dim, 1e6, "cuda"), slot_mapping=slots.int())
 
     def fn():
-        paged_attention_decode(q, cache, state[0] % layers, bt, cl, scale, 1 / math.sqrt(head_dim), q_heads, out=out)
+        paged_attention_decode(q, cache, state[0] % layers, bt, cl, scale, 1 / math.sqrt(head_dim), q_heads, out=out,
+                               num_splits=splits, **kw)
         state[0] += 1
 
     us = time_it(fn, iters)
     byts = batch * ctx * kv_heads * head_dim * 2 * cache.element_size()
-    return {"kernel": "decode_attn", "batch": batch, "ctx": ctx, "fp8": fp8, "us": round(us, 2),
+    return {"kernel": "decode_attn", "batch": batch, "ctx": ctx, "fp8": fp8, "kv_heads": kv_heads,
+            "q_heads": q_heads, "splits": splits or "auto", "fused": fused, "us": round(us, 2),
             "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
 
 
@@ -379,6 +390,10 @@ def main(argv=None):
     ap.add_argument("what", choices=["gemm", "nvfp4", "nvfp4-prefill", "fp8", "decode-attn", "all", "trace", "rmsnorm",
                                      "rope-kv", "prefill-attn", "sample", "turboquant", "act-quant", "others"])
     ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--kv-heads", type=int, default=8)
+    ap.add_argument("--q-heads", type=int, default=40)
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--fused", action="store_true", help="decode-attn: RoPE + KV write inside the kernel")
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--greedy", action="store_true")
     ap.add_argument("--m", type=int, default=1)
@@ -393,7 +408,8 @@ def main(argv=None):
     a = ap.parse_args(argv)
     native()
     if a.what == "trace":
-        for name, n, k in QWEN14B_DECODE[:4]:
+        shapes = QWEN14B_DECODE[:4] if (a.n, a.k) == (5120, 13824) else [("custom", a.n, a.k)]
+        for name, n, k in shapes:
             r = trace_gemm(a.m, n, k)
             r["name"] = name
             print(json.dumps(r))
@@ -416,7 +432,8 @@ def main(argv=None):
         for n, k in ([(a.n, a.k)] if a.n != 5120 or a.k != 13824 else [(27648, 5120), (5120, 13824), (7168, 5120)]):
             print(json.dumps(bench_nvfp4_prefill(a.m if a.m != 1 else 4096, n, k, a.iters)))
     elif a.what == "decode-attn":
-        print(json.dumps(bench_decode_attn(a.batch, a.ctx, fp8=a.fp8, iters=a.iters)))
+        print(json.dumps(bench_decode_attn(a.batch, a.ctx, kv_heads=a.kv_heads, q_heads=a.q_heads, fp8=a.fp8,
+                                           iters=a.iters, splits=a.splits, fused=a.fused)))
     elif a.what == "fp8":
         for m in ((a.m,) if a.m != 1 else (1, 32, 4096)):
             for name, n, k in QWEN14B_DECODE[:4]:
