@@ -21,6 +21,8 @@
 // Reference parity: csrc/paged_attention_kernel.cu:61-438 (SIMT decode over fp32 /
 // fp16 / q4 pages, not on the reference's forward path); the reference prefill runs
 // HF SDPA (core/turbo_engine.py:72-93).
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <climits>
 #include <cstdlib>
@@ -155,7 +157,12 @@ __device__ __forceinline__ void decode_write_new_kv(const DecodeParams& P, int b
   for (int d = lane; d < D; d += 32) put(vd, d, vs[d], vinv);
 }
 
-template <int D, bool kFp8>
+// kCluster: the splits of one (sequence, KV head) are the CTAs of one thread-block
+// cluster (2..8); each keeps its partial in shared memory and, after a cluster barrier,
+// merges a slice of the outputs from its peers' shared memory (no global partials, no
+// completion counter).  Otherwise splits merge through global scratch: the last CTA
+// to finish (counter) combines them.
+template <int D, bool kFp8, bool kCluster = false>
 __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   pdl_launch();
   using S = DecodeSmem<D, kFp8>;
@@ -375,6 +382,10 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   __syncthreads();
 
   const size_t grp = (size_t)b * KH + kvh;
+  // cluster partials: past the warp-merge area (which is at most half the buffer)
+  float* s_co = reinterpret_cast<float*>(smem + S::kTotal / 2);   // [G][D] normalised partial
+  float* s_cm = s_co + 8 * D;                                    // [G] max
+  float* s_cl = s_cm + 8;                                        // [G] sum
   for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
     const int h = idx / D, d = idx % D;
     float M = -INFINITY;
@@ -392,6 +403,12 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
     if (nsplit == 1) {
       const float r = L > 0.f ? acc / L * v_scale : 0.f;
       P.out[(size_t)b * P.ld_o + (size_t)(kvh * G + h) * D + d] = __float2bfloat16(r);
+    } else if (kCluster) {
+      s_co[h * D + d] = L > 0.f ? acc / L : 0.f;
+      if (d == 0) {
+        s_cm[h] = M;
+        s_cl[h] = L;
+      }
     } else {
       P.ws_o[((grp * nsplit + split) * G + h) * D + d] = L > 0.f ? acc / L : 0.f;
       if (d == 0) {
@@ -401,6 +418,35 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
     }
   }
   if (nsplit == 1) return;
+
+  if constexpr (kCluster) {
+    // ---- every CTA of the cluster merges its slice of the G x D outputs from the
+    // partials in its peers' shared memory
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const int rank = (int)cluster.block_rank();
+    const int n = G * D;
+    const int per = (n + nsplit - 1) / nsplit;
+    const int i0 = rank * per, i1 = min(n, i0 + per);
+    for (int idx = i0 + threadIdx.x; idx < i1; idx += blockDim.x) {
+      const int h = idx / D;
+      float M = -INFINITY;
+      for (int q = 0; q < nsplit; ++q) M = fmaxf(M, cluster.map_shared_rank(s_cm, q)[h]);
+      float L = 0.f, acc = 0.f;
+      if (M != -INFINITY) {
+        for (int q = 0; q < nsplit; ++q) {
+          const float w = cluster.map_shared_rank(s_cl, q)[h] * exp2f(cluster.map_shared_rank(s_cm, q)[h] - M);
+          L += w;
+          acc += w * cluster.map_shared_rank(s_co, q)[idx];
+        }
+      }
+      const float r = L > 0.f ? acc / L * v_scale : 0.f;
+      P.out[(size_t)b * P.ld_o + (size_t)(kvh * G) * D + idx] = __float2bfloat16(r);
+    }
+    cluster.sync();     // peers' shared memory stays valid until every CTA has read it
+    return;
+  }
 
   // ---- the last CTA of this (sequence, kv head) merges the splits
   __threadfence();
@@ -1036,10 +1082,10 @@ size_t decode_attention_scratch_bytes(int B, int Hq, int D, int splits) {
   return ((size_t)B * Hq * splits * D + (size_t)B * Hq * splits * 2) * sizeof(float);
 }
 
-template <int D, bool F8>
+template <int D, bool F8, bool C = false>
 static void launch_decode(dim3 grid, const DecodeParams& p, cudaStream_t st) {
   constexpr int smem = DecodeSmem<D, F8>::kTotal;
-  auto kern = paged_decode_kernel<D, F8>;
+  auto kern = paged_decode_kernel<D, F8, C>;
   static bool set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1047,7 +1093,17 @@ static void launch_decode(dim3 grid, const DecodeParams& p, cudaStream_t st) {
     VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     set[dev & 63] = true;
   }
-  launch_kernel(kern, grid, dim3(128), (size_t)smem, st, p);
+  if (C) launch_kernel_cluster(kern, grid, dim3(128), dim3(1, 1, grid.z), (size_t)smem, st, p);
+  else launch_kernel(kern, grid, dim3(128), (size_t)smem, st, p);
+}
+
+// split merge through a thread-block cluster (VRM_DECODE_CLUSTER=0 keeps the counter merge)
+static bool decode_cluster_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VRM_DECODE_CLUSTER");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows);
@@ -1115,7 +1171,11 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
     VRM_REQUIRE(a.slot_mapping != nullptr, "decode attention: fused KV write needs slot_mapping");
     VRM_REQUIRE(a.cos_sin == nullptr || a.rot_dim == a.D, "decode attention: fused RoPE needs rot_dim == head_dim");
   }
-  if (splits > 1) {
+  const int64_t pool_rows = a.cache_pages * a.num_layers * 2 * a.KH * kPage;
+  const bool tma = !a.cache_fp8 && a.positions == nullptr && a.cache_pages > 0 && pool_rows < (int64_t)INT32_MAX &&
+                   decode_tma_enabled() && (reinterpret_cast<uintptr_t>(a.cache) & 15) == 0;
+  const bool cluster = !tma && splits > 1 && splits <= 8 && a.ws == nullptr && decode_cluster_enabled();
+  if (splits > 1 && !cluster) {
     const size_t need = decode_attention_scratch_bytes(a.B, a.Hq, a.D, splits);
     float* ws = a.ws;
     if (ws == nullptr) {
@@ -1130,10 +1190,7 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
     p.counters = a.counters ? a.counters : tile_counters_get(st) + 32768;
   }
   // persistent TMA kernel: bf16 pages, row coordinates of the pool within int32
-  const int64_t pool_rows = a.cache_pages * a.num_layers * 2 * a.KH * kPage;
-  if (!a.cache_fp8 && a.positions == nullptr && a.cache_pages > 0 && pool_rows < (int64_t)INT32_MAX &&
-      decode_tma_enabled() &&
-      (reinterpret_cast<uintptr_t>(a.cache) & 15) == 0) {
+  if (tma) {
     if (splits > 1) VRM_REQUIRE(p.ws_o != nullptr && p.counters != nullptr, "decode attention: scratch");
     DecodeTmaParams t;
     t.q = p.q;
@@ -1164,6 +1221,18 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
     return;
   }
   dim3 grid(a.KH, a.B, splits);
+  // 2..8 splits of a caller without its own scratch merge inside a cluster (the caller
+  // that brings scratch keeps the counter merge over it)
+  if (cluster) {
+    if (a.D == 128) {
+      if (a.cache_fp8) launch_decode<128, true, true>(grid, p, st);
+      else launch_decode<128, false, true>(grid, p, st);
+    } else {
+      if (a.cache_fp8) launch_decode<64, true, true>(grid, p, st);
+      else launch_decode<64, false, true>(grid, p, st);
+    }
+    return;
+  }
   if (a.D == 128) {
     if (a.cache_fp8) launch_decode<128, true>(grid, p, st);
     else launch_decode<128, false>(grid, p, st);
