@@ -1188,13 +1188,18 @@ static void choose_split(int tiles, int k_tiles, int min_k, int* splits, int* kt
 // VRM_GEMM_PREFILL=streamk runs M > 128 on the stream-K swap kernel (default: the tiled
 // kernel, whose concurrent CTAs share each weight tile in L2; stream-K walks a weight
 // tile's token blocks one after another and re-reads it from HBM once it is evicted)
-static bool prefill_streamk() {
-  static const bool v = [] {
+// 0: tiled kernel, 1: stream-K with 128-token tiles, 2: stream-K with 256-token tiles
+// (MMA 128 x 256, four 48 KB stages, 512 TMEM columns: one CTA per SM)
+static int prefill_mode() {
+  static const int v = [] {
     const char* e = std::getenv("VRM_GEMM_PREFILL");
-    return e && std::string(e) == "streamk";
+    if (!e) return 0;
+    const std::string m(e);
+    return m == "streamk256" ? 2 : m == "streamk" ? 1 : 0;
   }();
   return v;
 }
+static bool prefill_streamk() { return prefill_mode() != 0; }
 
 // Persistent CTAs of the stream-K decode GEMM.  Latency model fitted on B200 (µs): a
 // CTA streams its share of the weights at ~80 GB/s; tiles shared by nc CTAs add ~1 µs
@@ -1323,8 +1328,13 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     // wave), six stages of 32 KB, one CTA per SM
     VRM_REQUIRE(!a.allreduce, "fused all-reduce needs M <= 128 (decode); use the collective for prefill");
     const CUtensorMap ma = make_kmajor_map(a.w, a.N, a.K, a.ldw, kBM);
-    const CUtensorMap mb = make_kmajor_map(a.x, a.M, a.K, a.ldx, 128);
-    launch_streamk<128, 6, false>(ma, mb, ep, a.N, a.K, device_sm_count(), stream, ARParams{}, (a.M + 127) / 128);
+    if (prefill_mode() == 2) {
+      const CUtensorMap mb = make_kmajor_map(a.x, a.M, a.K, a.ldx, 256);
+      launch_streamk<256, 4, false>(ma, mb, ep, a.N, a.K, device_sm_count(), stream, ARParams{}, (a.M + 255) / 256);
+    } else {
+      const CUtensorMap mb = make_kmajor_map(a.x, a.M, a.K, a.ldx, 128);
+      launch_streamk<128, 6, false>(ma, mb, ep, a.N, a.K, device_sm_count(), stream, ARParams{}, (a.M + 127) / 128);
+    }
   } else {
     VRM_REQUIRE(!a.allreduce, "fused all-reduce needs M <= 128 (decode); use the collective for prefill");
     constexpr int BN = 128;
