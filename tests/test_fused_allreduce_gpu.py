@@ -151,3 +151,58 @@ def test_fused_allreduce_wait_times_out_and_reports():
         assert float(torch.ones(4, device=DEV).sum().item()) == 4.0
     finally:
         ranks.free()
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+@pytest.mark.parametrize("m", [1, 32])
+def test_fused_push_reduce_one_kernel(world, m):
+    """GEMM + push + reduce into the residual + norm sums in one launch (rank 0); the
+    other emulated ranks' partials are pushed first by plain push GEMMs, so rank 0's
+    kernel finds every slot filled and waits on nothing that runs at the same time."""
+    n, k = 1024, 512
+    g = torch.Generator(device=DEV).manual_seed(7 * world + m)
+    ranks = Ranks(world)
+    try:
+        xs = [torch.randn(m, k, device=DEV, generator=g).bfloat16() for _ in range(world)]
+        ws = [(torch.randn(n, k, device=DEV, generator=g) * 0.05).bfloat16() for _ in range(world)]
+        bias = torch.randn(n, device=DEV, generator=g).bfloat16()
+        res0 = torch.randn(m, n, device=DEV, generator=g).bfloat16()
+        want_s, _ = _reference(xs, ws, bias, res0, torch.ones(n, device=DEV).bfloat16())
+        want_ssq = want_s.view(m, n // 128, 128).pow(2).sum(-1).t()
+        for it in range(3):
+            for r in range(1, world):
+                ranks.push(r, xs[r], ws[r])
+            resid = res0.clone()
+            ssq = torch.zeros(n // 128, 128, device=DEV)
+            ops.native().gemm_ar_push(xs[0], ws[0], ranks.ptrs, ranks.epoch[0], 0, world, ranks.half, None, None,
+                                      resid, bias, ssq, ranks.done[0], 0)
+            torch.cuda.synchronize()
+            assert _rel(resid, want_s) < 1e-2
+            assert _rel(ssq[:, :m], want_ssq) < 2e-2
+            # the other ranks' halves were consumed only by rank 0: empty them for the next round
+            for r in range(1, world):
+                ranks.reduce(r, m, n, residual=torch.zeros(m, n, device=DEV, dtype=torch.bfloat16))
+        assert int(ranks.epoch[0].item()) == 3
+        assert ops.read_and_clear_errors() == 0
+    finally:
+        ranks.free()
+
+
+def test_fused_push_reduce_times_out_and_reports():
+    m, n, k = 2, 512, 256
+    g = torch.Generator(device=DEV).manual_seed(5)
+    ranks = Ranks(2)
+    try:
+        x = torch.randn(m, k, device=DEV, generator=g).bfloat16()
+        w = (torch.randn(n, k, device=DEV, generator=g) * 0.05).bfloat16()
+        resid = torch.zeros(m, n, device=DEV, dtype=torch.bfloat16)
+        err_before = ops.read_and_clear_errors()
+        assert err_before == 0
+        ops.native().gemm_ar_push(x, w, ranks.ptrs, ranks.epoch[0], 0, 2, ranks.half, None, None, resid, None,
+                                  None, ranks.done[0], 2_000_000)
+        torch.cuda.synchronize()
+        assert ops.read_and_clear_errors() & K_ERR_FLAG_TIMEOUT
+        assert _rel(resid, x.float() @ w.float().t()) < 1e-2       # the missing rank counted as 0
+        assert float(torch.ones(4, device=DEV).sum().item()) == 4.0
+    finally:
+        ranks.free()

@@ -66,6 +66,39 @@ def test_gemm_silu_and_residual_epilogues(M, cuda_errors_clean):
     _close(rg, ref_r)
 
 
+@pytest.mark.parametrize("M", [1, 32])
+@pytest.mark.parametrize("N,K,epi", [(896, 5120, "bias"), (3456, 5120, "silu"), (5120, 640, "residual"),
+                                     (5120, 1728, "ssq")])
+def test_gemm_tp_shard_shapes(M, N, K, epi, cuda_errors_clean):
+    """Decode GEMMs of tensor-parallel shard shapes, whose tiles split over 2..8 CTAs of
+    one thread-block cluster (fixup through distributed shared memory): every epilogue
+    kind against the fp32 reference, and bitwise the same on a second call."""
+    torch.manual_seed(M + N + K)
+    x = (torch.randn(M, K) * 0.5).bfloat16()
+    w = (torch.randn(N, K) * 0.05).bfloat16()
+    b = (torch.randn(N) * 0.1).bfloat16()
+    xg, wg, bg = x.to(DEV), w.to(DEV), b.to(DEV)
+    if epi == "bias":
+        ref, got = ops.linear(x, w, b), [ops.linear(xg, wg, bg) for _ in range(2)]
+    elif epi == "silu":
+        ref = ops.linear(x, w, epilogue=ops.EPI_SILU_MUL)
+        got = [ops.linear(xg, wg, epilogue=ops.EPI_SILU_MUL) for _ in range(2)]
+    else:
+        r = torch.randn(M, N).bfloat16()
+        ref = ops.linear(x, w, residual=r)
+        got = []
+        for _ in range(2):
+            rg = r.to(DEV)
+            buf = torch.zeros((N + 127) // 128, 128, device=DEV) if epi == "ssq" else None
+            ops.linear(xg, wg, residual=rg, out=rg, ssq_out=buf)
+            got.append(rg)
+            if buf is not None:
+                want = (rg.float() ** 2).view(M, -1, 128).sum(-1).t()
+                _close(buf[:, :M], want, rtol=1e-5, atol=1e-3)
+    _close(got[0], ref)
+    assert torch.equal(got[0], got[1])
+
+
 # ------------------------------------------------------------------------- norms
 @pytest.mark.parametrize("H", [128, 768, 3584, 5120])
 @pytest.mark.parametrize("with_res", [False, True])

@@ -28,6 +28,8 @@
 #include <mutex>
 #include <unordered_map>
 
+#include <cooperative_groups.h>
+
 #include "vrm_common.cuh"
 #include "vrm_host.h"
 #include "vrm_kernels.h"
@@ -124,6 +126,39 @@ __device__ __forceinline__ void sum_partials16_t(const float* base, int nc, int 
         x[u][j] = q0 + u < nc ? __ldcg(base + (size_t)(q0 + u) * (kBM * BN) + (size_t)(c0 + j) * kBM) : 0.f;
 #pragma unroll
     for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) out[j] += x[u][j];
+  }
+}
+
+// Cluster barrier halves (non-aligned: threads of divergent roles call them on their own).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait;" ::: "memory"); }
+
+// Cluster fixup of a split tile: the owner (cluster rank 0) sums the 16-column chunk c0
+// of contributors 1 .. nc-1, read from their shared memory ([column][row] fp32), four
+// peers' loads in flight at once, in contributor order.
+template <int BN>
+__device__ __forceinline__ void sum_peers16(const float* s_part, int nc, int c0, int row, float (&out)[16]) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) out[j] = 0.f;
+  for (int q0 = 1; q0 < nc; q0 += 4) {
+    float x[4][16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (q0 + u < nc) {
+        const float* src = cluster.map_shared_rank(s_part, q0 + u) + row;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x[u][j] = src[(c0 + j) * kBM];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x[u][j] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
 #pragma unroll
       for (int j = 0; j < 16; ++j) out[j] += x[u][j];
   }
@@ -467,6 +502,9 @@ struct StreamK {
   int64_t iters;   // tiles * k_tiles
   int ctas;
   int tiles_x;     // token blocks of BN tokens; tile t = (weight block t / tiles_x, token block t % tiles_x)
+  // > 1: ctas == tiles * cluster, each tile's CTAs are one thread-block cluster and the
+  // split-tile fixup goes through distributed shared memory (no global partials)
+  int cluster;
   __device__ __forceinline__ int64_t start(int c) const { return (int64_t)c * iters / ctas; }
   __device__ __forceinline__ int owner(int64_t i) const {
     int c = (int)(((i + 1) * ctas - 1) / iters);
@@ -483,6 +521,84 @@ struct StreamK {
 // slot is local) and never waits.  No fence and no flag: ar_norm.cu polls the values
 // themselves (empty pattern 0x8000), so the transfer costs one NVLink write latency.
 using ARParams = ARPush;
+
+// Fused reduce of the all-reduce (ARPush::reduce), run by every warp of the push GEMM
+// after its own stores: item (token m, 128-feature chunk t); lane l takes 4 features.
+__device__ __forceinline__ void ar_reduce_tail(const ARParams& ar, int M, int N, uint32_t* __restrict__ err) {
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(ar.epoch);
+  __nv_bfloat16* half = ar.xbuf[ar.rank] + (size_t)(epoch & 1u) * ar.world * (size_t)ar.half_floats;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  const int parts = (N + 127) / 128;
+  const unsigned long long limit = ar.spin_limit ? ar.spin_limit : VRM_SPIN_LIMIT_CYCLES;
+  const auto* bias = reinterpret_cast<const __nv_bfloat16*>(ar.bias);
+  auto* res = reinterpret_cast<__nv_bfloat16*>(ar.residual);
+  const uint2 empty = make_uint2(kBf16EmptyX2, kBf16EmptyX2);
+  bool timed_out = false;
+  for (int item = blockIdx.x * nw + warp; item < M * parts; item += gridDim.x * nw) {
+    const int m = item / parts, t = item - m * parts;
+    const int f = t * 128 + lane * 4;
+    float q = 0.f;
+    if (f < N) {
+      __nv_bfloat16* src = half + (size_t)m * N + f;
+      uint2 x[8];
+#pragma unroll
+      for (int p = 0; p < 8; ++p)
+        if (p < ar.world) x[p] = ld_relaxed_sys_v2(src + (size_t)p * ar.half_floats);
+      const unsigned long long t0 = clock64();
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        if (p >= ar.world) continue;
+        while (bf16x4_has_empty(x[p])) {
+          if (timed_out || (unsigned long long)(clock64() - t0) > limit) {
+            if (!timed_out) report_error(err, kErrFlagTimeout);
+            timed_out = true;
+            auto z = [](uint32_t w) {
+              if ((w & 0xffffu) == kBf16Empty) w &= 0xffff0000u;
+              if ((w >> 16) == kBf16Empty) w &= 0x0000ffffu;
+              return w;
+            };
+            x[p] = make_uint2(z(x[p].x), z(x[p].y));
+            break;
+          }
+          x[p] = ld_relaxed_sys_v2(src + (size_t)p * ar.half_floats);
+        }
+      }
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        if (p >= ar.world) continue;
+        v[0] += bf16_lo(x[p].x); v[1] += bf16_hi(x[p].x); v[2] += bf16_lo(x[p].y); v[3] += bf16_hi(x[p].y);
+        *reinterpret_cast<uint2*>(src + (size_t)p * ar.half_floats) = empty;   // free for two calls on
+      }
+      if (bias) {
+        const uint2 b = *reinterpret_cast<const uint2*>(bias + f);
+        v[0] += bf16_lo(b.x); v[1] += bf16_hi(b.x); v[2] += bf16_lo(b.y); v[3] += bf16_hi(b.y);
+      }
+      __nv_bfloat16* rrow = res + (size_t)m * N + f;
+      const uint2 r = *reinterpret_cast<const uint2*>(rrow);
+      v[0] += bf16_lo(r.x); v[1] += bf16_hi(r.x); v[2] += bf16_lo(r.y); v[3] += bf16_hi(r.y);
+      uint2 o;
+      o.x = pack_bf16x2(v[0], v[1]);
+      o.y = pack_bf16x2(v[2], v[3]);
+      *reinterpret_cast<uint2*>(rrow) = o;
+      // the residual stream is bf16: the norm sums are over the rounded values
+      const float a0 = bf16_lo(o.x), a1 = bf16_hi(o.x), a2 = bf16_lo(o.y), a3 = bf16_hi(o.y);
+      q = a0 * a0 + a1 * a1 + a2 * a2 + a3 * a3;
+    }
+    q = warp_sum(q);
+    if (lane == 0 && ar.ssq_out != nullptr) ar.ssq_out[(size_t)t * ar.ssq_ld + m] = q;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ar.done) : "memory");
+    if (prev == gridDim.x - 1) {
+      *ar.done = 0u;
+      *reinterpret_cast<volatile uint32_t*>(const_cast<uint32_t*>(ar.epoch)) = epoch + 1u;
+    }
+  }
+}
 
 template <int BN, int STAGES, bool kAR, bool kF8 = false>
 __global__ void __launch_bounds__(kGemmThreads, 2)
@@ -675,6 +791,10 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       }
     }
     int chunk_no = 0;   // parity selects the s_ssq half (one barrier per chunk)
+    const bool clm = sk.cluster > 1;
+    bool phase1 = false;
+    // cluster mode: a contributor's partial, [column][row] fp32, in its (drained) stages
+    float* s_part = reinterpret_cast<float*>(smem);
     int seg = 0;
     for (int64_t it = it_begin; it < it_end; ++seg) {
       const int t = (int)(it / k_tiles);
@@ -703,17 +823,25 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 #pragma unroll
       for (int j = 0; j < 16; ++j) others0[j] = 0.f;
       if (is_owner && !whole) {
-        if (threadIdx.x == 64) {
-          const unsigned long long t0 = clock64();
-          while (ld_acquire_gpu(tile_counters + t) < (uint32_t)(nc - 1)) {
-            if ((unsigned long long)(clock64() - t0) > VRM_SPIN_LIMIT_CYCLES) {
-              report_error(err, kErrFlagTimeout);
-              break;
+        if (clm) {
+          // phase 1: every contributor of the cluster has its partial in shared memory
+          cluster_arrive();
+          cluster_wait();
+          phase1 = true;
+          sum_peers16<BN>(s_part, nc, 0, row, others0);
+        } else {
+          if (threadIdx.x == 64) {
+            const unsigned long long t0 = clock64();
+            while (ld_acquire_gpu(tile_counters + t) < (uint32_t)(nc - 1)) {
+              if ((unsigned long long)(clock64() - t0) > VRM_SPIN_LIMIT_CYCLES) {
+                report_error(err, kErrFlagTimeout);
+                break;
+              }
             }
           }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          sum_partials16_t<BN>(base, nc, 0, others0);
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        sum_partials16_t<BN>(base, nc, 0, others0);
       }
       const bool ok = mbar_wait(&tfull[acc], (uint32_t)((seg >> 1) & 1), err);
       tc_fence_after();
@@ -726,9 +854,14 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = ok ? __uint_as_float(r[j]) : 0.f;
         if (!is_owner) {
-          float* slot = workspace + (size_t)c * (size_t)(kBM * BN);
+          if (clm) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) __stcg(slot + (size_t)(c0 + j) * kBM + row, v[j]);
+            for (int j = 0; j < 16; ++j) s_part[(c0 + j) * kBM + row] = v[j];
+          } else {
+            float* slot = workspace + (size_t)c * (size_t)(kBM * BN);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) __stcg(slot + (size_t)(c0 + j) * kBM + row, v[j]);
+          }
           continue;
         }
         if (!whole) {
@@ -737,6 +870,8 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           if (c0 == 0) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) o[j] = others0[j];
+          } else if (clm) {
+            sum_peers16<BN>(s_part, nc, c0, row, o);
           } else {
             sum_partials16_t<BN>(base, nc, c0, o);
           }
@@ -798,7 +933,9 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
-      if (!is_owner) {
+      if (clm) {
+        // cluster mode: one segment per CTA, handed over through shared memory
+      } else if (!is_owner) {
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (threadIdx.x == 64) {
           uint32_t prev;
@@ -809,7 +946,24 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       }
       it += n;
     }
+    if (clm) {
+      // contributors (and idle CTAs) publish in phase 1; phase 2 keeps every CTA's
+      // shared memory alive until its cluster's owner has read it
+      if (!phase1) {
+        cluster_arrive();
+        cluster_wait();
+      }
+      cluster_arrive();
+      cluster_wait();
+    }
     if (tr && threadIdx.x == 64) tr[5] = globaltimer();
+  }
+  if (sk.cluster > 1 && warp < 2) {
+    // the producer / MMA warps take part in both cluster phases of the fixup
+    cluster_arrive();
+    cluster_wait();
+    cluster_arrive();
+    cluster_wait();
   }
 
   tc_fence_before();
@@ -818,6 +972,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  if (kAR && ar.reduce) ar_reduce_tail(ar, ep.M, ep.N, err);
 }
 
 // =====================================================================================
@@ -1167,8 +1322,26 @@ static void launch_streamk(const CUtensorMap& mw, const CUtensorMap& mx, const E
   VRM_REQUIRE(tiles <= 32768, "stream-K: too many tiles");
   float* ws = static_cast<float*>(workspace_get((size_t)sk.ctas * kBM * BN * sizeof(float), stream));
   if (kAR) VRM_REQUIRE((long long)ep.M * N <= ar.half_floats, "fused all-reduce: output larger than the symmetric buffer");
-  launch_kernel(kern, dim3(sk.ctas), dim3(kGemmThreads), (size_t)kSmem, stream, mw, mx, ep, ws, counters, k_tiles,
-                sk, error_word(), g_gemm_trace, ar);
+  if (kAR && ar.reduce) {
+    // every CTA polls data other CTAs of the launch produce: the whole grid must be
+    // resident at once (two CTAs per SM fit by registers and shared memory, BN <= 128)
+    VRM_REQUIRE(BN <= 128 && sk.ctas <= 2 * device_sm_count(), "fused reduce: grid larger than one resident wave");
+    VRM_REQUIRE(ar.world >= 1 && ar.world <= 8 && N % 4 == 0 && ar.residual && ar.done,
+                "fused reduce: world <= 8, N % 4 == 0, residual and completion counter required");
+  }
+  // a tile split evenly over k CTAs (k = 2..8) fixes up inside a thread-block cluster
+  static const bool cluster_on = [] {
+    const char* e = std::getenv("VRM_GEMM_CLUSTER");
+    return !(e && e[0] == '0');
+  }();
+  const int k = sk.ctas % tiles == 0 ? sk.ctas / tiles : 0;
+  sk.cluster = (cluster_on && k >= 2 && k <= 8 && k <= k_tiles) ? k : 0;
+  if (sk.cluster > 1)
+    launch_kernel_cluster(kern, dim3(sk.ctas), dim3(kGemmThreads), dim3(sk.cluster, 1, 1), (size_t)kSmem, stream,
+                          mw, mx, ep, ws, counters, k_tiles, sk, error_word(), g_gemm_trace, ar);
+  else
+    launch_kernel(kern, dim3(sk.ctas), dim3(kGemmThreads), (size_t)kSmem, stream, mw, mx, ep, ws, counters,
+                  k_tiles, sk, error_word(), g_gemm_trace, ar);
 }
 
 // Split count such that tiles * splits covers the SMs with >= min_k K-tiles per split.
@@ -1213,13 +1386,23 @@ static int streamk_ctas(int tiles, int k_tiles, int BN, double weight_bytes) {
   }();
   const int sms = device_sm_count();
   if (env > 0) return std::min(env, sms);
+  static const bool cluster_on = [] {
+    const char* e = std::getenv("VRM_GEMM_CLUSTER");
+    return !(e && e[0] == '0');
+  }();
   auto cost = [&](int ctas) {
     const int64_t iters = (int64_t)tiles * k_tiles;
     ctas = (int)std::min<int64_t>(ctas, iters);
     const double per_cta = weight_bytes / ctas;
     const int nc = (ctas + tiles - 1) / tiles;
     double t = per_cta / 80e3;
-    if (ctas > tiles || nc > 1) t += 1.0 + 0.6 * ((nc - 1 + 3) / 4) * (BN / 16);
+    const bool aligned = ctas % tiles == 0 && nc <= 8 && nc <= k_tiles;
+    if (ctas > tiles || nc > 1) {
+      // global fixup: the owner sums partials from L2, two per round; cluster fixup
+      // (aligned splits): from its peers' shared memory, four per round
+      t += (aligned && cluster_on) ? 0.5 + 0.25 * ((nc - 1 + 3) / 4) * (BN / 16)
+                                   : 1.0 + 0.6 * ((nc - 1 + 3) / 4) * (BN / 16);
+    }
     return t;
   };
   int best = sms;

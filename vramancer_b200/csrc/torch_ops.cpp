@@ -382,7 +382,9 @@ void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k
 // partial into this rank's slot of every rank's receive buffer (ARPush).  Nothing is
 // written to a tensor here.
 void gemm_ar_push(const Tensor& x, const Tensor& w, const Tensor& xbuf_ptrs, const Tensor& epoch, int64_t rank,
-                  int64_t world, int64_t half_floats, const OptT& scale_x, const OptT& scale_w) {
+                  int64_t world, int64_t half_floats, const OptT& scale_x, const OptT& scale_w,
+                  const OptT& residual, const OptT& bias, const OptT& ssq_out, const OptT& done,
+                  int64_t spin_limit) {
   const bool f8 = w.scalar_type() == torch::kFloat8_e4m3fn || w.scalar_type() == torch::kByte;
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1,
               "gemm_ar: 2-D CUDA operands with unit inner stride");
@@ -403,6 +405,28 @@ void gemm_ar_push(const Tensor& x, const Tensor& w, const Tensor& xbuf_ptrs, con
   ar.rank = (int)rank;
   ar.world = (int)world;
   ar.half_floats = half_floats;
+  if (has(residual)) {
+    // fused reduce: sum of every rank's partial (+ bias) into the residual stream, norm sums
+    same_device_opt(x, {&residual, &bias, &ssq_out, &done}, "gemm_ar");
+    TORCH_CHECK(residual->scalar_type() == torch::kBFloat16 && residual->is_contiguous() &&
+                    residual->numel() == M * N,
+                "gemm_ar: residual must be contiguous bf16 [M, N]");
+    TORCH_CHECK(has(done) && done->scalar_type() == torch::kInt32, "gemm_ar: fused reduce needs its done counter");
+    if (has(bias))
+      TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->numel() == N && bias->is_contiguous(),
+                  "gemm_ar: bias bf16 [N]");
+    if (has(ssq_out))
+      TORCH_CHECK(ssq_out->scalar_type() == torch::kFloat32 && ssq_out->dim() == 2 &&
+                      ssq_out->size(0) >= (N + 127) / 128 && ssq_out->size(1) >= M && ssq_out->is_contiguous(),
+                  "gemm_ar: ssq_out fp32 [>= ceil(N / 128), >= M]");
+    ar.reduce = 1;
+    ar.residual = residual->data_ptr();
+    ar.bias = has(bias) ? bias->data_ptr() : nullptr;
+    ar.ssq_out = has(ssq_out) ? ssq_out->data_ptr<float>() : nullptr;
+    ar.ssq_ld = has(ssq_out) ? (int)ssq_out->size(1) : 0;
+    ar.done = reinterpret_cast<uint32_t*>(done->data_ptr());
+    ar.spin_limit = spin_limit > 0 ? (unsigned long long)spin_limit : 0ull;
+  }
   vrm::GemmArgs a;
   a.x = x.data_ptr();
   a.ldx = x.stride(0);   // elements (bf16) or bytes (e4m3)
@@ -1111,8 +1135,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "routed experts of a MoE layer on the device (plan, gather, grouped tcgen05 GEMMs, combine)");
   m.def("gemm_ar_push", &gemm_ar_push, py::arg("x"), py::arg("w"), py::arg("xbuf_ptrs"), py::arg("epoch"),
         py::arg("rank"), py::arg("world"), py::arg("half_floats"), py::arg("scale_x") = py::none(),
-        py::arg("scale_w") = py::none(),
-        "row-parallel GEMM storing its partial into every rank's receive buffer (fused all-reduce, push)");
+        py::arg("scale_w") = py::none(), py::arg("residual") = py::none(), py::arg("bias") = py::none(),
+        py::arg("ssq_out") = py::none(), py::arg("done") = py::none(), py::arg("spin_limit") = 0,
+        "row-parallel GEMM storing its partial into every rank's receive buffer (fused all-reduce, push); with "
+        "residual, the same kernel also reduces into the residual stream and stores the RMSNorm sums");
   m.def("ar_norm", &ar_norm, py::arg("xbuf"), py::arg("epoch"), py::arg("done"), py::arg("rank"), py::arg("world"),
         py::arg("half_floats"), py::arg("T"), py::arg("H"), py::arg("bias"), py::arg("residual"), py::arg("w"),
         py::arg("b"), py::arg("out"), py::arg("mode"), py::arg("eps"), py::arg("spin_limit") = 0,

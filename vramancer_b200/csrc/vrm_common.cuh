@@ -373,6 +373,15 @@ __device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void* p) {
                : "memory");
   return v;
 }
+__device__ __forceinline__ uint2 ld_relaxed_sys_v2(const void* p) {
+  uint2 v;
+  asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool bf16x4_has_empty(uint2 x) {
+  auto e = [](uint32_t w) { return (w & 0xffffu) == kBf16Empty || (w >> 16) == kBf16Empty; };
+  return e(x.x) || e(x.y);
+}
 // true when any of the 8 bf16 lanes of x still holds the empty pattern
 __device__ __forceinline__ bool bf16x8_has_empty(uint4 x) {
   auto e = [](uint32_t w) { return (w & 0xffffu) == kBf16Empty || (w >> 16) == kBf16Empty; };

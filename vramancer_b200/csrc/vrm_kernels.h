@@ -61,6 +61,20 @@ struct ARPush {
   const uint32_t* epoch = nullptr;       // this rank's call counter (device, advanced by ar_norm)
   int rank = 0, world = 1;
   long long half_floats = 0;             // elements per (half, source rank) slot
+  // Fused reduce (reduce != 0, stream-K bf16 / e4m3 GEMM): after its push, the same
+  // kernel's warps take (token, 128-feature chunk) items of this rank's receive buffer,
+  // poll until every rank's values have arrived, sum them in rank order (+ bias) into
+  // the bf16 residual stream (in place) and store the chunk's sum of squares of the new
+  // residual at ssq_out[chunk * ssq_ld + token] (the next GEMM applies the RMSNorm from
+  // them, folded-norm consumer), empty the slots and, last warp of the launch, advance
+  // *epoch.  Needs every CTA of the launch resident at once (persistent grid).
+  int reduce = 0;
+  const void* bias = nullptr;            // bf16 [N] or null
+  void* residual = nullptr;              // bf16 [M, N] (row stride N), updated in place
+  float* ssq_out = nullptr;              // [ceil(N / 128)][ssq_ld] or null
+  int ssq_ld = 0;
+  uint32_t* done = nullptr;              // zeroed completion counter of this rank
+  unsigned long long spin_limit = 0;     // 0: the library default
 };
 void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
 // FP8 W8A8: x, w are e4m3 bytes ([M, K], [N, K], strides in bytes); y = (x w^T) *

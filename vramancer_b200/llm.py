@@ -121,7 +121,8 @@ class LLM:
                                       decode_microbatches=decode_microbatches)
         else:
             self.model = DecoderModel(cfg, weights, device=self.device, dtype=dtype, tp=tp, ep=ep)
-            if (fold_norms and self.quantization is None and ep is None and (tp is None or tp.size == 1)
+            if (fold_norms and self.quantization is None and ep is None
+                    and (tp is None or tp.size == 1 or getattr(tp, "fused_ar", None) is not None)
                     and os.environ.get("VRM_FOLD_NORM", "1") != "0"):
                 # small decode batches run the RMSNorms inside the GEMMs (weights folded in place)
                 self.model.fold_norms()

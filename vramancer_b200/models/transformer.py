@@ -70,6 +70,9 @@ class TPContext:
 # sums of squares the previous GEMM stored.
 _FOLDED = object()
 FOLD_MAX_TOKENS = int(os.environ.get("VRM_FOLD_MAX_TOKENS", "16"))
+# Under tensor parallelism the folded norm replaces the reduce kernel altogether (the
+# row-parallel GEMM reduces and stores the norm sums itself): every fused decode batch.
+FOLD_MAX_TOKENS_TP = int(os.environ.get("VRM_FOLD_MAX_TOKENS_TP", "128"))
 
 
 class DecoderModel:
@@ -134,7 +137,7 @@ class DecoderModel:
         cfg = self.cfg
         if self.folded:
             return self._alloc_fold()
-        if (self.device.type != "cuda" or self.tp_size != 1 or cfg.is_gpt2 or cfg.is_moe
+        if (self.device.type != "cuda" or not self._fold_capable() or cfg.is_gpt2 or cfg.is_moe
                 or self.dtype != torch.bfloat16 or cfg.hidden_size > 64 * 128 or self.last_layer <= self.first_layer):
             return False
         pairs = []
@@ -153,8 +156,13 @@ class DecoderModel:
         self._ones = torch.ones(cfg.hidden_size, dtype=self.dtype, device=self.device)
         return self._alloc_fold()
 
+    def _fold_capable(self) -> bool:
+        """One GPU, or tensor parallelism with the fused all-reduce (whose row-parallel
+        GEMM stores the norm sums of the reduced residual)."""
+        return self.tp_size == 1 or (self.tp is not None and self.tp.fused_ar is not None)
+
     def _alloc_fold(self) -> bool:
-        if self.device.type == "cuda" and self.tp_size == 1 and self._ssq is None:
+        if self.device.type == "cuda" and self._fold_capable() and self._ssq is None:
             self._ssq_parts = (self.cfg.hidden_size + 127) // 128
             self._ssq = torch.zeros(self._ssq_parts, 128, dtype=torch.float32, device=self.device)
         return self.folded
@@ -211,6 +219,14 @@ class DecoderModel:
             ops.linear(x, w, b, residual=r, out=r)
             return self._norm(r, nxt[0] if nxt[0] is not None else "final", nxt[1]) if nxt else None
         far = self.tp.fused_ar
+        if far is not None and x.is_cuda and self._fold_active and far.supports_reduce(x.shape[0], w):
+            # one kernel: GEMM, push to every rank, reduce + bias into the residual stream
+            # and the norm sums the next GEMM normalises from
+            last = not nxt or nxt[0] is None
+            far.push_reduce(x, w, residual=r, bias=b, ssq_out=None if last else self._ssq)
+            if not nxt:
+                return None
+            return _FOLDED if not last else self._norm(r, "final", "final")
         if far is not None and x.is_cuda and far.supports_weight(x.shape[0], w):
             # push the partial to every rank (bf16, fp8 or NVFP4 weights), then one
             # kernel: reduce + bias + residual + norm
@@ -236,6 +252,8 @@ class DecoderModel:
     def _norm_params(self, i: Optional[int], which: str):
         if i is None:
             return self.w["final_norm_w"], self.w.get("final_norm_b")
+        if self.folded and which in ("in_norm", "post_norm"):
+            return self._ones, None          # the weight lives in the next GEMM's columns
         return self.lw(i, f"{which}_w"), self.lw(i, f"{which}_b")
 
     def _mlp(self, i: int, x: torch.Tensor, r: torch.Tensor, nxt: Optional[tuple]) -> Optional[torch.Tensor]:
@@ -305,8 +323,12 @@ class DecoderModel:
         # (Qwen2.5-14B, graph-replayed step): batch 1 6.38 -> 6.26 ms, but batch 32 7.58 ->
         # 8.36 ms (the norm-sum epilogue and the per-token rsqrt cost more than the norm
         # launches they replace there), so batches above 16 keep the norm kernels.
-        self._fold_active = (self._ssq is not None and batch.is_decode and r.is_cuda
-                             and r.shape[0] <= FOLD_MAX_TOKENS)
+        if self.tp_size == 1:
+            limit = FOLD_MAX_TOKENS
+        else:
+            far = self.tp.fused_ar
+            limit = min(FOLD_MAX_TOKENS_TP, far.max_tokens) if far is not None else 0
+        self._fold_active = (self._ssq is not None and batch.is_decode and r.is_cuda and r.shape[0] <= limit)
         x = None
         for i in range(self.first_layer, self.last_layer):
             x = self.layer(i, r, batch, pool, x)

@@ -86,6 +86,21 @@ class FusedAllReduce:
         ops.native().gemm_ar_push(x, w, self.xbuf_ptrs, self.epoch, self.rank, self.world, self.half_floats,
                                   scale_x, scale_w)
 
+    def push_reduce(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
+                    bias: Optional[torch.Tensor] = None, ssq_out: Optional[torch.Tensor] = None,
+                    spin_limit: int = 0) -> None:
+        """One kernel: row-parallel GEMM x @ w.T whose partial goes to every rank, then
+        the launch's warps sum every rank's partial in rank order (+ bias) into
+        `residual` (in place) and store the RMSNorm sums of the new residual per
+        128-feature chunk in ssq_out [chunks, >= tokens] (the next GEMM normalises
+        from them).  bf16 weights, decode batches (<= max_tokens)."""
+        ops.native().gemm_ar_push(x, w, self.xbuf_ptrs, self.epoch, self.rank, self.world, self.half_floats,
+                                  None, None, residual, bias, ssq_out, self.done, int(spin_limit))
+
+    def supports_reduce(self, m: int, w) -> bool:
+        return (getattr(w, "_vrm_quant", None) is None and isinstance(w, torch.Tensor)
+                and w.dtype == torch.bfloat16 and self.supports(m, w.shape[0]) and w.shape[0] % 4 == 0)
+
     def push_weight(self, x: torch.Tensor, w) -> None:
         """push() for any weight format of a row-parallel projection: bf16, FP8Weight
         (activations quantised per row to e4m3 first) or NVFP4Weight (decode, W4A16)."""
