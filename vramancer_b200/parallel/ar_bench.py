@@ -7,6 +7,8 @@ with CUDA events and reports the max over ranks:
   local   GEMM + residual RMSNorm, no communication (lower bound)
   nccl    GEMM, NCCL all-reduce (bf16), residual RMSNorm
   fused   push GEMM (partials to every rank over NVLink) + reduce/residual/RMSNorm
+  fused_one_kernel  the push GEMM whose own warps reduce into the residual and store
+          the RMSNorm sums (the next GEMM normalises): one launch
   ar      the NCCL all-reduce alone
 One JSON line per shape on rank 0.
 
@@ -82,11 +84,17 @@ def run(shapes, iters: int = 48) -> list:
             far.push(x, w)
             far.reduce(m, n, residual=r, out=o, norm_w=nw, eps=1e-6)
 
+        ssq = torch.zeros((n + 127) // 128, 128, device=dev)
+
+        def fused1():
+            # one kernel: GEMM + push + reduce into the residual + norm sums
+            far.push_reduce(x, w, residual=r, ssq_out=ssq)
+
         def ar():
             dist.all_reduce(y)
 
         res = {"world": tp.size, "M": m, "N": n, "K": k}
-        for name, fn in (("local", local), ("nccl", nccl), ("fused", fused), ("ar", ar)):
+        for name, fn in (("local", local), ("nccl", nccl), ("fused", fused), ("fused_one_kernel", fused1), ("ar", ar)):
             res[name + "_us"] = round(_time_graph(fn, iters), 2)
         out.append(res)
         if tp.rank == 0:
