@@ -1,5 +1,7 @@
-// Paged attention over the KV pool  cache[page, layer, {k,v}, kv_head, 16, head_dim]
-// with bf16 or fp8-e4m3 pages (per-(layer, k/v, kv_head) fp32 scales).
+// Paged attention over the KV pool  cache[page, layer, {k,v}, kv_head, 16, row]
+// with bf16 rows, fp8-e4m3 rows (per-(layer, k/v, kv_head) fp32 scales) or four-bit rows
+// (head_dim/2 code bytes + one fp16 {scale, min} pair per 32 dims, dequantised into the
+// bf16 MMA tile in shared memory).
 //
 // decode  (one new token per sequence):
 //   grid (kv_heads, batch, splits), 4 warps.  One CTA serves the whole GQA group of a
@@ -77,13 +79,43 @@ __device__ __forceinline__ void convert_fp8_tile(const uint8_t* raw, uint8_t* ds
   }
 }
 
+// rows x D four-bit rows (kBytes each, contiguous) at raw -> the swizzled bf16 tile at
+// dst; one thread per (row, 32-dim group), spread over nthr threads from tid.
+template <int D>
+__device__ __forceinline__ void convert_q4_tile(const uint8_t* raw, uint8_t* dst, int rows, int tid, int nthr) {
+  constexpr int kRowB = PageRow<D, kFmtQ4>::kBytes;
+  constexpr int kGroups = D / 32;
+  for (int i = tid; i < rows * kGroups; i += nthr) {
+    const int r = i / kGroups, gi = i % kGroups;
+    const uint8_t* row = raw + r * kRowB;
+    // the group's 32 codes (rows are 8-byte aligned: D/2 + D/8 bytes, D = 64 or 128)
+    const uint2 v0 = *reinterpret_cast<const uint2*>(row + gi * 16);
+    const uint2 v1 = *reinterpret_cast<const uint2*>(row + gi * 16 + 8);
+    const __half2 sm = *reinterpret_cast<const __half2*>(row + D / 2 + gi * 4);
+    const float sc = __low2float(sm), mn = __high2float(sm);
+    const uint32_t w[4] = {v0.x, v0.y, v1.x, v1.y};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {          // 8 values per output chunk
+      uint4 o;
+      uint32_t* q = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = fmaf((float)((w[c] >> (8 * j)) & 15u), sc, mn);
+        const float b = fmaf((float)((w[c] >> (8 * j + 4)) & 15u), sc, mn);
+        q[j] = pack_bf16x2(a, b);
+      }
+      *reinterpret_cast<uint4*>(dst + swz<D * 2>(r, gi * 4 + c)) = o;
+    }
+  }
+}
+
 // ============================================================== decode
-template <int D, bool kFp8>
+template <int D, int FMT>
 struct DecodeSmem {
-  static constexpr int kTileB = kPage * D * 2;              // one bf16 16 x D tile
-  static constexpr int kRawB = kFp8 ? kPage * D : kTileB;   // bytes per K (or V) page chunk
-  static constexpr int kStageB = 2 * kRawB;                 // K + V
-  static constexpr int kWarpB = 2 * kStageB + (kFp8 ? 2 * kTileB : 0);
+  static constexpr int kTileB = kPage * D * 2;                       // one bf16 16 x D tile
+  static constexpr int kRawB = kPage * PageRow<D, FMT>::kBytes;      // bytes per K (or V) page chunk
+  static constexpr int kStageB = 2 * kRawB;                          // K + V
+  static constexpr int kWarpB = 2 * kStageB + (FMT != kFmtBf16 ? 2 * kTileB : 0);
   static constexpr int kTotal = 4 * kWarpB;
 };
 
@@ -117,22 +149,46 @@ struct DecodeParams {
 
 // Stores this step's k (rotated) and v of sequence b, KV head kvh, into its cache slot,
 // with the rounding of the standalone RoPE + KV write kernel (k rounded to bf16 after
-// rotation; fp8 pages take that bf16 value / scale, saturating).
-template <int D, bool kFp8>
+// rotation; fp8 pages take that bf16 value / scale, saturating; four-bit pages quantise
+// the bf16 row per 32-dim group).
+template <int D, int FMT>
 __device__ __forceinline__ void decode_write_new_kv(const DecodeParams& P, int b, int kvh, int lane) {
   const int slot = P.slot_mapping[b];
   if (slot < 0 || !in_bounds(slot / kPage, P.num_pages, P.err)) return;
-  constexpr int kEl = kFp8 ? 1 : 2;
+  constexpr bool kFp8 = FMT == kFmtFp8;
+  constexpr int kRowB = PageRow<D, FMT>::kBytes;
   constexpr int H2 = D / 2;
   const int KH = P.KH;
   const __nv_bfloat16* row = P.q + (size_t)b * P.ld_q;
   const __nv_bfloat16* ks = row + (size_t)(P.Hq + kvh) * D;
   const __nv_bfloat16* vs = row + (size_t)(P.Hq + KH + kvh) * D;
   const int page = slot / kPage, off = slot % kPage;
-  const size_t head_stride = (size_t)kPage * D * kEl;
+  const size_t head_stride = (size_t)kPage * kRowB;
   uint8_t* kd = P.cache_w + (size_t)page * ((size_t)P.num_layers * 2 * KH * head_stride) +
-                (((size_t)P.layer * 2 + 0) * KH + kvh) * head_stride + (size_t)off * D * kEl;
+                (((size_t)P.layer * 2 + 0) * KH + kvh) * head_stride + (size_t)off * kRowB;
   uint8_t* vd = kd + (size_t)KH * head_stride;
+  const float* cs = P.cos_sin ? P.cos_sin + (size_t)P.positions[b] * D : nullptr;
+  if constexpr (FMT == kFmtQ4) {
+    // lane l quantises dims [D/32 l, D/32 (l + 1)) of k and of v
+    constexpr int kV = D / 32;
+    float xk[kV], xv[kV];
+#pragma unroll
+    for (int j = 0; j < kV; ++j) {
+      const int d = lane * kV + j;
+      float k = __bfloat162float(ks[d]);
+      if (cs) {
+        const int i = d < H2 ? d : d - H2;
+        float o1, o2;
+        rope_rotate(__bfloat162float(ks[i]), __bfloat162float(ks[i + H2]), cs[i], cs[H2 + i], o1, o2);
+        k = __bfloat162float(__float2bfloat16(d < H2 ? o1 : o2));
+      }
+      xk[j] = k;
+      xv[j] = __bfloat162float(vs[d]);
+    }
+    q4_store_row<D>(kd, xk, lane);
+    q4_store_row<D>(vd, xv, lane);
+    return;
+  }
   float kinv = 1.f, vinv = 1.f;
   if (kFp8) {
     kinv = 1.f / P.kv_scale[(P.layer * 2 + 0) * KH + kvh];
@@ -142,7 +198,6 @@ __device__ __forceinline__ void decode_write_new_kv(const DecodeParams& P, int b
     if (kFp8) dst[d] = __nv_cvt_float_to_fp8(__bfloat162float(x) * inv, __NV_SATFINITE, __NV_E4M3);
     else reinterpret_cast<__nv_bfloat16*>(dst)[d] = x;
   };
-  const float* cs = P.cos_sin ? P.cos_sin + (size_t)P.positions[b] * D : nullptr;
   for (int i = lane; i < H2; i += 32) {
     __nv_bfloat16 a = ks[i], c2 = ks[i + H2];
     if (cs) {
@@ -162,13 +217,13 @@ __device__ __forceinline__ void decode_write_new_kv(const DecodeParams& P, int b
 // merges a slice of the outputs from its peers' shared memory (no global partials, no
 // completion counter).  Otherwise splits merge through global scratch: the last CTA
 // to finish (counter) combines them.
-template <int D, bool kFp8, bool kCluster = false>
+template <int D, int FMT, bool kCluster = false>
 __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   pdl_launch();
-  using S = DecodeSmem<D, kFp8>;
+  using S = DecodeSmem<D, FMT>;
+  constexpr bool kFp8 = FMT == kFmtFp8;
   constexpr int ROWB = D * 2;
-  constexpr int kEl = kFp8 ? 1 : 2;
-  constexpr int kChunkPerRow = D * kEl / 16;
+  constexpr int kChunkPerRow = D * 2 / 16;   // bf16 pages: swizzled 16-byte chunks per row
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float s_m[4][8], s_l[4][8];
   __shared__ uint32_t s_last;
@@ -193,7 +248,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
 
   uint8_t* wbase = smem + warp * S::kWarpB;
   const int* bt = P.block_tables + (size_t)b * P.bt_stride;
-  const size_t head_stride = (size_t)kPage * D * kEl;                       // one (k|v, head) chunk
+  const size_t head_stride = (size_t)S::kRawB;                              // one (k|v, head) chunk
   const size_t page_stride = (size_t)P.num_layers * 2 * KH * head_stride;   // one page, all layers
 
   auto issue = [&](int page_local, int stage) {
@@ -203,11 +258,12 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
     const uint8_t* vp = kp + (size_t)KH * head_stride;
     uint8_t* dst = wbase + stage * S::kStageB;
     const uint32_t dk = smem_u32(dst), dv = smem_u32(dst + S::kRawB);
-    constexpr int kTotalChunks = kPage * kChunkPerRow;
+    constexpr int kTotalChunks = S::kRawB / 16;
 #pragma unroll
     for (int i = lane; i < kTotalChunks; i += 32) {
-      const int r = i / kChunkPerRow, ch = i % kChunkPerRow;
-      const uint32_t off = kFp8 ? (uint32_t)(i * 16) : swz<ROWB>(r, ch);
+      // bf16 pages land swizzled for ldmatrix; fp8 / four-bit pages land as stored and
+      // are converted into a swizzled bf16 tile after the wait
+      const uint32_t off = FMT == kFmtBf16 ? swz<ROWB>(i / kChunkPerRow, i % kChunkPerRow) : (uint32_t)(i * 16);
       cp_async16(dk + off, kp + (size_t)i * 16, true);
       cp_async16(dv + off, vp + (size_t)i * 16, true);
     }
@@ -228,7 +284,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
       warp == ((live_page - p_begin) & 3)) {
     // fused KV write: the warp that reads the live page stores this step's token first;
     // the fence orders the stores before that warp's cp.async reads of the page
-    decode_write_new_kv<D, kFp8>(P, b, kvh, lane);
+    decode_write_new_kv<D, FMT>(P, b, kvh, lane);
     __threadfence();
     __syncwarp();
   }
@@ -286,11 +342,16 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
     __syncwarp();
     uint8_t* kt = wbase + stage * S::kStageB;
     uint8_t* vt = kt + S::kRawB;
-    if (kFp8) {
+    if constexpr (FMT != kFmtBf16) {
       uint8_t* ck = wbase + 2 * S::kStageB;
       uint8_t* cv = ck + S::kTileB;
-      convert_fp8_tile<D>(kt, ck, kPage, lane, 32);
-      convert_fp8_tile<D>(vt, cv, kPage, lane, 32);
+      if constexpr (FMT == kFmtFp8) {
+        convert_fp8_tile<D>(kt, ck, kPage, lane, 32);
+        convert_fp8_tile<D>(vt, cv, kPage, lane, 32);
+      } else {
+        convert_q4_tile<D>(kt, ck, kPage, lane, 32);
+        convert_q4_tile<D>(vt, cv, kPage, lane, 32);
+      }
       __syncwarp();
       kt = ck;
       vt = cv;
@@ -570,7 +631,6 @@ template <int D>
 __global__ void __launch_bounds__(160, 1) paged_decode_tma_kernel(const __grid_constant__ CUtensorMap kvmap,
                                                                    DecodeTmaParams P) {
   using S = DecodeTmaSmem<D>;
-  constexpr int kChunkPerRow = D * 2 / 16;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* ring = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -834,14 +894,14 @@ __global__ void __launch_bounds__(160, 1) paged_decode_tma_kernel(const __grid_c
 }
 
 // ============================================================== prefill
-template <int D, bool kFp8>
+template <int D, int FMT>
 struct PrefillSmem {
   static constexpr int kRows = 64;
   static constexpr int kQB = kRows * D * 2;
   static constexpr int kTileB = kRows * D * 2;
-  static constexpr int kRawB = kFp8 ? kRows * D : kTileB;
+  static constexpr int kRawB = kRows * PageRow<D, FMT>::kBytes;
   static constexpr int kStageB = 2 * kRawB;
-  static constexpr int kTotal = kQB + 2 * kStageB + (kFp8 ? 2 * kTileB : 0);
+  static constexpr int kTotal = kQB + 2 * kStageB + (FMT != kFmtBf16 ? 2 * kTileB : 0);
 };
 
 struct PrefillParams {
@@ -861,14 +921,14 @@ struct PrefillParams {
   uint32_t* err;
 };
 
-template <int D, bool kFp8>
+template <int D, int FMT>
 __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
   pdl_launch();
   pdl_wait();
-  using S = PrefillSmem<D, kFp8>;
+  using S = PrefillSmem<D, FMT>;
+  constexpr bool kFp8 = FMT == kFmtFp8;
   constexpr int ROWB = D * 2;
-  constexpr int kEl = kFp8 ? 1 : 2;
-  constexpr int kChunkPerRow = D * kEl / 16;
+  constexpr int kChunkPerRow = D * 2 / 16;   // bf16 pages: swizzled 16-byte chunks per row
   extern __shared__ __align__(128) uint8_t smem[];
 
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -906,13 +966,14 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
   const int kv_end = min(ctx, prefix + q0 + 64);
   const int nchunks = (kv_end + 63) / 64;
   const int* bt = P.block_tables + (size_t)b * P.bt_stride;
-  const size_t head_stride = (size_t)kPage * D * kEl;
+  constexpr int kPageB = kPage * PageRow<D, FMT>::kBytes;
+  const size_t head_stride = (size_t)kPageB;
   const size_t page_stride = (size_t)P.num_layers * 2 * KH * head_stride;
 
   auto issue = [&](int chunk, int stage) {
     uint8_t* dst = stages + stage * S::kStageB;
     const uint32_t dk = smem_u32(dst), dv = smem_u32(dst + S::kRawB);
-    constexpr int kPageChunks = kPage * kChunkPerRow;
+    constexpr int kPageChunks = kPageB / 16;
     for (int i = threadIdx.x; i < 4 * kPageChunks; i += 128) {
       const int pg = i / kPageChunks, w = i % kPageChunks;
       const int page_local = chunk * 4 + pg;
@@ -921,8 +982,8 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
       if (!in_bounds(page, P.num_pages, P.err)) page = 0;   // bounds-check builds
       const uint8_t* kp = P.cache + (size_t)page * page_stride + (((size_t)P.layer * 2 + 0) * KH + kvh) * head_stride;
       const uint8_t* vp = kp + (size_t)KH * head_stride;
-      const int r = pg * kPage + w / kChunkPerRow, ch = w % kChunkPerRow;
-      const uint32_t off = kFp8 ? (uint32_t)(r * D + ch * 16) : swz<ROWB>(r, ch);
+      const uint32_t off = FMT == kFmtBf16 ? swz<ROWB>(pg * kPage + w / kChunkPerRow, w % kChunkPerRow)
+                                           : (uint32_t)(pg * kPageB + w * 16);
       cp_async16(dk + off, kp + (size_t)w * 16, valid);
       cp_async16(dv + off, vp + (size_t)w * 16, valid);
     }
@@ -957,11 +1018,16 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
     __syncthreads();
     uint8_t* kt = stages + stage * S::kStageB;
     uint8_t* vt = kt + S::kRawB;
-    if (kFp8) {
+    if constexpr (FMT != kFmtBf16) {
       uint8_t* ckb = stages + 2 * S::kStageB;
       uint8_t* cvb = ckb + S::kTileB;
-      convert_fp8_tile<D>(kt, ckb, 64, threadIdx.x, 128);
-      convert_fp8_tile<D>(vt, cvb, 64, threadIdx.x, 128);
+      if constexpr (FMT == kFmtFp8) {
+        convert_fp8_tile<D>(kt, ckb, 64, threadIdx.x, 128);
+        convert_fp8_tile<D>(vt, cvb, 64, threadIdx.x, 128);
+      } else {
+        convert_q4_tile<D>(kt, ckb, 64, threadIdx.x, 128);
+        convert_q4_tile<D>(vt, cvb, 64, threadIdx.x, 128);
+      }
       __syncthreads();
       kt = ckb;
       vt = cvb;
@@ -1065,6 +1131,8 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
 }
 
 // ============================================================== host
+static int cache_format(bool fp8, bool q4) { return q4 ? kFmtQ4 : fp8 ? kFmtFp8 : kFmtBf16; }
+
 int decode_attention_choose_splits(int B, int KH, int max_pages) {
   // Chunks per sequence for the persistent kernel (2 resident CTAs per SM): about one
   // (sequence, head, chunk) item per resident CTA (an item's merge is serial work, so
@@ -1087,10 +1155,10 @@ size_t decode_attention_scratch_bytes(int B, int Hq, int D, int splits) {
   return ((size_t)B * Hq * splits * D + (size_t)B * Hq * splits * 2) * sizeof(float);
 }
 
-template <int D, bool F8, bool C = false>
+template <int D, int FMT, bool C = false>
 static void launch_decode(dim3 grid, const DecodeParams& p, cudaStream_t st) {
-  constexpr int smem = DecodeSmem<D, F8>::kTotal;
-  auto kern = paged_decode_kernel<D, F8, C>;
+  constexpr int smem = DecodeSmem<D, FMT>::kTotal;
+  auto kern = paged_decode_kernel<D, FMT, C>;
   static bool set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1144,6 +1212,7 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   VRM_REQUIRE(a.D == 64 || a.D == 128, "decode attention: head_dim must be 64 or 128");
   VRM_REQUIRE(a.KH > 0 && a.Hq % a.KH == 0 && a.Hq / a.KH <= 8, "decode attention: GQA group must be <= 8 heads");
   VRM_REQUIRE(!a.cache_fp8 || a.kv_scale != nullptr, "decode attention: fp8 cache needs kv_scale");
+  VRM_REQUIRE(!(a.cache_fp8 && a.cache_q4), "decode attention: one page format");
   if (a.B <= 0) return;
   const int G = a.Hq / a.KH;
   int splits = a.num_splits > 0 ? a.num_splits : decode_attention_choose_splits(a.B, a.KH, a.max_pages);
@@ -1177,7 +1246,7 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
     VRM_REQUIRE(a.cos_sin == nullptr || a.rot_dim == a.D, "decode attention: fused RoPE needs rot_dim == head_dim");
   }
   const int64_t pool_rows = a.cache_pages * a.num_layers * 2 * a.KH * kPage;
-  const bool tma = !a.cache_fp8 && a.positions == nullptr && a.cache_pages > 0 && pool_rows < (int64_t)INT32_MAX &&
+  const bool tma = !a.cache_fp8 && !a.cache_q4 && a.positions == nullptr && a.cache_pages > 0 && pool_rows < (int64_t)INT32_MAX &&
                    decode_tma_enabled() && (reinterpret_cast<uintptr_t>(a.cache) & 15) == 0;
   const bool cluster = !tma && splits > 1 && splits <= 8 && a.ws == nullptr && decode_cluster_enabled();
   if (splits > 1 && !cluster) {
@@ -1228,29 +1297,29 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   dim3 grid(a.KH, a.B, splits);
   // 2..8 splits of a caller without its own scratch merge inside a cluster (the caller
   // that brings scratch keeps the counter merge over it)
+  const int fmt = cache_format(a.cache_fp8, a.cache_q4);
+  auto go = [&](auto d_tag, auto c_tag) {
+    constexpr int D = decltype(d_tag)::value;
+    constexpr bool C = decltype(c_tag)::value;
+    if (fmt == kFmtFp8) launch_decode<D, kFmtFp8, C>(grid, p, st);
+    else if (fmt == kFmtQ4) launch_decode<D, kFmtQ4, C>(grid, p, st);
+    else launch_decode<D, kFmtBf16, C>(grid, p, st);
+  };
+  using D128 = std::integral_constant<int, 128>;
+  using D64 = std::integral_constant<int, 64>;
   if (cluster) {
-    if (a.D == 128) {
-      if (a.cache_fp8) launch_decode<128, true, true>(grid, p, st);
-      else launch_decode<128, false, true>(grid, p, st);
-    } else {
-      if (a.cache_fp8) launch_decode<64, true, true>(grid, p, st);
-      else launch_decode<64, false, true>(grid, p, st);
-    }
-    return;
-  }
-  if (a.D == 128) {
-    if (a.cache_fp8) launch_decode<128, true>(grid, p, st);
-    else launch_decode<128, false>(grid, p, st);
+    if (a.D == 128) go(D128{}, std::true_type{});
+    else go(D64{}, std::true_type{});
   } else {
-    if (a.cache_fp8) launch_decode<64, true>(grid, p, st);
-    else launch_decode<64, false>(grid, p, st);
+    if (a.D == 128) go(D128{}, std::false_type{});
+    else go(D64{}, std::false_type{});
   }
 }
 
-template <int D, bool F8>
+template <int D, int FMT>
 static void launch_prefill(dim3 grid, const PrefillParams& p, cudaStream_t st) {
-  constexpr int smem = PrefillSmem<D, F8>::kTotal;
-  auto kern = paged_prefill_kernel<D, F8>;
+  constexpr int smem = PrefillSmem<D, FMT>::kTotal;
+  auto kern = paged_prefill_kernel<D, FMT>;
   static bool set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1265,6 +1334,7 @@ void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
   VRM_REQUIRE(a.D == 64 || a.D == 128, "prefill attention: head_dim must be 64 or 128");
   VRM_REQUIRE(a.KH > 0 && a.Hq % a.KH == 0, "prefill attention: heads");
   VRM_REQUIRE(!a.cache_fp8 || a.kv_scale != nullptr, "prefill attention: fp8 cache needs kv_scale");
+  VRM_REQUIRE(!(a.cache_fp8 && a.cache_q4), "prefill attention: one page format");
   VRM_REQUIRE(a.ld_q % 8 == 0, "prefill attention: q row stride must be a multiple of 8");
   if (a.B <= 0 || a.max_q_len <= 0) return;
   PrefillParams p;
@@ -1286,12 +1356,15 @@ void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
   p.num_pages = a.cache_pages;
   p.err = error_word();
   dim3 grid((a.max_q_len + 63) / 64, a.Hq, a.B);
+  const int fmt = cache_format(a.cache_fp8, a.cache_q4);
   if (a.D == 128) {
-    if (a.cache_fp8) launch_prefill<128, true>(grid, p, st);
-    else launch_prefill<128, false>(grid, p, st);
+    if (fmt == kFmtFp8) launch_prefill<128, kFmtFp8>(grid, p, st);
+    else if (fmt == kFmtQ4) launch_prefill<128, kFmtQ4>(grid, p, st);
+    else launch_prefill<128, kFmtBf16>(grid, p, st);
   } else {
-    if (a.cache_fp8) launch_prefill<64, true>(grid, p, st);
-    else launch_prefill<64, false>(grid, p, st);
+    if (fmt == kFmtFp8) launch_prefill<64, kFmtFp8>(grid, p, st);
+    else if (fmt == kFmtQ4) launch_prefill<64, kFmtQ4>(grid, p, st);
+    else launch_prefill<64, kFmtBf16>(grid, p, st);
   }
 }
 

@@ -193,10 +193,12 @@ void layernorm(const void* x, int64_t ldx, void* residual, const void* w, const 
 // qkv: [T, (Hq + 2*KH) * D] (q heads, then k heads, then v heads), rotated in place.
 // K and V rows are stored into the paged cache
 //   cache[page, layer, {0:k,1:v}, kv_head, slot_in_page, d]
-// as bf16, or as fp8 e4m3 of value / scale[layer, k|v, kv_head] (saturating).
+// as bf16, as fp8 e4m3 of value / scale[layer, k|v, kv_head] (saturating), or as a
+// four-bit row (per 32 dims: scale = (max - min) / 15 and min in fp16, codes
+// round((x - min) / scale) in 0..15; D = 64 or 128).
 // cos_sin: [max_pos, rot_dim] fp32 = [cos(0..rot/2) | sin(0..rot/2)]; rotate-half form
 // (GPT-NeoX / Llama / Qwen2) over the first rot_dim dims.  rot_dim == 0: no rotation.
-template <bool kFp8>
+template <int FMT>
 __global__ void rope_kv_write_kernel(RopeKvArgs a) {
   pdl_launch();
   pdl_wait();
@@ -226,9 +228,27 @@ __global__ void rope_kv_write_kernel(RopeKvArgs a) {
       const int kvh = is_v ? h - a.Hq - a.KH : h - a.Hq;
       const int kv = is_v ? 1 : 0;
       const int page = slot / a.page_size, off = slot % a.page_size;
+      if constexpr (FMT == kFmtQ4) {
+        const size_t rb = (size_t)D / 2 + D / 8;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(a.cache) +
+                       ((((size_t)page * a.num_layers + a.layer) * 2 + kv) * a.KH + kvh) * (size_t)a.page_size * rb +
+                       (size_t)off * rb;
+        if (D == 128) {
+          float x[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) x[j] = __bfloat162float(hv[lane * 4 + j]);
+          q4_store_row<128>(dst, x, lane);
+        } else {
+          float x[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) x[j] = __bfloat162float(hv[lane * 2 + j]);
+          q4_store_row<64>(dst, x, lane);
+        }
+        continue;
+      }
       const size_t base =
           ((((size_t)page * a.num_layers + a.layer) * 2 + kv) * a.KH + kvh) * (size_t)a.page_size * D + (size_t)off * D;
-      if (kFp8) {
+      if (FMT == kFmtFp8) {
         const float inv = 1.f / a.kv_scale[(a.layer * 2 + kv) * a.KH + kvh];
         uint8_t* c8 = reinterpret_cast<uint8_t*>(a.cache) + base;
         for (int d = lane; d < D; d += 32) {
@@ -248,9 +268,11 @@ void rope_kv_write(const RopeKvArgs& a_in, cudaStream_t st) {
   RopeKvArgs a = a_in;
   a.err = error_word();
   VRM_REQUIRE(!a.cache_fp8 || a.kv_scale != nullptr, "rope_kv_write: fp8 cache needs kv_scale");
+  VRM_REQUIRE(!a.cache_q4 || a.D == 64 || a.D == 128, "rope_kv_write: four-bit pages need head_dim 64 or 128");
   const int threads = 32 * std::min(16, a.Hq + 2 * a.KH);
-  if (a.cache_fp8) launch_kernel(rope_kv_write_kernel<true>, dim3(a.T), dim3(threads), 0, st, a);
-  else launch_kernel(rope_kv_write_kernel<false>, dim3(a.T), dim3(threads), 0, st, a);
+  if (a.cache_q4) launch_kernel(rope_kv_write_kernel<kFmtQ4>, dim3(a.T), dim3(threads), 0, st, a);
+  else if (a.cache_fp8) launch_kernel(rope_kv_write_kernel<kFmtFp8>, dim3(a.T), dim3(threads), 0, st, a);
+  else launch_kernel(rope_kv_write_kernel<kFmtBf16>, dim3(a.T), dim3(threads), 0, st, a);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 

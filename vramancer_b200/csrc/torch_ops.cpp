@@ -37,15 +37,23 @@ void check_bf16_2d(const Tensor& t, const char* name) {
   TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, ": must be 2-D with unit inner stride");
 }
 
-bool is_fp8_cache(const Tensor& cache) {
-  return cache.scalar_type() == torch::kFloat8_e4m3fn || cache.scalar_type() == torch::kUInt8;
-}
+bool is_fp8_cache(const Tensor& cache) { return cache.scalar_type() == torch::kFloat8_e4m3fn; }
+
+// uint8 pools hold four-bit rows: head_dim/2 code bytes + head_dim/8 bytes of fp16
+// {scale, min} pairs, so the last dimension is head_dim * 5 / 8
+bool is_q4_cache(const Tensor& cache) { return cache.scalar_type() == torch::kUInt8; }
+
+int64_t cache_head_dim(const Tensor& cache) { return is_q4_cache(cache) ? cache.size(5) * 8 / 5 : cache.size(5); }
 
 void check_cache(const Tensor& cache) {
   TORCH_CHECK(cache.is_cuda() && cache.dim() == 6 && cache.is_contiguous(),
-              "kv cache must be a contiguous [pages, layers, 2, kv_heads, page_size, head_dim] CUDA tensor");
+              "kv cache must be a contiguous [pages, layers, 2, kv_heads, page_size, row] CUDA tensor");
   TORCH_CHECK(cache.size(2) == 2, "kv cache dim 2 must be 2 (k, v)");
-  TORCH_CHECK(is_fp8_cache(cache) || cache.scalar_type() == torch::kBFloat16, "kv cache dtype must be bf16 or fp8");
+  TORCH_CHECK(is_fp8_cache(cache) || is_q4_cache(cache) || cache.scalar_type() == torch::kBFloat16,
+              "kv cache dtype must be bf16, fp8 or uint8 (four-bit rows)");
+  if (is_q4_cache(cache))
+    TORCH_CHECK(cache.size(5) == 80 || cache.size(5) == 40,
+                "four-bit kv cache rows must be 80 (head_dim 128) or 40 (head_dim 64) bytes");
 }
 
 // ---------------------------------------------------------------- GEMM
@@ -160,7 +168,7 @@ void rope_kv_write(Tensor& qkv, const OptT& positions, const OptT& cos_sin, Tens
   check_bf16_2d(qkv, "rope qkv");
   TORCH_CHECK(qkv.size(1) == (Hq + 2 * KH) * D, "rope: qkv width must be (Hq + 2 KH) * D");
   check_cache(cache);
-  TORCH_CHECK(cache.size(3) == KH && cache.size(5) == D, "rope: cache kv_heads/head_dim mismatch");
+  TORCH_CHECK(cache.size(3) == KH && cache_head_dim(cache) == D, "rope: cache kv_heads/head_dim mismatch");
   TORCH_CHECK(layer >= 0 && layer < cache.size(1), "rope: layer out of range");
   same_device(qkv, {&cache}, "rope_kv_write");
   same_device_opt(qkv, {&positions, &cos_sin, &slot_mapping, &kv_scale}, "rope_kv_write");
@@ -183,6 +191,7 @@ void rope_kv_write(Tensor& qkv, const OptT& positions, const OptT& cos_sin, Tens
   }
   a.cache = cache.data_ptr();
   a.cache_fp8 = is_fp8_cache(cache);
+  a.cache_q4 = is_q4_cache(cache);
   a.num_pages = cache.size(0);
   a.num_layers = (int)cache.size(1);
   a.layer = (int)layer;
@@ -269,10 +278,11 @@ void attn_decode(const Tensor& q, const Tensor& cache, int64_t layer, const Tens
   a.ld_q = q.stride(0);
   a.cache = cache.data_ptr();
   a.cache_fp8 = is_fp8_cache(cache);
+  a.cache_q4 = is_q4_cache(cache);
   a.num_layers = (int)cache.size(1);
   a.layer = (int)layer;
   a.KH = (int)cache.size(3);
-  a.D = (int)cache.size(5);
+  a.D = (int)cache_head_dim(cache);
   a.Hq = (int)num_q_heads;
   TORCH_CHECK(q.size(1) >= a.Hq * a.D && out.size(1) >= a.Hq * a.D, "decode: q/out width");
   a.block_tables = block_tables.data_ptr<int>();
@@ -328,11 +338,12 @@ void attn_prefill(const Tensor& q, const Tensor& cache, int64_t layer, const Ten
   a.ld_q = q.stride(0);
   a.cache = cache.data_ptr();
   a.cache_fp8 = is_fp8_cache(cache);
+  a.cache_q4 = is_q4_cache(cache);
   a.cache_pages = cache.size(0);
   a.num_layers = (int)cache.size(1);
   a.layer = (int)layer;
   a.KH = (int)cache.size(3);
-  a.D = (int)cache.size(5);
+  a.D = (int)cache_head_dim(cache);
   a.Hq = (int)num_q_heads;
   a.block_tables = block_tables.data_ptr<int>();
   a.bt_stride = (int)block_tables.stride(0);

@@ -323,6 +323,49 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&t);
 }
 
+// ---- page formats: 0 bf16, 1 fp8 e4m3 (per-head scale), 2 four-bit (kFmtQ4).  A stored
+// 4-bit row of D values is D/2 code bytes (element 2i in the low nibble of byte i), then
+// D/32 groups of {scale, min} fp16: value = code * scale + min.
+constexpr int kFmtBf16 = 0, kFmtFp8 = 1, kFmtQ4 = 2;
+template <int D, int FMT>
+struct PageRow {
+  static constexpr int kBytes = FMT == kFmtBf16 ? 2 * D : FMT == kFmtFp8 ? D : D / 2 + D / 8;
+};
+
+// One warp quantises one row of D values (lane l holds dims D/32 * l ..): per 32-dim
+// group scale = (max - min) / 15 and min, both rounded to fp16 first so that the codes
+// are computed against what readers will use; codes = round((x - min) / scale) in 0..15.
+template <int D>
+__device__ __forceinline__ void q4_store_row(uint8_t* dst, const float (&x)[D / 32], int lane) {
+  constexpr int kV = D / 32;
+  constexpr int kLpg = 32 / kV;            // lanes of a 32-dim group
+  float mn = x[0], mx = x[0];
+#pragma unroll
+  for (int j = 1; j < kV; ++j) {
+    mn = fminf(mn, x[j]);
+    mx = fmaxf(mx, x[j]);
+  }
+#pragma unroll
+  for (int o = 1; o < kLpg; o <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  __half hs = __float2half_rn((mx - mn) / 15.f);
+  if (!(__half2float(hs) > 0.f)) hs = __float2half_rn(6.103515625e-05f);   // constant group
+  const __half hm = __float2half_rn(mn);
+  const float s = __half2float(hs), m = __half2float(hm);
+  uint32_t packed = 0;
+#pragma unroll
+  for (int j = 0; j < kV; ++j) {
+    const float cf = fminf(fmaxf(rintf((x[j] - m) / s), 0.f), 15.f);
+    packed |= (uint32_t)cf << (4 * j);
+  }
+  if (kV == 4) *reinterpret_cast<uint16_t*>(dst + lane * 2) = (uint16_t)packed;
+  else dst[lane] = (uint8_t)packed;
+  if (lane % kLpg == 0) *reinterpret_cast<__half2*>(dst + D / 2 + (lane / kLpg) * 4) = __halves2half2(hs, hm);
+}
+
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -304,8 +304,9 @@ struct RopeKvArgs {
   const int* positions = nullptr;   // [T] (null: no rotation)
   const float* cos_sin = nullptr;   // [max_pos, rot_dim] = [cos | sin]
   int rot_dim = 0;
-  void* cache = nullptr;            // [pages, layers, 2, KH, page_size, D]
+  void* cache = nullptr;            // [pages, layers, 2, KH, page_size, row]
   bool cache_fp8 = false;
+  bool cache_q4 = false;            // four-bit rows: D/2 code bytes + D/32 fp16 {scale, min}
   int num_layers = 0, layer = 0, page_size = 16;
   const int* slot_mapping = nullptr;   // [T] page * page_size + offset, < 0 skips
   const float* kv_scale = nullptr;     // [layers, 2, KH] (fp8 only)
@@ -326,6 +327,7 @@ struct DecodeAttnArgs {
   int64_t ld_q = 0;
   const void* cache = nullptr;
   bool cache_fp8 = false;
+  bool cache_q4 = false;   // four-bit rows (see RopeKvArgs)
   int num_layers = 0, layer = 0, KH = 0, D = 0, Hq = 0;
   const int* block_tables = nullptr;   // [B, bt_stride]
   int bt_stride = 0;
@@ -366,6 +368,7 @@ struct PrefillAttnArgs {
   int64_t ld_q = 0;
   const void* cache = nullptr;
   bool cache_fp8 = false;
+  bool cache_q4 = false;   // four-bit rows (see RopeKvArgs)
   int num_layers = 0, layer = 0, KH = 0, D = 0, Hq = 0;
   const int* block_tables = nullptr;
   int bt_stride = 0;

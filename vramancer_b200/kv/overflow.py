@@ -37,7 +37,7 @@ from .pool import KVPool, KVPoolSpec
 log = get_logger("vramancer.kv.overflow")
 
 _DTYPE_NAME = {torch.bfloat16: "bfloat16", torch.float8_e4m3fn: "float8_e4m3fn", torch.float32: "float32",
-               torch.float16: "float16"}
+               torch.float16: "float16", torch.uint8: "uint8"}
 
 
 class ExtensiblePagePool(KVPool):
@@ -70,7 +70,7 @@ class ExtensiblePagePool(KVPool):
         self.base = nat.vmm_reserve(total, gran)
         nat.vmm_map(self.base, 0, self.local_chunks * self.chunk_bytes, dev, self.access, False)
         total_pages = (self.local_chunks + self.max_chunks) * self.pages_per_chunk
-        shape = [total_pages, spec.num_layers, 2, spec.kv_heads, spec.page_size, spec.head_dim]
+        shape = [total_pages, spec.num_layers, 2, spec.kv_heads, spec.page_size, spec.row]
         self.cache = nat.tensor_from_ptr(self.base, shape, _DTYPE_NAME[spec.dtype], dev)
         self.cache[:self.local_chunks * self.pages_per_chunk].zero_()
         self.first_borrow_page = self.local_chunks * self.pages_per_chunk

@@ -1,13 +1,15 @@
 """Physical paged KV pool of one rank / pipeline stage.
 
-Layout ``[num_pages, num_layers, 2, kv_heads, page_size, head_dim]``: a page holds
+Layout ``[num_pages, num_layers, 2, kv_heads, page_size, head_dim]`` (row bytes for uint8): a page holds
 `page_size` tokens of every layer, so one page is one contiguous block (3 MiB for the
 Qwen2.5-14B shape: 16 tok x 48 layers x 8 heads x 128 dim x bf16 x K,V).  That makes a
 page the unit of migration between GPUs and of spill to host/NVMe, and the
 (page, layer, k|v, head) chunk of page_size x head_dim elements is contiguous, which
 is what the attention kernels stream.
 
-fp8 pools store e4m3 values with one fp32 scale per (layer, k|v, kv_head).
+fp8 pools store e4m3 values with one fp32 scale per (layer, k|v, kv_head).  uint8
+pools store four-bit rows (`kv.q4`): the last dimension is the row's byte count,
+head_dim * 5 / 8, and a page takes 5/16 of the bf16 page's bytes.
 
 Reference parity: the pool tensor of core/paged_attention.py:277-351 (same page
 shape and bytes/page, core/paged_attention.py:107-111).
@@ -30,6 +32,8 @@ def kv_dtype_from_str(s: str) -> torch.dtype:
         return torch.float8_e4m3fn
     if s in ("fp32", "float32"):
         return torch.float32
+    if s in ("q4", "int4", "4bit", "uint8"):
+        return torch.uint8
     raise ValueError(f"unsupported kv cache dtype {s!r}")
 
 
@@ -43,9 +47,17 @@ class KVPoolSpec:
     dtype: torch.dtype = torch.bfloat16
 
     @property
+    def row(self) -> int:
+        """Last dimension of the pool tensor: head_dim, or the four-bit row's bytes."""
+        if self.dtype == torch.uint8:
+            from .q4 import row_bytes
+            return row_bytes(self.head_dim)
+        return self.head_dim
+
+    @property
     def bytes_per_page(self) -> int:
         el = torch.empty(0, dtype=self.dtype).element_size()
-        return 2 * self.num_layers * self.kv_heads * self.page_size * self.head_dim * el
+        return 2 * self.num_layers * self.kv_heads * self.page_size * self.row * el
 
     @staticmethod
     def pages_for_budget(budget_bytes: int, num_layers: int, kv_heads: int, head_dim: int,
@@ -60,7 +72,7 @@ class KVPool:
     def __init__(self, spec: KVPoolSpec, device="cpu", kv_scale: Optional[torch.Tensor] = None):
         self.spec = spec
         self.device = torch.device(device)
-        shape = (spec.num_pages, spec.num_layers, 2, spec.kv_heads, spec.page_size, spec.head_dim)
+        shape = (spec.num_pages, spec.num_layers, 2, spec.kv_heads, spec.page_size, spec.row)
         # zero-initialised: stale slots past a sequence's length are finite
         self.cache = torch.zeros(shape, dtype=spec.dtype, device=self.device)
         self.is_fp8 = spec.dtype == torch.float8_e4m3fn

@@ -156,7 +156,8 @@ def rope_kv_write(qkv: torch.Tensor, positions: Optional[torch.Tensor], cos_sin:
                   cache: torch.Tensor, slot_mapping: Optional[torch.Tensor], kv_scale: Optional[torch.Tensor],
                   layer: int, num_q_heads: int, num_kv_heads: int, head_dim: int) -> None:
     """Rotates q/k of qkv [T, (Hq+2KH)*D] in place and stores k/v rows into the paged cache
-    [pages, layers, 2, KH, page_size, D] at slot_mapping (bf16, or fp8 e4m3 / kv_scale)."""
+    [pages, layers, 2, KH, page_size, row] at slot_mapping (bf16, fp8 e4m3 / kv_scale, or
+    four-bit rows in a uint8 cache: `kv.q4`)."""
     if qkv.is_cuda:
         native().rope_kv_write(qkv, positions, cos_sin, cache, slot_mapping, kv_scale, layer,
                                num_q_heads, num_kv_heads, head_dim)
@@ -185,13 +186,15 @@ def rope_kv_write(qkv: torch.Tensor, positions: Optional[torch.Tensor], cos_sin:
     page, off = slots[idx] // ps, slots[idx] % ps
     k = v[idx, Hq:Hq + KH, :]
     vv = v[idx, Hq + KH:, :]
-    if cache.dtype in (torch.float8_e4m3fn, torch.uint8):
+    if cache.dtype == torch.uint8:
+        from ..kv import q4
+        cache[page, layer, 0, :, off, :] = q4.quantize(k.float())
+        cache[page, layer, 1, :, off, :] = q4.quantize(vv.float())
+    elif cache.dtype == torch.float8_e4m3fn:
         sk = kv_scale[layer, 0].view(1, KH, 1)
         sv = kv_scale[layer, 1].view(1, KH, 1)
         kq = (k.float() / sk).clamp(-448, 448).to(torch.float8_e4m3fn)
         vq = (vv.float() / sv).clamp(-448, 448).to(torch.float8_e4m3fn)
-        if cache.dtype == torch.uint8:
-            kq, vq = kq.view(torch.uint8), vq.view(torch.uint8)
         cache[page, layer, 0, :, off, :] = kq
         cache[page, layer, 1, :, off, :] = vq
     else:
@@ -200,6 +203,11 @@ def rope_kv_write(qkv: torch.Tensor, positions: Optional[torch.Tensor], cos_sin:
 
 
 # --------------------------------------------------------------------------- attention
+def cache_head_dim(cache: torch.Tensor) -> int:
+    """Head dim of a KV pool [pages, layers, 2, KH, page_size, row] (uint8 = four-bit rows)."""
+    return cache.shape[5] * 8 // 5 if cache.dtype == torch.uint8 else cache.shape[5]
+
+
 def _gather_kv(cache: torch.Tensor, layer: int, pages: torch.Tensor, n: int,
                kv_scale: Optional[torch.Tensor]):
     """[n, KH, D] float K and V of one sequence from its page list."""
@@ -209,9 +217,10 @@ def _gather_kv(cache: torch.Tensor, layer: int, pages: torch.Tensor, n: int,
     k = k.permute(0, 2, 1, 3).reshape(-1, KH, D)[:n]
     v = v.permute(0, 2, 1, 3).reshape(-1, KH, D)[:n]
     if cache.dtype == torch.uint8:
-        k, v = k.view(torch.float8_e4m3fn), v.view(torch.float8_e4m3fn)
+        from ..kv import q4
+        return q4.dequantize(k), q4.dequantize(v)
     k, v = k.float(), v.float()
-    if kv_scale is not None and cache.dtype in (torch.float8_e4m3fn, torch.uint8):
+    if kv_scale is not None and cache.dtype == torch.float8_e4m3fn:
         k = k * kv_scale[layer, 0].view(1, KH, 1)
         v = v * kv_scale[layer, 1].view(1, KH, 1)
     return k, v
@@ -229,7 +238,7 @@ def paged_attention_decode(q: torch.Tensor, cache: torch.Tensor, layer: int, blo
     does this step's RoPE (cos_sin, rotate-half over all head dims; None = no rotation)
     and writes the token's k / v into the cache: the work of `rope_kv_write`, fused."""
     B = q.shape[0]
-    D = cache.shape[5]
+    D = cache_head_dim(cache)
     if out is None:
         out = torch.empty(B, num_q_heads * D, dtype=q.dtype, device=q.device)
     if q.is_cuda:
@@ -263,7 +272,7 @@ def paged_attention_prefill(q: torch.Tensor, cache: torch.Tensor, layer: int, bl
     """Causal attention of new tokens (rows of q, grouped by cu_q) over their sequence's
     cached prefix plus themselves; keys/values are read from the paged cache."""
     T = q.shape[0]
-    D = cache.shape[5]
+    D = cache_head_dim(cache)
     if out is None:
         out = torch.empty(T, num_q_heads * D, dtype=q.dtype, device=q.device)
     if q.is_cuda:

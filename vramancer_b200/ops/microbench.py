@@ -142,16 +142,24 @@ def bench_nvfp4(m, n, k, iters=50, copies=None):
             "bf16_equiv_tb_s": round(n * k * 2 / us / 1e6, 3), "peaks": src}
 
 
+def _kv_cache(shape, fp8, q4):
+    """Random KV pool of one page format (bf16, fp8 e4m3, or four-bit rows in uint8)."""
+    x = torch.randn(*shape, device="cuda")
+    if q4:
+        from ..kv import q4 as q4fmt
+        return q4fmt.quantize(x)
+    return x.to(torch.float8_e4m3fn if fp8 else torch.bfloat16)
+
+
 def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4, fp8=False, iters=50,
-                      splits=0, fused=False):
+                      splits=0, fused=False, q4=False):
     """splits > 0 forces the split count; fused runs the model's path (RoPE on q and the
-    step's K/V written into its page inside the kernel)."""
+    step's K/V written into its page inside the kernel); q4 reads four-bit pages."""
     hbm, _, src = peaks()
     ps = 16
     pages = (ctx + ps - 1) // ps
     P = batch * pages
-    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
-    cache = torch.randn(P, layers, 2, kv_heads, ps, head_dim, device="cuda").to(dt)
+    cache = _kv_cache((P, layers, 2, kv_heads, ps, head_dim), fp8, q4)
     bt = torch.arange(P, dtype=torch.int32, device="cuda").view(batch, pages)
     cl = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
     q = torch.randn(batch, (q_heads + (2 * kv_heads if fused else 0)) * head_dim, device="cuda",
@@ -171,8 +179,8 @@ def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4
         state[0] += 1
 
     us = time_it(fn, iters)
-    byts = batch * ctx * kv_heads * head_dim * 2 * cache.element_size()
-    return {"kernel": "decode_attn", "batch": batch, "ctx": ctx, "fp8": fp8, "kv_heads": kv_heads,
+    byts = batch * ctx * kv_heads * 2 * cache.shape[5] * cache.element_size()
+    return {"kernel": "decode_attn", "batch": batch, "ctx": ctx, "fp8": fp8, "q4": q4, "kv_heads": kv_heads,
             "q_heads": q_heads, "splits": splits or "auto", "fused": fused, "us": round(us, 2),
             "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
 
@@ -245,14 +253,13 @@ def bench_rope_kv(tokens, q_heads=40, kv_heads=8, head_dim=128, fp8=False, iters
             "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
 
 
-def bench_prefill_attn(batch, seq, q_heads=40, kv_heads=8, head_dim=128, fp8=False, iters=10):
+def bench_prefill_attn(batch, seq, q_heads=40, kv_heads=8, head_dim=128, fp8=False, iters=10, q4=False):
     """Causal paged prefill attention of `batch` sequences of `seq` new tokens (no prefix)."""
     _, tflops, src = peaks()
     ps, layers = 16, 1
     pages = (seq + ps - 1) // ps
     P = batch * pages
-    dt = torch.float8_e4m3fn if fp8 else torch.bfloat16
-    cache = torch.randn(P, layers, 2, kv_heads, ps, head_dim, device="cuda").to(dt)
+    cache = _kv_cache((P, layers, 2, kv_heads, ps, head_dim), fp8, q4)
     bt = torch.arange(P, dtype=torch.int32, device="cuda").view(batch, pages)
     cl = torch.full((batch,), seq, dtype=torch.int32, device="cuda")
     cu = torch.arange(0, (batch + 1) * seq, seq, dtype=torch.int32, device="cuda")
@@ -265,7 +272,7 @@ def bench_prefill_attn(batch, seq, q_heads=40, kv_heads=8, head_dim=128, fp8=Fal
 
     us = time_it(fn, iters)
     flop = batch * q_heads * 4.0 * head_dim * seq * (seq + 1) / 2   # causal QK^T + PV
-    return {"kernel": "prefill_attn", "batch": batch, "seq": seq, "fp8": fp8, "us": round(us, 2),
+    return {"kernel": "prefill_attn", "batch": batch, "seq": seq, "fp8": fp8, "q4": q4, "us": round(us, 2),
             "tflops": round(flop / us / 1e6, 1), "frac_of_measured_bf16": round(flop / us / 1e6 / tflops, 3),
             "peaks": src}
 
@@ -402,6 +409,7 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--ctx", type=int, default=768)
     ap.add_argument("--fp8", action="store_true")
+    ap.add_argument("--q4", action="store_true", help="decode-attn / prefill-attn: four-bit KV pages")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--residual", action="store_true")
     ap.add_argument("--fold", action="store_true", help="gemm: also the folded-norm producer / consumer modes")
@@ -433,7 +441,7 @@ def main(argv=None):
             print(json.dumps(bench_nvfp4_prefill(a.m if a.m != 1 else 4096, n, k, a.iters)))
     elif a.what == "decode-attn":
         print(json.dumps(bench_decode_attn(a.batch, a.ctx, kv_heads=a.kv_heads, q_heads=a.q_heads, fp8=a.fp8,
-                                           iters=a.iters, splits=a.splits, fused=a.fused)))
+                                           iters=a.iters, splits=a.splits, fused=a.fused, q4=a.q4)))
     elif a.what == "fp8":
         for m in ((a.m,) if a.m != 1 else (1, 32, 4096)):
             for name, n, k in QWEN14B_DECODE[:4]:
@@ -445,7 +453,7 @@ def main(argv=None):
     elif a.what == "rope-kv":
         print(json.dumps(bench_rope_kv(a.tokens or a.batch, fp8=a.fp8, iters=a.iters)))
     elif a.what == "prefill-attn":
-        print(json.dumps(bench_prefill_attn(a.batch, a.seq, fp8=a.fp8, iters=a.iters)))
+        print(json.dumps(bench_prefill_attn(a.batch, a.seq, fp8=a.fp8, iters=a.iters, q4=a.q4)))
     elif a.what == "sample":
         print(json.dumps(bench_sample(a.batch, greedy=a.greedy, iters=a.iters)))
     elif a.what == "turboquant":
