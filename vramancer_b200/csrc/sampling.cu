@@ -177,7 +177,10 @@ __device__ __forceinline__ float bf16_bits_to_float(uint16_t bits) { return __ui
 // match.any and only their leader updates it (no atomics: one writer per bin per
 // warp instruction), in mass mode the lanes add with shared atomics into their own
 // warp's bins.  The 32 warp histograms are summed before the scan.
-__device__ void radix_digit(const __nv_bfloat16* __restrict__ x, int V, int shift, uint32_t pref_mask, uint32_t pref,
+//
+// `scan(f)` calls f(i, bits, valid) for every element (GlobalRow, CandRow).
+template <class Scan>
+__device__ void radix_digit(const Scan& scan, int shift, uint32_t pref_mask, uint32_t pref,
                             uint32_t floor_key, bool mass, float M, float invT, float target,
                             float (*whist)[256], float* hist, uint32_t* out_digit, float* out_above) {
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -185,7 +188,7 @@ __device__ void radix_digit(const __nv_bfloat16* __restrict__ x, int V, int shif
   for (int i = threadIdx.x; i < nw * 256; i += blockDim.x) whist[i >> 8][i & 255] = 0.f;
   __syncthreads();
   float* my = whist[w];
-  scan_row(x, V, [&](int, uint16_t bits, bool ok) {
+  scan([&](int, uint16_t bits, bool ok) {
     uint32_t bin = 256u;                                // 256 = not counted
     float wt = 0.f;
     if (ok) {
@@ -254,67 +257,276 @@ __device__ void radix_digit(const __nv_bfloat16* __restrict__ x, int V, int shif
   __syncthreads();
 }
 
+// A bf16 logits row in global memory.
+struct GlobalRow {
+  const __nv_bfloat16* x;
+  int V;
+  template <class F>
+  __device__ __forceinline__ void operator()(F&& f) const { scan_row(x, V, f); }
+};
+
+// n candidate logits held in shared memory as bf16 bit patterns; kCandEmpty marks an
+// unused slot.  Trip counts are warp-uniform (blockDim is a multiple of 32).
+constexpr uint16_t kCandEmpty = 0xFFFFu;   // a NaN pattern no candidate carries
+struct CandRow {
+  const uint16_t* bits;
+  int n;
+  template <class F>
+  __device__ __forceinline__ void operator()(F&& f) const {
+    for (int b0 = 0; b0 < n; b0 += blockDim.x) {
+      const int i = b0 + threadIdx.x;
+      const uint16_t v = i < n ? bits[i] : kCandEmpty;
+      f(i, v, v != kCandEmpty);
+    }
+  }
+};
+
+struct SampleSmem {
+  ArgBest sh[32];
+  float shf[32];
+  float hist[256];
+  uint32_t digit;
+  float above;
+};
+
+// x / T + G(u), G = -log(-log u): no contraction, so every kernel that scores an
+// element gets the same bits
+__device__ __forceinline__ float gumbel_score(float x, float invT, float u) {
+  return __fadd_rn(__fmul_rn(x, invT), -logf(-logf(u)));
+}
+
+// Temperature / top-k / top-p selection over the elements `scan` visits (V of them
+// valid, maximum M), Gumbel-max draw keyed by gidx(i) (the element's vocabulary index).
+// Every thread of the block must call it; returns the chosen element's position i.
+template <class Scan, class GIdx>
+__device__ int sample_select(const Scan& scan, int V, float M, float T, int k, float p, uint64_t seed, int row,
+                             uint64_t step, const GIdx& gidx, SampleSmem& S, float (*whist)[256]) {
+  const float invT = 1.f / T;
+  // ---- top-k threshold: count radix select over the two bytes of the 16-bit key
+  uint32_t floor_key = 0u;
+  if (k > 0 && k < V) {
+    radix_digit(scan, 8, 0u, 0u, 0u, false, M, invT, (float)k, whist, S.hist, &S.digit, &S.above);
+    const uint32_t hi = S.digit;
+    const float need = (float)k - S.above;
+    radix_digit(scan, 0, 0xFF00u, hi << 8, 0u, false, M, invT, need, whist, S.hist, &S.digit, &S.above);
+    floor_key = (hi << 8) | S.digit;
+  }
+  // ---- top-p threshold: mass radix select inside the top-k set
+  if (p < 1.f) {
+    float z = 0.f;
+    scan([&](int, uint16_t bits, bool ok) {
+      if (ok && bf16_key(bits) >= floor_key) z += __expf((bf16_bits_to_float(bits) - M) * invT);
+    });
+    z = block_sum(z, S.shf);
+    const float target = fmaxf(p, 0.f) * z;
+    radix_digit(scan, 8, 0u, 0u, floor_key, true, M, invT, target, whist, S.hist, &S.digit, &S.above);
+    const uint32_t hi = S.digit;
+    const float need = target - S.above;
+    radix_digit(scan, 0, 0xFF00u, hi << 8, floor_key, true, M, invT, need, whist, S.hist, &S.digit, &S.above);
+    const uint32_t pk = (hi << 8) | S.digit;
+    floor_key = floor_key > pk ? floor_key : pk;
+  }
+  // ---- Gumbel-max draw over the kept set.  The score x / T + G does not subtract the
+  // row maximum, so a rank that holds part of the vocabulary scores its elements
+  // exactly as a rank holding all of it.
+  ArgBest gb{-INFINITY, 0x7fffffff};
+  scan([&](int i, uint16_t bits, bool ok) {
+    if (!ok || bf16_key(bits) < floor_key) return;
+    const float u = hash_uniform(seed, (uint64_t)row, step, (uint64_t)gidx(i));
+    gb = better(gb, ArgBest{gumbel_score(bf16_bits_to_float(bits), invT, u), i});
+  });
+  gb = block_argmax(gb, S.sh);
+  return gb.i;
+}
+
+struct IdentityIdx {
+  __device__ __forceinline__ int operator()(int i) const { return i; }
+};
+
 __global__ void __launch_bounds__(kSampThreads)
     sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temperature,
                   const int* __restrict__ top_k, const float* __restrict__ top_p, uint64_t seed,
                   const int* __restrict__ steps, int* __restrict__ out) {
   pdl_launch();
   pdl_wait_for(logits, temperature, top_k, top_p, steps);
-  __shared__ ArgBest sh[32];
-  __shared__ float shf[32];
-  __shared__ float hist[256];
+  __shared__ SampleSmem S;
   __shared__ float whist[kSampThreads / 32][256];
-  __shared__ uint32_t s_digit;
-  __shared__ float s_above;
   const int row = blockIdx.x;
   const __nv_bfloat16* x = logits + (size_t)row * ld;
   const float T = temperature ? temperature[row] : 0.f;
 
-  const ArgBest best = row_argmax(x, V, sh);
+  const ArgBest best = row_argmax(x, V, S.sh);
   if (!(T > 0.f)) {
     if (threadIdx.x == 0) out[row] = best.i;
     return;
   }
-  const float M = best.v;
-  const float invT = 1.f / T;
   const int k = top_k ? top_k[row] : 0;
   const float p = top_p ? top_p[row] : 1.f;
-
-  // ---- top-k threshold: count radix select over the two bytes of the 16-bit key
-  uint32_t floor_key = 0u;
-  if (k > 0 && k < V) {
-    radix_digit(x, V, 8, 0u, 0u, 0u, false, M, invT, (float)k, whist, hist, &s_digit, &s_above);
-    const uint32_t hi = s_digit;
-    const float need = (float)k - s_above;
-    radix_digit(x, V, 0, 0xFF00u, hi << 8, 0u, false, M, invT, need, whist, hist, &s_digit, &s_above);
-    floor_key = (hi << 8) | s_digit;
-  }
-  // ---- top-p threshold: mass radix select inside the top-k set
-  if (p < 1.f) {
-    float z = 0.f;
-    scan_row(x, V, [&](int, uint16_t bits, bool ok) {
-      if (ok && bf16_key(bits) >= floor_key) z += __expf((bf16_bits_to_float(bits) - M) * invT);
-    });
-    z = block_sum(z, shf);
-    const float target = fmaxf(p, 0.f) * z;
-    radix_digit(x, V, 8, 0u, 0u, floor_key, true, M, invT, target, whist, hist, &s_digit, &s_above);
-    const uint32_t hi = s_digit;
-    const float need = target - s_above;
-    radix_digit(x, V, 0, 0xFF00u, hi << 8, floor_key, true, M, invT, need, whist, hist, &s_digit, &s_above);
-    const uint32_t pk = (hi << 8) | s_digit;
-    floor_key = floor_key > pk ? floor_key : pk;
-  }
-  // ---- Gumbel-max draw over the kept set
   const uint64_t step = steps ? (uint64_t)steps[row] : 0ull;
-  ArgBest gb{-INFINITY, 0x7fffffff};
-  scan_row(x, V, [&](int i, uint16_t bits, bool ok) {
-    if (!ok || bf16_key(bits) < floor_key) return;
-    const float u = hash_uniform(seed, (uint64_t)row, step, (uint64_t)i);
-    const float gum = -logf(-logf(u));
-    gb = better(gb, ArgBest{(bf16_bits_to_float(bits) - M) * invT + gum, i});
-  });
-  gb = block_argmax(gb, sh);
-  if (threadIdx.x == 0) out[row] = gb.i < V ? gb.i : best.i;
+  const int i = sample_select(GlobalRow{x, V}, V, best.v, T, k, p, seed, row, step, IdentityIdx{}, S, whist);
+  if (threadIdx.x == 0) out[row] = i < V ? i : best.i;
+}
+
+// ---------------------------------------------------------------- vocabulary-parallel
+// Under tensor parallelism each rank holds logits of vocabulary columns
+// [v_off, v_off + Vs).  Instead of gathering every rank's logits, each rank reduces its
+// shard to at most KC candidates per row (vp_local_kernel), the ranks all-gather the
+// candidates (KC x 8 bytes per row and rank), and every rank picks the same token from
+// the gathered candidates (vp_combine_kernel):
+//   T <= 0            : the shard's argmax (value, index); the pick is the largest value,
+//                       lowest index on ties -- the full-row argmax.
+//   T > 0, no top-k,  : the shard's Gumbel-max winner x / T + G(seed, row, step, index);
+//   top-p >= 1          the pick is the largest score -- the full-row draw.
+//   T > 0, top-k <= KMAX: every element of the shard whose key is >= the shard's k-th
+//                       largest key (the global k-th largest can only be larger, so
+//                       every element of the global top-k set is a candidate); the
+//                       combine runs top-k, top-p and the Gumbel draw over the
+//                       candidates, keyed by vocabulary index.  Exact unless more than
+//                       KC - k elements of one shard tie at its k-th value (the extra
+//                       ties are dropped).
+// Rows with top-p < 1 and no top-k (or top-k > KMAX) need the whole distribution; the
+// caller gathers full logits for those steps.  Candidates: value (fp32: a bf16 logit,
+// or the Gumbel score) and vocabulary index; empty slots carry index -1.
+constexpr int kVpThreads = 256;
+
+__device__ __forceinline__ int vp_mode(float T, int k, float p, int V_total, int kmax) {
+  if (!(T > 0.f)) return 0;                       // greedy
+  if ((k <= 0 || k >= V_total) && p >= 1.f) return 1;   // plain temperature: Gumbel-max
+  if (k > 0 && k <= kmax) return 2;               // top-k (+ top-p): candidates
+  return 3;                                       // needs the full distribution
+}
+
+__global__ void __launch_bounds__(kSampThreads)
+    vp_local_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld, int Vs, int v_off, int V_total,
+                    const float* __restrict__ temperature, const int* __restrict__ top_k,
+                    const float* __restrict__ top_p, uint64_t seed, const int* __restrict__ steps, int KC, int kmax,
+                    float* __restrict__ cand_val, int* __restrict__ cand_idx) {
+  pdl_launch();
+  pdl_wait_for(logits, temperature, top_k, top_p, steps);
+  __shared__ SampleSmem S;
+  __shared__ float whist[kSampThreads / 32][256];
+  __shared__ int s_n;
+  const int row = blockIdx.x;
+  const __nv_bfloat16* x = logits + (size_t)row * ld;
+  const int V = max(0, min(Vs, V_total - v_off));   // the last shard may hold padding columns
+  float* cv = cand_val + (size_t)row * KC;
+  int* ci = cand_idx + (size_t)row * KC;
+  for (int j = threadIdx.x; j < KC; j += blockDim.x) {
+    cv[j] = -INFINITY;
+    ci[j] = -1;
+  }
+  const float T = temperature[row];
+  const int k = top_k[row];
+  const float p = top_p[row];
+  const int mode = vp_mode(T, k, p, V_total, kmax);
+  const ArgBest best = mode != 1 ? row_argmax(x, V, S.sh) : ArgBest{0.f, 0};
+  __syncthreads();   // the candidate slots are initialised before any thread fills them
+  if (mode == 0) {
+    if (threadIdx.x == 0 && V > 0) {
+      cv[0] = best.v;
+      ci[0] = v_off + best.i;
+    }
+    return;
+  }
+  const float invT = 1.f / T;
+  if (mode == 1) {
+    const uint64_t step = (uint64_t)steps[row];
+    ArgBest gb{-INFINITY, 0x7fffffff};
+    scan_row(x, V, [&](int i, uint16_t bits, bool ok) {
+      if (!ok) return;
+      const float u = hash_uniform(seed, (uint64_t)row, step, (uint64_t)(v_off + i));
+      gb = better(gb, ArgBest{gumbel_score(bf16_bits_to_float(bits), invT, u), i});
+    });
+    gb = block_argmax(gb, S.sh);
+    if (threadIdx.x == 0 && V > 0) {
+      cv[0] = gb.v;
+      ci[0] = v_off + gb.i;
+    }
+    return;
+  }
+  // modes 2 / 3: the shard's elements with key >= its k-th largest key (k = KC for
+  // rows that need the full distribution: the best KC of the shard)
+  const int kk = mode == 2 ? k : KC;
+  uint32_t floor_key = 0u;
+  const GlobalRow scan{x, V};
+  if (kk < V) {
+    radix_digit(scan, 8, 0u, 0u, 0u, false, best.v, invT, (float)kk, whist, S.hist, &S.digit, &S.above);
+    const uint32_t hi = S.digit;
+    const float need = (float)kk - S.above;
+    radix_digit(scan, 0, 0xFF00u, hi << 8, 0u, false, best.v, invT, need, whist, S.hist, &S.digit, &S.above);
+    floor_key = (hi << 8) | S.digit;
+  }
+  if (threadIdx.x == 0) s_n = 0;
+  __syncthreads();
+  // elements strictly above the threshold first (at most kk - 1 of them), then ties
+  for (int pass = 0; pass < 2; ++pass) {
+    scan([&](int i, uint16_t bits, bool ok) {
+      if (!ok) return;
+      const uint32_t key = bf16_key(bits);
+      if (pass == 0 ? key <= floor_key : key != floor_key) return;
+      const int slot = atomicAdd(&s_n, 1);
+      if (slot < KC) {
+        cv[slot] = bf16_bits_to_float(bits);
+        ci[slot] = v_off + i;
+      }
+    });
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kVpThreads)
+    vp_combine_kernel(const float* __restrict__ cand_val, const int* __restrict__ cand_idx, int64_t rank_stride, int tp,
+                      int B, int KC,
+                      int V_total, const float* __restrict__ temperature, const int* __restrict__ top_k,
+                      const float* __restrict__ top_p, uint64_t seed, const int* __restrict__ steps, int kmax,
+                      int* __restrict__ out) {
+  pdl_launch();
+  pdl_wait_for(cand_val, cand_idx, temperature, top_k, top_p, steps);
+  extern __shared__ __align__(16) uint8_t vp_smem[];
+  __shared__ SampleSmem S;
+  __shared__ float whist[kVpThreads / 32][256];
+  const int row = blockIdx.x;
+  const float T = temperature[row];
+  const int k = top_k[row];
+  const float p = top_p[row];
+  const int mode = vp_mode(T, k, p, V_total, kmax);
+  if (mode <= 1) {
+    // every rank's slot 0: the largest value (greedy) or score (Gumbel), lowest index on ties
+    ArgBest b{-INFINITY, 0x7fffffff};
+    for (int r = threadIdx.x; r < tp; r += blockDim.x) {
+      const size_t o = (size_t)r * rank_stride + (size_t)row * KC;
+      if (cand_idx[o] >= 0) b = better(b, ArgBest{cand_val[o], cand_idx[o]});
+    }
+    b = block_argmax(b, S.sh);
+    if (threadIdx.x == 0) out[row] = b.i != 0x7fffffff ? b.i : 0;
+    return;
+  }
+  const int n = tp * KC;
+  uint16_t* bits = reinterpret_cast<uint16_t*>(vp_smem);              // [n]
+  int* gidx = reinterpret_cast<int*>(vp_smem + ((n * 2 + 15) & ~15));   // [n]
+  ArgBest best{-INFINITY, 0x7fffffff};
+  int valid = 0;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const int r = j / KC, c = j % KC;
+    const size_t o = (size_t)r * rank_stride + (size_t)row * KC + c;
+    const int gi = cand_idx[o];
+    const float v = cand_val[o];
+    bits[j] = gi >= 0 ? __bfloat16_as_ushort(__float2bfloat16(v)) : kCandEmpty;
+    gidx[j] = gi;
+    if (gi >= 0) {
+      ++valid;
+      best = better(best, ArgBest{v, gi});
+    }
+  }
+  best = block_argmax(best, S.sh);
+  const int V = (int)block_sum((float)valid, S.shf);
+  const uint64_t step = (uint64_t)steps[row];
+  struct MapIdx {
+    const int* g;
+    __device__ __forceinline__ int operator()(int i) const { return g[i]; }
+  };
+  const int i = sample_select(CandRow{bits, n}, V, best.v, T, k, p, seed, row, step, MapIdx{gidx}, S, whist);
+  if (threadIdx.x == 0) out[row] = (i >= 0 && i < n && gidx[i] >= 0) ? gidx[i] : best.i;
 }
 
 void argmax_rows(const void* logits, int64_t ld, int B, int V, int* out, cudaStream_t st) {
@@ -329,6 +541,40 @@ void sample_rows(const void* logits, int64_t ld, int B, int V, const float* temp
   if (B <= 0) return;
   launch_kernel(sample_kernel, dim3(B), dim3(kSampThreads), 0, st, reinterpret_cast<const __nv_bfloat16*>(logits), ld,
                 V, temperature, top_k, top_p, seed, steps, out);
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+size_t vp_combine_smem(int tp, int KC) {
+  const int n = tp * KC;
+  return (size_t)((n * 2 + 15) & ~15) + (size_t)n * 4;
+}
+
+void sample_vp_local(const void* logits, int64_t ld, int B, int Vs, int v_off, int V_total, const float* temperature,
+                     const int* top_k, const float* top_p, uint64_t seed, const int* steps, int KC, int kmax,
+                     float* cand_val, int* cand_idx, cudaStream_t st) {
+  if (B <= 0) return;
+  VRM_REQUIRE(KC >= 1 && kmax >= 1 && kmax <= KC, "vocab-parallel sampling: 1 <= kmax <= KC");
+  launch_kernel(vp_local_kernel, dim3(B), dim3(kSampThreads), 0, st, reinterpret_cast<const __nv_bfloat16*>(logits),
+                ld, Vs, v_off, V_total, temperature, top_k, top_p, seed, steps, KC, kmax, cand_val, cand_idx);
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
+void sample_vp_combine(const float* cand_val, const int* cand_idx, int64_t rank_stride, int tp, int B, int KC,
+                       int V_total, const float* temperature, const int* top_k, const float* top_p, uint64_t seed,
+                       const int* steps, int kmax, int* out, cudaStream_t st) {
+  if (B <= 0) return;
+  const size_t smem = vp_combine_smem(tp, KC);
+  VRM_REQUIRE(smem <= 160 * 1024, "vocab-parallel sampling: tp * KC candidates exceed shared memory");
+  static bool set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!set[dev & 63]) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(vp_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+    set[dev & 63] = true;
+  }
+  launch_kernel(vp_combine_kernel, dim3(B), dim3(kVpThreads), smem, st, cand_val, cand_idx, rank_stride, tp, B, KC,
+                V_total,
+                temperature, top_k, top_p, seed, steps, kmax, out);
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 

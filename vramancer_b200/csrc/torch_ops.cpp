@@ -388,6 +388,46 @@ void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k
                    out.data_ptr<int>(), cur_stream());
 }
 
+// cand: int32 [2, B, KC]: [0] the candidates' fp32 values (bit patterns), [1] their
+// vocabulary indices (-1 = empty), one buffer so that a single all-gather moves both
+void sample_vp_local(const Tensor& logits, int64_t v_off, int64_t vocab, const Tensor& temperature,
+                     const Tensor& top_k, const Tensor& top_p, int64_t seed, const Tensor& steps, int64_t kmax,
+                     Tensor& cand) {
+  check_bf16_2d(logits, "sample_vp logits");
+  const int64_t B = logits.size(0);
+  TORCH_CHECK(temperature.scalar_type() == torch::kFloat32 && temperature.numel() >= B, "sample_vp: fp32 temperature");
+  TORCH_CHECK(top_k.scalar_type() == torch::kInt32 && top_k.numel() >= B, "sample_vp: int32 top_k");
+  TORCH_CHECK(top_p.scalar_type() == torch::kFloat32 && top_p.numel() >= B, "sample_vp: fp32 top_p");
+  TORCH_CHECK(steps.scalar_type() == torch::kInt32 && steps.numel() >= B, "sample_vp: int32 steps");
+  TORCH_CHECK(cand.scalar_type() == torch::kInt32 && cand.is_contiguous() && cand.dim() == 3 && cand.size(0) == 2 &&
+                  cand.size(1) == B, "sample_vp: int32 cand [2, B, KC]");
+  same_device(logits, {&temperature, &top_k, &top_p, &steps, &cand}, "sample_vp_local");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  int* base = cand.data_ptr<int>();
+  const int64_t KC = cand.size(2);
+  vrm::sample_vp_local(logits.data_ptr(), logits.stride(0), (int)B, (int)logits.size(1), (int)v_off, (int)vocab,
+                       temperature.data_ptr<float>(), top_k.data_ptr<int>(), top_p.data_ptr<float>(), (uint64_t)seed,
+                       steps.data_ptr<int>(), (int)KC, (int)kmax, reinterpret_cast<float*>(base), base + B * KC,
+                       cur_stream());
+}
+
+// gathered: int32 [tp, 2, B, KC], every rank's sample_vp_local output
+void sample_vp_combine(const Tensor& gathered, int64_t vocab, const Tensor& temperature, const Tensor& top_k,
+                       const Tensor& top_p, int64_t seed, const Tensor& steps, int64_t kmax, Tensor& out) {
+  TORCH_CHECK(gathered.is_cuda() && gathered.scalar_type() == torch::kInt32 && gathered.is_contiguous() &&
+                  gathered.dim() == 4 && gathered.size(1) == 2, "sample_vp: int32 candidates [tp, 2, B, KC]");
+  const int64_t B = gathered.size(2), KC = gathered.size(3);
+  TORCH_CHECK(temperature.numel() >= B && top_k.numel() >= B && top_p.numel() >= B && steps.numel() >= B &&
+                  out.numel() >= B && out.scalar_type() == torch::kInt32, "sample_vp: per-row inputs");
+  same_device(gathered, {&temperature, &top_k, &top_p, &steps, &out}, "sample_vp_combine");
+  const c10::cuda::CUDAGuard guard(gathered.device());
+  const int* base = gathered.data_ptr<int>();
+  vrm::sample_vp_combine(reinterpret_cast<const float*>(base), base + B * KC, 2 * B * KC, (int)gathered.size(0),
+                         (int)B, (int)KC, (int)vocab, temperature.data_ptr<float>(), top_k.data_ptr<int>(),
+                         top_p.data_ptr<float>(), (uint64_t)seed, steps.data_ptr<int>(), (int)kmax,
+                         out.data_ptr<int>(), cur_stream());
+}
+
 // ---------------------------------------------------------------- fused GEMM + all-reduce
 // Push half: row-parallel GEMM (bf16, or e4m3 with its scales) whose epilogue stores the
 // partial into this rank's slot of every rank's receive buffer (ARPush).  Nothing is
@@ -1097,6 +1137,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return vrm::decode_attention_choose_splits((int)B, (int)KH, (int)max_pages);
   });
   m.def("argmax", &argmax, py::arg("logits"), py::arg("out"));
+  m.def("sample_vp_local", &sample_vp_local, py::arg("logits"), py::arg("v_off"), py::arg("vocab"),
+        py::arg("temperature"), py::arg("top_k"), py::arg("top_p"), py::arg("seed"), py::arg("steps"),
+        py::arg("kmax"), py::arg("cand"));
+  m.def("sample_vp_combine", &sample_vp_combine, py::arg("gathered"), py::arg("vocab"), py::arg("temperature"),
+        py::arg("top_k"), py::arg("top_p"), py::arg("seed"), py::arg("steps"), py::arg("kmax"), py::arg("out"));
   m.def("sample", &sample, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"),
         py::arg("seed"), py::arg("steps"), py::arg("out"));
   m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {

@@ -387,6 +387,17 @@ void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t stream);
 void argmax_rows(const void* logits, int64_t ld, int B, int V, int* out, cudaStream_t stream);
 void sample_rows(const void* logits, int64_t ld, int B, int V, const float* temperature, const int* top_k,
                  const float* top_p, uint64_t seed, const int* steps, int* out, cudaStream_t stream);
+// Vocabulary-parallel sampling: a rank's logits shard [B, Vs] (columns v_off.. of a
+// V_total vocabulary) -> KC candidates per row (cand_val fp32, cand_idx int32, [B, KC]);
+// after an all-gather of every rank's candidates (rank r's at r * rank_stride elements
+// from cand_val / cand_idx) the combine picks the same token on every rank.  Rows with top-k > kmax, or top-p < 1 without top-k, need
+// the full logits (sampling.cu explains the exactness conditions).
+void sample_vp_local(const void* logits, int64_t ld, int B, int Vs, int v_off, int V_total, const float* temperature,
+                     const int* top_k, const float* top_p, uint64_t seed, const int* steps, int KC, int kmax,
+                     float* cand_val, int* cand_idx, cudaStream_t stream);
+void sample_vp_combine(const float* cand_val, const int* cand_idx, int64_t rank_stride, int tp, int B, int KC,
+                       int V_total, const float* temperature, const int* top_k, const float* top_p, uint64_t seed,
+                       const int* steps, int kmax, int* out, cudaStream_t stream);
 
 // ---------------------------------------------------------------- symmetric buffers (symm.cu)
 void* symm_malloc(size_t bytes);

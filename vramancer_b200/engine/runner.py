@@ -84,6 +84,12 @@ class ModelRunner:
             self.buckets.append(max_batch)
         self.seed = seed
         self._graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        # vocabulary-parallel sampling (TP): the decode graph samples from this rank's
+        # logits shard; steps with a row that needs the whole distribution (top-p without
+        # top-k) replay a second graph that gathers full logits (_graphs_alt)
+        self._vp_model = bool(getattr(model, "vocab_parallel", False))
+        self._vp_step = self._vp_model
+        self._graphs_alt: Dict[int, torch.cuda.CUDAGraph] = {}
         self._graph_pool = None
         self._alloc_decode_buffers()
         self.launches_per_decode = None
@@ -135,8 +141,18 @@ class ModelRunner:
 
     def _decode_body(self, B: int) -> None:
         batch = self._decode_batch(B)
-        logits = self.model.forward(batch, self.pool)
-        if logits is not None:                    # None: a pipeline stage before the last
+        vp = self._vp_step
+        if vp:
+            self.model.set_vp_logits(True)
+        try:
+            logits = self.model.forward(batch, self.pool)
+        finally:
+            if vp:
+                self.model.set_vp_logits(False)
+        if logits is not None and vp:             # this rank's vocabulary shard
+            self.model.sample_vocab_parallel(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.seed,
+                                             self.d_steps[:B], out=self.d_out[:B])
+        elif logits is not None:                  # None: a pipeline stage before the last
             if logits.device != self.device:      # in-process pipeline: last stage on another GPU
                 logits = logits.to(self.device)
             ops.sample(logits, self.d_temp[:B], self.d_topk[:B], self.d_topp[:B], self.seed, self.d_steps[:B],
@@ -164,6 +180,7 @@ class ModelRunner:
         self.hn_topp[:n] = top_p
         for r, bt in enumerate(block_tables):
             self.hn_bt[r, :len(bt)] = bt
+        self._vp_step = self._vp_model and ops.vp_sampling_ok(temperature, top_k, top_p, self.model.cfg.vocab_size)
         return B
 
     def upload_decode_inputs(self) -> None:
@@ -178,7 +195,7 @@ class ModelRunner:
     def decode(self, B: int) -> torch.Tensor:
         """Runs one decode step for bucket B on the uploaded inputs; returns d_out[:B]."""
         if self.use_graph:
-            g = self._graphs.get(B)
+            g = (self._graphs if self._vp_step == self._vp_model else self._graphs_alt).get(B)
             if g is None:
                 g = self.capture(B)
             g.replay()
@@ -242,15 +259,19 @@ class ModelRunner:
         with torch.cuda.graph(g, pool=self._graph_pool):
             self._decode_body(B)
         torch.cuda.synchronize()
-        self._graphs[B] = g
+        (self._graphs if self._vp_step == self._vp_model else self._graphs_alt)[B] = g
         return g
 
     def capture_all(self, sizes: Optional[Sequence[int]] = None) -> None:
         if not self.use_graph:
             return
-        for B in sorted(sizes or self.buckets, reverse=True):
-            if B not in self._graphs:
-                self.capture(B)
+        step_vp, self._vp_step = self._vp_step, self._vp_model    # the default variant
+        try:
+            for B in sorted(sizes or self.buckets, reverse=True):
+                if B not in self._graphs:
+                    self.capture(B)
+        finally:
+            self._vp_step = step_vp
 
     def copy_pages(self, pairs) -> None:
         """Copy-on-write page copies (src, dst) in every KV pool this runner drives."""
@@ -262,6 +283,7 @@ class ModelRunner:
 
     def release_graphs(self) -> None:
         self._graphs.clear()
+        self._graphs_alt.clear()
         self._graph_pool = None
 
     # ------------------------------------------------------------------ prefill

@@ -57,12 +57,16 @@ class TPContext:
     """What a tensor-parallel rank needs from the communication layer."""
 
     def __init__(self, rank: int, size: int, all_reduce: Callable[[torch.Tensor], torch.Tensor],
-                 all_gather_last: Callable[[torch.Tensor], torch.Tensor], fused_ar=None):
+                 all_gather_last: Callable[[torch.Tensor], torch.Tensor], fused_ar=None,
+                 all_gather_stack: Optional[Callable[[torch.Tensor], torch.Tensor]] = None):
         self.rank, self.size = rank, size
         self.all_reduce = all_reduce
         self.all_gather_last = all_gather_last
         # optional FusedAllReduce: row-parallel GEMM with the all-reduce in its epilogue
         self.fused_ar = fused_ar
+        # x [...] -> [ranks, ...] (every rank's x): the candidate exchange of
+        # vocabulary-parallel sampling; None keeps full-logit gathers
+        self.all_gather_stack = all_gather_stack
 
 
 # Returned in place of a normalised activation when the next GEMM applies the RMSNorm
@@ -306,9 +310,28 @@ class DecoderModel:
         h = r if rows is None else r.index_select(0, rows)
         x = self._norm(h.contiguous(), "final", "final")
         lg = ops.linear(x, self.w["lm_head"])
-        if self.tp_size > 1:
+        if self.tp_size > 1 and not self.vp_logits:
             lg = self.tp.all_gather_last(lg)[:, : self.cfg.vocab_size]
         return lg
+
+    # ------------------------------------------------------------------ vocabulary-parallel sampling
+    vp_logits = False   # set by the runner around a forward whose sampling is vocabulary-parallel
+
+    @property
+    def vocab_parallel(self) -> bool:
+        """Decode sampling can run on this rank's logits shard (candidates exchanged
+        between ranks instead of full logits): TP > 1 on CUDA with a candidate gather."""
+        return (self.tp_size > 1 and self.has_head and self.device.type == "cuda"
+                and getattr(self.tp, "all_gather_stack", None) is not None
+                and os.environ.get("VRM_VP_SAMPLE", "1") != "0")
+
+    def set_vp_logits(self, on: bool) -> None:
+        self.vp_logits = bool(on)
+
+    def sample_vocab_parallel(self, logits, temperature, top_k, top_p, seed, steps, out):
+        """Samples from this rank's logits shard [B, V / tp]; every rank gets the same ids."""
+        return ops.sample_vocab_parallel(logits, self.tp.rank * self.w["lm_head"].shape[0], self.cfg.vocab_size,
+                                         temperature, top_k, top_p, seed, steps, self.tp.all_gather_stack, out=out)
 
     # ------------------------------------------------------------------ entry points
     def forward(self, batch: ForwardBatch, pool: KVPool, hidden: Optional[torch.Tensor] = None) -> torch.Tensor:

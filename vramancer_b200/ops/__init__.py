@@ -388,6 +388,41 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
     return out
 
 
+# Vocabulary-parallel sampling (sampling.cu): candidates per row and rank, and the
+# largest top-k served from candidates.
+VP_KC, VP_KMAX = 256, 128
+
+
+def vp_sampling_ok(temperature, top_k, top_p, vocab: int, kmax: int = VP_KMAX) -> bool:
+    """True when every row can be sampled from per-rank candidates: greedy, plain
+    temperature, or top-k <= kmax (with any top-p).  Top-p without top-k needs the whole
+    distribution, so such steps gather the full logits."""
+    for t, k, p in zip(temperature, top_k, top_p):
+        if t > 0 and not ((k <= 0 or k >= vocab) and p >= 1.0) and not (0 < k <= kmax):
+            return False
+    return True
+
+
+def sample_vocab_parallel(logits: torch.Tensor, v_off: int, vocab: int, temperature: torch.Tensor,
+                          top_k: torch.Tensor, top_p: torch.Tensor, seed: int, steps: torch.Tensor,
+                          gather, out: Optional[torch.Tensor] = None, kc: int = VP_KC,
+                          kmax: int = VP_KMAX) -> torch.Tensor:
+    """Samples rows of a vocabulary that is split over tensor-parallel ranks.
+
+    logits: this rank's bf16 shard [B, Vs] of columns [v_off, v_off + Vs); gather(t)
+    returns every rank's t stacked ([ranks, ...]).  Each rank reduces its shard to kc
+    candidates per row, one all-gather moves B x kc x 8 bytes per rank, and every rank
+    picks the same ids -- for greedy rows, plain-temperature rows and rows with
+    top-k <= kmax, the ids the full-vocabulary sampler gives (same Gumbel keys)."""
+    B = logits.shape[0]
+    if out is None:
+        out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    cand = torch.empty(2, B, kc, dtype=torch.int32, device=logits.device)
+    native().sample_vp_local(logits, int(v_off), int(vocab), temperature, top_k, top_p, int(seed), steps, kmax, cand)
+    native().sample_vp_combine(gather(cand), int(vocab), temperature, top_k, top_p, int(seed), steps, kmax, out)
+    return out
+
+
 def _host_call():
     m = native()
     LAUNCHES[0] -= 1

@@ -74,12 +74,17 @@ def tp_context(group=None) -> Optional[TPContext]:
         dist.all_gather(parts, x.contiguous(), group=group)
         return torch.cat(parts, dim=-1)
 
+    def all_gather_stack(x: torch.Tensor) -> torch.Tensor:
+        out = torch.empty((size,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+        return out
+
     fused = None
     if torch.cuda.is_available() and dist.get_backend(group) == "nccl" and \
             os.environ.get("VRM_FUSED_AR", "1") not in ("0", "false"):
         from .symm import FusedAllReduce
         fused = FusedAllReduce(group, max_tokens=int(os.environ.get("VRM_FUSED_AR_MAX_TOKENS", "128")))
-    return TPContext(rank, size, all_reduce, all_gather_last, fused_ar=fused)
+    return TPContext(rank, size, all_reduce, all_gather_last, fused_ar=fused, all_gather_stack=all_gather_stack)
 
 
 def barrier() -> None:

@@ -146,6 +146,16 @@ class PPStageModel:
     def fold_norms(self) -> bool:
         return False
 
+    @property
+    def vocab_parallel(self) -> bool:
+        return self.grid.is_last and self.model.vocab_parallel
+
+    def set_vp_logits(self, on: bool) -> None:
+        self.model.set_vp_logits(on)
+
+    def sample_vocab_parallel(self, *a, **kw):
+        return self.model.sample_vocab_parallel(*a, **kw)
+
     def _stage(self, batch: ForwardBatch, pool) -> Optional[torch.Tensor]:
         g = self.grid
         h = None

@@ -6,7 +6,7 @@
 The context gives the model rank 0 of `size` ranks: weights are rank 0's shards, every
 row-parallel projection runs the fused push GEMM + reduce/norm kernels with a one-rank
 receive buffer (the same kernels and data volume on this GPU, no NVLink traffic), and
-the vocabulary-parallel logits stay rank 0's slice.  Timing a decode step on it gives a
+the vocabulary-parallel logits stay rank 0's slice (sampled from rank 0's candidates).  Timing a decode step on it gives a
 TP rank's compute floor; a real TP=N run adds only the collectives' cost, so the two
 together say where a TP=N step's time goes.  Outputs are not those of the full model.
 """
@@ -23,4 +23,4 @@ def shard_context(size: int, device: Optional[str] = None, fused: bool = True) -
     from .symm import FusedAllReduce
     dev = torch.device(device or f"cuda:{torch.cuda.current_device()}")
     far = FusedAllReduce(device=dev, local=True) if fused and dev.type == "cuda" else None
-    return TPContext(0, size, lambda x: x, lambda x: x, fused_ar=far)
+    return TPContext(0, size, lambda x: x, lambda x: x, fused_ar=far, all_gather_stack=lambda x: x.unsqueeze(0))
