@@ -17,6 +17,52 @@ def test_find_draft_and_accept():
     assert accept_greedy([8], [0, 5]) == ([0], 0)
 
 
+def test_native_ngram_index_matches_find_draft():
+    """The engine's incremental index proposes what the backward scan proposes, for every
+    prefix, n-gram range and draft length (tokens arrive in chunks, as in decoding)."""
+    import random
+    from vramancer_b200.engine.speculative import ngram_index
+    if ngram_index() is None:
+        pytest.skip("host runtime not built")
+    rnd = random.Random(0)
+    for _ in range(200):
+        L = rnd.randint(1, 60)
+        seq = [rnd.randint(0, 5) for _ in range(L)]
+        mx = rnd.randint(1, 4)
+        mn = rnd.randint(1, mx)
+        nd = rnd.randint(1, 8)
+        ix = ngram_index(mx, mn)
+        i = 0
+        while i < L:
+            j = min(L, i + rnd.randint(1, 7))
+            ix.extend(seq[i:j])
+            i = j
+            assert ix.draft(nd) == find_draft(seq[:i], mx, nd, mn)
+
+
+def test_forced_acceptance_draft_provider():
+    """Drafts from engine.draft_provider equal to the greedy continuation are all
+    accepted, and the output is the plain greedy output."""
+    llm, cfg = _llm(spec_num_draft=4)
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (9, 23)]
+    params = SamplingParams(max_tokens=12, ignore_eos=True)
+    eng = llm.engine
+    eng.spec_num_draft = 0
+    ref = [list(r.output_ids) for r in eng.generate(prompts, params)]
+    eng.spec_num_draft = 4
+    cont = {}
+    eng.draft_provider = lambda r: cont[r.request_id][len(r.output_ids):len(r.output_ids) + 4]
+    reqs = [eng.add_request(p, params) for p in prompts]
+    for r, c in zip(reqs, ref):
+        cont[r.request_id] = c
+    p0, a0 = eng.spec_stats.proposed, eng.spec_stats.accepted
+    while any(not r.finished for r in reqs):
+        eng.step()
+    assert [list(r.output_ids) for r in reqs] == ref
+    assert eng.spec_stats.proposed > p0 and eng.spec_stats.accepted - a0 == eng.spec_stats.proposed - p0
+
+
 def _llm(**kw):
     cfg = PRESETS["tiny-qwen2"]
     w = random_weights(cfg, device="cpu", dtype=torch.float32, seed=5, std=0.2)

@@ -111,6 +111,10 @@ class LLMEngine:
         self.spec_ngram = spec_ngram
         from .speculative import SpecStats
         self.spec_stats = SpecStats()
+        # per-request incremental n-gram indexes (native), and an optional override that
+        # supplies each request's draft (e.g. a known continuation: forced acceptance)
+        self._ngram: Dict[object, object] = {}
+        self.draft_provider: Optional[Callable[[Request], List[int]]] = None
         # overlapped decode: step n+1 is launched (fed from the device) before step n's
         # tokens are read back, so host scheduling hides behind the GPU's work
         self.lookahead = lookahead and ep_sync is None and os.environ.get("VRM_LOOKAHEAD", "1") != "0"
@@ -213,6 +217,24 @@ class LLMEngine:
             req.cached_tokens = cached
             self.running.append(req)
 
+    def _draft(self, r: Request) -> List[int]:
+        """Prompt-lookup draft of a running request (native n-gram index, extended by the
+        tokens generated since its last draft; the Python scan without the runtime)."""
+        if self.draft_provider is not None:
+            return list(self.draft_provider(r))[:self.spec_num_draft]
+        from .speculative import find_draft, ngram_index
+        ix = self._ngram.get(r.request_id)
+        if ix is None:
+            ix = ngram_index(self.spec_ngram)
+            if ix is None:
+                return find_draft(r.prompt_ids + r.output_ids, self.spec_ngram, self.spec_num_draft)
+            ix.extend(list(r.prompt_ids))
+            self._ngram[r.request_id] = ix
+        have = len(ix) - len(r.prompt_ids)
+        if have < len(r.output_ids):
+            ix.extend(list(r.output_ids[have:]))
+        return ix.draft(self.spec_num_draft)
+
     def _finish(self, req: Request, reason: str) -> None:
         if req.finished:
             return
@@ -224,6 +246,7 @@ class LLMEngine:
         elif req in self.waiting:
             self.waiting.remove(req)
         self.kv.free(req.request_id)
+        self._ngram.pop(req.request_id, None)
         self.stats["finished"] += 1
         if req.future is not None and not req.future.done():
             req.future.set_result(req)
@@ -313,14 +336,12 @@ class LLMEngine:
     def _decode(self, done: List[Request]) -> None:
         active = [r for r in self.running if r.prefill_done and not r.finished and r.output_ids]
         if self.spec_num_draft > 0 and active:
-            from .speculative import find_draft, speculative_decode_step
-            drafts = [find_draft(r.prompt_ids + r.output_ids, self.spec_ngram, self.spec_num_draft)
-                      for r in active]
+            from .speculative import speculative_decode_step
+            drafts = [self._draft(r) for r in active]
             if any(drafts):
                 self._drain(done)
                 active = [r for r in active if not r.finished]
-                drafts = [find_draft(r.prompt_ids + r.output_ids, self.spec_ngram, self.spec_num_draft)
-                          for r in active]
+                drafts = [self._draft(r) for r in active]
                 if not self._pages_for_verify(active, drafts):
                     drafts = []          # not enough KV pages: plain decode (with preemption)
             if drafts and any(drafts):

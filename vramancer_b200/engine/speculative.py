@@ -49,6 +49,16 @@ def find_draft(seq: Sequence[int], max_ngram: int = 3, num_draft: int = 8, min_n
     return []
 
 
+def ngram_index(max_ngram: int = 3, min_ngram: int = 1):
+    """A native incremental index with `find_draft`'s rule (extend(tokens), draft(k),
+    len), or None when the host runtime is not built."""
+    try:
+        from .. import _runtime
+    except ImportError:
+        return None
+    return _runtime.NgramIndex(max_ngram, min_ngram)
+
+
 def accept_greedy(draft: Sequence[int], preds: Sequence[int]) -> Tuple[List[int], int]:
     """(accepted drafts + bonus token, number of accepted drafts)."""
     acc = []
@@ -293,8 +303,14 @@ class DraftModelDecoder:
     def target_vocab(self) -> int:
         return self.target.cfg.vocab_size
 
+    def _draft_can_read(self, seq: Sequence[int]) -> bool:
+        """A draft with a smaller vocabulary cannot embed ids beyond it: no draft then."""
+        return not seq or max(seq) < self.draft.cfg.vocab_size
+
     def _propose(self, seq: List[int], k: int) -> List[int]:
         from .engine import SamplingParams
+        if not self._draft_can_read(seq):
+            return []
         r = self.draft.engine.generate([seq], SamplingParams(max_tokens=k))[0]
         out = []
         for t in r.output_ids:      # an id the target's vocabulary lacks ends the draft
@@ -312,6 +328,8 @@ class DraftModelDecoder:
         rows = []
         cur = list(seq)
         V = self.target_vocab
+        if not self._draft_can_read(cur):
+            return toks, None
         for _ in range(k):
             if len(cur) + 1 > self.draft.engine.max_model_len:
                 break

@@ -178,6 +178,13 @@ PYBIND11_MODULE(_runtime, m) {
       .def_property_readonly("num_free", &vrt::PageAllocator::num_free)
       .def_property_readonly("num_pages", &vrt::PageAllocator::num_pages);
 
+  // ---- prompt-lookup drafts
+  py::class_<vrt::NgramIndex>(m, "NgramIndex")
+      .def(py::init<int, int>(), py::arg("max_n") = 3, py::arg("min_n") = 1)
+      .def("extend", [](vrt::NgramIndex& ix, const std::vector<int32_t>& toks) { ix.extend(toks.data(), toks.size()); })
+      .def("draft", &vrt::NgramIndex::draft, py::arg("num_draft"))
+      .def("__len__", &vrt::NgramIndex::size);
+
   // ---- tokenizer
   m.def("basic_tokenize", [](const std::vector<std::string>& texts, int32_t vocab, int threads) {
     py::gil_scoped_release nogil;

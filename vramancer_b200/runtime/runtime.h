@@ -149,4 +149,21 @@ class PageAllocator {
 std::vector<std::vector<int32_t>> basic_tokenize(const std::vector<std::string>& texts, int32_t vocab,
                                                  int threads);
 
+// ---------------------------------------------------------------- ngram.cpp
+// Prompt-lookup draft index of one growing token sequence (see ngram.cpp).
+class NgramIndex {
+ public:
+  NgramIndex(int max_n, int min_n);
+  void extend(const int32_t* tokens, size_t count);
+  std::vector<int32_t> draft(int num_draft) const;
+  size_t size() const { return seq_.size(); }
+
+ private:
+  uint64_t key(size_t start, int n) const;
+  bool same(size_t a, size_t b, int n) const;
+  int max_n_, min_n_;
+  std::vector<int32_t> seq_;
+  std::vector<std::unordered_map<uint64_t, size_t>> maps_;   // [n]: n-gram -> latest earlier start
+};
+
 }  // namespace vrt

@@ -12,6 +12,8 @@ serve   continuous batching of N requests arriving at once, prompt lengths unifo
         [min, max], `output` tokens each (EOS ignored): output tok/s over the whole run
         (wall clock between device synchronisations: prefill, decode, scheduling and
         host<->device copies included), TTFT p50 / p99, mean batch per decode step.
+spec-cost  verify-step time against draft length 1..8 under forced acceptance (drafts =
+        the greedy continuation), and the speed-up it implies at acceptance 0.5..0.9.
 spec    prompt-lookup speculative decoding: prompts made of a random 64-token span
         repeated 8 times; greedy decode with speculation off and on (n-gram 3, 8
         drafted tokens), tok/s of each, acceptance and token-for-token equality.
@@ -209,6 +211,69 @@ def run_spec(args, info, dev, tp) -> dict:
     return out
 
 
+def run_spec_cost(args, info, dev, tp) -> dict:
+    """Verify-step cost against draft length under forced acceptance.
+
+    A plain greedy run gives each prompt's continuation; then, for every draft length d,
+    the same prompts run again with speculation whose drafts are the next d tokens of
+    that continuation (engine.draft_provider), so every draft is accepted.  The verify
+    step feeds d + 1 tokens per sequence whatever is accepted, so its measured time
+    t(d) also holds at lower acceptance: with acceptance a per draft token a step yields
+    (1 - a^(d+1)) / (1 - a) tokens per sequence, and the expected throughput at a is
+    batch x that / t(d), against batch / t(0) for plain decode (d = 0: graph-replayed
+    decode steps)."""
+    from .engine.engine import SamplingParams
+    B, P, G = args.batch, args.prompt_len, args.output
+    lens = [int(x) for x in args.draft_lens.split(",") if x.strip()]
+    llm = _build(args, dev, tp, max_batch=B, max_len=P + G + 64, spec_num_draft=0, spec_ngram=args.ngram)
+    vocab = llm.cfg.vocab_size
+    r2 = random.Random(args.seed)
+    prompts = [[r2.randrange(vocab) for _ in range(P)] for _ in range(B)]
+    params = SamplingParams(max_tokens=G, ignore_eos=True)
+    llm.warmup()
+    eng = llm.engine
+    ref = [list(r.output_ids) for r in eng.generate(prompts, params)]
+    cont = {}
+    rows = []
+    for d in [0] + lens:
+        eng.spec_num_draft = d
+        eng.draft_provider = (lambda r, d=d: cont[r.request_id][len(r.output_ids):len(r.output_ids) + d]) if d else None
+        st0 = (eng.spec_stats.proposed, eng.spec_stats.accepted)
+        reqs = [eng.add_request(p, params) for p in prompts]
+        for r, c in zip(reqs, ref):
+            cont[r.request_id] = c
+        while any(not r.output_ids for r in reqs):          # prefill (and first token)
+            eng.step()
+        _sync(dev)
+        t0 = time.perf_counter()
+        n0 = sum(len(r.output_ids) for r in reqs)
+        steps = 0
+        while any(not r.finished for r in reqs):
+            eng.step()
+            steps += 1
+        _sync(dev)
+        wall = time.perf_counter() - t0
+        toks = sum(len(r.output_ids) for r in reqs) - n0
+        row = {"draft_len": d, "steps": steps, "ms_per_step": round(wall / max(steps, 1) * 1e3, 3),
+               "tokens_per_step": round(toks / max(steps, 1), 2), "tok_s": round(toks / wall, 1),
+               "tokens_equal": [list(r.output_ids) for r in reqs] == ref}
+        if d:
+            drafted = eng.spec_stats.proposed - st0[0]
+            row["acceptance"] = round((eng.spec_stats.accepted - st0[1]) / max(drafted, 1), 3)
+        rows.append(row)
+    eng.draft_provider = None
+    base = rows[0]["ms_per_step"]
+    for row in rows[1:]:
+        d, t = row["draft_len"], row["ms_per_step"]
+        row["verify_cost_vs_decode"] = round(t / base, 3)
+        row["speedup_at_acceptance"] = {str(a): round(((1 - a ** (d + 1)) / (1 - a)) * base / t, 3)
+                                        for a in (0.5, 0.7, 0.8, 0.9)}
+    return {"workload": "spec-cost", "model": args.model, "quantization": args.quantization or "bf16",
+            "batch": B, "prompt_len": P, "output_tokens": G, "rows": rows,
+            "timing": "wall clock between device synchronisations over the decode phase (engine API)",
+            "data": "synthetic ids, random-init N(0,0.02) weights; drafts = the greedy continuation"}
+
+
 def run_prefill(args, info, dev, tp) -> dict:
     from .engine.engine import SamplingParams
     rng = random.Random(args.seed)
@@ -269,7 +334,7 @@ def run_decode(args, info, dev, tp) -> List[dict]:
 
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    ap.add_argument("what", choices=["serve", "spec", "prefill", "decode"])
+    ap.add_argument("what", choices=["serve", "spec", "spec-cost", "prefill", "decode"])
     ap.add_argument("--model", default="qwen2.5-14b")
     ap.add_argument("--quantization", default=None, choices=[None, "nvfp4", "fp8"])
     ap.add_argument("--kv-dtype", default="bf16")
@@ -287,6 +352,7 @@ def parse_args(argv=None):
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--batches", default="1,8,64")
+    ap.add_argument("--draft-lens", default="1,2,4,8", help="spec-cost: draft lengths to time")
     ap.add_argument("--prompt-len", type=int, default=1024)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
@@ -298,7 +364,8 @@ def parse_args(argv=None):
 def main(argv=None) -> None:
     args = parse_args(argv)
     info, dev, tp = _init(args)
-    fn = {"serve": run_serve, "spec": run_spec, "prefill": run_prefill, "decode": run_decode}[args.what]
+    fn = {"serve": run_serve, "spec": run_spec, "spec-cost": run_spec_cost, "prefill": run_prefill,
+          "decode": run_decode}[args.what]
     res = fn(args, info, dev, tp)
     if info.rank == 0:
         for r in (res if isinstance(res, list) else [res]):
