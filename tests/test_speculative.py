@@ -245,3 +245,42 @@ def test_prompt_lookup_on_gpu_greedy_and_sampled(cuda_errors_clean):
     reqs += llm.generate(prompts[:1], SamplingParams(max_tokens=24, temperature=0.7, top_k=20))
     assert [len(r.output_ids) for r in reqs] == [32, 32, 24]
     assert llm.engine.spec_stats.proposed > 0
+
+
+@pytest.mark.gpu
+def test_graph_verify_on_gpu_forced_acceptance(cuda_errors_clean):
+    """Greedy verify steps replay a CUDA graph per (batch bucket, tokens per sequence).
+    With drafts equal to the plain greedy continuation nearly every draft is accepted,
+    and the tokens agree with the eager verify forward (bf16: the verify GEMMs see
+    other token counts than decode, so a near-tie may flip)."""
+    from vramancer_b200.engine.engine import SamplingParams
+    from vramancer_b200.llm import LLM
+    llm = LLM("tiny-qwen2-d128", device="cuda:0", max_batch=4, max_model_len=256, kv_pages=64, spec_num_draft=4,
+              spec_ngram=2)
+    g = torch.Generator().manual_seed(7)
+    prompts = [torch.randint(0, 1024, (n,), generator=g).tolist() for n in (30, 12, 50)]
+    params = SamplingParams(max_tokens=24, ignore_eos=True)
+    eng = llm.engine
+    eng.spec_num_draft = 0
+    ref = [list(r.output_ids) for r in eng.generate(prompts, params)]
+    eng.spec_num_draft = 4
+    cont = {}
+    eng.draft_provider = lambda r: cont[r.request_id][len(r.output_ids):len(r.output_ids) + 4]
+
+    def run():
+        reqs = [eng.add_request(p, params) for p in prompts]
+        for r, c in zip(reqs, ref):
+            cont[r.request_id] = c
+        p0, a0 = eng.spec_stats.proposed, eng.spec_stats.accepted
+        while any(not r.finished for r in reqs):
+            eng.step()
+        acc = (eng.spec_stats.accepted - a0) / max(1, eng.spec_stats.proposed - p0)
+        return [list(r.output_ids) for r in reqs], acc
+
+    g_out, g_acc = run()
+    assert llm.runner._verify, "the graph verify path did not run"
+    llm.runner.verify_greedy = lambda items: None          # eager verify forward
+    e_out, e_acc = run()
+    assert [len(x) for x in g_out] == [24, 24, 24]
+    agree = sum(a == b for x, y in zip(g_out, e_out) for a, b in zip(x, y)) / 72
+    assert g_acc >= 0.9 and e_acc >= 0.9 and agree >= 0.9, (g_acc, e_acc, agree)

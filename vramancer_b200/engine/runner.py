@@ -93,6 +93,9 @@ class ModelRunner:
         self._graph_pool = None
         self._alloc_decode_buffers()
         self.launches_per_decode = None
+        # graph-replayed speculative verify: (batch bucket, tokens per sequence) ->
+        # (graph, static buffers)
+        self._verify: Dict[tuple, tuple] = {}
 
     # ------------------------------------------------------------------ buffers
     def _alloc_decode_buffers(self):
@@ -284,6 +287,7 @@ class ModelRunner:
     def release_graphs(self) -> None:
         self._graphs.clear()
         self._graphs_alt.clear()
+        self._verify.clear()
         self._graph_pool = None
 
     # ------------------------------------------------------------------ prefill
@@ -350,6 +354,101 @@ class ModelRunner:
         for j, r in enumerate(sel):
             res[r] = nxt[j]
         return res
+
+    # ------------------------------------------------------------------ speculative verify
+    VERIFY_TOKENS = (2, 3, 5, 9, 13, 17)     # tokens per sequence: 1 + draft length
+
+    def _verify_buffers(self, B: int, T: int):
+        P = self.max_pages
+        n = 3 * B * T + B * P + B + (B + 1)
+        d = torch.zeros(n, dtype=torch.int32, device=self.device)
+        h = torch.zeros(n, dtype=torch.int32, pin_memory=True)
+        views = {}
+        o = 0
+        for name, size in (("ids", B * T), ("pos", B * T), ("slots", B * T), ("bt", B * P), ("ctx", B),
+                           ("cu", B + 1)):
+            views[name] = (d[o:o + size], h[o:o + size])
+            o += size
+        out = torch.zeros(B * T, dtype=torch.int32, device=self.device)
+        h_out = torch.zeros(B * T, dtype=torch.int32, pin_memory=True)
+        return d, h, views, out, h_out
+
+    def _verify_body(self, B: int, T: int, views, out) -> None:
+        g = lambda k: views[k][0]   # noqa: E731
+        batch = ForwardBatch(input_ids=g("ids"), positions=g("pos"), slot_mapping=g("slots"),
+                             block_tables=g("bt").view(B, self.max_pages), context_lens=g("ctx"), is_decode=False,
+                             cu_q=g("cu"), max_q_len=T, logits_rows=None)
+        vp = self._vp_model
+        if vp:
+            self.model.set_vp_logits(True)
+        try:
+            logits = self.model.forward(batch, self.pool)
+        finally:
+            if vp:
+                self.model.set_vp_logits(False)
+        if vp:                                     # greedy over this rank's vocabulary shard
+            z = torch.zeros(B * T, dtype=torch.float32, device=self.device)
+            zi = torch.zeros(B * T, dtype=torch.int32, device=self.device)
+            self.model.sample_vocab_parallel(logits, z, zi, z, 0, zi, out)
+        else:
+            ops.argmax(logits, out=out)
+
+    def verify_greedy(self, items: List[PrefillItem]) -> Optional[List[List[int]]]:
+        """The target's greedy token after every fed position of each item (a speculative
+        verify step), from a CUDA graph per (batch bucket, tokens per sequence): every
+        sequence feeds T tokens; positions past an item's tokens write no KV and their
+        outputs are dropped.  None when it does not apply (no graphs, too many tokens)."""
+        if not self.use_graph or not items:
+            return None
+        n = len(items)
+        longest = max(len(it.token_ids) for it in items)
+        T = next((t for t in self.VERIFY_TOKENS if t >= longest), None)
+        if T is None or n > self.max_batch:
+            return None
+        B = self.bucket_for(n)
+        key = (B, T)
+        ent = self._verify.get(key)
+        if ent is None:
+            ent = self._verify_buffers(B, T)
+        d, h, views, out, h_out = ent[:5]
+        hn = {k: v[1].numpy() for k, v in views.items()}
+        hn["ids"][:] = 0
+        hn["pos"][:] = 0
+        hn["slots"][:] = -1
+        hn["ctx"][:] = 0
+        hn["cu"][:] = [T * i for i in range(B + 1)]
+        bt = hn["bt"].reshape(B, self.max_pages)
+        maxpos = self.model.cfg.max_position - 1
+        for r, it in enumerate(items):
+            m = len(it.token_ids)
+            ids = list(it.token_ids) + [it.token_ids[-1]] * (T - m)
+            hn["ids"][r * T:(r + 1) * T] = ids
+            hn["pos"][r * T:(r + 1) * T] = [min(it.start_pos + j, maxpos) for j in range(T)]
+            hn["slots"][r * T:r * T + m] = list(it.slots)
+            hn["ctx"][r] = it.start_pos + T
+            bt[r, :] = 0
+            bt[r, :len(it.block_table)] = it.block_table
+        d.copy_(h, non_blocking=True)
+        if len(ent) == 5:
+            # warm-up on these inputs (writes only the items' own KV slots), then capture
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                self._verify_body(B, T, views, out)
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            if self._graph_pool is None:
+                self._graph_pool = torch.cuda.graph_pool_handle()
+            with torch.cuda.graph(graph, pool=self._graph_pool):
+                self._verify_body(B, T, views, out)
+            ent = ent + (graph,)
+            self._verify[key] = ent
+        ent[5].replay()
+        h_out.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        o = h_out.numpy()
+        return [o[r * T:r * T + len(it.token_ids)].tolist() for r, it in enumerate(items)]
 
     def prefill_logits(self, items: List[PrefillItem]) -> torch.Tensor:
         """Prefill returning the raw logits rows (for scoring / speculative verify)."""

@@ -187,6 +187,11 @@ def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: S
         starts.append(start)
         ds.append(d)
     engine._apply_cow()
+    if all(r.params.greedy for r in active) and getattr(runner, "verify_greedy", None) is not None:
+        # greedy batch: the verify forward + argmax replay as one CUDA graph
+        vg = runner.verify_greedy(items)
+        if vg is not None:
+            return _accept_all_greedy(engine, active, feeds, starts, ds, [t for row in vg for t in row], stats)
     logits = runner.prefill_logits(items)
     if logits.is_cuda:
         preds = ops.argmax(logits).cpu().tolist()
@@ -231,6 +236,21 @@ def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: S
         stats.proposed += len(d)
         stats.accepted += na
         kv.truncate(r.request_id, start + 1 + na)
+        out.append(toks)
+    return out
+
+
+def _accept_all_greedy(engine, active, feeds, starts, ds, preds, stats):
+    out = []
+    off = 0
+    stats.steps += 1
+    for r, feed, start, d in zip(active, feeds, starts, ds):
+        p = preds[off:off + len(feed)]
+        off += len(feed)
+        toks, na = accept_greedy(d, p)
+        stats.proposed += len(d)
+        stats.accepted += na
+        engine.kv.truncate(r.request_id, start + 1 + na)
         out.append(toks)
     return out
 
