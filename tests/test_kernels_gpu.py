@@ -34,6 +34,33 @@ def test_gemm(M, N, K, cuda_errors_clean):
     _close(y, ref)
 
 
+@pytest.mark.parametrize("mode", [0, 1, 3, 4])
+@pytest.mark.parametrize("M,N,K", [(129, 512, 320), (512, 5120, 1024), (300, 2304, 5120), (1000, 1536, 640)])
+def test_gemm_prefill_modes(mode, M, N, K, cuda_errors_clean):
+    """Every prefill GEMM kernel (tiled, stream-K, persistent 128- and 256-wide) against
+    the fp32 reference, with bias + residual and with the SiLU-mul epilogue.  Shapes
+    leave partial tiles and (persistent) K-split tails of the last round."""
+    torch.manual_seed(M + N + K + mode)
+    x = (torch.randn(M, K) * 0.5).bfloat16()
+    w = (torch.randn(N, K) * 0.05).bfloat16()
+    b = (torch.randn(N) * 0.1).bfloat16()
+    r = torch.randn(M, N).bfloat16()
+    ref = ops.linear(x, w, b, residual=r)
+    ref_silu = ops.linear(x, w, b, epilogue=ops.EPI_SILU_MUL)
+    nat = ops.native()
+    nat.gemm_set_prefill_mode(mode)
+    try:
+        xg, wg, bg = x.to(DEV), w.to(DEV), b.to(DEV)
+        y = ops.linear(xg, wg, bg, residual=r.to(DEV))
+        y2 = ops.linear(xg, wg, bg, epilogue=ops.EPI_SILU_MUL)
+        y3 = ops.linear(xg, wg, bg, residual=r.to(DEV))
+    finally:
+        nat.gemm_set_prefill_mode(0)
+    _close(y, ref)
+    _close(y2, ref_silu)
+    assert torch.equal(y, y3)      # split tails sum in split order: deterministic
+
+
 @pytest.mark.parametrize("M", [1, 32, 256])
 @pytest.mark.parametrize("splits", [1, 2, 5])
 def test_gemm_splitk_deterministic(M, splits, cuda_errors_clean):

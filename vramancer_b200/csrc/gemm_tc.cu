@@ -488,6 +488,250 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // =====================================================================================
+// Persistent prefill GEMM: one CTA per SM walks work units u = blockIdx.x, + gridDim.x:
+// units [0, full_tiles) are whole 128 x BN output tiles (token-block fastest, so the
+// CTAs in flight share each weight tile through L2), later units are K-splits of the
+// tail tiles that the last round could not fill (partials summed by the tile's last
+// split, as in gemm_bf16_tc_kernel).  Warp 0 streams A/B tiles through a STAGES-deep
+// TMA ring that runs across unit boundaries; warp 1 issues the MMAs into one of two
+// TMEM accumulators (2 x BN columns); warps 2-5 drain the other accumulator, so a
+// tile's epilogue overlaps the next tile's main loop and the ring never restarts.
+template <int BN, int STAGES>
+struct PersistSmem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  // full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], then tmem slot + flag
+  static constexpr int kTotal = kBarOffset + (2 * STAGES + 4) * 8 + 16;
+  static constexpr int kAlloc = kTotal + 1024;
+};
+
+struct UnitMap {
+  int full_tiles, tail_splits, num_a_tiles, total_k_tiles;
+  __device__ __forceinline__ void get(int u, int& tile, int& split, int& nsplit, int& kb, int& ke) const {
+    if (u < full_tiles) {
+      tile = u;
+      split = 0;
+      nsplit = 1;
+    } else {
+      const int j = u - full_tiles;
+      tile = full_tiles + j / tail_splits;
+      split = j % tail_splits;
+      nsplit = tail_splits;
+    }
+    const int per = (total_k_tiles + nsplit - 1) / nsplit;
+    kb = split * per;
+    ke = min(total_k_tiles, kb + per);
+    if (ke < kb) ke = kb;
+  }
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                           EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters, int K,
+                           int num_a_tiles, int full_tiles, int tail_splits, int num_units,
+                           uint32_t* __restrict__ err) {
+  using L = PersistSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* acc_full = empty_bar + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint32_t* flag_slot = tmem_slot + 1;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const UnitMap um{full_tiles, tail_splits, num_a_tiles, (K + kBK - 1) / kBK};
+  constexpr uint32_t kTmemCols = 2 * BN;   // two accumulators
+
+  pdl_launch();
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);   // every epilogue thread arrives after its TMEM reads
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer: one ring position per k-tile, across units
+    const uint64_t pol_a = policy_evict_last();    // activations: re-read by every weight tile
+    const uint64_t pol_b = policy_evict_normal();  // weights: shared by the token blocks in flight
+    pdl_wait();
+    int it = 0;
+    bool failed = false;
+    for (int u = blockIdx.x; u < num_units && !failed; u += gridDim.x) {
+      int tile, split, nsplit, kb, ke;
+      um.get(u, tile, split, nsplit, kb, ke);
+      const int a_tile = tile % num_a_tiles, b_tile = tile / num_a_tiles;
+      for (int kt = kb; kt < ke; ++kt, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&empty_bar[s], ph ^ 1, err)) {
+          failed = true;
+          break;
+        }
+        uint8_t* sa = smem + s * L::kStageBytes;
+        mbar_arrive_expect_tx(&full_bar[s], L::kStageBytes);
+        tma_load_2d(sa, &map_a, &full_bar[s], kt * kBK, a_tile * kBM, pol_a);
+        tma_load_2d(sa + L::kABytes, &map_b, &full_bar[s], kt * kBK, b_tile * BN, pol_b);
+      }
+    }
+    // none of our bulk copies may still be in flight when the CTA exits
+    const int first = it > STAGES ? it - STAGES : 0;
+    for (int j = first; j < it; ++j) mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1, err);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    constexpr uint32_t idesc = make_idesc_bf16(kBM, BN);
+    int it = 0, n = 0;
+    bool failed = false;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++n) {
+      int tile, split, nsplit, kb, ke;
+      um.get(u, tile, split, nsplit, kb, ke);
+      const int acc = n & 1;
+      // the epilogue has read this accumulator's previous tile (first use passes)
+      if (!failed && !mbar_wait(&acc_empty[acc], ((n >> 1) & 1) ^ 1, err)) failed = true;
+      tc_fence_after();
+      const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+      for (int kt = kb; kt < ke && !failed; ++kt, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&full_bar[s], ph, err)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * L::kStageBytes);
+        const uint64_t da = make_sw128_desc(sa);
+        const uint64_t db = make_sw128_desc(sa + L::kABytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+          umma_f16(d, da + (uint64_t)(kk * 2), db + (uint64_t)(kk * 2), idesc, (kt > kb || kk > 0) ? 1u : 0u);
+        umma_commit(&empty_bar[s]);
+      }
+      umma_commit(&acc_full[acc]);   // always: the epilogue waits for every unit
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue (128 threads, one TMEM lane each)
+    const int lane_base = 32 * (warp & 3);
+    const int row = lane_base + lane;
+    pdl_wait();
+    int n = 0;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++n) {
+      int tile, split, nsplit, kb, ke;
+      um.get(u, tile, split, nsplit, kb, ke);
+      const int acc = n & 1;
+      const bool ok = mbar_wait(&acc_full[acc], (n >> 1) & 1, err);
+      tc_fence_after();
+      const int a_tile = tile % num_a_tiles, b_tile = tile / num_a_tiles;
+      const int r_glob = a_tile * kBM + row;
+      const int c_base = b_tile * BN;
+      const uint32_t t_row = tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN);
+      const bool direct = nsplit == 1;
+      const bool have = ok && ke > kb;
+      float* slot0 = direct ? nullptr
+                            : workspace + (((size_t)(tile - full_tiles) * nsplit) * kBM + row) * (size_t)BN;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r0[16], r1[16];
+        tmem_ld_32x32b_x16(t_row + c0, r0);
+        tmem_ld_32x32b_x16(t_row + c0 + 16, r1);
+        tmem_wait_ld();
+        float v0[16], v1[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          v0[j] = have ? __uint_as_float(r0[j]) : 0.f;
+          v1[j] = have ? __uint_as_float(r1[j]) : 0.f;
+        }
+        if (c0 + 32 >= BN) {
+          // the accumulator is read: the MMA warp may start the unit after next on it
+          tc_fence_before();
+          mbar_arrive(&acc_empty[acc]);
+        }
+        if (direct) {
+          epi_store<false>(ep, r_glob, c_base + c0, v0);
+          epi_store<false>(ep, r_glob, c_base + c0 + 16, v1);
+        } else {
+          float4* dst = reinterpret_cast<float4*>(slot0 + (size_t)split * kBM * BN + c0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            __stcg(dst + q, make_float4(v0[4 * q], v0[4 * q + 1], v0[4 * q + 2], v0[4 * q + 3]));
+            __stcg(dst + 4 + q, make_float4(v1[4 * q], v1[4 * q + 1], v1[4 * q + 2], v1[4 * q + 3]));
+          }
+        }
+      }
+      if (!direct) {
+        // the tile's last split sums every split's partial in split order
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          const uint32_t prev = atomicAdd(&tile_counters[tile], 1u);
+          *flag_slot = (prev == (uint32_t)(nsplit - 1)) ? 1u : 0u;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const bool last = *flag_slot != 0u;
+        asm volatile("bar.sync 1, 128;" ::: "memory");   // flag read before the next unit sets it
+        if (last) {
+          __threadfence();
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0.f;
+            for (int s0 = 0; s0 < nsplit; s0 += 4) {
+              float4 x[4][4];
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                const float4* src = reinterpret_cast<const float4*>(slot0 + (size_t)(s0 + w) * kBM * BN + c0);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  x[w][q] = s0 + w < nsplit ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int w = 0; w < 4; ++w)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  v[4 * q] += x[w][q].x;
+                  v[4 * q + 1] += x[w][q].y;
+                  v[4 * q + 2] += x[w][q].z;
+                  v[4 * q + 3] += x[w][q].w;
+                }
+            }
+            epi_store<false>(ep, r_glob, c_base + c0, v);
+          }
+          if (threadIdx.x == 64) tile_counters[tile] = 0u;   // ready for the next launch
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// =====================================================================================
 // Stream-K decode GEMM (swap-AB): one persistent CTA per SM.  The iteration space
 // tiles x k_tiles (tile = 128 weight rows, k_tile = 64 K elements) is cut into equal
 // contiguous ranges, one per CTA, so every SM streams the same number of weight bytes
@@ -1363,16 +1607,51 @@ static void choose_split(int tiles, int k_tiles, int min_k, int* splits, int* kt
 // tile's token blocks one after another and re-reads it from HBM once it is evicted)
 // 0: tiled kernel, 1: stream-K with 128-token tiles, 2: stream-K with 256-token tiles
 // (MMA 128 x 256, four 48 KB stages, 512 TMEM columns: one CTA per SM)
+// 0 tiled (default), 1 stream-K, 2 stream-K with 256-token tiles, 3 persistent,
+// 4 persistent with 256-wide weight tiles; VRM_GEMM_PREFILL or gemm_set_prefill_mode
+static int g_prefill_mode = -1;
+void gemm_set_prefill_mode(int mode) { g_prefill_mode = mode; }
 static int prefill_mode() {
-  static const int v = [] {
+  if (g_prefill_mode < 0) {
     const char* e = std::getenv("VRM_GEMM_PREFILL");
-    if (!e) return 0;
-    const std::string m(e);
-    return m == "streamk256" ? 2 : m == "streamk" ? 1 : 0;
-  }();
-  return v;
+    const std::string m(e ? e : "");
+    g_prefill_mode = m == "streamk256" ? 2 : m == "streamk" ? 1 : m == "persistent" ? 3 : m == "persistent256" ? 4 : 0;
+  }
+  return g_prefill_mode;
 }
-static bool prefill_streamk() { return prefill_mode() != 0; }
+static bool prefill_streamk() { return prefill_mode() == 1 || prefill_mode() == 2; }
+
+// Persistent prefill GEMM (gemm_persistent_kernel): whole tiles for the complete rounds
+// over the SMs, the tail split K-wise (choose_tail_split), one CTA per SM.
+template <int BN, int STAGES>
+static void launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, const EpiParams& ep, int K,
+                              int a_tiles, int b_tiles, cudaStream_t stream) {
+  using L = PersistSmem<BN, STAGES>;
+  auto kern = gemm_persistent_kernel<BN, STAGES>;
+  static int attr_dev_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
+    attr_dev_mask |= 1 << (dev & 31);
+  }
+  const int tiles = a_tiles * b_tiles;
+  const int k_tiles = (K + kBK - 1) / kBK;
+  int full = tiles, tail_splits = 1;
+  choose_tail_split(tiles, k_tiles, 8, &full, &tail_splits);
+  if (tail_splits <= 1) full = tiles;
+  float* ws = nullptr;
+  uint32_t* counters = nullptr;
+  if (full < tiles) {
+    ws = static_cast<float*>(workspace_get((size_t)(tiles - full) * tail_splits * kBM * BN * sizeof(float), stream));
+    VRM_REQUIRE((size_t)tiles <= 32768, "too many split-K tiles");
+    counters = tile_counters_get(stream);
+  }
+  const int units = full + (tiles - full) * std::max(1, tail_splits);
+  const int grid = std::min(units, device_sm_count());
+  launch_kernel(kern, dim3(grid), dim3(kGemmThreads), (size_t)L::kAlloc, stream, ma, mb, ep, ws, counters, K, a_tiles,
+                full, tail_splits, units, error_word());
+}
 
 // Persistent CTAs of the stream-K decode GEMM.  Latency model fitted on B200 (µs): a
 // CTA streams its share of the weights at ~80 GB/s; tiles shared by nc CTAs add ~1 µs
@@ -1536,6 +1815,16 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
       choose_tail_split(a_tiles * b_tiles, k_tiles, 8, &full, &tail_splits);
     }
     const CUtensorMap ma = make_kmajor_map(a.x, a.M, a.K, a.ldx, kBM);
+    if (prefill_mode() >= 3 && a.force_splits <= 0) {
+      if (prefill_mode() == 4 && a.N % 256 == 0) {
+        const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, 256);
+        launch_persistent<256, 4>(ma, mb, ep, a.K, a_tiles, a.N / 256, stream);
+      } else {
+        const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, BN);
+        launch_persistent<128, 6>(ma, mb, ep, a.K, a_tiles, b_tiles, stream);
+      }
+      return;
+    }
     const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, BN);
     if (prefill_stages() == 3)   // two CTAs per SM: one's epilogue overlaps the other's main loop
       launch_gemm<BN, 3, false>(ma, mb, ep, a.K, a_tiles, b_tiles, full, tail_splits, stream);

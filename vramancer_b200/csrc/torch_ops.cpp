@@ -1144,6 +1144,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("top_k"), py::arg("top_p"), py::arg("seed"), py::arg("steps"), py::arg("kmax"), py::arg("out"));
   m.def("sample", &sample, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"),
         py::arg("seed"), py::arg("steps"), py::arg("out"));
+  m.def("gemm_set_prefill_mode", [](int64_t mode) { vrm::gemm_set_prefill_mode((int)mode); });
   m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {
     vrm::gemm_set_trace(buf.has_value() && buf->defined() ? buf->data_ptr() : nullptr);
   });

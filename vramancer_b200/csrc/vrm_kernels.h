@@ -76,6 +76,9 @@ struct ARPush {
   uint32_t* done = nullptr;              // zeroed completion counter of this rank
   unsigned long long spin_limit = 0;     // 0: the library default
 };
+// Prefill (M > 128) GEMM kernel choice: 0 tiled, 1 stream-K, 2 stream-K 256-token
+// tiles, 3 persistent, 4 persistent 256-wide (VRM_GEMM_PREFILL sets the start value).
+void gemm_set_prefill_mode(int mode);
 void gemm_bf16(const GemmArgs& a, cudaStream_t stream);
 // FP8 W8A8: x, w are e4m3 bytes ([M, K], [N, K], strides in bytes); y = (x w^T) *
 // scale_x[m] * scale_w[n] (+ bias / residual / silu_mul as gemm_bf16).  K % 128 == 0.
