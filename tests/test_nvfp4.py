@@ -203,3 +203,48 @@ def test_nvfp4_weight_prefill_linear(epi, cuda_errors_clean):
     torch.cuda.synchronize()
     err = (out.float().cpu() - y).abs().max().item()
     assert err <= 2e-2 * y.abs().max().item() + 2e-2, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 7, 16, 33, 100, 128])
+@pytest.mark.parametrize("N,K", [(256, 512), (1280, 5120), (512, 13824)])
+@pytest.mark.parametrize("epi", ["none", "bias_residual", "silu_mul"])
+def test_nvfp4_tc_decode_gemm(M, N, K, epi, cuda_errors_clean):
+    """tcgen05 W4A16 decode GEMM (codes x block scales -> f16 tiles in shared memory)
+    against fp32 math on the dequantised weight and the f16-rounded activations."""
+    from vramancer_b200 import ops
+    from vramancer_b200.quant import nvfp4 as nv
+    g = torch.Generator().manual_seed(M * 31 + N + K)
+    w = (torch.randn(N, K, generator=g) * 0.02).bfloat16()
+    x = torch.randn(M, K, generator=g).bfloat16()
+    qw = nv.quantize(w.cuda())
+    assert qw.q_rows is not None
+    wd = nv.dequantize_ref(qw)
+    y = x.half().float() @ wd.t()
+    kw = {}
+    epilogue = ops.EPI_NONE
+    if epi == "bias_residual":
+        b = (torch.randn(N, generator=g) * 0.1).bfloat16()
+        r = torch.randn(M, N, generator=g).bfloat16()
+        kw = dict(bias=b.cuda(), residual=r.cuda())
+        y = y + b.float() + r.float()
+    elif epi == "silu_mul":
+        epilogue = ops.EPI_SILU_MUL
+        gg, u = y[:, 0::2], y[:, 1::2]
+        y = gg * torch.sigmoid(gg) * u
+    n_out = N // 2 if epi == "silu_mul" else N
+    out = torch.empty(M, n_out, dtype=torch.bfloat16, device="cuda")
+    ops.native().nvfp4_tc_gemm_out(x.cuda(), qw.q_rows, qw.s_atoms, qw.gs, kw.get("bias"), out, epilogue,
+                                   kw.get("residual"))
+    torch.cuda.synchronize()
+    err = (out.float().cpu() - y).abs()
+    tol = 2e-2 * y.abs().max().item() + 1e-2
+    assert err.max().item() <= tol, (err.max().item(), tol)
+    # the linear dispatch with the tcgen05 decode kernel selected gives the same bits
+    old = nv.DECODE_KERNEL
+    nv.DECODE_KERNEL = "tc"
+    try:
+        out2 = qw.linear(x.cuda(), kw.get("bias"), epilogue=epilogue, residual=kw.get("residual"))
+    finally:
+        nv.DECODE_KERNEL = old
+    assert torch.equal(out2, out)

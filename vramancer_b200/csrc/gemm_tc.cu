@@ -732,6 +732,314 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // =====================================================================================
+// NVFP4 W4A16 decode GEMM on tcgen05 (swap-AB: 128 weight rows = MMA M, the M <= 128
+// tokens = MMA N).  Weights stay 4-bit in HBM: per 128-K stage the producer brings the
+// tile's e2m1 codes (row-major [N, K/2] bytes, TMA, 8 KB), its two 512-byte e4m3 scale
+// atoms (128 rows x 4 blocks each, bulk copy) and the activation tile (bf16, 128-byte
+// swizzle).  Warps 2-5 turn each stage into MMA operands: codes x block scale -> f16
+// (exact: an e2m1 value times an e4m3 scale has at most 6 significant bits and lies in
+// f16's normal range) into a 128-byte-swizzled K-major tile, and the activations to f16
+// in place (saturating, like the warp-MMA W4A16 kernel); warp 1 issues kind::f16 MMAs
+// from it.  The 4-bit stream keeps 8-9 KB of weights per stage, so a deep ring (3-8
+// stages) keeps HBM busy; two converted tiles let conversion run one stage ahead of the
+// MMAs.  Grid = weight tiles x K-splits; the last split of a tile sums the partials in
+// split order (deterministic); the per-tensor scale multiplies the sum.
+constexpr int kW4KT = 128;                          // K per stage
+constexpr int kW4Atom = 512;                        // one scale atom: 128 rows x 4 blocks of 16
+template <int BN, int RS>
+struct W4Smem {
+  static constexpr int kXBytes = BN * kW4KT * 2;    // activations: two 128-byte-swizzled halves
+  static constexpr int kQBytes = kBM * kW4KT / 2;   // 8 KB of codes
+  static constexpr int kSfBytes = 2 * kW4Atom;
+  static constexpr int kStage = kXBytes + kQBytes + kSfBytes;   // a multiple of 1024
+  static constexpr int kConv = kBM * kW4KT * 2;     // 32 KB f16 weight tile (two halves)
+  static constexpr int kConvOff = RS * kStage;
+  static constexpr int kBarOff = kConvOff + 2 * kConv;
+  // raw_full[RS], raw_empty[RS], conv_full[2], conv_empty[2], tmem_full; tmem slot, flag
+  static constexpr int kTotal = kBarOff + (2 * RS + 5) * 8 + 16;
+  static constexpr int kAlloc = kTotal + 1024;
+  static_assert(kStage % 1024 == 0, "stages must keep the 1024-byte swizzle alignment");
+};
+
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N) {
+  return (1u << 4)                       // D format f32 (A, B format 0 = f16)
+         | ((uint32_t)(N >> 3) << 17)    // N / 8
+         | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// 4 bytes of e2m1 codes (8 values, low nibble first) -> 4 x f16x2
+__device__ __forceinline__ void w4_e2m1x8_to_f16(uint32_t w, uint32_t (&h)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+}
+__device__ __forceinline__ uint32_t w4_hmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t w4_e4m3x2_to_f16x2(uint16_t v) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
+  return r;
+}
+__device__ __forceinline__ uint32_t w4_bf16x2_to_f16x2_sat(uint32_t v) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(bf16_hi(v)), "f"(bf16_lo(v)));
+  return r;
+}
+__device__ __forceinline__ void fence_proxy_async_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <int BN, int RS>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    nvfp4_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_x,
+                    const uint8_t* __restrict__ sf_atoms, const float* __restrict__ gs, EpiParams ep,
+                    float* __restrict__ workspace, uint32_t* __restrict__ tile_counters, int k_tiles, int splits,
+                    uint32_t* __restrict__ err) {
+  using L = W4Smem<BN, RS>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* raw_empty = raw_full + RS;
+  uint64_t* conv_full = raw_empty + RS;
+  uint64_t* conv_empty = conv_full + 2;
+  uint64_t* tmem_full = conv_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  uint32_t* flag_slot = tmem_slot + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x / splits, split = blockIdx.x % splits;
+  const int per = (k_tiles + splits - 1) / splits;
+  const int kb = split * per, ke = min(k_tiles, kb + per);
+  const int n = max(0, ke - kb);
+  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+
+  pdl_launch();
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_x);
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 128 + 1);   // the converters read it, the MMAs read its activations
+    }
+    for (int c = 0; c < 2; ++c) {
+      mbar_init(&conv_full[c], 128);
+      mbar_init(&conv_empty[c], 1);
+    }
+    mbar_init(tmem_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- producer: weights first (they do not depend on the previous kernel)
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    const int pre = n < RS ? n : RS;
+    const uint8_t* sf_tile = sf_atoms + (size_t)tile * (size_t)(k_tiles * 2) * kW4Atom;
+    for (int g = 0; g < pre; ++g) {
+      uint8_t* st = smem + g * L::kStage;
+      const int kt = kb + g;
+      mbar_arrive_expect_tx(&raw_full[g], L::kStage);
+      tma_load_2d(st + L::kXBytes, &map_q, &raw_full[g], kt * (kW4KT / 2), tile * kBM, pol_w);
+      bulk_g2s(st + L::kXBytes + L::kQBytes, sf_tile + (size_t)kt * 2 * kW4Atom, 2 * kW4Atom, &raw_full[g]);
+    }
+    pdl_wait();
+    for (int g = 0; g < pre; ++g) {
+      uint8_t* st = smem + g * L::kStage;
+      const int kt = kb + g;
+      tma_load_2d(st, &map_x, &raw_full[g], kt * kW4KT, 0, pol_x);
+      tma_load_2d(st + BN * 128, &map_x, &raw_full[g], kt * kW4KT + 64, 0, pol_x);
+    }
+    int issued = pre;
+    for (int g = pre; g < n; ++g) {
+      const int s = g % RS;
+      if (!mbar_wait(&raw_empty[s], ((g / RS) & 1) ^ 1, err)) break;
+      uint8_t* st = smem + s * L::kStage;
+      const int kt = kb + g;
+      mbar_arrive_expect_tx(&raw_full[s], L::kStage);
+      tma_load_2d(st + L::kXBytes, &map_q, &raw_full[s], kt * (kW4KT / 2), tile * kBM, pol_w);
+      bulk_g2s(st + L::kXBytes + L::kQBytes, sf_tile + (size_t)kt * 2 * kW4Atom, 2 * kW4Atom, &raw_full[s]);
+      tma_load_2d(st, &map_x, &raw_full[s], kt * kW4KT, 0, pol_x);
+      tma_load_2d(st + BN * 128, &map_x, &raw_full[s], kt * kW4KT + 64, 0, pol_x);
+      issued = g + 1;
+    }
+    const int first = issued > RS ? issued - RS : 0;
+    for (int j = first; j < issued; ++j) mbar_wait(&raw_full[j % RS], (j / RS) & 1, err);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    constexpr uint32_t idesc = make_idesc_f16(kBM, BN);
+    for (int i = 0; i < n; ++i) {
+      const int s = i % RS, c = i & 1;
+      if (!mbar_wait(&conv_full[c], (i >> 1) & 1, err)) break;
+      tc_fence_after();
+      const uint32_t xa = smem_u32(smem + s * L::kStage);
+      const uint32_t ca = smem_u32(smem + L::kConvOff + c * L::kConv);
+#pragma unroll
+      for (int kk = 0; kk < kW4KT / kUmmaK; ++kk) {
+        const int h = kk >> 2;   // 64-K half: its own 128-byte swizzle atom
+        const uint64_t da = make_sw128_desc(ca + h * (kBM * 128)) + (uint64_t)((kk & 3) * 2);
+        const uint64_t db = make_sw128_desc(xa + h * (BN * 128)) + (uint64_t)((kk & 3) * 2);
+        umma_f16(tmem_base, da, db, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(&raw_empty[s]);
+      umma_commit(&conv_empty[c]);
+    }
+    umma_commit(tmem_full);
+  } else if (warp >= 2) {
+    const int ct = threadIdx.x - 64;   // 0..127
+    // ---------------- converters
+    for (int i = 0; i < n; ++i) {
+      const int s = i % RS, c = i & 1;
+      const bool ok = mbar_wait(&raw_full[s], (i / RS) & 1, err) &&
+                      mbar_wait(&conv_empty[c], ((i >> 1) & 1) ^ 1, err);
+      uint8_t* st = smem + s * L::kStage;
+      uint8_t* cv = smem + L::kConvOff + c * L::kConv;
+      if (ok) {
+        // activations -> f16 in place (position-independent: the swizzle is unchanged)
+        for (int ch = ct; ch < BN * 16; ch += 128) {
+          uint4 v = *reinterpret_cast<const uint4*>(st + ch * 16);
+          v.x = w4_bf16x2_to_f16x2_sat(v.x);
+          v.y = w4_bf16x2_to_f16x2_sat(v.y);
+          v.z = w4_bf16x2_to_f16x2_sat(v.z);
+          v.w = w4_bf16x2_to_f16x2_sat(v.w);
+          *reinterpret_cast<uint4*>(st + ch * 16) = v;
+        }
+        // weights: item (row r, 16-byte code chunk qc) = 32 values of blocks 2 qc, 2 qc + 1;
+        // a warp's 32 items are 8 whole rows (512 contiguous bytes)
+        const uint8_t* q = st + L::kXBytes;
+        const uint8_t* sf = q + L::kQBytes;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int item = ct + 128 * j;
+          const int r = item >> 2, qc = item & 3;
+          const uint4 codes = *reinterpret_cast<const uint4*>(q + r * 64 + qc * 16);
+          const int h = qc >> 1;
+          const uint16_t sc2 =
+              *reinterpret_cast<const uint16_t*>(sf + h * kW4Atom + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (qc & 1) * 2);
+          const uint32_t sh = w4_e4m3x2_to_f16x2(sc2);          // (scale of block 2 qc, of 2 qc + 1)
+          const uint32_t s_lo = __byte_perm(sh, 0, 0x1010), s_hi = __byte_perm(sh, 0, 0x3232);
+          const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
+          uint8_t* rowbase = cv + h * (kBM * 128) + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint32_t hh[4];
+            w4_e2m1x8_to_f16(words[u], hh);
+            const uint32_t sc = u < 2 ? s_lo : s_hi;
+            uint4 o;
+            o.x = w4_hmul2(hh[0], sc);
+            o.y = w4_hmul2(hh[1], sc);
+            o.z = w4_hmul2(hh[2], sc);
+            o.w = w4_hmul2(hh[3], sc);
+            const int c8 = (qc & 1) * 4 + u;   // 16-byte chunk (8 K) of the 128-byte row
+            *reinterpret_cast<uint4*>(rowbase + ((c8 ^ (r & 7)) << 4)) = o;
+          }
+        }
+      }
+      fence_proxy_async_cta();   // generic-proxy writes -> visible to the tensor core / TMA
+      mbar_arrive(&conv_full[c]);
+      mbar_arrive(&raw_empty[s]);
+      if (!ok) break;
+    }
+    // ---------------- epilogue (one TMEM lane = one weight row each)
+    const int lane_base = 32 * (warp & 3);
+    const int row = lane_base + lane;
+    pdl_wait();
+    const bool ok = mbar_wait(tmem_full, 0, err);
+    tc_fence_after();
+    const float g = gs ? *gs : 1.f;
+    const int r_glob = tile * kBM + row;
+    const uint32_t t_row = tmem_base + ((uint32_t)lane_base << 16);
+    const bool direct = splits == 1;
+    auto slot = [&](int sp) { return workspace + (((size_t)tile * splits + sp) * kBM + row) * (size_t)BN; };
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t r[16];
+      tmem_ld_32x32b_x16(t_row + c0, r);
+      tmem_wait_ld();
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] = (ok && n > 0) ? __uint_as_float(r[j]) : 0.f;
+      if (direct) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] *= g;
+        epi_store<true>(ep, r_glob, c0, v);
+      } else {
+        float4* dst = reinterpret_cast<float4*>(slot(split) + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) __stcg(dst + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+      }
+    }
+    if (!direct) {
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        const uint32_t prev = atomicAdd(&tile_counters[tile], 1u);
+        *flag_slot = (prev == (uint32_t)(splits - 1)) ? 1u : 0u;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (*flag_slot) {
+        __threadfence();
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0.f;
+          for (int s0 = 0; s0 < splits; s0 += 4) {
+            float4 x[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float4* src = reinterpret_cast<const float4*>(slot(s0 + u) + c0);
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                x[u][q] = s0 + u < splits ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                v[4 * q] += x[u][q].x;
+                v[4 * q + 1] += x[u][q].y;
+                v[4 * q + 2] += x[u][q].z;
+                v[4 * q + 3] += x[u][q].w;
+              }
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] *= g;
+          epi_store<true>(ep, r_glob, c0, v);
+        }
+        if (threadIdx.x == 64) tile_counters[tile] = 0u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// =====================================================================================
 // Stream-K decode GEMM (swap-AB): one persistent CTA per SM.  The iteration space
 // tiles x k_tiles (tile = 128 weight rows, k_tile = 64 K elements) is cut into equal
 // contiguous ranges, one per CTA, so every SM streams the same number of weight bytes
@@ -1839,6 +2147,76 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
 // TMA as bf16 pairs, so one K-tile is still a 128-byte swizzle row (128 elements) and
 // every address, box and descriptor step is the bf16 one; the epilogue scales by
 // scale_w[n] * scale_x[m].  Any M: token blocks of 128 beyond the first.
+// ---------------------------------------------------------------- NVFP4 W4A16 decode (tcgen05)
+// uint8 [rows, cols] row-major, box 64 bytes x 128 rows, no swizzle (the converters read
+// whole 16-byte chunks of a row)
+static CUtensorMap make_u8_rows_map(const void* ptr, int64_t rows, int64_t cols) {
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {(cuuint32_t)(kW4KT / 2), (cuuint32_t)kBM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_tensor_map()(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box,
+                                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  VRM_REQUIRE(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (nvfp4 codes) failed (code " + std::to_string((int)r) + ")");
+  return map;
+}
+
+template <int BN, int RS>
+static void launch_nvfp4_tc(const CUtensorMap& mq, const CUtensorMap& mx, const uint8_t* sf, const float* gs,
+                            const EpiParams& ep, int a_tiles, int k_tiles, int splits, cudaStream_t stream) {
+  using L = W4Smem<BN, RS>;
+  auto kern = nvfp4_tc_kernel<BN, RS>;
+  static int attr_dev_mask = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_dev_mask & (1 << (dev & 31)))) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
+    attr_dev_mask |= 1 << (dev & 31);
+  }
+  float* ws = nullptr;
+  uint32_t* counters = nullptr;
+  if (splits > 1) {
+    ws = static_cast<float*>(workspace_get((size_t)a_tiles * splits * kBM * BN * sizeof(float), stream));
+    VRM_REQUIRE((size_t)a_tiles <= 32768, "too many split-K tiles");
+    counters = tile_counters_get(stream);
+  }
+  launch_kernel(kern, dim3(a_tiles * splits), dim3(kGemmThreads), (size_t)L::kAlloc, stream, mq, mx, sf, gs, ep, ws,
+                counters, k_tiles, splits, error_word());
+}
+
+void nvfp4_tc_gemm(const Nvfp4TcArgs& a, cudaStream_t stream) {
+  VRM_REQUIRE(a.M >= 1 && a.M <= 128, "nvfp4 tcgen05 decode gemm: 1 <= M <= 128");
+  VRM_REQUIRE(a.N % kBM == 0 && a.K % kW4KT == 0, "nvfp4 tcgen05 decode gemm: N % 128 and K % 128");
+  VRM_REQUIRE(a.ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(a.q_rows) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.sf) & 15) == 0,
+              "nvfp4 tcgen05 decode gemm: 16-byte aligned operands");
+  VRM_REQUIRE(a.epilogue != kEpiSiluMul || (a.N % 2 == 0 && a.residual == nullptr), "nvfp4 gemm: silu_mul epilogue");
+  EpiParams ep;
+  ep.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  ep.ldo = (int)a.ldo;
+  ep.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  ep.residual = reinterpret_cast<const __nv_bfloat16*>(a.residual);
+  ep.M = a.M;
+  ep.N = a.N;
+  ep.epilogue = a.epilogue;
+  ep.scale_w = nullptr;
+  ep.scale_x = nullptr;
+  const int a_tiles = a.N / kBM, k_tiles = a.K / kW4KT;
+  int splits, ktps;
+  choose_split(a_tiles, k_tiles, 2, &splits, &ktps);
+  const int BN = a.M <= 16 ? 16 : a.M <= 32 ? 32 : a.M <= 64 ? 64 : 128;
+  const CUtensorMap mq = make_u8_rows_map(a.q_rows, a.N, a.K / 2);
+  const CUtensorMap mx = make_kmajor_map(a.x, a.M, a.K, a.ldx, BN);
+  switch (BN) {
+    case 16: launch_nvfp4_tc<16, 8>(mq, mx, a.sf, a.gs, ep, a_tiles, k_tiles, splits, stream); break;
+    case 32: launch_nvfp4_tc<32, 7>(mq, mx, a.sf, a.gs, ep, a_tiles, k_tiles, splits, stream); break;
+    case 64: launch_nvfp4_tc<64, 5>(mq, mx, a.sf, a.gs, ep, a_tiles, k_tiles, splits, stream); break;
+    default: launch_nvfp4_tc<128, 3>(mq, mx, a.sf, a.gs, ep, a_tiles, k_tiles, splits, stream); break;
+  }
+}
+
 void gemm_fp8(const GemmArgs& a, const float* scale_x, const float* scale_w, cudaStream_t stream) {
   VRM_REQUIRE(a.K % 128 == 0 && a.ldx % 16 == 0 && a.ldw % 16 == 0, "gemm fp8: K % 128, row strides % 16 bytes");
   VRM_REQUIRE((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15) == 0,

@@ -572,6 +572,49 @@ Tensor nvfp4_dequantize(const Tensor& q, const Tensor& sc, const Tensor& gs, int
   return out;
 }
 
+// W4A16 decode on tcgen05 over the block-scaled layout (q_rows [N, K/2], scale atoms)
+void nvfp4_tc_gemm_out(const Tensor& x, const Tensor& q_rows, const Tensor& sf, const Tensor& gs, const OptT& bias,
+                       Tensor& out, int64_t epilogue, const OptT& residual) {
+  check_bf16_2d(x, "nvfp4_tc x");
+  check_bf16_2d(out, "nvfp4_tc out");
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(q_rows.is_cuda() && q_rows.scalar_type() == torch::kUInt8 && q_rows.is_contiguous() &&
+                  q_rows.dim() == 2 && q_rows.size(1) * 2 == K, "nvfp4_tc: q_rows must be uint8 [N, K/2]");
+  const int64_t N = q_rows.size(0);
+  TORCH_CHECK(sf.scalar_type() == torch::kUInt8 && sf.is_contiguous() && sf.numel() >= N * K / 16,
+              "nvfp4_tc: scale atoms");
+  TORCH_CHECK(gs.scalar_type() == torch::kFloat32 && gs.numel() >= 1, "nvfp4_tc: fp32 gs");
+  same_device(x, {&q_rows, &sf, &gs, &out}, "nvfp4_tc_gemm");
+  same_device_opt(x, {&bias, &residual}, "nvfp4_tc_gemm");
+  const int64_t n_out = epilogue == vrm::kEpiSiluMul ? N / 2 : N;
+  TORCH_CHECK(out.size(0) == M && out.size(1) == n_out, "nvfp4_tc: out must be [", M, ", ", n_out, "]");
+  vrm::Nvfp4TcArgs a;
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.q_rows = q_rows.data_ptr<uint8_t>();
+  a.sf = sf.data_ptr<uint8_t>();
+  a.gs = gs.data_ptr<float>();
+  if (has(bias)) {
+    TORCH_CHECK(bias->scalar_type() == torch::kBFloat16 && bias->is_contiguous() && bias->numel() == N,
+                "nvfp4_tc: bias must be contiguous bf16 [N]");
+    a.bias = bias->data_ptr();
+  }
+  if (has(residual)) {
+    check_bf16_2d(*residual, "nvfp4_tc residual");
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N && residual->stride(0) == out.stride(0),
+                "nvfp4_tc: residual must match out");
+    a.residual = residual->data_ptr();
+  }
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.epilogue = (int)epilogue;
+  const c10::cuda::CUDAGuard guard(x.device());
+  vrm::nvfp4_tc_gemm(a, cur_stream());
+}
+
 void nvfp4_gemm_out(const Tensor& x, const Tensor& q, const Tensor& sc, const Tensor& gs, int64_t N,
                     const OptT& bias, Tensor& out, int64_t epilogue, const OptT& residual) {
   check_bf16_2d(x, "nvfp4_gemm x");
@@ -1151,6 +1194,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_quantize", &nvfp4_quantize, py::arg("w"), py::arg("gs"),
         "bf16 [N, K] -> (q, s) NVFP4 bytes in fragment order, per-tensor scale gs on the device");
   m.def("nvfp4_dequantize", &nvfp4_dequantize, py::arg("q"), py::arg("s"), py::arg("gs"), py::arg("N"), py::arg("K"));
+  m.def("nvfp4_tc_gemm_out", &nvfp4_tc_gemm_out, py::arg("x"), py::arg("q_rows"), py::arg("sf"), py::arg("gs"),
+        py::arg("bias"), py::arg("out"), py::arg("epilogue"), py::arg("residual"));
   m.def("nvfp4_gemm_out", &nvfp4_gemm_out, py::arg("x"), py::arg("q"), py::arg("s"), py::arg("gs"), py::arg("N"),
         py::arg("bias"), py::arg("out"), py::arg("epilogue"), py::arg("residual"),
         "W4A16 decode GEMM (M <= 32) over NVFP4 weights");

@@ -291,6 +291,23 @@ struct Nvfp4GemmArgs {
   ARPush ar;
 };
 void nvfp4_gemm(const Nvfp4GemmArgs& a, cudaStream_t stream);
+// W4A16 decode GEMM on tcgen05 (M <= 128) over the block-scaled layout of nvfp4_bs.cu:
+// codes uint8 [N, K/2] row-major, e4m3 scale atoms (128 rows x 4 blocks of 16), fp32
+// per-tensor scale.  N % 128 == 0, K % 128 == 0.  Epilogues as gemm_bf16.
+struct Nvfp4TcArgs {
+  const void* x = nullptr;      // bf16 [M, K]
+  int64_t ldx = 0;
+  const uint8_t* q_rows = nullptr;
+  const uint8_t* sf = nullptr;
+  const float* gs = nullptr;
+  const void* bias = nullptr;
+  const void* residual = nullptr;
+  void* out = nullptr;
+  int64_t ldo = 0;
+  int M = 0, N = 0, K = 0;
+  int epilogue = kEpiNone;
+};
+void nvfp4_tc_gemm(const Nvfp4TcArgs& a, cudaStream_t stream);
 int nvfp4_gemm_max_m();
 
 // ---------------------------------------------------------------- TurboQuant records (turboquant.cu)

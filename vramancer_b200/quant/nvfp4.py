@@ -34,6 +34,11 @@ _BOUNDS = (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0)
 QUANTIZED_KEYS = ("qkv_w", "o_w", "gate_up_w", "down_w", "fc_w", "proj_w")
 
 
+# Decode GEMM kernel (M <= 128 tokens): "mma" = warp-MMA W4A16 over fragment-order codes,
+# "tc" = tcgen05 W4A16 over the block-scaled copy (VRM_NVFP4_DECODE)
+DECODE_KERNEL = os.environ.get("VRM_NVFP4_DECODE", "mma")
+
+
 @dataclass
 class NVFP4Weight:
     q: torch.Tensor      # uint8 [N * K / 2], fragment order
@@ -74,6 +79,15 @@ class NVFP4Weight:
 
     def linear(self, x: torch.Tensor, bias: Optional[torch.Tensor] = None, *, out: Optional[torch.Tensor] = None,
                epilogue: int = ops.EPI_NONE, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if (x.is_cuda and x.shape[0] <= 128 and self.q_rows is not None and DECODE_KERNEL == "tc"
+                and self.N % 128 == 0 and x.dtype == torch.bfloat16):
+            # decode: W4A16 on tcgen05 (codes dequantised to f16 tiles in shared memory)
+            if out is None:
+                n = self.N // 2 if epilogue == ops.EPI_SILU_MUL else self.N
+                out = torch.empty(x.shape[0], n, dtype=x.dtype, device=x.device)
+            ops.native().nvfp4_tc_gemm_out(x.contiguous(), self.q_rows, self.s_atoms, self.gs, bias, out, epilogue,
+                                           residual)
+            return out
         if x.is_cuda and x.shape[0] <= 32:
             # decode: W4A16, bandwidth-bound (fragment-order codes, warp-level MMAs)
             if out is None:
