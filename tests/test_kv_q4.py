@@ -225,20 +225,24 @@ def test_q4_paged_prefill_gpu(D, Hq, KH, cuda_errors_clean):
 
 @pytest.mark.gpu
 def test_q4_engine_gpu(cuda_errors_clean):
-    """A bf16 model over a four-bit pool on the GPU (CUDA graphs, fused decode write):
-    greedy tokens of a short run agree with the same model over a bf16 pool on most
-    positions, and the pool is 5/16 of the bf16 pool's bytes."""
+    """A bf16 model over a four-bit pool on the GPU: generation runs through the CUDA
+    graphs with the fused decode write, the pool is 5/16 of the bf16 pool's bytes, and
+    the logits after a 70-token context stay close to those over a bf16 pool (random
+    weights give near-flat logits, so greedy tokens are not compared)."""
+    from vramancer_b200.engine.speculative import _full_logits
     cfg = PRESETS["tiny-qwen2-d128"]
     w = random_weights(cfg, device=DEV, dtype=torch.bfloat16, seed=3, std=0.02)
     g = torch.Generator().manual_seed(9)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (9, 40, 70)]
-    outs, sizes = [], []
+    sizes, logits = [], []
     for kv in ("bf16", "q4"):
         llm = LLM(cfg, device=DEV, dtype=torch.bfloat16, kv_cache_dtype=kv, weights=w, max_batch=4,
                   max_model_len=256, kv_pages=64)
-        outs.append([r.output_ids for r in llm.generate(prompts, SamplingParams(max_tokens=12))])
+        reqs = llm.generate(prompts, SamplingParams(max_tokens=12))
+        assert [len(r.output_ids) for r in reqs] == [12, 12, 12]
         sizes.append(llm.pool.nbytes())
+        logits.append(_full_logits(llm, prompts[2])[0].float().cpu())
         del llm
     assert sizes[1] * 16 == sizes[0] * 5
-    same = sum(a == b for x, y in zip(*outs) for a, b in zip(x, y))
-    assert same >= 0.75 * sum(len(x) for x in outs[0]), outs
+    cos = torch.nn.functional.cosine_similarity(logits[0], logits[1], dim=0).item()
+    assert cos >= 0.98, cos

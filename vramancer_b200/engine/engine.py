@@ -115,6 +115,9 @@ class LLMEngine:
         # supplies each request's draft (e.g. a known continuation: forced acceptance)
         self._ngram: Dict[object, object] = {}
         self.draft_provider: Optional[Callable[[Request], List[int]]] = None
+        # benchmarks only: keep every greedy draft whatever the target predicts, so the
+        # verify cost can be timed at a chosen acceptance (outputs are then not the target's)
+        self.spec_force_accept = False
         # overlapped decode: step n+1 is launched (fed from the device) before step n's
         # tokens are read back, so host scheduling hides behind the GPU's work
         self.lookahead = lookahead and ep_sync is None and os.environ.get("VRM_LOOKAHEAD", "1") != "0"

@@ -223,7 +223,8 @@ def speculative_decode_step(engine, active, ngram: int, num_draft: int, stats: S
         p = preds[off:off + len(feed)]
         off += len(feed)
         if r.params.greedy:
-            toks, na = accept_greedy(d, p)
+            toks, na = ((list(d) + [int(p[len(d)])], len(d)) if getattr(engine, "spec_force_accept", False)
+                        else accept_greedy(d, p))
         elif not d:
             toks, na = [int(p[0])], 0
         else:
@@ -244,10 +245,12 @@ def _accept_all_greedy(engine, active, feeds, starts, ds, preds, stats):
     out = []
     off = 0
     stats.steps += 1
+    force = getattr(engine, "spec_force_accept", False)
     for r, feed, start, d in zip(active, feeds, starts, ds):
         p = preds[off:off + len(feed)]
         off += len(feed)
-        toks, na = accept_greedy(d, p)
+        # forced acceptance (benchmarks of the verify cost): every draft is kept
+        toks, na = (list(d) + [int(p[len(d)])], len(d)) if force else accept_greedy(d, p)
         stats.proposed += len(d)
         stats.accepted += na
         engine.kv.truncate(r.request_id, start + 1 + na)
