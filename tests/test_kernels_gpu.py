@@ -396,6 +396,36 @@ def test_paged_prefill(D, Hq, KH, fp8, cuda_errors_clean):
     _close(out, ref, rtol=3e-2, atol=3e-2)
 
 
+@pytest.mark.parametrize("D,Hq,KH", [(128, 40, 8), (128, 16, 16), (64, 12, 4)])
+def test_paged_prefill_tc_matches_warp_mma(D, Hq, KH, cuda_errors_clean):
+    """The tcgen05 prefill kernel (bf16 pages) against the fp32 reference and the
+    warp-MMA kernel: multi-block causal rows, chunked prefill behind a cached prefix,
+    partial tiles and pages, GQA groups."""
+    specs = [(300, 300), (1, 700), (129, 129), (200, 1000), (64, 64), (513, 600)]
+    L, layer = 2, 1
+    cache, bt, _ = _make_cache([s[1] for s in specs], L, KH, D, torch.bfloat16, layer, seed=D + Hq)
+    cu = [0]
+    for ql, _ in specs:
+        cu.append(cu[-1] + ql)
+    q = torch.randn(cu[-1], (Hq + 2 * KH) * D).bfloat16()      # q rows of a qkv buffer (strided)
+    cu_q = torch.tensor(cu, dtype=torch.int32)
+    cl = torch.tensor([s[1] for s in specs], dtype=torch.int32)
+    sm = 1.0 / math.sqrt(D)
+    mq = max(s[0] for s in specs)
+    ref = ops.paged_attention_prefill(q, cache, layer, bt, cu_q, cl, None, sm, Hq, mq)
+    args = (q.to(DEV), cache.to(DEV), layer, bt.to(DEV), cu_q.to(DEV), cl.to(DEV), None, sm, Hq, mq)
+    nat = ops.native()
+    nat.set_prefill_tc(True)
+    tc = ops.paged_attention_prefill(*args)
+    nat.set_prefill_tc(False)
+    try:
+        mma = ops.paged_attention_prefill(*args)
+    finally:
+        nat.set_prefill_tc(True)
+    _close(tc, ref, rtol=3e-2, atol=3e-2)
+    _close(tc, mma, rtol=3e-2, atol=3e-2)
+
+
 # ------------------------------------------------------------------------- elementwise + sampling
 def test_elementwise(cuda_errors_clean):
     torch.manual_seed(3)

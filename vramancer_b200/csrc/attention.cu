@@ -1130,6 +1130,318 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
   }
 }
 
+// ============================================================== prefill on tcgen05
+// Causal paged prefill with the 5th-generation tensor cores, bf16 pages.  One CTA per
+// (128-query tile, query head, sequence); keys in blocks of 128 (8 pages).
+//   warp 0      TMA: the Q tile once, then each block's K and V page chunks (16 rows x 64
+//               dims boxes, 128-byte swizzle) into a 2-stage ring
+//   warp 1      MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers (128 cols),
+//               then O_j = P_j V_j into one of two TMEM output buffers (D cols), V read
+//               as an MN-major operand straight from its TMA layout
+//   warps 2-5   one query row per thread (its TMEM lane): scores -> online softmax ->
+//               P_j (bf16, K-major, 128-byte swizzle) in shared memory; then O_j from
+//               TMEM into a register accumulator rescaled by the running max
+// S_{j+1} runs on the tensor cores while the softmax of block j runs, and O_j while the
+// softmax of block j+1 runs.  Query tiles are taken last-first (the diagonal-heavy
+// tiles start first).  The mma.sync kernel above stays for fp8 / four-bit pages.
+template <int D>
+struct PrefillTcSmem {
+  static constexpr int kQ = 128 * D * 2;             // Q tile [128, D] (D/64 swizzle columns)
+  static constexpr int kP = 128 * 128 * 2;           // P tile [128 q, 128 keys]
+  static constexpr int kKV = 128 * D * 2;            // one K (or V) block [128 keys, D]
+  static constexpr int kStages = 2;
+  static constexpr int kPOff = kQ;
+  static constexpr int kKVOff = kPOff + 2 * kP;
+  static constexpr int kBarOff = kKVOff + kStages * 2 * kKV;
+  // q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2]
+  static constexpr int kTotal = kBarOff + 16 * 8 + 16;
+  static constexpr int kAlloc = kTotal + 1024;
+  static constexpr uint32_t kTmemCols = 512;         // S x 2 (256) + O x 2 (2 D <= 256)
+};
+
+struct PrefillTcParams {
+  const int* block_tables;
+  int bt_stride;
+  const int* cu_q;
+  const int* context_lens;
+  int layer, num_layers, KH, G, Hq;
+  float sm_scale;
+  __nv_bfloat16* out;
+  int64_t ld_o;
+  int max_tiles;
+  long long num_pages;
+  uint32_t* err;
+};
+
+// MN-major operand, 128-byte swizzle: 64-element (128 B) MN blocks lbo bytes apart,
+// 8-row K groups sbo bytes apart
+__device__ __forceinline__ uint64_t make_mn_sw128_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+template <int D>
+__global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                   const __grid_constant__ CUtensorMap kvmap,
+                                                                   PrefillTcParams P) {
+  using S = PrefillTcSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 3;
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_empty = bars + 7;
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_full = bars + 11;
+  uint64_t* o_empty = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int q_start = P.cu_q[b];
+  const int q_len = P.cu_q[b + 1] - q_start;
+  const int ntiles = (q_len + 127) / 128;
+  const int qt = ntiles - 1 - (int)blockIdx.x;   // the longest (diagonal-heavy) tiles first
+  if (qt < 0) return;
+  const int q0 = qt * 128;
+  const int ctx = P.context_lens[b];
+  const int prefix = ctx - q_len;
+  const int kvh = h / P.G;
+  const int kv_end = min(ctx, prefix + q0 + 128);
+  const int nblk = (kv_end + 127) / 128;
+  const int npages = (ctx + kPage - 1) / kPage;
+  const int* bt = P.block_tables + (size_t)b * P.bt_stride;
+
+  pdl_launch();
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&qmap);
+    tma_prefetch_desc(&kvmap);
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_o = tmem + 256;   // S[2] at columns 0 / 128, O[2] at 256 / 256 + D
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- producer
+    const uint64_t pol = policy_evict_normal();
+    pdl_wait();   // q and this chunk's K / V come from the previous kernel
+    mbar_arrive_expect_tx(q_full, S::kQ);
+#pragma unroll
+    for (int hh = 0; hh < D / 64; ++hh)
+      tma_load_2d(smem + hh * (128 * 128), &qmap, q_full, h * D + hh * 64, q_start + q0, pol);
+    for (int j = 0; j < nblk; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1, P.err)) break;
+      uint8_t* kb = smem + S::kKVOff + st * 2 * S::kKV;
+      uint8_t* vb = kb + S::kKV;
+      mbar_arrive_expect_tx(&kv_full[st], 2 * S::kKV);
+#pragma unroll 1
+      for (int pg = 0; pg < 8; ++pg) {
+        const int pl = j * 8 + pg;
+        int page = bt[pl < npages ? pl : npages - 1];   // past the context: any valid page (masked)
+        if (!in_bounds(page, P.num_pages, P.err)) page = 0;
+        const int row = (((page * P.num_layers + P.layer) * 2 + 0) * P.KH + kvh) * kPage;
+        const int vrow = row + P.KH * kPage;
+#pragma unroll
+        for (int hh = 0; hh < D / 64; ++hh) {
+          tma_load_2d(kb + hh * (128 * 128) + pg * (kPage * 128), &kvmap, &kv_full[st], hh * 64, row, pol);
+          tma_load_2d(vb + hh * (128 * 128) + pg * (kPage * 128), &kvmap, &kv_full[st], hh * 64, vrow, pol);
+        }
+      }
+    }
+    // drain: none of our copies may be in flight at exit
+    mbar_wait(q_full, 0, P.err);
+    const int first = nblk > 2 ? nblk - 2 : 0;
+    for (int j = first; j < nblk; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, P.err);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, 128);
+    constexpr uint32_t idesc_o = make_idesc_bf16(128, D) | (1u << 16);   // B (V) MN-major
+    const uint32_t q_addr = smem_u32(smem);
+    bool failed = !mbar_wait(q_full, 0, P.err);
+    auto issue_s = [&](int j) {
+      const int st = j & 1;
+      if (!mbar_wait(&kv_full[st], (j >> 1) & 1, P.err) || !mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1, P.err)) {
+        failed = true;
+        return;
+      }
+      tc_fence_after();
+      const uint32_t kb = smem_u32(smem + S::kKVOff + st * 2 * S::kKV);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int hh = kk >> 2;
+        const uint64_t da = make_sw128_desc(q_addr + hh * (128 * 128)) + (uint64_t)((kk & 3) * 2);
+        const uint64_t db = make_sw128_desc(kb + hh * (128 * 128)) + (uint64_t)((kk & 3) * 2);
+        umma_f16(t_s + st * 128, da, db, idesc_s, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(&s_full[st]);
+    };
+    if (!failed && nblk > 0) issue_s(0);
+    for (int j = 0; j < nblk && !failed; ++j) {
+      if (j + 1 < nblk) issue_s(j + 1);
+      if (failed) break;
+      const int st = j & 1;
+      if (!mbar_wait(&p_full[st], (j >> 1) & 1, P.err) || !mbar_wait(&o_empty[st], ((j >> 1) & 1) ^ 1, P.err)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t pa = smem_u32(smem + S::kPOff + st * S::kP);
+      const uint32_t vb = smem_u32(smem + S::kKVOff + st * 2 * S::kKV + S::kKV);
+#pragma unroll
+      for (int kk = 0; kk < 128 / 16; ++kk) {
+        const uint64_t da = make_sw128_desc(pa + (kk >> 2) * (128 * 128)) + (uint64_t)((kk & 3) * 2);
+        const uint64_t db = make_mn_sw128_desc(vb + kk * (16 * 128), 128 * 128, 1024);
+        umma_f16(t_o + st * D, da, db, idesc_o, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(&o_full[st]);
+      umma_commit(&kv_empty[st]);   // K_j (read by S_j, issued earlier) and V_j are consumed
+    }
+  } else if (warp >= 2) {
+    // ---------------- softmax + output accumulation (row = TMEM lane)
+    const int lb = 32 * (warp & 3);
+    const int r = lb + lane;
+    const uint32_t lane_off = (uint32_t)lb << 16;
+    const int qpos = prefix + q0 + r;
+    const float sl2 = P.sm_scale * 1.4426950408889634f;
+    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
+    float o[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) o[d] = 0.f;
+    bool ok = true;
+    // accumulate O_j (TMEM) into the registers: o = o * alpha + O_j
+    auto take_o = [&](int j, float alpha) {
+      const int st = j & 1;
+      if (!mbar_wait(&o_full[st], (j >> 1) & 1, P.err)) ok = false;
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(t_o + st * D + lane_off + c0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) o[c0 + t] = o[c0 + t] * alpha + (ok ? __uint_as_float(v[t]) : 0.f);
+      }
+      tc_fence_before();
+      mbar_arrive(&o_empty[st]);
+    };
+    for (int j = 0; j < nblk; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(&s_full[st], (j >> 1) & 1, P.err)) ok = false;
+      tc_fence_after();
+      const uint32_t srow = t_s + st * 128 + lane_off;
+      const int key0 = j * 128;
+      const bool need_mask = key0 + 127 > qpos || key0 + 128 > ctx;
+      // pass 1: block max of the scaled, masked scores
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c0 = 0; c0 < 128; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(srow + c0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const int key = key0 + c0 + t;
+          float x = __uint_as_float(v[t]) * sl2;
+          if (need_mask && (key > qpos || key >= ctx)) x = -INFINITY;
+          mx = fmaxf(mx, x);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m_run - m_new);
+      // pass 2: P = exp2(s - m_new) -> bf16 K-major swizzled rows; row sum
+      uint8_t* prow = smem + S::kPOff + st * S::kP + (r >> 3) * 1024 + (r & 7) * 128;
+      float sum = 0.f;
+#pragma unroll
+      for (int c0 = 0; c0 < 128; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(srow + c0, v);
+        tmem_wait_ld();
+        float pv[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const int key = key0 + c0 + t;
+          float x = __uint_as_float(v[t]) * sl2;
+          if (need_mask && (key > qpos || key >= ctx)) x = -INFINITY;
+          pv[t] = (m_new == -INFINITY || !ok) ? 0.f : exp2f(x - m_new);
+          sum += pv[t];
+        }
+        // keys c0 .. c0 + 15: 64-key half c0 / 64, 16-byte chunks (c0 % 64) / 8 and + 1
+        uint8_t* half = prow + (c0 >> 6) * (128 * 128);
+        const int ch = (c0 & 63) >> 3;
+        uint4 w0, w1;
+        w0.x = pack_bf16x2(pv[0], pv[1]);
+        w0.y = pack_bf16x2(pv[2], pv[3]);
+        w0.z = pack_bf16x2(pv[4], pv[5]);
+        w0.w = pack_bf16x2(pv[6], pv[7]);
+        w1.x = pack_bf16x2(pv[8], pv[9]);
+        w1.y = pack_bf16x2(pv[10], pv[11]);
+        w1.z = pack_bf16x2(pv[12], pv[13]);
+        w1.w = pack_bf16x2(pv[14], pv[15]);
+        *reinterpret_cast<uint4*>(half + ((ch ^ (r & 7)) << 4)) = w0;
+        *reinterpret_cast<uint4*>(half + (((ch + 1) ^ (r & 7)) << 4)) = w1;
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[st]);          // the scores are read: the slot takes S_{j+2}
+      fence_proxy_async_smem();           // P written by this thread -> visible to the MMA
+      mbar_arrive(&p_full[st]);
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
+      // O_{j-1} (finished while this block's softmax ran) into the accumulator
+      if (j > 0) take_o(j - 1, alpha_prev);
+      alpha_prev = alpha;
+    }
+    if (nblk > 0) take_o(nblk - 1, alpha_prev);
+    // O_j is relative to the running max after block j; taking it with that block's
+    // alpha keeps the accumulator (and l_run) relative to the final running max
+    if (q0 + r < q_len && ok) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* orow = P.out + (size_t)(q_start + q0 + r) * P.ld_o + (size_t)h * D;
+#pragma unroll
+      for (int d = 0; d < D; d += 8) {
+        uint4 w;
+        w.x = pack_bf16x2(o[d] * inv, o[d + 1] * inv);
+        w.y = pack_bf16x2(o[d + 2] * inv, o[d + 3] * inv);
+        w.z = pack_bf16x2(o[d + 4] * inv, o[d + 5] * inv);
+        w.w = pack_bf16x2(o[d + 6] * inv, o[d + 7] * inv);
+        *reinterpret_cast<uint4*>(orow + d) = w;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, S::kTmemCols);
+  }
+}
+
 // ============================================================== host
 static int cache_format(bool fp8, bool q4) { return q4 ? kFmtQ4 : fp8 ? kFmtFp8 : kFmtBf16; }
 
@@ -1316,6 +1628,33 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   }
 }
 
+// tcgen05 prefill for bf16 pages (VRM_PREFILL_TC=0 or set_prefill_tc(false) keeps the
+// warp-MMA kernel)
+static int g_prefill_tc = -1;
+void set_prefill_tc(bool on) { g_prefill_tc = on ? 1 : 0; }
+static bool prefill_tc_enabled() {
+  if (g_prefill_tc < 0) {
+    const char* e = std::getenv("VRM_PREFILL_TC");
+    g_prefill_tc = (e && e[0] == '0') ? 0 : 1;
+  }
+  return g_prefill_tc == 1;
+}
+
+template <int D>
+static void launch_prefill_tc(const CUtensorMap& qm, const CUtensorMap& kv, const PrefillTcParams& p, dim3 grid,
+                              cudaStream_t st) {
+  constexpr int smem = PrefillTcSmem<D>::kAlloc;
+  auto kern = paged_prefill_tc_kernel<D>;
+  static bool set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!set[dev & 63]) {
+    VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set[dev & 63] = true;
+  }
+  launch_kernel(kern, grid, dim3(192), (size_t)smem, st, qm, kv, p);
+}
+
 template <int D, int FMT>
 static void launch_prefill(dim3 grid, const PrefillParams& p, cudaStream_t st) {
   constexpr int smem = PrefillSmem<D, FMT>::kTotal;
@@ -1355,8 +1694,35 @@ void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
   p.ld_o = a.ld_o;
   p.num_pages = a.cache_pages;
   p.err = error_word();
-  dim3 grid((a.max_q_len + 63) / 64, a.Hq, a.B);
+  const int64_t pool_rows = a.cache_pages * a.num_layers * 2 * a.KH * kPage;
   const int fmt = cache_format(a.cache_fp8, a.cache_q4);
+  if (fmt == kFmtBf16 && prefill_tc_enabled() && a.cache_pages > 0 && a.num_tokens > 0 &&
+      pool_rows < (int64_t)INT32_MAX && a.num_tokens < (int64_t)INT32_MAX &&
+      (reinterpret_cast<uintptr_t>(a.cache) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0) {
+    PrefillTcParams t;
+    t.block_tables = a.block_tables;
+    t.bt_stride = a.bt_stride;
+    t.cu_q = a.cu_q;
+    t.context_lens = a.context_lens;
+    t.layer = a.layer;
+    t.num_layers = a.num_layers;
+    t.KH = a.KH;
+    t.G = a.Hq / a.KH;
+    t.Hq = a.Hq;
+    t.sm_scale = a.sm_scale;
+    t.out = p.out;
+    t.ld_o = a.ld_o;
+    t.max_tiles = (a.max_q_len + 127) / 128;
+    t.num_pages = a.cache_pages;
+    t.err = p.err;
+    const CUtensorMap kv = make_kmajor_map(a.cache, pool_rows, a.D, a.D, kPage);
+    const CUtensorMap qm = make_kmajor_map(a.q, a.num_tokens, (int64_t)a.Hq * a.D, a.ld_q, 128);
+    const dim3 grid(t.max_tiles, a.Hq, a.B);
+    if (a.D == 128) launch_prefill_tc<128>(qm, kv, t, grid, st);
+    else launch_prefill_tc<64>(qm, kv, t, grid, st);
+    return;
+  }
+  dim3 grid((a.max_q_len + 63) / 64, a.Hq, a.B);
   if (a.D == 128) {
     if (fmt == kFmtFp8) launch_prefill<128, kFmtFp8>(grid, p, st);
     else if (fmt == kFmtQ4) launch_prefill<128, kFmtQ4>(grid, p, st);

@@ -340,6 +340,7 @@ void attn_prefill(const Tensor& q, const Tensor& cache, int64_t layer, const Ten
   a.cache_fp8 = is_fp8_cache(cache);
   a.cache_q4 = is_q4_cache(cache);
   a.cache_pages = cache.size(0);
+  a.num_tokens = q.size(0);
   a.num_layers = (int)cache.size(1);
   a.layer = (int)layer;
   a.KH = (int)cache.size(3);
@@ -1187,6 +1188,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("top_k"), py::arg("top_p"), py::arg("seed"), py::arg("steps"), py::arg("kmax"), py::arg("out"));
   m.def("sample", &sample, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"),
         py::arg("seed"), py::arg("steps"), py::arg("out"));
+  m.def("set_prefill_tc", [](bool on) { vrm::set_prefill_tc(on); });
   m.def("gemm_set_prefill_mode", [](int64_t mode) { vrm::gemm_set_prefill_mode((int)mode); });
   m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {
     vrm::gemm_set_trace(buf.has_value() && buf->defined() ? buf->data_ptr() : nullptr);

@@ -400,8 +400,11 @@ struct PrefillAttnArgs {
   int64_t ld_o = 0;
   int B = 0, max_q_len = 0;
   int64_t cache_pages = 0;             // pool pages (checked in bounds-check builds)
+  int64_t num_tokens = 0;              // rows of q (> 0 enables the tcgen05 kernel for bf16 pages)
 };
 void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t stream);
+// Selects the tcgen05 prefill kernel for bf16 pages (default on, VRM_PREFILL_TC=0 off).
+void set_prefill_tc(bool on);
 
 // ---------------------------------------------------------------- sampling (sampling.cu)
 void argmax_rows(const void* logits, int64_t ld, int B, int V, int* out, cudaStream_t stream);
