@@ -1986,8 +1986,10 @@ static int streamk_ctas(int tiles, int k_tiles, int BN, double weight_bytes) {
     const bool aligned = ctas % tiles == 0 && nc <= 8 && nc <= k_tiles;
     if (ctas > tiles || nc > 1) {
       // global fixup: the owner sums partials from L2, two per round; cluster fixup
-      // (aligned splits): from its peers' shared memory, four per round
-      t += (aligned && cluster_on) ? 0.5 + 0.25 * ((nc - 1 + 3) / 4) * (BN / 16)
+      // (aligned splits): from its peers' shared memory, four per round.  Refitted on
+      // B200: at K = 640 (10 k-tiles) two-CTA clusters lost to whole tiles (8.5 vs 7.5 us
+      // at M = 32, N = 5120), at K = 5120 / 1728 they won (11.7 vs 13.3, 10.3 vs 11.3 us)
+      t += (aligned && cluster_on) ? 0.9 + 0.3 * ((nc - 1 + 3) / 4) * (BN / 16)
                                    : 1.0 + 0.6 * ((nc - 1 + 3) / 4) * (BN / 16);
     }
     return t;
@@ -2123,6 +2125,17 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
       choose_tail_split(a_tiles * b_tiles, k_tiles, 8, &full, &tail_splits);
     }
     const CUtensorMap ma = make_kmajor_map(a.x, a.M, a.K, a.ldx, kBM);
+    // default (mode 0): the persistent kernel with 256-wide weight tiles for GEMMs of many
+    // tiles with a long K or a wide N -- measured on B200 at M = 4096 (Qwen2.5-14B):
+    // gate/up 27648 x 5120 1356 vs 1105 TFLOP/s, down 5120 x 13824 1199 vs 938; at M = 512
+    // and for the narrower projections the tiled kernel stays ahead
+    const bool auto_persist = prefill_mode() == 0 && a.force_splits <= 0 && a.N % 256 == 0 && a.M >= 2048 &&
+                              (a.K >= 8192 || a.N >= 16384);
+    if (auto_persist) {
+      const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, 256);
+      launch_persistent<256, 4>(ma, mb, ep, a.K, a_tiles, a.N / 256, stream);
+      return;
+    }
     if (prefill_mode() >= 3 && a.force_splits <= 0) {
       if (prefill_mode() == 4 && a.N % 256 == 0) {
         const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, 256);
