@@ -109,6 +109,91 @@ __device__ __forceinline__ void convert_q4_tile(const uint8_t* raw, uint8_t* dst
   }
 }
 
+// ---- f16 operand path of the fp8 / four-bit decode kernels.  Their K fragments are
+// built straight from the stored rows in registers (no shared-memory tile), their V
+// tile is converted to f16 (exact for e4m3; one FMA per value for four-bit), and the
+// MMAs run f16 x f16 -> f32.
+__device__ __forceinline__ void mma_f16_m16n8k16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t v) { return pack_f16x2(bf16_lo(v), bf16_hi(v)); }
+__device__ __forceinline__ uint32_t fp8x2_to_f16x2(uint16_t v) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(v, __NV_E4M3);
+  return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+// one code byte (element 2i low nibble, 2i+1 high) -> f16x2 of code * s + m: 1024 + code is
+// an exact f16 (the nibble in the mantissa), 1024 is subtracted exactly, then one FMA
+__device__ __forceinline__ uint32_t q4_byte_to_f16x2(uint32_t byte, uint32_t s2, uint32_t m2) {
+  const uint32_t x = 0x64006400u | (byte & 0xFu) | ((byte & 0xF0u) << 12);
+  uint32_t y, r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(y) : "r"(x), "r"(0x64006400u));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(y), "r"(s2), "r"(m2));
+  return r;
+}
+// 16-byte chunk of a stored fp8 K row: swizzled so the fragment gathers of the eight
+// rows g of a warp hit different banks
+template <int D>
+__device__ __forceinline__ uint32_t f8_kchunk(int r, int ch) {
+  return (uint32_t)(r * D + ((ch ^ (D == 128 ? (r & 7) : ((r >> 1) & 3))) << 4));
+}
+
+// fp8 rows -> swizzled f16 tile (V operand)
+template <int D>
+__device__ __forceinline__ void convert_fp8_tile_f16(const uint8_t* raw, uint8_t* dst, int rows, int tid, int nthr) {
+  constexpr int kChunks = D / 16;
+  for (int i = tid; i < rows * kChunks; i += nthr) {
+    const int r = i / kChunks, c = i % kChunks;
+    const uint4 v = *reinterpret_cast<const uint4*>(raw + r * D + c * 16);
+    const uint16_t* p = reinterpret_cast<const uint16_t*>(&v);
+    uint4 o0, o1;
+    o0.x = fp8x2_to_f16x2(p[0]);
+    o0.y = fp8x2_to_f16x2(p[1]);
+    o0.z = fp8x2_to_f16x2(p[2]);
+    o0.w = fp8x2_to_f16x2(p[3]);
+    o1.x = fp8x2_to_f16x2(p[4]);
+    o1.y = fp8x2_to_f16x2(p[5]);
+    o1.z = fp8x2_to_f16x2(p[6]);
+    o1.w = fp8x2_to_f16x2(p[7]);
+    *reinterpret_cast<uint4*>(dst + swz<D * 2>(r, 2 * c)) = o0;
+    *reinterpret_cast<uint4*>(dst + swz<D * 2>(r, 2 * c + 1)) = o1;
+  }
+}
+
+// four-bit rows -> swizzled f16 tile (V operand): one thread per (row, 32-dim group)
+template <int D>
+__device__ __forceinline__ void convert_q4_tile_f16(const uint8_t* raw, uint8_t* dst, int rows, int tid, int nthr) {
+  constexpr int kRowB = PageRow<D, kFmtQ4>::kBytes;
+  constexpr int kGroups = D / 32;
+  for (int i = tid; i < rows * kGroups; i += nthr) {
+    const int r = i / kGroups, gi = i % kGroups;
+    const uint8_t* row = raw + r * kRowB;
+    const uint2 v0 = *reinterpret_cast<const uint2*>(row + gi * 16);
+    const uint2 v1 = *reinterpret_cast<const uint2*>(row + gi * 16 + 8);
+    const uint32_t sm = *reinterpret_cast<const uint32_t*>(row + D / 2 + gi * 4);   // {scale, min} f16
+    const uint32_t s2 = __byte_perm(sm, 0, 0x1010), m2 = __byte_perm(sm, 0, 0x3232);
+    const uint32_t w[4] = {v0.x, v0.y, v1.x, v1.y};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint4 o;
+      o.x = q4_byte_to_f16x2(w[c] & 0xFFu, s2, m2);
+      o.y = q4_byte_to_f16x2((w[c] >> 8) & 0xFFu, s2, m2);
+      o.z = q4_byte_to_f16x2((w[c] >> 16) & 0xFFu, s2, m2);
+      o.w = q4_byte_to_f16x2(w[c] >> 24, s2, m2);
+      *reinterpret_cast<uint4*>(dst + swz<D * 2>(r, gi * 4 + c)) = o;
+    }
+  }
+}
+
 // ============================================================== decode
 template <int D, int FMT>
 struct DecodeSmem {
@@ -261,10 +346,11 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
     constexpr int kTotalChunks = S::kRawB / 16;
 #pragma unroll
     for (int i = lane; i < kTotalChunks; i += 32) {
-      // bf16 pages land swizzled for ldmatrix; fp8 / four-bit pages land as stored and
-      // are converted into a swizzled bf16 tile after the wait
+      // bf16 pages land swizzled for ldmatrix; fp8 K rows with a chunk swizzle for the
+      // register gathers; other fp8 / four-bit rows as stored
       const uint32_t off = FMT == kFmtBf16 ? swz<ROWB>(i / kChunkPerRow, i % kChunkPerRow) : (uint32_t)(i * 16);
-      cp_async16(dk + off, kp + (size_t)i * 16, true);
+      const uint32_t koff = FMT == kFmtFp8 ? f8_kchunk<D>(i / (D / 16), i % (D / 16)) : off;
+      cp_async16(dk + koff, kp + (size_t)i * 16, true);
       cp_async16(dv + off, vp + (size_t)i * 16, true);
     }
   };
@@ -325,6 +411,15 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
     }
   }
 
+  if constexpr (FMT != kFmtBf16) {
+    // fp8 / four-bit pages run f16 MMAs: Q as f16 (saturating)
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      qb[kk][0] = bf16x2_to_f16x2(qb[kk][0]);
+      qb[kk][1] = bf16x2_to_f16x2(qb[kk][1]);
+    }
+  }
+
   // O^T accumulators: tile mt covers dims [16 mt, 16 mt + 16); this thread holds
   // (dim 16 mt + g, heads 2c, 2c+1) in [0], [1] and (dim 16 mt + g + 8, same heads) in [2], [3]
   float o[D / 16][4];
@@ -343,30 +438,60 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
     uint8_t* kt = wbase + stage * S::kStageB;
     uint8_t* vt = kt + S::kRawB;
     if constexpr (FMT != kFmtBf16) {
-      uint8_t* ck = wbase + 2 * S::kStageB;
-      uint8_t* cv = ck + S::kTileB;
-      if constexpr (FMT == kFmtFp8) {
-        convert_fp8_tile<D>(kt, ck, kPage, lane, 32);
-        convert_fp8_tile<D>(vt, cv, kPage, lane, 32);
-      } else {
-        convert_q4_tile<D>(kt, ck, kPage, lane, 32);
-        convert_q4_tile<D>(vt, cv, kPage, lane, 32);
-      }
+      // V -> swizzled f16 tile (K is read from its stored rows below)
+      uint8_t* cv = wbase + 2 * S::kStageB + S::kTileB;
+      if constexpr (FMT == kFmtFp8) convert_fp8_tile_f16<D>(vt, cv, kPage, lane, 32);
+      else convert_q4_tile_f16<D>(vt, cv, kPage, lane, 32);
       __syncwarp();
-      kt = ck;
       vt = cv;
     }
     const uint32_t kaddr = smem_u32(kt), vaddr = smem_u32(vt);
 
     // S^T = K Q^T: A = the page's K rows (tokens) x 16 dims, four 8x8 matrices
     float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (FMT == kFmtBf16) {
 #pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-      const int ch = 2 * kk + (lane >> 4);
-      uint32_t a0, a1, a2, a3;
-      ldsm_x4(kaddr + swz<ROWB>(row, ch), a0, a1, a2, a3);
-      mma_bf16_16816(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int ch = 2 * kk + (lane >> 4);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(kaddr + swz<ROWB>(row, ch), a0, a1, a2, a3);
+        mma_bf16_16816(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      }
+    } else if constexpr (FMT == kFmtFp8) {
+      // fragment (row g / g + 8, dims 16 kk + 2c (+ 8)): two e4m3 bytes each, exact in f16
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint8_t* r0 = kt + f8_kchunk<D>(g, kk) + 2 * c;
+        const uint8_t* r1 = kt + f8_kchunk<D>(g + 8, kk) + 2 * c;
+        const uint32_t a0 = fp8x2_to_f16x2(*reinterpret_cast<const uint16_t*>(r0));
+        const uint32_t a1 = fp8x2_to_f16x2(*reinterpret_cast<const uint16_t*>(r1));
+        const uint32_t a2 = fp8x2_to_f16x2(*reinterpret_cast<const uint16_t*>(r0 + 8));
+        const uint32_t a3 = fp8x2_to_f16x2(*reinterpret_cast<const uint16_t*>(r1 + 8));
+        mma_f16_m16n8k16(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      }
+    } else {
+      // four-bit: the fragment's dims 2c, 2c + 1 are one code byte; scale / min per
+      // 32-dim group of rows g and g + 8
+      constexpr int kRowB = PageRow<D, kFmtQ4>::kBytes;
+      const uint8_t* r0 = kt + g * kRowB;
+      const uint8_t* r1 = kt + (g + 8) * kRowB;
+#pragma unroll
+      for (int gi = 0; gi < D / 32; ++gi) {
+        const uint32_t sm0 = *reinterpret_cast<const uint32_t*>(r0 + D / 2 + gi * 4);
+        const uint32_t sm1 = *reinterpret_cast<const uint32_t*>(r1 + D / 2 + gi * 4);
+        const uint32_t s0 = __byte_perm(sm0, 0, 0x1010), m0 = __byte_perm(sm0, 0, 0x3232);
+        const uint32_t s1 = __byte_perm(sm1, 0, 0x1010), m1 = __byte_perm(sm1, 0, 0x3232);
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int kk = 2 * gi + h2;
+          const uint32_t a0 = q4_byte_to_f16x2(r0[8 * kk + c], s0, m0);
+          const uint32_t a1 = q4_byte_to_f16x2(r1[8 * kk + c], s1, m1);
+          const uint32_t a2 = q4_byte_to_f16x2(r0[8 * kk + c + 4], s0, m0);
+          const uint32_t a3 = q4_byte_to_f16x2(r1[8 * kk + c + 4], s1, m1);
+          mma_f16_m16n8k16(sc, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+        }
+      }
     }
     // sc[0] = (token g, head 2c), [1] = (g, 2c+1), [2] = (g+8, 2c), [3] = (g+8, 2c+1)
     const int tok0 = p * kPage;
@@ -405,10 +530,15 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
       o[mt][2] *= alpha[0];
       o[mt][3] *= alpha[1];
     }
-    // P^T as the B operand (k = tokens, n = heads): transpose the two 8x8 bf16 blocks
+    // P^T as the B operand (k = tokens, n = heads): transpose the two 8x8 16-bit blocks
     uint32_t pb0, pb1;
-    movmatrix_trans(pack_bf16x2(pr[0], pr[1]), pb0);
-    movmatrix_trans(pack_bf16x2(pr[2], pr[3]), pb1);
+    if constexpr (FMT == kFmtBf16) {
+      movmatrix_trans(pack_bf16x2(pr[0], pr[1]), pb0);
+      movmatrix_trans(pack_bf16x2(pr[2], pr[3]), pb1);
+    } else {
+      movmatrix_trans(pack_f16x2(pr[0], pr[1]), pb0);
+      movmatrix_trans(pack_f16x2(pr[2], pr[3]), pb1);
+    }
     // O^T += V^T P^T: A = V^T (dims x tokens) from the V tile with transposing loads
 #pragma unroll
     for (int mt = 0; mt < D / 16; ++mt) {
@@ -416,7 +546,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
       const int ch = 2 * mt + ((lane >> 3) & 1);
       uint32_t a0, a1, a2, a3;
       ldsm_x4_t(vaddr + swz<ROWB>(row, ch), a0, a1, a2, a3);
-      mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+      if constexpr (FMT == kFmtBf16) mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+      else mma_f16_m16n8k16(o[mt], a0, a1, a2, a3, pb0, pb1);
     }
     __syncwarp();
   }
