@@ -86,3 +86,128 @@ def test_cuda_round_trip_fp32_input():
     xd = c.decompress(c.compress(x), torch.float32)
     rel = ((xd - x).norm(dim=-1) / x.norm(dim=-1)).mean()
     assert rel < 0.3
+
+
+# ---------------------------------------------------------------- TurboQuant KV pages
+def _tq_pool_case(B=3, KH=2, G=3, L=2, lens=(5, 40, 77), seed=0, device="cpu"):
+    from vramancer_b200.kv.pool import KVPool, KVPoolSpec
+    g = torch.Generator().manual_seed(seed)
+    P = sum((n + 15) // 16 for n in lens) + 2
+    pool = KVPool(KVPoolSpec(P, L, KH, 128, dtype=torch.int8), device=device)
+    perm = torch.randperm(P, generator=g)
+    bt = torch.zeros(B, max((n + 15) // 16 for n in lens), dtype=torch.int32)
+    k = 0
+    slots = []
+    for b, n in enumerate(lens):
+        np_ = (n + 15) // 16
+        bt[b, :np_] = perm[k:k + np_].to(torch.int32)
+        k += np_
+        slots += [int(bt[b, t // 16]) * 16 + t % 16 for t in range(n)]
+    Hq = KH * G
+    qkv = (torch.randn(len(slots), (Hq + 2 * KH) * 128, generator=g) * 2).bfloat16()
+    return pool, bt, torch.tensor(slots, dtype=torch.int32), qkv, Hq, KH
+
+
+def test_tq_pages_cpu_write_and_decode():
+    """Records written into a TurboQuant pool decode (CPU path) to the oracle's attention
+    over the same records, and the pool is a quarter of a bf16 pool."""
+    from vramancer_b200 import ops
+    from vramancer_b200.kv.pool import KVPoolSpec
+    pool, bt, slots, qkv, Hq, KH = _tq_pool_case()
+    assert KVPoolSpec(4, 2, 2, 128, dtype=torch.int8).bytes_per_page * 4 == \
+        KVPoolSpec(4, 2, 2, 128, dtype=torch.bfloat16).bytes_per_page
+    ops.tq_kv_write(qkv, slots, pool.cache, 1, Hq, KH, pool.tq)
+    lens = [5, 40, 77]
+    cl = torch.tensor(lens, dtype=torch.int32)
+    q = (torch.randn(3, Hq * 128) * 2).bfloat16()
+    out = ops.tq_paged_decode(q, pool.cache, 1, bt, cl, pool.tq, 1 / math.sqrt(128), Hq)
+    # oracle: the same math on records gathered per sequence
+    off = 0
+    G = Hq // KH
+    for b, n in enumerate(lens):
+        v = qkv[off:off + n].view(n, Hq + 2 * KH, 128)
+        off += n
+        for h in range(KH):
+            krec = pool.tq.compress(v[:, Hq + h].float())
+            vrec = pool.tq.compress(v[:, Hq + KH + h].float())
+            s = pool.tq.attention_score(q[b, h * G * 128:(h + 1) * G * 128].float().view(G, 128), krec)
+            w = torch.softmax(s / math.sqrt(128), -1)
+            ref = w @ pool.tq.decompress(vrec, torch.float32)
+            assert torch.allclose(out[b, h * G * 128:(h + 1) * G * 128].float().view(G, 128), ref, atol=2e-2,
+                                  rtol=2e-2)
+
+
+def test_tq_engine_cpu():
+    """An engine over a TurboQuant pool generates, and its logits stay near those of an
+    fp32 pool (records are ~4 bits per value)."""
+    from vramancer_b200.engine.engine import SamplingParams
+    from vramancer_b200.engine.speculative import _full_logits
+    from vramancer_b200.llm import LLM
+    from vramancer_b200.models.config import PRESETS
+    from vramancer_b200.models.weights import random_weights
+    cfg = PRESETS["tiny-qwen2-d128"]
+    w = random_weights(cfg, device="cpu", dtype=torch.float32, seed=3, std=0.02)
+    g = torch.Generator().manual_seed(9)
+    seq = torch.randint(0, cfg.vocab_size, (50,), generator=g).tolist()
+    logits = []
+    for kv in ("fp32", "tq"):
+        llm = LLM(cfg, device="cpu", dtype=torch.float32, kv_cache_dtype=kv, weights=w, max_batch=4,
+                  max_model_len=256, kv_pages=64)
+        r = llm.generate([seq[:20]], SamplingParams(max_tokens=6))[0]
+        assert len(r.output_ids) == 6
+        logits.append(_full_logits(llm, seq)[0])
+    cos = torch.nn.functional.cosine_similarity(logits[0], logits[1], dim=0).item()
+    assert cos > 0.9, cos
+
+
+@pytest.mark.gpu
+def test_tq_pages_gpu_match_cpu(cuda_errors_clean):
+    """The CUDA record writer and the decode attention over TurboQuant pages against the
+    CPU path (the oracle): records agree as the compressor test allows, outputs within
+    the estimator's tolerance."""
+    from vramancer_b200 import ops
+    pool_c, bt, slots, qkv, Hq, KH = _tq_pool_case(B=3, KH=4, G=5, lens=(5, 140, 300), seed=4)
+    pool_g, *_ = _tq_pool_case(B=3, KH=4, G=5, lens=(5, 140, 300), seed=4, device="cuda")
+    ops.tq_kv_write(qkv, slots, pool_c.cache, 1, Hq, KH, pool_c.tq)
+    ops.tq_kv_write(qkv.cuda(), slots.cuda(), pool_g.cache, 1, Hq, KH, pool_g.tq)
+    torch.cuda.synchronize()
+    rg = pool_g.cache.cpu().view(torch.uint8)
+    rc = pool_c.cache.view(torch.uint8)
+    ia, ra, _, _ = pool_c.tq._fields(rc.reshape(-1, 64).clone())
+    ib, rb, _, _ = pool_c.tq._fields(rg.reshape(-1, 64).clone())
+    assert (ia == ib).float().mean() > 0.99
+    assert torch.allclose(ra.float(), rb.float(), rtol=1e-3, atol=1e-3)
+    cl = torch.tensor([5, 140, 300], dtype=torch.int32)
+    q = (torch.randn(3, Hq * 128) * 2).bfloat16()
+    ref = ops.tq_paged_decode(q, pool_c.cache, 1, bt, cl, pool_c.tq, 1 / math.sqrt(128), Hq)
+    # the kernel on the oracle's records (same inputs, so only the kernel's arithmetic differs)
+    pool_g.cache.copy_(pool_c.cache.cuda())
+    out = ops.tq_paged_decode(q.cuda(), pool_g.cache, 1, bt.cuda(), cl.cuda(), pool_g.tq, 1 / math.sqrt(128), Hq)
+    torch.cuda.synchronize()
+    err = (out.float().cpu() - ref.float()).abs().max().item()
+    assert err <= 3e-2 * ref.float().abs().max().item() + 2e-2, err
+
+
+@pytest.mark.gpu
+def test_tq_engine_gpu(cuda_errors_clean):
+    """A bf16 model over a TurboQuant pool on the GPU: graph-replayed decode through the
+    record writer and the record attention; logits close to a bf16 pool's."""
+    from vramancer_b200.engine.engine import SamplingParams
+    from vramancer_b200.engine.speculative import _full_logits
+    from vramancer_b200.llm import LLM
+    from vramancer_b200.models.config import PRESETS
+    from vramancer_b200.models.weights import random_weights
+    cfg = PRESETS["tiny-qwen2-d128"]
+    w = random_weights(cfg, device="cuda", dtype=torch.bfloat16, seed=3, std=0.02)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (9, 40, 70)]
+    logits = []
+    for kv in ("bf16", "tq"):
+        llm = LLM(cfg, device="cuda", dtype=torch.bfloat16, kv_cache_dtype=kv, weights=w, max_batch=4,
+                  max_model_len=256, kv_pages=64)
+        reqs = llm.generate(prompts, SamplingParams(max_tokens=12))
+        assert [len(r.output_ids) for r in reqs] == [12, 12, 12]
+        logits.append(_full_logits(llm, prompts[2])[0].float().cpu())
+        del llm
+    cos = torch.nn.functional.cosine_similarity(logits[0], logits[1], dim=0).item()
+    assert cos > 0.9, cos

@@ -1759,14 +1759,15 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   }
 }
 
-// tcgen05 prefill for bf16 pages (VRM_PREFILL_TC=0 or set_prefill_tc(false) keeps the
-// warp-MMA kernel)
+// tcgen05 prefill for bf16 pages: opt-in (VRM_PREFILL_TC=1 or set_prefill_tc(true)).
+// Measured on B200 (40 / 8 heads, D = 128): 160-199 TFLOP/s against 206-234 for the
+// warp-MMA kernel; its four softmax warps (one per TMEM lane quarter) are the bottleneck.
 static int g_prefill_tc = -1;
 void set_prefill_tc(bool on) { g_prefill_tc = on ? 1 : 0; }
 static bool prefill_tc_enabled() {
   if (g_prefill_tc < 0) {
     const char* e = std::getenv("VRM_PREFILL_TC");
-    g_prefill_tc = (e && e[0] == '0') ? 0 : 1;
+    g_prefill_tc = (e && e[0] == '1') ? 1 : 0;
   }
   return g_prefill_tc == 1;
 }

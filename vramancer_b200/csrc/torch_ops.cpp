@@ -700,6 +700,60 @@ Tensor tq_compress(const Tensor& x, const Tensor& signs, const Tensor& jl) {
   return out;
 }
 
+// TurboQuant KV pages: pool int8 [pages, layers, 2, KH, 16, 64] (records as bytes)
+static void check_tq_pool(const Tensor& pool, int64_t layer, const char* what) {
+  TORCH_CHECK(pool.is_cuda() && pool.is_contiguous() && pool.dim() == 6 && pool.size(2) == 2 && pool.size(5) == 64 &&
+                  (pool.scalar_type() == torch::kInt8 || pool.scalar_type() == torch::kUInt8),
+              what, ": TurboQuant pool must be a contiguous int8 [pages, layers, 2, kv_heads, 16, 64] CUDA tensor");
+  TORCH_CHECK(pool.size(4) == 16, what, ": 16-token pages");
+  TORCH_CHECK(layer >= 0 && layer < pool.size(1), what, ": layer out of range");
+}
+static void check_tq_params(const Tensor& signs, const Tensor& jl, const char* what) {
+  TORCH_CHECK(signs.scalar_type() == torch::kFloat32 && signs.is_contiguous() && signs.numel() == 128, what,
+              ": fp32 signs [128]");
+  TORCH_CHECK(jl.scalar_type() == torch::kFloat32 && jl.is_contiguous() && jl.numel() == 64 * 128, what,
+              ": fp32 jl [64, 128]");
+}
+
+void tq_kv_write(const Tensor& qkv, const Tensor& slot_mapping, Tensor& pool, int64_t layer, int64_t Hq, int64_t KH,
+                 const Tensor& signs, const Tensor& jl) {
+  check_bf16_2d(qkv, "tq_kv_write qkv");
+  check_tq_pool(pool, layer, "tq_kv_write");
+  check_tq_params(signs, jl, "tq_kv_write");
+  TORCH_CHECK(pool.size(3) == KH && qkv.size(1) >= (Hq + 2 * KH) * 128 && qkv.stride(0) % 4 == 0,
+              "tq_kv_write: qkv must hold (Hq + 2 KH) heads of 128 dims");
+  TORCH_CHECK(slot_mapping.scalar_type() == torch::kInt32 && slot_mapping.numel() >= qkv.size(0),
+              "tq_kv_write: int32 slot_mapping");
+  same_device(qkv, {&slot_mapping, &pool, &signs, &jl}, "tq_kv_write");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  vrm::tq_kv_write(qkv.data_ptr(), qkv.stride(0), (int)qkv.size(0), (int)Hq, (int)KH, slot_mapping.data_ptr<int>(),
+                   reinterpret_cast<uint8_t*>(pool.data_ptr()), (int)pool.size(1), (int)layer, pool.size(0),
+                   signs.data_ptr<float>(), jl.data_ptr<float>(), cur_stream());
+}
+
+void tq_paged_decode(const Tensor& q, const Tensor& pool, int64_t layer, const Tensor& block_tables,
+                     const Tensor& context_lens, const Tensor& signs, const Tensor& jl, double sm_scale, Tensor& out,
+                     int64_t num_q_heads) {
+  check_tq_pool(pool, layer, "tq_paged_decode");
+  check_tq_params(signs, jl, "tq_paged_decode");
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 2 && q.stride(1) == 1 &&
+                  q.stride(0) % 4 == 0 && q.size(1) >= num_q_heads * 128,
+              "tq_paged_decode: q must be bf16 [B, >= Hq * 128] with unit inner stride");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.dim() == 2 && out.stride(1) == 1 &&
+                  out.size(1) >= num_q_heads * 128 && out.stride(0) % 4 == 0, "tq_paged_decode: out");
+  TORCH_CHECK(block_tables.scalar_type() == torch::kInt32 && block_tables.dim() == 2 && block_tables.stride(1) == 1,
+              "tq_paged_decode: int32 block_tables [B, max_pages]");
+  TORCH_CHECK(context_lens.scalar_type() == torch::kInt32 && context_lens.numel() >= q.size(0),
+              "tq_paged_decode: int32 context_lens");
+  same_device(q, {&pool, &block_tables, &context_lens, &signs, &jl, &out}, "tq_paged_decode");
+  const c10::cuda::CUDAGuard guard(q.device());
+  vrm::tq_paged_decode(q.data_ptr(), q.stride(0), reinterpret_cast<const uint8_t*>(pool.data_ptr()),
+                       (int)pool.size(1), (int)layer, (int)pool.size(3), (int)num_q_heads,
+                       block_tables.data_ptr<int>(), (int)block_tables.stride(0), context_lens.data_ptr<int>(),
+                       (int)q.size(0), signs.data_ptr<float>(), jl.data_ptr<float>(), (float)sm_scale,
+                       out.data_ptr(), out.stride(0), pool.size(0), cur_stream());
+}
+
 Tensor tq_decompress(const Tensor& rec, const Tensor& signs) {
   TORCH_CHECK(rec.is_cuda() && rec.is_contiguous() && rec.scalar_type() == torch::kUInt8 && rec.size(-1) == 64,
               "tq_decompress: contiguous CUDA uint8 [..., 64]");
@@ -1207,6 +1261,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_gemm_max_m", &vrm::nvfp4_gemm_max_m);
   m.def("tq_compress", &tq_compress, py::arg("x"), py::arg("signs"), py::arg("jl"),
         "TurboQuant: [..., 128] -> 64-byte records (Hadamard + PolarQuant + QJL)");
+  m.def("tq_kv_write", &tq_kv_write, py::arg("qkv"), py::arg("slot_mapping"), py::arg("pool"), py::arg("layer"),
+        py::arg("num_q_heads"), py::arg("num_kv_heads"), py::arg("signs"), py::arg("jl"));
+  m.def("tq_paged_decode", &tq_paged_decode, py::arg("q"), py::arg("pool"), py::arg("layer"),
+        py::arg("block_tables"), py::arg("context_lens"), py::arg("signs"), py::arg("jl"), py::arg("sm_scale"),
+        py::arg("out"), py::arg("num_q_heads"));
   m.def("tq_decompress", &tq_decompress, py::arg("rec"), py::arg("signs"),
         "TurboQuant: 64-byte records -> bf16 [..., 128]");
   m.def("set_decode_tma", &vrm::set_decode_tma, py::arg("on"),

@@ -316,6 +316,17 @@ int nvfp4_gemm_max_m();
 void tq_compress(const void* x, bool x_bf16, int64_t n, const float* signs, const float* jl, uint8_t* out,
                  cudaStream_t stream);
 void tq_decompress(const uint8_t* rec, int64_t n, const float* signs, void* out, cudaStream_t stream);
+// TurboQuant KV pages: pool [pages, layers, 2, KH, 16, 64] uint8 records (D = 128).
+// tq_kv_write: the rotated k / v rows of qkv [T, (Hq + 2 KH) * 128] -> records at
+// slot_mapping (< 0 skips).  tq_paged_decode: decode attention scored from the records
+// (asymmetric QJL estimator), values from their polar decodes; out [B, Hq * 128] bf16.
+void tq_kv_write(const void* qkv, int64_t ld, int T, int Hq, int KH, const int* slot_mapping, uint8_t* pool,
+                 int num_layers, int layer, int64_t num_pages, const float* signs, const float* jl,
+                 cudaStream_t stream);
+void tq_paged_decode(const void* q, int64_t ld_q, const uint8_t* pool, int num_layers, int layer, int KH, int Hq,
+                     const int* block_tables, int bt_stride, const int* context_lens, int B, const float* signs,
+                     const float* jl, float sm_scale, void* out, int64_t ld_o, int64_t num_pages,
+                     cudaStream_t stream);
 
 struct RopeKvArgs {
   void* qkv = nullptr;          // bf16 [T, (Hq + 2 KH) * D], rotated in place
@@ -403,7 +414,7 @@ struct PrefillAttnArgs {
   int64_t num_tokens = 0;              // rows of q (> 0 enables the tcgen05 kernel for bf16 pages)
 };
 void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t stream);
-// Selects the tcgen05 prefill kernel for bf16 pages (default on, VRM_PREFILL_TC=0 off).
+// Selects the tcgen05 prefill kernel for bf16 pages (default off, VRM_PREFILL_TC=1 on).
 void set_prefill_tc(bool on);
 
 // ---------------------------------------------------------------- sampling (sampling.cu)

@@ -9,7 +9,8 @@ is what the attention kernels stream.
 
 fp8 pools store e4m3 values with one fp32 scale per (layer, k|v, kv_head).  uint8
 pools store four-bit rows (`kv.q4`): the last dimension is the row's byte count,
-head_dim * 5 / 8, and a page takes 5/16 of the bf16 page's bytes.
+head_dim * 5 / 8, and a page takes 5/16 of the bf16 page's bytes.  int8 pools store
+TurboQuant records (`kv.turboquant`, 64 bytes per 128-dim row, 1/4 of bf16).
 
 Reference parity: the pool tensor of core/paged_attention.py:277-351 (same page
 shape and bytes/page, core/paged_attention.py:107-111).
@@ -34,6 +35,8 @@ def kv_dtype_from_str(s: str) -> torch.dtype:
         return torch.float32
     if s in ("q4", "int4", "4bit", "uint8"):
         return torch.uint8
+    if s in ("tq", "turboquant", "int8"):
+        return torch.int8
     raise ValueError(f"unsupported kv cache dtype {s!r}")
 
 
@@ -52,6 +55,10 @@ class KVPoolSpec:
         if self.dtype == torch.uint8:
             from .q4 import row_bytes
             return row_bytes(self.head_dim)
+        if self.dtype == torch.int8:
+            if self.head_dim != 128:
+                raise ValueError("TurboQuant KV pages need head_dim 128")
+            return 64
         return self.head_dim
 
     @property
@@ -76,6 +83,13 @@ class KVPool:
         # zero-initialised: stale slots past a sequence's length are finite
         self.cache = torch.zeros(shape, dtype=spec.dtype, device=self.device)
         self.is_fp8 = spec.dtype == torch.float8_e4m3fn
+        # TurboQuant pages (int8 pool of 64-byte records): the compressor's rotation signs
+        # and JL matrix on the pool's device
+        self.is_tq = spec.dtype == torch.int8
+        self.tq = None
+        if self.is_tq:
+            from .turboquant import KVCacheCompressor
+            self.tq = KVCacheCompressor(head_dim=128).to(self.device)
         if self.is_fp8:
             if kv_scale is None:
                 kv_scale = torch.ones(spec.num_layers, 2, spec.kv_heads, dtype=torch.float32)

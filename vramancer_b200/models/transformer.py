@@ -99,6 +99,7 @@ class DecoderModel:
         self.kvh = max(1, cfg.num_kv_heads // tps)
         self.D = cfg.head_dim
         self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
+        self._rope_dummy = None      # one-page bf16 pool for RoPE without a KV write (TurboQuant pages)
         self.cos_sin = (ops.rope_cos_sin(cfg.max_position, cfg.rot_dim, cfg.rope_theta, self.device)
                         if cfg.rot_dim > 0 else None)
         # decode attention does RoPE + the KV write itself when rotation covers the whole
@@ -196,6 +197,8 @@ class DecoderModel:
         hq, kvh, D = self.hq, self.kvh, self.D
         qkv = self._in_proj(x, r, self.lw(i, "qkv_w"), self.lw(i, "qkv_b"))
         li = i - self.first_layer
+        if getattr(pool, "is_tq", False):
+            return self._attention_tq(qkv, batch, pool, li)
         if batch.is_decode and self.fused_rope and qkv.is_cuda:
             # RoPE + KV-page write inside the decode attention kernel (one launch fewer)
             return ops.paged_attention_decode(qkv, pool.cache, li, batch.block_tables, batch.context_lens,
@@ -210,6 +213,26 @@ class DecoderModel:
         return ops.paged_attention_prefill(qkv, pool.cache, li, batch.block_tables, batch.cu_q,
                                            batch.context_lens, pool.kv_scale, self.sm_scale, hq,
                                            batch.max_q_len)
+
+    def _attention_tq(self, qkv: torch.Tensor, batch: ForwardBatch, pool: KVPool, li: int) -> torch.Tensor:
+        """Attention over TurboQuant KV pages: RoPE in place, the step's k / v written as
+        records, decode scored from the records; prefill decodes the batch's pages of this
+        layer to bf16 and runs the regular prefill kernel on them."""
+        hq, kvh, D = self.hq, self.kvh, self.D
+        if self._rope_dummy is None:
+            # RoPE without a KV write goes through the same kernel with a one-page bf16 pool
+            self._rope_dummy = torch.zeros(1, 1, 2, kvh, 16, D, dtype=torch.bfloat16, device=qkv.device)
+        ops.rope_kv_write(qkv, batch.positions, self.cos_sin, self._rope_dummy, None, None, 0, hq, kvh, D)
+        ops.tq_kv_write(qkv, batch.slot_mapping, pool.cache, li, hq, kvh, pool.tq)
+        if batch.is_decode:
+            return ops.tq_paged_decode(qkv, pool.cache, li, batch.block_tables, batch.context_lens, pool.tq,
+                                       self.sm_scale, hq)
+        bt = batch.block_tables
+        pages = bt.reshape(-1)
+        mini = ops.tq_decompress_pool(pool.cache, li, pages, pool.tq)
+        bt_mini = torch.arange(pages.numel(), dtype=torch.int32, device=bt.device).view(bt.shape)
+        return ops.paged_attention_prefill(qkv, mini, 0, bt_mini, batch.cu_q, batch.context_lens, None,
+                                           self.sm_scale, hq, batch.max_q_len)
 
     def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor], r: torch.Tensor,
                       nxt: Optional[tuple]) -> Optional[torch.Tensor]:

@@ -202,6 +202,62 @@ def rope_kv_write(qkv: torch.Tensor, positions: Optional[torch.Tensor], cos_sin:
         cache[page, layer, 1, :, off, :] = vv.to(cache.dtype)
 
 
+# --------------------------------------------------------------------------- TurboQuant KV pages
+def tq_kv_write(qkv: torch.Tensor, slot_mapping: torch.Tensor, pool: torch.Tensor, layer: int,
+                num_q_heads: int, num_kv_heads: int, comp) -> None:
+    """The (rotated) k / v rows of qkv [T, (Hq + 2 KH) * 128] as 64-byte TurboQuant records
+    into pool int8 [pages, layers, 2, KH, 16, 64] at slot_mapping (< 0 skips); comp is
+    the pool's kv.turboquant.KVCacheCompressor (rotation signs, JL matrix)."""
+    if qkv.is_cuda:
+        native().tq_kv_write(qkv, slot_mapping, pool, layer, num_q_heads, num_kv_heads, comp.signs, comp.jl)
+        return
+    T = qkv.shape[0]
+    Hq, KH = num_q_heads, num_kv_heads
+    v = qkv.view(T, Hq + 2 * KH, 128)
+    slots = slot_mapping.long()
+    idx = torch.nonzero(slots >= 0).flatten()
+    if idx.numel() == 0:
+        return
+    rec = comp.compress(torch.stack([v[idx, Hq:Hq + KH], v[idx, Hq + KH:]], 1).float())   # [n, 2, KH, 64]
+    pool[slots[idx] // 16, layer, :, :, slots[idx] % 16] = rec.view(torch.int8)
+
+
+def tq_paged_decode(q: torch.Tensor, pool: torch.Tensor, layer: int, block_tables: torch.Tensor,
+                    context_lens: torch.Tensor, comp, sm_scale: float, num_q_heads: int,
+                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode attention scored straight from TurboQuant K records (asymmetric QJL
+    estimator) with values from their polar decodes; q [B, >= Hq * 128] -> [B, Hq * 128]."""
+    B = q.shape[0]
+    if out is None:
+        out = torch.empty(B, num_q_heads * 128, dtype=q.dtype, device=q.device)
+    if q.is_cuda:
+        native().tq_paged_decode(q, pool, layer, block_tables, context_lens, comp.signs, comp.jl, sm_scale, out,
+                                 num_q_heads)
+        return out
+    KH = pool.shape[3]
+    G = num_q_heads // KH
+    for b in range(B):
+        n = int(context_lens[b])
+        pages = block_tables[b, : (n + 15) // 16].long()
+        rec = pool[pages, layer].view(torch.uint8)                      # [P, 2, KH, 16, 64]
+        rec = rec.permute(1, 2, 0, 3, 4).reshape(2, KH, -1, 64)[:, :, :n]
+        qb = q[b, : num_q_heads * 128].float().view(KH, G, 128)
+        for h in range(KH):
+            s = comp.attention_score(qb[h], rec[0, h]) * sm_scale
+            w = torch.softmax(s, dim=-1)
+            vv = comp.decompress(rec[1, h], torch.float32)
+            out[b, h * G * 128:(h + 1) * G * 128] = (w @ vv).reshape(-1).to(out.dtype)
+    return out
+
+
+def tq_decompress_pool(pool: torch.Tensor, layer: int, pages: torch.Tensor, comp) -> torch.Tensor:
+    """bf16 pages [len(pages), 1, 2, KH, 16, 128] decoded from a TurboQuant pool's layer."""
+    rec = pool[pages.long(), layer].contiguous()                          # [n, 2, KH, 16, 64]
+    n, _, KH = rec.shape[0], rec.shape[1], rec.shape[2]
+    dec = comp.decompress(rec.view(torch.uint8).reshape(-1, 64), torch.bfloat16)
+    return dec.view(n, 1, 2, KH, 16, 128)
+
+
 # --------------------------------------------------------------------------- attention
 def cache_head_dim(cache: torch.Tensor) -> int:
     """Head dim of a KV pool [pages, layers, 2, KH, page_size, row] (uint8 = four-bit rows)."""
