@@ -416,12 +416,11 @@ def test_paged_prefill_tc_matches_warp_mma(D, Hq, KH, cuda_errors_clean):
     args = (q.to(DEV), cache.to(DEV), layer, bt.to(DEV), cu_q.to(DEV), cl.to(DEV), None, sm, Hq, mq)
     nat = ops.native()
     nat.set_prefill_tc(True)
-    tc = ops.paged_attention_prefill(*args)
-    nat.set_prefill_tc(False)
     try:
-        mma = ops.paged_attention_prefill(*args)
+        tc = ops.paged_attention_prefill(*args)
     finally:
-        nat.set_prefill_tc(True)
+        nat.set_prefill_tc(False)
+    mma = ops.paged_attention_prefill(*args)
     _close(tc, ref, rtol=3e-2, atol=3e-2)
     _close(tc, mma, rtol=3e-2, atol=3e-2)
 

@@ -185,6 +185,35 @@ def bench_decode_attn(batch, ctx, kv_heads=8, q_heads=40, head_dim=128, layers=4
             "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
 
 
+def bench_tq_decode(batch, ctx, kv_heads=8, q_heads=40, layers=4, iters=50):
+    """Decode attention straight from TurboQuant KV pages (64-byte records per row)."""
+    from ..kv.pool import KVPool, KVPoolSpec
+    from . import tq_kv_write, tq_paged_decode
+    hbm, _, src = peaks()
+    ps, D = 16, 128
+    pages = (ctx + ps - 1) // ps
+    P = batch * pages
+    pool = KVPool(KVPoolSpec(P, layers, kv_heads, D, dtype=torch.int8), device="cuda")
+    bt = torch.arange(P, dtype=torch.int32, device="cuda").view(batch, pages)
+    cl = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    slots = torch.arange(P * ps, dtype=torch.int32, device="cuda")
+    qkv = torch.randn(P * ps, (q_heads + 2 * kv_heads) * D, device="cuda", dtype=torch.bfloat16)
+    for layer in range(layers):
+        tq_kv_write(qkv, slots, pool.cache, layer, q_heads, kv_heads, pool.tq)
+    q = torch.randn(batch, q_heads * D, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    state = [0]
+
+    def fn():
+        tq_paged_decode(q, pool.cache, state[0] % layers, bt, cl, pool.tq, 1 / math.sqrt(D), q_heads, out=out)
+        state[0] += 1
+
+    us = time_it(fn, iters)
+    byts = batch * ctx * kv_heads * 2 * 64
+    return {"kernel": "tq_paged_decode", "batch": batch, "ctx": ctx, "us": round(us, 2),
+            "tb_s": round(byts / us / 1e6, 3), "frac_hbm": round(byts / us / 1e6 / hbm, 3), "peaks": src}
+
+
 def bench_nvfp4_prefill(m, n, k, iters=20):
     """Prefill-sized GEMM three ways: bf16 tcgen05 GEMM, NVFP4 W4A4 block-scaled tcgen05
     GEMM (codes already quantised), and W4A4 including the activation quantisation."""
@@ -395,7 +424,7 @@ QWEN14B_DECODE = [("qkv", 7168, 5120), ("o_proj", 5120, 5120), ("gate_up", 27648
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "nvfp4", "nvfp4-prefill", "fp8", "decode-attn", "all", "trace", "rmsnorm",
-                                     "rope-kv", "prefill-attn", "sample", "turboquant", "act-quant", "others"])
+                                     "rope-kv", "prefill-attn", "sample", "turboquant", "act-quant", "others", "tq-decode"])
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--kv-heads", type=int, default=8)
     ap.add_argument("--q-heads", type=int, default=40)
@@ -439,6 +468,8 @@ def main(argv=None):
     elif a.what == "nvfp4-prefill":
         for n, k in ([(a.n, a.k)] if a.n != 5120 or a.k != 13824 else [(27648, 5120), (5120, 13824), (7168, 5120)]):
             print(json.dumps(bench_nvfp4_prefill(a.m if a.m != 1 else 4096, n, k, a.iters)))
+    elif a.what == "tq-decode":
+        print(json.dumps(bench_tq_decode(a.batch, a.ctx, kv_heads=a.kv_heads, q_heads=a.q_heads, iters=a.iters)))
     elif a.what == "decode-attn":
         print(json.dumps(bench_decode_attn(a.batch, a.ctx, kv_heads=a.kv_heads, q_heads=a.q_heads, fp8=a.fp8,
                                            iters=a.iters, splits=a.splits, fused=a.fused, q4=a.q4)))
