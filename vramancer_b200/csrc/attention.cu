@@ -1269,8 +1269,10 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(PrefillParams P) {
 //   warp 1      MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers (128 cols),
 //               then O_j = P_j V_j into one of two TMEM output buffers (D cols), V read
 //               as an MN-major operand straight from its TMA layout
-//   warps 2-5   one query row per thread (its TMEM lane): scores -> online softmax ->
-//               P_j (bf16, K-major, 128-byte swizzle) in shared memory; then O_j from
+//   warps 2-9   two warps per TMEM lane quarter, one query row per thread, each warp of
+//               a pair owning half the key columns and half the output dims: scores ->
+//               online softmax (row max / sum exchanged within the pair) -> P_j (bf16,
+//               K-major, 128-byte swizzle) in shared memory; then its half of O_j from
 //               TMEM into a register accumulator rescaled by the running max
 // S_{j+1} runs on the tensor cores while the softmax of block j runs, and O_j while the
 // softmax of block j+1 runs.  Query tiles are taken last-first (the diagonal-heavy
@@ -1284,8 +1286,9 @@ struct PrefillTcSmem {
   static constexpr int kPOff = kQ;
   static constexpr int kKVOff = kPOff + 2 * kP;
   static constexpr int kBarOff = kKVOff + kStages * 2 * kKV;
-  // q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2]
-  static constexpr int kTotal = kBarOff + 16 * 8 + 16;
+  // q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2],
+  // tmem slot (16 B), softmax pair exchange [2 halves][128 rows] fp32 (max, then sum)
+  static constexpr int kTotal = kBarOff + 16 * 8 + 16 + 2 * 128 * 4;
   static constexpr int kAlloc = kTotal + 1024;
   static constexpr uint32_t kTmemCols = 512;         // S x 2 (256) + O x 2 (2 D <= 256)
 };
@@ -1317,7 +1320,7 @@ __device__ __forceinline__ uint64_t make_mn_sw128_desc(uint32_t addr, uint32_t l
 }
 
 template <int D>
-__global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                    const __grid_constant__ CUtensorMap kvmap,
                                                                    PrefillTcParams P) {
   using S = PrefillTcSmem<D>;
@@ -1360,10 +1363,10 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(const __grid_c
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&s_empty[i], 256);
+      mbar_init(&p_full[i], 256);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
+      mbar_init(&o_empty[i], 256);
     }
     fence_mbar_init();
   }
@@ -1454,26 +1457,32 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(const __grid_c
       umma_commit(&kv_empty[st]);   // K_j (read by S_j, issued earlier) and V_j are consumed
     }
   } else if (warp >= 2) {
-    // ---------------- softmax + output accumulation (row = TMEM lane)
-    const int lb = 32 * (warp & 3);
+    // ---------------- softmax + output accumulation: two warps per TMEM lane quarter,
+    // warp half hf owns key columns [64 hf, 64 hf + 64) of S and output dims
+    // [hf D/2, (hf + 1) D/2); the pair exchanges row maxima and sums in shared memory
+    constexpr int DH = D / 2;
+    const int quarter = warp & 3, hf = (warp - 2) >> 2;
+    const int lb = 32 * quarter;
     const int r = lb + lane;
     const uint32_t lane_off = (uint32_t)lb << 16;
     const int qpos = prefix + q0 + r;
     const float sl2 = P.sm_scale * 1.4426950408889634f;
+    float* red = reinterpret_cast<float*>(bars + 16) + 4;   // [2 halves][128 rows]: max, then sum
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory"); };
     float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
-    float o[D];
+    float o[DH];
 #pragma unroll
-    for (int d = 0; d < D; ++d) o[d] = 0.f;
+    for (int d = 0; d < DH; ++d) o[d] = 0.f;
     bool ok = true;
-    // accumulate O_j (TMEM) into the registers: o = o * alpha + O_j
+    // accumulate this warp's half of O_j (TMEM) into the registers: o = o * alpha + O_j
     auto take_o = [&](int j, float alpha) {
       const int st = j & 1;
       if (!mbar_wait(&o_full[st], (j >> 1) & 1, P.err)) ok = false;
       tc_fence_after();
 #pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 16) {
+      for (int c0 = 0; c0 < DH; c0 += 16) {
         uint32_t v[16];
-        tmem_ld_32x32b_x16(t_o + st * D + lane_off + c0, v);
+        tmem_ld_32x32b_x16(t_o + st * D + hf * DH + lane_off + c0, v);
         tmem_wait_ld();
 #pragma unroll
         for (int t = 0; t < 16; ++t) o[c0 + t] = o[c0 + t] * alpha + (ok ? __uint_as_float(v[t]) : 0.f);
@@ -1485,13 +1494,13 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(const __grid_c
       const int st = j & 1;
       if (!mbar_wait(&s_full[st], (j >> 1) & 1, P.err)) ok = false;
       tc_fence_after();
-      const uint32_t srow = t_s + st * 128 + lane_off;
-      const int key0 = j * 128;
-      const bool need_mask = key0 + 127 > qpos || key0 + 128 > ctx;
-      // pass 1: block max of the scaled, masked scores
+      const uint32_t srow = t_s + st * 128 + hf * 64 + lane_off;
+      const int key0 = j * 128 + hf * 64;
+      const bool need_mask = key0 + 63 > qpos || key0 + 64 > ctx;
+      // pass 1: this half's maximum of the scaled, masked scores
       float mx = -INFINITY;
 #pragma unroll
-      for (int c0 = 0; c0 < 128; c0 += 16) {
+      for (int c0 = 0; c0 < 64; c0 += 16) {
         uint32_t v[16];
         tmem_ld_32x32b_x16(srow + c0, v);
         tmem_wait_ld();
@@ -1503,13 +1512,16 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(const __grid_c
           mx = fmaxf(mx, x);
         }
       }
-      const float m_new = fmaxf(m_run, mx);
+      red[hf * 128 + r] = mx;
+      pair_sync();
+      const float m_new = fmaxf(m_run, fmaxf(mx, red[(hf ^ 1) * 128 + r]));
+      pair_sync();                        // both maxima read before the slots take the sums
       const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m_run - m_new);
-      // pass 2: P = exp2(s - m_new) -> bf16 K-major swizzled rows; row sum
-      uint8_t* prow = smem + S::kPOff + st * S::kP + (r >> 3) * 1024 + (r & 7) * 128;
+      // pass 2: P = exp2(s - m_new) -> this half of the bf16 K-major swizzled P rows
+      uint8_t* half = smem + S::kPOff + st * S::kP + hf * (128 * 128) + (r >> 3) * 1024 + (r & 7) * 128;
       float sum = 0.f;
 #pragma unroll
-      for (int c0 = 0; c0 < 128; c0 += 16) {
+      for (int c0 = 0; c0 < 64; c0 += 16) {
         uint32_t v[16];
         tmem_ld_32x32b_x16(srow + c0, v);
         tmem_wait_ld();
@@ -1522,9 +1534,7 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(const __grid_c
           pv[t] = (m_new == -INFINITY || !ok) ? 0.f : exp2f(x - m_new);
           sum += pv[t];
         }
-        // keys c0 .. c0 + 15: 64-key half c0 / 64, 16-byte chunks (c0 % 64) / 8 and + 1
-        uint8_t* half = prow + (c0 >> 6) * (128 * 128);
-        const int ch = (c0 & 63) >> 3;
+        const int ch = c0 >> 3;
         uint4 w0, w1;
         w0.x = pack_bf16x2(pv[0], pv[1]);
         w0.y = pack_bf16x2(pv[2], pv[3]);
@@ -1541,7 +1551,9 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(const __grid_c
       mbar_arrive(&s_empty[st]);          // the scores are read: the slot takes S_{j+2}
       fence_proxy_async_smem();           // P written by this thread -> visible to the MMA
       mbar_arrive(&p_full[st]);
-      l_run = l_run * alpha + sum;
+      red[hf * 128 + r] = sum;
+      pair_sync();
+      l_run = l_run * alpha + sum + red[(hf ^ 1) * 128 + r];
       m_run = m_new;
       // O_{j-1} (finished while this block's softmax ran) into the accumulator
       if (j > 0) take_o(j - 1, alpha_prev);
@@ -1552,9 +1564,9 @@ __global__ void __launch_bounds__(192, 1) paged_prefill_tc_kernel(const __grid_c
     // alpha keeps the accumulator (and l_run) relative to the final running max
     if (q0 + r < q_len && ok) {
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* orow = P.out + (size_t)(q_start + q0 + r) * P.ld_o + (size_t)h * D;
+      __nv_bfloat16* orow = P.out + (size_t)(q_start + q0 + r) * P.ld_o + (size_t)h * D + hf * DH;
 #pragma unroll
-      for (int d = 0; d < D; d += 8) {
+      for (int d = 0; d < DH; d += 8) {
         uint4 w;
         w.x = pack_bf16x2(o[d] * inv, o[d + 1] * inv);
         w.y = pack_bf16x2(o[d + 2] * inv, o[d + 3] * inv);
@@ -1784,7 +1796,7 @@ static void launch_prefill_tc(const CUtensorMap& qm, const CUtensorMap& kv, cons
     VRM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     set[dev & 63] = true;
   }
-  launch_kernel(kern, grid, dim3(192), (size_t)smem, st, qm, kv, p);
+  launch_kernel(kern, grid, dim3(320), (size_t)smem, st, qm, kv, p);
 }
 
 template <int D, int FMT>
