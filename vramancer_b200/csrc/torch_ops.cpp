@@ -724,6 +724,9 @@ void tq_kv_write(const Tensor& qkv, const Tensor& slot_mapping, Tensor& pool, in
               "tq_kv_write: qkv must hold (Hq + 2 KH) heads of 128 dims");
   TORCH_CHECK(slot_mapping.scalar_type() == torch::kInt32 && slot_mapping.numel() >= qkv.size(0),
               "tq_kv_write: int32 slot_mapping");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(qkv.data_ptr()) & 7) == 0 &&
+                  (reinterpret_cast<uintptr_t>(pool.data_ptr()) & 63) == 0,
+              "tq_kv_write: qkv 8-byte and pool 64-byte aligned");
   same_device(qkv, {&slot_mapping, &pool, &signs, &jl}, "tq_kv_write");
   const c10::cuda::CUDAGuard guard(qkv.device());
   vrm::tq_kv_write(qkv.data_ptr(), qkv.stride(0), (int)qkv.size(0), (int)Hq, (int)KH, slot_mapping.data_ptr<int>(),
@@ -745,6 +748,9 @@ void tq_paged_decode(const Tensor& q, const Tensor& pool, int64_t layer, const T
               "tq_paged_decode: int32 block_tables [B, max_pages]");
   TORCH_CHECK(context_lens.scalar_type() == torch::kInt32 && context_lens.numel() >= q.size(0),
               "tq_paged_decode: int32 context_lens");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(q.data_ptr()) & 7) == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 7) == 0 &&
+                  (reinterpret_cast<uintptr_t>(pool.data_ptr()) & 63) == 0,
+              "tq_paged_decode: q / out 8-byte and pool 64-byte aligned");
   same_device(q, {&pool, &block_tables, &context_lens, &signs, &jl, &out}, "tq_paged_decode");
   const c10::cuda::CUDAGuard guard(q.device());
   vrm::tq_paged_decode(q.data_ptr(), q.stride(0), reinterpret_cast<const uint8_t*>(pool.data_ptr()),

@@ -390,8 +390,11 @@ __global__ void __launch_bounds__(kTqAttnWarps * 32) tq_paged_decode_kernel(
     float kv4[4], vv4[4];
     polar_decode_tab(s_idx[warp][0], kr, lane, T, kv4);
     polar_decode_tab(s_idx[warp][1], vr, lane, T, vv4);
-    const uint32_t sg0 = *reinterpret_cast<const uint32_t*>(krec + 50);
-    const uint32_t sg1 = *reinterpret_cast<const uint32_t*>(krec + 54);
+    // sign words at record bytes 50..53 and 54..57: not 4-byte aligned, assembled bytewise
+    const uint32_t sg0 = (uint32_t)krec[50] | (uint32_t)krec[51] << 8 | (uint32_t)krec[52] << 16 |
+                         (uint32_t)krec[53] << 24;
+    const uint32_t sg1 = (uint32_t)krec[54] | (uint32_t)krec[55] << 8 | (uint32_t)krec[56] << 16 |
+                         (uint32_t)krec[57] << 24;
     const float nrm = __half2float(__ushort_as_half((unsigned short)(krec[58] | (krec[59] << 8))));
     const float sa = (sg0 >> lane) & 1u ? 1.f : -1.f, sb = (sg1 >> lane) & 1u ? 1.f : -1.f;
     float sc[8];
