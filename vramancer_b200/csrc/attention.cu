@@ -1319,7 +1319,19 @@ __device__ __forceinline__ uint64_t make_mn_sw128_desc(uint32_t addr, uint32_t l
   return d;
 }
 
-template <int D>
+// 2^x on the FMA pipes, for half of the softmax exponentials (the other half stays on
+// the multi-function unit, whose throughput bounds a 128 x 128 score block): x = n + f,
+// n = floor(x), 2^f by a cubic fitted here by weighted least squares on [0, 1)
+// (relative error < 9e-5, far below bf16's 2^-8 for P), n added to the exponent bits.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -127.f);
+  const float n = floorf(x);
+  const float f = x - n;
+  const float p = fmaf(fmaf(fmaf(0.07705975f, f, 0.22764372f), f, 0.69512331f), f, 1.0f);
+  return __int_as_float(__float_as_int(p) + ((int)n << 23));
+}
+
+template <int D, bool kPoly>
 __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                    const __grid_constant__ CUtensorMap kvmap,
                                                                    PrefillTcParams P) {
@@ -1531,7 +1543,8 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(const __grid_c
           const int key = key0 + c0 + t;
           float x = __uint_as_float(v[t]) * sl2;
           if (need_mask && (key > qpos || key >= ctx)) x = -INFINITY;
-          pv[t] = (m_new == -INFINITY || !ok) ? 0.f : exp2f(x - m_new);
+          const float e = (kPoly && (t & 1)) ? exp2_fma(x - m_new) : exp2f(x - m_new);
+          pv[t] = (m_new == -INFINITY || !ok) ? 0.f : e;
           sum += pv[t];
         }
         const int ch = c0 >> 3;
@@ -1784,11 +1797,11 @@ static bool prefill_tc_enabled() {
   return g_prefill_tc == 1;
 }
 
-template <int D>
+template <int D, bool kPoly>
 static void launch_prefill_tc(const CUtensorMap& qm, const CUtensorMap& kv, const PrefillTcParams& p, dim3 grid,
                               cudaStream_t st) {
   constexpr int smem = PrefillTcSmem<D>::kAlloc;
-  auto kern = paged_prefill_tc_kernel<D>;
+  auto kern = paged_prefill_tc_kernel<D, kPoly>;
   static bool set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1862,8 +1875,18 @@ void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
     const CUtensorMap kv = make_kmajor_map(a.cache, pool_rows, a.D, a.D, kPage);
     const CUtensorMap qm = make_kmajor_map(a.q, a.num_tokens, (int64_t)a.Hq * a.D, a.ld_q, 128);
     const dim3 grid(t.max_tiles, a.Hq, a.B);
-    if (a.D == 128) launch_prefill_tc<128>(qm, kv, t, grid, st);
-    else launch_prefill_tc<64>(qm, kv, t, grid, st);
+    // VRM_PREFILL_TC_EXP=fma: half the exponentials on the FMA pipes
+    static const bool poly = [] {
+      const char* e = std::getenv("VRM_PREFILL_TC_EXP");
+      return e && e[0] == 'f';
+    }();
+    if (a.D == 128) {
+      if (poly) launch_prefill_tc<128, true>(qm, kv, t, grid, st);
+      else launch_prefill_tc<128, false>(qm, kv, t, grid, st);
+    } else {
+      if (poly) launch_prefill_tc<64, true>(qm, kv, t, grid, st);
+      else launch_prefill_tc<64, false>(qm, kv, t, grid, st);
+    }
     return;
   }
   dim3 grid((a.max_q_len + 63) / 64, a.Hq, a.B);
