@@ -1319,6 +1319,12 @@ __device__ __forceinline__ uint64_t make_mn_sw128_desc(uint32_t addr, uint32_t l
   return d;
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // 2^x on the FMA pipes, for half of the softmax exponentials (the other half stays on
 // the multi-function unit, whose throughput bounds a 128 x 128 score block): x = n + f,
 // n = floor(x), 2^f by a cubic fitted here by weighted least squares on [0, 1)
@@ -1509,19 +1515,29 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(const __grid_c
       const uint32_t srow = t_s + st * 128 + hf * 64 + lane_off;
       const int key0 = j * 128 + hf * 64;
       const bool need_mask = key0 + 63 > qpos || key0 + 64 > ctx;
-      // pass 1: this half's maximum of the scaled, masked scores
+      // pass 1: this half's maximum of the scaled, masked scores (unmasked blocks: the
+      // raw maximum, scaled once -- sl2 > 0)
       float mx = -INFINITY;
+      if (!need_mask) {
 #pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld_32x32b_x16(srow + c0, v);
-        tmem_wait_ld();
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld_32x32b_x16(srow + c0, v);
+          tmem_wait_ld();
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          const int key = key0 + c0 + t;
-          float x = __uint_as_float(v[t]) * sl2;
-          if (need_mask && (key > qpos || key >= ctx)) x = -INFINITY;
-          mx = fmaxf(mx, x);
+          for (int t = 0; t < 16; ++t) mx = fmaxf(mx, __uint_as_float(v[t]));
+        }
+        mx *= sl2;
+      } else {
+#pragma unroll
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld_32x32b_x16(srow + c0, v);
+          tmem_wait_ld();
+          // keys past this row's last valid key: key0 + c0 + t > min(qpos, ctx - 1)
+          const int lim = min(qpos, ctx - 1) - (key0 + c0);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) mx = fmaxf(mx, t <= lim ? __uint_as_float(v[t]) * sl2 : -INFINITY);
         }
       }
       red[hf * 128 + r] = mx;
@@ -1532,19 +1548,20 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(const __grid_c
       // pass 2: P = exp2(s - m_new) -> this half of the bf16 K-major swizzled P rows
       uint8_t* half = smem + S::kPOff + st * S::kP + hf * (128 * 128) + (r >> 3) * 1024 + (r & 7) * 128;
       float sum = 0.f;
+      const bool live = m_new != -INFINITY && ok;
+      const float nm = live ? -m_new : 0.f;
 #pragma unroll
       for (int c0 = 0; c0 < 64; c0 += 16) {
         uint32_t v[16];
         tmem_ld_32x32b_x16(srow + c0, v);
         tmem_wait_ld();
         float pv[16];
+        const int lim = need_mask ? min(qpos, ctx - 1) - (key0 + c0) : 15;
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          const int key = key0 + c0 + t;
-          float x = __uint_as_float(v[t]) * sl2;
-          if (need_mask && (key > qpos || key >= ctx)) x = -INFINITY;
-          const float e = (kPoly && (t & 1)) ? exp2_fma(x - m_new) : exp2f(x - m_new);
-          pv[t] = (m_new == -INFINITY || !ok) ? 0.f : e;
+          const float x = fmaf(__uint_as_float(v[t]), sl2, nm);   // score * scale - running max
+          const float e = (kPoly && (t & 1)) ? exp2_fma(x) : ex2_approx(x);
+          pv[t] = (live && t <= lim) ? e : 0.f;
           sum += pv[t];
         }
         const int ch = c0 >> 3;

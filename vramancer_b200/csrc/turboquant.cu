@@ -11,6 +11,7 @@
 //
 // Reference parity: csrc/turboquant_kernel.cu:36-405 (Hadamard + polar encode/decode +
 // QJL in fused compress / decompress kernels).
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include "vrm_common.cuh"
@@ -307,6 +308,7 @@ __device__ __forceinline__ float unpack_record(const uint8_t* rec, uint8_t* idx,
   return __half2float(__ushort_as_half((unsigned short)(rec[48] | (rec[49] << 8))));
 }
 
+template <bool kCluster>
 __global__ void __launch_bounds__(kTqAttnWarps * 32) tq_paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q, int64_t ld_q, const uint8_t* __restrict__ pool, int num_layers, int layer,
     int KH, int G, const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ context_lens,
@@ -320,8 +322,10 @@ __global__ void __launch_bounds__(kTqAttnWarps * 32) tq_paged_decode_kernel(
   __shared__ uint8_t s_idx[kTqAttnWarps][2][kTqD];
   __shared__ float s_m[kTqAttnWarps][8], s_l[kTqAttnWarps][8];
   __shared__ float s_acc[kTqAttnWarps][8][kTqD];
+  __shared__ float s_fm[8], s_fl[8];              // this CTA's merged (max, sum) per head
+  __shared__ float s_fo[8][kTqD];                 // and its rotated output (unnormalised)
   pdl_launch();
-  const int kvh = blockIdx.x, b = blockIdx.y;
+  const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z, nsplit = gridDim.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x < 16) {
     const int lv = threadIdx.x >> 3, qb = threadIdx.x & 7;
@@ -354,6 +358,8 @@ __global__ void __launch_bounds__(kTqAttnWarps * 32) tq_paged_decode_kernel(
   }
   __syncthreads();
   const int ctx = context_lens[b];
+  const int per = (ctx + nsplit - 1) / nsplit;
+  const int t_begin = split * per, t_end = min(ctx, t_begin + per);
   const int* bt = block_tables + (size_t)b * bt_stride;
   const float qjl_c = 1.2533141373155003f / (float)kTqM;   // sqrt(pi / 2) / m
   const float sl2 = sm_scale * 1.4426950408889634f;
@@ -375,14 +381,36 @@ __global__ void __launch_bounds__(kTqAttnWarps * 32) tq_paged_decode_kernel(
   }
   uint8_t* krec = s_rec[warp][0];
   uint8_t* vrec = s_rec[warp][1];
-  for (int t = warp; t < ctx; t += kTqAttnWarps) {
-    int page = bt[t >> 4];
-    if (!in_bounds(page, num_pages, err)) page = 0;
-    const size_t base = ((((size_t)page * num_layers + layer) * 2 * KH + kvh) * 16 + (t & 15)) * kTqRec;
-    const size_t vofs = (size_t)KH * 16 * kTqRec;
+  const size_t vofs = (size_t)KH * 16 * kTqRec;
+  // records of this warp's next kPre tokens in flight in registers (lanes 0-15: 4 bytes
+  // of the K record and 4 of the V record each): the loads of token i + kPre overlap
+  // the arithmetic of token i
+  constexpr int kPre = 4;
+  uint32_t pk[kPre], pv[kPre];
+  auto fetch = [&](int t, uint32_t& kw, uint32_t& vw) {
+    kw = vw = 0u;
+    if (t < t_end && lane < 16) {
+      int page = bt[t >> 4];
+      if (!in_bounds(page, num_pages, err)) page = 0;
+      const uint8_t* base = pool + ((((size_t)page * num_layers + layer) * 2 * KH + kvh) * 16 + (t & 15)) * kTqRec;
+      kw = __ldg(reinterpret_cast<const uint32_t*>(base) + lane);
+      vw = __ldg(reinterpret_cast<const uint32_t*>(base + vofs) + lane);
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < kPre; ++i) fetch(t_begin + warp + i * kTqAttnWarps, pk[i], pv[i]);
+  for (int t = t_begin + warp; t < t_end; t += kTqAttnWarps) {
+    // this token's words -> shared; refill the slot with the token kPre steps ahead
+    uint32_t kw = pk[0], vw = pv[0];
+#pragma unroll
+    for (int i = 0; i < kPre - 1; ++i) {
+      pk[i] = pk[i + 1];
+      pv[i] = pv[i + 1];
+    }
+    fetch(t + kPre * kTqAttnWarps, pk[kPre - 1], pv[kPre - 1]);
     if (lane < 16) {
-      reinterpret_cast<uint32_t*>(krec)[lane] = __ldg(reinterpret_cast<const uint32_t*>(pool + base) + lane);
-      reinterpret_cast<uint32_t*>(vrec)[lane] = __ldg(reinterpret_cast<const uint32_t*>(pool + base + vofs) + lane);
+      reinterpret_cast<uint32_t*>(krec)[lane] = kw;
+      reinterpret_cast<uint32_t*>(vrec)[lane] = vw;
     }
     __syncwarp();
     const float kr = unpack_record(krec, s_idx[warp][0], lane);
@@ -420,7 +448,7 @@ __global__ void __launch_bounds__(kTqAttnWarps * 32) tq_paged_decode_kernel(
     }
     __syncwarp();
   }
-  // ---- merge the warps, unrotate, store
+  // ---- merge this CTA's warps (rotated domain, unnormalised)
 #pragma unroll
   for (int h = 0; h < 8; ++h) {
     if (h >= G) continue;
@@ -447,14 +475,57 @@ __global__ void __launch_bounds__(kTqAttnWarps * 32) tq_paged_decode_kernel(
         for (int j = 0; j < 4; ++j) v[j] += s_acc[w][h][4 * lane + j] * f;
       }
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
+    if (lane == 0) {
+      s_fm[h] = M;
+      s_fl[h] = L;
+    }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] *= inv;
-    fwht4(v, lane);                            // H / sqrt(D): its own inverse
-    uint2 o;
-    o.x = pack_bf16x2(v[0] * s_sign[4 * lane], v[1] * s_sign[4 * lane + 1]);
-    o.y = pack_bf16x2(v[2] * s_sign[4 * lane + 2], v[3] * s_sign[4 * lane + 3]);
-    *reinterpret_cast<uint2*>(out + (size_t)b * ld_o + (size_t)(kvh * G + h) * kTqD + 4 * lane) = o;
+    for (int j = 0; j < 4; ++j) s_fo[h][4 * lane + j] = v[j];
+  }
+  // ---- merge the splits of the cluster (DSMEM): CTA rank r finishes heads r, r + S, ...
+  if constexpr (kCluster) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const int rank = (int)cluster.block_rank();
+    for (int h = rank + warp * nsplit; h < G; h += kTqAttnWarps * nsplit) {
+      float M = -INFINITY;
+      for (int r = 0; r < nsplit; ++r) M = fmaxf(M, cluster.map_shared_rank(s_fm, r)[h]);
+      float L = 0.f, v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (M != -INFINITY) {
+        for (int r = 0; r < nsplit; ++r) {
+          const float f = exp2f(cluster.map_shared_rank(s_fm, r)[h] - M);
+          L += cluster.map_shared_rank(s_fl, r)[h] * f;
+          const float* o = cluster.map_shared_rank(&s_fo[0][0], r) + h * kTqD + 4 * lane;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[j] += o[j] * f;
+        }
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] *= inv;
+      fwht4(v, lane);                            // H / sqrt(D): its own inverse
+      uint2 o2;
+      o2.x = pack_bf16x2(v[0] * s_sign[4 * lane], v[1] * s_sign[4 * lane + 1]);
+      o2.y = pack_bf16x2(v[2] * s_sign[4 * lane + 2], v[3] * s_sign[4 * lane + 3]);
+      *reinterpret_cast<uint2*>(out + (size_t)b * ld_o + (size_t)(kvh * G + h) * kTqD + 4 * lane) = o2;
+    }
+    cluster.sync();     // peers' shared memory stays valid until every CTA has read it
+  } else {
+    __syncthreads();
+    if (warp < G) {
+      const int h = warp;
+      const float L = s_fl[h];
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = s_fo[h][4 * lane + j] * inv;
+      fwht4(v, lane);
+      uint2 o2;
+      o2.x = pack_bf16x2(v[0] * s_sign[4 * lane], v[1] * s_sign[4 * lane + 1]);
+      o2.y = pack_bf16x2(v[2] * s_sign[4 * lane + 2], v[3] * s_sign[4 * lane + 3]);
+      *reinterpret_cast<uint2*>(out + (size_t)b * ld_o + (size_t)(kvh * G + h) * kTqD + 4 * lane) = o2;
+    }
   }
 }
 
@@ -491,10 +562,22 @@ void tq_paged_decode(const void* q, int64_t ld_q, const uint8_t* pool, int num_l
                      const float* jl, float sm_scale, void* out, int64_t ld_o, int64_t num_pages, cudaStream_t st) {
   VRM_REQUIRE(KH > 0 && Hq % KH == 0 && Hq / KH <= 8, "turboquant decode: GQA group <= 8 heads");
   if (B <= 0) return;
-  launch_kernel(tq_paged_decode_kernel, dim3(KH, B), dim3(kTqAttnWarps * 32), 0, st,
-                reinterpret_cast<const __nv_bfloat16*>(q), ld_q, pool, num_layers, layer, KH, Hq / KH, block_tables,
-                bt_stride, context_lens, signs, jl, sm_scale, reinterpret_cast<__nv_bfloat16*>(out), ld_o,
-                (long long)num_pages, error_word());
+  // splits of the context over the CTAs of a cluster (merged over DSMEM) when the
+  // (sequence, KV head) groups alone leave SMs idle
+  const int groups = B * KH;
+  int splits = 1;
+  while (splits < 8 && groups * splits * 2 <= device_sm_count()) splits *= 2;
+  const dim3 grid(KH, B, splits);
+  if (splits > 1)
+    launch_kernel_cluster(tq_paged_decode_kernel<true>, grid, dim3(kTqAttnWarps * 32), dim3(1, 1, splits), 0, st,
+                          reinterpret_cast<const __nv_bfloat16*>(q), ld_q, pool, num_layers, layer, KH, Hq / KH,
+                          block_tables, bt_stride, context_lens, signs, jl, sm_scale,
+                          reinterpret_cast<__nv_bfloat16*>(out), ld_o, (long long)num_pages, error_word());
+  else
+    launch_kernel(tq_paged_decode_kernel<false>, grid, dim3(kTqAttnWarps * 32), 0, st,
+                  reinterpret_cast<const __nv_bfloat16*>(q), ld_q, pool, num_layers, layer, KH, Hq / KH, block_tables,
+                  bt_stride, context_lens, signs, jl, sm_scale, reinterpret_cast<__nv_bfloat16*>(out), ld_o,
+                  (long long)num_pages, error_word());
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
