@@ -1319,25 +1319,7 @@ __device__ __forceinline__ uint64_t make_mn_sw128_desc(uint32_t addr, uint32_t l
   return d;
 }
 
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// 2^x on the FMA pipes, for half of the softmax exponentials (the other half stays on
-// the multi-function unit, whose throughput bounds a 128 x 128 score block): x = n + f,
-// n = floor(x), 2^f by a cubic fitted here by weighted least squares on [0, 1)
-// (relative error < 9e-5, far below bf16's 2^-8 for P), n added to the exponent bits.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -127.f);
-  const float n = floorf(x);
-  const float f = x - n;
-  const float p = fmaf(fmaf(fmaf(0.07705975f, f, 0.22764372f), f, 0.69512331f), f, 1.0f);
-  return __int_as_float(__float_as_int(p) + ((int)n << 23));
-}
-
-template <int D, bool kPoly>
+template <int D>
 __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                    const __grid_constant__ CUtensorMap kvmap,
                                                                    PrefillTcParams P) {
@@ -1515,29 +1497,19 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(const __grid_c
       const uint32_t srow = t_s + st * 128 + hf * 64 + lane_off;
       const int key0 = j * 128 + hf * 64;
       const bool need_mask = key0 + 63 > qpos || key0 + 64 > ctx;
-      // pass 1: this half's maximum of the scaled, masked scores (unmasked blocks: the
-      // raw maximum, scaled once -- sl2 > 0)
+      // pass 1: this half's maximum of the scaled, masked scores
       float mx = -INFINITY;
-      if (!need_mask) {
 #pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld_32x32b_x16(srow + c0, v);
-          tmem_wait_ld();
+      for (int c0 = 0; c0 < 64; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(srow + c0, v);
+        tmem_wait_ld();
 #pragma unroll
-          for (int t = 0; t < 16; ++t) mx = fmaxf(mx, __uint_as_float(v[t]));
-        }
-        mx *= sl2;
-      } else {
-#pragma unroll
-        for (int c0 = 0; c0 < 64; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld_32x32b_x16(srow + c0, v);
-          tmem_wait_ld();
-          // keys past this row's last valid key: key0 + c0 + t > min(qpos, ctx - 1)
-          const int lim = min(qpos, ctx - 1) - (key0 + c0);
-#pragma unroll
-          for (int t = 0; t < 16; ++t) mx = fmaxf(mx, t <= lim ? __uint_as_float(v[t]) * sl2 : -INFINITY);
+        for (int t = 0; t < 16; ++t) {
+          const int key = key0 + c0 + t;
+          float x = __uint_as_float(v[t]) * sl2;
+          if (need_mask && (key > qpos || key >= ctx)) x = -INFINITY;
+          mx = fmaxf(mx, x);
         }
       }
       red[hf * 128 + r] = mx;
@@ -1548,20 +1520,18 @@ __global__ void __launch_bounds__(320, 1) paged_prefill_tc_kernel(const __grid_c
       // pass 2: P = exp2(s - m_new) -> this half of the bf16 K-major swizzled P rows
       uint8_t* half = smem + S::kPOff + st * S::kP + hf * (128 * 128) + (r >> 3) * 1024 + (r & 7) * 128;
       float sum = 0.f;
-      const bool live = m_new != -INFINITY && ok;
-      const float nm = live ? -m_new : 0.f;
 #pragma unroll
       for (int c0 = 0; c0 < 64; c0 += 16) {
         uint32_t v[16];
         tmem_ld_32x32b_x16(srow + c0, v);
         tmem_wait_ld();
         float pv[16];
-        const int lim = need_mask ? min(qpos, ctx - 1) - (key0 + c0) : 15;
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          const float x = fmaf(__uint_as_float(v[t]), sl2, nm);   // score * scale - running max
-          const float e = (kPoly && (t & 1)) ? exp2_fma(x) : ex2_approx(x);
-          pv[t] = (live && t <= lim) ? e : 0.f;
+          const int key = key0 + c0 + t;
+          float x = __uint_as_float(v[t]) * sl2;
+          if (need_mask && (key > qpos || key >= ctx)) x = -INFINITY;
+          pv[t] = (m_new == -INFINITY || !ok) ? 0.f : exp2f(x - m_new);
           sum += pv[t];
         }
         const int ch = c0 >> 3;
@@ -1814,11 +1784,11 @@ static bool prefill_tc_enabled() {
   return g_prefill_tc == 1;
 }
 
-template <int D, bool kPoly>
+template <int D>
 static void launch_prefill_tc(const CUtensorMap& qm, const CUtensorMap& kv, const PrefillTcParams& p, dim3 grid,
                               cudaStream_t st) {
   constexpr int smem = PrefillTcSmem<D>::kAlloc;
-  auto kern = paged_prefill_tc_kernel<D, kPoly>;
+  auto kern = paged_prefill_tc_kernel<D>;
   static bool set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1892,18 +1862,8 @@ void paged_attention_prefill(const PrefillAttnArgs& a, cudaStream_t st) {
     const CUtensorMap kv = make_kmajor_map(a.cache, pool_rows, a.D, a.D, kPage);
     const CUtensorMap qm = make_kmajor_map(a.q, a.num_tokens, (int64_t)a.Hq * a.D, a.ld_q, 128);
     const dim3 grid(t.max_tiles, a.Hq, a.B);
-    // VRM_PREFILL_TC_EXP=fma: half the exponentials on the FMA pipes
-    static const bool poly = [] {
-      const char* e = std::getenv("VRM_PREFILL_TC_EXP");
-      return e && e[0] == 'f';
-    }();
-    if (a.D == 128) {
-      if (poly) launch_prefill_tc<128, true>(qm, kv, t, grid, st);
-      else launch_prefill_tc<128, false>(qm, kv, t, grid, st);
-    } else {
-      if (poly) launch_prefill_tc<64, true>(qm, kv, t, grid, st);
-      else launch_prefill_tc<64, false>(qm, kv, t, grid, st);
-    }
+    if (a.D == 128) launch_prefill_tc<128>(qm, kv, t, grid, st);
+    else launch_prefill_tc<64>(qm, kv, t, grid, st);
     return;
   }
   dim3 grid((a.max_q_len + 63) / 64, a.Hq, a.B);
