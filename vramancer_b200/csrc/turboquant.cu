@@ -308,9 +308,8 @@ __device__ __forceinline__ float unpack_record(const uint8_t* rec, uint8_t* idx,
   return __half2float(__ushort_as_half((unsigned short)(rec[48] | (rec[49] << 8))));
 }
 
-// two CTAs per SM (<= 128 registers): with one, batches of 32+ sequences ran slower
 template <bool kCluster>
-__global__ void __launch_bounds__(kTqAttnWarps * 32, 2) tq_paged_decode_kernel(
+__global__ void __launch_bounds__(kTqAttnWarps * 32) tq_paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q, int64_t ld_q, const uint8_t* __restrict__ pool, int num_layers, int layer,
     int KH, int G, const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ context_lens,
     const float* __restrict__ signs, const float* __restrict__ jl, float sm_scale, __nv_bfloat16* __restrict__ out,
