@@ -7,6 +7,8 @@ Public API (the reference's names where they exist):
     LLMEngine (ContinuousBatcher)                        continuous batching over paged KV
     PagedKVCacheManager, KVPool                          paged KV
     split_model_into_blocks, auto_configure              placement
+    TurboEngine, MultiGPUTurboEngine,                    engine object over a loaded HF model
+    SpeculativeTurboEngine, create_turbo_engine          (or preset / checkpoint directory)
 """
 __version__ = "0.1.0"
 
@@ -25,6 +27,10 @@ _LAZY = {
     "TurboQuantCache": ("kv.turboquant", "TurboQuantCache"),
     "DirectFP4Linear": ("quant.nvfp4", "DirectFP4Linear"),
     "apply_tensor_parallel": ("parallel.tensor_parallel", "apply_tensor_parallel"),
+    "TurboEngine": ("engine.turbo", "TurboEngine"), "MultiGPUTurboEngine": ("engine.turbo", "MultiGPUTurboEngine"),
+    "SpeculativeTurboEngine": ("engine.turbo", "SpeculativeTurboEngine"),
+    "create_turbo_engine": ("engine.turbo", "create_turbo_engine"),
+    "weights_from_state_dict": ("models.weights", "weights_from_state_dict"),
 }
 
 

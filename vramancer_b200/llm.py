@@ -181,6 +181,28 @@ class LLM:
         return max(16, min(need * 2, budget // per))
 
     # ------------------------------------------------------------------ API
+    @classmethod
+    def from_local_pipeline(cls, cfg: ModelConfig, blocks, *, num_pages: int, max_batch: int = 64,
+                            max_model_len: int = 4096, dtype: torch.dtype = torch.bfloat16, kv_dtype=None,
+                            weights=None, transfer=None, eos_token_id: Optional[int] = None) -> "LLM":
+        """An LLM over an in-process layer pipeline: one stage (layers, KV pool) per block
+        of `blocks` (parallel.placement.Block: start, end, device), activations moved
+        between the stages' devices by `transfer(tensor, device)` (a peer copy by
+        default).  Decode runs eagerly (no CUDA graph across devices)."""
+        from .parallel.pipeline import LocalPipeline, build_local_pipeline
+        pipe = build_local_pipeline(cfg, blocks, num_pages=num_pages, dtype=dtype, kv_dtype=kv_dtype or dtype,
+                                    weights=weights)
+        if transfer is not None:
+            pipe = LocalPipeline(pipe.stages, transfer=transfer)
+        llm = cls.__new__(cls)
+        llm.cfg, llm.device, llm.model, llm.pool = cfg, pipe.device, pipe, None
+        llm.tp, llm.pp_grid, llm.quantization, llm.offload = None, None, None, None
+        llm.weights = weights
+        llm.kv = PagedKVCacheManager(num_pages)
+        llm.runner = ModelRunner(pipe, None, max_batch=max_batch, max_model_len=max_model_len, use_cuda_graph=False)
+        llm.engine = LLMEngine(llm.runner, llm.kv, eos_token_id=eos_token_id)
+        return llm
+
     def generate(self, prompts: Sequence[Sequence[int]], params: Optional[SamplingParams] = None) -> List[Request]:
         return self.engine.generate(prompts, params)
 

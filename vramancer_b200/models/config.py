@@ -11,7 +11,7 @@ from __future__ import annotations
 import json
 import os
 from dataclasses import asdict, dataclass, field, replace
-from typing import Any, Dict, Optional
+from typing import Any, Dict, Optional, Tuple
 
 
 @dataclass(frozen=True)
@@ -28,6 +28,9 @@ class ModelConfig:
     norm_eps: float = 1e-6
     rope_theta: float = 1_000_000.0
     rotary_dim: Optional[int] = None     # None -> head_dim (no RoPE for gpt2)
+    # RoPE frequency scaling as sorted (key, value) pairs of the HF rope parameters
+    # ("rope_type" linear | llama3 | yarn | dynamic, "factor", ...); None = plain RoPE
+    rope_scaling: Optional[Tuple[Tuple[str, Any], ...]] = None
     qkv_bias: bool = True
     tie_embeddings: bool = False
     # MoE
@@ -101,6 +104,22 @@ class ModelConfig:
         nh = cfg["num_attention_heads"]
         kvh = cfg.get("num_key_value_heads", nh)
         hd = cfg.get("head_dim") or H // nh
+        # RoPE: transformers 5 writes `rope_parameters` ({"rope_theta", "rope_type", ...});
+        # older configs a top-level `rope_theta` and an optional `rope_scaling`
+        rp = dict(cfg.get("rope_parameters") or {})
+        theta = rp.pop("rope_theta", None) or cfg.get("rope_theta", 10000.0)
+        if cfg.get("rope_scaling"):
+            rp.update(cfg["rope_scaling"])
+        if "type" in rp and "rope_type" not in rp:
+            rp["rope_type"] = rp.pop("type")
+        rp.pop("partial_rotary_factor", None)
+        scaling = None
+        if rp.get("rope_type", "default") != "default":
+            if "original_max_position_embeddings" not in rp and cfg.get("original_max_position_embeddings"):
+                rp["original_max_position_embeddings"] = cfg["original_max_position_embeddings"]
+            scaling = tuple(sorted((k, v) for k, v in rp.items() if not isinstance(v, (list, dict))))
+        prf = cfg.get("partial_rotary_factor") or (cfg.get("rope_parameters") or {}).get("partial_rotary_factor")
+        rot = int(hd * prf) if prf else None
         arch = {"qwen2": "qwen2", "llama": "llama", "mistral": "mistral", "qwen2_moe": "qwen2_moe",
                 "qwen3_moe": "qwen2_moe"}.get(mt, "llama")
         moe = {}
@@ -113,7 +132,8 @@ class ModelConfig:
                            num_layers=cfg["num_hidden_layers"], num_heads=nh, num_kv_heads=kvh, head_dim=hd,
                            intermediate_size=cfg.get("intermediate_size", 4 * H),
                            max_position=cfg.get("max_position_embeddings", 32768),
-                           norm_eps=cfg.get("rms_norm_eps", 1e-6), rope_theta=cfg.get("rope_theta", 10000.0),
+                           norm_eps=cfg.get("rms_norm_eps", 1e-6), rope_theta=float(theta), rotary_dim=rot,
+                           rope_scaling=scaling,
                            qkv_bias=bool(cfg.get("attention_bias", arch in ("qwen2", "qwen2_moe"))),
                            tie_embeddings=bool(cfg.get("tie_word_embeddings", False)), name=name, **moe)
 
@@ -135,6 +155,10 @@ class ModelConfig:
              "max_position_embeddings": self.max_position, "rms_norm_eps": self.norm_eps,
              "rope_theta": self.rope_theta, "tie_word_embeddings": self.tie_embeddings,
              "hidden_act": "silu", "torch_dtype": "bfloat16"}
+        if self.rope_scaling:
+            d["rope_scaling"] = dict(self.rope_scaling)
+        if self.rotary_dim is not None and self.rotary_dim != self.head_dim:
+            d["partial_rotary_factor"] = self.rotary_dim / self.head_dim
         if self.arch == "qwen2":
             d["architectures"] = ["Qwen2ForCausalLM"]
         elif self.arch in ("llama", "mistral"):

@@ -100,7 +100,8 @@ class DecoderModel:
         self.D = cfg.head_dim
         self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
         self._rope_dummy = None      # one-page bf16 pool for RoPE without a KV write (TurboQuant pages)
-        self.cos_sin = (ops.rope_cos_sin(cfg.max_position, cfg.rot_dim, cfg.rope_theta, self.device)
+        self.cos_sin = (ops.rope_cos_sin(cfg.max_position, cfg.rot_dim, cfg.rope_theta, self.device,
+                                          scaling=cfg.rope_scaling)
                         if cfg.rot_dim > 0 else None)
         # decode attention does RoPE + the KV write itself when rotation covers the whole
         # head (or there is none); VRM_FUSED_ROPE=0 keeps the separate kernel

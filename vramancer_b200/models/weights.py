@@ -279,6 +279,68 @@ def _tp_slice(cfg: ModelConfig, iname: str, role: str, shape, rank: int, size: i
     return None
 
 
+def _place(out: Weights, parts: Dict[str, Dict[str, torch.Tensor]], iname: str, role: str,
+           t: torch.Tensor) -> None:
+    """One mapped HF tensor: whole tensors (GPT-2 Conv1D weights transposed to [out, in])
+    go to `out`, pieces of fused tensors (q / k / v, gate / up, one expert) to `parts`."""
+    if role == "conv1d":
+        out[iname] = t.t().contiguous()
+    elif role == "copy":
+        out[iname] = t
+    else:
+        parts.setdefault(iname, {})[role] = t
+
+
+def _fuse_parts(out: Weights, parts: Dict[str, Dict[str, torch.Tensor]], experts) -> None:
+    """q|k|v rows concatenated, gate / up interleaved, experts stacked (in id order)."""
+    for iname, p in parts.items():
+        base = iname.split(".")[-1]
+        if base in ("qkv_w", "qkv_b"):
+            out[iname] = torch.cat([p["q"], p["k"], p["v"]], 0)
+        elif base in ("gate_up_w", "shared_gate_up_w"):
+            out[iname] = interleave_gate_up(p["gate"], p["up"])
+        elif base == "experts_gate_up_w":
+            out[iname] = torch.stack([interleave_gate_up(p[f"egate:{e}"], p[f"eup:{e}"]) for e in sorted(experts)])
+        elif base == "experts_down_w":
+            out[iname] = torch.stack([p[f"edown:{e}"] for e in sorted(experts)])
+
+
+def weights_from_state_dict(cfg: ModelConfig, state_dict, *, device="cpu", dtype=torch.bfloat16) -> Weights:
+    """Internal weights from an in-memory HF state dict (a loaded `PreTrainedModel`'s
+    `state_dict()`): the name mapping and fusing of `load_safetensors`, one device, no
+    sharding.  Transformers 5 stores MoE experts fused ([E, 2I, H] gate_up_proj,
+    [E, H, I] down_proj); those are split back into per-expert pieces here."""
+    out: Weights = {}
+    parts: Dict[str, Dict[str, torch.Tensor]] = {}
+    experts = range(cfg.num_experts) if cfg.is_moe else range(0)
+    for name, t in state_dict.items():
+        t = t.detach()
+        if name.endswith("mlp.experts.gate_up_proj") or name.endswith("mlp.experts.down_proj"):
+            pre = name.rsplit(".", 1)[0]
+            for e in experts:
+                if name.endswith("gate_up_proj"):
+                    g, u = t[e].chunk(2, 0) if t.shape[1] == 2 * cfg.expert_intermediate_size else t[e].t().chunk(2, 0)
+                    for part, v in (("gate_proj", g), ("up_proj", u)):
+                        m = _hf_map(cfg, f"{pre}.{e}.{part}.weight")
+                        _place(out, parts, m[0], m[1], v)
+                else:
+                    v = t[e] if t.shape[1] == cfg.hidden_size else t[e].t()
+                    m = _hf_map(cfg, f"{pre}.{e}.down_proj.weight")
+                    _place(out, parts, m[0], m[1], v)
+            continue
+        m = _hf_map(cfg, name)
+        if m is None:
+            continue
+        _place(out, parts, m[0], m[1], t)
+    _fuse_parts(out, parts, experts)
+    if "lm_head" not in out and "embed" in out:
+        out["lm_head"] = out["embed"]
+    res = {k: v.to(device=device, dtype=dtype).contiguous() for k, v in out.items()}
+    if out.get("lm_head") is out.get("embed"):
+        res["lm_head"] = res["embed"]
+    return res
+
+
 def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.bfloat16,
                      layers: Optional[Iterable[int]] = None, embed: bool = True, head: bool = True,
                      tp_rank: int = 0, tp_size: int = 1, ep_rank: int = 0, ep_size: int = 1) -> Weights:
@@ -336,22 +398,8 @@ def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.b
                     t = sl[rows] if cols is None else sl[:, cols]
                     t = t.contiguous()
                     sharded.add(iname)
-                if role == "conv1d":
-                    t = t.t().contiguous()
-                if role == "copy":
-                    out[iname] = t
-                else:
-                    parts.setdefault(iname, {})[role] = t
-    for iname, p in parts.items():
-        base = iname.split(".")[-1]
-        if base in ("qkv_w", "qkv_b"):
-            out[iname] = torch.cat([p["q"], p["k"], p["v"]], 0)
-        elif base in ("gate_up_w", "shared_gate_up_w"):
-            out[iname] = interleave_gate_up(p["gate"], p["up"])
-        elif base == "experts_gate_up_w":
-            out[iname] = torch.stack([interleave_gate_up(p[f"egate:{e}"], p[f"eup:{e}"]) for e in sorted(own_experts)])
-        elif base == "experts_down_w":
-            out[iname] = torch.stack([p[f"edown:{e}"] for e in sorted(own_experts)])
+                _place(out, parts, iname, role, t)
+    _fuse_parts(out, parts, own_experts)
     if head and "lm_head" not in out and "embed" in out:
         out["lm_head"] = out["embed"]
     if not embed:

@@ -140,12 +140,75 @@ def layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, *,
 
 
 # --------------------------------------------------------------------------- RoPE
-def rope_cos_sin(max_pos: int, rot_dim: int, theta: float, device=None) -> torch.Tensor:
-    """[max_pos, rot_dim] fp32 table = [cos(p * f_i) | sin(p * f_i)], f_i = theta^(-2i/rot_dim)."""
-    inv = 1.0 / (theta ** (torch.arange(0, rot_dim, 2, dtype=torch.float64) / rot_dim))
+def rope_inv_freq(rot_dim: int, theta: float, scaling=None, max_pos: int = 0):
+    """RoPE frequencies f_i = theta^(-2i/rot_dim), i < rot_dim/2, rescaled for long
+    context, and the factor the cos / sin table is multiplied by.
+
+    `scaling` is a mapping (or (key, value) pairs) of HF rope parameters:
+      linear   f_i / factor (position interpolation)
+      llama3   frequencies with wavelength above original_ctx / low_freq_factor divided
+               by factor, below original_ctx / high_freq_factor kept, a linear blend of
+               the two in between (the Llama 3.1 rule)
+      yarn     NTK-by-parts (Peng et al., "YaRN", 2023): dimensions that turn fewer than
+               beta_slow times over the original context are interpolated (f / factor),
+               more than beta_fast times extrapolated (f), a linear ramp between; the
+               table is scaled by 0.1 ln(factor) + 1 (or the mscale / mscale_all_dim
+               ratio, or attention_factor)
+      dynamic  the unscaled frequencies: NTK re-basing that depends on the current
+               sequence length cannot live in one static table; exact while sequences
+               stay within original_max_position_embeddings
+    Returns (float64 tensor [rot_dim / 2], float table factor)."""
+    i2 = torch.arange(0, rot_dim, 2, dtype=torch.float64) / rot_dim
+    inv = 1.0 / (theta ** i2)
+    sc = dict(scaling or {})
+    kind = sc.get("rope_type", sc.get("type", "default"))
+    if kind in ("default", "dynamic", None):
+        return inv, 1.0
+    factor = float(sc.get("factor", 1.0))
+    if kind == "linear":
+        return inv / factor, 1.0
+    orig = float(sc.get("original_max_position_embeddings") or max_pos)
+    if kind == "llama3":
+        lo, hi = float(sc.get("low_freq_factor", 1.0)), float(sc.get("high_freq_factor", 4.0))
+        wavelen = 2 * math.pi / inv
+        smooth = ((orig / wavelen - lo) / (hi - lo)).clamp(0.0, 1.0)
+        blended = (1 - smooth) * inv / factor + smooth * inv
+        return torch.where(wavelen > orig / lo, inv / factor, torch.where(wavelen < orig / hi, inv, blended)), 1.0
+    if kind == "yarn":
+        if "factor" not in sc and max_pos and orig:
+            factor = max_pos / orig
+        beta_fast, beta_slow = float(sc.get("beta_fast", 32.0)), float(sc.get("beta_slow", 1.0))
+
+        def dim_of(turns):      # dimension index whose frequency turns `turns` times over orig
+            return rot_dim * math.log(orig / (turns * 2 * math.pi)) / (2 * math.log(theta))
+
+        lo = max(math.floor(dim_of(beta_fast)), 0)
+        hi = min(math.ceil(dim_of(beta_slow)), rot_dim - 1)
+        if hi == lo:
+            hi += 0.001
+        ramp = ((torch.arange(rot_dim // 2, dtype=torch.float64) - lo) / (hi - lo)).clamp(0.0, 1.0)
+        inv = (inv / factor) * ramp + inv * (1 - ramp)
+
+        def mscale(s, m=1.0):
+            return 1.0 if s <= 1 else 0.1 * m * math.log(s) + 1.0
+
+        att = sc.get("attention_factor")
+        if att is None:
+            if sc.get("mscale") and sc.get("mscale_all_dim"):
+                att = mscale(factor, float(sc["mscale"])) / mscale(factor, float(sc["mscale_all_dim"]))
+            else:
+                att = mscale(factor)
+        return inv, float(att)
+    raise ValueError(f"unsupported rope scaling {kind!r} (linear, llama3, yarn, dynamic)")
+
+
+def rope_cos_sin(max_pos: int, rot_dim: int, theta: float, device=None, scaling=None) -> torch.Tensor:
+    """[max_pos, rot_dim] fp32 table = [cos(p * f_i) | sin(p * f_i)] x table factor, with
+    the frequencies and factor of `rope_inv_freq` (f_i = theta^(-2i/rot_dim) unscaled)."""
+    inv, att = rope_inv_freq(rot_dim, theta, scaling, max_pos)
     p = torch.arange(max_pos, dtype=torch.float64)
     ang = torch.outer(p, inv)
-    return torch.cat([ang.cos(), ang.sin()], dim=1).to(torch.float32).to(device)
+    return (torch.cat([ang.cos(), ang.sin()], dim=1) * att).to(torch.float32).to(device)
 
 
 def _fp8_dtype():

@@ -30,8 +30,7 @@ from typing import Any, Dict, Iterator, List, Optional, Sequence, Union
 import torch
 
 from .engine.engine import LLMEngine, Request, SamplingParams
-from .engine.runner import ModelRunner, PrefillItem
-from .kv.paged import PagedKVCacheManager
+from .engine.runner import PrefillItem
 from .llm import LLM
 from .models.config import get_config
 from .serving.tokenizer import load_tokenizer
@@ -135,20 +134,12 @@ class InferencePipeline:
 
     def _build_pp(self, cfg, n, max_batch, max_model_len, kv_pages, kvd, dtype, **kw) -> LLM:
         from .kv.pool import kv_dtype_from_str
-        from .parallel.pipeline import build_local_pipeline
         from .parallel.placement import detect_gpus, split_model_into_blocks
         devs = [f"cuda:{i}" for i in range(n)]
         blocks = split_model_into_blocks(cfg, devs, gpus=detect_gpus()[:n])
         pages = kv_pages or max_batch * ((max_model_len + 15) // 16) + 16
-        pipe = build_local_pipeline(cfg, blocks, num_pages=pages, dtype=dtype, kv_dtype=kv_dtype_from_str(kvd))
-        llm = LLM.__new__(LLM)
-        llm.cfg, llm.device, llm.model, llm.pool = cfg, pipe.device, pipe, None
-        llm.kv = PagedKVCacheManager(pages)
-        llm.runner = ModelRunner(pipe, None, max_batch=max_batch, max_model_len=max_model_len, use_cuda_graph=False)
-        llm.engine = LLMEngine(llm.runner, llm.kv)
-        llm.weights = None
-        llm.tp = None
-        return llm
+        return LLM.from_local_pipeline(cfg, blocks, num_pages=pages, max_batch=max_batch, max_model_len=max_model_len,
+                                       dtype=dtype, kv_dtype=kv_dtype_from_str(kvd))
 
     # ------------------------------------------------------------------ engine loop
     def start(self) -> None:
