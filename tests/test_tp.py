@@ -31,7 +31,7 @@ def _torchrun(nproc, args, env_extra=None, timeout=600):
     return json.loads(line)
 
 
-@pytest.mark.parametrize("model", ["tiny-qwen2", "tiny-gpt2"])
+@pytest.mark.parametrize("model", ["tiny-qwen2", "tiny-gpt2", "tiny-qwen3"])
 def test_tp2_matches_tp1_cpu_gloo(model):
     res = _torchrun(2, ["--model", model, "--device", "cpu"], {"CUDA_VISIBLE_DEVICES": ""})
     assert res["world"] == 2

@@ -23,15 +23,16 @@ __version__ = "0.1.0"
 
 # `-q` accepts the reference's names too.  nf4 / int8 are served by the formats the B200
 # tensor cores run natively (4-bit NVFP4, 8-bit FP8 e4m3 W8A8); gptq / awq name
-# pre-quantised checkpoint layouts, which this loader does not read.
+# pre-quantised checkpoint layouts, which the loader recognises from the checkpoint's
+# quantization_config and dequantises at load (add -q fp8 / nvfp4 to re-quantise).
 QUANT_CHOICES = ["nvfp4", "fp8", "none", "nf4", "int8", "gptq", "awq"]
 _QUANT_ALIASES = {"nf4": "nvfp4", "int8": "fp8"}
 
 
 def resolve_quantization(q):
     if q in ("gptq", "awq"):
-        raise SystemExit(f"-q {q}: pre-quantised {q.upper()} checkpoints are not read by this loader; load the "
-                         f"bf16 checkpoint with -q nvfp4 (4-bit) or -q fp8 (8-bit) instead")
+        print(f"-q {q}: the checkpoint's {q.upper()} tensors are dequantised at load (bf16 weights)")
+        return None
     if q in _QUANT_ALIASES:
         print(f"-q {q}: using {_QUANT_ALIASES[q]} (the B200-native {'4' if q == 'nf4' else '8'}-bit weight format)")
         return _QUANT_ALIASES[q]

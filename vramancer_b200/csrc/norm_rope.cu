@@ -276,6 +276,52 @@ void rope_kv_write(const RopeKvArgs& a_in, cudaStream_t st) {
   VRM_CUDA_CHECK(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------- per-head q / k RMSNorm
+// Qwen3's q_norm / k_norm: every q head and k head row of qkv [T, (Hq + 2 KH) * D] is
+// normalised in place, x[d] = x[d] * rsqrt(mean(x^2) + eps) * w[d] (fp32 math, one bf16
+// rounding), w = wq [D] for q heads and wk [D] for k heads; v heads are untouched.  One
+// warp per head row, lane j holding dims j, j + 32, ... (coalesced); runs between the
+// QKV projection and RoPE.
+template <int kPer>
+__global__ void qk_rmsnorm_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ld, const __nv_bfloat16* __restrict__ wq,
+                                  const __nv_bfloat16* __restrict__ wk, int Hq, int KH, float eps) {
+  pdl_launch();
+  pdl_wait_for(qkv, wq, wk);
+  constexpr int D = kPer * 32;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int h = warp; h < Hq + KH; h += nwarps) {
+    __nv_bfloat16* row = qkv + (size_t)t * ld + (size_t)h * D;
+    const __nv_bfloat16* w = h < Hq ? wq : wk;
+    float v[kPer];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      v[j] = __bfloat162float(row[lane + 32 * j]);
+      ss += v[j] * v[j];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss * (1.f / D) + eps);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) row[lane + 32 * j] = __float2bfloat16(v[j] * r * __bfloat162float(w[lane + 32 * j]));
+  }
+}
+
+void qk_rmsnorm(void* qkv, int64_t ld, const void* wq, const void* wk, int T, int Hq, int KH, int D, float eps,
+                cudaStream_t st) {
+  if (T <= 0) return;
+  VRM_REQUIRE(D == 64 || D == 128 || D == 256, "qk_rmsnorm: head_dim must be 64, 128 or 256");
+  auto q = static_cast<__nv_bfloat16*>(qkv);
+  auto a = static_cast<const __nv_bfloat16*>(wq);
+  auto b = static_cast<const __nv_bfloat16*>(wk);
+  const int threads = 32 * std::min(16, Hq + KH);
+  if (D == 64) launch_kernel(qk_rmsnorm_kernel<2>, dim3(T), dim3(threads), 0, st, q, ld, a, b, Hq, KH, eps);
+  else if (D == 128) launch_kernel(qk_rmsnorm_kernel<4>, dim3(T), dim3(threads), 0, st, q, ld, a, b, Hq, KH, eps);
+  else launch_kernel(qk_rmsnorm_kernel<8>, dim3(T), dim3(threads), 0, st, q, ld, a, b, Hq, KH, eps);
+  VRM_CUDA_CHECK(cudaGetLastError());
+}
+
 // ---------------------------------------------------------------- activations
 // out[t, i] = silu(x[t, i]) * x[t, I + i]   (gate | up concatenated)
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out, int I,

@@ -211,6 +211,18 @@ void rope_kv_write(Tensor& qkv, const OptT& positions, const OptT& cos_sin, Tens
   vrm::rope_kv_write(a, cur_stream());
 }
 
+void qk_rmsnorm(Tensor& qkv, const Tensor& wq, const Tensor& wk, int64_t Hq, int64_t KH, int64_t D, double eps) {
+  check_bf16_2d(qkv, "qk_rmsnorm qkv");
+  TORCH_CHECK(qkv.size(1) == (Hq + 2 * KH) * D, "qk_rmsnorm: qkv width must be (Hq + 2 KH) * D");
+  for (const Tensor* w : {&wq, &wk})
+    TORCH_CHECK(w->scalar_type() == torch::kBFloat16 && w->is_contiguous() && w->numel() == D,
+                "qk_rmsnorm: norm weights must be contiguous bf16 [head_dim]");
+  same_device(qkv, {&wq, &wk}, "qk_rmsnorm");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  vrm::qk_rmsnorm(qkv.data_ptr(), qkv.stride(0), wq.data_ptr(), wk.data_ptr(), (int)qkv.size(0), (int)Hq, (int)KH,
+                  (int)D, (float)eps, cur_stream());
+}
+
 // ---------------------------------------------------------------- elementwise
 void silu_mul(const Tensor& x, Tensor& out) {
   check_bf16_2d(x, "silu_mul x");
@@ -1222,6 +1234,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"));
   m.def("layernorm", &layernorm, py::arg("x"), py::arg("residual"), py::arg("w"), py::arg("b"), py::arg("out"),
         py::arg("eps"));
+  m.def("qk_rmsnorm", &qk_rmsnorm, py::arg("qkv"), py::arg("wq"), py::arg("wk"), py::arg("num_q_heads"),
+        py::arg("num_kv_heads"), py::arg("head_dim"), py::arg("eps"));
   m.def("rope_kv_write", &rope_kv_write, py::arg("qkv"), py::arg("positions"), py::arg("cos_sin"), py::arg("cache"),
         py::arg("slot_mapping"), py::arg("kv_scale"), py::arg("layer"), py::arg("num_q_heads"),
         py::arg("num_kv_heads"), py::arg("head_dim"));

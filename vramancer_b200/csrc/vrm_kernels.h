@@ -345,6 +345,9 @@ struct RopeKvArgs {
   uint32_t* err = nullptr;             // error word (set by rope_kv_write)
 };
 void rope_kv_write(const RopeKvArgs& a, cudaStream_t stream);
+// per-head RMSNorm of the q and k heads of qkv [T, ld] in place (Qwen3 q_norm / k_norm)
+void qk_rmsnorm(void* qkv, int64_t ld, const void* wq, const void* wk, int T, int Hq, int KH, int D, float eps,
+                cudaStream_t stream);
 
 void silu_mul(const void* x, int64_t ldx, void* out, int64_t ldo, int T, int I, cudaStream_t stream);
 void gelu_tanh(void* x, size_t n, cudaStream_t stream);

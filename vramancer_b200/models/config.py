@@ -2,9 +2,13 @@
 
 One `ModelConfig` covers the decoder-only families the reference serves through HF
 (core/backends.py:1185-1412): Llama / Qwen2 / Mistral (RMSNorm, RoPE, GQA, SwiGLU),
-GPT-2 (LayerNorm, learned positions, GELU, fused c_attn) and Qwen-MoE style decoders
-(top-k softmax router over SwiGLU experts).  `from_hf_config` reads an HF
-`config.json` so checkpoints load without transformers.
+Qwen3 (the same plus a per-head RMSNorm of q and k), GPT-2 (LayerNorm, learned
+positions, GELU, fused c_attn) and mixture-of-experts decoders (top-k softmax router
+over SwiGLU experts: Qwen2-MoE with a gated shared expert, Qwen3-MoE, Mixtral).  RoPE
+scaling (linear, Llama 3, YaRN) is part of the config.  `from_hf_config` reads an HF
+`config.json` so checkpoints load without transformers, and raises
+`UnsupportedArchitecture` for anything else (the backend factory then picks another
+backend rather than run a different model).
 """
 from __future__ import annotations
 
@@ -14,9 +18,14 @@ from dataclasses import asdict, dataclass, field, replace
 from typing import Any, Dict, Optional, Tuple
 
 
+class UnsupportedArchitecture(ValueError):
+    """An HF config the native engine does not implement (the backend factory then
+    serves the model through another backend)."""
+
+
 @dataclass(frozen=True)
 class ModelConfig:
-    arch: str = "qwen2"              # qwen2 | llama | mistral | gpt2 | qwen2_moe
+    arch: str = "qwen2"              # qwen2 | qwen3 | llama | mistral | gpt2 | qwen2_moe
     vocab_size: int = 152064
     hidden_size: int = 5120
     num_layers: int = 48
@@ -32,6 +41,7 @@ class ModelConfig:
     # ("rope_type" linear | llama3 | yarn | dynamic, "factor", ...); None = plain RoPE
     rope_scaling: Optional[Tuple[Tuple[str, Any], ...]] = None
     qkv_bias: bool = True
+    qk_norm: bool = False                # per-head RMSNorm of q and k before RoPE (Qwen3)
     tie_embeddings: bool = False
     # MoE
     num_experts: int = 0
@@ -121,20 +131,39 @@ class ModelConfig:
         prf = cfg.get("partial_rotary_factor") or (cfg.get("rope_parameters") or {}).get("partial_rotary_factor")
         rot = int(hd * prf) if prf else None
         arch = {"qwen2": "qwen2", "llama": "llama", "mistral": "mistral", "qwen2_moe": "qwen2_moe",
-                "qwen3_moe": "qwen2_moe"}.get(mt, "llama")
+                "qwen3": "qwen3", "qwen3_moe": "qwen2_moe", "mixtral": "qwen2_moe"}.get(mt)
+        if arch is None:
+            raise UnsupportedArchitecture(f"model_type {mt!r} is not implemented by the native engine")
+        act = cfg.get("hidden_act", "silu")
+        if act not in ("silu", "swish"):
+            raise UnsupportedArchitecture(f"hidden_act {act!r} (the native SwiGLU MLP needs silu)")
+        if cfg.get("mlp_bias"):
+            raise UnsupportedArchitecture("MLP biases are not implemented by the native engine")
+        if mt in ("qwen2_moe", "qwen3_moe") and (cfg.get("mlp_only_layers") or cfg.get("decoder_sparse_step", 1) != 1):
+            raise UnsupportedArchitecture("MoE models with dense layers between sparse ones are not implemented")
         moe = {}
         if arch == "qwen2_moe":
-            moe = dict(num_experts=cfg.get("num_experts", 0), experts_per_token=cfg.get("num_experts_per_tok", 0),
-                       expert_intermediate_size=cfg.get("moe_intermediate_size", 0),
+            # transformers 5 writes num_local_experts for Qwen3-MoE (Mixtral always did);
+            # Mixtral's experts are intermediate_size wide and its top-k weights renormalised
+            moe = dict(num_experts=cfg.get("num_experts") or cfg.get("num_local_experts") or 0,
+                       experts_per_token=cfg.get("num_experts_per_tok", 0),
+                       expert_intermediate_size=cfg.get("moe_intermediate_size") or cfg.get("intermediate_size", 0),
                        shared_expert_intermediate_size=cfg.get("shared_expert_intermediate_size", 0),
-                       norm_topk_prob=cfg.get("norm_topk_prob", True))
+                       norm_topk_prob=True if mt == "mixtral" else cfg.get("norm_topk_prob", True))
+        max_pos = cfg.get("max_position_embeddings", 32768)
+        sw = cfg.get("sliding_window")
+        if sw and cfg.get("use_sliding_window", True) and sw < max_pos:
+            # sliding-window attention equals full attention while a sequence fits in
+            # the window: the context is capped there instead of running SWA
+            max_pos = int(sw)
         return ModelConfig(arch=arch, vocab_size=cfg["vocab_size"], hidden_size=H,
                            num_layers=cfg["num_hidden_layers"], num_heads=nh, num_kv_heads=kvh, head_dim=hd,
                            intermediate_size=cfg.get("intermediate_size", 4 * H),
-                           max_position=cfg.get("max_position_embeddings", 32768),
+                           max_position=max_pos,
                            norm_eps=cfg.get("rms_norm_eps", 1e-6), rope_theta=float(theta), rotary_dim=rot,
                            rope_scaling=scaling,
-                           qkv_bias=bool(cfg.get("attention_bias", arch in ("qwen2", "qwen2_moe"))),
+                           qkv_bias=bool(cfg.get("attention_bias", mt in ("qwen2", "qwen2_moe"))),
+                           qk_norm=mt in ("qwen3", "qwen3_moe"),
                            tie_embeddings=bool(cfg.get("tie_word_embeddings", False)), name=name, **moe)
 
     @staticmethod
@@ -159,8 +188,13 @@ class ModelConfig:
             d["rope_scaling"] = dict(self.rope_scaling)
         if self.rotary_dim is not None and self.rotary_dim != self.head_dim:
             d["partial_rotary_factor"] = self.rotary_dim / self.head_dim
+        if self.qk_norm:
+            d["model_type"] = "qwen3_moe" if self.is_moe else "qwen3"
+            d["attention_bias"] = self.qkv_bias
         if self.arch == "qwen2":
             d["architectures"] = ["Qwen2ForCausalLM"]
+        elif self.arch == "qwen3":
+            d["architectures"] = ["Qwen3ForCausalLM"]
         elif self.arch in ("llama", "mistral"):
             d["architectures"] = ["LlamaForCausalLM"] if self.arch == "llama" else ["MistralForCausalLM"]
             d["attention_bias"] = self.qkv_bias
@@ -168,7 +202,8 @@ class ModelConfig:
             d.update(num_experts=self.num_experts, num_experts_per_tok=self.experts_per_token,
                      moe_intermediate_size=self.expert_intermediate_size,
                      shared_expert_intermediate_size=self.shared_expert_intermediate_size,
-                     norm_topk_prob=self.norm_topk_prob, architectures=["Qwen2MoeForCausalLM"])
+                     norm_topk_prob=self.norm_topk_prob,
+                     architectures=["Qwen3MoeForCausalLM" if self.qk_norm else "Qwen2MoeForCausalLM"])
         return d
 
 
@@ -192,7 +227,30 @@ PRESETS: Dict[str, ModelConfig] = {
                                 max_position=32768, norm_eps=1e-6, rope_theta=1_000_000.0, qkv_bias=False,
                                 num_experts=128, experts_per_token=8, expert_intermediate_size=768,
                                 norm_topk_prob=True, name="moe-48l-128e"),
+    # further families served natively (random-init presets for the workloads)
+    "qwen3-8b": ModelConfig(arch="qwen3", vocab_size=151936, hidden_size=4096, num_layers=36, num_heads=32,
+                            num_kv_heads=8, head_dim=128, intermediate_size=12288, max_position=40960,
+                            norm_eps=1e-6, rope_theta=1_000_000.0, qkv_bias=False, qk_norm=True, name="qwen3-8b"),
+    "qwen3-30b-a3b": ModelConfig(arch="qwen2_moe", vocab_size=151936, hidden_size=2048, num_layers=48,
+                                 num_heads=32, num_kv_heads=4, head_dim=128, intermediate_size=6144,
+                                 max_position=40960, norm_eps=1e-6, rope_theta=1_000_000.0, qkv_bias=False,
+                                 qk_norm=True, num_experts=128, experts_per_token=8, expert_intermediate_size=768,
+                                 norm_topk_prob=True, name="qwen3-30b-a3b"),
+    "llama-3.1-8b": ModelConfig(arch="llama", vocab_size=128256, hidden_size=4096, num_layers=32, num_heads=32,
+                                num_kv_heads=8, head_dim=128, intermediate_size=14336, max_position=131072,
+                                norm_eps=1e-5, rope_theta=500_000.0, qkv_bias=False,
+                                rope_scaling=(("factor", 8.0), ("high_freq_factor", 4.0), ("low_freq_factor", 1.0),
+                                              ("original_max_position_embeddings", 8192), ("rope_type", "llama3")),
+                                name="llama-3.1-8b"),
+    "mixtral-8x7b": ModelConfig(arch="qwen2_moe", vocab_size=32000, hidden_size=4096, num_layers=32, num_heads=32,
+                                num_kv_heads=8, head_dim=128, intermediate_size=14336, max_position=32768,
+                                norm_eps=1e-5, rope_theta=1_000_000.0, qkv_bias=False, num_experts=8,
+                                experts_per_token=2, expert_intermediate_size=14336, norm_topk_prob=True,
+                                name="mixtral-8x7b"),
     # small shapes for tests
+    "tiny-qwen3": ModelConfig(arch="qwen3", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
+                              num_kv_heads=2, head_dim=64, intermediate_size=512, max_position=2048,
+                              norm_eps=1e-6, rope_theta=10000.0, qkv_bias=False, qk_norm=True, name="tiny-qwen3"),
     "tiny-qwen2": ModelConfig(arch="qwen2", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
                               num_kv_heads=2, head_dim=64, intermediate_size=512, max_position=2048,
                               norm_eps=1e-6, rope_theta=10000.0, qkv_bias=True, name="tiny-qwen2"),
@@ -220,6 +278,9 @@ PRESETS: Dict[str, ModelConfig] = {
 ALIASES = {
     "Qwen/Qwen2.5-14B": "qwen2.5-14b", "Qwen/Qwen2.5-14B-Instruct": "qwen2.5-14b",
     "Qwen/Qwen2.5-7B": "qwen2.5-7b", "Qwen/Qwen2.5-7B-Instruct": "qwen2.5-7b",
+    "Qwen/Qwen3-8B": "qwen3-8b", "Qwen/Qwen3-30B-A3B": "qwen3-30b-a3b",
+    "meta-llama/Llama-3.1-8B": "llama-3.1-8b", "meta-llama/Llama-3.1-8B-Instruct": "llama-3.1-8b",
+    "mistralai/Mixtral-8x7B-v0.1": "mixtral-8x7b", "mistralai/Mixtral-8x7B-Instruct-v0.1": "mixtral-8x7b",
     "openai-community/gpt2": "gpt2", "qwen2.5-14b-arch": "qwen2.5-14b", "qwen2.5-7b-arch": "qwen2.5-7b",
 }
 

@@ -197,6 +197,8 @@ class DecoderModel:
         cfg = self.cfg
         hq, kvh, D = self.hq, self.kvh, self.D
         qkv = self._in_proj(x, r, self.lw(i, "qkv_w"), self.lw(i, "qkv_b"))
+        if cfg.qk_norm:          # Qwen3: per-head RMSNorm of q and k before RoPE
+            ops.qk_rmsnorm(qkv, self.lw(i, "q_norm_w"), self.lw(i, "k_norm_w"), hq, kvh, D, cfg.norm_eps)
         li = i - self.first_layer
         if getattr(pool, "is_tq", False):
             return self._attention_tq(qkv, batch, pool, li)

@@ -49,6 +49,9 @@ def layer_shapes(cfg: ModelConfig, tp_rank: int = 0, tp_size: int = 1) -> Dict[s
     }
     if cfg.qkv_bias:
         s["qkv_b"] = ((hq + 2 * kvh) * D,)
+    if cfg.qk_norm:
+        s["q_norm_w"] = (D,)
+        s["k_norm_w"] = (D,)
     if cfg.is_gpt2:
         I = cfg.intermediate_size // tp_size
         s.update({"in_norm_b": (H,), "post_norm_b": (H,), "o_b": (H,), "fc_w": (I, H), "fc_b": (I,),
@@ -219,6 +222,7 @@ def _hf_map(cfg: ModelConfig, name: str) -> Optional[Tuple[str, str]]:
     rest = ".".join(parts[3:])
     pre = f"layers.{i}."
     simple = {"input_layernorm.weight": ("in_norm_w", "copy"),
+              "self_attn.q_norm.weight": ("q_norm_w", "copy"), "self_attn.k_norm.weight": ("k_norm_w", "copy"),
               "post_attention_layernorm.weight": ("post_norm_w", "copy"),
               "self_attn.o_proj.weight": ("o_w", "copy"),
               "self_attn.q_proj.weight": ("qkv_w", "q"), "self_attn.k_proj.weight": ("qkv_w", "k"),
@@ -233,12 +237,16 @@ def _hf_map(cfg: ModelConfig, name: str) -> Optional[Tuple[str, str]]:
     if rest in simple:
         n, role = simple[rest]
         return pre + n, role
-    if rest.startswith("mlp.experts."):
+    if rest == "block_sparse_moe.gate.weight":                 # Mixtral router
+        return pre + "router_w", "copy"
+    if rest.startswith("mlp.experts.") or rest.startswith("block_sparse_moe.experts."):
         e = rest.split(".")[2]
         tail = ".".join(rest.split(".")[3:])
-        m = {"gate_proj.weight": ("experts_gate_up_w", f"egate:{e}"),
-             "up_proj.weight": ("experts_gate_up_w", f"eup:{e}"),
-             "down_proj.weight": ("experts_down_w", f"edown:{e}")}.get(tail)
+        # Qwen-MoE names, and Mixtral's w1 (gate) / w3 (up) / w2 (down)
+        m = {"gate_proj.weight": ("experts_gate_up_w", f"egate:{e}"), "w1.weight": ("experts_gate_up_w", f"egate:{e}"),
+             "up_proj.weight": ("experts_gate_up_w", f"eup:{e}"), "w3.weight": ("experts_gate_up_w", f"eup:{e}"),
+             "down_proj.weight": ("experts_down_w", f"edown:{e}"),
+             "w2.weight": ("experts_down_w", f"edown:{e}")}.get(tail)
         if m:
             return pre + m[0], m[1]
     return None
@@ -341,6 +349,33 @@ def weights_from_state_dict(cfg: ModelConfig, state_dict, *, device="cpu", dtype
     return res
 
 
+def _quantization_config(path: str) -> Optional[dict]:
+    """The checkpoint's GPTQ / AWQ quantization_config (None for dense checkpoints and
+    for the NVFP4 layouts, which are read tensor by tensor)."""
+    fn = os.path.join(path, "config.json")
+    if not os.path.exists(fn):
+        return None
+    with open(fn) as f:
+        qc = json.load(f).get("quantization_config")
+    if not qc or str(qc.get("quant_method", "")).lower() not in ("gptq", "awq"):
+        return None
+    from ..quant import int4_ckpt
+    int4_ckpt.check_config(qc)
+    return qc
+
+
+def _wanted(cfg: ModelConfig, m: Tuple[str, str], want_layers, embed: bool, head: bool, own_experts) -> bool:
+    iname, role = m
+    if iname.startswith("layers."):
+        if int(iname.split(".")[1]) not in want_layers:
+            return False
+    elif iname in ("embed", "pos_embed") and not embed and not (head and cfg.tie_embeddings):
+        return False
+    elif iname in ("final_norm_w", "final_norm_b", "lm_head") and not head:
+        return False
+    return not (":" in role and int(role.split(":")[1]) not in own_experts)
+
+
 def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.bfloat16,
                      layers: Optional[Iterable[int]] = None, embed: bool = True, head: bool = True,
                      tp_rank: int = 0, tp_size: int = 1, ep_rank: int = 0, ep_size: int = 1) -> Weights:
@@ -351,23 +386,32 @@ def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.b
     expert-parallel ranks only their experts, so no rank reads the whole checkpoint.
     Projections stored NVFP4-quantised (the reference's DirectFP4Linear buffers
     w_qdata / w_scale / w_per_tensor_scale, or ModelOpt weight / weight_scale /
-    weight_scale_2) load as NVFP4Weight without re-quantisation."""
+    weight_scale_2) load as NVFP4Weight without re-quantisation.  GPTQ / AWQ checkpoints
+    (quantization_config in config.json) are dequantised per linear layer
+    (quant/int4_ckpt.py) into the dense layout."""
     from safetensors import safe_open
 
     want_layers = set(range(cfg.num_layers) if layers is None else layers)
     files = sorted(f for f in os.listdir(path) if f.endswith(".safetensors"))
     if not files:
         raise FileNotFoundError(f"no .safetensors files in {path}")
+    qc = _quantization_config(path)
     n_exp = cfg.num_experts // ep_size if cfg.is_moe else 0
     own_experts = set(range(ep_rank * n_exp, (ep_rank + 1) * n_exp))
     parts: Dict[str, Dict[str, torch.Tensor]] = {}
     nv_parts: Dict[str, Dict[str, Dict[str, torch.Tensor]]] = {}
+    int_parts: Dict[Tuple[str, str], Dict[str, torch.Tensor]] = {}
     out: Weights = {}
     sharded = set()
     for fn in files:
         with safe_open(os.path.join(path, fn), framework="pt", device="cpu") as f:
             for name in f.keys():
                 mod, _, leaf = name.rpartition(".")
+                if qc is not None and leaf in ("qweight", "qzeros", "scales", "g_idx"):
+                    m = _hf_map(cfg, mod + ".weight")
+                    if m is not None and _wanted(cfg, m, want_layers, embed, head, own_experts):
+                        int_parts.setdefault(m, {})[leaf] = f.get_tensor(name)
+                    continue
                 nv_part = _NVFP4_SUFFIX.get(leaf, "") if leaf in _NVFP4_SUFFIX else ""
                 if nv_part is None:
                     continue                     # activation scale: not used
@@ -399,6 +443,11 @@ def load_safetensors(path: str, cfg: ModelConfig, *, device="cpu", dtype=torch.b
                     t = t.contiguous()
                     sharded.add(iname)
                 _place(out, parts, iname, role, t)
+    if int_parts:
+        from ..quant import int4_ckpt
+        for (iname, role), pp in int_parts.items():
+            w = int4_ckpt.dequantize_module(qc, pp)
+            _place(out, parts, iname, role, w.t() if role == "conv1d" else w)
     _fuse_parts(out, parts, own_experts)
     if head and "lm_head" not in out and "embed" in out:
         out["lm_head"] = out["embed"]

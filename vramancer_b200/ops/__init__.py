@@ -140,6 +140,22 @@ def layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float, *,
 
 
 # --------------------------------------------------------------------------- RoPE
+def qk_rmsnorm(qkv: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+               head_dim: int, eps: float) -> None:
+    """Per-head RMSNorm of the q and k heads of qkv [T, (Hq + 2 KH) * D] in place
+    (Qwen3 q_norm / k_norm; v heads untouched)."""
+    if qkv.is_cuda:
+        native().qk_rmsnorm(qkv, wq, wk, num_q_heads, num_kv_heads, head_dim, eps)
+        return
+    T = qkv.shape[0]
+    Hq, KH, D = num_q_heads, num_kv_heads, head_dim
+    v = qkv.view(T, Hq + 2 * KH, D)
+    for sl, w in ((slice(0, Hq), wq), (slice(Hq, Hq + KH), wk)):
+        h = v[:, sl].float()
+        y = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+        v[:, sl] = y.to(qkv.dtype)
+
+
 def rope_inv_freq(rot_dim: int, theta: float, scaling=None, max_pos: int = 0):
     """RoPE frequencies f_i = theta^(-2i/rot_dim), i < rot_dim/2, rescaled for long
     context, and the factor the cos / sin table is multiplied by.
