@@ -36,6 +36,7 @@ import json
 import random
 import statistics
 import time
+from contextlib import nullcontext
 from typing import List, Optional
 
 import torch
@@ -291,7 +292,11 @@ def run_prefill(args, info, dev, tp) -> dict:
         prompts = [[rng.randrange(vocab) for _ in range(S)] for _ in range(B)]
         reqs = [llm.engine.add_request(p, params) for p in prompts]
         tm = _Timer(dev)
-        llm.engine.step()          # one step: the whole batch in one prefill chunk
+        # NVTX range "vrm_prefill" around the measured steps: a launch list of one prefill
+        # is `ncu --nvtx --nvtx-include "vrm_prefill/" --metrics gpu__time_duration.sum`
+        rng_ctx = torch.cuda.nvtx.range("vrm_prefill") if (dev.type == "cuda" and it >= args.warmup) else nullcontext()
+        with rng_ctx:
+            llm.engine.step()          # one step: the whole batch in one prefill chunk
         dt = tm.stop()
         while llm.engine.has_unfinished():
             llm.engine.step()
