@@ -286,3 +286,30 @@ def test_graph_verify_on_gpu_forced_acceptance(cuda_errors_clean):
     # the eager verify's GEMMs see other token counts than the decode steps that made
     # the continuation, so bf16 near-ties flip more often there (measured 0.90-1.0)
     assert g_acc >= 0.9 and e_acc >= 0.75 and agree >= 0.9, (g_acc, e_acc, agree)
+
+
+def test_draft_model_map_picks_family_defaults():
+    from vramancer_b200.engine.speculative import guess_draft_model
+    assert guess_draft_model("Qwen/Qwen2.5-14B-Instruct") == "Qwen/Qwen2.5-0.5B-Instruct"
+    assert guess_draft_model("qwen2.5-14b") == "qwen2.5-0.5b"
+    assert guess_draft_model("meta-llama/Llama-3.1-8B") == "meta-llama/Llama-3.2-1B"
+    assert guess_draft_model("gpt2") == "distilgpt2"
+    assert guess_draft_model("qwen2.5-0.5b") is None            # never the target itself
+    assert guess_draft_model("tiny-qwen2") is None
+
+
+def test_pipeline_enable_speculative_uses_the_draft_model(monkeypatch):
+    """VRM_DRAFT_MODEL names the draft; generate(enable_speculative=True) runs draft-model
+    speculation and, greedy, returns the target's own tokens."""
+    from vramancer_b200.pipeline import InferencePipeline
+    monkeypatch.setenv("VRM_DRAFT_MODEL", "tiny-qwen2")       # same weights as the target: all accepted
+    pipe = InferencePipeline(enable_metrics=False).load("tiny-qwen2", device="cpu", max_model_len=128, max_batch=2)
+    try:
+        prompt = list(range(5, 25))
+        plain = pipe.generate(prompt, max_new_tokens=12, return_ids=True)
+        spec = pipe.generate(prompt, max_new_tokens=12, return_ids=True, enable_speculative=True)
+        assert spec == plain
+        st = pipe._draft.stats
+        assert st.proposed > 0 and st.accepted == st.proposed
+    finally:
+        pipe.shutdown()

@@ -308,6 +308,33 @@ def _full_logits(llm, seq: Sequence[int]) -> torch.Tensor:
             eng.kv.free(rid)
 
 
+# default small draft model per target-model family, by name prefix (the reference's
+# choices; a draft must share the target's tokenizer)
+DRAFT_MODEL_MAP = (
+    ("Qwen/Qwen2.5-", "Qwen/Qwen2.5-0.5B-Instruct"),
+    ("qwen2.5-", "qwen2.5-0.5b"),
+    ("Qwen/Qwen2-", "Qwen/Qwen2-0.5B-Instruct"),
+    ("meta-llama/Llama-3", "meta-llama/Llama-3.2-1B"),
+    ("llama-3", "llama-3.2-1b"),
+    ("meta-llama/Llama-2", "TinyLlama/TinyLlama-1.1B-Chat-v1.0"),
+    ("mistralai/", "TinyLlama/TinyLlama-1.1B-Chat-v1.0"),
+    ("gpt2", "distilgpt2"),
+    ("openai-community/gpt2", "distilgpt2"),
+)
+
+
+def guess_draft_model(main_model_name: str) -> Optional[str]:
+    """The default draft model for a target model name (None when no family matches,
+    and never the target itself: a draft as large as the target saves nothing)."""
+    name = str(main_model_name or "")
+    base = name.rstrip("/").rsplit("/", 1)[-1]
+    for prefix, draft in DRAFT_MODEL_MAP:
+        if name.startswith(prefix) or base.startswith(prefix):
+            if draft.lower() not in (name.lower(), base.lower()):
+                return draft
+    return None
+
+
 class DraftModelDecoder:
     """Draft-model speculation: a small model proposes gamma tokens greedily, the
     target verifies them in one forward; gamma adapts to the running acceptance

@@ -247,6 +247,20 @@ PRESETS: Dict[str, ModelConfig] = {
                                 norm_eps=1e-5, rope_theta=1_000_000.0, qkv_bias=False, num_experts=8,
                                 experts_per_token=2, expert_intermediate_size=14336, norm_topk_prob=True,
                                 name="mixtral-8x7b"),
+    # default draft models for speculative decoding
+    "qwen2.5-0.5b": ModelConfig(arch="qwen2", vocab_size=151936, hidden_size=896, num_layers=24, num_heads=14,
+                                num_kv_heads=2, head_dim=64, intermediate_size=4864, max_position=32768,
+                                norm_eps=1e-6, rope_theta=1_000_000.0, qkv_bias=True, tie_embeddings=True,
+                                name="qwen2.5-0.5b"),
+    "llama-3.2-1b": ModelConfig(arch="llama", vocab_size=128256, hidden_size=2048, num_layers=16, num_heads=32,
+                                num_kv_heads=8, head_dim=64, intermediate_size=8192, max_position=131072,
+                                norm_eps=1e-5, rope_theta=500_000.0, qkv_bias=False, tie_embeddings=True,
+                                rope_scaling=(("factor", 32.0), ("high_freq_factor", 4.0), ("low_freq_factor", 1.0),
+                                              ("original_max_position_embeddings", 8192), ("rope_type", "llama3")),
+                                name="llama-3.2-1b"),
+    "distilgpt2": ModelConfig(arch="gpt2", vocab_size=50257, hidden_size=768, num_layers=6, num_heads=12,
+                              num_kv_heads=12, head_dim=64, intermediate_size=3072, max_position=1024, norm_eps=1e-5,
+                              rope_theta=0.0, qkv_bias=True, tie_embeddings=True, name="distilgpt2"),
     # small shapes for tests
     "tiny-qwen3": ModelConfig(arch="qwen3", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4,
                               num_kv_heads=2, head_dim=64, intermediate_size=512, max_position=2048,
@@ -279,6 +293,8 @@ ALIASES = {
     "Qwen/Qwen2.5-14B": "qwen2.5-14b", "Qwen/Qwen2.5-14B-Instruct": "qwen2.5-14b",
     "Qwen/Qwen2.5-7B": "qwen2.5-7b", "Qwen/Qwen2.5-7B-Instruct": "qwen2.5-7b",
     "Qwen/Qwen3-8B": "qwen3-8b", "Qwen/Qwen3-30B-A3B": "qwen3-30b-a3b",
+    "Qwen/Qwen2.5-0.5B": "qwen2.5-0.5b", "Qwen/Qwen2.5-0.5B-Instruct": "qwen2.5-0.5b",
+    "meta-llama/Llama-3.2-1B": "llama-3.2-1b", "distilbert/distilgpt2": "distilgpt2",
     "meta-llama/Llama-3.1-8B": "llama-3.1-8b", "meta-llama/Llama-3.1-8B-Instruct": "llama-3.1-8b",
     "mistralai/Mixtral-8x7B-v0.1": "mixtral-8x7b", "mistralai/Mixtral-8x7B-Instruct-v0.1": "mixtral-8x7b",
     "openai-community/gpt2": "gpt2", "qwen2.5-14b-arch": "qwen2.5-14b", "qwen2.5-7b-arch": "qwen2.5-7b",

@@ -71,6 +71,7 @@ class InferencePipeline:
         self.loaded_at: Optional[float] = None
         self.lora = None
         self.spec = None
+        self._draft = None            # draft-model decoder for enable_speculative (False: none)
         self._bcast = None            # TP serving: rank 0 broadcasts request events
         self._events: List = []
 
@@ -226,7 +227,14 @@ class InferencePipeline:
                  return_ids: bool = False, **kw) -> Union[str, List[int]]:
         t0 = time.perf_counter()
         with span("pipeline.generate", model=str(self.model_name), max_new_tokens=max_new_tokens):
-            if (enable_speculative or self.spec is not None) and temperature <= 0 and self.spec is not None:
+            draft = self._speculator() if enable_speculative else None
+            if draft is not None:
+                # draft-model speculation: greedy requests exact, sampled ones by rejection
+                # sampling (outputs follow the target's distribution)
+                sp = SamplingParams(max_tokens=max_new_tokens, temperature=temperature, top_k=top_k, top_p=top_p)
+                ids = draft.generate(self._encode(prompt), max_new_tokens, params=sp)
+                out_ids, ttft, itl = ids, None, None
+            elif (enable_speculative or self.spec is not None) and temperature <= 0 and self.spec is not None:
                 ids = self.spec.generate(self._encode(prompt), max_new_tokens)
                 out_ids, ttft, itl = ids, None, None
             else:
@@ -246,6 +254,35 @@ class InferencePipeline:
                 METRICS.itl.observe(itl)
         self.history.record("generate", str(self.model_name), len(self._encode(prompt)), len(out_ids), dt, ttft)
         return out_ids if return_ids else self.tokenizer.decode(out_ids)
+
+    def _speculator(self):
+        """Draft-model decoder for `generate(enable_speculative=True)`: the draft is
+        VRM_DRAFT_MODEL, else the family default of the loaded model
+        (engine.speculative.DRAFT_MODEL_MAP), when it names a preset or a local
+        checkpoint; None when there is none (prompt lookup, if loaded, then applies).
+        Single-process serving only (tensor-parallel ranks keep the engine lockstep)."""
+        if self._draft is not None or self.llm is None or self._bcast is not None:
+            return self._draft or None
+        from .engine.speculative import DraftModelDecoder, guess_draft_model
+        from .utils.config import flags
+        self._draft = False
+        name = flags.VRM_DRAFT_MODEL or guess_draft_model(str(self.model_name))
+        if not name:
+            return None
+        try:
+            get_config(name)
+        except Exception as e:  # noqa: BLE001 - not a preset, alias or local checkpoint
+            log.warning("draft model %s not available (%s); speculative decoding off", name, e)
+            return None
+        dev = self.llm.device
+        cuda = dev.type == "cuda"
+        draft = LLM(name, device=str(dev), dtype=torch.bfloat16 if cuda else torch.float32,
+                    kv_cache_dtype="bf16" if cuda else "fp32", max_batch=2,
+                    max_model_len=self.engine.max_model_len, kv_pages=None if cuda else 256,
+                    use_cuda_graph=self.llm.runner.use_graph)
+        self._draft = DraftModelDecoder(self.llm, draft, gamma=flags.VRM_SPEC_GAMMA, adaptive=flags.VRM_SPEC_ADAPTIVE)
+        log.info("speculative decoding with draft model %s", name)
+        return self._draft
 
     def generate_stream(self, prompt: Union[str, Sequence[int]], max_new_tokens: int = 128, temperature: float = 0.0,
                         top_p: float = 1.0, top_k: int = 0, stop: Optional[Sequence[str]] = None,
