@@ -234,3 +234,17 @@ def test_family_presets_have_published_sizes():
                            ("mixtral-8x7b", 46.7), ("Qwen/Qwen3-30B-A3B", 30.5)):
         assert abs(get_config(name).num_params() / 1e9 - billions) < 0.1, name
     assert get_config("qwen3-30b-a3b").qk_norm and dict(get_config("llama-3.1-8b").rope_scaling)["factor"] == 8.0
+
+
+def test_hub_reports_native_support(tmp_path, capsys):
+    import json as _json
+
+    from vramancer_b200.cli import main
+    for mt, native in (("qwen3", True), ("gemma2", False)):
+        d = tmp_path / mt
+        d.mkdir()
+        (d / "config.json").write_text(_json.dumps({"model_type": mt, "hidden_size": 64, "num_attention_heads": 4,
+                                                    "num_hidden_layers": 1, "vocab_size": 10}))
+        assert main(["hub", str(d)]) == 0
+        out = _json.loads(capsys.readouterr().out)
+        assert out["native_engine"] is native

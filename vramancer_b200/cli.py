@@ -215,8 +215,10 @@ def _cmd_hub(a) -> int:
         cfg = get_config(p)
         out["config"] = cfg.to_dict()
         out["params_b"] = round(cfg.num_params() / 1e9, 3)
-    except KeyError as e:
+        out["native_engine"] = True
+    except (KeyError, ValueError) as e:      # unknown name, or an architecture the engine lacks
         out["error"] = str(e)
+        out["native_engine"] = False
     _print(out)
     return 0
 
