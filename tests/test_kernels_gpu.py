@@ -34,7 +34,7 @@ def test_gemm(M, N, K, cuda_errors_clean):
     _close(y, ref)
 
 
-@pytest.mark.parametrize("mode", [0, 1, 3, 4])
+@pytest.mark.parametrize("mode", [0, 1, 3, 4, 5])
 @pytest.mark.parametrize("M,N,K", [(129, 512, 320), (512, 5120, 1024), (300, 2304, 5120), (1000, 1536, 640),
                                    (2048, 16384, 256)])
 def test_gemm_prefill_modes(mode, M, N, K, cuda_errors_clean):

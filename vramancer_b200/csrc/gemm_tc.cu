@@ -1915,15 +1915,17 @@ static void choose_split(int tiles, int k_tiles, int min_k, int* splits, int* kt
 // tile's token blocks one after another and re-reads it from HBM once it is evicted)
 // 0: tiled kernel, 1: stream-K with 128-token tiles, 2: stream-K with 256-token tiles
 // (MMA 128 x 256, four 48 KB stages, 512 TMEM columns: one CTA per SM)
-// 0 tiled (default), 1 stream-K, 2 stream-K with 256-token tiles, 3 persistent,
-// 4 persistent with 256-wide weight tiles; VRM_GEMM_PREFILL or gemm_set_prefill_mode
+// 0 automatic (tiled, or the 256-wide persistent kernel where it was measured faster),
+// 1 stream-K, 2 stream-K with 256-token tiles, 3 persistent, 4 persistent with 256-wide
+// weight tiles, 5 tiled only; VRM_GEMM_PREFILL or gemm_set_prefill_mode
 static int g_prefill_mode = -1;
 void gemm_set_prefill_mode(int mode) { g_prefill_mode = mode; }
 static int prefill_mode() {
   if (g_prefill_mode < 0) {
     const char* e = std::getenv("VRM_GEMM_PREFILL");
     const std::string m(e ? e : "");
-    g_prefill_mode = m == "streamk256" ? 2 : m == "streamk" ? 1 : m == "persistent" ? 3 : m == "persistent256" ? 4 : 0;
+    g_prefill_mode = m == "streamk256" ? 2 : m == "streamk" ? 1 : m == "persistent" ? 3 : m == "persistent256" ? 4
+                   : m == "tiled" ? 5 : 0;
   }
   return g_prefill_mode;
 }
@@ -2127,16 +2129,23 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     const CUtensorMap ma = make_kmajor_map(a.x, a.M, a.K, a.ldx, kBM);
     // default (mode 0): the persistent kernel with 256-wide weight tiles for GEMMs of many
     // tiles with a long K or a wide N -- measured on B200 at M = 4096 (Qwen2.5-14B):
-    // gate/up 27648 x 5120 1356 vs 1105 TFLOP/s, down 5120 x 13824 1199 vs 938; at M = 512
-    // and for the narrower projections the tiled kernel stays ahead
-    const bool auto_persist = prefill_mode() == 0 && a.force_splits <= 0 && a.N % 256 == 0 && a.M >= 2048 &&
-                              (a.K >= 8192 || a.N >= 16384);
+    // gate/up 27648 x 5120 1356 vs 1105 TFLOP/s, down 5120 x 13824 1199 vs 938; for the
+    // narrower projections the tiled kernel stays ahead there.  Short prompts (M 512 to
+    // 1024): the 256-wide tiles' deeper pipeline wins where they fit one wave or N is wide
+    // and K is short -- at M = 512, qkv 7168 x 5120 39.2 vs 40.8 us, o 5120 x 5120 37.5 vs
+    // 49.1, gate/up 27648 x 5120 125.1 vs 134.2; down 5120 x 13824 (80 tiles, long K)
+    // stays tiled (85.8 vs 110.2)
+    const bool wide_ok = prefill_mode() == 0 && a.force_splits <= 0 && a.N % 256 == 0;
+    const bool long_prompt = a.M >= 2048 && (a.K >= 8192 || a.N >= 16384);
+    const bool short_prompt = a.M >= 512 && a_tiles <= 8 && a.K < 8192 &&
+                              (a_tiles * (a.N / 256) <= device_sm_count() || a.N >= 16384);
+    const bool auto_persist = wide_ok && (long_prompt || short_prompt);
     if (auto_persist) {
       const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, 256);
       launch_persistent<256, 4>(ma, mb, ep, a.K, a_tiles, a.N / 256, stream);
       return;
     }
-    if (prefill_mode() >= 3 && a.force_splits <= 0) {
+    if ((prefill_mode() == 3 || prefill_mode() == 4) && a.force_splits <= 0) {
       if (prefill_mode() == 4 && a.N % 256 == 0) {
         const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, 256);
         launch_persistent<256, 4>(ma, mb, ep, a.K, a_tiles, a.N / 256, stream);
