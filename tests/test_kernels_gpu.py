@@ -36,12 +36,14 @@ def test_gemm(M, N, K, cuda_errors_clean):
 
 @pytest.mark.parametrize("mode", [0, 1, 3, 4, 5])
 @pytest.mark.parametrize("M,N,K", [(129, 512, 320), (512, 5120, 1024), (300, 2304, 5120), (1000, 1536, 640),
-                                   (2048, 16384, 256)])
+                                   (2048, 16384, 256), (384, 2560, 8192), (640, 768, 12800)])
 def test_gemm_prefill_modes(mode, M, N, K, cuda_errors_clean):
-    """Every prefill GEMM kernel (tiled, stream-K, persistent 128- and 256-wide) against
-    the fp32 reference, with bias + residual and with the SiLU-mul epilogue.  Shapes
-    leave partial tiles and (persistent) K-split tails of the last round; the widest one
-    takes the default mode's automatic 256-wide persistent kernel."""
+    """Every prefill GEMM kernel (tiled, stream-K, persistent 128- and 256-wide, tiled
+    only) against the fp32 reference, with bias + residual and with the SiLU-mul
+    epilogue.  Shapes leave partial tiles; in the persistent kernel they give whole-tile
+    rounds plus stream-K remainders whose tiles collect 2 to 6 partials (the last two
+    shapes), or whole tiles only; the (2048, 16384) and (512, 5120) shapes take the
+    default mode's automatic 256-wide persistent kernel."""
     torch.manual_seed(M + N + K + mode)
     x = (torch.randn(M, K) * 0.5).bfloat16()
     w = (torch.randn(N, K) * 0.05).bfloat16()

@@ -488,14 +488,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // =====================================================================================
-// Persistent prefill GEMM: one CTA per SM walks work units u = blockIdx.x, + gridDim.x:
-// units [0, full_tiles) are whole 128 x BN output tiles (token-block fastest, so the
-// CTAs in flight share each weight tile through L2), later units are K-splits of the
-// tail tiles that the last round could not fill (partials summed by the tile's last
-// split, as in gemm_bf16_tc_kernel).  Warp 0 streams A/B tiles through a STAGES-deep
-// TMA ring that runs across unit boundaries; warp 1 issues the MMAs into one of two
-// TMEM accumulators (2 x BN columns); warps 2-5 drain the other accumulator, so a
-// tile's epilogue overlaps the next tile's main loop and the ring never restarts.
+// Persistent prefill GEMM: one CTA per SM.  CTA c first takes whole 128 x BN output
+// tiles in data-parallel rounds (tiles c, c + G, ... below dp_tiles; token block fastest,
+// so the CTAs in flight share each weight tile through L2), then its stream-K share of
+// the remaining tiles: their k-iterations laid end to end (S = sk_tiles x k_tiles), CTA c
+// takes [c S / G, (c + 1) S / G), cut at tile boundaries into segments.  Every CTA has
+// the same number of k-iterations (G' <= G CTAs take part, each at least 8 and a
+// quarter of a tile's k-iterations, so no tile collects more than a few partials), and a
+// GEMM of fewer tiles than SMs (short prompts) still keeps every SM busy.  A tile covered by several segments writes one fp32 partial
+// per segment; the last to arrive sums them in segment order (deterministic).  Warp 0
+// streams A/B tiles through a STAGES-deep TMA ring that runs across unit boundaries;
+// warp 1 issues the MMAs into one of two TMEM accumulators (2 x BN columns); warps 2-5
+// drain the other accumulator, so a tile's epilogue overlaps the next one's main loop.
 template <int BN, int STAGES>
 struct PersistSmem {
   static constexpr int kABytes = kBM * kBK * 2;
@@ -507,23 +511,41 @@ struct PersistSmem {
   static constexpr int kAlloc = kTotal + 1024;
 };
 
-struct UnitMap {
-  int full_tiles, tail_splits, num_a_tiles, total_k_tiles;
-  __device__ __forceinline__ void get(int u, int& tile, int& split, int& nsplit, int& kb, int& ke) const {
-    if (u < full_tiles) {
-      tile = u;
-      split = 0;
-      nsplit = 1;
-    } else {
-      const int j = u - full_tiles;
-      tile = full_tiles + j / tail_splits;
-      split = j % tail_splits;
-      nsplit = tail_splits;
+struct WorkMap {
+  int dp_tiles, grid, k_tiles, sk_tiles, sk_grid, max_seg;
+  long long sk_work;   // sk_tiles * k_tiles; >= sk_grid whenever sk_tiles > 0 (no empty range)
+  __device__ __forceinline__ int n_dp(int c) const { return c < dp_tiles ? (dp_tiles - 1 - c) / grid + 1 : 0; }
+  // the CTA whose stream-K range holds k-iteration x: the largest c with c S / G' <= x
+  // (G' = sk_grid: CTAs c < G' share the stream-K work)
+  __device__ __forceinline__ int owner(long long x) const { return (int)(((x + 1) * sk_grid - 1) / sk_work); }
+  // unit i of CTA c: tile, k-range [kb, ke), its segment index / count on the tile and
+  // its workspace slot; false past the CTA's last unit
+  __device__ __forceinline__ bool get(int c, int i, int& tile, int& kb, int& ke, int& seg, int& nseg,
+                                      int& slot) const {
+    const int nd = n_dp(c);
+    if (i < nd) {
+      tile = c + i * grid;
+      kb = 0;
+      ke = k_tiles;
+      seg = 0;
+      nseg = 1;
+      slot = 0;
+      return true;
     }
-    const int per = (total_k_tiles + nsplit - 1) / nsplit;
-    kb = split * per;
-    ke = min(total_k_tiles, kb + per);
-    if (ke < kb) ke = kb;
+    if (sk_tiles <= 0 || c >= sk_grid) return false;
+    const long long b = (long long)c * sk_work / sk_grid, e = (long long)(c + 1) * sk_work / sk_grid;
+    const long long t0 = b / k_tiles;
+    const long long ts = t0 + (i - nd);
+    if (ts >= sk_tiles || ts * k_tiles >= e) return false;
+    kb = ts == t0 ? (int)(b - t0 * k_tiles) : 0;
+    ke = (int)min((long long)k_tiles, e - ts * k_tiles);
+    if (kb >= ke) return false;
+    tile = dp_tiles + (int)ts;
+    const int first = owner(ts * k_tiles), last = owner((ts + 1) * k_tiles - 1);
+    seg = c - first;
+    nseg = last - first + 1;
+    slot = (int)ts * max_seg;
+    return true;
   }
 };
 
@@ -531,8 +553,7 @@ template <int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                            EpiParams ep, float* __restrict__ workspace, uint32_t* __restrict__ tile_counters, int K,
-                           int num_a_tiles, int full_tiles, int tail_splits, int num_units,
-                           uint32_t* __restrict__ err) {
+                           int num_a_tiles, WorkMap wm, uint32_t* __restrict__ err) {
   using L = PersistSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -545,7 +566,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* flag_slot = tmem_slot + 1;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const UnitMap um{full_tiles, tail_splits, num_a_tiles, (K + kBK - 1) / kBK};
   constexpr uint32_t kTmemCols = 2 * BN;   // two accumulators
 
   pdl_launch();
@@ -578,9 +598,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     pdl_wait();
     int it = 0;
     bool failed = false;
-    for (int u = blockIdx.x; u < num_units && !failed; u += gridDim.x) {
-      int tile, split, nsplit, kb, ke;
-      um.get(u, tile, split, nsplit, kb, ke);
+    int tile, kb, ke, seg, nseg, slot;
+    for (int i = 0; !failed && wm.get(blockIdx.x, i, tile, kb, ke, seg, nseg, slot); ++i) {
       const int a_tile = tile % num_a_tiles, b_tile = tile / num_a_tiles;
       for (int kt = kb; kt < ke; ++kt, ++it) {
         const int s = it % STAGES;
@@ -603,9 +622,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr uint32_t idesc = make_idesc_bf16(kBM, BN);
     int it = 0, n = 0;
     bool failed = false;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++n) {
-      int tile, split, nsplit, kb, ke;
-      um.get(u, tile, split, nsplit, kb, ke);
+    int tile, kb, ke, seg, nseg, slot;
+    for (int i = 0; wm.get(blockIdx.x, i, tile, kb, ke, seg, nseg, slot); ++i, ++n) {
       const int acc = n & 1;
       // the epilogue has read this accumulator's previous tile (first use passes)
       if (!failed && !mbar_wait(&acc_empty[acc], ((n >> 1) & 1) ^ 1, err)) failed = true;
@@ -635,9 +653,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int row = lane_base + lane;
     pdl_wait();
     int n = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++n) {
-      int tile, split, nsplit, kb, ke;
-      um.get(u, tile, split, nsplit, kb, ke);
+    int tile, kb, ke, seg, nseg, slot;
+    for (int i = 0; wm.get(blockIdx.x, i, tile, kb, ke, seg, nseg, slot); ++i, ++n) {
       const int acc = n & 1;
       const bool ok = mbar_wait(&acc_full[acc], (n >> 1) & 1, err);
       tc_fence_after();
@@ -645,10 +662,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int r_glob = a_tile * kBM + row;
       const int c_base = b_tile * BN;
       const uint32_t t_row = tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN);
-      const bool direct = nsplit == 1;
+      const bool direct = nseg == 1;
       const bool have = ok && ke > kb;
-      float* slot0 = direct ? nullptr
-                            : workspace + (((size_t)(tile - full_tiles) * nsplit) * kBM + row) * (size_t)BN;
+      float* slot0 = direct ? nullptr : workspace + ((size_t)slot * kBM + row) * (size_t)BN;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r0[16], r1[16];
@@ -670,7 +686,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           epi_store<false>(ep, r_glob, c_base + c0, v0);
           epi_store<false>(ep, r_glob, c_base + c0 + 16, v1);
         } else {
-          float4* dst = reinterpret_cast<float4*>(slot0 + (size_t)split * kBM * BN + c0);
+          float4* dst = reinterpret_cast<float4*>(slot0 + (size_t)seg * kBM * BN + c0);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             __stcg(dst + q, make_float4(v0[4 * q], v0[4 * q + 1], v0[4 * q + 2], v0[4 * q + 3]));
@@ -679,12 +695,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       if (!direct) {
-        // the tile's last split sums every split's partial in split order
+        // the tile's last segment to arrive sums every segment's partial in segment order
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (threadIdx.x == 64) {
           const uint32_t prev = atomicAdd(&tile_counters[tile], 1u);
-          *flag_slot = (prev == (uint32_t)(nsplit - 1)) ? 1u : 0u;
+          *flag_slot = (prev == (uint32_t)(nseg - 1)) ? 1u : 0u;
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const bool last = *flag_slot != 0u;
@@ -696,14 +712,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             float v[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.f;
-            for (int s0 = 0; s0 < nsplit; s0 += 4) {
+            for (int s0 = 0; s0 < nseg; s0 += 4) {
               float4 x[4][4];
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
                 const float4* src = reinterpret_cast<const float4*>(slot0 + (size_t)(s0 + w) * kBM * BN + c0);
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                  x[w][q] = s0 + w < nsplit ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  x[w][q] = s0 + w < nseg ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
               }
 #pragma unroll
               for (int w = 0; w < 4; ++w)
@@ -1932,7 +1948,7 @@ static int prefill_mode() {
 static bool prefill_streamk() { return prefill_mode() == 1 || prefill_mode() == 2; }
 
 // Persistent prefill GEMM (gemm_persistent_kernel): whole tiles for the complete rounds
-// over the SMs, the tail split K-wise (choose_tail_split), one CTA per SM.
+// over the SMs, the remaining tiles stream-K (WorkMap), one CTA per SM.
 template <int BN, int STAGES>
 static void launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, const EpiParams& ep, int K,
                               int a_tiles, int b_tiles, cudaStream_t stream) {
@@ -1947,20 +1963,36 @@ static void launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, cons
   }
   const int tiles = a_tiles * b_tiles;
   const int k_tiles = (K + kBK - 1) / kBK;
-  int full = tiles, tail_splits = 1;
-  choose_tail_split(tiles, k_tiles, 8, &full, &tail_splits);
-  if (tail_splits <= 1) full = tiles;
+  const int sms = device_sm_count();
+  // whole-tile rounds while every SM has a tile; the remaining tiles stream-K over G'
+  // CTAs, each taking at least max(8, k_tiles / 4) k-iterations -- when that leaves no
+  // more CTAs than remaining tiles, whole tiles are as good and the remainder stays whole
+  WorkMap wm{};
+  wm.k_tiles = k_tiles;
+  wm.dp_tiles = (tiles / sms) * sms;
+  wm.sk_tiles = tiles - wm.dp_tiles;
+  wm.sk_work = (long long)wm.sk_tiles * k_tiles;
+  const long long min_share = std::max(8, (k_tiles + 3) / 4);
+  wm.sk_grid = (int)std::min<long long>(sms, wm.sk_work / min_share);
+  if (wm.sk_tiles == 0 || wm.sk_grid <= wm.sk_tiles) {
+    wm.dp_tiles = tiles;
+    wm.sk_tiles = 0;
+    wm.sk_work = 0;
+    wm.sk_grid = 0;
+  }
+  wm.grid = wm.sk_tiles > 0 ? (wm.dp_tiles > 0 ? sms : wm.sk_grid) : std::min(tiles, sms);
   float* ws = nullptr;
   uint32_t* counters = nullptr;
-  if (full < tiles) {
-    ws = static_cast<float*>(workspace_get((size_t)(tiles - full) * tail_splits * kBM * BN * sizeof(float), stream));
+  if (wm.sk_tiles > 0) {
+    // segments per tile <= k_tiles / (shortest CTA share) + 2
+    wm.max_seg = (int)(k_tiles / (wm.sk_work / wm.sk_grid)) + 2;
+    ws = static_cast<float*>(
+        workspace_get((size_t)wm.sk_tiles * wm.max_seg * kBM * BN * sizeof(float), stream));
     VRM_REQUIRE((size_t)tiles <= 32768, "too many split-K tiles");
     counters = tile_counters_get(stream);
   }
-  const int units = full + (tiles - full) * std::max(1, tail_splits);
-  const int grid = std::min(units, device_sm_count());
-  launch_kernel(kern, dim3(grid), dim3(kGemmThreads), (size_t)L::kAlloc, stream, ma, mb, ep, ws, counters, K, a_tiles,
-                full, tail_splits, units, error_word());
+  launch_kernel(kern, dim3(wm.grid), dim3(kGemmThreads), (size_t)L::kAlloc, stream, ma, mb, ep, ws, counters, K,
+                a_tiles, wm, error_word());
 }
 
 // Persistent CTAs of the stream-K decode GEMM.  Latency model fitted on B200 (µs): a
