@@ -514,6 +514,9 @@ struct PersistSmem {
 struct WorkMap {
   int dp_tiles, grid, k_tiles, sk_tiles, sk_grid, max_seg;
   long long sk_work;   // sk_tiles * k_tiles; >= sk_grid whenever sk_tiles > 0 (no empty range)
+  // split schedule instead of stream-K (tail_splits > 0): units u = c, c + G, ... below
+  // num_units; units past dp_tiles are tail_splits equal K pieces of the remaining tiles
+  int tail_splits, num_units;
   __device__ __forceinline__ int n_dp(int c) const { return c < dp_tiles ? (dp_tiles - 1 - c) / grid + 1 : 0; }
   // the CTA whose stream-K range holds k-iteration x: the largest c with c S / G' <= x
   // (G' = sk_grid: CTAs c < G' share the stream-K work)
@@ -522,6 +525,26 @@ struct WorkMap {
   // its workspace slot; false past the CTA's last unit
   __device__ __forceinline__ bool get(int c, int i, int& tile, int& kb, int& ke, int& seg, int& nseg,
                                       int& slot) const {
+    if (tail_splits > 0) {
+      const int u = c + i * grid;
+      if (u >= num_units) return false;
+      if (u < dp_tiles) {
+        tile = u;
+        seg = 0;
+        nseg = 1;
+      } else {
+        const int j = u - dp_tiles;
+        tile = dp_tiles + j / tail_splits;
+        seg = j % tail_splits;
+        nseg = tail_splits;
+      }
+      const int per = (k_tiles + nseg - 1) / nseg;
+      kb = seg * per;
+      ke = min(k_tiles, kb + per);
+      if (ke < kb) ke = kb;
+      slot = (tile - dp_tiles) * tail_splits;
+      return true;
+    }
     const int nd = n_dp(c);
     if (i < nd) {
       tile = c + i * grid;
@@ -1949,6 +1972,14 @@ static bool prefill_streamk() { return prefill_mode() == 1 || prefill_mode() == 
 
 // Persistent prefill GEMM (gemm_persistent_kernel): whole tiles for the complete rounds
 // over the SMs, the remaining tiles stream-K (WorkMap), one CTA per SM.
+static int persist_sk_env() {
+  static const int v = [] {
+    const char* e = std::getenv("VRM_GEMM_PERSIST_SK");
+    return e && e[0] ? (e[0] == '1' ? 1 : 0) : -1;
+  }();
+  return v;
+}
+
 template <int BN, int STAGES>
 static void launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, const EpiParams& ep, int K,
                               int a_tiles, int b_tiles, cudaStream_t stream) {
@@ -1964,11 +1995,35 @@ static void launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, cons
   const int tiles = a_tiles * b_tiles;
   const int k_tiles = (K + kBK - 1) / kBK;
   const int sms = device_sm_count();
-  // whole-tile rounds while every SM has a tile; the remaining tiles stream-K over G'
-  // CTAs, each taking at least max(8, k_tiles / 4) k-iterations -- when that leaves no
-  // more CTAs than remaining tiles, whole tiles are as good and the remainder stays whole
+  // Two schedules for the tiles left after the whole-tile rounds.  Split: each split into
+  // equal K pieces (choose_tail_split), pieces dealt round-robin.  Stream-K: their
+  // k-iterations shared evenly by G' CTAs, each taking at least max(8, k_tiles / 4) (when
+  // that leaves no more CTAs than remaining tiles, the remainder stays whole).
+  // VRM_GEMM_PERSIST_SK=1 / 0 forces one; by default stream-K runs for M >= 1024.
   WorkMap wm{};
   wm.k_tiles = k_tiles;
+  const int sk_env = persist_sk_env();
+  const bool use_sk = sk_env >= 0 ? sk_env == 1 : a_tiles >= 8;
+  if (!use_sk) {
+    int full = tiles, tail_splits = 1;
+    choose_tail_split(tiles, k_tiles, 8, &full, &tail_splits);
+    if (tail_splits <= 1) full = tiles;
+    wm.dp_tiles = full;
+    wm.tail_splits = std::max(1, tail_splits);
+    wm.num_units = full + (tiles - full) * wm.tail_splits;
+    wm.grid = std::min(wm.num_units, sms);
+    float* ws = nullptr;
+    uint32_t* counters = nullptr;
+    if (full < tiles) {
+      ws = static_cast<float*>(workspace_get((size_t)(tiles - full) * wm.tail_splits * kBM * BN * sizeof(float),
+                                             stream));
+      VRM_REQUIRE((size_t)tiles <= 32768, "too many split-K tiles");
+      counters = tile_counters_get(stream);
+    }
+    launch_kernel(kern, dim3(wm.grid), dim3(kGemmThreads), (size_t)L::kAlloc, stream, ma, mb, ep, ws, counters, K,
+                  a_tiles, wm, error_word());
+    return;
+  }
   wm.dp_tiles = (tiles / sms) * sms;
   wm.sk_tiles = tiles - wm.dp_tiles;
   wm.sk_work = (long long)wm.sk_tiles * k_tiles;
