@@ -1999,11 +1999,12 @@ static void launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, cons
   // equal K pieces (choose_tail_split), pieces dealt round-robin.  Stream-K: their
   // k-iterations shared evenly by G' CTAs, each taking at least max(8, k_tiles / 4) (when
   // that leaves no more CTAs than remaining tiles, the remainder stays whole).
-  // VRM_GEMM_PERSIST_SK=1 / 0 forces one; by default stream-K runs for M >= 1024.
+  // Split is the default: it measured faster at every Qwen2.5-14B projection and prompt
+  // length tried (M 512-4096; stream-K 2 % slower at M = 4096, up to 1.9x at M = 512,
+  // where every tile collects partials); VRM_GEMM_PERSIST_SK=1 selects stream-K.
   WorkMap wm{};
   wm.k_tiles = k_tiles;
-  const int sk_env = persist_sk_env();
-  const bool use_sk = sk_env >= 0 ? sk_env == 1 : a_tiles >= 8;
+  const bool use_sk = persist_sk_env() == 1;
   if (!use_sk) {
     int full = tiles, tail_splits = 1;
     choose_tail_split(tiles, k_tiles, 8, &full, &tail_splits);
@@ -2214,19 +2215,14 @@ void gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
       choose_tail_split(a_tiles * b_tiles, k_tiles, 8, &full, &tail_splits);
     }
     const CUtensorMap ma = make_kmajor_map(a.x, a.M, a.K, a.ldx, kBM);
-    // default (mode 0): the persistent kernel with 256-wide weight tiles for GEMMs of many
-    // tiles with a long K or a wide N -- measured on B200 at M = 4096 (Qwen2.5-14B):
-    // gate/up 27648 x 5120 1356 vs 1105 TFLOP/s, down 5120 x 13824 1199 vs 938; for the
-    // narrower projections the tiled kernel stays ahead there.  Short prompts (M 512 to
-    // 1024): the 256-wide tiles' deeper pipeline wins where they fit one wave or N is wide
-    // and K is short -- at M = 512, qkv 7168 x 5120 39.2 vs 40.8 us, o 5120 x 5120 37.5 vs
-    // 49.1, gate/up 27648 x 5120 125.1 vs 134.2; down 5120 x 13824 (80 tiles, long K)
-    // stays tiled (85.8 vs 110.2)
-    const bool wide_ok = prefill_mode() == 0 && a.force_splits <= 0 && a.N % 256 == 0;
-    const bool long_prompt = a.M >= 2048 && (a.K >= 8192 || a.N >= 16384);
-    const bool short_prompt = a.M >= 512 && a_tiles <= 8 && a.K < 8192 &&
-                              (a_tiles * (a.N / 256) <= device_sm_count() || a.N >= 16384);
-    const bool auto_persist = wide_ok && (long_prompt || short_prompt);
+    // default (mode 0): the persistent kernel with 256-wide weight tiles (split-tail
+    // schedule) for every prompt of 512+ tokens -- measured on B200 at M = 512 / 1024 /
+    // 2048 / 4096 over the Qwen2.5-14B projections it beats the tiled kernel everywhere
+    // (e.g. o 5120 x 5120: 37.6 vs 49.4, 72.4 vs 85.4, 106.9 vs 124.5, 186.7 vs 190.0 us)
+    // except a long K over at most 4 token blocks (down 5120 x 13824 at M = 512: 80
+    // tiles leave 68 SMs idle, 110.3 vs 85.7 us), which stays tiled
+    const bool auto_persist = prefill_mode() == 0 && a.force_splits <= 0 && a.N % 256 == 0 && a.M >= 512 &&
+                              !(a_tiles <= 4 && a.K >= 8192);
     if (auto_persist) {
       const CUtensorMap mb = make_kmajor_map(a.w, a.N, a.K, a.ldw, 256);
       launch_persistent<256, 4>(ma, mb, ep, a.K, a_tiles, a.N / 256, stream);
