@@ -230,7 +230,26 @@ struct DecodeParams {
   int Hq;
   long long num_pages;       // pool pages (checked in bounds-check builds)
   uint32_t* err;
+  const uint8_t* pf;         // L2 prefetch region (the next GEMM's weights) or null
+  unsigned long long pf_bytes;
 };
+
+// Bulk L2 prefetch of this CTA's equal slice of [pf, pf + bytes) (16-byte granules, in
+// pieces of at most 64 KB).  Fire and forget: nothing waits on it, and the data only
+// warms L2 for the kernel that follows.
+__device__ __forceinline__ void l2_prefetch_slice(const uint8_t* pf, unsigned long long bytes) {
+  const unsigned long long nct = (unsigned long long)gridDim.x * gridDim.y * gridDim.z;
+  const unsigned long long id =
+      blockIdx.x + (unsigned long long)gridDim.x * (blockIdx.y + (unsigned long long)gridDim.y * blockIdx.z);
+  const unsigned long long chunk = (((bytes + nct - 1) / nct) + 15ull) & ~15ull;
+  const unsigned long long beg = id * chunk;
+  if (beg >= bytes) return;
+  const unsigned long long end = beg + chunk < bytes ? beg + chunk : bytes;
+  for (unsigned long long o = beg; o < end; o += 65536ull) {
+    const uint32_t n = (uint32_t)((end - o) < 65536ull ? (end - o) : 65536ull);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf + o), "r"(n) : "memory");
+  }
+}
 
 // Stores this step's k (rotated) and v of sequence b, KV head kvh, into its cache slot,
 // with the rounding of the standalone RoPE + KV write kernel (k rounded to bf16 after
@@ -305,6 +324,8 @@ __device__ __forceinline__ void decode_write_new_kv(const DecodeParams& P, int b
 template <int D, int FMT, bool kCluster = false>
 __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams P) {
   pdl_launch();
+  // weights are constant: their prefetch may start before the previous kernel ends
+  if (P.pf != nullptr && threadIdx.x == 0) l2_prefetch_slice(P.pf, P.pf_bytes);
   using S = DecodeSmem<D, FMT>;
   constexpr bool kFp8 = FMT == kFmtFp8;
   constexpr int ROWB = D * 2;
@@ -1663,6 +1684,16 @@ static void launch_decode_tma(const CUtensorMap& map, const DecodeTmaParams& p, 
   launch_kernel(kern, dim3(grid), dim3(160), (size_t)smem, st, map, p);
 }
 
+// L2 prefetch of the next GEMM's weights from the decode attention kernel (VRM_L2_PREFETCH=1;
+// off by default)
+static bool l2_prefetch_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VRM_L2_PREFETCH");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   VRM_REQUIRE(a.D == 64 || a.D == 128, "decode attention: head_dim must be 64 or 128");
   VRM_REQUIRE(a.KH > 0 && a.Hq % a.KH == 0 && a.Hq / a.KH <= 8, "decode attention: GQA group must be <= 8 heads");
@@ -1696,6 +1727,8 @@ void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   p.Hq = a.Hq;
   p.num_pages = a.cache_pages;
   p.err = a.err ? a.err : error_word();
+  p.pf = l2_prefetch_enabled() && a.l2_prefetch_bytes >= 16 ? reinterpret_cast<const uint8_t*>(a.l2_prefetch) : nullptr;
+  p.pf_bytes = p.pf != nullptr ? (a.l2_prefetch_bytes & ~15ull) : 0ull;
   if (a.positions != nullptr) {
     VRM_REQUIRE(a.slot_mapping != nullptr, "decode attention: fused KV write needs slot_mapping");
     VRM_REQUIRE(a.cos_sin == nullptr || a.rot_dim == a.D, "decode attention: fused RoPE needs rot_dim == head_dim");

@@ -271,7 +271,8 @@ void add_(Tensor& a, const Tensor& b) {
 // ---------------------------------------------------------------- attention
 void attn_decode(const Tensor& q, const Tensor& cache, int64_t layer, const Tensor& block_tables,
                  const Tensor& context_lens, const OptT& kv_scale, double sm_scale, Tensor& out, int64_t num_splits,
-                 int64_t num_q_heads, const OptT& positions, const OptT& cos_sin, const OptT& slot_mapping) {
+                 int64_t num_q_heads, const OptT& positions, const OptT& cos_sin, const OptT& slot_mapping,
+                 const OptT& l2_prefetch) {
   check_cache(cache);
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.dim() == 2 && q.stride(1) == 1 &&
                   q.stride(0) % 2 == 0,
@@ -311,6 +312,15 @@ void attn_decode(const Tensor& q, const Tensor& cache, int64_t layer, const Tens
   a.max_pages = (int)block_tables.size(1);
   a.num_splits = (int)num_splits;
   a.cache_pages = cache.size(0);
+  if (has(l2_prefetch)) {
+    same_device_opt(q, {&l2_prefetch}, "paged_attention_decode");
+    TORCH_CHECK(l2_prefetch->is_contiguous(), "decode: l2_prefetch must be contiguous");
+    const uint64_t bytes = (uint64_t)l2_prefetch->numel() * l2_prefetch->element_size();
+    if (reinterpret_cast<uintptr_t>(l2_prefetch->data_ptr()) % 16 == 0 && bytes >= 16) {
+      a.l2_prefetch = l2_prefetch->data_ptr();
+      a.l2_prefetch_bytes = bytes & ~uint64_t(15);
+    }
+  }
   if (has(positions)) {
     // fused RoPE + KV write: q is the whole qkv row
     TORCH_CHECK(has(slot_mapping), "decode: fused KV write needs slot_mapping");
@@ -1247,7 +1257,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention_decode", &attn_decode, py::arg("q"), py::arg("cache"), py::arg("layer"),
         py::arg("block_tables"), py::arg("context_lens"), py::arg("kv_scale"), py::arg("sm_scale"), py::arg("out"),
         py::arg("num_splits"), py::arg("num_q_heads"), py::arg("positions") = py::none(),
-        py::arg("cos_sin") = py::none(), py::arg("slot_mapping") = py::none());
+        py::arg("cos_sin") = py::none(), py::arg("slot_mapping") = py::none(),
+        py::arg("l2_prefetch") = py::none());
   m.def("paged_attention_prefill", &attn_prefill, py::arg("q"), py::arg("cache"), py::arg("layer"),
         py::arg("block_tables"), py::arg("cu_q"), py::arg("context_lens"), py::arg("kv_scale"), py::arg("sm_scale"),
         py::arg("out"), py::arg("max_q_len"), py::arg("num_q_heads"));

@@ -389,6 +389,11 @@ struct DecodeAttnArgs {
   // device word that bounds / timeout errors are OR-ed into; null -> the per-device
   // error word (error_word())
   uint32_t* err = nullptr;
+  // optional L2 prefetch of the bytes the next kernel streams (the o_proj weights): the
+  // CTAs issue bulk L2 prefetches of equal slices at their start, so those bytes load
+  // while attention, which leaves HBM bandwidth spare at short contexts, runs
+  const void* l2_prefetch = nullptr;   // 16-byte aligned
+  uint64_t l2_prefetch_bytes = 0;      // multiple of 16
 };
 void paged_attention_decode(const DecodeAttnArgs& a, cudaStream_t stream);
 // Selects the persistent TMA decode kernel for bf16 pages (default off, VRM_DECODE_TMA=1).

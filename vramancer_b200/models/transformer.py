@@ -202,20 +202,33 @@ class DecoderModel:
         li = i - self.first_layer
         if getattr(pool, "is_tq", False):
             return self._attention_tq(qkv, batch, pool, li)
+        # decode attention leaves HBM bandwidth spare at short contexts: it prefetches the
+        # o_proj weights into L2 for the GEMM that follows it
+        pf = self._o_prefetch(i) if batch.is_decode and qkv.is_cuda else None
         if batch.is_decode and self.fused_rope and qkv.is_cuda:
             # RoPE + KV-page write inside the decode attention kernel (one launch fewer)
             return ops.paged_attention_decode(qkv, pool.cache, li, batch.block_tables, batch.context_lens,
                                               pool.kv_scale, self.sm_scale, hq, num_splits=batch.attn_splits,
                                               positions=batch.positions, cos_sin=self.cos_sin,
-                                              slot_mapping=batch.slot_mapping)
+                                              slot_mapping=batch.slot_mapping, l2_prefetch=pf)
         ops.rope_kv_write(qkv, batch.positions, self.cos_sin, pool.cache, batch.slot_mapping, pool.kv_scale,
                           li, hq, kvh, D)
         if batch.is_decode:
             return ops.paged_attention_decode(qkv, pool.cache, li, batch.block_tables, batch.context_lens,
-                                              pool.kv_scale, self.sm_scale, hq, num_splits=batch.attn_splits)
+                                              pool.kv_scale, self.sm_scale, hq, num_splits=batch.attn_splits,
+                                              l2_prefetch=pf)
         return ops.paged_attention_prefill(qkv, pool.cache, li, batch.block_tables, batch.cu_q,
                                            batch.context_lens, pool.kv_scale, self.sm_scale, hq,
                                            batch.max_q_len)
+
+    def _o_prefetch(self, i: int) -> Optional[torch.Tensor]:
+        """The tensor holding layer i's o_proj weights (bf16 / fp8 matrix, or NVFP4
+        codes), for the decode attention kernel's L2 prefetch; None when there is none."""
+        w = self.lw(i, "o_w")
+        if isinstance(w, torch.Tensor):
+            return w if w.is_contiguous() else None
+        codes = getattr(w, "q", None)             # NVFP4Weight / FP8Weight codes
+        return codes if isinstance(codes, torch.Tensor) and codes.is_contiguous() else None
 
     def _attention_tq(self, qkv: torch.Tensor, batch: ForwardBatch, pool: KVPool, li: int) -> torch.Tensor:
         """Attention over TurboQuant KV pages: RoPE in place, the step's k / v written as

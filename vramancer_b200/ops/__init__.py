@@ -366,19 +366,22 @@ def paged_attention_decode(q: torch.Tensor, cache: torch.Tensor, layer: int, blo
                            num_q_heads: int, *, out: Optional[torch.Tensor] = None,
                            num_splits: int = 0, positions: Optional[torch.Tensor] = None,
                            cos_sin: Optional[torch.Tensor] = None,
-                           slot_mapping: Optional[torch.Tensor] = None) -> torch.Tensor:
+                           slot_mapping: Optional[torch.Tensor] = None,
+                           l2_prefetch: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One query token per sequence: q [B, >=Hq*D] -> out [B, Hq*D].
 
     With `positions` (and `slot_mapping`) q is the unrotated qkv row and the kernel also
     does this step's RoPE (cos_sin, rotate-half over all head dims; None = no rotation)
-    and writes the token's k / v into the cache: the work of `rope_kv_write`, fused."""
+    and writes the token's k / v into the cache: the work of `rope_kv_write`, fused.
+    `l2_prefetch` (a contiguous tensor, e.g. the next projection's weights) is brought
+    into L2 by the kernel's CTAs while attention runs (GPU only; no effect on results)."""
     B = q.shape[0]
     D = cache_head_dim(cache)
     if out is None:
         out = torch.empty(B, num_q_heads * D, dtype=q.dtype, device=q.device)
     if q.is_cuda:
         native().paged_attention_decode(q, cache, layer, block_tables, context_lens, kv_scale, sm_scale, out,
-                                        num_splits, num_q_heads, positions, cos_sin, slot_mapping)
+                                        num_splits, num_q_heads, positions, cos_sin, slot_mapping, l2_prefetch)
         return out
     if positions is not None:
         rope_kv_write(q, positions, cos_sin, cache, slot_mapping, kv_scale, layer, num_q_heads, cache.shape[3], D)
