@@ -107,3 +107,33 @@ def _free_udp_port():
     p = s.getsockname()[1]
     s.close()
     return p
+
+
+def test_every_environment_variable_read_is_registered():
+    """Each VRM_* variable the package reads (os.environ in Python, getenv in the CUDA /
+    C++ sources) has a typed, documented registry entry; the reference's names for the
+    same settings resolve through the aliases."""
+    import pathlib
+    import re
+
+    from vramancer_b200.utils.config import FLAG_ALIASES, FLAG_REGISTRY, flags
+    root = pathlib.Path(__file__).resolve().parents[1] / "vramancer_b200"
+    pat = re.compile(r'(?:environ\.get|environ\[|getenv|_env)\(\s*"(VRM_[A-Z0-9_]+)"|environ\["(VRM_[A-Z0-9_]+)"\]')
+    read = set()
+    for f in list(root.rglob("*.py")) + list(root.rglob("*.cu")) + list(root.rglob("*.cpp")):
+        for m in pat.finditer(f.read_text(errors="ignore")):
+            read.add(m.group(1) or m.group(2))
+    assert read, "no environment reads found"
+    missing = sorted(read - set(FLAG_REGISTRY) - set(FLAG_ALIASES.values()))
+    assert not missing, missing
+    for name, (typ, default, cat, doc) in FLAG_REGISTRY.items():
+        assert doc and cat and isinstance(default, typ) or default is None, name
+
+
+def test_reference_flag_names_are_aliases(monkeypatch):
+    from vramancer_b200.utils.config import flags
+    monkeypatch.delenv("VRM_MAX_BODY_BYTES", raising=False)
+    monkeypatch.setenv("VRM_MAX_BODY", "1234")
+    assert flags.VRM_MAX_BODY_BYTES == 1234
+    monkeypatch.setenv("VRM_MAX_BODY_BYTES", "99")
+    assert flags.VRM_MAX_BODY_BYTES == 99

@@ -72,6 +72,50 @@ FLAG_REGISTRY: Dict[str, tuple] = {
     "VRM_MINIMAL_TEST": (bool, False, "test", "stub heavy subsystems"),
     "VRM_CLUSTER_PORT": (int, 5040, "cluster", "data-parallel cluster port"),
     "VRM_DISCOVERY_PORT": (int, 5353, "cluster", "UDP discovery port"),
+    "VRM_NODES": (str, "", "cluster", "static node list (comma-separated host:port)"),
+    "VRM_CLUSTER_KEY": (str, "", "cluster", "shared key of the cluster worker routes"),
+    # security / accounts
+    "VRM_AUTH_SECRET": (str, "", "security", "HS256 signing key of access tokens (random per process when empty)"),
+    "VRM_AUTH_EXP": (int, 900, "security", "access-token lifetime, seconds"),
+    "VRM_AUTH_REFRESH_EXP": (int, 86400, "security", "refresh-token lifetime, seconds"),
+    "VRM_AUTH_USERS_FILE": (str, "", "security", "JSON file of accounts (PBKDF2 hashes)"),
+    "VRM_DEFAULT_ADMIN_PASS": (str, "", "security", "password of the bootstrap admin account"),
+    "VRM_CORS_ORIGINS": (str, "", "security", "allowed CORS origins (comma-separated; empty = none)"),
+    "VRM_HMAC_SECRET": (str, "", "security", "HMAC-SHA256 request-signing secret"),
+    "VRM_AUDIT_DB": (str, "", "security", "SQLite audit log path"),
+    "VRM_CONFIG": (str, "", "misc", "YAML configuration file"),
+    # engine
+    "VRM_LOOKAHEAD": (bool, True, "backend", "launch decode step n+1 before reading back step n"),
+    "VRM_FOLD_NORM": (bool, True, "backend", "fold RMSNorm weights into the next GEMM's columns"),
+    "VRM_FOLD_MAX_TOKENS": (int, 16, "backend", "largest batch that runs the folded norms (TP=1)"),
+    "VRM_FOLD_MAX_TOKENS_TP": (int, 128, "backend", "largest batch that runs the folded norms (TP>1)"),
+    "VRM_FUSED_ROPE": (bool, True, "backend", "RoPE + KV write inside decode attention"),
+    "VRM_FUSED_AR": (bool, True, "backend", "tensor-parallel all-reduce fused into the GEMMs"),
+    "VRM_FUSED_AR_MIN_TOKENS": (int, 1, "backend", "smallest batch on the fused all-reduce"),
+    "VRM_FUSED_AR_MAX_TOKENS": (int, 128, "backend", "largest batch on the fused all-reduce"),
+    "VRM_VP_SAMPLE": (bool, True, "backend", "vocabulary-parallel sampling under TP"),
+    "VRM_NVFP4_DECODE": (str, "mma", "backend", "NVFP4 decode GEMM: mma (warp MMA) | tc (tcgen05)"),
+    "VRM_NVFP4_PREFILL": (str, "w4a4", "backend", "NVFP4 prefill: w4a4 (block-scaled tcgen05) or dequant"),
+    # kernel selection / tuning (read once per process by the CUDA extension)
+    "VRM_GEMM_PREFILL": (str, "", "kernel", "prefill GEMM: tiled | streamk | streamk256 | persistent | persistent256"),
+    "VRM_GEMM_PREFILL_STAGES": (int, 3, "kernel", "tiled prefill GEMM pipeline depth (3 or 6)"),
+    "VRM_GEMM_PERSIST_SK": (bool, False, "kernel", "persistent GEMM remainder as stream-K instead of split"),
+    "VRM_GEMM_CTAS": (int, 0, "kernel", "stream-K decode GEMM CTA count (0 = cost model)"),
+    "VRM_GEMM_CLUSTER": (bool, True, "kernel", "cluster split-K reduction in the decode GEMM"),
+    "VRM_GEMM_LEGACY_DECODE": (bool, False, "kernel", "older non-stream-K decode GEMM"),
+    "VRM_DECODE_CLUSTER": (bool, True, "kernel", "decode attention split merge through cluster shared memory"),
+    "VRM_DECODE_TMA": (bool, False, "kernel", "persistent TMA decode attention for bf16 pages"),
+    "VRM_PREFILL_TC": (bool, False, "kernel", "tcgen05 prefill attention (bf16 pages)"),
+    "VRM_L2_PREFETCH": (bool, False, "kernel", "decode attention prefetches the o_proj weights into L2"),
+}
+
+# the reference's names for variables that mean the same thing here (read when the
+# name on the left is unset)
+FLAG_ALIASES: Dict[str, str] = {
+    "VRM_MAX_BODY_BYTES": "VRM_MAX_BODY",
+    "VRM_MAX_QUEUE": "VRM_MAX_QUEUE_SIZE",
+    "VRM_REQUEST_TIMEOUT": "VRM_GENERATE_TIMEOUT",
+    "VRM_RATE_LIMIT_RPM": "VRM_RATE_MAX",
 }
 
 
@@ -83,6 +127,8 @@ class _Flags:
             raise AttributeError(name)
         typ, default, _, _ = FLAG_REGISTRY[name]
         raw = os.environ.get(name)
+        if (raw is None or raw == "") and name in FLAG_ALIASES:
+            raw = os.environ.get(FLAG_ALIASES[name])
         if raw is None or raw == "":
             return default
         if typ is bool:
