@@ -91,6 +91,12 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
     if os.environ.get("VRM_DEFAULT_ADMIN_PASS"):
         auth.ensure_default_admin(production=bool(flags.VRM_PRODUCTION))
     app.state.auth, app.state.cors = auth, cors
+    # credit ledger for sk-VRAM- keys (VRM_LEDGER_DB names its SQLite file; off when unset)
+    ledger = None
+    if os.environ.get("VRM_LEDGER_DB"):
+        from .ledger import CreditLedger
+        ledger = CreditLedger(os.environ["VRM_LEDGER_DB"])
+    app.state.ledger = ledger
     executor = ThreadPoolExecutor(max_workers=max(1, int(flags.VRM_MAX_CONCURRENT)) * 8,
                                   thread_name_prefix="vrm-api")
     monitor = GPUMonitor()
@@ -109,6 +115,13 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
         token = os.environ.get("VRM_API_TOKEN", "")
         authz = request.headers.get("authorization", "")
         cred = authz[7:] if authz.startswith("Bearer ") else request.headers.get("x-api-key", "")
+        if cred and ledger is not None and cred.startswith("sk-VRAM-"):
+            info = ledger.verify(cred)
+            if info is None:
+                return None
+            request.state.user = info["alias"]
+            request.state.ledger_user = info
+            return "user"
         if cred:
             claims = auth.access_claims(cred)
             if claims is not None:
@@ -162,6 +175,36 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
         for k, v in cors.headers(origin).items():
             resp.headers[k] = v
         return resp
+
+    def ledger_charge(request: Request, max_tokens: int):
+        """402 response when a ledger user's balance is spent, else None after charging
+        the request's max_tokens (a short balance is charged nothing and still served,
+        as the reference does)."""
+        info = getattr(request.state, "ledger_user", None)
+        if info is None or ledger is None:
+            return None
+        bal = ledger.balance(info["id"])
+        if bal is None or bal <= 0:
+            return JSONResponse({"error": {"message": "Payment Required: insufficient VRAM credits",
+                                           "type": "insufficient_credits"}, "credit_balance": bal or 0.0},
+                                status_code=402)
+        ledger.consume(info["id"], max_tokens)
+        return None
+
+    @app.post("/api/ledger/users")
+    async def ledger_create_user(request: Request):
+        if ledger is None:
+            return _err(404, "no ledger configured (VRM_LEDGER_DB)", "not_found")
+        body = await request.json()
+        uid, key = ledger.create_user(str(body.get("alias", "user")), float(body.get("credits", 100.0)))
+        return {"id": uid, "api_key": key, "credits": ledger.balance(uid)}
+
+    @app.get("/api/ledger/balance")
+    async def ledger_balance(request: Request):
+        info = getattr(request.state, "ledger_user", None)
+        if info is None or ledger is None:
+            return _err(404, "not a ledger key", "not_found")
+        return {"id": info["id"], "alias": info["alias"], "credit_balance": ledger.balance(info["id"])}
 
     # ------------------------------------------------------------------ accounts
     @app.post("/api/auth/login")
@@ -289,6 +332,9 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
             params["max_new_tokens"] = context_check(p, n_prompt, params["max_new_tokens"])
         except ValidationError as e:
             return _err(400, str(e), code="context_length_exceeded")
+        denied = ledger_charge(request, params["max_new_tokens"] * int(params.get("n", 1) or 1))
+        if denied is not None:
+            return denied
         rid = f"cmpl-{uuid.uuid4().hex[:24]}"
         created = int(time.time())
         stops, n_choices = params.pop("stop"), params.pop("n")
@@ -343,6 +389,9 @@ def create_app(pipeline=None, *, model_alias: Optional[str] = None) -> FastAPI:
             params["max_new_tokens"] = context_check(p, n_prompt, params["max_new_tokens"])
         except ValidationError as e:
             return _err(400, str(e), code="context_length_exceeded")
+        denied = ledger_charge(request, params["max_new_tokens"] * int(params.get("n", 1) or 1))
+        if denied is not None:
+            return denied
         rid = f"chatcmpl-{uuid.uuid4().hex[:24]}"
         created = int(time.time())
         stops, n_choices = params.pop("stop"), params.pop("n")

@@ -39,6 +39,7 @@ PBKDF2_ROUNDS = 120_000
 # (method or "*", path) -> lowest role allowed.  Inference routes need "user".
 ROLE_REQUIRED: Dict[Tuple[str, str], str] = {
     ("POST", "/api/models/load"): "ops",
+    ("POST", "/api/ledger/users"): "admin",
     ("POST", "/api/lora"): "ops",
     ("*", "/api/nodes"): "ops",
     ("POST", "/api/worker/load_partial"): "ops",

@@ -80,7 +80,9 @@ FLAG_REGISTRY: Dict[str, tuple] = {
     "VRM_AUTH_REFRESH_EXP": (int, 86400, "security", "refresh-token lifetime, seconds"),
     "VRM_AUTH_USERS_FILE": (str, "", "security", "JSON file of accounts (PBKDF2 hashes)"),
     "VRM_DEFAULT_ADMIN_PASS": (str, "", "security", "password of the bootstrap admin account"),
-    "VRM_CORS_ORIGINS": (str, "", "security", "allowed CORS origins (comma-separated; empty = none)"),
+    "VRM_CORS_ORIGINS": (str, "http://localhost,http://127.0.0.1", "security",
+                         "allowed CORS origins (comma-separated, * for any)"),
+    "VRM_LEDGER_DB": (str, "", "security", "SQLite file of the credit ledger for sk-VRAM- keys (off when empty)"),
     "VRM_HMAC_SECRET": (str, "", "security", "HMAC-SHA256 request-signing secret"),
     "VRM_AUDIT_DB": (str, "", "security", "SQLite audit log path"),
     "VRM_CONFIG": (str, "", "misc", "YAML configuration file"),
