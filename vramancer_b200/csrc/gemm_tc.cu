@@ -1972,6 +1972,14 @@ static bool prefill_streamk() { return prefill_mode() == 1 || prefill_mode() == 
 
 // Persistent prefill GEMM (gemm_persistent_kernel): whole tiles for the complete rounds
 // over the SMs, the remaining tiles stream-K (WorkMap), one CTA per SM.
+static int persist_splits_env() {
+  static const int v = [] {
+    const char* e = std::getenv("VRM_GEMM_PERSIST_SPLITS");
+    return e ? std::atoi(e) : 0;
+  }();
+  return v;
+}
+
 static int persist_sk_env() {
   static const int v = [] {
     const char* e = std::getenv("VRM_GEMM_PERSIST_SK");
@@ -2008,6 +2016,11 @@ static void launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, cons
   if (!use_sk) {
     int full = tiles, tail_splits = 1;
     choose_tail_split(tiles, k_tiles, 8, &full, &tail_splits);
+    const int forced = persist_splits_env();   // tuning: split the remainder this many ways
+    if (forced > 1 && tiles % sms != 0) {
+      full = (tiles / sms) * sms;
+      tail_splits = std::min(forced, std::max(1, k_tiles / 8));
+    }
     if (tail_splits <= 1) full = tiles;
     wm.dp_tiles = full;
     wm.tail_splits = std::max(1, tail_splits);

@@ -102,6 +102,7 @@ FLAG_REGISTRY: Dict[str, tuple] = {
     "VRM_GEMM_PREFILL": (str, "", "kernel", "prefill GEMM: tiled | streamk | streamk256 | persistent | persistent256"),
     "VRM_GEMM_PREFILL_STAGES": (int, 3, "kernel", "tiled prefill GEMM pipeline depth (3 or 6)"),
     "VRM_GEMM_PERSIST_SK": (bool, False, "kernel", "persistent GEMM remainder as stream-K instead of split"),
+    "VRM_GEMM_PERSIST_SPLITS": (int, 0, "kernel", "persistent GEMM: split the remainder tiles this many ways (0 = cost model)"),
     "VRM_GEMM_CTAS": (int, 0, "kernel", "stream-K decode GEMM CTA count (0 = cost model)"),
     "VRM_GEMM_CLUSTER": (bool, True, "kernel", "cluster split-K reduction in the decode GEMM"),
     "VRM_GEMM_LEGACY_DECODE": (bool, False, "kernel", "older non-stream-K decode GEMM"),
