@@ -730,35 +730,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");   // flag read before the next unit sets it
         if (last) {
           __threadfence();
-          // 32 columns of up to four partials per round: 32 independent 16-byte loads in
-          // flight per thread (the reduction is bound by the latency of these rounds)
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 32) {
-            float v[2][16];
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[0][j] = v[1][j] = 0.f;
+            for (int j = 0; j < 16; ++j) v[j] = 0.f;
             for (int s0 = 0; s0 < nseg; s0 += 4) {
-              float4 x[4][8];
+              float4 x[4][4];
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
                 const float4* src = reinterpret_cast<const float4*>(slot0 + (size_t)(s0 + w) * kBM * BN + c0);
 #pragma unroll
-                for (int q = 0; q < 8; ++q)
+                for (int q = 0; q < 4; ++q)
                   x[w][q] = s0 + w < nseg ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
               }
 #pragma unroll
               for (int w = 0; w < 4; ++w)
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                  float* t = v[q >> 2] + 4 * (q & 3);
-                  t[0] += x[w][q].x;
-                  t[1] += x[w][q].y;
-                  t[2] += x[w][q].z;
-                  t[3] += x[w][q].w;
+                for (int q = 0; q < 4; ++q) {
+                  v[4 * q] += x[w][q].x;
+                  v[4 * q + 1] += x[w][q].y;
+                  v[4 * q + 2] += x[w][q].z;
+                  v[4 * q + 3] += x[w][q].w;
                 }
             }
-            epi_store<false>(ep, r_glob, c_base + c0, v[0]);
-            epi_store<false>(ep, r_glob, c_base + c0 + 16, v[1]);
+            epi_store<false>(ep, r_glob, c_base + c0, v);
           }
           if (threadIdx.x == 64) tile_counters[tile] = 0u;   // ready for the next launch
         }
